@@ -1,0 +1,201 @@
+/*
+ * n3d.h -- C ABI of the B200 (sm_100a) backend for the Nemotron-3 diarization
+ * forward pass.
+ *
+ * This is the `extern "C"` layer a Rust `Model` would bind with `extern "C"`
+ * declarations.  It replaces the reference crate's public
+ * API (src/lib.rs:45-64) and its accelerator plug point
+ * `Model.accel: Option<RefCell<GpuEngine>>` (src/model.rs:137-139):
+ *
+ *   Model::load_gpu              -> n3d_model_load_gpu
+ *   Model::run_offline           -> n3d_run_offline
+ *   Model::run_streaming         -> n3d_run_streaming
+ *   Model::num_speakers          -> n3d_num_speakers
+ *   extract_speaker_dict         -> n3d_extract_speaker_dict
+ *   GpuEngine::{embed_mel_range, forward_embeds, head_forward, forward_window}
+ *                                -> n3d_embed_range, n3d_forward_embeds,
+ *                                   n3d_head_forward, n3d_forward_window
+ *
+ * Conventions: all pointers are plain host pointers unless a parameter name
+ * starts with `d_` (device memory on the model's GPU).  Every call returns an
+ * n3d_status; on failure n3d_last_error() holds a thread-local message.
+ * Calls on one model are serialised by the caller (the reference `Model` is
+ * not Sync either); different models may be used from different threads.
+ * Outputs allocated by the library are released with the matching *_free.
+ */
+#ifndef N3D_H
+#define N3D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Mirrors DiarizationError (src/error.rs:7-45) plus the CUDA-specific cases. */
+typedef enum n3d_status {
+    N3D_OK = 0,
+    N3D_ERR_IO = 1,
+    N3D_ERR_JSON = 2,
+    N3D_ERR_SAFETENSORS = 3,
+    N3D_ERR_TENSOR_DTYPE = 4,
+    N3D_ERR_MISSING_TENSOR = 5,
+    N3D_ERR_TENSOR_SHAPE = 6,
+    N3D_ERR_UNSUPPORTED_AUDIO = 7,
+    N3D_ERR_NPY = 8,
+    N3D_ERR_GPU = 9,
+    N3D_ERR_CUDA = 10,
+    N3D_ERR_TIMEOUT = 11, /* a bounded device-side wait gave up; the context is still usable */
+    N3D_ERR_NO_DEVICE = 12,
+    N3D_ERR_INVALID_ARGUMENT = 13
+} n3d_status;
+
+/* StreamingMode, src/config.rs:21-27. */
+typedef enum n3d_mode {
+    N3D_MODE_LOW_LATENCY = 0,
+    N3D_MODE_VERY_LOW_LATENCY = 1,
+    N3D_MODE_ULTRA_LOW_LATENCY = 2,
+    N3D_MODE_OFFLINE = 3
+} n3d_mode;
+
+typedef struct n3d_model n3d_model;
+
+/* RunOutput, src/model.rs:43-53.  `logits` is [num_frames, num_speakers], pre-sigmoid. */
+typedef struct n3d_run_output {
+    float *logits;
+    size_t num_frames;
+    size_t num_speakers;
+    size_t num_chunks;
+    int cache_compressed;
+    size_t cache_frames;
+    size_t fifo_frames;
+} n3d_run_output;
+
+/* Segment, src/segments.rs:9-14. */
+typedef struct n3d_segment {
+    float start;
+    float end;
+    size_t speaker;
+} n3d_segment;
+
+/* ------------------------------------------------------------- model + runs */
+
+/* Model::load_gpu (src/model.rs:160-166): reads config.json, processor_config.json
+ * and model.safetensors from `dir` and uploads the weights to CUDA device `device`. */
+n3d_status n3d_model_load_gpu(const char *dir, int device, n3d_model **out);
+void n3d_model_free(n3d_model *model);
+
+/* Run the model's work on the caller's CUDA stream (a cudaStream_t passed as
+ * void*), or on the model's own stream again when `stream` is NULL.  No
+ * reference counterpart (wgpu owns its single queue, src/gpu.rs:55-64). */
+n3d_status n3d_model_set_stream(n3d_model *model, void *stream);
+
+/* Model::num_speakers (src/model.rs:211-213) and Model::hidden_size (src/model.rs:215-217). */
+size_t n3d_num_speakers(const n3d_model *model);
+size_t n3d_hidden_size(const n3d_model *model);
+
+/* Model::run_offline (src/model.rs:232-234). */
+n3d_status n3d_run_offline(n3d_model *model, const float *samples, size_t n, n3d_run_output *out);
+
+/* Model::run_streaming (src/model.rs:313-336). `mode` must not be N3D_MODE_OFFLINE. */
+n3d_status n3d_run_streaming(n3d_model *model, const float *samples, size_t n, n3d_mode mode,
+                             n3d_run_output *out);
+
+void n3d_run_output_free(n3d_run_output *out);
+
+/* Many independent clips in one call (no reference counterpart: the reference
+ * runs one clip per call).  outs[i] is clip i's RunOutput, exactly what
+ * n3d_run_offline / n3d_run_streaming returns for it alone. */
+n3d_status n3d_run_batch(n3d_model *model, n3d_mode mode, const float *const *samples, const size_t *lens,
+                         size_t n_clips, n3d_run_output *outs);
+
+/* Device-resident batch (inputs already in HBM): clip i is d_audio[offsets[i] ..
+ * offsets[i] + lens[i]); its logits land at d_logits[out_offsets[i] * num_speakers]
+ * with n3d_batch_out_frames() rows.  Runs on the model's stream and returns
+ * after the device work completes. */
+n3d_status n3d_batch_out_frames(const n3d_model *model, n3d_mode mode, const size_t *lens, size_t n_clips,
+                                size_t *frames_out);
+n3d_status n3d_run_batch_device(n3d_model *model, n3d_mode mode, const float *d_audio, const size_t *offsets,
+                                const size_t *lens, size_t n_clips, float *d_logits, const size_t *out_offsets);
+
+/* ------------------------------------------------------------------ stages */
+
+/* mel::log_mel (src/mel.rs:160-225) on the device.  `out` holds
+ * frame_count(n) * 128 floats; *frames receives that count. */
+n3d_status n3d_log_mel(n3d_model *model, const float *samples, size_t n, int centered, float *out,
+                       size_t out_cap, size_t *frames);
+
+/* GpuEngine::embed_mel_range (src/gpu_engine.rs:1335-1379) / Tower::embed_range
+ * (src/encoder.rs:126-146): groups lo..hi of 8 stacked mel frames -> [hi-lo, hidden]. */
+n3d_status n3d_embed_range(n3d_model *model, const float *mel, size_t num_frames, size_t lo, size_t hi,
+                           float *out);
+
+/* GpuEngine::forward_embeds (src/gpu_engine.rs:1506-1514): the 31-layer tower on one
+ * window [frames, hidden] with `valid` unmasked keys -> final LayerNorm output. */
+n3d_status n3d_forward_embeds(n3d_model *model, const float *embeds, size_t frames, size_t valid, float *out);
+
+/* GpuEngine::head_forward (src/gpu_engine.rs:1695-1699): [frames, hidden] -> [frames*8, ns] logits. */
+n3d_status n3d_head_forward(n3d_model *model, const float *encoder_out, size_t frames, float *logits);
+
+/* GpuEngine::forward_window (src/gpu_engine.rs:1516-1520): tower + head on one window. */
+n3d_status n3d_forward_window(n3d_model *model, const float *embeds, size_t frames, size_t valid, float *logits);
+
+/* ------------------------------------------------------------ segments */
+
+/* extract_speaker_dict (src/segments.rs:70-109).  `mask` may be NULL. */
+n3d_status n3d_extract_speaker_dict(const float *logits, size_t num_frames, size_t num_speakers, float duration,
+                                    const uint8_t *mask, float threshold, n3d_segment **out, size_t *count);
+void n3d_segments_free(n3d_segment *segments);
+
+/* activity_stats (src/segments.rs:113-141): returns the speech percentage. */
+float n3d_activity_stats(const float *logits, size_t num_frames, size_t num_speakers, const uint8_t *mask,
+                         float threshold, size_t *per_speaker);
+
+/* frame_duration (src/segments.rs:36-38). */
+float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate);
+
+/* -------------------------------------------------- single kernels (device) */
+
+/* tensor::linear (src/tensor.rs:22-57) on device buffers: d_y[rows, out] =
+ * d_x[rows, cols] * d_w[out, cols]^T + d_bias (nullable).  cols % 32 == 0.
+ * Uses temporary device memory for the TF32 hi/lo operand split. */
+n3d_status n3d_linear(int device, const float *d_x, size_t rows, size_t cols, const float *d_w, size_t out,
+                      const float *d_bias, float *d_y);
+
+/* tensor::layer_norm (src/tensor.rs:97-110), cols 512 or 1024. */
+n3d_status n3d_layer_norm(int device, const float *d_x, size_t rows, size_t cols, const float *d_w,
+                          const float *d_b, float *d_y);
+
+/* RoPE (src/encoder.rs:163-185, 281-296, positions 0..seq-1, when `rope` != 0) followed
+ * by attention over the first `valid` keys (src/encoder.rs:302-329) on device buffers
+ * q, k, v, out of shape [seq, heads * head_dim]; head_dim 64 or 128. */
+n3d_status n3d_attention(int device, const float *d_q, const float *d_k, const float *d_v, size_t seq,
+                         size_t heads, size_t head_dim, size_t valid, int rope, double rope_theta, float *d_out);
+
+/* ------------------------------------------------------------- profiling */
+
+/* Device time per kernel class of the launches n3d_run_* make while profiling
+ * is on, from CUDA events on the model's own stream.  No reference
+ * counterpart: replaces the env-gated wall-clock timers GPU_PROFILE /
+ * STEP_PROFILE / STAGE_BENCH (src/gpu_engine.rs:1682-1690, src/model.rs:417-473,
+ * src/bin/gpu_check.rs:132-289).  Enabling resets the counters. */
+typedef struct n3d_kernel_stats {
+    const char *name;     /* "gemm_tf32x3", "attention", "layer_norm", "mel", "cache_update", "assemble", "other" */
+    size_t launches;
+    double ms;            /* summed device time */
+    double flops;         /* algorithmic FLOPs of those launches (2*M*N*K for GEMMs) */
+    double bytes;         /* algorithmic DRAM bytes (memory-bound classes) */
+} n3d_kernel_stats;
+n3d_status n3d_profile_enable(n3d_model *model, int on);
+size_t n3d_profile_read(const n3d_model *model, n3d_kernel_stats *out, size_t cap);
+
+/* ------------------------------------------------------------------ misc */
+
+const char *n3d_last_error(void);
+const char *n3d_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

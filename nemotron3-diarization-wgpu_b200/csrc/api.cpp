@@ -1,0 +1,400 @@
+// extern "C" boundary (include/n3d.h): status codes, thread-local error
+// messages, ownership of returned buffers, and the host-only pieces of the
+// reference API (extract_speaker_dict, activity_stats).
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/n3d.h"
+#include "model.h"
+
+struct n3d_model {
+    std::unique_ptr<n3d::Model> m;
+};
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <class F>
+n3d_status guarded(F&& f) {
+    try {
+        f();
+        g_last_error.clear();
+        return N3D_OK;
+    } catch (const n3d::Error& e) {
+        g_last_error = e.what();
+        return (n3d_status)e.status;
+    } catch (const std::bad_alloc&) {
+        g_last_error = "out of host memory";
+        return N3D_ERR_GPU;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return N3D_ERR_GPU;
+    }
+}
+
+void arg_check(bool ok, const char* what) {
+    if (!ok) throw n3d::Error(N3D_ERR_INVALID_ARGUMENT, what);
+}
+
+void fill_output(n3d_run_output* out, std::vector<float>& logits, const n3d::ClipPlan& p, size_t ns) {
+    out->num_speakers = ns;
+    out->num_frames = logits.size() / ns;
+    out->logits = (float*)std::malloc(std::max<size_t>(logits.size(), 1) * sizeof(float));
+    if (!out->logits) throw std::bad_alloc();
+    if (!logits.empty()) std::memcpy(out->logits, logits.data(), logits.size() * sizeof(float));
+    out->num_chunks = (size_t)p.num_chunks;
+    out->cache_compressed = p.cache_compressed;
+    out->cache_frames = (size_t)p.cache_frames;
+    out->fifo_frames = (size_t)p.fifo_frames;
+}
+
+// torch.sigmoid in fp32 (src/segments.rs:41-43)
+float sigmoidf(float x) { return 1.0f / (1.0f + std::exp(-x)); }
+
+// Python round(x, 2), half to even (src/segments.rs:51-62)
+float round2(float v) {
+    const double scaled = (double)v * 100.0;
+    double r = std::round(scaled);
+    if (std::fabs(scaled - std::trunc(scaled)) == 0.5) {
+        const double t = std::trunc(scaled);
+        r = ((long long)t % 2 == 0) ? t : t + 1.0;
+    }
+    return (float)(r / 100.0);
+}
+
+// Per-device scratch for the single-kernel entry points.
+struct KernelCtx {
+    cudaStream_t stream = nullptr;
+    int* err = nullptr;
+};
+KernelCtx& kctx(int device) {
+    static std::mutex mu;
+    static std::vector<KernelCtx> ctxs(64);
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0 || device >= 64) throw n3d::Error(N3D_ERR_NO_DEVICE, "bad device index");
+    KernelCtx& k = ctxs[device];
+    if (!k.stream) {
+        N3D_CUDA(cudaSetDevice(device));
+        N3D_CUDA(cudaStreamCreateWithFlags(&k.stream, cudaStreamNonBlocking));
+        N3D_CUDA(cudaMalloc(&k.err, sizeof(int)));
+        N3D_CUDA(cudaMemset(k.err, 0, sizeof(int)));
+    }
+    return k;
+}
+void kcheck(KernelCtx& k) {
+    N3D_CUDA(cudaStreamSynchronize(k.stream));
+    int e = 0;
+    N3D_CUDA(cudaMemcpy(&e, k.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        N3D_CUDA(cudaMemset(k.err, 0, sizeof(int)));
+        throw n3d::Error(N3D_ERR_TIMEOUT, "a device-side wait timed out (site " + std::to_string(e) + ")");
+    }
+}
+
+struct DevScratch {
+    std::vector<void*> ptrs;
+    float* get(size_t n) {
+        void* p = nullptr;
+        N3D_CUDA(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(float) + 256));
+        ptrs.push_back(p);
+        return (float*)p;
+    }
+    ~DevScratch() {
+        for (void* p : ptrs) cudaFree(p);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+const char* n3d_last_error(void) { return g_last_error.c_str(); }
+const char* n3d_version(void) { return "n3d-b200 0.1 (sm_100a, 3xTF32 tcgen05)"; }
+
+n3d_status n3d_model_load_gpu(const char* dir, int device, n3d_model** out) {
+    return guarded([&] {
+        arg_check(dir && out, "n3d_model_load_gpu: null argument");
+        *out = nullptr;
+        auto* h = new n3d_model;
+        try {
+            h->m = std::make_unique<n3d::Model>(dir, device);
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+
+void n3d_model_free(n3d_model* model) { delete model; }
+
+n3d_status n3d_model_set_stream(n3d_model* model, void* stream) {
+    return guarded([&] {
+        arg_check(model != nullptr, "n3d_model_set_stream: null model");
+        model->m->set_stream((cudaStream_t)stream);
+    });
+}
+
+size_t n3d_num_speakers(const n3d_model* model) { return model ? (size_t)model->m->cfg().num_speakers : 0; }
+size_t n3d_hidden_size(const n3d_model* model) { return model ? (size_t)model->m->cfg().hidden : 0; }
+
+static n3d_status run_one(n3d_model* model, const float* samples, size_t n, int mode, n3d_run_output* out) {
+    return guarded([&] {
+        arg_check(model && out && (samples || n == 0), "null argument");
+        std::memset(out, 0, sizeof(*out));
+        std::vector<std::vector<float>> res(1);
+        std::vector<n3d::ClipPlan> plans;
+        model->m->run_batch(mode, {samples}, nullptr, {0}, {(long long)n}, &res, nullptr, nullptr, &plans);
+        fill_output(out, res[0], plans[0], (size_t)model->m->cfg().num_speakers);
+    });
+}
+
+n3d_status n3d_run_offline(n3d_model* model, const float* samples, size_t n, n3d_run_output* out) {
+    return run_one(model, samples, n, 3, out);
+}
+
+n3d_status n3d_run_streaming(n3d_model* model, const float* samples, size_t n, n3d_mode mode, n3d_run_output* out) {
+    if (mode == N3D_MODE_OFFLINE || (int)mode < 0 || (int)mode > 3) {
+        g_last_error = "n3d_run_streaming: mode must be a streaming mode";
+        return N3D_ERR_INVALID_ARGUMENT;
+    }
+    return run_one(model, samples, n, (int)mode, out);
+}
+
+void n3d_run_output_free(n3d_run_output* out) {
+    if (!out) return;
+    std::free(out->logits);
+    out->logits = nullptr;
+}
+
+n3d_status n3d_run_batch(n3d_model* model, n3d_mode mode, const float* const* samples, const size_t* lens,
+                         size_t n_clips, n3d_run_output* outs) {
+    return guarded([&] {
+        arg_check(model && (n_clips == 0 || (samples && lens && outs)), "n3d_run_batch: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_run_batch: bad mode");
+        std::vector<const float*> a(samples, samples + n_clips);
+        std::vector<long long> l(lens, lens + n_clips), off(n_clips, 0);
+        std::vector<std::vector<float>> res(n_clips);
+        std::vector<n3d::ClipPlan> plans;
+        model->m->run_batch((int)mode, a, nullptr, off, l, &res, nullptr, nullptr, &plans);
+        for (size_t i = 0; i < n_clips; i++) std::memset(&outs[i], 0, sizeof(outs[i]));
+        for (size_t i = 0; i < n_clips; i++)
+            fill_output(&outs[i], res[i], plans[i], (size_t)model->m->cfg().num_speakers);
+    });
+}
+
+n3d_status n3d_batch_out_frames(const n3d_model* model, n3d_mode mode, const size_t* lens, size_t n_clips,
+                                size_t* frames_out) {
+    return guarded([&] {
+        arg_check(model && (n_clips == 0 || (lens && frames_out)), "n3d_batch_out_frames: null argument");
+        for (size_t i = 0; i < n_clips; i++) {
+            n3d::ClipPlan p = mode == N3D_MODE_OFFLINE ? n3d::plan_offline(model->m->cfg(), (long long)lens[i])
+                                                       : n3d::plan_streaming(model->m->cfg(), (long long)lens[i], (int)mode);
+            frames_out[i] = (size_t)p.out_rows;
+        }
+    });
+}
+
+n3d_status n3d_run_batch_device(n3d_model* model, n3d_mode mode, const float* d_audio, const size_t* offsets,
+                                const size_t* lens, size_t n_clips, float* d_logits, const size_t* out_offsets) {
+    return guarded([&] {
+        arg_check(model && (n_clips == 0 || (d_audio && offsets && lens && d_logits && out_offsets)),
+                  "n3d_run_batch_device: null argument");
+        std::vector<long long> off(offsets, offsets + n_clips), l(lens, lens + n_clips),
+            oo(out_offsets, out_offsets + n_clips);
+        model->m->run_batch((int)mode, {}, d_audio, off, l, nullptr, d_logits, &oo, nullptr);
+    });
+}
+
+n3d_status n3d_log_mel(n3d_model* model, const float* samples, size_t n, int centered, float* out, size_t out_cap,
+                       size_t* frames) {
+    return guarded([&] {
+        arg_check(model && (samples || n == 0) && frames, "n3d_log_mel: null argument");
+        std::vector<float> mel;
+        const int f = model->m->log_mel(samples, (long long)n, centered != 0, mel);
+        *frames = (size_t)f;
+        arg_check(out_cap >= mel.size() && (out || mel.empty()), "n3d_log_mel: output buffer too small");
+        if (!mel.empty()) std::memcpy(out, mel.data(), mel.size() * sizeof(float));
+    });
+}
+
+n3d_status n3d_embed_range(n3d_model* model, const float* mel, size_t num_frames, size_t lo, size_t hi, float* out) {
+    return guarded([&] {
+        arg_check(model && out && (mel || num_frames == 0) && hi >= lo, "n3d_embed_range: bad argument");
+        model->m->embed_range(mel, (long long)num_frames, (long long)lo, (long long)hi, out);
+    });
+}
+
+n3d_status n3d_forward_embeds(n3d_model* model, const float* embeds, size_t frames, size_t valid, float* out) {
+    return guarded([&] {
+        arg_check(model && embeds && out, "n3d_forward_embeds: null argument");
+        model->m->forward_window(embeds, (int)frames, (int)valid, out, nullptr);
+    });
+}
+
+n3d_status n3d_head_forward(n3d_model* model, const float* encoder_out, size_t frames, float* logits) {
+    return guarded([&] {
+        arg_check(model && encoder_out && logits, "n3d_head_forward: null argument");
+        model->m->head_forward(encoder_out, (int)frames, logits);
+    });
+}
+
+n3d_status n3d_forward_window(n3d_model* model, const float* embeds, size_t frames, size_t valid, float* logits) {
+    return guarded([&] {
+        arg_check(model && embeds && logits, "n3d_forward_window: null argument");
+        model->m->forward_window(embeds, (int)frames, (int)valid, nullptr, logits);
+    });
+}
+
+n3d_status n3d_extract_speaker_dict(const float* logits, size_t num_frames, size_t ns, float duration,
+                                    const uint8_t* mask, float threshold, n3d_segment** out, size_t* count) {
+    return guarded([&] {
+        arg_check(out && count && (logits || num_frames == 0 || ns == 0), "n3d_extract_speaker_dict: null argument");
+        std::vector<n3d_segment> segs;
+        for (size_t s = 0; s < ns; s++) {
+            long long start = -1;
+            for (size_t t = 0; t <= num_frames; t++) {
+                const bool active = t < num_frames && sigmoidf(logits[t * ns + s]) > threshold && (!mask || mask[t]);
+                if (active && start < 0) {
+                    start = (long long)t;
+                } else if (!active && start >= 0) {
+                    segs.push_back(n3d_segment{round2((float)start * duration), round2((float)t * duration), s});
+                    start = -1;
+                }
+            }
+        }
+        std::stable_sort(segs.begin(), segs.end(), [](const n3d_segment& a, const n3d_segment& b) {
+            if (a.start != b.start) return a.start < b.start;
+            return a.speaker < b.speaker;
+        });
+        *count = segs.size();
+        *out = (n3d_segment*)std::malloc(std::max<size_t>(segs.size(), 1) * sizeof(n3d_segment));
+        if (!*out) throw std::bad_alloc();
+        if (!segs.empty()) std::memcpy(*out, segs.data(), segs.size() * sizeof(n3d_segment));
+    });
+}
+
+void n3d_segments_free(n3d_segment* segments) { std::free(segments); }
+
+float n3d_activity_stats(const float* logits, size_t num_frames, size_t ns, const uint8_t* mask, float threshold,
+                         size_t* per_speaker) {
+    size_t any = 0, total = 0;
+    for (size_t s = 0; s < ns; s++) per_speaker[s] = 0;
+    for (size_t t = 0; t < num_frames; t++) {
+        if (mask && !mask[t]) continue;
+        total++;
+        bool hot = false;
+        for (size_t s = 0; s < ns; s++)
+            if (sigmoidf(logits[t * ns + s]) > threshold) {
+                per_speaker[s]++;
+                hot = true;
+            }
+        any += hot;
+    }
+    return total == 0 ? 0.0f : (float)any * 100.0f / (float)total;
+}
+
+float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate) {
+    return (float)hop_length / (float)sampling_rate;
+}
+
+n3d_status n3d_profile_enable(n3d_model* model, int on) {
+    return guarded([&] {
+        arg_check(model != nullptr, "n3d_profile_enable: null model");
+        model->m->profile_enable(on != 0);
+    });
+}
+
+size_t n3d_profile_read(const n3d_model* model, n3d_kernel_stats* out, size_t cap) {
+    static const char* names[n3d::K_NCLASS] = {"gemm_tf32x3", "attention", "layer_norm", "mel",
+                                               "cache_update", "assemble", "other"};
+    if (!model) return 0;
+    const n3d::ProfTotals* t = model->m->profile_totals();
+    size_t n = 0;
+    for (int i = 0; i < n3d::K_NCLASS && n < cap; i++, n++)
+        out[n] = n3d_kernel_stats{names[i], (size_t)t[i].launches, t[i].ms, t[i].flops, t[i].bytes};
+    return n;
+}
+
+n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
+                      const float* d_bias, float* d_y) {
+    return guarded([&] {
+        arg_check(d_x && d_w && d_y, "n3d_linear: null argument");
+        arg_check(cols % 32 == 0 && cols > 0, "n3d_linear: cols must be a positive multiple of 32");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        DevScratch sc;
+        float* xh = sc.get(rows * cols);
+        float* xl = sc.get(rows * cols);
+        float* wh = sc.get(out * cols);
+        float* wl = sc.get(out * cols);
+        n3d::launch_split(k.stream, d_x, (long long)(rows * cols), xh, xl);
+        n3d::launch_split(k.stream, d_w, (long long)(out * cols), wh, wl);
+        n3d::Epi e;
+        e.mode = n3d::EPI_STORE;
+        e.bias = d_bias;
+        e.out = d_y;
+        e.ldo = (long long)out;
+        n3d::gemm_tf32x3(k.stream, n3d::SplitOperand{xh, xl, (long long)rows, (long long)cols, (long long)cols},
+                         n3d::SplitOperand{wh, wl, (long long)out, (long long)cols, (long long)cols}, (int)rows,
+                         (int)out, (int)cols, 0, e, k.err);
+        kcheck(k);
+    });
+}
+
+n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, const float* d_b,
+                          float* d_y) {
+    return guarded([&] {
+        arg_check(d_x && d_w && d_b && d_y, "n3d_layer_norm: null argument");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, d_y, nullptr);
+        kcheck(k);
+    });
+}
+
+n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const float* d_v, size_t seq, size_t heads,
+                         size_t head_dim, size_t valid, int rope, double rope_theta, float* d_out) {
+    return guarded([&] {
+        arg_check(d_q && d_k && d_v && d_out, "n3d_attention: null argument");
+        arg_check(head_dim == 64 || head_dim == 128, "n3d_attention: head_dim must be 64 or 128");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        DevScratch sc;
+        float* qkv = sc.get(seq * 3 * heads * head_dim);
+        float *cs = nullptr, *sn = nullptr;
+        if (rope) {
+            // rope_tables (src/encoder.rs:163-185), positions 0..seq-1
+            const size_t half = head_dim / 2;
+            std::vector<float> inv(half), hc(seq * head_dim), hs(seq * head_dim);
+            for (size_t i = 0; i < half; i++)
+                inv[i] = (float)(1.0 / std::pow(rope_theta, 2.0 * (double)i / (double)head_dim));
+            for (size_t p = 0; p < seq; p++)
+                for (size_t i = 0; i < half; i++) {
+                    const float a = (float)p * inv[i];
+                    hc[p * head_dim + i] = hc[p * head_dim + half + i] = std::cos(a);
+                    hs[p * head_dim + i] = hs[p * head_dim + half + i] = std::sin(a);
+                }
+            cs = sc.get(seq * head_dim);
+            sn = sc.get(seq * head_dim);
+            N3D_CUDA(cudaMemcpyAsync(cs, hc.data(), hc.size() * 4, cudaMemcpyHostToDevice, k.stream));
+            N3D_CUDA(cudaMemcpyAsync(sn, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, k.stream));
+        }
+        n3d::launch_pack_qkv(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, qkv);
+        int v = (int)std::min(valid, seq);
+        int* dv = (int*)sc.get(1);
+        N3D_CUDA(cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, k.stream));
+        n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out, nullptr);
+        kcheck(k);
+    });
+}
+
+}  // extern "C"

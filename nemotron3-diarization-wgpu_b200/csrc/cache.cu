@@ -1,0 +1,303 @@
+// Device-resident speaker cache (AOSC + FIFO) and encoder-window assembly.
+//
+// Replaces the reference's CPU `SpeakerCache` (src/streaming.rs:130-482) and the
+// host-side window concatenation of `Model::step` (src/model.rs:383-391,
+// 444-461).  All bookkeeping counts (cache/FIFO sizes, pops, whether a step
+// compresses) depend only on the chunk schedule, never on data, so the host
+// precomputes them per step and these kernels only move and rank data.
+//
+// Per sequence, the state carried between steps is its *prefix*: the rows
+// `[cache ++ fifo]` that open the next window, plus the probabilities stored
+// with a compressed cache.  Both live in ping-pong buffers.
+
+#include <cmath>
+
+#include "n3d_device.cuh"
+#include "n3d_internal.h"
+#include "n3d_cache.h"
+
+namespace n3d {
+
+namespace {
+
+constexpr float kLn2 = 0.69314718055994531f;
+
+// Rust `f32::ln` / `f32::exp` call the platform libm; evaluating in double and
+// rounding once lands on the correctly rounded float, which is what that libm
+// returns for these arguments.
+__device__ __forceinline__ float ln_f(float x) { return (float)log((double)x); }
+__device__ __forceinline__ float exp_f(float x) { return (float)exp((double)x); }
+
+// window row t of sequence i: prefix rows from the previous step, then this
+// step's new embeddings, then zeros up to the batch stride.
+__global__ void assemble_kernel(const SeqStep* __restrict__ steps, const float* __restrict__ embeds,
+                                float* __restrict__ win, int stride, int hidden) {
+    const int i = blockIdx.y, t = blockIdx.x;
+    const SeqStep st = steps[i];
+    const int prefix = st.ncache + st.nfifo;
+    const float4* src = nullptr;
+    if (t < prefix)
+        src = reinterpret_cast<const float4*>(st.pre_in + (long long)t * hidden);
+    else if (t < st.S)
+        src = reinterpret_cast<const float4*>(embeds + (st.emb_row + t - prefix) * hidden);
+    float4* dst = reinterpret_cast<float4*>(win + ((long long)i * stride + t) * hidden);
+    for (int c = threadIdx.x; c < hidden / 4; c += blockDim.x) dst[c] = src ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// Stable descending order on (value, index): a goes first iff it has the larger
+// value, or an equal value and the smaller index (Rust's stable `sort_by`).
+__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+struct CacheParams {
+    int hidden, ns, sub, cache_len, n_sil, min_pos, k_strong, k_weak;
+    float thr, latest_boost;
+};
+
+// One CTA per sequence.  Shared layout (floats unless noted):
+//   probs [S*ns]      pooled step probabilities (_pool_probs)
+//   cand  [ne*ns]     probabilities of the compression candidates
+//   sc    [ne*ns]     frame scores
+//   key   [P] / idx [P] (int) bitonic-sorted flat scores (P = pow2 >= ns*(ne+n_sil))
+//   aux   [P] (int)   ranks / selection flags
+__global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __restrict__ steps,
+                                                           const float* __restrict__ win,
+                                                           const float* __restrict__ logits, int stride,
+                                                           CacheParams cp, const float* __restrict__ silence,
+                                                           int P_max) {
+    extern __shared__ float sm[];
+    const int i = blockIdx.x;
+    const SeqStep st = steps[i];
+    const int ns = cp.ns, sub = cp.sub, hidden = cp.hidden;
+    const int S = st.S;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const float* wrow = win + (long long)i * stride * hidden;
+    const float* lrow = logits + (long long)i * stride * sub * ns;
+
+    float* probs = sm;
+    float* cand = probs + stride * ns;
+    float* sc = cand + stride * ns;
+    float* key = sc + stride * ns;
+    int* idx = reinterpret_cast<int*>(key + P_max);
+    int* aux = idx + P_max;
+
+    // ---- _pool_probs (src/streaming.rs:202-217): sigmoid averaged over sub-frames, mask after
+    for (int e = tid; e < S * ns; e += nt) {
+        const int g = e / ns, c = e % ns;
+        float acc = 0.0f;
+        for (int k = 0; k < sub; k++) {
+            const float l = lrow[((long long)g * sub + k) * ns + c];
+            acc = __fadd_rn(acc, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f(-l))));
+        }
+        probs[e] = g < st.valid ? __fdiv_rn(acc, (float)sub) : 0.0f;
+    }
+    // ---- scored logit rows [cached*sub, (cached+nchunk)*sub), capped (src/model.rs:455-461)
+    {
+        const long long s0 = (long long)(st.ncache + st.nfifo) * sub * ns;
+        const long long n = (long long)st.keep_rows * ns;
+        for (long long e = tid; e < n; e += nt) st.out_logits[e] = lrow[s0 + e];
+    }
+    __syncthreads();
+
+    const int ne = st.ncache + st.popped;
+    // ---- candidates' probabilities: stored (compressed cache) or this step's, then popped FIFO frames
+    for (int e = tid; e < ne * ns; e += nt) {
+        const int f = e / ns;
+        cand[e] = (f < st.ncache && st.was_compressed) ? st.cp_in[e] : probs[e];
+    }
+    __syncthreads();
+
+    // ---- new FIFO: window rows [ncache + popped, ncache + nfifo + nchunk)
+    const int cf_new = st.popped > 0 ? (st.compress ? cp.cache_len : ne) : st.ncache;
+    const int ff_new = st.nfifo + st.nchunk - st.popped;
+    for (long long e = tid; e < (long long)ff_new * (hidden / 4); e += nt) {
+        const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
+        reinterpret_cast<float4*>(st.pre_out + (long long)(cf_new + r) * hidden)[c] =
+            reinterpret_cast<const float4*>(wrow + (long long)(st.ncache + st.popped + r) * hidden)[c];
+    }
+
+    if (!st.compress) {
+        // cache rows = window rows [0, cf_new); stored probs follow them
+        for (long long e = tid; e < (long long)cf_new * (hidden / 4); e += nt) {
+            const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
+            reinterpret_cast<float4*>(st.pre_out + (long long)r * hidden)[c] =
+                reinterpret_cast<const float4*>(wrow + (long long)r * hidden)[c];
+        }
+        if (st.popped > 0)
+            for (int e = tid; e < ne * ns; e += nt) st.cp_out[e] = cand[e];
+        else if (st.was_compressed)
+            for (int e = tid; e < st.ncache * ns; e += nt) st.cp_out[e] = st.cp_in[e];
+        return;
+    }
+
+    // ================= _compress (src/streaming.rs:410-482) =================
+    // ---- _get_frame_scores (src/streaming.rs:294-330)
+    for (int f = tid; f < ne; f += nt) {
+        const float* row = cand + f * ns;
+        float lp[16], lc[16];
+        float sum_lc = 0.0f;
+        for (int s = 0; s < ns; s++) {
+            lp[s] = ln_f(fmaxf(row[s], cp.thr));
+            lc[s] = ln_f(fmaxf(__fsub_rn(1.0f, row[s]), cp.thr));
+        }
+        for (int s = 0; s < ns; s++) sum_lc = __fadd_rn(sum_lc, lc[s]);
+        for (int s = 0; s < ns; s++) {
+            const float v = __fadd_rn(__fadd_rn(__fsub_rn(lp[s], lc[s]), sum_lc), kLn2);
+            sc[f * ns + s] = row[s] > 0.5f ? v : -INFINITY;
+        }
+    }
+    if (tid < ns) aux[tid] = 0;
+    __syncthreads();
+    for (int e = tid; e < ne * ns; e += nt)
+        if (sc[e] > 0.0f) atomicAdd(&aux[e % ns], 1);
+    __syncthreads();
+    for (int e = tid; e < ne * ns; e += nt) {
+        const int s = e % ns;
+        if (aux[s] >= cp.min_pos && sc[e] <= 0.0f && cand[e] > 0.5f) sc[e] = -INFINITY;
+    }
+    __syncthreads();
+    // ---- latest-frames boost: frames past the cache capacity were just popped
+    for (int e = tid; e < ne * ns; e += nt)
+        if (e / ns >= cp.cache_len) sc[e] = __fadd_rn(sc[e], cp.latest_boost);
+    __syncthreads();
+    // ---- _boost_scores twice (src/streaming.rs:333-346): per speaker, the k best frames
+    for (int pass = 0; pass < 2; pass++) {
+        const int k = pass == 0 ? cp.k_strong : cp.k_weak;
+        const float boost = pass == 0 ? 2.0f * kLn2 : kLn2;
+        for (int e = tid; e < ne * ns; e += nt) {
+            const int f = e / ns, s = e % ns;
+            const float v = sc[e];
+            int rank = 0;
+            for (int g = 0; g < ne && rank < k; g++) {
+                const float u = sc[g * ns + s];
+                rank += (u > v) || (u == v && g < f);
+            }
+            aux[e] = rank < k;
+        }
+        __syncthreads();
+        for (int e = tid; e < ne * ns; e += nt)
+            if (aux[e]) sc[e] = __fadd_rn(sc[e], boost);
+        __syncthreads();
+    }
+    // ---- flat speaker-major scores with +inf silence slots, bitonic sort (value desc, index asc)
+    const int nsc = ne + cp.n_sil;
+    const int total = ns * nsc;
+    int P = 1;
+    while (P < total) P <<= 1;
+    for (int e = tid; e < P; e += nt) {
+        float v = -INFINITY;
+        if (e < total) {
+            const int s = e / nsc, f = e % nsc;
+            v = f < ne ? sc[f * ns + s] : INFINITY;
+        }
+        key[e] = v;
+        idx[e] = e;  // padding entries carry indices >= total, so they sort after every real one
+    }
+    __syncthreads();
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int e = tid; e < P; e += nt) {
+                const int p = e ^ j;
+                if (p > e) {
+                    const bool asc = (e & k) == 0;  // this block ends in "before" order
+                    const float ve = key[e], vp = key[p];
+                    const int ie = idx[e], ip = idx[p];
+                    const bool swap = asc ? before(vp, ip, ve, ie) : before(ve, ie, vp, ip);
+                    if (swap) {
+                        key[e] = vp;
+                        key[p] = ve;
+                        idx[e] = ip;
+                        idx[p] = ie;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    // ---- topk = first cache_len; -inf picks become the sentinel; indices sorted ascending
+    const int L = cp.cache_len;
+    for (int e = tid; e < P; e += nt) aux[e] = 0;
+    __syncthreads();
+    for (int r = tid; r < L && r < total; r += nt)
+        if (key[r] != -INFINITY) aux[idx[r]] = 1;
+    __syncthreads();
+    // exclusive scan of aux over [0, total) -> position of each kept index (block scan in chunks)
+    __shared__ int carry, warp_tot[16];
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < total; base += nt) {
+        const int e = base + tid;
+        const int flag = e < total ? aux[e] : 0;
+        int x = flag;
+        const int lane = tid & 31, w = tid >> 5;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[w] = x;
+        __syncthreads();
+        int woff = 0;
+        for (int q = 0; q < w; q++) woff += warp_tot[q];
+        const int pos = carry + woff + x - flag;
+        __syncthreads();
+        if (e < total && flag) idx[pos] = e;  // idx reused as the picked list (sorted ascending)
+        if (tid == nt - 1) carry = pos + flag;
+        __syncthreads();
+    }
+    const int n_real = carry;
+    // ---- gather (src/streaming.rs:464-481): silence rows are silence_embeds with zero probs
+    for (long long e = tid; e < (long long)L * (hidden / 4); e += nt) {
+        const int p = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
+        int frame = ne;
+        if (p < n_real) {
+            const int f = idx[p] % nsc;
+            frame = f < ne ? f : ne;
+        }
+        const float4* src = frame < ne ? reinterpret_cast<const float4*>(wrow + (long long)frame * hidden)
+                                       : reinterpret_cast<const float4*>(silence);
+        reinterpret_cast<float4*>(st.pre_out + (long long)p * hidden)[c] = src[c];
+    }
+    for (int e = tid; e < L * ns; e += nt) {
+        const int p = e / ns, s = e % ns;
+        int frame = ne;
+        if (p < n_real) {
+            const int f = idx[p] % nsc;
+            frame = f < ne ? f : ne;
+        }
+        st.cp_out[e] = frame < ne ? cand[frame * ns + s] : 0.0f;
+    }
+}
+
+}  // namespace
+
+void launch_assemble(cudaStream_t s, const SeqStep* steps, int nseq, const float* embeds, float* win, int stride,
+                     int hidden) {
+    if (nseq <= 0 || stride <= 0) return;
+    assemble_kernel<<<dim3(stride, nseq), 128, 0, s>>>(steps, embeds, win, stride, hidden);
+    N3D_CUDA(cudaGetLastError());
+}
+
+size_t cache_update_smem(int stride, int ns, int P_max) {
+    return (size_t)3 * stride * ns * 4 + (size_t)P_max * 4 * 3;
+}
+
+void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const float* win, const float* logits,
+                         int stride, const CacheConst& c, const float* silence) {
+    if (nseq <= 0) return;
+    int P = 1;
+    while (P < c.ns * (stride + c.n_sil)) P <<= 1;
+    const size_t smem = cache_update_smem(stride, c.ns, P);
+    static size_t attr = 0;
+    if (smem > attr) {
+        N3D_CUDA(cudaFuncSetAttribute(cache_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr = smem;
+    }
+    CacheParams cp{c.hidden, c.ns, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
+                   c.latest_boost};
+    cache_update_kernel<<<nseq, 512, smem, s>>>(steps, win, logits, stride, cp, silence, P);
+    N3D_CUDA(cudaGetLastError());
+}
+
+}  // namespace n3d

@@ -1,0 +1,348 @@
+// C[M, N] = A[M, K] * B[N, K]^T on the sm_100a tensor cores (tcgen05, kind::tf32)
+// with 3xTF32 error compensation and fused epilogues.
+//
+// Replaces the reference's WGSL `gemm` pipeline (src/gpu.rs:1005-1611, wrapper
+// src/gpu.rs:726-744) and the separate `add`, `unary` (GELU/ReLU), `rope` and
+// `col3` dispatches that followed it (src/gpu.rs:1768-1838, 1973-1999): those
+// become epilogue modes of this one kernel.  The reference arithmetic it must
+// agree with is `tensor::linear` (src/tensor.rs:22-57) in fp32; every operand
+// is a TF32 hi/lo pair and each k-step issues lo*hi + hi*lo + hi*hi, which
+// keeps the products at fp32 grade (a plain TF32 GEMM flips sigmoid>0.5
+// decisions on this model, see the design notes).
+//
+// CTA = 6 warps, one 128 x BN output tile:
+//   warp 0      one thread issues TMA loads of A_hi, A_lo, B_hi, B_lo per k-block
+//   warp 1      allocates TMEM; one thread issues the UMMAs and the commits
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w owns TMEM lanes
+//               32*(w%4) .. +31, i.e. output rows), apply the mode, store.
+// Shared memory holds STAGES k-blocks of 32 fp32 (128 B rows, 128-byte swizzle).
+// Every wait is bounded; a wait that expires records its site in *err.
+
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "n3d_device.cuh"
+#include "n3d_internal.h"
+
+namespace n3d {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int A_BYTES = BM * BK * 4;
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+    static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static_assert(STAGES >= 2, "need at least two pipeline stages");
+};
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    // 0.5 * x * (1 + erf(x / sqrt(2))), the exact form of src/tensor.rs:113-120
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Store 32 consecutive fp32 values of one output row.
+__device__ __forceinline__ void store_row32(float* dst, const float* v, int ncols_left) {
+    if (ncols_left >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+        for (int i = 0; i < 32 && i < ncols_left; i++) dst[i] = v[i];
+    }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                       const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo, int M,
+                       int N, int K, int kb_per_tap, const __grid_constant__ Epi epi, int* err) {
+    using Cfg = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nkb = K / BK;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < Cfg::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&tA_hi);
+        tma_prefetch_desc(&tA_lo);
+        tma_prefetch_desc(&tB_hi);
+        tma_prefetch_desc(&tB_lo);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % Cfg::STAGES;
+                const uint32_t ph = (kb / Cfg::STAGES) & 1;
+                if (kb >= Cfg::STAGES && !mbar_wait(&empty[s], ph ^ 1, err, DEV_TIMEOUT_TMA_EMPTY)) break;
+                uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
+                const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * BK : kb * BK;
+                tma_load_2d(st, &tA_hi, &full[s], ka, m0 + tap);
+                tma_load_2d(st + Cfg::A_BYTES, &tA_lo, &full[s], ka, m0 + tap);
+                tma_load_2d(st + 2 * Cfg::A_BYTES, &tB_hi, &full[s], kb * BK, n0);
+                tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tB_lo, &full[s], kb * BK, n0);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(BN);
+            bool ok = true;
+            for (int kb = 0; kb < nkb; kb++) {
+                const int s = kb % Cfg::STAGES;
+                const uint32_t ph = (kb / Cfg::STAGES) & 1;
+                if (!mbar_wait(&full[s], ph, err, DEV_TIMEOUT_TMA_FULL)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a_hi = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                const uint32_t a_lo = a_hi + Cfg::A_BYTES;
+                const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES;
+                const uint32_t b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 8; k++) {
+                    const uint32_t off = k * 32;  // 8 tf32 = 32 bytes along the swizzled row
+                    const uint64_t dah = desc_k_sw128(a_hi + off), dal = desc_k_sw128(a_lo + off);
+                    const uint64_t dbh = desc_k_sw128(b_hi + off), dbl = desc_k_sw128(b_lo + off);
+                    umma_tf32(tmem, dal, dbh, idesc, (kb | k) != 0);
+                    umma_tf32(tmem, dah, dbl, idesc, 1);
+                    umma_tf32(tmem, dah, dbh, idesc, 1);
+                }
+                umma_commit(&empty[s]);
+            }
+            if (ok) umma_commit(acc_full);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const bool ok = mbar_wait(acc_full, 0, err, DEV_TIMEOUT_ACC);
+        tc_fence_after();
+        if (ok) {
+            const int r = m0 + q * 32 + lane;
+            const bool row_ok = r < M;
+            const int qq = r / epi.rdiv, t = r - qq * epi.rdiv;
+            const bool keep = row_ok && t < epi.rkeep;
+            const long long orow = (long long)qq * epi.rmul + t + epi.roff;
+            const bool zero_row = epi.seq_len != nullptr && keep && t >= epi.seq_len[qq];
+            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+
+            if (epi.mode == EPI_QKV_ROPE) {
+                // 64-column chunks = one head; rotate-half RoPE (src/encoder.rs:281-296)
+                for (int c = 0; c < BN; c += 64) {
+                    float v[64];
+                    tmem_ld32(tl + c, v);
+                    tmem_ld32(tl + c + 32, v + 32);
+                    const int col0 = n0 + c;
+                    if (!keep || col0 >= N) continue;
+                    if (col0 < epi.q_cols + epi.k_cols) {
+                        const int pos = r % epi.rope_seq;
+                        const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
+                        const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            const float x1 = v[i], x2 = v[32 + i];
+                            v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+                            v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                        }
+                    }
+                    float* dst = epi.out + orow * epi.ldo + col0;
+                    store_row32(dst, v, N - col0);
+                    store_row32(dst + 32, v + 32, N - col0 - 32);
+                }
+            } else if (epi.mode == EPI_DENSE_OUT) {
+                // relu(dense) then the out projection, sequential over the hidden
+                // index with separate multiply and add (src/tensor.rs:33-43)
+                float acc[8];
+#pragma unroll
+                for (int o = 0; o < 8; o++) acc[o] = 0.0f;
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(tl + c, v);
+                    if (!keep) continue;
+                    for (int i = 0; i < 32; i++) {
+                        const int col = n0 + c + i;
+                        if (col >= N) break;
+                        const float rr = fmaxf(__fadd_rn(v[i], epi.bias[col]), 0.0f);
+#pragma unroll
+                        for (int o = 0; o < 8; o++)
+                            if (o < epi.n2) acc[o] = __fadd_rn(acc[o], __fmul_rn(rr, epi.w2[o * N + col]));
+                    }
+                }
+                if (keep)
+                    for (int o = 0; o < epi.n2; o++) epi.out[orow * epi.ldo + o] = __fadd_rn(acc[o], epi.b2[o]);
+            } else {
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(tl + c, v);
+                    const int col0 = n0 + c;
+                    if (!keep || col0 >= N) continue;
+                    const int left = N - col0;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float b = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
+                        v[i] = __fadd_rn(v[i], b);
+                    }
+                    float* dst = epi.out + orow * epi.ldo + col0;
+                    switch (epi.mode) {
+                        case EPI_STORE:
+                            store_row32(dst, v, left);
+                            break;
+                        case EPI_RESID: {
+                            for (int i = 0; i < 32 && i < left; i++) dst[i] = __fadd_rn(dst[i], v[i]);
+                            break;
+                        }
+                        default: {
+                            float lo[32];
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                float x = v[i];
+                                if (epi.mode == EPI_GELU_SPLIT) x = gelu_erf(x);
+                                if (epi.mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
+                                if (zero_row) x = 0.0f;
+                                split_tf32(x, v[i], lo[i]);
+                            }
+                            store_row32(dst, v, left);
+                            store_row32(epi.out_lo + orow * epi.ldo + col0, lo, left);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+// ------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) throw Error(9 /*N3D_ERR_GPU*/, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+// 2-D map over a row-major fp32 matrix [rows, cols] (row stride ld elements),
+// box = 32 columns x box_rows rows, 128-byte swizzle, zero fill out of bounds.
+CUtensorMap make_map(const float* ptr, long long rows, long long cols, long long ld, int box_rows) {
+    using Key = std::tuple<const float*, long long, long long, long long, int>;
+    static std::map<Key, CUtensorMap> cache;
+    static std::mutex mu;
+    const Key key{ptr, rows, cols, ld, box_rows};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 4) % 16 || cols % BK)
+        throw Error(9, "GEMM operand is not 16-byte aligned or K is not a multiple of 32");
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    return m;
+}
+
+template <int BN>
+void launch(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+            const Epi& epi, int* err) {
+    using Cfg = GemmCfg<BN>;
+    static bool attr = false;
+    if (!attr) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM));
+        attr = true;
+    }
+    const CUtensorMap a_hi = make_map(A.hi, A.rows, A.cols, A.ld, BM);
+    const CUtensorMap a_lo = make_map(A.lo, A.rows, A.cols, A.ld, BM);
+    const CUtensorMap b_hi = make_map(B.hi, B.rows, B.cols, B.ld, BN);
+    const CUtensorMap b_lo = make_map(B.lo, B.rows, B.cols, B.ld, BN);
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    gemm_tf32x3_kernel<BN><<<grid, 192, Cfg::SMEM, s>>>(a_hi, a_lo, b_hi, b_lo, M, N, K, kb_per_tap, epi, err);
+    N3D_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                 int kb_per_tap, const Epi& epi, int* err) {
+    if (M <= 0 || N <= 0) return;
+    if (K % BK) throw Error(9, "GEMM K must be a multiple of 32");
+    int bn;
+    if (epi.mode == EPI_DENSE_OUT) {
+        if (N != 192) throw Error(9, "the fused dense+out_proj epilogue needs N == 192");
+        bn = 192;
+    } else if (N == 192) {
+        bn = 192;
+    } else if (N % 256 == 0 && M >= 4096) {
+        bn = 256;
+    } else if (N % 128 == 0 || N > 64) {
+        bn = 128;
+    } else {
+        bn = 64;
+    }
+    if (epi.mode == EPI_QKV_ROPE && (bn % 64)) throw Error(9, "QKV epilogue needs 64-column chunks");
+    switch (bn) {
+        case 64: launch<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 128: launch<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 192: launch<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        default: launch<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+    }
+}
+
+// Explicit tile choice, for the kernel tests and tile sweeps.
+void gemm_tf32x3_bn(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                    int kb_per_tap, const Epi& epi, int* err, int bn) {
+    switch (bn) {
+        case 64: launch<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 128: launch<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 192: launch<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 256: launch<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        default: throw Error(13, "unsupported GEMM tile width");
+    }
+}
+
+}  // namespace n3d

@@ -1,0 +1,328 @@
+// Memory-bound and small kernels of the diarization path: LayerNorm, softmax
+// attention, and the fused log-mel front-end.
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+
+#include "n3d_device.cuh"
+#include "n3d_internal.h"
+
+namespace n3d {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------- LayerNorm
+// torch LayerNorm, eps 1e-5, two-pass population variance (src/tensor.rs:97-110).
+// One warp per row, VPL values per lane held in registers (128-bit loads).
+// Writes either a plain fp32 row (out_lo == nullptr) or a TF32 hi/lo pair.
+template <int VPL>
+__global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
+                                  const float* __restrict__ b, float* __restrict__ out, float* __restrict__ out_lo) {
+    constexpr int COLS = VPL * 32;
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* src = x + row * COLS;
+    float v[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; i += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(src + (i / 4) * 128 + lane * 4);
+        v[i] = t.x;
+        v[i + 1] = t.y;
+        v[i + 2] = t.z;
+        v[i + 3] = t.w;
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) s += v[i];
+    const float mean = __fdiv_rn(warp_sum(s), (float)COLS);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const float d = __fsub_rn(v[i], mean);
+        q = __fadd_rn(q, __fmul_rn(d, d));
+    }
+    const float var = __fdiv_rn(warp_sum(q), (float)COLS);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+    float* dst = out + row * COLS;
+    float* dlo = out_lo ? out_lo + row * COLS : nullptr;
+#pragma unroll
+    for (int i = 0; i < VPL; i += 4) {
+        const int c = (i / 4) * 128 + lane * 4;
+        float y[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i + j], mean), inv), w[c + j]), b[c + j]);
+            if (dlo) split_tf32(y[j], y[j], lo[j]);
+        }
+        *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
+        if (dlo) *reinterpret_cast<float4*>(dlo + c) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// ---------------------------------------------------------------- attention
+// Softmax attention over the first valid[b] keys of each sequence
+// (src/encoder.rs:302-329): scores q.k * hd^-1/2, online softmax over key tiles
+// of 32 staged in shared memory, one query row per thread.  qkv is
+// [seqs * seq_stride, 3 * heads * HD] = Q | K | V (Q and K already rotated);
+// ctx is written as a TF32 hi/lo pair [seqs * seq_stride, heads * HD].
+template <int HD>
+__global__ void __launch_bounds__(128) attention_kernel(const float* __restrict__ qkv, int seq_stride,
+                                                        const int* __restrict__ valid_arr, int heads,
+                                                        float* __restrict__ ctx_hi, float* __restrict__ ctx_lo) {
+    constexpr int KT = 32;
+    __shared__ __align__(16) float ks[KT][HD];
+    __shared__ __align__(16) float vs[KT][HD];
+    const int b = blockIdx.z, h = blockIdx.y;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int width = 3 * heads * HD;
+    const int valid = valid_arr[b];
+    const long long base = (long long)b * seq_stride;
+    const bool active = t < seq_stride;
+    const float scaling = 1.0f / sqrtf((float)HD);
+
+    float q[HD], o[HD];
+    if (active) {
+        const float* qr = qkv + (base + t) * width + h * HD;
+#pragma unroll
+        for (int d = 0; d < HD; d += 4) {
+            const float4 v4 = *reinterpret_cast<const float4*>(qr + d);
+            q[d] = v4.x;
+            q[d + 1] = v4.y;
+            q[d + 2] = v4.z;
+            q[d + 3] = v4.w;
+        }
+    }
+#pragma unroll
+    for (int d = 0; d < HD; d++) o[d] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+
+    for (int k0 = 0; k0 < valid; k0 += KT) {
+        const int nk = min(KT, valid - k0);
+        for (int i = threadIdx.x; i < KT * HD / 4; i += blockDim.x) {
+            const int j = i / (HD / 4), d = (i % (HD / 4)) * 4;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (j < nk) {
+                const float* row = qkv + (base + k0 + j) * width;
+                kv = *reinterpret_cast<const float4*>(row + heads * HD + h * HD + d);
+                vv = *reinterpret_cast<const float4*>(row + 2 * heads * HD + h * HD + d);
+            }
+            *reinterpret_cast<float4*>(&ks[j][d]) = kv;
+            *reinterpret_cast<float4*>(&vs[j][d]) = vv;
+        }
+        __syncthreads();
+        if (active) {
+            float s[KT];
+            float mt = m;
+#pragma unroll
+            for (int j = 0; j < KT; j++) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int d = 0; d < HD; d++) acc = fmaf(q[d], ks[j][d], acc);
+                s[j] = j < nk ? acc * scaling : -INFINITY;
+                mt = fmaxf(mt, s[j]);
+            }
+            const float corr = expf(m - mt);
+            l *= corr;
+#pragma unroll
+            for (int d = 0; d < HD; d++) o[d] *= corr;
+#pragma unroll
+            for (int j = 0; j < KT; j++) {
+                const float p = j < nk ? expf(s[j] - mt) : 0.0f;
+                l += p;
+#pragma unroll
+                for (int d = 0; d < HD; d++) o[d] = fmaf(p, vs[j][d], o[d]);
+            }
+            m = mt;
+        }
+        __syncthreads();
+    }
+    if (!active) return;
+    const float inv = valid > 0 ? 1.0f / l : 0.0f;
+    float* dh = ctx_hi + (base + t) * (heads * HD) + h * HD;
+    if (ctx_lo == nullptr) {
+#pragma unroll
+        for (int d = 0; d < HD; d += 4)
+            *reinterpret_cast<float4*>(dh + d) =
+                make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+        return;
+    }
+    float* dl = ctx_lo + (base + t) * (heads * HD) + h * HD;
+#pragma unroll
+    for (int d = 0; d < HD; d += 4) {
+        float hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) split_tf32(o[d + j] * inv, hi[j], lo[j]);
+        *reinterpret_cast<float4*>(dh + d) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(dl + d) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+// ------------------------------------------------------------------- log-mel
+// One CTA of 256 threads per frame: preemphasis on the fly, centred 400-tap
+// Hann in the 512 frame, radix-2 FFT in shared memory, power, sparse slaney
+// filterbank, ln(x + 2^-24) (src/mel.rs:160-225).  The butterflies, twiddles
+// and accumulation order are the CPU restatement's exactly, and every
+// operation is explicitly rounded, so the spectrum is bit-identical to it.
+constexpr int NFFT = 512;
+constexpr int NBINS = NFFT / 2 + 1;
+
+__global__ void __launch_bounds__(256) mel_kernel(const float* __restrict__ audio, const long long* __restrict__ f_base,
+                                                  const int* __restrict__ f_meta, const float* __restrict__ window,
+                                                  const float* __restrict__ twiddle, const float* __restrict__ filters,
+                                                  const int* __restrict__ filt_lo, const int* __restrict__ filt_hi,
+                                                  float preemph, float* __restrict__ mel_hi,
+                                                  float* __restrict__ mel_lo, float* __restrict__ mel_plain,
+                                                  const long long* __restrict__ f_out) {
+    __shared__ float re[NFFT], im[NFFT], pw[NBINS];
+    const long long f = blockIdx.x;
+    const long long base = f_base[f];
+    const int p0 = f_meta[2 * f], n = f_meta[2 * f + 1];
+    const int tid = threadIdx.x;
+    for (int j = tid; j < NFFT; j += 256) {
+        const int p = p0 + j;
+        float x = 0.0f;
+        if (p >= 0 && p < n) {
+            const float cur = audio[base + p];
+            x = p >= 1 ? __fsub_rn(cur, __fmul_rn(preemph, audio[base + p - 1])) : cur;
+        }
+        const int r = __brev(j) >> (32 - 9);
+        re[r] = __fmul_rn(x, window[j]);
+        im[r] = 0.0f;
+    }
+    __syncthreads();
+    for (int half = 1; half < NFFT; half <<= 1) {
+        const int len = half * 2, step = NFFT / len;
+        const int b = tid;  // 256 butterflies per stage
+        const int j = b % half, i = (b / half) * len + j;
+        const float wr = twiddle[2 * (j * step)], wi = twiddle[2 * (j * step) + 1];
+        const float xr = re[i + half], xi = im[i + half];
+        const float vr = __fsub_rn(__fmul_rn(xr, wr), __fmul_rn(xi, wi));
+        const float vi = __fadd_rn(__fmul_rn(xr, wi), __fmul_rn(xi, wr));
+        const float ur = re[i], ui = im[i];
+        re[i] = __fadd_rn(ur, vr);
+        im[i] = __fadd_rn(ui, vi);
+        re[i + half] = __fsub_rn(ur, vr);
+        im[i + half] = __fsub_rn(ui, vi);
+        __syncthreads();
+    }
+    for (int k = tid; k < NBINS; k += 256) pw[k] = __fadd_rn(__fmul_rn(re[k], re[k]), __fmul_rn(im[k], im[k]));
+    __syncthreads();
+    if (tid < 128) {
+        const int m = tid;
+        float acc = 0.0f;
+        for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(filters[m * NBINS + k], pw[k]));
+        const float v = (float)log((double)__fadd_rn(acc, 5.9604645e-8f));
+        const long long o = f_out[f] * 128 + m;
+        float hi, lo;
+        split_tf32(v, hi, lo);
+        mel_hi[o] = hi;
+        mel_lo[o] = lo;
+        if (mel_plain) mel_plain[o] = v;
+    }
+}
+
+__global__ void split_kernel(const float* __restrict__ x, long long n, float* __restrict__ hi,
+                             float* __restrict__ lo) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        split_tf32(x[i], hi[i], lo[i]);
+}
+
+// Packs q | k | v per row; RoPE as src/encoder.rs:281-296 with explicit rounding.
+__global__ void pack_qkv_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                const float* __restrict__ v, long long seq, int heads, int hd,
+                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                float* __restrict__ qkv) {
+    const long long W = (long long)heads * hd;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < seq * W;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / W;
+        const int c = (int)(e % W), d = c % hd, half = hd / 2;
+        float qo = q[e], ko = k[e];
+        if (cos_t) {
+            const float* cs = cos_t + r * hd;
+            const float* sn = sin_t + r * hd;
+            const long long pe = d < half ? e + half : e - half;
+            if (d < half) {
+                qo = __fsub_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
+                ko = __fsub_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
+            } else {
+                qo = __fadd_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
+                ko = __fadd_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
+            }
+        }
+        float* row = qkv + r * 3 * W;
+        row[c] = qo;
+        row[W + c] = ko;
+        row[2 * W + c] = v[e];
+    }
+}
+
+}  // namespace
+
+void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo) {
+    if (n <= 0) return;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+    split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n, hi, lo);
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
+                     int hd, const float* cos_t, const float* sin_t, float* qkv) {
+    const long long n = seq * heads * hd;
+    if (n <= 0) return;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+    pack_qkv_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, hd, cos_t, sin_t, qkv);
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
+                       float* out, float* out_lo) {
+    if (rows <= 0) return;
+    const int warps = 8;
+    const unsigned grid = (unsigned)((rows + warps - 1) / warps);
+    if (cols == 512)
+        layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo);
+    else if (cols == 1024)
+        layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo);
+    else
+        throw Error(13, "layer_norm supports 512 or 1024 columns");
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
+                      int head_dim, float* ctx_hi, float* ctx_lo) {
+    if (seqs <= 0 || seq_stride <= 0) return;
+    dim3 grid((seq_stride + 127) / 128, heads, seqs);
+    if (head_dim == 64)
+        attention_kernel<64><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx_hi, ctx_lo);
+    else if (head_dim == 128)
+        attention_kernel<128><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx_hi, ctx_lo);
+    else
+        throw Error(13, "attention supports head_dim 64 or 128");
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
+                const float* window, const float* twiddle, const float* filters, const int* filt_lo,
+                const int* filt_hi, float preemph, float* mel_hi, float* mel_lo, float* mel_plain,
+                const long long* f_out) {
+    if (n_frames <= 0) return;
+    mel_kernel<<<(unsigned)n_frames, 256, 0, s>>>(audio, f_base, f_meta, window, twiddle, filters, filt_lo, filt_hi,
+                                                  preemph, mel_hi, mel_lo, mel_plain, f_out);
+    N3D_CUDA(cudaGetLastError());
+}
+
+}  // namespace n3d

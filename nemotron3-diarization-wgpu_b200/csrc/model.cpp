@@ -1,0 +1,1053 @@
+// Host runtime of the diarization path: config and checkpoint loading, weight
+// upload, the data-independent chunk schedule, and the batched chunk loop.
+//
+// Mirrors the reference's `Model` (src/model.rs) and `GpuEngine`
+// (src/gpu_engine.rs:238-532) but keeps the whole step on the device: mel,
+// embedder, window assembly, tower, head and speaker cache run as kernels on
+// one stream, and the host only ships audio in and logits out.
+
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+#include "json.h"
+
+namespace n3d {
+
+void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
+void gemm_tf32x3_bn(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                    int kb_per_tap, const Epi& epi, int* err, int bn);
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) throw Error(10 /*N3D_ERR_CUDA*/, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+
+constexpr int kStatusIo = 1, kStatusJson = 2, kStatusSafetensors = 3, kStatusDtype = 4, kStatusMissing = 5,
+              kStatusShape = 6, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11, kStatusNoDevice = 12,
+              kStatusArg = 13;
+
+std::string read_file(const std::string& path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) throw Error(kStatusIo, "io error at " + path + ": cannot open");
+    std::ostringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+const json::Value& need(const json::Value& v, const char* key, const std::string& file) {
+    const json::Value* p = v.get(key);
+    if (!p) throw Error(kStatusJson, "failed to parse " + file + ": missing field `" + key + "`");
+    return *p;
+}
+int need_int(const json::Value& v, const char* key, const std::string& f) { return (int)need(v, key, f).num; }
+double need_num(const json::Value& v, const char* key, const std::string& f) { return need(v, key, f).num; }
+
+// Round to the nearest TF32 (11 significant bits), ties away from zero: the
+// host twin of cvt.rna.tf32.f32.
+float tf32_rna_host(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+// ------------------------------------------------------------- safetensors
+struct Tensor {
+    std::vector<long long> shape;
+    const float* data;
+};
+
+struct SafeTensors {
+    std::string raw;
+    std::map<std::string, Tensor> tensors;
+
+    explicit SafeTensors(const std::string& path) {
+        raw = read_file(path);
+        if (raw.size() < 8) throw Error(kStatusSafetensors, "safetensors error: file too short");
+        uint64_t hlen = 0;
+        std::memcpy(&hlen, raw.data(), 8);
+        if (8 + hlen > raw.size()) throw Error(kStatusSafetensors, "safetensors error: header out of range");
+        json::Value h;
+        try {
+            h = json::parse(raw.substr(8, hlen));
+        } catch (const std::exception& e) {
+            throw Error(kStatusSafetensors, std::string("safetensors error: ") + e.what());
+        }
+        const size_t base = 8 + hlen;
+        for (const auto& kv : h.obj) {
+            if (kv.first == "__metadata__") continue;
+            const json::Value& t = kv.second;
+            const json::Value* dt = t.get("dtype");
+            const json::Value* sh = t.get("shape");
+            const json::Value* off = t.get("data_offsets");
+            if (!dt || !sh || !off || off->arr.size() != 2)
+                throw Error(kStatusSafetensors, "safetensors error: bad entry " + kv.first);
+            if (dt->str != "F32")
+                throw Error(kStatusDtype, "tensor `" + kv.first + "` has dtype " + dt->str + ", this port only reads F32");
+            Tensor tt;
+            long long numel = 1;
+            for (const auto& d : sh->arr) {
+                tt.shape.push_back((long long)d.num);
+                numel *= (long long)d.num;
+            }
+            const size_t s = (size_t)off->arr[0].num, e = (size_t)off->arr[1].num;
+            if (e < s || base + e > raw.size() || (e - s) != (size_t)numel * 4)
+                throw Error(kStatusSafetensors, "safetensors error: bad data offsets for " + kv.first);
+            if ((base + s) % 4) throw Error(kStatusSafetensors, "safetensors error: misaligned tensor " + kv.first);
+            tt.data = reinterpret_cast<const float*>(raw.data() + base + s);
+            tensors[kv.first] = tt;
+        }
+    }
+
+    // Weights::tensor (src/weights.rs:78-93): fetch with a shape check.
+    const float* get(const std::string& name, std::vector<long long> shape) const {
+        auto it = tensors.find(name);
+        if (it == tensors.end()) throw Error(kStatusMissing, "tensor `" + name + "` is missing from the checkpoint");
+        if (it->second.shape != shape) {
+            auto fmt = [](const std::vector<long long>& v) {
+                std::string s = "[";
+                for (size_t i = 0; i < v.size(); i++) s += (i ? ", " : "") + std::to_string(v[i]);
+                return s + "]";
+            };
+            throw Error(kStatusShape,
+                        "tensor `" + name + "` has shape " + fmt(it->second.shape) + ", expected " + fmt(shape));
+        }
+        return it->second.data;
+    }
+};
+
+// ------------------------------------------------------------- mel constants
+// librosa slaney filterbank (src/mel.rs:81-123), f64 math stored as f32.
+double logstep() { return std::log(6.4) / 27.0; }
+double hz_to_mel(double f) {
+    const double f_sp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / f_sp;
+    return f < min_log_hz ? f / f_sp : min_log_mel + std::log(f / min_log_hz) / logstep();
+}
+double mel_to_hz(double m) {
+    const double f_sp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / f_sp;
+    return m < min_log_mel ? f_sp * m : min_log_hz * std::exp(logstep() * (m - min_log_mel));
+}
+std::vector<float> slaney(int n_mels, int n_fft, int sr, double fmin, double fmax) {
+    const int nf = n_fft / 2 + 1;
+    std::vector<double> freqs(nf), mel_f(n_mels + 2);
+    for (int k = 0; k < nf; k++) freqs[k] = (double)k * (double)sr / (double)n_fft;
+    const double lo = hz_to_mel(fmin), hi = hz_to_mel(fmax);
+    for (int i = 0; i < n_mels + 2; i++) mel_f[i] = mel_to_hz(lo + ((double)i / (double)(n_mels + 1)) * (hi - lo));
+    std::vector<float> w((size_t)n_mels * nf);
+    for (int i = 0; i < n_mels; i++) {
+        const double enorm = 2.0 / (mel_f[i + 2] - mel_f[i]);
+        for (int k = 0; k < nf; k++) {
+            const double lower = -(mel_f[i] - freqs[k]) / (mel_f[i + 1] - mel_f[i]);
+            const double upper = (mel_f[i + 2] - freqs[k]) / (mel_f[i + 2] - mel_f[i + 1]);
+            w[(size_t)i * nf + k] = (float)(std::max(std::min(lower, upper), 0.0) * enorm);
+        }
+    }
+    return w;
+}
+
+long long frame_count(const Config& c, long long n, bool centered) {  // src/mel.rs:143-154
+    if (centered) return n / c.hop;
+    return n < c.n_fft ? 0 : (n - c.n_fft) / c.hop + 1;
+}
+
+long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+}  // namespace
+
+// ------------------------------------------------------------------ config
+Config load_config(const std::string& dir) {
+    const std::string fc = dir + "/config.json", fp = dir + "/processor_config.json";
+    json::Value m, p;
+    try {
+        m = json::parse(read_file(fc));
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw Error(kStatusJson, "failed to parse " + fc + ": " + e.what());
+    }
+    try {
+        p = json::parse(read_file(fp));
+    } catch (const Error&) {
+        throw;
+    } catch (const std::exception& e) {
+        throw Error(kStatusJson, "failed to parse " + fp + ": " + e.what());
+    }
+    Config c;
+    const json::Value& a = need(m, "audio_config", fc);
+    c.hidden = need_int(a, "hidden_size", fc);
+    c.layers = need_int(a, "num_hidden_layers", fc);
+    c.heads = need_int(a, "num_attention_heads", fc);
+    c.kv_heads = need_int(a, "num_key_value_heads", fc);
+    c.inter = need_int(a, "intermediate_size", fc);
+    c.n_mels = need_int(a, "num_mel_bins", fc);
+    c.sub = need_int(a, "subsampling_factor", fc);
+    c.rope_theta = need_num(need(a, "rope_parameters", fc), "rope_theta", fc);
+    const json::Value& h = need(m, "head_config", fc);
+    c.head_hidden = need_int(h, "hidden_size", fc);
+    c.num_speakers = need_int(h, "num_speakers", fc);
+    const json::Value& s = need(m, "streaming_config", fc);
+    c.s_fifo = need_int(s, "fifo_length", fc);
+    c.cache_len = need_int(s, "speaker_cache_length", fc);
+    c.n_sil = need_int(s, "speaker_cache_silence_frames_per_speaker", fc);
+    c.s_period = need_int(s, "speaker_cache_update_period", fc);
+    c.thr = (float)need_num(s, "prediction_score_threshold", fc);
+    c.min_pos_rate = (float)need_num(s, "min_positive_scores_rate", fc);
+    c.strong_rate = (float)need_num(s, "strong_boost_rate", fc);
+    c.weak_rate = (float)need_num(s, "weak_boost_rate", fc);
+    c.latest_boost = (float)need_num(s, "latest_frames_score_boost", fc);
+    c.s_sub = need_int(s, "subsampling_factor", fc);
+    c.s_ns = need_int(s, "num_speakers", fc);
+    c.chunk_length = need_int(m, "chunk_length", fc);
+    c.chunk_rc = need_int(m, "chunk_right_context", fc);
+    c.o_fifo = need_int(m, "fifo_length", fc);
+    c.o_period = need_int(m, "speaker_cache_update_period", fc);
+    const json::Value& fe = need(p, "feature_extractor", fp);
+    c.feature_size = need_int(fe, "feature_size", fp);
+    c.n_fft = need_int(fe, "n_fft", fp);
+    c.hop = need_int(fe, "hop_length", fp);
+    c.win = need_int(fe, "win_length", fp);
+    c.sr = need_int(fe, "sampling_rate", fp);
+    c.preemph = (float)need_num(fe, "preemphasis", fp);
+    c.proc_sub = need_int(p, "subsampling_factor", fp);
+    const json::Value& sm = need(p, "streaming_modes", fp);
+    const char* names[3] = {"low_latency", "very_low_latency", "ultra_low_latency"};
+    for (int i = 0; i < 3; i++) {
+        const json::Value& v = need(sm, names[i], fp);
+        if (v.arr.size() != 2) throw Error(kStatusJson, "failed to parse " + fp + ": bad streaming mode");
+        c.modes[i][0] = (int)v.arr[0].num;
+        c.modes[i][1] = (int)v.arr[1].num;
+    }
+    // CacheConfig::from_model (src/streaming.rs:54-72)
+    const int budget = c.cache_len / c.s_ns - c.n_sil;
+    c.min_pos = (int)std::floor((float)budget * c.min_pos_rate);
+    c.k_strong = (int)std::floor((float)budget * c.strong_rate);
+    c.k_weak = (int)std::floor((float)budget * c.weak_rate);
+    // Shapes the kernels are built for.
+    auto unsupported = [&](const std::string& what) {
+        throw Error(kStatusJson, "failed to parse " + fc + ": unsupported " + what);
+    };
+    if (c.hidden != 512 || c.heads * 64 != c.hidden || c.kv_heads != c.heads) unsupported("attention geometry");
+    if (c.inter % 128 || c.n_mels != 128 || c.feature_size != 128 || c.n_fft != 512 || c.win > c.n_fft)
+        unsupported("front-end geometry");
+    if (c.head_hidden != 192 || c.num_speakers > 8 || c.num_speakers != c.s_ns || c.sub != c.proc_sub ||
+        c.sub != c.s_sub || (c.sub * c.n_mels) % 32)
+        unsupported("head geometry");
+    return c;
+}
+
+// ---------------------------------------------------------------- schedule
+namespace {
+
+// SpeakerCache counts only (src/streaming.rs:220-284): data-independent.
+struct CacheSim {
+    int fifo_len, period, cache_len;
+    int ncache = 0, nfifo = 0, compressed = 0;
+    int num_popped(int n) const {  // src/streaming.rs:220-228
+        if (n <= fifo_len) return 0;
+        return std::min(std::max(period, n - fifo_len), n);
+    }
+    void step(StepPlan& sp) {
+        sp.ncache = ncache;
+        sp.nfifo = nfifo;
+        sp.was_compressed = compressed;
+        const int nf = nfifo + sp.nchunk;
+        sp.popped = num_popped(nf);
+        const int ne = ncache + sp.popped;
+        sp.compress = sp.popped > 0 && ne > cache_len;
+        if (sp.popped > 0) {
+            ncache = sp.compress ? cache_len : ne;
+            compressed |= sp.compress;
+        }
+        nfifo = nf - sp.popped;
+    }
+};
+
+}  // namespace
+
+// Model::run_offline_capturing + chunk_loop's Offline arm (src/model.rs:242-310, 485-503).
+ClipPlan plan_offline(const Config& c, long long n) {
+    ClipPlan p;
+    const long long valid = frame_count(c, n, true);
+    const long long groups = ceil_div(valid + 1, c.sub);
+    MelSeg seg{0, n, 1, (int)valid, (int)groups, 0};
+    p.segs.push_back(seg);
+    CacheSim cs{c.o_fifo, c.o_period, c.cache_len};
+    const long long valid_groups = ceil_div(valid, c.sub);  // g * sub < valid
+    for (long long start = 0; start < groups; start += c.chunk_length) {
+        const long long end = std::min(start + (long long)c.chunk_length, groups);
+        const long long hi = std::min(end + (long long)c.chunk_rc, groups);
+        StepPlan sp{};
+        sp.seg = 0;
+        sp.group_lo = (int)start;
+        sp.n_new = (int)(hi - start);
+        sp.nchunk = (int)(end - start);
+        const int prefix = cs.ncache + cs.nfifo;
+        sp.S = prefix + sp.n_new;
+        sp.valid = prefix + (int)std::min(std::max(valid_groups - start, 0LL), hi - start);
+        sp.keep_rows = sp.nchunk * c.sub;
+        cs.step(sp);
+        p.steps.push_back(sp);
+        p.emitted_rows += sp.keep_rows;
+    }
+    p.out_rows = std::min(p.emitted_rows, valid + 1);
+    p.num_chunks = (int)p.steps.size();
+    p.cache_compressed = cs.compressed;
+    p.cache_frames = cs.ncache;
+    p.fifo_frames = cs.nfifo;
+    return p;
+}
+
+// Model::streaming_chunks + run_streaming + chunk_loop's Streaming arm
+// (src/model.rs:313-365, 504-510; geometry from ModeParams::resolve, src/config.rs:152-202).
+ClipPlan plan_streaming(const Config& c, long long n, int mode) {
+    if (mode < 0 || mode > 2) throw Error(kStatusArg, "streaming mode must be low, very low or ultra low latency");
+    const int cl = c.modes[mode][0], rc = c.modes[mode][1];
+    const long long mel_chunk = (long long)(cl + rc) * c.sub, mel_step = (long long)cl * c.sub;
+    const long long first = (mel_chunk - 1) * c.hop + c.win / 2;
+    const long long per_chunk = mel_chunk * c.hop + c.win;
+    ClipPlan p;
+    struct Ch {
+        long long off, len;
+        int centered, la;
+    };
+    std::vector<Ch> chunks;
+    chunks.push_back({0, std::min(first, n), 1, rc});
+    long long mel_idx = mel_step;
+    long long start = mel_idx * c.hop - c.n_fft / 2;
+    while (start + per_chunk <= n) {
+        chunks.push_back({start, per_chunk, 0, rc});
+        mel_idx += mel_step;
+        start = mel_idx * c.hop - c.n_fft / 2;
+    }
+    const long long ls = std::min(start, n);
+    chunks.push_back({ls, n - ls, 1, 0});
+
+    CacheSim cs{c.s_fifo, c.s_period, c.cache_len};
+    for (size_t i = 0; i < chunks.size(); i++) {
+        const Ch& ch = chunks[i];
+        const long long nm = frame_count(c, ch.len, ch.centered != 0);
+        const long long groups = ceil_div(nm, c.sub);
+        if (groups < ch.la)
+            throw Error(kStatusAudio, "unsupported audio: a streaming chunk holds " + std::to_string(groups) +
+                                          " encoder frames, fewer than the look-ahead of " + std::to_string(ch.la));
+        p.segs.push_back(MelSeg{ch.off, ch.len, ch.centered, (int)nm, (int)groups, 0});
+        StepPlan sp{};
+        sp.seg = (int)i;
+        sp.group_lo = 0;
+        sp.n_new = (int)groups;
+        sp.nchunk = (int)(groups - ch.la);
+        const int prefix = cs.ncache + cs.nfifo;
+        sp.S = prefix + sp.n_new;
+        sp.valid = sp.S;
+        sp.keep_rows = (int)std::min((long long)sp.nchunk * c.sub, nm);
+        cs.step(sp);
+        p.steps.push_back(sp);
+        p.emitted_rows += sp.keep_rows;
+    }
+    p.out_rows = p.emitted_rows;
+    p.num_chunks = (int)p.steps.size();
+    p.cache_compressed = cs.compressed;
+    p.cache_frames = cs.ncache;
+    p.fifo_frames = cs.nfifo;
+    return p;
+}
+
+// ------------------------------------------------------------------ model
+
+Model::Model(const std::string& dir, int device) : device_(device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) throw Error(kStatusNoDevice, "no CUDA device is visible");
+    if (device < 0 || device >= n) throw Error(kStatusNoDevice, "CUDA device " + std::to_string(device) + " does not exist");
+    N3D_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop{};
+    N3D_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        throw Error(kStatusGpu, std::string("this build targets sm_100a (B200); device is ") + prop.name);
+    cfg_ = load_config(dir);
+    N3D_CUDA(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
+    stream_ = own_stream_;
+    N3D_CUDA(cudaMalloc(&dev_err_, sizeof(int)));
+    N3D_CUDA(cudaMemset(dev_err_, 0, sizeof(int)));
+    upload_weights(dir);
+}
+
+Model::~Model() {
+    cudaSetDevice(device_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (const ProfRec& r : pending_) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+    for (void* p : owned_) cudaFree(p);
+    for (auto& kv : ws_) cudaFree(kv.second.p);
+    if (dev_err_) cudaFree(dev_err_);
+    if (own_stream_) cudaStreamDestroy(own_stream_);
+}
+
+void Model::set_stream(cudaStream_t s) {
+    N3D_CUDA(cudaSetDevice(device_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    prof_collect();
+    stream_ = s ? s : own_stream_;
+}
+
+void Model::upload_weights(const std::string& dir) {
+    SafeTensors st(dir + "/model.safetensors");
+    const Config& c = cfg_;
+    const long long h = c.hidden, hh = c.head_hidden;
+    auto dev = [&](const std::vector<float>& v) {
+        float* p = nullptr;
+        N3D_CUDA(cudaMalloc(&p, v.size() * 4 + 16));
+        N3D_CUDA(cudaMemcpy(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+        owned_.push_back(p);
+        return p;
+    };
+    auto plain = [&](const std::string& name, std::vector<long long> shape) {
+        const float* d = st.get(name, shape);
+        long long n = 1;
+        for (long long x : shape) n *= x;
+        return dev(std::vector<float>(d, d + n));
+    };
+    auto split = [&](const std::vector<float>& w, int out, int in, const float* bias) {
+        std::vector<float> hi(w.size()), lo(w.size());
+        for (size_t i = 0; i < w.size(); i++) {
+            hi[i] = tf32_rna_host(w[i]);
+            lo[i] = tf32_rna_host(w[i] - hi[i]);
+        }
+        DevLinear L;
+        L.hi = dev(hi);
+        L.lo = dev(lo);
+        L.out = out;
+        L.in = in;
+        if (bias) L.bias = dev(std::vector<float>(bias, bias + out));
+        return L;
+    };
+    auto linear = [&](const std::string& name, int out, int in, const char* bias_name) {
+        const float* w = st.get(name, {out, in});
+        const float* b = bias_name ? st.get(bias_name, {out}) : nullptr;
+        return split(std::vector<float>(w, w + (size_t)out * in), out, in, b);
+    };
+    const std::string P = "model.audio_tower";
+    embed_ = linear(P + ".embedder.projection.weight", (int)h, c.sub * c.n_mels, nullptr);
+    in_ln_w_ = plain(P + ".input_layer_norm.weight", {h});
+    in_ln_b_ = plain(P + ".input_layer_norm.bias", {h});
+    fin_ln_w_ = plain(P + ".layer_norm.weight", {h});
+    fin_ln_b_ = plain(P + ".layer_norm.bias", {h});
+    for (int i = 0; i < c.layers; i++) {
+        const std::string b = P + ".layers." + std::to_string(i);
+        DevLayer L;
+        L.ln1_w = plain(b + ".layer_norm1.weight", {h});
+        L.ln1_b = plain(b + ".layer_norm1.bias", {h});
+        L.ln2_w = plain(b + ".layer_norm2.weight", {h});
+        L.ln2_b = plain(b + ".layer_norm2.bias", {h});
+        // q, k, v stacked row-wise into one [3h, h] weight (src/gpu_engine.rs:263-276)
+        std::vector<float> qkv;
+        qkv.reserve((size_t)3 * h * h);
+        for (const char* nm : {".self_attn.q_proj.weight", ".self_attn.k_proj.weight", ".self_attn.v_proj.weight"}) {
+            const float* w = st.get(b + nm, {h, h});
+            qkv.insert(qkv.end(), w, w + h * h);
+        }
+        L.qkv = split(qkv, (int)(3 * h), (int)h, nullptr);
+        L.o = linear(b + ".self_attn.o_proj.weight", (int)h, (int)h, (b + ".self_attn.o_proj.bias").c_str());
+        L.fc1 = linear(b + ".mlp.fc1.weight", c.inter, (int)h, (b + ".mlp.fc1.bias").c_str());
+        L.fc2 = linear(b + ".mlp.fc2.weight", (int)h, c.inter, (b + ".mlp.fc2.bias").c_str());
+        layers_.push_back(L);
+    }
+    proj_ = linear("model.proj.weight", (int)hh, (int)h, "model.proj.bias");
+    {
+        // Conv1d weight [out, in, 3] -> tap-major [out, 3 * in] so the k=3 conv is
+        // a GEMM over three row-shifted copies of the padded input.
+        const int oc = (int)hh * c.sub;
+        const float* w = st.get("model.upsampler.conv.weight", {oc, hh, 3});
+        const float* b = st.get("model.upsampler.conv.bias", {oc});
+        std::vector<float> r((size_t)oc * 3 * hh);
+        for (int o = 0; o < oc; o++)
+            for (int ic = 0; ic < hh; ic++)
+                for (int j = 0; j < 3; j++) r[(size_t)o * 3 * hh + j * hh + ic] = w[((size_t)o * hh + ic) * 3 + j];
+        conv_ = split(r, oc, (int)(3 * hh), b);
+    }
+    dense_ = linear("classifier.dense.weight", (int)hh, (int)hh, "classifier.dense.bias");
+    out_w_ = plain("classifier.out_proj.weight", {c.num_speakers, hh});
+    out_b_ = plain("classifier.out_proj.bias", {c.num_speakers});
+    silence_ = plain("silence_embeds", {h});
+
+    // front-end constants
+    const int nf = c.n_fft / 2 + 1;
+    std::vector<float> filt = slaney(c.n_mels, c.n_fft, c.sr, 0.0, (double)c.sr / 2.0);
+    std::vector<int> flo(c.n_mels), fhi(c.n_mels);
+    for (int m = 0; m < c.n_mels; m++) {
+        int lo = nf, hi = -1;
+        for (int k = 0; k < nf; k++)
+            if (filt[(size_t)m * nf + k] != 0.0f) {
+                lo = std::min(lo, k);
+                hi = std::max(hi, k);
+            }
+        flo[m] = lo;
+        fhi[m] = hi;
+    }
+    mel_filters_ = dev(filt);
+    auto devi = [&](const std::vector<int>& v) {
+        int* p = nullptr;
+        N3D_CUDA(cudaMalloc(&p, v.size() * 4));
+        N3D_CUDA(cudaMemcpy(p, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+        owned_.push_back(p);
+        return p;
+    };
+    filt_lo_ = devi(flo);
+    filt_hi_ = devi(fhi);
+    // torch.hann_window(win, periodic=False) centred in the n_fft frame (src/mel.rs:43-48, 197-200)
+    std::vector<float> window(c.n_fft, 0.0f);
+    const int left = (c.n_fft - c.win) / 2;
+    const float denom = (float)(c.win - 1);
+    for (int i = 0; i < c.win; i++)
+        window[left + i] = 0.5f * (1.0f - std::cos(2.0f * 3.14159265358979323846f * (float)i / denom));
+    window_ = dev(window);
+    std::vector<float> tw(c.n_fft);
+    for (int k = 0; k < c.n_fft / 2; k++) {
+        const double ang = -2.0 * 3.14159265358979323846 * (double)k / (double)c.n_fft;
+        tw[2 * k] = (float)std::cos(ang);
+        tw[2 * k + 1] = (float)std::sin(ang);
+    }
+    twiddle_ = dev(tw);
+    // RoPE tables for positions 0..s_cap-1 (src/encoder.rs:163-185)
+    const int hd = c.hidden / c.heads, half = hd / 2;
+    std::vector<float> inv(half), cs((size_t)s_cap_ * hd), sn((size_t)s_cap_ * hd);
+    for (int i = 0; i < half; i++) inv[i] = (float)(1.0 / std::pow(c.rope_theta, 2.0 * (double)i / (double)hd));
+    for (int p = 0; p < s_cap_; p++)
+        for (int i = 0; i < half; i++) {
+            const float a = (float)p * inv[i];
+            cs[(size_t)p * hd + i] = cs[(size_t)p * hd + half + i] = std::cos(a);
+            sn[(size_t)p * hd + i] = sn[(size_t)p * hd + half + i] = std::sin(a);
+        }
+    rope_cos_ = dev(cs);
+    rope_sin_ = dev(sn);
+}
+
+void* Model::ws(const char* name, size_t bytes) {
+    bytes = (bytes + 255) & ~size_t(255);
+    if (bytes == 0) bytes = 256;
+    Buf& b = ws_[name];
+    if (b.bytes < bytes) {
+        if (b.p) {
+            N3D_CUDA(cudaStreamSynchronize(stream_));
+            N3D_CUDA(cudaFree(b.p));
+        }
+        b.p = nullptr;
+        N3D_CUDA(cudaMalloc(&b.p, bytes));
+        b.bytes = bytes;
+    }
+    return b.p;
+}
+
+void Model::check_dev_error() {
+    int e = 0;
+    N3D_CUDA(cudaMemcpy(&e, dev_err_, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e != 0) {
+        N3D_CUDA(cudaMemset(dev_err_, 0, sizeof(int)));
+        throw Error(kStatusTimeout, "a device-side wait timed out (site " + std::to_string(e) + ")");
+    }
+}
+
+void Model::profile_enable(bool on) {
+    N3D_CUDA(cudaSetDevice(device_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    prof_collect();
+    prof_ = on;
+    for (auto& t : totals_) t = ProfTotals{};
+}
+
+void Model::prof_begin() {
+    if (!prof_) return;
+    if (event_pool_.size() < 2) {
+        for (int i = 0; i < 64; i++) {
+            cudaEvent_t e;
+            N3D_CUDA(cudaEventCreate(&e));
+            event_pool_.push_back(e);
+        }
+    }
+    cur_begin_ = event_pool_.back();
+    event_pool_.pop_back();
+    N3D_CUDA(cudaEventRecord(cur_begin_, stream_));
+}
+
+void Model::prof_end(int cls, double flops, double bytes) {
+    if (!prof_ || !cur_begin_) return;
+    cudaEvent_t b = event_pool_.back();
+    event_pool_.pop_back();
+    N3D_CUDA(cudaEventRecord(b, stream_));
+    pending_.push_back(ProfRec{cls, cur_begin_, b, flops, bytes});
+    cur_begin_ = nullptr;
+    if (pending_.size() > 4096) {
+        N3D_CUDA(cudaStreamSynchronize(stream_));
+        prof_collect();
+    }
+}
+
+// Resolve recorded event pairs (the stream must be idle).
+void Model::prof_collect() {
+    for (const ProfRec& r : pending_) {
+        float ms = 0.0f;
+        N3D_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+        ProfTotals& t = totals_[r.cls];
+        t.launches++;
+        t.ms += ms;
+        t.flops += r.flops;
+        t.bytes += r.bytes;
+        event_pool_.push_back(r.a);
+        event_pool_.push_back(r.b);
+    }
+    pending_.clear();
+}
+
+// The 31-layer tower on B sequences of stride S rows held in ws "win".
+// Output: the final LayerNorm as a TF32 pair in "n_hi"/"n_lo" (and plain in
+// enc_plain when given).
+void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain) {
+    const Config& c = cfg_;
+    const long long M = (long long)B * S, h = c.hidden;
+    const long long cap = M;
+    float* win = (float*)ws("win", M * h * 4);
+    float* x = (float*)ws("x", M * h * 4);
+    float* n_hi = (float*)ws("n_hi", M * h * 4);
+    float* n_lo = (float*)ws("n_lo", M * h * 4);
+    float* qkv = (float*)ws("qkv", M * 3 * h * 4);
+    float* ctx_hi = (float*)ws("ctx_hi", M * h * 4);
+    float* ctx_lo = (float*)ws("ctx_lo", M * h * 4);
+    float* f_hi = (float*)ws("f_hi", M * c.inter * 4);
+    float* f_lo = (float*)ws("f_lo", M * c.inter * 4);
+    const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_ctx = ws_["ctx_hi"].bytes / (h * 4);
+    const long long rows_f = ws_["f_hi"].bytes / (c.inter * 4);
+    (void)cap;
+    const SplitOperand An{n_hi, n_lo, rows_n, h, h};
+    const SplitOperand Actx{ctx_hi, ctx_lo, rows_ctx, h, h};
+    const SplitOperand Af{f_hi, f_lo, rows_f, c.inter, c.inter};
+
+    const double ln_bytes = (double)M * h * 4 * 3;  // read x, write a TF32 pair
+    prof_begin();
+    launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, x, nullptr);
+    prof_end(K_LN, 0, (double)M * h * 8);
+    for (int l = 0; l < c.layers; l++) {
+        const DevLayer& L = layers_[l];
+        prof_begin();
+        launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
+        prof_end(K_LN, 0, ln_bytes);
+        Epi e;
+        e.mode = EPI_QKV_ROPE;
+        e.out = qkv;
+        e.ldo = 3 * h;
+        e.cos_t = rope_cos_;
+        e.sin_t = rope_sin_;
+        e.rope_seq = S;
+        e.head_dim = (int)(h / c.heads);
+        e.q_cols = (int)h;
+        e.k_cols = (int)h;
+        prof_begin();
+        gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
+        prof_end(K_GEMM, 2.0 * M * 3 * h * h, 0);
+        prof_begin();
+        launch_attention(stream_, qkv, B, S, d_valid, c.heads, (int)(h / c.heads), ctx_hi, ctx_lo);
+        prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
+        Epi eo;
+        eo.mode = EPI_RESID;
+        eo.out = x;
+        eo.ldo = h;
+        eo.bias = L.o.bias;
+        prof_begin();
+        gemm_tf32x3(stream_, Actx, L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
+        prof_end(K_GEMM, 2.0 * M * h * h, 0);
+        prof_begin();
+        launch_layer_norm(stream_, x, M, (int)h, L.ln2_w, L.ln2_b, n_hi, n_lo);
+        prof_end(K_LN, 0, ln_bytes);
+        Epi e1;
+        e1.mode = EPI_GELU_SPLIT;
+        e1.out = f_hi;
+        e1.out_lo = f_lo;
+        e1.ldo = c.inter;
+        e1.bias = L.fc1.bias;
+        prof_begin();
+        gemm_tf32x3(stream_, An, L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
+        prof_end(K_GEMM, 2.0 * M * c.inter * h, 0);
+        Epi e2;
+        e2.mode = EPI_RESID;
+        e2.out = x;
+        e2.ldo = h;
+        e2.bias = L.fc2.bias;
+        prof_begin();
+        gemm_tf32x3(stream_, Af, L.fc2.op(), (int)M, (int)h, c.inter, 0, e2, dev_err_);
+        prof_end(K_GEMM, 2.0 * M * h * c.inter, 0);
+    }
+    prof_begin();
+    launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, n_hi, n_lo);
+    prof_end(K_LN, 0, ln_bytes);
+    if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, enc_plain, nullptr);
+    (void)d_seq_len;
+}
+
+// Classification head (src/head.rs:147-157) on the encoder output in n_hi/n_lo:
+// proj -> implicit-GEMM k=3 conv with the sub-pixel reshape folded into the
+// store -> dense + ReLU + out_proj fused.  Logits land in ws "logits"
+// [B * S * sub, ns].
+void Model::head(int B, int S, const int* d_seq_len) {
+    const Config& c = cfg_;
+    const long long M = (long long)B * S, h = c.hidden, hh = c.head_hidden, up = c.sub;
+    const long long PR = (long long)B * (S + 2);
+    float* n_hi = (float*)ws("n_hi", M * h * 4);
+    float* n_lo = (float*)ws("n_lo", M * h * 4);
+    float* p_hi = (float*)ws("p_hi", PR * hh * 4);
+    float* p_lo = (float*)ws("p_lo", PR * hh * 4);
+    float* u_hi = (float*)ws("u_hi", M * up * hh * 4);
+    float* u_lo = (float*)ws("u_lo", M * up * hh * 4);
+    float* logits = (float*)ws("logits", M * up * 8 * 4);
+    const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_p = ws_["p_hi"].bytes / (hh * 4);
+    const long long rows_u = ws_["u_hi"].bytes / (hh * 4);
+    N3D_CUDA(cudaMemsetAsync(p_hi, 0, PR * hh * 4, stream_));
+    N3D_CUDA(cudaMemsetAsync(p_lo, 0, PR * hh * 4, stream_));
+    Epi ep;
+    ep.mode = EPI_SPLIT;
+    ep.out = p_hi;
+    ep.out_lo = p_lo;
+    ep.ldo = hh;
+    ep.bias = proj_.bias;
+    ep.rdiv = S;
+    ep.rkeep = S;
+    ep.rmul = S + 2;
+    ep.roff = 1;
+    ep.seq_len = d_seq_len;
+    prof_begin();
+    gemm_tf32x3(stream_, SplitOperand{n_hi, n_lo, rows_n, h, h}, proj_.op(), (int)M, (int)hh, (int)h, 0, ep,
+                dev_err_);
+    prof_end(K_GEMM, 2.0 * M * hh * h, 0);
+    Epi ec;
+    ec.mode = EPI_RELU_SPLIT;
+    ec.out = u_hi;
+    ec.out_lo = u_lo;
+    ec.ldo = up * hh;
+    ec.bias = conv_.bias;
+    ec.rdiv = S + 2;
+    ec.rkeep = S;
+    ec.rmul = S;
+    ec.roff = 0;
+    prof_begin();
+    gemm_tf32x3(stream_, SplitOperand{p_hi, p_lo, rows_p, hh, hh}, conv_.op(), (int)(PR - 2), (int)(up * hh),
+                (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
+    prof_end(K_GEMM, 2.0 * M * up * hh * 3 * hh, 0);
+    Epi ed;
+    ed.mode = EPI_DENSE_OUT;
+    ed.out = logits;
+    ed.ldo = c.num_speakers;
+    ed.bias = dense_.bias;
+    ed.w2 = out_w_;
+    ed.b2 = out_b_;
+    ed.n2 = c.num_speakers;
+    prof_begin();
+    gemm_tf32x3(stream_, SplitOperand{u_hi, u_lo, rows_u, hh, hh}, dense_.op(), (int)(M * up), (int)hh, (int)hh, 0,
+                ed, dev_err_);
+    prof_end(K_GEMM, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
+}
+
+void Model::run_batch(int mode, const std::vector<const float*>& host_audio, const float* d_audio_in,
+                      const std::vector<long long>& offsets_in, const std::vector<long long>& lens,
+                      std::vector<std::vector<float>>* host_out, float* d_logits,
+                      const std::vector<long long>* out_offsets, std::vector<ClipPlan>* plans_out) {
+    const Config& c = cfg_;
+    N3D_CUDA(cudaSetDevice(device_));
+    const int nclips = (int)lens.size();
+    std::vector<ClipPlan> plans(nclips);
+    for (int i = 0; i < nclips; i++)
+        plans[i] = mode == 3 ? plan_offline(c, lens[i]) : plan_streaming(c, lens[i], mode);
+    if (plans_out) *plans_out = plans;
+    const int ns = c.num_speakers, h = c.hidden, sub = c.sub;
+    const int B_CAP = 128;
+
+    for (int c0 = 0; c0 < nclips; c0 += B_CAP) {
+        const int c1 = std::min(nclips, c0 + B_CAP), nb = c1 - c0;
+        // ---- audio
+        std::vector<long long> aoff(nb);
+        long long total_samples = 0;
+        const float* d_audio = d_audio_in;
+        if (!d_audio_in) {
+            for (int i = 0; i < nb; i++) {
+                aoff[i] = total_samples;
+                total_samples += lens[c0 + i];
+            }
+            float* buf = (float*)ws("audio", (size_t)std::max(total_samples, 1LL) * 4);
+            for (int i = 0; i < nb; i++)
+                if (lens[c0 + i])
+                    N3D_CUDA(cudaMemcpyAsync(buf + aoff[i], host_audio[c0 + i], lens[c0 + i] * 4,
+                                             cudaMemcpyHostToDevice, stream_));
+            d_audio = buf;
+        } else {
+            for (int i = 0; i < nb; i++) aoff[i] = offsets_in[c0 + i];
+        }
+        // ---- mel segments and frames
+        long long total_groups = 0, total_frames = 0;
+        for (int i = 0; i < nb; i++)
+            for (MelSeg& s : plans[c0 + i].segs) {
+                s.group_base = total_groups;
+                total_groups += s.groups;
+                total_frames += s.frames;
+            }
+        std::vector<long long> f_base(total_frames), f_out(total_frames);
+        std::vector<int> f_meta(2 * total_frames);
+        {
+            long long f = 0;
+            for (int i = 0; i < nb; i++)
+                for (const MelSeg& s : plans[c0 + i].segs)
+                    for (int t = 0; t < s.frames; t++, f++) {
+                        f_base[f] = aoff[i] + s.audio_off;
+                        f_meta[2 * f] = t * c.hop - (s.centered ? c.n_fft / 2 : 0);
+                        f_meta[2 * f + 1] = (int)s.len;
+                        f_out[f] = s.group_base * sub + t;
+                    }
+        }
+        const long long mel_rows = std::max(total_groups * sub, 1LL);
+        float* mel_hi = (float*)ws("mel_hi", mel_rows * c.n_mels * 4);
+        float* mel_lo = (float*)ws("mel_lo", mel_rows * c.n_mels * 4);
+        N3D_CUDA(cudaMemsetAsync(mel_hi, 0, mel_rows * c.n_mels * 4, stream_));
+        N3D_CUDA(cudaMemsetAsync(mel_lo, 0, mel_rows * c.n_mels * 4, stream_));
+        if (total_frames > 0) {
+            long long* d_fb = (long long*)ws("f_base", total_frames * 8);
+            long long* d_fo = (long long*)ws("f_out", total_frames * 8);
+            int* d_fm = (int*)ws("f_meta", total_frames * 8);
+            N3D_CUDA(cudaMemcpyAsync(d_fb, f_base.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+            N3D_CUDA(cudaMemcpyAsync(d_fo, f_out.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+            N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+            prof_begin();
+            launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_,
+                       filt_hi_, c.preemph, mel_hi, mel_lo, nullptr, d_fo);
+            prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
+        }
+        // ---- embedder: one GEMM over every group of every segment
+        const long long K_emb = (long long)sub * c.n_mels;
+        float* embeds = (float*)ws("embeds", std::max(total_groups, 1LL) * h * 4);
+        if (total_groups > 0) {
+            Epi e;
+            e.mode = EPI_STORE;
+            e.out = embeds;
+            e.ldo = h;
+            const long long rows_cap = ws_["mel_hi"].bytes / (K_emb * 4);
+            prof_begin();
+            gemm_tf32x3(stream_, SplitOperand{mel_hi, mel_lo, rows_cap, K_emb, K_emb}, embed_.op(),
+                        (int)total_groups, h, (int)K_emb, 0, e, dev_err_);
+            prof_end(K_GEMM, 2.0 * total_groups * h * K_emb, 0);
+        }
+        // ---- per-clip state and outputs
+        int max_steps = 0;
+        long long out_total = 0;
+        std::vector<long long> out_base(nb);
+        for (int i = 0; i < nb; i++) {
+            max_steps = std::max(max_steps, (int)plans[c0 + i].steps.size());
+            out_base[i] = out_total;
+            out_total += plans[c0 + i].emitted_rows;
+        }
+        const long long pre_rows = s_cap_;
+        float* pre = (float*)ws("pre", (size_t)2 * nb * pre_rows * h * 4);
+        float* cprob = (float*)ws("cprob", (size_t)2 * nb * pre_rows * ns * 4);
+        float* outl = (float*)ws("out_logits", std::max(out_total, 1LL) * ns * 4);
+        // ---- step table (all steps, compact per step)
+        std::vector<SeqStep> table;
+        std::vector<int> seq_len, valid;
+        std::vector<int> step_first(max_steps + 1), step_S(max_steps);
+        std::vector<long long> out_cursor(out_base);
+        for (int w = 0; w < max_steps; w++) {
+            step_first[w] = (int)table.size();
+            int Smax = 0;
+            for (int i = 0; i < nb; i++) {
+                const ClipPlan& p = plans[c0 + i];
+                if (w >= (int)p.steps.size()) continue;
+                const StepPlan& sp = p.steps[w];
+                if (sp.S == 0) continue;  // an empty final chunk changes nothing
+                SeqStep q{};
+                q.S = sp.S;
+                q.valid = sp.valid;
+                q.ncache = sp.ncache;
+                q.nfifo = sp.nfifo;
+                q.nchunk = sp.nchunk;
+                q.popped = sp.popped;
+                q.compress = sp.compress;
+                q.was_compressed = sp.was_compressed;
+                q.keep_rows = sp.keep_rows;
+                q.emb_row = p.segs[sp.seg].group_base + sp.group_lo;
+                const int cur = w & 1, nxt = cur ^ 1;
+                q.pre_in = pre + ((size_t)cur * nb + i) * pre_rows * h;
+                q.pre_out = pre + ((size_t)nxt * nb + i) * pre_rows * h;
+                q.cp_in = cprob + ((size_t)cur * nb + i) * pre_rows * ns;
+                q.cp_out = cprob + ((size_t)nxt * nb + i) * pre_rows * ns;
+                q.out_logits = outl + out_cursor[i] * ns;
+                out_cursor[i] += sp.keep_rows;
+                if (sp.S > s_cap_) throw Error(kStatusGpu, "window of " + std::to_string(sp.S) + " frames exceeds 1024");
+                table.push_back(q);
+                seq_len.push_back(sp.S);
+                valid.push_back(sp.valid);
+                Smax = std::max(Smax, sp.S);
+            }
+            step_S[w] = Smax;
+        }
+        step_first[max_steps] = (int)table.size();
+        // Clips whose plans skip a step (S == 0) must still carry state forward:
+        // that can only happen on a final empty chunk, after which nothing reads it.
+        if (!table.empty()) {
+            SeqStep* d_table = (SeqStep*)ws("steps", table.size() * sizeof(SeqStep));
+            int* d_len = (int*)ws("seq_len", table.size() * 4);
+            int* d_valid = (int*)ws("valid", table.size() * 4);
+            N3D_CUDA(cudaMemcpyAsync(d_table, table.data(), table.size() * sizeof(SeqStep), cudaMemcpyHostToDevice,
+                                     stream_));
+            N3D_CUDA(cudaMemcpyAsync(d_len, seq_len.data(), seq_len.size() * 4, cudaMemcpyHostToDevice, stream_));
+            N3D_CUDA(cudaMemcpyAsync(d_valid, valid.data(), valid.size() * 4, cudaMemcpyHostToDevice, stream_));
+            CacheConst cc{h, ns, sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr, c.latest_boost};
+            for (int w = 0; w < max_steps; w++) {
+                const int B = step_first[w + 1] - step_first[w];
+                if (B == 0) continue;
+                const int S = step_S[w];
+                const SeqStep* d_st = d_table + step_first[w];
+                float* win = (float*)ws("win", (size_t)B * S * h * 4);
+                prof_begin();
+                launch_assemble(stream_, d_st, B, embeds, win, S, h);
+                prof_end(K_ASSEMBLE, 0, 2.0 * B * S * h * 4);
+                tower(B, S, d_len + step_first[w], d_valid + step_first[w], nullptr);
+                head(B, S, d_len + step_first[w]);
+                prof_begin();
+                launch_cache_update(stream_, d_st, B, (float*)ws("win", 0), (float*)ws("logits", 0), S, cc,
+                                    silence_);
+                prof_end(K_CACHE, 0, 0);
+            }
+        }
+        // ---- results
+        if (host_out) {
+            std::vector<float> all((size_t)out_total * ns);
+            if (out_total)
+                N3D_CUDA(cudaMemcpyAsync(all.data(), outl, out_total * ns * 4, cudaMemcpyDeviceToHost, stream_));
+            N3D_CUDA(cudaStreamSynchronize(stream_));
+            for (int i = 0; i < nb; i++) {
+                const ClipPlan& p = plans[c0 + i];
+                (*host_out)[c0 + i].assign(all.begin() + out_base[i] * ns,
+                                           all.begin() + (out_base[i] + p.out_rows) * ns);
+            }
+        } else {
+            for (int i = 0; i < nb; i++) {
+                const ClipPlan& p = plans[c0 + i];
+                if (p.out_rows)
+                    N3D_CUDA(cudaMemcpyAsync(d_logits + (*out_offsets)[c0 + i] * ns, outl + out_base[i] * ns,
+                                             p.out_rows * ns * 4, cudaMemcpyDeviceToDevice, stream_));
+            }
+            N3D_CUDA(cudaStreamSynchronize(stream_));
+        }
+        prof_collect();
+        check_dev_error();
+    }
+}
+
+// ------------------------------------------------------------ stage APIs
+
+int Model::log_mel(const float* samples, long long n, bool centered, std::vector<float>& out) {
+    const Config& c = cfg_;
+    N3D_CUDA(cudaSetDevice(device_));
+    const long long frames = frame_count(c, n, centered);
+    out.assign((size_t)frames * c.n_mels, 0.0f);
+    if (frames == 0) return 0;
+    float* a = (float*)ws("audio", n * 4);
+    N3D_CUDA(cudaMemcpyAsync(a, samples, n * 4, cudaMemcpyHostToDevice, stream_));
+    std::vector<long long> fb(frames, 0), fo(frames);
+    std::vector<int> fm(2 * frames);
+    for (long long t = 0; t < frames; t++) {
+        fm[2 * t] = (int)(t * c.hop - (centered ? c.n_fft / 2 : 0));
+        fm[2 * t + 1] = (int)n;
+        fo[t] = t;
+    }
+    long long* d_fb = (long long*)ws("f_base", frames * 8);
+    long long* d_fo = (long long*)ws("f_out", frames * 8);
+    int* d_fm = (int*)ws("f_meta", frames * 8);
+    float* hi = (float*)ws("mel_hi", frames * c.n_mels * 4);
+    float* lo = (float*)ws("mel_lo", frames * c.n_mels * 4);
+    float* pl = (float*)ws("mel_plain", frames * c.n_mels * 4);
+    N3D_CUDA(cudaMemcpyAsync(d_fb, fb.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
+    N3D_CUDA(cudaMemcpyAsync(d_fo, fo.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
+    N3D_CUDA(cudaMemcpyAsync(d_fm, fm.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
+    launch_mel(stream_, a, d_fb, d_fm, frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph, hi, lo,
+               pl, d_fo);
+    N3D_CUDA(cudaMemcpyAsync(out.data(), pl, frames * c.n_mels * 4, cudaMemcpyDeviceToHost, stream_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    return (int)frames;
+}
+
+void Model::embed_range(const float* mel, long long num_frames, long long lo, long long hi, float* out) {
+    const Config& c = cfg_;
+    N3D_CUDA(cudaSetDevice(device_));
+    const long long groups = hi - lo, K = (long long)c.sub * c.n_mels;
+    if (groups <= 0) return;
+    std::vector<float> buf((size_t)groups * K, 0.0f);
+    const long long end = std::min(hi * c.sub, num_frames);
+    if (lo * c.sub < end) std::memcpy(buf.data(), mel + lo * c.sub * c.n_mels, (end - lo * c.sub) * c.n_mels * 4);
+    float* plain = (float*)ws("stage_in", groups * K * 4);
+    float* shi = (float*)ws("mel_hi", groups * K * 4);
+    float* slo = (float*)ws("mel_lo", groups * K * 4);
+    float* o = (float*)ws("embeds", groups * c.hidden * 4);
+    N3D_CUDA(cudaMemcpyAsync(plain, buf.data(), groups * K * 4, cudaMemcpyHostToDevice, stream_));
+    launch_split(stream_, plain, groups * K, shi, slo);
+    Epi e;
+    e.mode = EPI_STORE;
+    e.out = o;
+    e.ldo = c.hidden;
+    gemm_tf32x3(stream_, SplitOperand{shi, slo, (long long)(ws_["mel_hi"].bytes / (K * 4)), K, K}, embed_.op(),
+                (int)groups, c.hidden, (int)K, 0, e, dev_err_);
+    N3D_CUDA(cudaMemcpyAsync(out, o, groups * c.hidden * 4, cudaMemcpyDeviceToHost, stream_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    check_dev_error();
+}
+
+void Model::forward_window(const float* embeds, int frames, int valid, float* enc_out, float* logits) {
+    const Config& c = cfg_;
+    N3D_CUDA(cudaSetDevice(device_));
+    if (frames <= 0 || frames > s_cap_)
+        throw Error(kStatusGpu, "seq " + std::to_string(frames) + " outside 1..=1024");
+    valid = std::min(valid, frames);
+    const long long M = frames, h = c.hidden;
+    float* win = (float*)ws("win", M * h * 4);
+    N3D_CUDA(cudaMemcpyAsync(win, embeds, M * h * 4, cudaMemcpyHostToDevice, stream_));
+    int* d_len = (int*)ws("seq_len", 4);
+    int* d_valid = (int*)ws("valid", 4);
+    N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
+    N3D_CUDA(cudaMemcpyAsync(d_valid, &valid, 4, cudaMemcpyHostToDevice, stream_));
+    float* enc = enc_out ? (float*)ws("enc_plain", M * h * 4) : nullptr;
+    tower(1, frames, d_len, d_valid, enc);
+    if (enc_out) N3D_CUDA(cudaMemcpyAsync(enc_out, enc, M * h * 4, cudaMemcpyDeviceToHost, stream_));
+    if (logits) {
+        head(1, frames, d_len);
+        N3D_CUDA(cudaMemcpyAsync(logits, ws("logits", 0), M * c.sub * c.num_speakers * 4, cudaMemcpyDeviceToHost,
+                                 stream_));
+    }
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    check_dev_error();
+}
+
+void Model::head_forward(const float* enc, int frames, float* logits) {
+    const Config& c = cfg_;
+    N3D_CUDA(cudaSetDevice(device_));
+    if (frames <= 0 || frames > s_cap_)
+        throw Error(kStatusGpu, "head frames " + std::to_string(frames) + " outside 1..=1024");
+    const long long M = frames, h = c.hidden;
+    float* plain = (float*)ws("enc_plain", M * h * 4);
+    float* n_hi = (float*)ws("n_hi", M * h * 4);
+    float* n_lo = (float*)ws("n_lo", M * h * 4);
+    N3D_CUDA(cudaMemcpyAsync(plain, enc, M * h * 4, cudaMemcpyHostToDevice, stream_));
+    launch_split(stream_, plain, M * h, n_hi, n_lo);
+    int* d_len = (int*)ws("seq_len", 4);
+    N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
+    head(1, frames, d_len);
+    N3D_CUDA(cudaMemcpyAsync(logits, ws("logits", 0), M * c.sub * c.num_speakers * 4, cudaMemcpyDeviceToHost,
+                             stream_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    check_dev_error();
+}
+
+}  // namespace n3d

@@ -1,0 +1,165 @@
+// Host-side model: configuration, device weights, workspace and the batched
+// chunk-loop runner behind the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "n3d_cache.h"
+#include "n3d_internal.h"
+
+namespace n3d {
+
+// ----------------------------------------------------------------- config
+
+// config.json + processor_config.json, the fields src/config.rs:43-131 reads.
+struct Config {
+    int hidden = 0, layers = 0, heads = 0, kv_heads = 0, inter = 0, n_mels = 0, sub = 0;
+    double rope_theta = 10000.0;
+    int head_hidden = 0, num_speakers = 0;
+    // streaming_config
+    int s_fifo = 0, cache_len = 0, n_sil = 0, s_period = 0, s_sub = 0, s_ns = 0;
+    float thr = 0, min_pos_rate = 0, strong_rate = 0, weak_rate = 0, latest_boost = 0;
+    // offline chunking
+    int chunk_length = 0, chunk_rc = 0, o_fifo = 0, o_period = 0;
+    // feature extractor
+    int feature_size = 0, n_fft = 0, hop = 0, win = 0, sr = 0;
+    float preemph = 0;
+    int proc_sub = 0;
+    int modes[3][2] = {{0, 0}, {0, 0}, {0, 0}};
+    // CacheConfig::from_model derived counts (src/streaming.rs:54-72)
+    int min_pos = 0, k_strong = 0, k_weak = 0;
+};
+
+Config load_config(const std::string& dir);
+
+// ----------------------------------------------------------------- weights
+
+// A linear layer's weight [out, in] as a TF32 hi/lo pair plus optional bias.
+struct DevLinear {
+    float* hi = nullptr;
+    float* lo = nullptr;
+    float* bias = nullptr;
+    int out = 0, in = 0;
+    SplitOperand op() const { return SplitOperand{hi, lo, out, in, in}; }
+};
+
+struct DevLayer {
+    float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
+    DevLinear qkv, o, fc1, fc2;
+};
+
+// ----------------------------------------------------------------- schedule
+
+struct MelSeg {           // one log_mel call of the reference
+    long long audio_off;  // within the clip
+    long long len;
+    int centered;
+    int frames;           // frame_count(len)
+    int groups;           // ceil(mel rows / sub); mel rows are padded with zeros to groups * sub
+    long long group_base; // global row in the [groups, sub * n_mels] view (set at batch assembly)
+};
+
+struct StepPlan {
+    int S, valid, ncache, nfifo, nchunk, popped, compress, was_compressed, keep_rows;
+    int seg;              // mel segment holding this step's new frames
+    int group_lo;         // first new group within that segment
+    int n_new;            // new embedding rows
+};
+
+struct ClipPlan {
+    std::vector<MelSeg> segs;
+    std::vector<StepPlan> steps;
+    long long emitted_rows = 0;  // 10 ms rows written by the steps
+    long long out_rows = 0;      // rows returned (offline truncates to valid + 1)
+    int num_chunks = 0, cache_compressed = 0, cache_frames = 0, fifo_frames = 0;
+};
+
+ClipPlan plan_offline(const Config& c, long long n);
+ClipPlan plan_streaming(const Config& c, long long n, int mode);
+
+// ----------------------------------------------------------------- model
+
+struct Buf {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+// Per-kernel-class device time, measured with CUDA events on the model's stream.
+enum KernelClass : int { K_GEMM = 0, K_ATTN, K_LN, K_MEL, K_CACHE, K_ASSEMBLE, K_OTHER, K_NCLASS };
+struct ProfTotals {
+    long long launches = 0;
+    double ms = 0.0, flops = 0.0, bytes = 0.0;
+};
+
+class Model {
+  public:
+    Model(const std::string& dir, int device);
+    ~Model();
+
+    const Config& cfg() const { return cfg_; }
+    int device() const { return device_; }
+
+    // Batched chunk loop over independent clips (offline mode = 3).  Host or
+    // device audio; results either copied to host vectors or left in d_logits.
+    void run_batch(int mode, const std::vector<const float*>& host_audio, const float* d_audio,
+                   const std::vector<long long>& offsets, const std::vector<long long>& lens,
+                   std::vector<std::vector<float>>* host_out, float* d_logits,
+                   const std::vector<long long>* out_offsets, std::vector<ClipPlan>* plans_out);
+
+    // Stage entry points (single sequence, host buffers).
+    int log_mel(const float* samples, long long n, bool centered, std::vector<float>& out);
+    void embed_range(const float* mel, long long num_frames, long long lo, long long hi, float* out);
+    void forward_window(const float* embeds, int frames, int valid, float* enc_out, float* logits);
+    void head_forward(const float* enc, int frames, float* logits);
+
+    // Work runs on `s` (caller-owned) or, for nullptr, on the model's own stream.
+    void set_stream(cudaStream_t s);
+
+    // Profiling of the launches of run_batch (off by default).
+    void profile_enable(bool on);
+    const ProfTotals* profile_totals() const { return totals_; }
+
+  private:
+    void prof_begin();
+    void prof_end(int cls, double flops, double bytes);
+    void prof_collect();
+    void upload_weights(const std::string& dir);
+    void tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain);
+    void head(int B, int S, const int* d_seq_len);
+    void* ws(const char* name, size_t bytes);
+    void check_dev_error();
+
+    Config cfg_;
+    int device_ = 0;
+    cudaStream_t stream_ = nullptr;
+    cudaStream_t own_stream_ = nullptr;
+    int* dev_err_ = nullptr;
+
+    DevLinear embed_, proj_, conv_, dense_;
+    std::vector<DevLayer> layers_;
+    float *in_ln_w_, *in_ln_b_, *fin_ln_w_, *fin_ln_b_;
+    float *out_w_, *out_b_, *silence_;
+    float *mel_filters_, *window_, *twiddle_;
+    int *filt_lo_, *filt_hi_;
+    float *rope_cos_, *rope_sin_;
+    int s_cap_ = 1024;  // MAX_SEQ, src/gpu_engine.rs:12
+    std::vector<void*> owned_;
+    bool prof_ = false;
+    struct ProfRec {
+        int cls;
+        cudaEvent_t a, b;
+        double flops, bytes;
+    };
+    std::vector<ProfRec> pending_;
+    std::vector<cudaEvent_t> event_pool_;
+    cudaEvent_t cur_begin_ = nullptr;
+    ProfTotals totals_[K_NCLASS];
+    std::map<std::string, Buf> ws_;
+};
+
+}  // namespace n3d

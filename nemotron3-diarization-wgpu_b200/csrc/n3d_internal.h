@@ -1,0 +1,91 @@
+// Internal host/device interfaces of the diarization path (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace n3d {
+
+// Error carrying an n3d_status code (include/n3d.h) up to the C ABI.
+struct Error : std::runtime_error {
+    int status;
+    Error(int s, const std::string& m) : std::runtime_error(m), status(s) {}
+};
+
+void cuda_check(cudaError_t e, const char* what);
+#define N3D_CUDA(x) ::n3d::cuda_check((x), #x)
+
+// ------------------------------------------------------------------ GEMM
+
+// Epilogue applied to each 128 x BN accumulator tile of C = A * B^T.
+enum EpiMode : int {
+    EPI_STORE = 0,       // out[r, c] = acc + bias                     (fp32)
+    EPI_SPLIT = 1,       // (out, out_lo) = split(acc + bias)          (TF32 hi/lo pair)
+    EPI_GELU_SPLIT = 2,  // split(gelu(acc + bias))
+    EPI_RESID = 3,       // out[r, c] += acc + bias                    (residual stream, in place)
+    EPI_RELU_SPLIT = 4,  // split(relu(acc + bias))
+    EPI_QKV_ROPE = 5,    // Q,K columns rotated by RoPE, V as is; fp32 out
+    EPI_DENSE_OUT = 6,   // r = relu(acc + bias); out[r, 0:ns] = r . w2^T + b2
+};
+
+struct Epi {
+    int mode = EPI_STORE;
+    const float* bias = nullptr;
+    float* out = nullptr;
+    float* out_lo = nullptr;
+    long long ldo = 0;
+    // Row remap: q = r / rdiv, t = r % rdiv; rows with t >= rkeep are skipped;
+    // the output row is q * rmul + t + roff.
+    int rdiv = 0x7fffffff, rkeep = 0x7fffffff;
+    long long rmul = 0, roff = 0;
+    // Rows with t >= seq_len[q] are written as zeros (needs rdiv = sequence stride).
+    const int* seq_len = nullptr;
+    // RoPE tables [max_pos, head_dim]; position = r % rope_seq.
+    const float* cos_t = nullptr;
+    const float* sin_t = nullptr;
+    int rope_seq = 1;
+    int head_dim = 64;
+    int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
+    // EPI_DENSE_OUT second projection
+    const float* w2 = nullptr;
+    const float* b2 = nullptr;
+    int n2 = 0;
+};
+
+// A K-major fp32 operand stored as a TF32 hi/lo pair, [rows, cols] with row stride ld.
+struct SplitOperand {
+    const float* hi = nullptr;
+    const float* lo = nullptr;
+    long long rows = 0, cols = 0, ld = 0;
+};
+
+// C[M, N] = A[M, K] * B[N, K]^T in 3xTF32 on tcgen05. `kb_per_tap` > 0 turns on
+// the shifted-row (implicit k=3 conv) mode: k-block kb reads A at column
+// (kb % kb_per_tap) * 32 and row m0 + kb / kb_per_tap.
+void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                 int kb_per_tap, const Epi& epi, int* dev_err);
+
+// --------------------------------------------------------------- other kernels
+void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
+                       float* out, float* out_lo);
+void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
+                      int head_dim, float* ctx_hi, float* ctx_lo);
+// Log-mel frames: frame f reads audio[f_base[f] + p] for p in [p0, p0 + n_fft) with
+// p0 = f_meta[2f] and the clip length f_meta[2f+1] (zeros outside [0, len)), and
+// writes row f_out[f] of the [rows, 128] mel outputs (TF32 pair, plain optional).
+void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
+                const float* window, const float* twiddle, const float* filters, const int* filt_lo,
+                const int* filt_hi, float preemph, float* mel_hi, float* mel_lo, float* mel_plain,
+                const long long* f_out);
+// x -> (hi, lo) TF32 pair, elementwise.
+void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
+// q, k, v [seq, heads*hd] -> qkv [seq, 3*heads*hd] with RoPE applied to q and k when cos_t != nullptr.
+void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
+                     int hd, const float* cos_t, const float* sin_t, float* qkv);
+
+}  // namespace n3d

@@ -1,0 +1,320 @@
+"""Python binding of the C ABI (include/n3d.h) over libn3d.so.
+
+It mirrors the reference crate's public API (src/lib.rs:45-64) so callers and
+tests read like the reference's own code:
+
+    model = Model.load_gpu(checkpoint_dir)          # Model::load_gpu
+    out = model.run_offline(samples)                # Model::run_offline
+    out = model.run_streaming(samples, "ultra_low_latency")
+    segs = extract_speaker_dict(out.logits, out.num_frames, model.num_speakers, 0.01)
+
+There is no CPU fallback: if libn3d.so is missing or no B200 is visible the
+calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libn3d.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "n3d.h")
+
+MODES = {"low_latency": 0, "very_low_latency": 1, "ultra_low_latency": 2, "offline": 3}
+STATUS = {0: "OK", 1: "Io", 2: "Json", 3: "Safetensors", 4: "TensorDtype", 5: "MissingTensor", 6: "TensorShape",
+          7: "UnsupportedAudio", 8: "Npy", 9: "Gpu", 10: "Cuda", 11: "Timeout", 12: "NoDevice",
+          13: "InvalidArgument"}
+
+_sz = C.c_size_t
+_fp = C.POINTER(C.c_float)
+
+
+class DiarizationError(RuntimeError):
+    """A non-OK n3d_status; `.kind` names the DiarizationError variant (src/error.rs:7-45)."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        self.kind = STATUS.get(status, str(status))
+        super().__init__(f"{self.kind}: {message}")
+
+
+class _RunOutput(C.Structure):
+    _fields_ = [("logits", _fp), ("num_frames", _sz), ("num_speakers", _sz), ("num_chunks", _sz),
+                ("cache_compressed", C.c_int), ("cache_frames", _sz), ("fifo_frames", _sz)]
+
+
+class _Segment(C.Structure):
+    _fields_ = [("start", C.c_float), ("end", C.c_float), ("speaker", _sz)]
+
+
+class _KernelStats(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("launches", _sz), ("ms", C.c_double), ("flops", C.c_double),
+                ("bytes", C.c_double)]
+
+
+@dataclass
+class RunOutput:
+    """RunOutput (src/model.rs:43-53)."""
+    logits: np.ndarray  # [num_frames, num_speakers]
+    num_frames: int
+    num_chunks: int
+    cache_compressed: bool
+    cache_frames: int
+    fifo_frames: int
+
+
+@dataclass(frozen=True)
+class Segment:
+    start: float
+    end: float
+    speaker: int
+
+
+def build() -> str:
+    """Compile libn3d.so for sm_100a with the Makefile beside this file."""
+    subprocess.run(["make", "-s", "-C", HERE, "-j8"], check=True)
+    return LIB_PATH
+
+
+def header_functions() -> list[str]:
+    """Names of every function include/n3d.h declares."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(n3d_[a-z_0-9]+)\s*\(", src)))
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise OSError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` (no CPU fallback exists)")
+    L = C.CDLL(LIB_PATH)
+    vp, fpp = C.c_void_p, _fp
+    sig = {
+        "n3d_model_load_gpu": ([C.c_char_p, C.c_int, C.POINTER(vp)], C.c_int),
+        "n3d_model_free": ([vp], None),
+        "n3d_model_set_stream": ([vp, vp], C.c_int),
+        "n3d_num_speakers": ([vp], _sz),
+        "n3d_hidden_size": ([vp], _sz),
+        "n3d_run_offline": ([vp, fpp, _sz, C.POINTER(_RunOutput)], C.c_int),
+        "n3d_run_streaming": ([vp, fpp, _sz, C.c_int, C.POINTER(_RunOutput)], C.c_int),
+        "n3d_run_output_free": ([C.POINTER(_RunOutput)], None),
+        "n3d_run_batch": ([vp, C.c_int, C.POINTER(fpp), C.POINTER(_sz), _sz, C.POINTER(_RunOutput)], C.c_int),
+        "n3d_batch_out_frames": ([vp, C.c_int, C.POINTER(_sz), _sz, C.POINTER(_sz)], C.c_int),
+        "n3d_run_batch_device": ([vp, C.c_int, vp, C.POINTER(_sz), C.POINTER(_sz), _sz, vp, C.POINTER(_sz)],
+                                 C.c_int),
+        "n3d_log_mel": ([vp, fpp, _sz, C.c_int, fpp, _sz, C.POINTER(_sz)], C.c_int),
+        "n3d_embed_range": ([vp, fpp, _sz, _sz, _sz, fpp], C.c_int),
+        "n3d_forward_embeds": ([vp, fpp, _sz, _sz, fpp], C.c_int),
+        "n3d_head_forward": ([vp, fpp, _sz, fpp], C.c_int),
+        "n3d_forward_window": ([vp, fpp, _sz, _sz, fpp], C.c_int),
+        "n3d_extract_speaker_dict": ([fpp, _sz, _sz, C.c_float, vp, C.c_float, C.POINTER(C.POINTER(_Segment)),
+                                      C.POINTER(_sz)], C.c_int),
+        "n3d_segments_free": ([C.POINTER(_Segment)], None),
+        "n3d_activity_stats": ([fpp, _sz, _sz, vp, C.c_float, C.POINTER(_sz)], C.c_float),
+        "n3d_frame_duration": ([_sz, C.c_uint32], C.c_float),
+        "n3d_linear": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp], C.c_int),
+        "n3d_layer_norm": ([C.c_int, vp, _sz, _sz, vp, vp, vp], C.c_int),
+        "n3d_attention": ([C.c_int, vp, vp, vp, _sz, _sz, _sz, _sz, C.c_int, C.c_double, vp], C.c_int),
+        "n3d_profile_enable": ([vp, C.c_int], C.c_int),
+        "n3d_profile_read": ([vp, C.POINTER(_KernelStats), _sz], _sz),
+        "n3d_last_error": ([], C.c_char_p),
+        "n3d_version": ([], C.c_char_p),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        raise DiarizationError(status, lib().n3d_last_error().decode())
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(_fp)
+
+
+def _collect(o: _RunOutput) -> RunOutput:
+    n = o.num_frames * o.num_speakers
+    logits = np.ctypeslib.as_array(o.logits, shape=(n,)).copy() if n else np.zeros(0, np.float32)
+    res = RunOutput(logits.reshape(o.num_frames, o.num_speakers), int(o.num_frames), int(o.num_chunks),
+                    bool(o.cache_compressed), int(o.cache_frames), int(o.fifo_frames))
+    lib().n3d_run_output_free(C.byref(o))
+    return res
+
+
+class Model:
+    """The reference `Model` (src/model.rs:128-365) on a B200."""
+
+    def __init__(self, handle: int, device: int):
+        self._h = C.c_void_p(handle)
+        self.device = device
+
+    @classmethod
+    def load_gpu(cls, directory: str, device: int = 0) -> "Model":
+        h = C.c_void_p()
+        _check(lib().n3d_model_load_gpu(directory.encode(), device, C.byref(h)))
+        return cls(h.value, device)
+
+    def close(self) -> None:
+        if self._h:
+            lib().n3d_model_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream_handle: int | None) -> None:
+        """Run on a caller-owned cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream)."""
+        _check(lib().n3d_model_set_stream(self._h, C.c_void_p(stream_handle) if stream_handle else None))
+
+    @property
+    def num_speakers(self) -> int:
+        return lib().n3d_num_speakers(self._h)
+
+    @property
+    def hidden_size(self) -> int:
+        return lib().n3d_hidden_size(self._h)
+
+    def run_offline(self, samples) -> RunOutput:
+        s = _f32(samples)
+        o = _RunOutput()
+        _check(lib().n3d_run_offline(self._h, _ptr(s), s.size, C.byref(o)))
+        return _collect(o)
+
+    def run_streaming(self, samples, mode: str) -> RunOutput:
+        s = _f32(samples)
+        o = _RunOutput()
+        _check(lib().n3d_run_streaming(self._h, _ptr(s), s.size, MODES[mode], C.byref(o)))
+        return _collect(o)
+
+    def run_batch(self, clips, mode: str = "offline") -> list[RunOutput]:
+        arrs = [_f32(c) for c in clips]
+        n = len(arrs)
+        ptrs = (_fp * max(n, 1))(*[_ptr(a) for a in arrs])
+        lens = (_sz * max(n, 1))(*[a.size for a in arrs])
+        outs = (_RunOutput * max(n, 1))()
+        _check(lib().n3d_run_batch(self._h, MODES[mode], ptrs, lens, n, outs))
+        return [_collect(outs[i]) for i in range(n)]
+
+    def batch_out_frames(self, lens, mode: str = "offline") -> list[int]:
+        n = len(lens)
+        arr = (_sz * max(n, 1))(*lens)
+        out = (_sz * max(n, 1))()
+        _check(lib().n3d_batch_out_frames(self._h, MODES[mode], arr, n, out))
+        return [int(out[i]) for i in range(n)]
+
+    def run_batch_device(self, mode: str, d_audio: int, offsets, lens, d_logits: int, out_offsets) -> None:
+        n = len(lens)
+        _check(lib().n3d_run_batch_device(self._h, MODES[mode], C.c_void_p(d_audio), (_sz * max(n, 1))(*offsets),
+                                          (_sz * max(n, 1))(*lens), n, C.c_void_p(d_logits),
+                                          (_sz * max(n, 1))(*out_offsets)))
+
+    # ---- profiling (device time per kernel class, CUDA events on the model's stream)
+    def profile_enable(self, on: bool = True) -> None:
+        _check(lib().n3d_profile_enable(self._h, int(on)))
+
+    def profile_read(self) -> dict:
+        buf = (_KernelStats * 16)()
+        n = lib().n3d_profile_read(self._h, buf, 16)
+        return {buf[i].name.decode(): dict(launches=int(buf[i].launches), ms=buf[i].ms, flops=buf[i].flops,
+                                           bytes=buf[i].bytes) for i in range(n)}
+
+    # ---- stages (GpuEngine, src/gpu_engine.rs)
+    def log_mel(self, samples, centered: bool = True) -> np.ndarray:
+        s = _f32(samples)
+        cap = (s.size // 160 + 2) * 128
+        out = np.zeros(max(cap, 1), np.float32)
+        frames = _sz()
+        _check(lib().n3d_log_mel(self._h, _ptr(s), s.size, int(centered), _ptr(out), out.size, C.byref(frames)))
+        return out[: frames.value * 128].reshape(frames.value, 128)
+
+    def embed_range(self, mel, num_frames: int, lo: int, hi: int) -> np.ndarray:
+        m = _f32(mel) if num_frames else np.zeros(1, np.float32)
+        out = np.zeros((hi - lo) * self.hidden_size, np.float32)
+        _check(lib().n3d_embed_range(self._h, _ptr(m), num_frames, lo, hi, _ptr(out)))
+        return out.reshape(hi - lo, self.hidden_size)
+
+    def forward_embeds(self, embeds, valid: int) -> np.ndarray:
+        e = _f32(embeds)
+        frames = e.size // self.hidden_size
+        out = np.zeros(e.size, np.float32)
+        _check(lib().n3d_forward_embeds(self._h, _ptr(e), frames, valid, _ptr(out)))
+        return out.reshape(frames, self.hidden_size)
+
+    def head_forward(self, encoder_out, frames: int) -> np.ndarray:
+        e = _f32(encoder_out)
+        out = np.zeros(frames * 8 * self.num_speakers, np.float32)
+        _check(lib().n3d_head_forward(self._h, _ptr(e), frames, _ptr(out)))
+        return out.reshape(frames * 8, self.num_speakers)
+
+    def forward_window(self, embeds, valid: int) -> np.ndarray:
+        e = _f32(embeds)
+        frames = e.size // self.hidden_size
+        out = np.zeros(frames * 8 * self.num_speakers, np.float32)
+        _check(lib().n3d_forward_window(self._h, _ptr(e), frames, valid, _ptr(out)))
+        return out.reshape(frames * 8, self.num_speakers)
+
+
+def extract_speaker_dict(logits, num_frames: int, num_speakers: int, duration: float, mask=None,
+                         threshold: float = 0.5) -> list[Segment]:
+    """extract_speaker_dict (src/segments.rs:70-109)."""
+    lg = _f32(logits) if num_frames and num_speakers else np.zeros(1, np.float32)
+    m = np.ascontiguousarray(mask, dtype=np.uint8) if mask is not None else None
+    out = C.POINTER(_Segment)()
+    n = _sz()
+    _check(lib().n3d_extract_speaker_dict(_ptr(lg), num_frames, num_speakers, duration,
+                                          m.ctypes.data if m is not None else None, threshold, C.byref(out),
+                                          C.byref(n)))
+    segs = [Segment(out[i].start, out[i].end, int(out[i].speaker)) for i in range(n.value)]
+    lib().n3d_segments_free(out)
+    return segs
+
+
+def activity_stats(logits, num_frames: int, num_speakers: int, mask=None, threshold: float = 0.5):
+    """activity_stats (src/segments.rs:113-141): (speech percentage, per-speaker frame counts)."""
+    lg = _f32(logits) if num_frames and num_speakers else np.zeros(1, np.float32)
+    m = np.ascontiguousarray(mask, dtype=np.uint8) if mask is not None else None
+    per = (_sz * max(num_speakers, 1))()
+    pct = lib().n3d_activity_stats(_ptr(lg), num_frames, num_speakers, m.ctypes.data if m is not None else None,
+                                   threshold, per)
+    return pct, [int(per[i]) for i in range(num_speakers)]
+
+
+def frame_duration(hop_length: int = 160, sampling_rate: int = 16000) -> float:
+    return lib().n3d_frame_duration(hop_length, sampling_rate)
+
+
+def linear(device: int, d_x: int, rows: int, cols: int, d_w: int, out: int, d_bias: int | None, d_y: int) -> None:
+    """tensor::linear on device pointers (3xTF32 tcgen05 GEMM)."""
+    _check(lib().n3d_linear(device, d_x, rows, cols, d_w, out, d_bias, d_y))
+
+
+def layer_norm(device: int, d_x: int, rows: int, cols: int, d_w: int, d_b: int, d_y: int) -> None:
+    _check(lib().n3d_layer_norm(device, d_x, rows, cols, d_w, d_b, d_y))
+
+
+def attention(device: int, d_q: int, d_k: int, d_v: int, seq: int, heads: int, head_dim: int, valid: int,
+              d_out: int, rope: bool = True, theta: float = 10000.0) -> None:
+    _check(lib().n3d_attention(device, d_q, d_k, d_v, seq, heads, head_dim, valid, int(rope), theta, d_out))

@@ -1,0 +1,70 @@
+"""The C-ABI library on the CPU: it loads, exports every symbol include/n3d.h
+declares, fails loudly without a B200, and its host-only functions
+(extract_speaker_dict, activity_stats) match the oracle exactly."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import n3d
+import oracle
+from conftest import gpu_available
+
+
+def test_library_exports_every_header_symbol():
+    L = n3d.lib()
+    names = n3d.header_functions()
+    assert len(names) >= 24
+    missing = [n for n in names if not hasattr(L, n)]
+    assert missing == []
+
+
+def test_version_string():
+    assert b"sm_100a" in n3d.lib().n3d_version()
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks the no-device path")
+def test_load_without_a_gpu_fails_loudly(checkpoint_dir):
+    with pytest.raises(n3d.DiarizationError) as e:
+        n3d.Model.load_gpu(checkpoint_dir, 0)
+    assert e.value.kind in ("NoDevice", "Cuda")
+
+
+def test_null_arguments_are_rejected():
+    out = n3d._RunOutput()
+    st = n3d.lib().n3d_run_offline(None, None, 0, C.byref(out))
+    assert n3d.STATUS[st] == "InvalidArgument"
+    assert b"null" in n3d.lib().n3d_last_error()
+
+
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_extract_speaker_dict_matches_oracle(seed):
+    rng = np.random.default_rng(seed)
+    T, ns = 3000, 8
+    # many logits near zero, as random-init weights produce
+    logits = (rng.standard_normal(T * ns) * 0.006).astype(np.float32)
+    mask = (rng.random(T) > 0.1).astype(np.uint8) if seed == 2 else None
+    got = n3d.extract_speaker_dict(logits, T, ns, 0.01, mask, 0.5)
+    want = oracle.extract_speaker_dict(logits, T, ns, 0.01, mask, 0.5)
+    assert [(s.start, s.end, s.speaker) for s in got] == [(np.float32(a), np.float32(b), s) for a, b, s in want]
+
+
+def test_extract_speaker_dict_reference_cases():  # src/segments.rs:153-205
+    logit = lambda a: 2.0 if a else -2.0
+    acts = [[0, 0, 1, 1, 0, 0], [0, 1, 0, 0, 1, 1]]
+    logits = [logit(acts[s][t]) for t in range(6) for s in range(2)]
+    segs = n3d.extract_speaker_dict(logits, 6, 2, 0.01)
+    f = np.float32
+    assert [(s.start, s.end, s.speaker) for s in segs] == [(f(0.01), f(0.02), 1), (f(0.02), f(0.04), 0),
+                                                          (f(0.04), f(0.06), 1)]
+    segs = n3d.extract_speaker_dict([logit(t % 2 == 0) for t in range(6)], 6, 1, 0.01, [0, 1, 1, 1, 1, 0])
+    assert [(s.start, s.end) for s in segs] == [(f(0.02), f(0.03)), (f(0.04), f(0.05))]
+    assert n3d.extract_speaker_dict([], 0, 8, 0.01) == []
+
+
+def test_activity_stats_matches_oracle():
+    rng = np.random.default_rng(5)
+    logits = (rng.standard_normal(800) * 0.01).astype(np.float32)
+    assert n3d.activity_stats(logits, 100, 8) == oracle.activity_stats(logits, 100, 8)
+    assert n3d.frame_duration(160, 16000) == np.float32(0.01)
