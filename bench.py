@@ -1,0 +1,312 @@
+#!/usr/bin/env python
+"""Offline RTFx of the Nemotron-3 diarization forward pass on B200.
+
+Workload (offline mode): independent 60 s, 16 kHz clips
+(seeds 1000+), random-init weights of the reference architecture (seed 0),
+sharded over GPUs with no collective on the data path (weak scaling: each rank
+runs its own clips).  One step = one batch of clips per GPU through the whole
+chunk loop (mel -> embedder -> windows of [cache ++ FIFO ++ chunk ++ look-ahead]
+-> 31-layer tower -> head -> device speaker cache).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.  `value` is whole-job audio seconds per device
+second with inputs already in HBM; `e2e` is the same metric through the public
+C-ABI batch call from pinned host buffers (H2D + D2H inside the timed region).
+`--impl reference` times the CPU oracle (the C restatement of the reference's
+Rust CPU path; the Rust crate cannot be built here) on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "nemotron3-diarization-wgpu_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+
+METRIC = "offline RTFx (audio-s/wall-s)"
+UNIT = "audio-s/s"
+CLIP_S = 60.0
+SR = 16000
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def make_clips(rank: int, n: int, seconds: float):
+    import synth
+
+    return [synth.config4_clip(rank * 100000 + i, seconds) for i in range(n)]
+
+
+def oracle_rtfx(ckpt: str, clip: np.ndarray, reps: int = 1):
+    """Time the CPU oracle (all host threads) on `clip`; returns (RTFx, seconds per run)."""
+    import oracle
+
+    om = oracle.OracleModel.load(ckpt)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        om.run_offline(clip)
+    dt = (time.perf_counter() - t0) / reps
+    return clip.size / SR / dt, dt
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def checkpoint(rank: int, world: int) -> str:
+    import synth
+
+    d = os.path.join(tempfile.gettempdir(), "n3d_bench_ckpt_seed0")
+    if rank == 0 and not os.path.exists(os.path.join(d, "model.safetensors")):
+        tmp = d + f".tmp{os.getpid()}"
+        synth.write_checkpoint(tmp, seed=0)
+        os.replace(tmp, d) if not os.path.exists(d) else None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    return d
+
+
+def run_reference(args, world, rank):
+    """CPU oracle on the same workload, bounded sample: one 60 s clip per step."""
+    if rank != 0:
+        return
+    ckpt = checkpoint(0, 1)
+    import oracle
+
+    om = oracle.OracleModel.load(ckpt)
+    clip = make_clips(0, 1, CLIP_S)[0]
+    for _ in range(args.warmup):  # CPU code has nothing to JIT: warm the thread pool on a 2 s clip
+        om.run_offline(clip[: 2 * SR])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        om.run_offline(clip)
+    dt = time.perf_counter() - t0
+    value = args.steps * CLIP_S / dt
+    cores = os.cpu_count()
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": "C4 offline: 60 s 16 kHz clips, random-init weights (seed 0)",
+                       "clip_seconds": CLIP_S, "clips_per_step": 1},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": "one 60 s clip per step through the C restatement of the reference's "
+                                       "Rust CPU path (OpenMP over rows, as rayon)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--clips", type=int, default=64, help="60 s clips per GPU per step")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args()
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    import torch
+
+    import n3d
+
+    torch.cuda.set_device(local)
+    ckpt = checkpoint(rank, world)
+    clips = make_clips(rank, args.clips, CLIP_S)
+    lens = [c.size for c in clips]
+    model = n3d.Model.load_gpu(ckpt, local)
+    stream = torch.cuda.current_stream()
+    model.set_stream(stream.cuda_stream)
+    frames = model.batch_out_frames(lens, "offline")
+    offs = [int(x) for x in np.cumsum([0] + lens[:-1])]
+    ooffs = [int(x) for x in np.cumsum([0] + frames[:-1])]
+    d_audio = torch.from_numpy(np.concatenate(clips)).cuda()
+    d_out = torch.empty(sum(frames) * 8, dtype=torch.float32, device="cuda")
+
+    def step():
+        model.run_batch_device("offline", d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timed region
+    for _ in range(args.warmup):
+        step()
+    model.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    prof = model.profile_read()
+    model.profile_enable(False)
+    audio_s = world * args.clips * CLIP_S * args.steps
+    value = audio_s / (ms / 1e3)
+
+    # ---- end-to-end through the public C-ABI batch call, pinned host buffers
+    pinned = [torch.from_numpy(c).pin_memory() for c in clips]
+    host = [t.numpy() for t in pinned]
+    model.run_batch(host, "offline")  # warm the host path
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        outs = model.run_batch(host, "offline")
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    assert all(o.num_frames == f for o, f in zip(outs, frames))
+    h2d = sum(lens) * 4
+    d2h = sum(frames) * 8 * 4
+
+    # ---- roofline of the dominant kernel class (by device time)
+    peaks, src = _peaks()
+    top = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    g = prof["gemm_tf32x3"]
+    achieved = g["flops"] / (g["ms"] / 1e3) / 1e12 if g["ms"] else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    launches = sum(v["launches"] for v in prof.values())
+    total_prof_ms = sum(v["ms"] for v in prof.values())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rt, dt = oracle_rtfx(ckpt, clips[0])
+        cpu = {"value": rt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+               "sample": f"one 60 s clip (3 windows) through the CPU oracle, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (3xTF32 on tcgen05)", "data": "synthetic",
+            "config": {"workload": f"C4 offline: {args.clips} x 60 s 16 kHz clips per GPU per step, "
+                                   "random-init weights (seed 0), clips seeded 1000+",
+                       "clip_seconds": CLIP_S, "clips_per_step_per_gpu": args.clips, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},
+            "e2e": {"value": world * args.clips * CLIP_S * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "kernel": "gemm_tf32x3", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "peak_source": f"{src} bf16 dense sustained (MEASURED_PEAKS.json)",
+                         "note": "3xTF32: each algorithmic FLOP issues 3 TF32 tensor FLOPs at half the bf16 "
+                                 "rate, so the ceiling for this kernel is peak/6",
+                         "frac_of_3xtf32_ceiling": achieved / (peak / 6.0),
+                         "avg_launch_ms": g["ms"] / max(g["launches"], 1)},
+            "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in prof.items() if v["launches"]},
+            "dominant_kernel": top[0],
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
