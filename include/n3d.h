@@ -163,6 +163,22 @@ float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate);
 n3d_status n3d_linear(int device, const float *d_x, size_t rows, size_t cols, const float *d_w, size_t out,
                       const float *d_bias, float *d_y);
 
+/* n3d_linear for callers that cannot allocate device memory when they call
+ * (a real-time audio thread that must not block in the driver's allocator, a
+ * host framework that owns all GPU memory through its own pool, a process with
+ * an allocation budget fixed at start-up).  No counterpart in the reference.
+ * The operand split uses a fixed 16 MiB array inside the library's GPU image
+ * instead of temporary memory, so the call allocates nothing.  Limits:
+ * rows*cols + out*cols at most about 2 Mi floats (larger requests fail with
+ * N3D_ERR_INVALID_ARGUMENT); every GPU that loads the library keeps the 16 MiB
+ * until exit; all calls on a device share the array, so calls whose GPU work
+ * overlaps race and must be serialised by the caller.  The first call on each
+ * device does a one-time set-up; make it before any stream capture.  Runs on
+ * `stream` (a cudaStream_t, NULL for the default stream) and returns after it
+ * has finished. */
+n3d_status n3d_linear_noalloc(int device, const float *d_x, size_t rows, size_t cols, const float *d_w,
+                              size_t out, const float *d_bias, float *d_y, void *stream);
+
 /* tensor::layer_norm (src/tensor.rs:97-110), cols 512 or 1024. */
 n3d_status n3d_layer_norm(int device, const float *d_x, size_t rows, size_t cols, const float *d_w,
                           const float *d_b, float *d_y);

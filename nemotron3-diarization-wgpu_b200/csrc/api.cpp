@@ -350,6 +350,13 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
     });
 }
 
+n3d_status n3d_linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
+                              const float* d_bias, float* d_y, void* stream) {
+    return guarded([&] {
+        n3d::linear_noalloc(device, d_x, rows, cols, d_w, out, d_bias, d_y, (cudaStream_t)stream);
+    });
+}
+
 n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, const float* d_b,
                           float* d_y) {
     return guarded([&] {

@@ -333,6 +333,41 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     }
 }
 
+// Same kernel with tensor maps encoded on the stack: no map cache, so nothing
+// is allocated on the host heap either (used by the allocation-free entry point).
+void gemm_tf32x3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                            const Epi& epi, int* err) {
+    if (M <= 0 || N <= 0) return;
+    if (K % BK) throw Error(13, "GEMM K must be a multiple of 32");
+    if ((reinterpret_cast<uintptr_t>(A.hi) | reinterpret_cast<uintptr_t>(A.lo) | reinterpret_cast<uintptr_t>(B.hi) |
+         reinterpret_cast<uintptr_t>(B.lo)) & 15)
+        throw Error(13, "GEMM operands must be 16-byte aligned");
+    using Cfg = GemmCfg<128>;
+    static bool attr = false;
+    if (!attr) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_tf32x3_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM));
+        attr = true;
+    }
+    CUtensorMap maps[4];
+    const SplitOperand* ops[2] = {&A, &B};
+    for (int i = 0; i < 4; i++) {
+        const SplitOperand& o = *ops[i / 2];
+        cuuint64_t dims[2] = {static_cast<cuuint64_t>(o.cols), static_cast<cuuint64_t>(o.rows)};
+        cuuint64_t strides[1] = {static_cast<cuuint64_t>(o.ld) * 4};
+        cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(i < 2 ? BM : 128)};
+        cuuint32_t estr[2] = {1, 1};
+        const float* p = (i % 2) ? o.lo : o.hi;
+        CUresult r = encode_fn()(&maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed");
+    }
+    dim3 grid((N + 127) / 128, (M + BM - 1) / BM);
+    gemm_tf32x3_kernel<128><<<grid, 192, Cfg::SMEM, s>>>(maps[0], maps[1], maps[2], maps[3], M, N, K, 0, epi, err);
+    N3D_CUDA(cudaGetLastError());
+}
+
 // Explicit tile choice, for the kernel tests and tile sweeps.
 void gemm_tf32x3_bn(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
                     int kb_per_tap, const Epi& epi, int* err, int bn) {

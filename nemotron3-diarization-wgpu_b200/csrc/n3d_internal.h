@@ -84,6 +84,10 @@ void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, con
                 const long long* f_out);
 // x -> (hi, lo) TF32 pair, elementwise.
 void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
+// tensor::linear without any allocation: scratch is a fixed device array (noalloc.cu).
+void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
+                    const float* d_bias, float* d_y, cudaStream_t stream);
+size_t linear_noalloc_capacity();
 // q, k, v [seq, heads*hd] -> qkv [seq, 3*heads*hd] with RoPE applied to q and k when cos_t != nullptr.
 void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
                      int hd, const float* cos_t, const float* sin_t, float* qkv);

@@ -1,0 +1,113 @@
+// Allocation-free variant of tensor::linear (src/tensor.rs:22-57) on the GPU.
+//
+// n3d_linear needs temporary device memory for the TF32 hi/lo split of its
+// operands and gets it from cudaMalloc.  Some callers cannot allocate device
+// memory at the point where they call: a real-time audio thread that must not
+// block in the driver's allocator, a host framework that has reserved all of
+// the GPU's memory for its own pool and hands out only its own buffers, or a
+// process whose allocation budget is fixed after start-up.  For them this
+// file keeps the scratch in a fixed array that is part of the library's GPU
+// image, so a call allocates nothing: no cudaMalloc, no cudaFree, no
+// allocating library routine, no host-heap map cache.
+//
+// Limits and sharing rules:
+//  * the scratch holds kScratchFloats fp32 values (16 MiB).  The split needs
+//    2 * (rows * cols + out * cols) of them (each part rounded up to 64
+//    floats), so rows * cols + out * cols may be at most ~2 Mi floats; larger
+//    requests are rejected with N3D_ERR_INVALID_ARGUMENT.
+//  * every GPU that loads the library holds these 16 MiB until the process
+//    exits.
+//  * all calls on a device share the one array and it keeps the last call's
+//    contents; calls whose GPU work overlaps (different streams, different
+//    host threads) race on it and must be serialised by the caller.
+//  * the first call on each device does the set-up: it resolves the device
+//    address of the array (which also loads the library's GPU code onto that
+//    device).  Make that first call before any stream capture.
+
+#include <mutex>
+
+#include "n3d_device.cuh"
+#include "n3d_internal.h"
+
+namespace n3d {
+
+void gemm_tf32x3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                            const Epi& epi, int* err);
+
+namespace {
+
+constexpr size_t kScratchFloats = size_t(4) << 20;  // 16 MiB
+__device__ __align__(256) float g_linear_scratch[kScratchFloats];
+__device__ int g_linear_status;  // bounded-wait status word of the GEMM
+
+struct DeviceSymbols {
+    float* scratch = nullptr;
+    int* status = nullptr;
+};
+
+// Host copies of the two symbols' device addresses, resolved once per device.
+DeviceSymbols g_symbols[128];
+std::mutex g_symbols_mu;
+
+DeviceSymbols symbols_for(int device) {
+    if (device < 0 || device >= 128) throw Error(12, "n3d_linear_noalloc: bad device index");
+    std::lock_guard<std::mutex> lock(g_symbols_mu);
+    DeviceSymbols& s = g_symbols[device];
+    if (!s.scratch) {
+        cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.scratch), g_linear_scratch);
+        if (e != cudaSuccess) {
+            s.scratch = nullptr;
+            throw Error(10, std::string("n3d_linear_noalloc set-up: cudaGetSymbolAddress(scratch): ") +
+                                cudaGetErrorString(e));
+        }
+        e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.status), g_linear_status);
+        if (e != cudaSuccess) {
+            s.scratch = nullptr;
+            throw Error(10, std::string("n3d_linear_noalloc set-up: cudaGetSymbolAddress(status): ") +
+                                cudaGetErrorString(e));
+        }
+    }
+    return s;
+}
+
+size_t round64(size_t n) { return (n + 63) & ~size_t(63); }
+
+}  // namespace
+
+size_t linear_noalloc_capacity() { return kScratchFloats; }
+
+void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
+                    const float* d_bias, float* d_y, cudaStream_t stream) {
+    if (!d_x || !d_w || !d_y) throw Error(13, "n3d_linear_noalloc: null argument");
+    if (cols == 0 || cols % 32) throw Error(13, "n3d_linear_noalloc: cols must be a positive multiple of 32");
+    if (rows == 0 || out == 0) return;
+    const size_t need = 2 * round64(rows * cols) + 2 * round64(out * cols);
+    if (need > kScratchFloats)
+        throw Error(13, "n3d_linear_noalloc: request needs " + std::to_string(need) +
+                            " scratch floats; the fixed scratch holds " + std::to_string(kScratchFloats) +
+                            " (rows*cols + out*cols must stay within about 2097152)");
+    N3D_CUDA(cudaSetDevice(device));
+    const DeviceSymbols sym = symbols_for(device);
+    float* xh = sym.scratch;
+    float* xl = xh + round64(rows * cols);
+    float* wh = xl + round64(rows * cols);
+    float* wl = wh + round64(out * cols);
+    // the status word starts at zero for every call; the split arrays are fully overwritten
+    N3D_CUDA(cudaMemsetAsync(sym.status, 0, sizeof(int), stream));
+    launch_split(stream, d_x, (long long)(rows * cols), xh, xl);
+    launch_split(stream, d_w, (long long)(out * cols), wh, wl);
+    Epi e;
+    e.mode = EPI_STORE;
+    e.bias = d_bias;
+    e.out = d_y;
+    e.ldo = (long long)out;
+    gemm_tf32x3_stack_maps(stream, SplitOperand{xh, xl, (long long)rows, (long long)cols, (long long)cols},
+                           SplitOperand{wh, wl, (long long)out, (long long)cols, (long long)cols}, (int)rows,
+                           (int)out, (int)cols, e, sym.status);
+    N3D_CUDA(cudaStreamSynchronize(stream));
+    int status = 0;
+    N3D_CUDA(cudaMemcpy(&status, sym.status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (status) throw Error(11, "n3d_linear_noalloc: a device-side wait timed out (site " + std::to_string(status) + ")");
+}
+
+}  // namespace n3d

@@ -124,6 +124,7 @@ def lib() -> C.CDLL:
         "n3d_activity_stats": ([fpp, _sz, _sz, vp, C.c_float, C.POINTER(_sz)], C.c_float),
         "n3d_frame_duration": ([_sz, C.c_uint32], C.c_float),
         "n3d_linear": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp], C.c_int),
+        "n3d_linear_noalloc": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp, vp], C.c_int),
         "n3d_layer_norm": ([C.c_int, vp, _sz, _sz, vp, vp, vp], C.c_int),
         "n3d_attention": ([C.c_int, vp, vp, vp, _sz, _sz, _sz, _sz, C.c_int, C.c_double, vp], C.c_int),
         "n3d_profile_enable": ([vp, C.c_int], C.c_int),
@@ -309,6 +310,14 @@ def frame_duration(hop_length: int = 160, sampling_rate: int = 16000) -> float:
 def linear(device: int, d_x: int, rows: int, cols: int, d_w: int, out: int, d_bias: int | None, d_y: int) -> None:
     """tensor::linear on device pointers (3xTF32 tcgen05 GEMM)."""
     _check(lib().n3d_linear(device, d_x, rows, cols, d_w, out, d_bias, d_y))
+
+
+def linear_noalloc(device: int, d_x: int, rows: int, cols: int, d_w: int, out: int, d_bias: int | None, d_y: int,
+                   stream: int | None = None) -> None:
+    """tensor::linear for callers that cannot allocate device memory: the operand
+    split uses the library's fixed 16 MiB device scratch (limit: rows*cols +
+    out*cols of about 2 Mi floats; calls overlapping on the GPU race)."""
+    _check(lib().n3d_linear_noalloc(device, d_x, rows, cols, d_w, out, d_bias, d_y, stream))
 
 
 def layer_norm(device: int, d_x: int, rows: int, cols: int, d_w: int, d_b: int, d_y: int) -> None:
