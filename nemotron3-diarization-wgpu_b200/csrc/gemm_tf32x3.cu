@@ -141,7 +141,8 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else {
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const bool ok = mbar_wait(acc_full, 0, err, DEV_TIMEOUT_ACC);
+        // warp-uniform result: the TMEM loads below are .sync.aligned
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, err, DEV_TIMEOUT_ACC));
         tc_fence_after();
         if (ok) {
             const int r = m0 + q * 32 + lane;
@@ -174,6 +175,45 @@ __global__ void __launch_bounds__(192, 1)
                     float* dst = epi.out + orow * epi.ldo + col0;
                     store_row32(dst, v, N - col0);
                     store_row32(dst + 32, v + 32, N - col0 - 32);
+                }
+            } else if (epi.mode == EPI_QKV_ATTN) {
+                // Q | K | V sections of epi.q_cols columns each, one head = 64 columns
+                for (int c = 0; c < BN; c += 64) {
+                    float v[64];
+                    tmem_ld32(tl + c, v);
+                    tmem_ld32(tl + c + 32, v + 32);
+                    const int col0 = n0 + c;
+                    if (!keep || col0 >= N) continue;
+                    const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
+                    const int pos = r % epi.rope_seq;
+                    if (sec < 2) {
+                        const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
+                        const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            const float x1 = v[i], x2 = v[32 + i];
+                            v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+                            v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                        }
+                    }
+                    float lo[64];
+#pragma unroll
+                    for (int i = 0; i < 64; i++) split_tf32(v[i], v[i], lo[i]);
+                    if (sec < 2) {
+                        float* dh = (sec == 0 ? epi.out : epi.k_hi) + orow * epi.ldo + hcol;
+                        float* dl = (sec == 0 ? epi.out_lo : epi.k_lo) + orow * epi.ldo + hcol;
+                        store_row32(dh, v, 32);
+                        store_row32(dh + 32, v + 32, 32);
+                        store_row32(dl, lo, 32);
+                        store_row32(dl + 32, lo + 32, 32);
+                    } else {
+                        const long long vrow = ((long long)(r / epi.rope_seq) * epi.heads + hcol / 64) * 64;
+#pragma unroll 8
+                        for (int d = 0; d < 64; d++) {
+                            epi.vt_hi[(vrow + d) * epi.vt_ld + pos] = v[d];
+                            epi.vt_lo[(vrow + d) * epi.vt_ld + pos] = lo[d];
+                        }
+                    }
                 }
             } else if (epi.mode == EPI_DENSE_OUT) {
                 // relu(dense) then the out projection, sequential over the hidden
@@ -324,7 +364,8 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     } else {
         bn = 64;
     }
-    if (epi.mode == EPI_QKV_ROPE && (bn % 64)) throw Error(9, "QKV epilogue needs 64-column chunks");
+    if ((epi.mode == EPI_QKV_ROPE || epi.mode == EPI_QKV_ATTN) && (bn % 64))
+        throw Error(9, "QKV epilogue needs 64-column chunks");
     switch (bn) {
         case 64: launch<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 128: launch<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;

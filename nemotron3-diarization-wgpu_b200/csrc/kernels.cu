@@ -270,7 +270,50 @@ __global__ void pack_qkv_kernel(const float* __restrict__ q, const float* __rest
     }
 }
 
+// Kernel-level attention operands: RoPE'd Q and K as TF32 pairs, V transposed as a pair.
+__global__ void pack_attn_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                 const float* __restrict__ v, long long seq, int heads,
+                                 const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                 float* __restrict__ q_hi, float* __restrict__ q_lo, float* __restrict__ k_hi,
+                                 float* __restrict__ k_lo, float* __restrict__ vt_hi, float* __restrict__ vt_lo,
+                                 long long vt_ld) {
+    const int hd = 64, half = 32;
+    const long long W = (long long)heads * hd;
+    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < seq * W;
+         e += (long long)gridDim.x * blockDim.x) {
+        const long long r = e / W;
+        const int c = (int)(e % W), d = c % hd;
+        float qo = q[e], ko = k[e];
+        if (cos_t) {
+            const float* cs = cos_t + r * hd;
+            const float* sn = sin_t + r * hd;
+            const long long pe = d < half ? e + half : e - half;
+            if (d < half) {
+                qo = __fsub_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
+                ko = __fsub_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
+            } else {
+                qo = __fadd_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
+                ko = __fadd_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
+            }
+        }
+        split_tf32(qo, q_hi[e], q_lo[e]);
+        split_tf32(ko, k_hi[e], k_lo[e]);
+        split_tf32(v[e], vt_hi[(long long)c * vt_ld + r], vt_lo[(long long)c * vt_ld + r]);
+    }
+}
+
 }  // namespace
+
+void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
+                      const float* cos_t, const float* sin_t, float* q_hi, float* q_lo, float* k_hi, float* k_lo,
+                      float* vt_hi, float* vt_lo, long long vt_ld) {
+    const long long n = seq * heads * 64;
+    if (n <= 0) return;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, cos_t, sin_t, q_hi, q_lo, k_hi, k_lo,
+                                                      vt_hi, vt_lo, vt_ld);
+    N3D_CUDA(cudaGetLastError());
+}
 
 void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo) {
     if (n <= 0) return;

@@ -620,7 +620,14 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     float* x = (float*)ws("x", M * h * 4);
     float* n_hi = (float*)ws("n_hi", M * h * 4);
     float* n_lo = (float*)ws("n_lo", M * h * 4);
-    float* qkv = (float*)ws("qkv", M * 3 * h * 4);
+    float* q_hi = (float*)ws("q_hi", M * h * 4);
+    float* q_lo = (float*)ws("q_lo", M * h * 4);
+    float* k_hi = (float*)ws("k_hi", M * h * 4);
+    float* k_lo = (float*)ws("k_lo", M * h * 4);
+    const long long vt_ld = (S + 3) / 4 * 4;
+    float* vt_hi = (float*)ws("vt_hi", (long long)B * h * vt_ld * 4);
+    float* vt_lo = (float*)ws("vt_lo", (long long)B * h * vt_ld * 4);
+    const long long rows_qk = ws_["q_hi"].bytes / (h * 4);
     float* ctx_hi = (float*)ws("ctx_hi", M * h * 4);
     float* ctx_lo = (float*)ws("ctx_lo", M * h * 4);
     float* f_hi = (float*)ws("f_hi", M * c.inter * 4);
@@ -642,9 +649,16 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
         prof_end(K_LN, 0, ln_bytes);
         Epi e;
-        e.mode = EPI_QKV_ROPE;
-        e.out = qkv;
-        e.ldo = 3 * h;
+        e.mode = EPI_QKV_ATTN;
+        e.out = q_hi;
+        e.out_lo = q_lo;
+        e.k_hi = k_hi;
+        e.k_lo = k_lo;
+        e.vt_hi = vt_hi;
+        e.vt_lo = vt_lo;
+        e.vt_ld = vt_ld;
+        e.heads = c.heads;
+        e.ldo = h;
         e.cos_t = rope_cos_;
         e.sin_t = rope_sin_;
         e.rope_seq = S;
@@ -655,7 +669,8 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM, 2.0 * M * 3 * h * h, 0);
         prof_begin();
-        launch_attention(stream_, qkv, B, S, d_valid, c.heads, (int)(h / c.heads), ctx_hi, ctx_lo);
+        launch_attention_tc(stream_, q_hi, q_lo, k_hi, k_lo, rows_qk, vt_hi, vt_lo, vt_ld, B, S, d_valid, c.heads,
+                            ctx_hi, ctx_lo, dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
         Epi eo;
         eo.mode = EPI_RESID;

@@ -31,6 +31,8 @@ enum EpiMode : int {
     EPI_RELU_SPLIT = 4,  // split(relu(acc + bias))
     EPI_QKV_ROPE = 5,    // Q,K columns rotated by RoPE, V as is; fp32 out
     EPI_DENSE_OUT = 6,   // r = relu(acc + bias); out[r, 0:ns] = r . w2^T + b2
+    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> TF32 pairs (out/out_lo, k_hi/k_lo);
+                         // V -> transposed TF32 pair vt[(seq*heads + head)*64 + d][t]
 };
 
 struct Epi {
@@ -51,6 +53,13 @@ struct Epi {
     int rope_seq = 1;
     int head_dim = 64;
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
+    // EPI_QKV_ATTN destinations
+    float* k_hi = nullptr;
+    float* k_lo = nullptr;
+    float* vt_hi = nullptr;
+    float* vt_lo = nullptr;
+    long long vt_ld = 0;
+    int heads = 8;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
     const float* b2 = nullptr;
@@ -84,6 +93,15 @@ void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, con
                 const long long* f_out);
 // x -> (hi, lo) TF32 pair, elementwise.
 void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
+// tcgen05 attention, head_dim 64 (attention_tc.cu).  ctx_lo == nullptr writes plain fp32.
+void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, const float* k_hi,
+                         const float* k_lo, long long rows_cap, const float* vt_hi, const float* vt_lo,
+                         long long vt_ld, int seqs, int S, const int* valid, int heads, float* ctx_hi,
+                         float* ctx_lo, int* err);
+// q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
+void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
+                      const float* cos_t, const float* sin_t, float* q_hi, float* q_lo, float* k_hi, float* k_lo,
+                      float* vt_hi, float* vt_lo, long long vt_ld);
 // tensor::linear without any allocation: scratch is a fixed device array (noalloc.cu).
 void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
                     const float* d_bias, float* d_y, cudaStream_t stream);
