@@ -60,6 +60,140 @@ __device__ __forceinline__ void store_row32(float* dst, const float* v, int ncol
     }
 }
 
+// Epilogue of one 128 x BN accumulator tile held in TMEM at `tl` (this warp's
+// lane quadrant and the tile's first column): row r = m0 + 32 * q + lane.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
+                                              int lane) {
+    const int r = m0 + q * 32 + lane;
+    const bool row_ok = r < M;
+    const int qq = r / epi.rdiv, t = r - qq * epi.rdiv;
+    const bool keep = row_ok && t < epi.rkeep;
+    const long long orow = (long long)qq * epi.rmul + t + epi.roff;
+    const bool zero_row = epi.seq_len != nullptr && keep && t >= epi.seq_len[qq];
+    
+    if (epi.mode == EPI_QKV_ROPE) {
+        // 64-column chunks = one head; rotate-half RoPE (src/encoder.rs:281-296)
+        for (int c = 0; c < BN; c += 64) {
+            float v[64];
+            tmem_ld32(tl + c, v);
+            tmem_ld32(tl + c + 32, v + 32);
+            const int col0 = n0 + c;
+            if (!keep || col0 >= N) continue;
+            if (col0 < epi.q_cols + epi.k_cols) {
+                const int pos = r % epi.rope_seq;
+                const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
+                const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float x1 = v[i], x2 = v[32 + i];
+                    v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+                    v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                }
+            }
+            float* dst = epi.out + orow * epi.ldo + col0;
+            store_row32(dst, v, N - col0);
+            store_row32(dst + 32, v + 32, N - col0 - 32);
+        }
+    } else if (epi.mode == EPI_QKV_ATTN) {
+        // Q | K | V sections of epi.q_cols columns each, one head = 64 columns
+        for (int c = 0; c < BN; c += 64) {
+            float v[64];
+            tmem_ld32(tl + c, v);
+            tmem_ld32(tl + c + 32, v + 32);
+            const int col0 = n0 + c;
+            if (!keep || col0 >= N) continue;
+            const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
+            const int pos = r % epi.rope_seq;
+            if (sec < 2) {
+                const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
+                const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float x1 = v[i], x2 = v[32 + i];
+                    v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+                    v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                }
+            }
+            float lo[64];
+#pragma unroll
+            for (int i = 0; i < 64; i++) split_tf32(v[i], v[i], lo[i]);
+            if (sec < 2) {
+                float* dh = (sec == 0 ? epi.out : epi.k_hi) + orow * epi.ldo + hcol;
+                float* dl = (sec == 0 ? epi.out_lo : epi.k_lo) + orow * epi.ldo + hcol;
+                store_row32(dh, v, 32);
+                store_row32(dh + 32, v + 32, 32);
+                store_row32(dl, lo, 32);
+                store_row32(dl + 32, lo + 32, 32);
+            } else {
+                const long long vrow = ((long long)(r / epi.rope_seq) * epi.heads + hcol / 64) * 64;
+#pragma unroll 8
+                for (int d = 0; d < 64; d++) {
+                    epi.vt_hi[(vrow + d) * epi.vt_ld + pos] = v[d];
+                    epi.vt_lo[(vrow + d) * epi.vt_ld + pos] = lo[d];
+                }
+            }
+        }
+    } else if (epi.mode == EPI_DENSE_OUT) {
+        // relu(dense) then the out projection, sequential over the hidden
+        // index with separate multiply and add (src/tensor.rs:33-43)
+        float acc[8];
+#pragma unroll
+        for (int o = 0; o < 8; o++) acc[o] = 0.0f;
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tl + c, v);
+            if (!keep) continue;
+            for (int i = 0; i < 32; i++) {
+                const int col = n0 + c + i;
+                if (col >= N) break;
+                const float rr = fmaxf(__fadd_rn(v[i], epi.bias[col]), 0.0f);
+#pragma unroll
+                for (int o = 0; o < 8; o++)
+                    if (o < epi.n2) acc[o] = __fadd_rn(acc[o], __fmul_rn(rr, epi.w2[o * N + col]));
+            }
+        }
+        if (keep)
+            for (int o = 0; o < epi.n2; o++) epi.out[orow * epi.ldo + o] = __fadd_rn(acc[o], epi.b2[o]);
+    } else {
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tl + c, v);
+            const int col0 = n0 + c;
+            if (!keep || col0 >= N) continue;
+            const int left = N - col0;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float b = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
+                v[i] = __fadd_rn(v[i], b);
+            }
+            float* dst = epi.out + orow * epi.ldo + col0;
+            switch (epi.mode) {
+                case EPI_STORE:
+                    store_row32(dst, v, left);
+                    break;
+                case EPI_RESID: {
+                    for (int i = 0; i < 32 && i < left; i++) dst[i] = __fadd_rn(dst[i], v[i]);
+                    break;
+                }
+                default: {
+                    float lo[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        float x = v[i];
+                        if (epi.mode == EPI_GELU_SPLIT) x = gelu_erf(x);
+                        if (epi.mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
+                        if (zero_row) x = 0.0f;
+                        split_tf32(x, v[i], lo[i]);
+                    }
+                    store_row32(dst, v, left);
+                    store_row32(epi.out_lo + orow * epi.ldo + col0, lo, left);
+                }
+            }
+        }
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
@@ -145,134 +279,146 @@ __global__ void __launch_bounds__(192, 1)
         const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, err, DEV_TIMEOUT_ACC));
         tc_fence_after();
         if (ok) {
-            const int r = m0 + q * 32 + lane;
-            const bool row_ok = r < M;
-            const int qq = r / epi.rdiv, t = r - qq * epi.rdiv;
-            const bool keep = row_ok && t < epi.rkeep;
-            const long long orow = (long long)qq * epi.rmul + t + epi.roff;
-            const bool zero_row = epi.seq_len != nullptr && keep && t >= epi.seq_len[qq];
-            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+            epilogue_tile<BN>(epi, tmem + (static_cast<uint32_t>(q * 32) << 16), m0, n0, M, N, q, lane);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
 
-            if (epi.mode == EPI_QKV_ROPE) {
-                // 64-column chunks = one head; rotate-half RoPE (src/encoder.rs:281-296)
-                for (int c = 0; c < BN; c += 64) {
-                    float v[64];
-                    tmem_ld32(tl + c, v);
-                    tmem_ld32(tl + c + 32, v + 32);
-                    const int col0 = n0 + c;
-                    if (!keep || col0 >= N) continue;
-                    if (col0 < epi.q_cols + epi.k_cols) {
-                        const int pos = r % epi.rope_seq;
-                        const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
-                        const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
-#pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const float x1 = v[i], x2 = v[32 + i];
-                            v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
-                            v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
-                        }
+// Persistent variant: one CTA per SM walks the output tiles (t = blockIdx.x,
+// + gridDim.x, ...), k-blocks of 16 fp32 (64 B rows, 64-byte swizzle) so that
+// even BN = 256 gets 4 shared-memory stages, and two TMEM accumulators so the
+// epilogue of tile i overlaps the main loop of tile i + 1.
+constexpr int PBK = 16;
+
+template <int BN>
+struct PCfg {
+    static constexpr int A_BYTES = BM * PBK * 4;
+    static constexpr int B_BYTES = BN * PBK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+    static constexpr int ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static_assert(STAGES >= 3, "persistent GEMM wants at least three stages");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                           const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo,
+                           int M, int N, int K, int kb_per_tap, const __grid_constant__ Epi epi, int* err) {
+    using Cfg = PCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + BN - 1) / BN;
+    const int tiles = ((M + BM - 1) / BM) * tiles_n;
+    const int nkb = K / PBK;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < Cfg::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_fence_init();
+        tma_prefetch_desc(&tA_hi);
+        tma_prefetch_desc(&tA_lo);
+        tma_prefetch_desc(&tB_hi);
+        tma_prefetch_desc(&tB_lo);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (g >= (uint32_t)Cfg::STAGES &&
+                        !mbar_wait(&empty[s], ((g / Cfg::STAGES) - 1) & 1, err, DEV_TIMEOUT_TMA_EMPTY)) {
+                        ok = false;
+                        break;
                     }
-                    float* dst = epi.out + orow * epi.ldo + col0;
-                    store_row32(dst, v, N - col0);
-                    store_row32(dst + 32, v + 32, N - col0 - 32);
-                }
-            } else if (epi.mode == EPI_QKV_ATTN) {
-                // Q | K | V sections of epi.q_cols columns each, one head = 64 columns
-                for (int c = 0; c < BN; c += 64) {
-                    float v[64];
-                    tmem_ld32(tl + c, v);
-                    tmem_ld32(tl + c + 32, v + 32);
-                    const int col0 = n0 + c;
-                    if (!keep || col0 >= N) continue;
-                    const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
-                    const int pos = r % epi.rope_seq;
-                    if (sec < 2) {
-                        const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
-                        const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
-#pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const float x1 = v[i], x2 = v[32 + i];
-                            v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
-                            v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
-                        }
-                    }
-                    float lo[64];
-#pragma unroll
-                    for (int i = 0; i < 64; i++) split_tf32(v[i], v[i], lo[i]);
-                    if (sec < 2) {
-                        float* dh = (sec == 0 ? epi.out : epi.k_hi) + orow * epi.ldo + hcol;
-                        float* dl = (sec == 0 ? epi.out_lo : epi.k_lo) + orow * epi.ldo + hcol;
-                        store_row32(dh, v, 32);
-                        store_row32(dh + 32, v + 32, 32);
-                        store_row32(dl, lo, 32);
-                        store_row32(dl + 32, lo + 32, 32);
-                    } else {
-                        const long long vrow = ((long long)(r / epi.rope_seq) * epi.heads + hcol / 64) * 64;
-#pragma unroll 8
-                        for (int d = 0; d < 64; d++) {
-                            epi.vt_hi[(vrow + d) * epi.vt_ld + pos] = v[d];
-                            epi.vt_lo[(vrow + d) * epi.vt_ld + pos] = lo[d];
-                        }
-                    }
-                }
-            } else if (epi.mode == EPI_DENSE_OUT) {
-                // relu(dense) then the out projection, sequential over the hidden
-                // index with separate multiply and add (src/tensor.rs:33-43)
-                float acc[8];
-#pragma unroll
-                for (int o = 0; o < 8; o++) acc[o] = 0.0f;
-                for (int c = 0; c < BN; c += 32) {
-                    float v[32];
-                    tmem_ld32(tl + c, v);
-                    if (!keep) continue;
-                    for (int i = 0; i < 32; i++) {
-                        const int col = n0 + c + i;
-                        if (col >= N) break;
-                        const float rr = fmaxf(__fadd_rn(v[i], epi.bias[col]), 0.0f);
-#pragma unroll
-                        for (int o = 0; o < 8; o++)
-                            if (o < epi.n2) acc[o] = __fadd_rn(acc[o], __fmul_rn(rr, epi.w2[o * N + col]));
-                    }
-                }
-                if (keep)
-                    for (int o = 0; o < epi.n2; o++) epi.out[orow * epi.ldo + o] = __fadd_rn(acc[o], epi.b2[o]);
-            } else {
-                for (int c = 0; c < BN; c += 32) {
-                    float v[32];
-                    tmem_ld32(tl + c, v);
-                    const int col0 = n0 + c;
-                    if (!keep || col0 >= N) continue;
-                    const int left = N - col0;
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const float b = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
-                        v[i] = __fadd_rn(v[i], b);
-                    }
-                    float* dst = epi.out + orow * epi.ldo + col0;
-                    switch (epi.mode) {
-                        case EPI_STORE:
-                            store_row32(dst, v, left);
-                            break;
-                        case EPI_RESID: {
-                            for (int i = 0; i < 32 && i < left; i++) dst[i] = __fadd_rn(dst[i], v[i]);
-                            break;
-                        }
-                        default: {
-                            float lo[32];
-#pragma unroll
-                            for (int i = 0; i < 32; i++) {
-                                float x = v[i];
-                                if (epi.mode == EPI_GELU_SPLIT) x = gelu_erf(x);
-                                if (epi.mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
-                                if (zero_row) x = 0.0f;
-                                split_tf32(x, v[i], lo[i]);
-                            }
-                            store_row32(dst, v, left);
-                            store_row32(epi.out_lo + orow * epi.ldo + col0, lo, left);
-                        }
-                    }
+                    uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
+                    const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * PBK : kb * PBK;
+                    tma_load_2d(st, &tA_hi, &full[s], ka, m0 + tap);
+                    tma_load_2d(st + Cfg::A_BYTES, &tA_lo, &full[s], ka, m0 + tap);
+                    tma_load_2d(st + 2 * Cfg::A_BYTES, &tB_hi, &full[s], kb * PBK, n0);
+                    tma_load_2d(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tB_lo, &full[s], kb * PBK, n0);
                 }
             }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(BN);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, it++) {
+                const int buf = it & 1;
+                if (it >= 2 && !mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * Cfg::ACC_COLS;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (!mbar_wait(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_hi = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                    const uint32_t a_lo = a_hi + Cfg::A_BYTES;
+                    const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES;
+                    const uint32_t b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < PBK / 8; k++) {
+                        const uint32_t off = k * 32;
+                        const uint64_t dah = desc_k_sw64(a_hi + off), dal = desc_k_sw64(a_lo + off);
+                        const uint64_t dbh = desc_k_sw64(b_hi + off), dbl = desc_k_sw64(b_lo + off);
+                        umma_tf32(d, dal, dbh, idesc, (kb | k) != 0);
+                        umma_tf32(d, dah, dbl, idesc, 1);
+                        umma_tf32(d, dah, dbh, idesc, 1);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        int it = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+            const int buf = it & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            epilogue_tile<BN>(epi, tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS, m0, n0, M, N,
+                              q, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
     }
     tc_fence_before();
@@ -302,23 +448,24 @@ EncodeTiledFn encode_fn() {
 
 // 2-D map over a row-major fp32 matrix [rows, cols] (row stride ld elements),
 // box = 32 columns x box_rows rows, 128-byte swizzle, zero fill out of bounds.
-CUtensorMap make_map(const float* ptr, long long rows, long long cols, long long ld, int box_rows) {
-    using Key = std::tuple<const float*, long long, long long, long long, int>;
+CUtensorMap make_map(const float* ptr, long long rows, long long cols, long long ld, int box_rows, int box_cols = BK) {
+    using Key = std::tuple<const float*, long long, long long, long long, int, int>;
     static std::map<Key, CUtensorMap> cache;
     static std::mutex mu;
-    const Key key{ptr, rows, cols, ld, box_rows};
+    const Key key{ptr, rows, cols, ld, box_rows, box_cols};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
-    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 4) % 16 || cols % BK)
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 4) % 16 || cols % box_cols)
         throw Error(9, "GEMM operand is not 16-byte aligned or K is not a multiple of 32");
     CUtensorMap m;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
-                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             box_cols == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     if (cache.size() > 4096) cache.clear();
@@ -345,6 +492,37 @@ void launch(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M,
     N3D_CUDA(cudaGetLastError());
 }
 
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        N3D_CUDA(cudaGetDevice(&dev));
+        N3D_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    }
+    return n;
+}
+
+template <int BN>
+void launch_persistent(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                       int kb_per_tap, const Epi& epi, int* err) {
+    using Cfg = PCfg<BN>;
+    static bool attr = false;
+    if (!attr) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM));
+        attr = true;
+    }
+    const CUtensorMap a_hi = make_map(A.hi, A.rows, A.cols, A.ld, BM, PBK);
+    const CUtensorMap a_lo = make_map(A.lo, A.rows, A.cols, A.ld, BM, PBK);
+    const CUtensorMap b_hi = make_map(B.hi, B.rows, B.cols, B.ld, BN, PBK);
+    const CUtensorMap b_lo = make_map(B.lo, B.rows, B.cols, B.ld, BN, PBK);
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    gemm_persistent_kernel<BN><<<grid, 192, Cfg::SMEM, s>>>(a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                                             kb_per_tap > 0 ? kb_per_tap * (BK / PBK) : 0, epi, err);
+    N3D_CUDA(cudaGetLastError());
+}
+
 }  // namespace
 
 void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
@@ -367,10 +545,10 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     if ((epi.mode == EPI_QKV_ROPE || epi.mode == EPI_QKV_ATTN) && (bn % 64))
         throw Error(9, "QKV epilogue needs 64-column chunks");
     switch (bn) {
-        case 64: launch<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
-        case 128: launch<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
-        case 192: launch<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
-        default: launch<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 64: launch_persistent<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 128: launch_persistent<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        case 192: launch_persistent<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        default: launch_persistent<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
     }
 }
 

@@ -112,6 +112,18 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
     return d;
 }
 
+// Same for a K-major tile written with the 64-byte swizzle: rows of 64 B
+// (16 fp32), 8-row atoms 512 B apart, layout SWIZZLE_64B (4).
+__device__ __forceinline__ uint64_t desc_k_sw64(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+    d |= static_cast<uint64_t>(1) << 16;
+    d |= static_cast<uint64_t>(512 >> 4) << 32;
+    d |= static_cast<uint64_t>(1) << 46;
+    d |= static_cast<uint64_t>(4) << 61;
+    return d;
+}
+
 // Instruction descriptor for kind::tf32: D f32, A/B tf32, both K-major, M=128.
 __host__ __device__ constexpr uint32_t idesc_tf32(int n) {
     return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
