@@ -100,10 +100,8 @@ __global__ void __launch_bounds__(192, 1)
                 for (int a = 0; a < 2; a++) {
                     tma_load_2d(sb + a * KV_ATOM, &tKh, &kv_full[st], h * HD + 32 * a, row0 + j * KB);
                     tma_load_2d(sb + KV_BYTES + a * KV_ATOM, &tKl, &kv_full[st], h * HD + 32 * a, row0 + j * KB);
-                    tma_load_2d(sb + 2 * KV_BYTES + a * KV_ATOM, &tVh, &kv_full[st], j * KB + 32 * a,
-                                (b * heads + h) * HD);
-                    tma_load_2d(sb + 3 * KV_BYTES + a * KV_ATOM, &tVl, &kv_full[st], j * KB + 32 * a,
-                                (b * heads + h) * HD);
+                    tma_load_2d(sb + 2 * KV_BYTES + a * KV_ATOM, &tVh, &kv_full[st], row0 + j * KB + 32 * a, h * HD);
+                    tma_load_2d(sb + 3 * KV_BYTES + a * KV_ATOM, &tVl, &kv_full[st], row0 + j * KB + 32 * a, h * HD);
                 }
             }
         }
@@ -292,12 +290,14 @@ CUtensorMap map2d(const float* p, long long rows, long long cols, long long ld, 
 }  // namespace
 
 // Q, K: TF32 pairs [rows_cap, heads*64] (sequence b at rows b*S ..), RoPE applied.
-// V^T: TF32 pair [seqs*heads*64, vt_ld] (row (b*heads + h)*64 + d holds v[.., d] over keys).
+// V^T: TF32 pair [heads*64, vt_ld]; row h*64 + d holds v[r, h, d] at column r (global row).
 void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, const float* k_hi,
                          const float* k_lo, long long rows_cap, const float* vt_hi, const float* vt_lo,
                          long long vt_ld, int seqs, int S, const int* valid, int heads, float* ctx_hi,
                          float* ctx_lo, int* err) {
     if (seqs <= 0 || S <= 0) return;
+    if ((seqs > 1 && S % 4) || vt_ld % 4)
+        throw Error(9, "attention: the sequence stride and V^T row stride must be multiples of 4");
     static bool attr = false;
     if (!attr) {
         N3D_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -306,8 +306,8 @@ void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, c
     const long long W = (long long)heads * HD;
     const CUtensorMap qh = map2d(q_hi, rows_cap, W, W, QT), ql = map2d(q_lo, rows_cap, W, W, QT);
     const CUtensorMap kh = map2d(k_hi, rows_cap, W, W, KB), kl = map2d(k_lo, rows_cap, W, W, KB);
-    const CUtensorMap vh = map2d(vt_hi, (long long)seqs * W, S, vt_ld, HD);
-    const CUtensorMap vl = map2d(vt_lo, (long long)seqs * W, S, vt_ld, HD);
+    const CUtensorMap vh = map2d(vt_hi, W, (long long)seqs * S, vt_ld, HD);
+    const CUtensorMap vl = map2d(vt_lo, W, (long long)seqs * S, vt_ld, HD);
     dim3 grid((S + QT - 1) / QT, heads, seqs);
     attention_tc_kernel<<<grid, 192, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx_hi, ctx_lo, err);
     N3D_CUDA(cudaGetLastError());

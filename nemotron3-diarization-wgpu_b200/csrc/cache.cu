@@ -64,8 +64,8 @@ struct CacheParams {
 __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __restrict__ steps,
                                                            const float* __restrict__ win,
                                                            const float* __restrict__ logits, int stride,
-                                                           CacheParams cp, const float* __restrict__ silence,
-                                                           int P_max) {
+                                                           long long logit_rows, CacheParams cp,
+                                                           const float* __restrict__ silence, int P_max) {
     extern __shared__ float sm[];
     const int i = blockIdx.x;
     const SeqStep st = steps[i];
@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
     const int S = st.S;
     const int tid = threadIdx.x, nt = blockDim.x;
     const float* wrow = win + (long long)i * stride * hidden;
-    const float* lrow = logits + (long long)i * stride * sub * ns;
+    const float* lrow = logits + (long long)i * logit_rows * ns;  // head output keeps 2 pad rows per sequence
 
     float* probs = sm;
     float* cand = probs + stride * ns;
@@ -296,7 +296,8 @@ void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const f
     }
     CacheParams cp{c.hidden, c.ns, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
                    c.latest_boost};
-    cache_update_kernel<<<nseq, 512, smem, s>>>(steps, win, logits, stride, cp, silence, P);
+    cache_update_kernel<<<nseq, 512, smem, s>>>(steps, win, logits, stride, (long long)(stride + 2) * c.sub, cp,
+                                                silence, P);
     N3D_CUDA(cudaGetLastError());
 }
 

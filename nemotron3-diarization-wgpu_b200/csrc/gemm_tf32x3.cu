@@ -287,6 +287,123 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
+// ------------------------------------------------------- TMA-store epilogue
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+                 "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One warp's 32 x 32 fp32 block into a 4 KB 128-byte-swizzled staging box:
+// lane = box row, v = its 32 columns.
+__device__ __forceinline__ void stage_rows(uint8_t* box, int lane, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        *reinterpret_cast<float4*>(box + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+// Transposed: box row = element index d, column = lane.
+__device__ __forceinline__ void stage_cols(uint8_t* box, int lane, const float* v) {
+#pragma unroll
+    for (int d = 0; d < 32; d++)
+        *reinterpret_cast<float*>(box + d * 128 + ((((lane >> 2) ^ (d & 7)) << 4) | ((lane & 3) << 2))) = v[d];
+}
+
+// Hand the staged boxes to TMA: wait until the previous boxes have been read,
+// which the caller does before staging; here fence and issue.
+__device__ __forceinline__ void stage_begin(int lane) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+}
+__device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, const void* b0, const CUtensorMap* m1,
+                                            const void* b1, int x, int y) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(m0, b0, x, y);
+        if (m1) tma_store_2d(m1, b1, x, y);
+        bulk_commit();
+    }
+}
+
+// Epilogue with TMA stores, for modes whose output rows are the tile's rows:
+// EPI_STORE, EPI_SPLIT, EPI_GELU_SPLIT, EPI_RELU_SPLIT, EPI_QKV_ATTN.
+// `stg` is this warp's 8 KB staging area (hi box, lo box).
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
+                                                  int lane, uint8_t* stg) {
+    const int rowbase = m0 + q * 32;
+    if (rowbase >= M) return;  // whole warp past the end: nothing to load or store
+    const int r = rowbase + lane;
+    uint8_t* bhi = stg;
+    uint8_t* blo = stg + 4096;
+    if (epi.mode == EPI_QKV_ATTN) {
+        for (int c = 0; c < BN; c += 64) {
+            float v[64];
+            tmem_ld32(tl + c, v);
+            tmem_ld32(tl + c + 32, v + 32);
+            const int col0 = n0 + c;
+            if (col0 >= N) break;
+            const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
+            if (sec < 2) {
+                const int pos = r % epi.rope_seq;
+                const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
+                const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const float x1 = v[i], x2 = v[32 + i];
+                    v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
+                    v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                }
+            }
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                float hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) split_tf32(v[32 * half + i], hi[i], lo[i]);
+                stage_begin(lane);
+                if (sec < 2) {
+                    stage_rows(bhi, lane, hi);
+                    stage_rows(blo, lane, lo);
+                    stage_issue(lane, sec == 0 ? &epi.map_out : &epi.map_k_hi, bhi,
+                                sec == 0 ? &epi.map_out_lo : &epi.map_k_lo, blo, hcol + 32 * half, rowbase);
+                } else {
+                    stage_cols(bhi, lane, hi);
+                    stage_cols(blo, lane, lo);
+                    stage_issue(lane, &epi.map_vt_hi, bhi, &epi.map_vt_lo, blo, rowbase, hcol + 32 * half);
+                }
+            }
+        }
+    } else {
+        const bool pair = epi.mode != EPI_STORE;
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tl + c, v);
+            const int col0 = n0 + c;
+            if (col0 >= N) break;
+            float lo[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float b = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
+                float x = __fadd_rn(v[i], b);
+                if (epi.mode == EPI_GELU_SPLIT) x = gelu_erf(x);
+                if (epi.mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
+                if (pair)
+                    split_tf32(x, v[i], lo[i]);
+                else
+                    v[i] = x;
+            }
+            stage_begin(lane);
+            stage_rows(bhi, lane, v);
+            if (pair) stage_rows(blo, lane, lo);
+            stage_issue(lane, &epi.map_out, bhi, pair ? &epi.map_out_lo : nullptr, blo, col0, rowbase);
+        }
+    }
+}
+
 // Persistent variant: one CTA per SM walks the output tiles (t = blockIdx.x,
 // + gridDim.x, ...), k-blocks of 16 fp32 (64 B rows, 64-byte swizzle) so that
 // even BN = 256 gets 4 shared-memory stages, and two TMEM accumulators so the
@@ -298,11 +415,12 @@ struct PCfg {
     static constexpr int A_BYTES = BM * PBK * 4;
     static constexpr int B_BYTES = BN * PBK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+    static constexpr int STAGING = 4 * 8192;  // per epilogue warp: hi + lo 32 x 32 boxes
+    static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
     static constexpr int TMEM_COLS = 2 * ACC_COLS;
-    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
     static_assert(STAGES >= 3, "persistent GEMM wants at least three stages");
 };
 
@@ -414,12 +532,18 @@ __global__ void __launch_bounds__(192, 1)
             if (!ok) break;
             tc_fence_after();
             const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
-            epilogue_tile<BN>(epi, tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS, m0, n0, M, N,
-                              q, lane);
+            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS;
+            if (epi.tma)
+                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+            else
+                epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -456,8 +580,8 @@ CUtensorMap make_map(const float* ptr, long long rows, long long cols, long long
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
-    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 4) % 16 || cols % box_cols)
-        throw Error(9, "GEMM operand is not 16-byte aligned or K is not a multiple of 32");
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 4) % 16)
+        throw Error(9, "GEMM operand or output is not 16-byte aligned");
     CUtensorMap m;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
@@ -524,6 +648,10 @@ void launch_persistent(cudaStream_t s, const SplitOperand& A, const SplitOperand
 }
 
 }  // namespace
+
+CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld) {
+    return make_map(p, rows, cols, ld, 32, 32);
+}
 
 void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
                  int kb_per_tap, const Epi& epi, int* err) {

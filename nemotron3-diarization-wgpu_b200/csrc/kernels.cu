@@ -29,7 +29,8 @@ __device__ __forceinline__ float warp_max(float v) {
 // Writes either a plain fp32 row (out_lo == nullptr) or a TF32 hi/lo pair.
 template <int VPL>
 __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
-                                  const float* __restrict__ b, float* __restrict__ out, float* __restrict__ out_lo) {
+                                  const float* __restrict__ b, float* __restrict__ out, float* __restrict__ out_lo,
+                                  const float* __restrict__ delta = nullptr, float* __restrict__ x_out = nullptr) {
     constexpr int COLS = VPL * 32;
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -43,6 +44,19 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, c
         v[i + 1] = t.y;
         v[i + 2] = t.z;
         v[i + 3] = t.w;
+    }
+    if (delta) {  // residual stream: x += delta, exactly the reference's x1[i] += out[i]
+        const float* dsrc = delta + row * COLS;
+#pragma unroll
+        for (int i = 0; i < VPL; i += 4) {
+            const int c = (i / 4) * 128 + lane * 4;
+            const float4 t = *reinterpret_cast<const float4*>(dsrc + c);
+            v[i] = __fadd_rn(v[i], t.x);
+            v[i + 1] = __fadd_rn(v[i + 1], t.y);
+            v[i + 2] = __fadd_rn(v[i + 2], t.z);
+            v[i + 3] = __fadd_rn(v[i + 3], t.w);
+            *reinterpret_cast<float4*>(x_out + row * COLS + c) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        }
     }
     float s = 0.0f;
 #pragma unroll
@@ -342,6 +356,16 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
         layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
+                           const float* b, float* out, float* out_lo) {
+    if (rows <= 0) return;
+    if (cols != 512) throw Error(13, "add_layer_norm supports 512 columns");
+    const int warps = 8;
+    const unsigned grid = (unsigned)((rows + warps - 1) / warps);
+    layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo, delta, x);
     N3D_CUDA(cudaGetLastError());
 }
 

@@ -609,24 +609,25 @@ void Model::prof_collect() {
     pending_.clear();
 }
 
-// The 31-layer tower on B sequences of stride S rows held in ws "win".
-// Output: the final LayerNorm as a TF32 pair in "n_hi"/"n_lo" (and plain in
-// enc_plain when given).
+// The 31-layer tower on B sequences of stride S rows (S a multiple of 4) held in
+// ws "win".  Output: the final LayerNorm as a TF32 pair in "n_hi"/"n_lo" (and
+// plain in enc_plain when given).  Residual adds are fused into the LayerNorm
+// that follows them, so every GEMM epilogue is a pure (TMA) store.
 void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain) {
     const Config& c = cfg_;
     const long long M = (long long)B * S, h = c.hidden;
-    const long long cap = M;
     float* win = (float*)ws("win", M * h * 4);
     float* x = (float*)ws("x", M * h * 4);
+    float* tmp = (float*)ws("tmp", M * h * 4);
     float* n_hi = (float*)ws("n_hi", M * h * 4);
     float* n_lo = (float*)ws("n_lo", M * h * 4);
     float* q_hi = (float*)ws("q_hi", M * h * 4);
     float* q_lo = (float*)ws("q_lo", M * h * 4);
     float* k_hi = (float*)ws("k_hi", M * h * 4);
     float* k_lo = (float*)ws("k_lo", M * h * 4);
-    const long long vt_ld = (S + 3) / 4 * 4;
-    float* vt_hi = (float*)ws("vt_hi", (long long)B * h * vt_ld * 4);
-    float* vt_lo = (float*)ws("vt_lo", (long long)B * h * vt_ld * 4);
+    const long long vt_ld = M;  // V^T [heads*64, M]: column = global row
+    float* vt_hi = (float*)ws("vt_hi", h * vt_ld * 4);
+    float* vt_lo = (float*)ws("vt_lo", h * vt_ld * 4);
     const long long rows_qk = ws_["q_hi"].bytes / (h * 4);
     float* ctx_hi = (float*)ws("ctx_hi", M * h * 4);
     float* ctx_lo = (float*)ws("ctx_lo", M * h * 4);
@@ -634,37 +635,48 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     float* f_lo = (float*)ws("f_lo", M * c.inter * 4);
     const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_ctx = ws_["ctx_hi"].bytes / (h * 4);
     const long long rows_f = ws_["f_hi"].bytes / (c.inter * 4);
-    (void)cap;
     const SplitOperand An{n_hi, n_lo, rows_n, h, h};
     const SplitOperand Actx{ctx_hi, ctx_lo, rows_ctx, h, h};
     const SplitOperand Af{f_hi, f_lo, rows_f, c.inter, c.inter};
 
-    const double ln_bytes = (double)M * h * 4 * 3;  // read x, write a TF32 pair
+    Epi e;  // QKV: Q/K pairs with RoPE, V^T pair
+    e.mode = EPI_QKV_ATTN;
+    e.tma = 1;
+    e.map_out = make_store_map(q_hi, M, h, h);
+    e.map_out_lo = make_store_map(q_lo, M, h, h);
+    e.map_k_hi = make_store_map(k_hi, M, h, h);
+    e.map_k_lo = make_store_map(k_lo, M, h, h);
+    e.map_vt_hi = make_store_map(vt_hi, h, M, vt_ld);
+    e.map_vt_lo = make_store_map(vt_lo, h, M, vt_ld);
+    e.cos_t = rope_cos_;
+    e.sin_t = rope_sin_;
+    e.rope_seq = S;
+    e.head_dim = (int)(h / c.heads);
+    e.q_cols = (int)h;
+    e.k_cols = (int)h;
+    e.heads = c.heads;
+    Epi eo;  // o_proj / fc2: acc + bias -> tmp (added into x by the next LayerNorm)
+    eo.mode = EPI_STORE;
+    eo.tma = 1;
+    eo.map_out = make_store_map(tmp, M, h, h);
+    Epi e1;  // fc1: GELU(acc + bias) -> TF32 pair
+    e1.mode = EPI_GELU_SPLIT;
+    e1.tma = 1;
+    e1.map_out = make_store_map(f_hi, M, c.inter, c.inter);
+    e1.map_out_lo = make_store_map(f_lo, M, c.inter, c.inter);
+
+    const double ln_bytes = (double)M * h * 4 * 5;  // read x + delta, write x and a TF32 pair
     prof_begin();
     launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, x, nullptr);
     prof_end(K_LN, 0, (double)M * h * 8);
     for (int l = 0; l < c.layers; l++) {
         const DevLayer& L = layers_[l];
         prof_begin();
-        launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
+        if (l == 0)
+            launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
+        else
+            launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
         prof_end(K_LN, 0, ln_bytes);
-        Epi e;
-        e.mode = EPI_QKV_ATTN;
-        e.out = q_hi;
-        e.out_lo = q_lo;
-        e.k_hi = k_hi;
-        e.k_lo = k_lo;
-        e.vt_hi = vt_hi;
-        e.vt_lo = vt_lo;
-        e.vt_ld = vt_ld;
-        e.heads = c.heads;
-        e.ldo = h;
-        e.cos_t = rope_cos_;
-        e.sin_t = rope_sin_;
-        e.rope_seq = S;
-        e.head_dim = (int)(h / c.heads);
-        e.q_cols = (int)h;
-        e.k_cols = (int)h;
         prof_begin();
         gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM, 2.0 * M * 3 * h * h, 0);
@@ -672,57 +684,45 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         launch_attention_tc(stream_, q_hi, q_lo, k_hi, k_lo, rows_qk, vt_hi, vt_lo, vt_ld, B, S, d_valid, c.heads,
                             ctx_hi, ctx_lo, dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
-        Epi eo;
-        eo.mode = EPI_RESID;
-        eo.out = x;
-        eo.ldo = h;
         eo.bias = L.o.bias;
         prof_begin();
         gemm_tf32x3(stream_, Actx, L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
         prof_end(K_GEMM, 2.0 * M * h * h, 0);
         prof_begin();
-        launch_layer_norm(stream_, x, M, (int)h, L.ln2_w, L.ln2_b, n_hi, n_lo);
+        launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln2_w, L.ln2_b, n_hi, n_lo);
         prof_end(K_LN, 0, ln_bytes);
-        Epi e1;
-        e1.mode = EPI_GELU_SPLIT;
-        e1.out = f_hi;
-        e1.out_lo = f_lo;
-        e1.ldo = c.inter;
         e1.bias = L.fc1.bias;
         prof_begin();
         gemm_tf32x3(stream_, An, L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
         prof_end(K_GEMM, 2.0 * M * c.inter * h, 0);
-        Epi e2;
-        e2.mode = EPI_RESID;
-        e2.out = x;
-        e2.ldo = h;
-        e2.bias = L.fc2.bias;
+        eo.bias = L.fc2.bias;
         prof_begin();
-        gemm_tf32x3(stream_, Af, L.fc2.op(), (int)M, (int)h, c.inter, 0, e2, dev_err_);
+        gemm_tf32x3(stream_, Af, L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
         prof_end(K_GEMM, 2.0 * M * h * c.inter, 0);
     }
     prof_begin();
-    launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, n_hi, n_lo);
+    launch_add_layer_norm(stream_, x, tmp, M, (int)h, fin_ln_w_, fin_ln_b_, n_hi, n_lo);
     prof_end(K_LN, 0, ln_bytes);
     if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, enc_plain, nullptr);
     (void)d_seq_len;
 }
 
 // Classification head (src/head.rs:147-157) on the encoder output in n_hi/n_lo:
-// proj -> implicit-GEMM k=3 conv with the sub-pixel reshape folded into the
-// store -> dense + ReLU + out_proj fused.  Logits land in ws "logits"
-// [B * S * sub, ns].
+// proj into a per-sequence zero-padded layout [B, S+2, hh] -> implicit-GEMM k=3
+// conv over it (its output keeps that padded row layout; the sub-pixel reshape
+// is free on row-major memory) -> dense + ReLU + out_proj fused.  Logits land
+// in ws "logits" with sequence i at rows i * (S + 2) * sub.
 void Model::head(int B, int S, const int* d_seq_len) {
     const Config& c = cfg_;
     const long long M = (long long)B * S, h = c.hidden, hh = c.head_hidden, up = c.sub;
-    const long long PR = (long long)B * (S + 2);
+    const long long PR = (long long)B * (S + 2), MC = PR - 2;
     float* n_hi = (float*)ws("n_hi", M * h * 4);
     float* n_lo = (float*)ws("n_lo", M * h * 4);
     float* p_hi = (float*)ws("p_hi", PR * hh * 4);
     float* p_lo = (float*)ws("p_lo", PR * hh * 4);
-    float* u_hi = (float*)ws("u_hi", M * up * hh * 4);
-    float* u_lo = (float*)ws("u_lo", M * up * hh * 4);
-    float* logits = (float*)ws("logits", M * up * 8 * 4);
+    float* u_hi = (float*)ws("u_hi", PR * up * hh * 4);
+    float* u_lo = (float*)ws("u_lo", PR * up * hh * 4);
+    float* logits = (float*)ws("logits", PR * up * c.num_speakers * 4);
     const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_p = ws_["p_hi"].bytes / (hh * 4);
     const long long rows_u = ws_["u_hi"].bytes / (hh * 4);
     N3D_CUDA(cudaMemsetAsync(p_hi, 0, PR * hh * 4, stream_));
@@ -744,16 +744,12 @@ void Model::head(int B, int S, const int* d_seq_len) {
     prof_end(K_GEMM, 2.0 * M * hh * h, 0);
     Epi ec;
     ec.mode = EPI_RELU_SPLIT;
-    ec.out = u_hi;
-    ec.out_lo = u_lo;
-    ec.ldo = up * hh;
+    ec.tma = 1;
     ec.bias = conv_.bias;
-    ec.rdiv = S + 2;
-    ec.rkeep = S;
-    ec.rmul = S;
-    ec.roff = 0;
+    ec.map_out = make_store_map(u_hi, MC, up * hh, up * hh);
+    ec.map_out_lo = make_store_map(u_lo, MC, up * hh, up * hh);
     prof_begin();
-    gemm_tf32x3(stream_, SplitOperand{p_hi, p_lo, rows_p, hh, hh}, conv_.op(), (int)(PR - 2), (int)(up * hh),
+    gemm_tf32x3(stream_, SplitOperand{p_hi, p_lo, rows_p, hh, hh}, conv_.op(), (int)MC, (int)(up * hh),
                 (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
     prof_end(K_GEMM, 2.0 * M * up * hh * 3 * hh, 0);
     Epi ed;
@@ -765,8 +761,8 @@ void Model::head(int B, int S, const int* d_seq_len) {
     ed.b2 = out_b_;
     ed.n2 = c.num_speakers;
     prof_begin();
-    gemm_tf32x3(stream_, SplitOperand{u_hi, u_lo, rows_u, hh, hh}, dense_.op(), (int)(M * up), (int)hh, (int)hh, 0,
-                ed, dev_err_);
+    gemm_tf32x3(stream_, SplitOperand{u_hi, u_lo, rows_u, hh, hh}, dense_.op(), (int)(MC * up), (int)hh, (int)hh,
+                0, ed, dev_err_);
     prof_end(K_GEMM, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
 }
 
@@ -906,7 +902,7 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 valid.push_back(sp.valid);
                 Smax = std::max(Smax, sp.S);
             }
-            step_S[w] = Smax;
+            step_S[w] = (Smax + 3) / 4 * 4;  // row stride: a multiple of 4 keeps TMA coordinates 16-byte aligned
         }
         step_first[max_steps] = (int)table.size();
         // Clips whose plans skip a step (S == 0) must still carry state forward:
@@ -1026,18 +1022,20 @@ void Model::forward_window(const float* embeds, int frames, int valid, float* en
     if (frames <= 0 || frames > s_cap_)
         throw Error(kStatusGpu, "seq " + std::to_string(frames) + " outside 1..=1024");
     valid = std::min(valid, frames);
+    const int S = (frames + 3) / 4 * 4;  // row stride (multiple of 4), rows past `frames` are zero
     const long long M = frames, h = c.hidden;
-    float* win = (float*)ws("win", M * h * 4);
+    float* win = (float*)ws("win", (long long)S * h * 4);
+    N3D_CUDA(cudaMemsetAsync(win, 0, (long long)S * h * 4, stream_));
     N3D_CUDA(cudaMemcpyAsync(win, embeds, M * h * 4, cudaMemcpyHostToDevice, stream_));
     int* d_len = (int*)ws("seq_len", 4);
     int* d_valid = (int*)ws("valid", 4);
     N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
     N3D_CUDA(cudaMemcpyAsync(d_valid, &valid, 4, cudaMemcpyHostToDevice, stream_));
-    float* enc = enc_out ? (float*)ws("enc_plain", M * h * 4) : nullptr;
-    tower(1, frames, d_len, d_valid, enc);
+    float* enc = enc_out ? (float*)ws("enc_plain", (long long)S * h * 4) : nullptr;
+    tower(1, S, d_len, d_valid, enc);
     if (enc_out) N3D_CUDA(cudaMemcpyAsync(enc_out, enc, M * h * 4, cudaMemcpyDeviceToHost, stream_));
     if (logits) {
-        head(1, frames, d_len);
+        head(1, S, d_len);
         N3D_CUDA(cudaMemcpyAsync(logits, ws("logits", 0), M * c.sub * c.num_speakers * 4, cudaMemcpyDeviceToHost,
                                  stream_));
     }
@@ -1050,15 +1048,17 @@ void Model::head_forward(const float* enc, int frames, float* logits) {
     N3D_CUDA(cudaSetDevice(device_));
     if (frames <= 0 || frames > s_cap_)
         throw Error(kStatusGpu, "head frames " + std::to_string(frames) + " outside 1..=1024");
+    const int S = (frames + 3) / 4 * 4;
     const long long M = frames, h = c.hidden;
-    float* plain = (float*)ws("enc_plain", M * h * 4);
-    float* n_hi = (float*)ws("n_hi", M * h * 4);
-    float* n_lo = (float*)ws("n_lo", M * h * 4);
+    float* plain = (float*)ws("enc_plain", (long long)S * h * 4);
+    float* n_hi = (float*)ws("n_hi", (long long)S * h * 4);
+    float* n_lo = (float*)ws("n_lo", (long long)S * h * 4);
+    N3D_CUDA(cudaMemsetAsync(plain, 0, (long long)S * h * 4, stream_));
     N3D_CUDA(cudaMemcpyAsync(plain, enc, M * h * 4, cudaMemcpyHostToDevice, stream_));
-    launch_split(stream_, plain, M * h, n_hi, n_lo);
+    launch_split(stream_, plain, (long long)S * h, n_hi, n_lo);
     int* d_len = (int*)ws("seq_len", 4);
     N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
-    head(1, frames, d_len);
+    head(1, S, d_len);
     N3D_CUDA(cudaMemcpyAsync(logits, ws("logits", 0), M * c.sub * c.num_speakers * 4, cudaMemcpyDeviceToHost,
                              stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));

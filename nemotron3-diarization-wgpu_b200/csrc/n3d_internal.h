@@ -53,6 +53,11 @@ struct Epi {
     int rope_seq = 1;
     int head_dim = 64;
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
+    // Stores through TMA (tma != 0): tensor maps over the destinations, box 32 columns
+    // x 32 rows, 128-byte swizzle.  map_out/map_out_lo: the output (pair); for
+    // EPI_QKV_ATTN also map_k_* (K pair) and map_vt_* over V^T [heads*64, rows].
+    int tma = 0;
+    CUtensorMap map_out, map_out_lo, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
     // EPI_QKV_ATTN destinations
     float* k_hi = nullptr;
     float* k_lo = nullptr;
@@ -73,6 +78,9 @@ struct SplitOperand {
     long long rows = 0, cols = 0, ld = 0;
 };
 
+// TMA-store map (box 32 x 32, 128-byte swizzle) over a row-major fp32 matrix.
+CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
+
 // C[M, N] = A[M, K] * B[N, K]^T in 3xTF32 on tcgen05. `kb_per_tap` > 0 turns on
 // the shifted-row (implicit k=3 conv) mode: k-block kb reads A at column
 // (kb % kb_per_tap) * 32 and row m0 + kb / kb_per_tap.
@@ -82,6 +90,9 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
 // --------------------------------------------------------------- other kernels
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
                        float* out, float* out_lo);
+// Residual add fused into the next LayerNorm: x += delta (in place), out = LN(x) as a TF32 pair.
+void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
+                           const float* b, float* out, float* out_lo);
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
                       int head_dim, float* ctx_hi, float* ctx_lo);
 // Log-mel frames: frame f reads audio[f_base[f] + p] for p in [p0, p0 + n_fft) with
@@ -93,7 +104,9 @@ void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, con
                 const long long* f_out);
 // x -> (hi, lo) TF32 pair, elementwise.
 void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
-// tcgen05 attention, head_dim 64 (attention_tc.cu).  ctx_lo == nullptr writes plain fp32.
+// tcgen05 attention, head_dim 64 (attention_tc.cu).  Q, K: TF32 pairs [rows_cap, heads*64]
+// with sequence b at rows b*S..; V^T: TF32 pair [heads*64, vt_ld] whose column is the
+// global row (S and the row stride must be multiples of 4).  ctx_lo == nullptr writes plain fp32.
 void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, const float* k_hi,
                          const float* k_lo, long long rows_cap, const float* vt_hi, const float* vt_lo,
                          long long vt_ld, int seqs, int S, const int* valid, int heads, float* ctx_hi,
