@@ -197,7 +197,9 @@ n3d_status n3d_attention(int device, const float *d_q, const float *d_k, const f
  * STEP_PROFILE / STAGE_BENCH (src/gpu_engine.rs:1682-1690, src/model.rs:417-473,
  * src/bin/gpu_check.rs:132-289).  Enabling resets the counters. */
 typedef struct n3d_kernel_stats {
-    const char *name;     /* "gemm_tf32x3", "attention", "layer_norm", "mel", "cache_update", "assemble", "other" */
+    const char *name;     /* "attention", "layer_norm", "mel", "cache_update", "assemble", and one
+                             "gemm_*" class per GEMM site (qkv, o, fc1, fc2, head_proj, head_conv,
+                             head_dense, embed) */
     size_t launches;
     double ms;            /* summed device time */
     double flops;         /* algorithmic FLOPs of those launches (2*M*N*K for GEMMs) */

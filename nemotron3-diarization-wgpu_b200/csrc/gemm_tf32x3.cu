@@ -349,14 +349,22 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             if (col0 >= N) break;
             const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
             if (sec < 2) {
+                // the tables repeat their first half (cat(freqs, freqs)), so one float4 of
+                // cos and of sin serves four rotation pairs
                 const int pos = r % epi.rope_seq;
-                const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
-                const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
+                const float4* cs = reinterpret_cast<const float4*>(epi.cos_t + (long long)pos * epi.head_dim);
+                const float4* sn = reinterpret_cast<const float4*>(epi.sin_t + (long long)pos * epi.head_dim);
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const float x1 = v[i], x2 = v[32 + i];
-                    v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
-                    v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
+                for (int i4 = 0; i4 < 8; i4++) {
+                    const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+                    const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int i = 4 * i4 + j;
+                        const float x1 = v[i], x2 = v[32 + i];
+                        v[i] = __fsub_rn(__fmul_rn(x1, cc[j]), __fmul_rn(x2, ss[j]));
+                        v[32 + i] = __fadd_rn(__fmul_rn(x2, cc[j]), __fmul_rn(x1, ss[j]));
+                    }
                 }
             }
 #pragma unroll
@@ -384,11 +392,23 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             tmem_ld32(tl + c, v);
             const int col0 = n0 + c;
             if (col0 >= N) break;
-            float lo[32];
+            float lo[32], bias[32];
+            if (epi.bias != nullptr && col0 + 32 <= N) {
+#pragma unroll
+                for (int i4 = 0; i4 < 8; i4++) {
+                    const float4 b4 = __ldg(reinterpret_cast<const float4*>(epi.bias + col0) + i4);
+                    bias[4 * i4] = b4.x;
+                    bias[4 * i4 + 1] = b4.y;
+                    bias[4 * i4 + 2] = b4.z;
+                    bias[4 * i4 + 3] = b4.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) bias[i] = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
+            }
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-                const float b = (epi.bias != nullptr && col0 + i < N) ? epi.bias[col0 + i] : 0.0f;
-                float x = __fadd_rn(v[i], b);
+                float x = __fadd_rn(v[i], bias[i]);
                 if (epi.mode == EPI_GELU_SPLIT) x = gelu_erf(x);
                 if (epi.mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
                 if (pair)

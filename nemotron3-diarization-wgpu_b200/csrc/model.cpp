@@ -679,7 +679,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         prof_end(K_LN, 0, ln_bytes);
         prof_begin();
         gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
-        prof_end(K_GEMM, 2.0 * M * 3 * h * h, 0);
+        prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);
         prof_begin();
         launch_attention_tc(stream_, q_hi, q_lo, k_hi, k_lo, rows_qk, vt_hi, vt_lo, vt_ld, B, S, d_valid, c.heads,
                             ctx_hi, ctx_lo, dev_err_);
@@ -687,18 +687,18 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         eo.bias = L.o.bias;
         prof_begin();
         gemm_tf32x3(stream_, Actx, L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
-        prof_end(K_GEMM, 2.0 * M * h * h, 0);
+        prof_end(K_GEMM_O, 2.0 * M * h * h, 0);
         prof_begin();
         launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln2_w, L.ln2_b, n_hi, n_lo);
         prof_end(K_LN, 0, ln_bytes);
         e1.bias = L.fc1.bias;
         prof_begin();
         gemm_tf32x3(stream_, An, L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
-        prof_end(K_GEMM, 2.0 * M * c.inter * h, 0);
+        prof_end(K_GEMM_FC1, 2.0 * M * c.inter * h, 0);
         eo.bias = L.fc2.bias;
         prof_begin();
         gemm_tf32x3(stream_, Af, L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
-        prof_end(K_GEMM, 2.0 * M * h * c.inter, 0);
+        prof_end(K_GEMM_FC2, 2.0 * M * h * c.inter, 0);
     }
     prof_begin();
     launch_add_layer_norm(stream_, x, tmp, M, (int)h, fin_ln_w_, fin_ln_b_, n_hi, n_lo);
@@ -741,7 +741,7 @@ void Model::head(int B, int S, const int* d_seq_len) {
     prof_begin();
     gemm_tf32x3(stream_, SplitOperand{n_hi, n_lo, rows_n, h, h}, proj_.op(), (int)M, (int)hh, (int)h, 0, ep,
                 dev_err_);
-    prof_end(K_GEMM, 2.0 * M * hh * h, 0);
+    prof_end(K_GEMM_PROJ, 2.0 * M * hh * h, 0);
     Epi ec;
     ec.mode = EPI_RELU_SPLIT;
     ec.tma = 1;
@@ -751,7 +751,7 @@ void Model::head(int B, int S, const int* d_seq_len) {
     prof_begin();
     gemm_tf32x3(stream_, SplitOperand{p_hi, p_lo, rows_p, hh, hh}, conv_.op(), (int)MC, (int)(up * hh),
                 (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
-    prof_end(K_GEMM, 2.0 * M * up * hh * 3 * hh, 0);
+    prof_end(K_GEMM_CONV, 2.0 * M * up * hh * 3 * hh, 0);
     Epi ed;
     ed.mode = EPI_DENSE_OUT;
     ed.out = logits;
@@ -763,7 +763,7 @@ void Model::head(int B, int S, const int* d_seq_len) {
     prof_begin();
     gemm_tf32x3(stream_, SplitOperand{u_hi, u_lo, rows_u, hh, hh}, dense_.op(), (int)(MC * up), (int)hh, (int)hh,
                 0, ed, dev_err_);
-    prof_end(K_GEMM, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
+    prof_end(K_GEMM_DENSE, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
 }
 
 void Model::run_batch(int mode, const std::vector<const float*>& host_audio, const float* d_audio_in,
@@ -850,7 +850,7 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
             prof_begin();
             gemm_tf32x3(stream_, SplitOperand{mel_hi, mel_lo, rows_cap, K_emb, K_emb}, embed_.op(),
                         (int)total_groups, h, (int)K_emb, 0, e, dev_err_);
-            prof_end(K_GEMM, 2.0 * total_groups * h * K_emb, 0);
+            prof_end(K_GEMM_EMBED, 2.0 * total_groups * h * K_emb, 0);
         }
         // ---- per-clip state and outputs
         int max_steps = 0;

@@ -90,7 +90,10 @@ struct Buf {
 };
 
 // Per-kernel-class device time, measured with CUDA events on the model's stream.
-enum KernelClass : int { K_GEMM = 0, K_ATTN, K_LN, K_MEL, K_CACHE, K_ASSEMBLE, K_OTHER, K_NCLASS };
+enum KernelClass : int {
+    K_GEMM = 0, K_ATTN, K_LN, K_MEL, K_CACHE, K_ASSEMBLE, K_OTHER,
+    K_GEMM_QKV, K_GEMM_O, K_GEMM_FC1, K_GEMM_FC2, K_GEMM_PROJ, K_GEMM_CONV, K_GEMM_DENSE, K_GEMM_EMBED, K_NCLASS
+};
 struct ProfTotals {
     long long launches = 0;
     double ms = 0.0, flops = 0.0, bytes = 0.0;
