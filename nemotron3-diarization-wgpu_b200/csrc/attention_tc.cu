@@ -12,7 +12,8 @@
 //   warp 1      TMEM owner; one thread issues S_j = Q K_j^T (into one of two S
 //               buffers, so block j+1's QK^T overlaps block j's softmax) and
 //               O_j = P_j V_j with P_j read straight from TMEM
-//   warps 2..5  softmax, one query row per thread (TMEM lane): online max/sum,
+//   warps 2..9  softmax, two warps per query row (TMEM lane): each takes half of
+//               the block's keys and half of the output columns; online max/sum,
 //               P_j as a TF32 pair written back to TMEM, O folded in registers
 // TMEM columns: S[2] 0..127, P_hi/P_lo[2] 128..383, O[2] 384..511.
 // Every wait is bounded; an expired wait records its site in *err.
@@ -32,14 +33,15 @@ constexpr int KV_ATOM = KB * 128;        // [64 rows x 128 B] = 8 KB
 constexpr int Q_BYTES = 2 * Q_ATOM;      // one of hi / lo: 32 KB
 constexpr int KV_BYTES = 2 * KV_ATOM;    // one of K_hi / K_lo / V_hi / V_lo: 16 KB
 constexpr int STAGE_BYTES = 4 * KV_BYTES;
-constexpr int SMEM_BYTES = 2 * Q_BYTES + 2 * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = 2 * Q_BYTES + 2 * STAGE_BYTES + 1024 + 256 + 6 * QT * 4;
+constexpr int THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps
 constexpr uint32_t COL_S = 0, COL_PHI = 128, COL_PLO = 192, COL_O = 384;  // P buffers: +128 per buffer
 constexpr int DEV_TIMEOUT_ATTN = 5;
 
 __device__ __forceinline__ uint32_t col_p_hi(int b) { return COL_PHI + 128u * b; }
 __device__ __forceinline__ uint32_t col_p_lo(int b) { return COL_PLO + 128u * b; }
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tQh, const __grid_constant__ CUtensorMap tQl,
                         const __grid_constant__ CUtensorMap tKh, const __grid_constant__ CUtensorMap tKl,
                         const __grid_constant__ CUtensorMap tVh, const __grid_constant__ CUtensorMap tVl, int S,
@@ -60,6 +62,8 @@ __global__ void __launch_bounds__(192, 1)
     uint64_t* o_full = bars + 11;   // 2
     uint64_t* o_free = bars + 13;   // 2
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    float* red_max = reinterpret_cast<float*>(bars + 32);  // [2 blocks][2 halves][QT]
+    float* red_sum = red_max + 4 * QT;                      // [2 halves][QT]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
@@ -73,10 +77,10 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&kv_full[i], 1);
             mbar_init(&kv_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
-            mbar_init(&p_full[i], 4);
+            mbar_init(&s_free[i], 8);
+            mbar_init(&p_full[i], 8);
             mbar_init(&o_full[i], 1);
-            mbar_init(&o_free[i], 4);
+            mbar_init(&o_free[i], 8);
         }
         mbar_fence_init();
     }
@@ -155,66 +159,67 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
-        // ---- softmax warps: thread owns query row r of the tile (TMEM lane r)
-        const int qd = warp & 3;
+        // ---- softmax warps 2..9: warp w owns TMEM lane quadrant w % 4 (query rows) and
+        // half hf of each 64-key block and of the 64 output columns; the two warps of
+        // a quadrant exchange row maxima and sums through shared memory.
+        const int qd = warp & 3, hf = (warp - 2) >> 2;
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-        const float scaling = 0.125f;  // 1 / sqrt(64)
-        float o[HD];
+        const uint32_t bar_id = 1 + qd;  // named barrier of this quadrant's two warps
+        const float scaling = 0.125f;    // 1 / sqrt(64)
+        float o[32];
 #pragma unroll
-        for (int d = 0; d < HD; d++) o[d] = 0.0f;
+        for (int d = 0; d < 32; d++) o[d] = 0.0f;
         float m = -INFINITY, l = 0.0f, c_prev = 0.0f;
         bool ok = true;
-        auto fold = [&](int jj, float c) {
-            // O <- O * c + PV_jj (the previous rescale factor is folded with it)
+        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
+        auto fold = [&](int jj, float c) {  // O <- O * c + PV_jj, this warp's 32 columns
+            float v[32];
+            tmem_ld32(lb + COL_O + 64u * (jj & 1) + 32 * hf, v);
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                float v[32];
-                tmem_ld32(lb + COL_O + 64u * (jj & 1) + 32 * half, v);
-#pragma unroll
-                for (int i = 0; i < 32; i++) o[32 * half + i] = fmaf(o[32 * half + i], c, v[i]);
-            }
+            for (int i = 0; i < 32; i++) o[i] = fmaf(o[i], c, v[i]);
         };
         for (int j = 0; j < nblk; j++) {
             const int bf = j & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[bf], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN));
-            if (!ok) break;
+            // after an expired wait the loop keeps running (work skipped, results unused)
+            // so both warps of the pair reach every pair_sync
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[bf], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN));
             tc_fence_after();
-            float s[KB];
-            tmem_ld32(lb + COL_S + 64u * bf, s);
-            tmem_ld32(lb + COL_S + 64u * bf + 32, s + 32);
+            float s[32];
+            tmem_ld32(lb + COL_S + 64u * bf + 32 * hf, s);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[bf]);
-            float mx = m;
+            float mloc = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < KB; c++) {
-                s[c] = (j * KB + c < valid) ? s[c] * scaling : -INFINITY;
-                mx = fmaxf(mx, s[c]);
+            for (int c = 0; c < 32; c++) {
+                s[c] = (j * KB + 32 * hf + c < valid) ? s[c] * scaling : -INFINITY;
+                mloc = fmaxf(mloc, s[c]);
             }
+            red_max[(bf * 2 + hf) * QT + r] = mloc;
+            pair_sync();
+            const float mx = fmaxf(m, fmaxf(mloc, red_max[(bf * 2 + (hf ^ 1)) * QT + r]));
             const float corr = (m == -INFINITY) ? 0.0f : expf(m - mx);
             float sum = 0.0f;
 #pragma unroll
-            for (int c = 0; c < KB; c++) {
+            for (int c = 0; c < 32; c++) {
                 s[c] = (s[c] == -INFINITY) ? 0.0f : expf(s[c] - mx);
                 sum += s[c];
             }
-            l = l * corr + sum;
+            l = l * corr + sum;  // this half's partial row sum, at the common running max
             m = mx;
             // PV_{j-1} done => P buffer bf (read by PV_{j-2}) is free and O_{j-1} is ready
             if (j >= 1) {
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
-                if (!ok) break;
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err,
+                                                             DEV_TIMEOUT_ATTN));
                 tc_fence_after();
             }
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
+            {
                 float hi[32], lo[32];
 #pragma unroll
-                for (int i = 0; i < 32; i++) split_tf32(s[32 * half + i], hi[i], lo[i]);
-                tmem_st32(lb + col_p_hi(bf) + 32 * half, hi);
-                tmem_st32(lb + col_p_lo(bf) + 32 * half, lo);
+                for (int i = 0; i < 32; i++) split_tf32(s[i], hi[i], lo[i]);
+                tmem_st32(lb + col_p_hi(bf) + 32 * hf, hi);
+                tmem_st32(lb + col_p_lo(bf) + 32 * hf, lo);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -236,13 +241,16 @@ __global__ void __launch_bounds__(192, 1)
                 fold(nblk - 1, c_prev);
             }
         }
-        // ---- context row (TF32 pair, or plain fp32 when ctx_lo is null)
+        red_sum[hf * QT + r] = l;
+        pair_sync();
+        const float ltot = l + red_sum[(hf ^ 1) * QT + r];
+        // ---- context row, this warp's 32 columns (TF32 pair, or plain fp32 when ctx_lo is null)
         if (q0 + r < S) {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD;
+            const float inv = ltot > 0.0f ? 1.0f / ltot : 0.0f;
+            const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD + 32 * hf;
             float* dh = ctx_hi + off;
 #pragma unroll
-            for (int d = 0; d < HD; d += 4) {
+            for (int d = 0; d < 32; d += 4) {
                 float x[4], lo[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) x[i] = o[d + i] * inv;
@@ -309,7 +317,7 @@ void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, c
     const CUtensorMap vh = map2d(vt_hi, W, (long long)seqs * S, vt_ld, HD);
     const CUtensorMap vl = map2d(vt_lo, W, (long long)seqs * S, vt_ld, HD);
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    attention_tc_kernel<<<grid, 192, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx_hi, ctx_lo, err);
+    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx_hi, ctx_lo, err);
     N3D_CUDA(cudaGetLastError());
 }
 
