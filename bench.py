@@ -101,6 +101,7 @@ def oracle_rtfx(ckpt: str, clip: np.ndarray, reps: int = 1):
     """Time the CPU oracle (all host threads) on `clip`; returns (RTFx, seconds per run)."""
     import oracle
 
+    oracle.lib().orc_set_threads(os.cpu_count())  # torchrun exports OMP_NUM_THREADS=1
     om = oracle.OracleModel.load(ckpt)
     t0 = time.perf_counter()
     for _ in range(reps):
@@ -147,6 +148,7 @@ def run_reference(args, world, rank):
     ckpt = checkpoint(0, 1)
     import oracle
 
+    oracle.lib().orc_set_threads(os.cpu_count())  # all host threads (torchrun exports OMP_NUM_THREADS=1)
     om = oracle.OracleModel.load(ckpt)
     clip = make_clips(0, 1, CLIP_S)[0]
     for _ in range(args.warmup):  # CPU code has nothing to JIT: warm the thread pool on a 2 s clip
@@ -176,7 +178,10 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--clips", type=int, default=64, help="60 s clips per GPU per step")
+    p.add_argument("--workload", default="c4", choices=["c4", "c3"],
+                   help="c4: offline 60 s clips (headline); c3: ultra_low_latency streaming sessions")
+    p.add_argument("--clips", type=int, default=None, help="clips (c4) or sessions (c3) per GPU per step")
+    p.add_argument("--session-seconds", type=float, default=600.0, help="c3 session length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     args = p.parse_args()
     world, rank, local = dist_setup()
@@ -194,19 +199,31 @@ def main():
 
     torch.cuda.set_device(local)
     ckpt = checkpoint(rank, world)
-    clips = make_clips(rank, args.clips, CLIP_S)
-    lens = [c.size for c in clips]
+    if args.workload == "c4":
+        mode, item_s, n_items = "offline", CLIP_S, args.clips or 64
+        items = make_clips(rank, n_items, item_s)
+        metric, desc = METRIC, (f"C4 offline: {n_items} x 60 s 16 kHz clips per GPU per step, random-init weights "
+                                "(seed 0), clips seeded 1000+")
+    else:
+        import synth
+
+        mode, item_s, n_items = "ultra_low_latency", args.session_seconds, args.clips or 32
+        items = [synth.config3_session(rank * n_items + i, item_s) for i in range(n_items)]
+        metric = "ultra_low_latency streaming RTFx (audio-s/wall-s); p50/p99 chunk-step latency"
+        desc = (f"C3 ultra_low_latency: {n_items} concurrent {item_s:.0f} s sessions per GPU (seeds 100+), "
+                "3 scored encoder frames per step, random-init weights (seed 0)")
+    lens = [c.size for c in items]
     model = n3d.Model.load_gpu(ckpt, local)
     stream = torch.cuda.current_stream()
     model.set_stream(stream.cuda_stream)
-    frames = model.batch_out_frames(lens, "offline")
+    frames = model.batch_out_frames(lens, mode)
     offs = [int(x) for x in np.cumsum([0] + lens[:-1])]
     ooffs = [int(x) for x in np.cumsum([0] + frames[:-1])]
-    d_audio = torch.from_numpy(np.concatenate(clips)).cuda()
+    d_audio = torch.from_numpy(np.concatenate(items)).cuda()
     d_out = torch.empty(sum(frames) * 8, dtype=torch.float32, device="cuda")
 
     def step():
-        model.run_batch_device("offline", d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
+        model.run_batch_device(mode, d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
 
     def barrier():
         if world > 1:
@@ -223,10 +240,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident timed region
+    # ---- device-resident timed region: two CUDA events per chunk-loop step only
     for _ in range(args.warmup):
         step()
-    model.profile_enable(True)
+    model.step_timing_enable(True)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -238,21 +255,29 @@ def main():
         torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1))
+    step_ms = np.array(model.step_times())
+    model.step_timing_enable(False)
+    # ---- the same K steps again with CUDA events around every launch: per-kernel
+    # device time for the roofline and the kernel shares
+    model.profile_enable(True)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
     prof = model.profile_read()
     model.profile_enable(False)
-    audio_s = world * args.clips * CLIP_S * args.steps
+    audio_s = world * n_items * item_s * args.steps
     value = audio_s / (ms / 1e3)
 
     # ---- end-to-end through the public C-ABI batch call, pinned host buffers
-    pinned = [torch.from_numpy(c).pin_memory() for c in clips]
+    pinned = [torch.from_numpy(c).pin_memory() for c in items]
     host = [t.numpy() for t in pinned]
-    model.run_batch(host, "offline")  # warm the host path
+    model.run_batch(host, mode)  # warm the host path
     barrier()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.steps):
-        outs = model.run_batch(host, "offline")
+        outs = model.run_batch(host, mode)
     f1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -275,21 +300,24 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rt, dt = oracle_rtfx(ckpt, clips[0])
+        rt, dt = oracle_rtfx(ckpt, make_clips(0, 1, CLIP_S)[0])
         cpu = {"value": rt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-               "sample": f"one 60 s clip (3 windows) through the CPU oracle, {dt:.1f} s"}
+               "sample": f"one 60 s clip offline (3 windows) through the CPU oracle, {dt:.1f} s"}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (3xTF32 on tcgen05)", "data": "synthetic",
-            "config": {"workload": f"C4 offline: {args.clips} x 60 s 16 kHz clips per GPU per step, "
-                                   "random-init weights (seed 0), clips seeded 1000+",
-                       "clip_seconds": CLIP_S, "clips_per_step_per_gpu": args.clips, "parallelism": f"dp{world}",
+            "config": {"workload": desc, "seconds_per_item": item_s, "items_per_step_per_gpu": n_items,
+                       "mode": mode, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},
-            "e2e": {"value": world * args.clips * CLIP_S * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+            "e2e": {"value": world * n_items * item_s * args.steps / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+            "chunk_step_latency_ms": {
+                "p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
+                "max": float(step_ms.max()), "count": int(step_ms.size),
+                "what": f"device time of one chunk-loop step for all {n_items} items of a GPU (rank 0)"},
             "gpu_launches": launches,
             "roofline": {"bound": "tensor", "kernel": "gemm_tf32x3", "achieved": achieved, "peak": peak,
                          "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
@@ -298,7 +326,9 @@ def main():
                                  "the bf16 rate (nominal 1125 of 2250 TFLOP/s), so this kernel's nominal ceiling "
                                  "is 375 TFLOP/s algorithmic",
                          "frac_of_3xtf32_ceiling": achieved / 375.0,
-                         "avg_launch_ms": g["ms"] / max(g["launches"], 1)},
+                         "avg_launch_ms": g["ms"] / max(g["launches"], 1),
+                         "measured": "CUDA events around each launch on the model's stream, over a second "
+                                     "run of the same K steps (events would perturb the headline region)"},
             "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in classes.items()},
             "gemm_sites": {k: {"share": round(v["ms"] / total_prof_ms, 4),
                                "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}

@@ -208,6 +208,13 @@ typedef struct n3d_kernel_stats {
 n3d_status n3d_profile_enable(n3d_model *model, int on);
 size_t n3d_profile_read(const n3d_model *model, n3d_kernel_stats *out, size_t cap);
 
+/* Device time of each chunk-loop step (one step of every clip in the batch:
+ * window assembly, tower, head, cache update), from two CUDA events per step.
+ * Replaces STEP_PROFILE (src/model.rs:314, 417-473).  Enabling clears the list;
+ * n3d_step_times copies up to `cap` values (ms) and returns how many exist. */
+n3d_status n3d_step_timing_enable(n3d_model *model, int on);
+size_t n3d_step_times(const n3d_model *model, double *ms, size_t cap);
+
 /* ------------------------------------------------------------------ misc */
 
 const char *n3d_last_error(void);

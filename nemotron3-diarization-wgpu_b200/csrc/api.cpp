@@ -326,6 +326,20 @@ size_t n3d_profile_read(const n3d_model* model, n3d_kernel_stats* out, size_t ca
     return n;
 }
 
+n3d_status n3d_step_timing_enable(n3d_model* model, int on) {
+    return guarded([&] {
+        arg_check(model != nullptr, "n3d_step_timing_enable: null model");
+        model->m->step_timing_enable(on != 0);
+    });
+}
+
+size_t n3d_step_times(const n3d_model* model, double* ms, size_t cap) {
+    if (!model) return 0;
+    const std::vector<float>& t = model->m->step_times();
+    for (size_t i = 0; i < t.size() && i < cap; i++) ms[i] = t[i];
+    return t.size();
+}
+
 n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
                       const float* d_bias, float* d_y) {
     return guarded([&] {

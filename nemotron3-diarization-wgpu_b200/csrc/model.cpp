@@ -566,6 +566,27 @@ void Model::profile_enable(bool on) {
     for (auto& t : totals_) t = ProfTotals{};
 }
 
+void Model::step_timing_enable(bool on) {
+    N3D_CUDA(cudaSetDevice(device_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    prof_collect();
+    step_timing_ = on;
+    step_ms_.clear();
+}
+
+cudaEvent_t Model::pool_event() {
+    if (event_pool_.empty()) {
+        for (int i = 0; i < 64; i++) {
+            cudaEvent_t e;
+            N3D_CUDA(cudaEventCreate(&e));
+            event_pool_.push_back(e);
+        }
+    }
+    cudaEvent_t e = event_pool_.back();
+    event_pool_.pop_back();
+    return e;
+}
+
 void Model::prof_begin() {
     if (!prof_) return;
     if (event_pool_.size() < 2) {
@@ -595,6 +616,14 @@ void Model::prof_end(int cls, double flops, double bytes) {
 
 // Resolve recorded event pairs (the stream must be idle).
 void Model::prof_collect() {
+    for (const auto& pr : step_ev_) {
+        float ms = 0.0f;
+        N3D_CUDA(cudaEventElapsedTime(&ms, pr.first, pr.second));
+        step_ms_.push_back(ms);
+        event_pool_.push_back(pr.first);
+        event_pool_.push_back(pr.second);
+    }
+    step_ev_.clear();
     for (const ProfRec& r : pending_) {
         float ms = 0.0f;
         N3D_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
@@ -922,6 +951,11 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 const int S = step_S[w];
                 const SeqStep* d_st = d_table + step_first[w];
                 float* win = (float*)ws("win", (size_t)B * S * h * 4);
+                cudaEvent_t step_begin = nullptr;
+                if (step_timing_) {
+                    step_begin = pool_event();
+                    N3D_CUDA(cudaEventRecord(step_begin, stream_));
+                }
                 prof_begin();
                 launch_assemble(stream_, d_st, B, embeds, win, S, h);
                 prof_end(K_ASSEMBLE, 0, 2.0 * B * S * h * 4);
@@ -931,6 +965,11 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 launch_cache_update(stream_, d_st, B, (float*)ws("win", 0), (float*)ws("logits", 0), S, cc,
                                     silence_);
                 prof_end(K_CACHE, 0, 0);
+                if (step_timing_) {
+                    cudaEvent_t step_end = pool_event();
+                    N3D_CUDA(cudaEventRecord(step_end, stream_));
+                    step_ev_.emplace_back(step_begin, step_end);
+                }
             }
         }
         // ---- results

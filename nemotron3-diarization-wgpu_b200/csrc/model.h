@@ -126,6 +126,10 @@ class Model {
     // Profiling of the launches of run_batch (off by default).
     void profile_enable(bool on);
     const ProfTotals* profile_totals() const { return totals_; }
+    // Device time of every chunk-loop step (all sequences of the batch), two
+    // events per step; enabling clears the list.
+    void step_timing_enable(bool on);
+    const std::vector<float>& step_times() const { return step_ms_; }
 
   private:
     void prof_begin();
@@ -153,6 +157,10 @@ class Model {
     int s_cap_ = 1024;  // MAX_SEQ, src/gpu_engine.rs:12
     std::vector<void*> owned_;
     bool prof_ = false;
+    bool step_timing_ = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> step_ev_;
+    std::vector<float> step_ms_;
+    cudaEvent_t pool_event();
     struct ProfRec {
         int cls;
         cudaEvent_t a, b;

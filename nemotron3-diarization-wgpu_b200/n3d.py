@@ -129,6 +129,8 @@ def lib() -> C.CDLL:
         "n3d_attention": ([C.c_int, vp, vp, vp, _sz, _sz, _sz, _sz, C.c_int, C.c_double, vp], C.c_int),
         "n3d_profile_enable": ([vp, C.c_int], C.c_int),
         "n3d_profile_read": ([vp, C.POINTER(_KernelStats), _sz], _sz),
+        "n3d_step_timing_enable": ([vp, C.c_int], C.c_int),
+        "n3d_step_times": ([vp, C.POINTER(C.c_double), _sz], _sz),
         "n3d_last_error": ([], C.c_char_p),
         "n3d_version": ([], C.c_char_p),
     }
@@ -241,6 +243,15 @@ class Model:
         n = lib().n3d_profile_read(self._h, buf, 16)
         return {buf[i].name.decode(): dict(launches=int(buf[i].launches), ms=buf[i].ms, flops=buf[i].flops,
                                            bytes=buf[i].bytes) for i in range(n)}
+
+    def step_timing_enable(self, on: bool = True) -> None:
+        _check(lib().n3d_step_timing_enable(self._h, int(on)))
+
+    def step_times(self) -> list[float]:
+        n = lib().n3d_step_times(self._h, None, 0)
+        buf = (C.c_double * max(n, 1))()
+        lib().n3d_step_times(self._h, buf, n)
+        return [buf[i] for i in range(n)]
 
     # ---- stages (GpuEngine, src/gpu_engine.rs)
     def log_mel(self, samples, centered: bool = True) -> np.ndarray:
