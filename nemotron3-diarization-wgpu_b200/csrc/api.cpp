@@ -415,18 +415,19 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
         int* dv = (int*)sc.get(1);
         N3D_CUDA(cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, k.stream));
         if (head_dim == 64) {
-            // tcgen05 path (the model's): operands as TF32 pairs, V transposed
-            const size_t W = heads * 64, vt_ld = (seq + 3) / 4 * 4;
-            float* qh = sc.get(seq * W);
-            float* ql = sc.get(seq * W);
-            float* kh = sc.get(seq * W);
-            float* kl = sc.get(seq * W);
-            float* vh = sc.get(W * vt_ld);
-            float* vl = sc.get(W * vt_ld);
-            n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, cs, sn, qh, ql, kh, kl, vh, vl,
-                                  (long long)vt_ld);
-            n3d::launch_attention_tc(k.stream, qh, ql, kh, kl, (long long)seq, vh, vl, (long long)vt_ld, 1, (int)seq,
-                                     dv, (int)heads, d_out, nullptr, k.err);
+            // tcgen05 path (the model's): operands as bfloat16 pairs, V transposed
+            const size_t W = heads * 64, vt_ld = (seq + 7) / 8 * 8;
+            n3d::AttnOperands op;
+            op.q_hi = sc.get(seq * W / 2);
+            op.q_lo = sc.get(seq * W / 2);
+            op.k_hi = sc.get(seq * W / 2);
+            op.k_lo = sc.get(seq * W / 2);
+            op.rows_cap = (long long)seq;
+            op.vt_hi = sc.get(W * vt_ld / 2);
+            op.vt_lo = sc.get(W * vt_ld / 2);
+            op.vt_ld = (long long)vt_ld;
+            n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, cs, sn, op);
+            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, d_out, nullptr, k.err);
         } else {
             n3d::launch_pack_qkv(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, qkv);
             n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out, nullptr);

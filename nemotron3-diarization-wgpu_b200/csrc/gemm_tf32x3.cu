@@ -95,45 +95,6 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m
             store_row32(dst, v, N - col0);
             store_row32(dst + 32, v + 32, N - col0 - 32);
         }
-    } else if (epi.mode == EPI_QKV_ATTN) {
-        // Q | K | V sections of epi.q_cols columns each, one head = 64 columns
-        for (int c = 0; c < BN; c += 64) {
-            float v[64];
-            tmem_ld32(tl + c, v);
-            tmem_ld32(tl + c + 32, v + 32);
-            const int col0 = n0 + c;
-            if (!keep || col0 >= N) continue;
-            const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
-            const int pos = r % epi.rope_seq;
-            if (sec < 2) {
-                const float* cs = epi.cos_t + (long long)pos * epi.head_dim;
-                const float* sn = epi.sin_t + (long long)pos * epi.head_dim;
-#pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const float x1 = v[i], x2 = v[32 + i];
-                    v[i] = __fsub_rn(__fmul_rn(x1, cs[i]), __fmul_rn(x2, sn[i]));
-                    v[32 + i] = __fadd_rn(__fmul_rn(x2, cs[32 + i]), __fmul_rn(x1, sn[32 + i]));
-                }
-            }
-            float lo[64];
-#pragma unroll
-            for (int i = 0; i < 64; i++) split_tf32(v[i], v[i], lo[i]);
-            if (sec < 2) {
-                float* dh = (sec == 0 ? epi.out : epi.k_hi) + orow * epi.ldo + hcol;
-                float* dl = (sec == 0 ? epi.out_lo : epi.k_lo) + orow * epi.ldo + hcol;
-                store_row32(dh, v, 32);
-                store_row32(dh + 32, v + 32, 32);
-                store_row32(dl, lo, 32);
-                store_row32(dl + 32, lo + 32, 32);
-            } else {
-                const long long vrow = ((long long)(r / epi.rope_seq) * epi.heads + hcol / 64) * 64;
-#pragma unroll 8
-                for (int d = 0; d < 64; d++) {
-                    epi.vt_hi[(vrow + d) * epi.vt_ld + pos] = v[d];
-                    epi.vt_lo[(vrow + d) * epi.vt_ld + pos] = lo[d];
-                }
-            }
-        }
     } else if (epi.mode == EPI_DENSE_OUT) {
         // relu(dense) then the out projection, sequential over the hidden
         // index with separate multiply and add (src/tensor.rs:33-43)
@@ -305,12 +266,6 @@ __device__ __forceinline__ void stage_rows(uint8_t* box, int lane, const float* 
         *reinterpret_cast<float4*>(box + lane * 128 + ((i ^ (lane & 7)) << 4)) =
             make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
-// Transposed: box row = element index d, column = lane.
-__device__ __forceinline__ void stage_cols(uint8_t* box, int lane, const float* v) {
-#pragma unroll
-    for (int d = 0; d < 32; d++)
-        *reinterpret_cast<float*>(box + d * 128 + ((((lane >> 2) ^ (d & 7)) << 4) | ((lane & 3) << 2))) = v[d];
-}
 
 // Hand the staged boxes to TMA: wait until the previous boxes have been read,
 // which the caller does before staging; here fence and issue.
@@ -367,22 +322,30 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                     }
                 }
             }
+            // bf16 pairs: Q / K rows (64 values = one 128-byte swizzled box row), V
+            // transposed (box row = d, 32 rows of the tile = 64 bytes, unswizzled)
+            uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                float hi[32], lo[32];
+            for (int i = 0; i < 32; i++) split_bf16x2(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
+            stage_begin(lane);
+            if (sec < 2) {
 #pragma unroll
-                for (int i = 0; i < 32; i++) split_tf32(v[32 * half + i], hi[i], lo[i]);
-                stage_begin(lane);
-                if (sec < 2) {
-                    stage_rows(bhi, lane, hi);
-                    stage_rows(blo, lane, lo);
-                    stage_issue(lane, sec == 0 ? &epi.map_out : &epi.map_k_hi, bhi,
-                                sec == 0 ? &epi.map_out_lo : &epi.map_k_lo, blo, hcol + 32 * half, rowbase);
-                } else {
-                    stage_cols(bhi, lane, hi);
-                    stage_cols(blo, lane, lo);
-                    stage_issue(lane, &epi.map_vt_hi, bhi, &epi.map_vt_lo, blo, rowbase, hcol + 32 * half);
+                for (int i = 0; i < 8; i++) {
+                    const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
+                    *reinterpret_cast<uint4*>(bhi + o) = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
+                    *reinterpret_cast<uint4*>(blo + o) = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
                 }
+                stage_issue(lane, sec == 0 ? &epi.map_out : &epi.map_k_hi, bhi,
+                            sec == 0 ? &epi.map_out_lo : &epi.map_k_lo, blo, hcol, rowbase);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    *reinterpret_cast<uint16_t*>(bhi + (2 * i) * 64 + lane * 2) = (uint16_t)(hi[i] & 0xffffu);
+                    *reinterpret_cast<uint16_t*>(bhi + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(hi[i] >> 16);
+                    *reinterpret_cast<uint16_t*>(blo + (2 * i) * 64 + lane * 2) = (uint16_t)(lo[i] & 0xffffu);
+                    *reinterpret_cast<uint16_t*>(blo + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(lo[i] >> 16);
+                }
+                stage_issue(lane, &epi.map_vt_hi, bhi, &epi.map_vt_lo, blo, rowbase, hcol);
             }
         }
     } else {
@@ -673,6 +636,32 @@ CUtensorMap make_store_map(const float* p, long long rows, long long cols, long 
     return make_map(p, rows, cols, ld, 32, 32);
 }
 
+CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
+                          bool swizzle) {
+    using Key = std::tuple<const void*, long long, long long, long long, int, int, bool>;
+    static std::map<Key, CUtensorMap> cache;
+    static std::mutex mu;
+    const Key key{p, rows, cols, ld, box_cols, box_rows, swizzle};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) || (ld * 2) % 16 || (swizzle && box_cols != 64))
+        throw Error(9, "bf16 operand is not 16-byte aligned");
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(p), dims, strides, box, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed (bf16, " + std::to_string(int(r)) + ")");
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    return m;
+}
+
 void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
                  int kb_per_tap, const Epi& epi, int* err) {
     if (M <= 0 || N <= 0) return;
@@ -692,6 +681,7 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     }
     if ((epi.mode == EPI_QKV_ROPE || epi.mode == EPI_QKV_ATTN) && (bn % 64))
         throw Error(9, "QKV epilogue needs 64-column chunks");
+    if (epi.mode == EPI_QKV_ATTN && !epi.tma) throw Error(9, "the attention-operand epilogue stores through TMA only");
     switch (bn) {
         case 64: launch_persistent<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 128: launch_persistent<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;

@@ -1,6 +1,7 @@
 // Memory-bound and small kernels of the diarization path: LayerNorm, softmax
 // attention, and the fused log-mel front-end.
 
+#include <cuda_bf16.h>
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -17,20 +18,17 @@ __device__ __forceinline__ float warp_sum(float v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
 
 // ---------------------------------------------------------------- LayerNorm
 // torch LayerNorm, eps 1e-5, two-pass population variance (src/tensor.rs:97-110).
 // One warp per row, VPL values per lane held in registers (128-bit loads).
 // Writes either a plain fp32 row (out_lo == nullptr) or a TF32 hi/lo pair.
+// x_out may alias x (in-place residual add): each lane reads its elements of x before
+// writing them, so neither is __restrict__.
 template <int VPL>
-__global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
+__global__ void layer_norm_kernel(const float* x, long long rows, const float* __restrict__ w,
                                   const float* __restrict__ b, float* __restrict__ out, float* __restrict__ out_lo,
-                                  const float* __restrict__ delta = nullptr, float* __restrict__ x_out = nullptr) {
+                                  const float* __restrict__ delta = nullptr, float* x_out = nullptr) {
     constexpr int COLS = VPL * 32;
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -284,12 +282,17 @@ __global__ void pack_qkv_kernel(const float* __restrict__ q, const float* __rest
     }
 }
 
-// Kernel-level attention operands: RoPE'd Q and K as TF32 pairs, V transposed as a pair.
+// Kernel-level attention operands: RoPE'd Q and K as bfloat16 pairs, V transposed as a pair.
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+}
 __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                  const float* __restrict__ v, long long seq, int heads,
                                  const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                 float* __restrict__ q_hi, float* __restrict__ q_lo, float* __restrict__ k_hi,
-                                 float* __restrict__ k_lo, float* __restrict__ vt_hi, float* __restrict__ vt_lo,
+                                 __nv_bfloat16* __restrict__ q_hi, __nv_bfloat16* __restrict__ q_lo,
+                                 __nv_bfloat16* __restrict__ k_hi, __nv_bfloat16* __restrict__ k_lo,
+                                 __nv_bfloat16* __restrict__ vt_hi, __nv_bfloat16* __restrict__ vt_lo,
                                  long long vt_ld) {
     const int hd = 64, half = 32;
     const long long W = (long long)heads * hd;
@@ -310,22 +313,23 @@ __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __res
                 ko = __fadd_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
             }
         }
-        split_tf32(qo, q_hi[e], q_lo[e]);
-        split_tf32(ko, k_hi[e], k_lo[e]);
-        split_tf32(v[e], vt_hi[(long long)c * vt_ld + r], vt_lo[(long long)c * vt_ld + r]);
+        split_bf16(qo, q_hi[e], q_lo[e]);
+        split_bf16(ko, k_hi[e], k_lo[e]);
+        split_bf16(v[e], vt_hi[(long long)c * vt_ld + r], vt_lo[(long long)c * vt_ld + r]);
     }
 }
 
 }  // namespace
 
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                      const float* cos_t, const float* sin_t, float* q_hi, float* q_lo, float* k_hi, float* k_lo,
-                      float* vt_hi, float* vt_lo, long long vt_ld) {
+                      const float* cos_t, const float* sin_t, const AttnOperands& op) {
+    using bf = __nv_bfloat16;
     const long long n = seq * heads * 64;
     if (n <= 0) return;
     const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
-    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, cos_t, sin_t, q_hi, q_lo, k_hi, k_lo,
-                                                      vt_hi, vt_lo, vt_ld);
+    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, cos_t, sin_t, (bf*)op.q_hi, (bf*)op.q_lo,
+                                                      (bf*)op.k_hi, (bf*)op.k_lo, (bf*)op.vt_hi, (bf*)op.vt_lo,
+                                                      op.vt_ld);
     N3D_CUDA(cudaGetLastError());
 }
 

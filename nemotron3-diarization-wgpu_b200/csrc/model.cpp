@@ -638,7 +638,7 @@ void Model::prof_collect() {
     pending_.clear();
 }
 
-// The 31-layer tower on B sequences of stride S rows (S a multiple of 4) held in
+// The 31-layer tower on B sequences of stride S rows (S a multiple of 8) held in
 // ws "win".  Output: the final LayerNorm as a TF32 pair in "n_hi"/"n_lo" (and
 // plain in enc_plain when given).  Residual adds are fused into the LayerNorm
 // that follows them, so every GEMM epilogue is a pure (TMA) store.
@@ -650,14 +650,16 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     float* tmp = (float*)ws("tmp", M * h * 4);
     float* n_hi = (float*)ws("n_hi", M * h * 4);
     float* n_lo = (float*)ws("n_lo", M * h * 4);
-    float* q_hi = (float*)ws("q_hi", M * h * 4);
-    float* q_lo = (float*)ws("q_lo", M * h * 4);
-    float* k_hi = (float*)ws("k_hi", M * h * 4);
-    float* k_lo = (float*)ws("k_lo", M * h * 4);
-    const long long vt_ld = M;  // V^T [heads*64, M]: column = global row
-    float* vt_hi = (float*)ws("vt_hi", h * vt_ld * 4);
-    float* vt_lo = (float*)ws("vt_lo", h * vt_ld * 4);
-    const long long rows_qk = ws_["q_hi"].bytes / (h * 4);
+    // attention operands as bfloat16 pairs: Q, K [M, h]; V^T [h, M] (column = global row)
+    AttnOperands ao;
+    ao.q_hi = ws("q_hi", M * h * 2);
+    ao.q_lo = ws("q_lo", M * h * 2);
+    ao.k_hi = ws("k_hi", M * h * 2);
+    ao.k_lo = ws("k_lo", M * h * 2);
+    ao.vt_ld = M;
+    ao.vt_hi = ws("vt_hi", h * M * 2);
+    ao.vt_lo = ws("vt_lo", h * M * 2);
+    ao.rows_cap = (long long)(ws_["q_hi"].bytes / (h * 2));
     float* ctx_hi = (float*)ws("ctx_hi", M * h * 4);
     float* ctx_lo = (float*)ws("ctx_lo", M * h * 4);
     float* f_hi = (float*)ws("f_hi", M * c.inter * 4);
@@ -671,19 +673,18 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     Epi e;  // QKV: Q/K pairs with RoPE, V^T pair
     e.mode = EPI_QKV_ATTN;
     e.tma = 1;
-    e.map_out = make_store_map(q_hi, M, h, h);
-    e.map_out_lo = make_store_map(q_lo, M, h, h);
-    e.map_k_hi = make_store_map(k_hi, M, h, h);
-    e.map_k_lo = make_store_map(k_lo, M, h, h);
-    e.map_vt_hi = make_store_map(vt_hi, h, M, vt_ld);
-    e.map_vt_lo = make_store_map(vt_lo, h, M, vt_ld);
+    e.map_out = make_bf16_map(ao.q_hi, M, h, h, 64, 32, true);
+    e.map_out_lo = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
+    e.map_k_hi = make_bf16_map(ao.k_hi, M, h, h, 64, 32, true);
+    e.map_k_lo = make_bf16_map(ao.k_lo, M, h, h, 64, 32, true);
+    e.map_vt_hi = make_bf16_map(ao.vt_hi, h, M, ao.vt_ld, 32, 64, false);
+    e.map_vt_lo = make_bf16_map(ao.vt_lo, h, M, ao.vt_ld, 32, 64, false);
     e.cos_t = rope_cos_;
     e.sin_t = rope_sin_;
     e.rope_seq = S;
     e.head_dim = (int)(h / c.heads);
     e.q_cols = (int)h;
     e.k_cols = (int)h;
-    e.heads = c.heads;
     Epi eo;  // o_proj / fc2: acc + bias -> tmp (added into x by the next LayerNorm)
     eo.mode = EPI_STORE;
     eo.tma = 1;
@@ -710,8 +711,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);
         prof_begin();
-        launch_attention_tc(stream_, q_hi, q_lo, k_hi, k_lo, rows_qk, vt_hi, vt_lo, vt_ld, B, S, d_valid, c.heads,
-                            ctx_hi, ctx_lo, dev_err_);
+        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx_hi, ctx_lo, dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
         eo.bias = L.o.bias;
         prof_begin();
@@ -931,7 +931,7 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 valid.push_back(sp.valid);
                 Smax = std::max(Smax, sp.S);
             }
-            step_S[w] = (Smax + 3) / 4 * 4;  // row stride: a multiple of 4 keeps TMA coordinates 16-byte aligned
+            step_S[w] = (Smax + 7) / 8 * 8;  // row stride: a multiple of 8 keeps TMA coordinates 16-byte aligned
         }
         step_first[max_steps] = (int)table.size();
         // Clips whose plans skip a step (S == 0) must still carry state forward:
@@ -1061,7 +1061,7 @@ void Model::forward_window(const float* embeds, int frames, int valid, float* en
     if (frames <= 0 || frames > s_cap_)
         throw Error(kStatusGpu, "seq " + std::to_string(frames) + " outside 1..=1024");
     valid = std::min(valid, frames);
-    const int S = (frames + 3) / 4 * 4;  // row stride (multiple of 4), rows past `frames` are zero
+    const int S = (frames + 7) / 8 * 8;  // row stride (multiple of 8), rows past `frames` are zero
     const long long M = frames, h = c.hidden;
     float* win = (float*)ws("win", (long long)S * h * 4);
     N3D_CUDA(cudaMemsetAsync(win, 0, (long long)S * h * 4, stream_));
@@ -1087,7 +1087,7 @@ void Model::head_forward(const float* enc, int frames, float* logits) {
     N3D_CUDA(cudaSetDevice(device_));
     if (frames <= 0 || frames > s_cap_)
         throw Error(kStatusGpu, "head frames " + std::to_string(frames) + " outside 1..=1024");
-    const int S = (frames + 3) / 4 * 4;
+    const int S = (frames + 7) / 8 * 8;
     const long long M = frames, h = c.hidden;
     float* plain = (float*)ws("enc_plain", (long long)S * h * 4);
     float* n_hi = (float*)ws("n_hi", (long long)S * h * 4);

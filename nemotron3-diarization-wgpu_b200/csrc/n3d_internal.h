@@ -31,8 +31,8 @@ enum EpiMode : int {
     EPI_RELU_SPLIT = 4,  // split(relu(acc + bias))
     EPI_QKV_ROPE = 5,    // Q,K columns rotated by RoPE, V as is; fp32 out
     EPI_DENSE_OUT = 6,   // r = relu(acc + bias); out[r, 0:ns] = r . w2^T + b2
-    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> TF32 pairs (out/out_lo, k_hi/k_lo);
-                         // V -> transposed TF32 pair vt[(seq*heads + head)*64 + d][t]
+    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_out*, map_k_*);
+                         // V -> transposed bf16 pair V^T[head*64 + d][row] (map_vt_*); TMA only
 };
 
 struct Epi {
@@ -54,17 +54,12 @@ struct Epi {
     int head_dim = 64;
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
     // Stores through TMA (tma != 0): tensor maps over the destinations, box 32 columns
-    // x 32 rows, 128-byte swizzle.  map_out/map_out_lo: the output (pair); for
-    // EPI_QKV_ATTN also map_k_* (K pair) and map_vt_* over V^T [heads*64, rows].
+    // x 32 rows, 128-byte swizzle (make_store_map).  map_out/map_out_lo: the output
+    // (pair).  EPI_QKV_ATTN: bf16 maps (make_bf16_map) -- map_out*/map_k_* with box
+    // 64 x 32 and 128-byte swizzle, map_vt_* over V^T [heads*64, rows] with box
+    // 32 x 64 and no swizzle.
     int tma = 0;
     CUtensorMap map_out, map_out_lo, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
-    // EPI_QKV_ATTN destinations
-    float* k_hi = nullptr;
-    float* k_lo = nullptr;
-    float* vt_hi = nullptr;
-    float* vt_lo = nullptr;
-    long long vt_ld = 0;
-    int heads = 8;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
     const float* b2 = nullptr;
@@ -80,6 +75,10 @@ struct SplitOperand {
 
 // TMA-store map (box 32 x 32, 128-byte swizzle) over a row-major fp32 matrix.
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
+// 2-D map over a row-major bfloat16 matrix [rows, cols] with row stride ld elements;
+// box box_cols x box_rows, 128-byte swizzle when `swizzle` (box_cols must then be 64).
+CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
+                          bool swizzle);
 
 // C[M, N] = A[M, K] * B[N, K]^T in 3xTF32 on tcgen05. `kb_per_tap` > 0 turns on
 // the shifted-row (implicit k=3 conv) mode: k-block kb reads A at column
@@ -104,17 +103,22 @@ void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, con
                 const long long* f_out);
 // x -> (hi, lo) TF32 pair, elementwise.
 void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
-// tcgen05 attention, head_dim 64 (attention_tc.cu).  Q, K: TF32 pairs [rows_cap, heads*64]
-// with sequence b at rows b*S..; V^T: TF32 pair [heads*64, vt_ld] whose column is the
-// global row (S and the row stride must be multiples of 4).  ctx_lo == nullptr writes plain fp32.
-void launch_attention_tc(cudaStream_t s, const float* q_hi, const float* q_lo, const float* k_hi,
-                         const float* k_lo, long long rows_cap, const float* vt_hi, const float* vt_lo,
-                         long long vt_ld, int seqs, int S, const int* valid, int heads, float* ctx_hi,
-                         float* ctx_lo, int* err);
+// Operands of the tcgen05 attention (head_dim 64), all bfloat16 hi/lo pairs:
+// Q, K [rows_cap, heads*64] with sequence b at rows b*S..; V^T [heads*64, vt_ld]
+// whose column is the global row.
+struct AttnOperands {
+    const void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr;
+    long long rows_cap = 0;
+    const void *vt_hi = nullptr, *vt_lo = nullptr;
+    long long vt_ld = 0;
+};
+// tcgen05 attention (attention_tc.cu); S (when seqs > 1) and vt_ld must be multiples
+// of 8.  Context [seqs*S, heads*64] as a TF32 pair, or plain fp32 when ctx_lo == nullptr.
+void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
+                         float* ctx_hi, float* ctx_lo, int* err);
 // q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                      const float* cos_t, const float* sin_t, float* q_hi, float* q_lo, float* k_hi, float* k_lo,
-                      float* vt_hi, float* vt_lo, long long vt_ld);
+                      const float* cos_t, const float* sin_t, const AttnOperands& op);
 // tensor::linear without any allocation: scratch is a fixed device array (noalloc.cu).
 void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
                     const float* d_bias, float* d_y, cudaStream_t stream);
