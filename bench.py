@@ -333,6 +333,9 @@ def main():
             "gemm_sites": {k: {"share": round(v["ms"] / total_prof_ms, 4),
                                "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}
                            for k, v in gemm_sites.items()},
+            "class_rates": {k: ({"tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1)} if v["flops"] else
+                                {"gbs": round(v["bytes"] / (v["ms"] / 1e3) / 1e9, 1)} if v["bytes"] else {})
+                            for k, v in prof.items() if not k.startswith("gemm") and v["launches"] and v["ms"]},
             "dominant_kernel": top[0],
             "clocks": clk.summary(),
             "cpu_baseline": cpu,

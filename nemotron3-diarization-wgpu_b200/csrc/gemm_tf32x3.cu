@@ -533,6 +533,160 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
 }
 
+// CTA-pair variant: a cluster of two CTAs walks 256 x BN output tiles with
+// M = 256 UMMAs (cta_group::2).  CTA r of the pair loads A rows m0 + 128 r and
+// B rows n0 + r * BN / 2, so each SM streams half the B tile of the one-CTA
+// kernel for the same work; its TMEM receives output rows m0 + 128 r, which its
+// own epilogue warps store.  Barriers: full[s] lives in the leader (both CTAs'
+// loads complete on it), empty[s] and acc_full[b] in both (arrived by the
+// leader's multicast commits), acc_empty[b] in the leader (8 epilogue warps).
+template <int BN>
+struct PairCfg {
+    static constexpr int A_BYTES = BM * PBK * 4;
+    static constexpr int B_BYTES = (BN / 2) * PBK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGING = 4 * 8192;
+    static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
+    static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
+                     const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo, int M,
+                     int N, int K, int kb_per_tap, const __grid_constant__ Epi epi, int* err) {
+    using Cfg = PairCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = static_cast<int>(cluster_rank());
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
+    const int tiles_n = (N + BN - 1) / BN;
+    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * tiles_n;
+    const int nkb = K / PBK;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < Cfg::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);
+        }
+        mbar_fence_init();
+        tma_prefetch_desc(&tA_hi);
+        tma_prefetch_desc(&tA_lo);
+        tma_prefetch_desc(&tB_hi);
+        tma_prefetch_desc(&tB_lo);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = cid; ok && t < tiles; t += ncl) {
+                const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN + rank * (BN / 2);
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (g >= (uint32_t)Cfg::STAGES &&
+                        !mbar_wait_cluster(&empty[s], ((g / Cfg::STAGES) - 1) & 1, err, DEV_TIMEOUT_TMA_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * Cfg::STAGE_BYTES;
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    const uint32_t fb = leader_addr(&full[s]);
+                    const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
+                    const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * PBK : kb * PBK;
+                    tma_load_2d_pair(st, &tA_hi, fb, ka, m0 + tap);
+                    tma_load_2d_pair(st + Cfg::A_BYTES, &tA_lo, fb, ka, m0 + tap);
+                    tma_load_2d_pair(st + 2 * Cfg::A_BYTES, &tB_hi, fb, kb * PBK, n0);
+                    tma_load_2d_pair(st + 2 * Cfg::A_BYTES + Cfg::B_BYTES, &tB_lo, fb, kb * PBK, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32_pair(BN);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = cid; ok && t < tiles; t += ncl, it++) {
+                const int buf = it & 1;
+                if (it >= 2 && !mbar_wait_cluster(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * BN;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (!mbar_wait_cluster(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_hi = smem_u32(smem + s * Cfg::STAGE_BYTES);
+                    const uint32_t a_lo = a_hi + Cfg::A_BYTES;
+                    const uint32_t b_hi = a_hi + 2 * Cfg::A_BYTES;
+                    const uint32_t b_lo = b_hi + Cfg::B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < PBK / 8; k++) {
+                        const uint32_t off = k * 32;
+                        const uint64_t dah = desc_k_sw64(a_hi + off), dal = desc_k_sw64(a_lo + off);
+                        const uint64_t dbh = desc_k_sw64(b_hi + off), dbl = desc_k_sw64(b_lo + off);
+                        umma_tf32_pair(d, dal, dbh, idesc, (kb | k) != 0);
+                        umma_tf32_pair(d, dah, dbl, idesc, 1);
+                        umma_tf32_pair(d, dah, dbh, idesc, 1);
+                    }
+                    umma_commit_pair(&empty[s]);
+                }
+                if (ok) umma_commit_pair(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
+        int it = 0;
+        for (int t = cid; t < tiles; t += ncl, it++) {
+            const int buf = it & 1;
+            const bool ok =
+                __all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN;
+            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+            if (epi.tma)
+                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+            else
+                epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8u * buf);
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the peer's TMEM reads and remote arrives are done
+    if (warp == 1) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+}
+
 // ------------------------------------------------------------ tensor maps
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -630,6 +784,38 @@ void launch_persistent(cudaStream_t s, const SplitOperand& A, const SplitOperand
     N3D_CUDA(cudaGetLastError());
 }
 
+template <int BN>
+void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                 const Epi& epi, int* err) {
+    using Cfg = PairCfg<BN>;
+    static int max_clusters = 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    if (!max_clusters) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        cfg.gridDim = dim3(2 * (sm_count() / 2));
+        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN>, &cfg));
+        if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
+    }
+    const CUtensorMap a_hi = make_map(A.hi, A.rows, A.cols, A.ld, BM, PBK);
+    const CUtensorMap a_lo = make_map(A.lo, A.rows, A.cols, A.ld, BM, PBK);
+    const CUtensorMap b_hi = make_map(B.hi, B.rows, B.cols, B.ld, BN / 2, PBK);
+    const CUtensorMap b_lo = make_map(B.lo, B.rows, B.cols, B.ld, BN / 2, PBK);
+    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+    cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, a_hi, a_lo, b_hi, b_lo, M, N, K,
+                                kb_per_tap > 0 ? kb_per_tap * (BK / PBK) : 0, epi, err));
+}
+
 }  // namespace
 
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld) {
@@ -673,7 +859,7 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     } else if (N == 192) {
         bn = 192;
     } else if (N % 256 == 0 && M >= 4096) {
-        bn = 256;
+        bn = 512;  // 256 x 256 tiles on CTA pairs
     } else if (N % 128 == 0 || N > 64) {
         bn = 128;
     } else {
@@ -686,7 +872,7 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         case 64: launch_persistent<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 128: launch_persistent<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 192: launch_persistent<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
-        default: launch_persistent<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        default: launch_pair<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
     }
 }
 
