@@ -172,6 +172,11 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# Mean DRAM read + write bytes of one encoder GEMM launch (QKV, O, FC1, FC2 of one layer)
+# at 32 clips per step, from the ncu capture summarised in profiles/ (grows with rows).
+GEMM_DRAM_BYTES_32CLIPS = 144.6e6
+
+
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -320,7 +325,11 @@ def main():
                 "what": f"device time of one chunk-loop step for all {n_items} items of a GPU (rank 0)"},
             "gpu_launches": launches,
             "roofline": {"bound": "tensor", "kernel": "gemm_tf32x3", "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "unit": "TFLOP/s", "frac": achieved / peak,
+                         "traffic": (GEMM_DRAM_BYTES_32CLIPS * n_items / 32) if args.workload == "c4" else None,
+                         "traffic_unit": "DRAM bytes read+written per launch",
+                         "traffic_source": "profiles/gemm_pair_c4_offline_32clips.md: mean of the 4 encoder GEMM "
+                                           "launches of one layer at 32 clips, scaled by rows to this run",
                          "peak_source": f"{src} bf16 dense sustained (MEASURED_PEAKS.json)",
                          "note": "3xTF32: each algorithmic FLOP issues 3 TF32 tensor FLOPs; dense TF32 is half "
                                  "the bf16 rate (nominal 1125 of 2250 TFLOP/s), so this kernel's nominal ceiling "

@@ -119,6 +119,38 @@ n3d_status n3d_batch_out_frames(const n3d_model *model, n3d_mode mode, const siz
 n3d_status n3d_run_batch_device(n3d_model *model, n3d_mode mode, const float *d_audio, const size_t *offsets,
                                 const size_t *lens, size_t n_clips, float *d_logits, const size_t *out_offsets);
 
+/* ---------------------------------------------------------- streaming sessions */
+
+/* Incremental streaming: one recording that arrives in pieces (a live call, a
+ * microphone).  No reference counterpart: Model::run_streaming (src/model.rs:313-336)
+ * takes the whole recording; a session produces the same logits as that call on the
+ * concatenated audio, but emits each chunk's rows as soon as the chunk's samples are
+ * complete.  The chunk schedule is the reference's (Model::streaming_chunks,
+ * src/model.rs:343-365): chunk 0 runs once its (c+r)*8 mel frames of audio have
+ * arrived, each later full chunk once all of its samples have, and the final, centred
+ * chunk at n3d_session_close.  The speaker cache and FIFO stay in device memory between
+ * calls (about 4 MiB per session).
+ *
+ * Each call fills `out` with the NEW logits rows only (out->num_frames of them, freed
+ * with n3d_run_output_free, also when there are none) and the running totals:
+ * num_chunks so far, cache_compressed, cache_frames, fifo_frames.  After close these
+ * totals equal run_streaming's RunOutput fields.  A session belongs to one model and
+ * must be freed before it; calls on one model (sessions included) are serialised by
+ * the caller.  After a call fails the session can only be freed. */
+typedef struct n3d_session n3d_session;
+n3d_status n3d_session_open(n3d_model *model, n3d_mode mode, n3d_session **out);
+n3d_status n3d_session_push(n3d_session *session, const float *samples, size_t n, n3d_run_output *out);
+n3d_status n3d_session_close(n3d_session *session, n3d_run_output *out);
+void n3d_session_free(n3d_session *session);
+
+/* Many sessions of one model at once (a server's concurrent streams): appends
+ * samples[i] (lens[i] of them) to sessions[i], then runs every ready chunk of every
+ * session, the steps of different sessions batched into the same kernels; with
+ * `close` != 0 it also runs each session's final chunk.  outs[i] as for
+ * n3d_session_push.  Results equal pushing to each session alone. */
+n3d_status n3d_sessions_push(n3d_session *const *sessions, const float *const *samples, const size_t *lens,
+                             size_t count, int close, n3d_run_output *outs);
+
 /* ------------------------------------------------------------------ stages */
 
 /* mel::log_mel (src/mel.rs:160-225) on the device.  `out` holds

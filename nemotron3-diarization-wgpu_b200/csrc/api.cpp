@@ -8,6 +8,7 @@
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -16,6 +17,11 @@
 
 struct n3d_model {
     std::unique_ptr<n3d::Model> m;
+};
+
+struct n3d_session {
+    n3d_model* owner;
+    n3d::Session* s;
 };
 
 namespace {
@@ -173,6 +179,75 @@ void n3d_run_output_free(n3d_run_output* out) {
     if (!out) return;
     std::free(out->logits);
     out->logits = nullptr;
+}
+
+n3d_status n3d_session_open(n3d_model* model, n3d_mode mode, n3d_session** out) {
+    return guarded([&] {
+        arg_check(model && out, "n3d_session_open: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 2, "n3d_session_open: mode must be a streaming mode");
+        *out = nullptr;
+        n3d::Session* s = model->m->session_open((int)mode);
+        auto* h = new (std::nothrow) n3d_session{model, s};
+        if (!h) {
+            model->m->session_free(s);
+            throw std::bad_alloc();
+        }
+        *out = h;
+    });
+}
+
+void n3d_session_free(n3d_session* session) {
+    if (!session) return;
+    session->owner->m->session_free(session->s);
+    delete session;
+}
+
+n3d_status n3d_sessions_push(n3d_session* const* sessions, const float* const* samples, const size_t* lens,
+                             size_t count, int close, n3d_run_output* outs) {
+    return guarded([&] {
+        if (count == 0) return;
+        arg_check(sessions && lens && outs, "n3d_sessions_push: null argument");
+        for (size_t i = 0; i < count; i++) outs[i] = n3d_run_output{};
+        std::vector<n3d::Session*> ss(count);
+        std::vector<const float*> a(count);
+        std::vector<long long> l(count);
+        n3d_model* owner = nullptr;
+        for (size_t i = 0; i < count; i++) {
+            arg_check(sessions[i] != nullptr, "n3d_sessions_push: null session");
+            arg_check(lens[i] == 0 || (samples && samples[i]), "n3d_sessions_push: null samples");
+            if (!owner) owner = sessions[i]->owner;
+            arg_check(sessions[i]->owner == owner, "n3d_sessions_push: sessions of different models");
+            ss[i] = sessions[i]->s;
+            a[i] = lens[i] ? samples[i] : nullptr;
+            l[i] = (long long)lens[i];
+        }
+        std::vector<std::vector<float>> rows;
+        owner->m->sessions_push(ss, a, l, close != 0, rows);
+        const size_t ns = (size_t)owner->m->cfg().num_speakers;
+        try {
+            for (size_t i = 0; i < count; i++) {
+                n3d::ClipPlan totals;
+                totals.num_chunks = ss[i]->num_chunks;
+                totals.cache_compressed = ss[i]->compressed;
+                totals.cache_frames = ss[i]->ncache;
+                totals.fifo_frames = ss[i]->nfifo;
+                fill_output(&outs[i], rows[i], totals, ns);
+            }
+        } catch (...) {
+            for (size_t i = 0; i < count; i++) n3d_run_output_free(&outs[i]);
+            throw;
+        }
+    });
+}
+
+n3d_status n3d_session_push(n3d_session* session, const float* samples, size_t n, n3d_run_output* out) {
+    return n3d_sessions_push(&session, &samples, &n, 1, 0, out);
+}
+
+n3d_status n3d_session_close(n3d_session* session, n3d_run_output* out) {
+    const float* none = nullptr;
+    size_t zero = 0;
+    return n3d_sessions_push(&session, &none, &zero, 1, 1, out);
 }
 
 n3d_status n3d_run_batch(n3d_model* model, n3d_mode mode, const float* const* samples, const size_t* lens,

@@ -8,6 +8,7 @@
 
 #include "model.h"
 
+#include <memory>
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -31,7 +32,7 @@ namespace {
 
 constexpr int kStatusIo = 1, kStatusJson = 2, kStatusSafetensors = 3, kStatusDtype = 4, kStatusMissing = 5,
               kStatusShape = 6, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11, kStatusNoDevice = 12,
-              kStatusArg = 13;
+              kStatusArg = 13, kStatusCuda = 10;
 
 std::string read_file(const std::string& path) {
     std::ifstream f(path, std::ios::binary);
@@ -829,58 +830,19 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
         } else {
             for (int i = 0; i < nb; i++) aoff[i] = offsets_in[c0 + i];
         }
-        // ---- mel segments and frames
+        // ---- mel segments, log-mel and the embedder over every segment of every clip
         long long total_groups = 0, total_frames = 0;
+        std::vector<MelSeg> flat;
+        std::vector<long long> flat_base;
         for (int i = 0; i < nb; i++)
             for (MelSeg& s : plans[c0 + i].segs) {
                 s.group_base = total_groups;
                 total_groups += s.groups;
                 total_frames += s.frames;
+                flat.push_back(s);
+                flat_base.push_back(aoff[i] + s.audio_off);
             }
-        std::vector<long long> f_base(total_frames), f_out(total_frames);
-        std::vector<int> f_meta(2 * total_frames);
-        {
-            long long f = 0;
-            for (int i = 0; i < nb; i++)
-                for (const MelSeg& s : plans[c0 + i].segs)
-                    for (int t = 0; t < s.frames; t++, f++) {
-                        f_base[f] = aoff[i] + s.audio_off;
-                        f_meta[2 * f] = t * c.hop - (s.centered ? c.n_fft / 2 : 0);
-                        f_meta[2 * f + 1] = (int)s.len;
-                        f_out[f] = s.group_base * sub + t;
-                    }
-        }
-        const long long mel_rows = std::max(total_groups * sub, 1LL);
-        float* mel_hi = (float*)ws("mel_hi", mel_rows * c.n_mels * 4);
-        float* mel_lo = (float*)ws("mel_lo", mel_rows * c.n_mels * 4);
-        N3D_CUDA(cudaMemsetAsync(mel_hi, 0, mel_rows * c.n_mels * 4, stream_));
-        N3D_CUDA(cudaMemsetAsync(mel_lo, 0, mel_rows * c.n_mels * 4, stream_));
-        if (total_frames > 0) {
-            long long* d_fb = (long long*)ws("f_base", total_frames * 8);
-            long long* d_fo = (long long*)ws("f_out", total_frames * 8);
-            int* d_fm = (int*)ws("f_meta", total_frames * 8);
-            N3D_CUDA(cudaMemcpyAsync(d_fb, f_base.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
-            N3D_CUDA(cudaMemcpyAsync(d_fo, f_out.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
-            N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
-            prof_begin();
-            launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_,
-                       filt_hi_, c.preemph, mel_hi, mel_lo, nullptr, d_fo);
-            prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
-        }
-        // ---- embedder: one GEMM over every group of every segment
-        const long long K_emb = (long long)sub * c.n_mels;
-        float* embeds = (float*)ws("embeds", std::max(total_groups, 1LL) * h * 4);
-        if (total_groups > 0) {
-            Epi e;
-            e.mode = EPI_STORE;
-            e.out = embeds;
-            e.ldo = h;
-            const long long rows_cap = ws_["mel_hi"].bytes / (K_emb * 4);
-            prof_begin();
-            gemm_tf32x3(stream_, SplitOperand{mel_hi, mel_lo, rows_cap, K_emb, K_emb}, embed_.op(),
-                        (int)total_groups, h, (int)K_emb, 0, e, dev_err_);
-            prof_end(K_GEMM_EMBED, 2.0 * total_groups * h * K_emb, 0);
-        }
+        const float* embeds = mel_embed(d_audio, flat_base, flat, total_groups, total_frames);
         // ---- per-clip state and outputs
         int max_steps = 0;
         long long out_total = 0;
@@ -944,32 +906,11 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                                      stream_));
             N3D_CUDA(cudaMemcpyAsync(d_len, seq_len.data(), seq_len.size() * 4, cudaMemcpyHostToDevice, stream_));
             N3D_CUDA(cudaMemcpyAsync(d_valid, valid.data(), valid.size() * 4, cudaMemcpyHostToDevice, stream_));
-            CacheConst cc{h, ns, sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr, c.latest_boost};
             for (int w = 0; w < max_steps; w++) {
                 const int B = step_first[w + 1] - step_first[w];
                 if (B == 0) continue;
-                const int S = step_S[w];
-                const SeqStep* d_st = d_table + step_first[w];
-                float* win = (float*)ws("win", (size_t)B * S * h * 4);
-                cudaEvent_t step_begin = nullptr;
-                if (step_timing_) {
-                    step_begin = pool_event();
-                    N3D_CUDA(cudaEventRecord(step_begin, stream_));
-                }
-                prof_begin();
-                launch_assemble(stream_, d_st, B, embeds, win, S, h);
-                prof_end(K_ASSEMBLE, 0, 2.0 * B * S * h * 4);
-                tower(B, S, d_len + step_first[w], d_valid + step_first[w], nullptr);
-                head(B, S, d_len + step_first[w]);
-                prof_begin();
-                launch_cache_update(stream_, d_st, B, (float*)ws("win", 0), (float*)ws("logits", 0), S, cc,
-                                    silence_);
-                prof_end(K_CACHE, 0, 0);
-                if (step_timing_) {
-                    cudaEvent_t step_end = pool_event();
-                    N3D_CUDA(cudaEventRecord(step_end, stream_));
-                    step_ev_.emplace_back(step_begin, step_end);
-                }
+                run_step(d_table + step_first[w], B, step_S[w], d_len + step_first[w], d_valid + step_first[w],
+                         embeds);
             }
         }
         // ---- results
@@ -994,6 +935,313 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
         }
         prof_collect();
         check_dev_error();
+    }
+}
+
+// Log-mel of every segment (segment i's samples start at d_audio[base[i]]) into one
+// [groups·sub, n_mels] TF32 pair, then one embedder GEMM over all groups ->
+// [total_groups, hidden] (src/mel.rs:160-225, src/encoder.rs:126-146).
+const float* Model::mel_embed(const float* d_audio, const std::vector<long long>& base,
+                              const std::vector<MelSeg>& segs, long long total_groups, long long total_frames) {
+    const Config& c = cfg_;
+    const int h = c.hidden, sub = c.sub;
+    std::vector<long long> f_base(total_frames), f_out(total_frames);
+    std::vector<int> f_meta(2 * total_frames);
+    {
+        long long f = 0;
+        for (size_t i = 0; i < segs.size(); i++) {
+            const MelSeg& s = segs[i];
+            for (int t = 0; t < s.frames; t++, f++) {
+                f_base[f] = base[i];
+                f_meta[2 * f] = t * c.hop - (s.centered ? c.n_fft / 2 : 0);
+                f_meta[2 * f + 1] = (int)s.len;
+                f_out[f] = s.group_base * sub + t;
+            }
+        }
+    }
+    const long long mel_rows = std::max(total_groups * sub, 1LL);
+    float* mel_hi = (float*)ws("mel_hi", mel_rows * c.n_mels * 4);
+    float* mel_lo = (float*)ws("mel_lo", mel_rows * c.n_mels * 4);
+    N3D_CUDA(cudaMemsetAsync(mel_hi, 0, mel_rows * c.n_mels * 4, stream_));
+    N3D_CUDA(cudaMemsetAsync(mel_lo, 0, mel_rows * c.n_mels * 4, stream_));
+    if (total_frames > 0) {
+        long long* d_fb = (long long*)ws("f_base", total_frames * 8);
+        long long* d_fo = (long long*)ws("f_out", total_frames * 8);
+        int* d_fm = (int*)ws("f_meta", total_frames * 8);
+        N3D_CUDA(cudaMemcpyAsync(d_fb, f_base.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+        N3D_CUDA(cudaMemcpyAsync(d_fo, f_out.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+        N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+        prof_begin();
+        launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_,
+                   c.preemph, mel_hi, mel_lo, nullptr, d_fo);
+        prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
+    }
+    const long long K_emb = (long long)sub * c.n_mels;
+    float* embeds = (float*)ws("embeds", std::max(total_groups, 1LL) * h * 4);
+    if (total_groups > 0) {
+        Epi e;
+        e.mode = EPI_STORE;
+        e.out = embeds;
+        e.ldo = h;
+        const long long rows_cap = ws_["mel_hi"].bytes / (K_emb * 4);
+        prof_begin();
+        gemm_tf32x3(stream_, SplitOperand{mel_hi, mel_lo, rows_cap, K_emb, K_emb}, embed_.op(), (int)total_groups, h,
+                    (int)K_emb, 0, e, dev_err_);
+        prof_end(K_GEMM_EMBED, 2.0 * total_groups * h * K_emb, 0);
+    }
+    return embeds;
+}
+
+void Model::run_step(const SeqStep* d_st, int B, int S, const int* d_len, const int* d_valid, const float* embeds) {
+    const Config& c = cfg_;
+    const int h = c.hidden;
+    float* win = (float*)ws("win", (size_t)B * S * h * 4);
+    cudaEvent_t step_begin = nullptr;
+    if (step_timing_) {
+        step_begin = pool_event();
+        N3D_CUDA(cudaEventRecord(step_begin, stream_));
+    }
+    prof_begin();
+    launch_assemble(stream_, d_st, B, embeds, win, S, h);
+    prof_end(K_ASSEMBLE, 0, 2.0 * B * S * h * 4);
+    tower(B, S, d_len, d_valid, nullptr);
+    head(B, S, d_len);
+    const CacheConst cc{h, c.num_speakers, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
+                        c.latest_boost};
+    prof_begin();
+    launch_cache_update(stream_, d_st, B, (float*)ws("win", 0), (float*)ws("logits", 0), S, cc, silence_);
+    prof_end(K_CACHE, 0, 0);
+    if (step_timing_) {
+        cudaEvent_t step_end = pool_event();
+        N3D_CUDA(cudaEventRecord(step_end, stream_));
+        step_ev_.emplace_back(step_begin, step_end);
+    }
+}
+
+// ------------------------------------------------------------ sessions
+
+struct Model::SessionChunk {
+    Session* s;
+    int idx;             // position in the caller's list
+    long long off, len;  // samples, absolute
+    int centered, la;
+    bool last;
+};
+
+namespace {
+
+// The next chunk of `s` whose samples are all present: plan_streaming's chunk list,
+// decided as audio arrives (`final`: no more audio will come).
+bool next_session_chunk(const Config& c, const Session& s, bool final, Model::SessionChunk& ch) {
+    if (s.done) return false;
+    const int cl = c.modes[s.mode][0], rc = c.modes[s.mode][1];
+    const long long mel_chunk = (long long)(cl + rc) * c.sub, mel_step = (long long)cl * c.sub;
+    const long long first = (mel_chunk - 1) * c.hop + c.win / 2;
+    const long long per_chunk = mel_chunk * c.hop + c.win;
+    const long long n = s.received;
+    if (s.next_chunk == 0) {
+        if (n < first && !final) return false;
+        ch.off = 0, ch.len = std::min(first, n), ch.centered = 1, ch.la = rc, ch.last = false;
+        return true;
+    }
+    const long long start = (long long)s.next_chunk * mel_step * c.hop - c.n_fft / 2;
+    if (start + per_chunk <= n) {
+        ch.off = start, ch.len = per_chunk, ch.centered = 0, ch.la = rc, ch.last = false;
+        return true;
+    }
+    if (!final) return false;
+    ch.off = std::min(start, n), ch.len = n - ch.off, ch.centered = 1, ch.la = 0, ch.last = true;
+    return true;
+}
+
+}  // namespace
+
+Session* Model::session_open(int mode) {
+    if (mode < 0 || mode > 2) throw Error(kStatusArg, "streaming mode must be low, very low or ultra low latency");
+    N3D_CUDA(cudaSetDevice(device_));
+    auto s = std::make_unique<Session>();
+    s->model = this;
+    s->mode = mode;
+    const size_t pre_bytes = (size_t)2 * s_cap_ * cfg_.hidden * 4, cp_bytes = (size_t)2 * s_cap_ * cfg_.num_speakers * 4;
+    N3D_CUDA(cudaMalloc(&s->pre, pre_bytes));
+    if (cudaMalloc(&s->cprob, cp_bytes) != cudaSuccess) {
+        cudaFree(s->pre);
+        throw Error(kStatusCuda, "CUDA error in session state allocation: out of device memory");
+    }
+    return s.release();
+}
+
+void Model::session_free(Session* s) {
+    if (!s) return;
+    cudaSetDevice(device_);
+    cudaStreamSynchronize(stream_);  // no step of this session is still in flight
+    cudaFree(s->pre);
+    cudaFree(s->cprob);
+    delete s;
+}
+
+void Model::sessions_push(const std::vector<Session*>& ss, const std::vector<const float*>& samples,
+                          const std::vector<long long>& lens, bool close, std::vector<std::vector<float>>& rows) {
+    N3D_CUDA(cudaSetDevice(device_));
+    const int n = (int)ss.size();
+    for (int i = 0; i < n; i++) {
+        const Session* s = ss[i];
+        if (!s || s->model != this) throw Error(kStatusArg, "session does not belong to this model");
+        if (s->failed) throw Error(kStatusArg, "session failed in an earlier call; free it");
+        if (s->closed) throw Error(kStatusArg, "session is closed");
+        for (int j = 0; j < i; j++)
+            if (ss[j] == s) throw Error(kStatusArg, "a session appears twice in one call");
+    }
+    rows.assign(n, {});
+    try {
+        for (int i = 0; i < n; i++) {
+            if (lens[i] > 0) ss[i]->audio.insert(ss[i]->audio.end(), samples[i], samples[i] + lens[i]);
+            ss[i]->received += lens[i];
+        }
+        for (;;) {  // one round = the next ready chunk of every session
+            std::vector<SessionChunk> items;
+            for (int i = 0; i < n; i++) {
+                SessionChunk ch{};
+                ch.s = ss[i];
+                ch.idx = i;
+                if (next_session_chunk(cfg_, *ss[i], close, ch)) items.push_back(ch);
+            }
+            if (items.empty()) break;
+            session_round(items, rows);
+        }
+        if (close)
+            for (Session* s : ss) s->closed = true;
+    } catch (...) {
+        for (Session* s : ss) s->failed = true;
+        throw;
+    }
+}
+
+void Model::session_round(std::vector<SessionChunk>& items, std::vector<std::vector<float>>& rows) {
+    const Config& c = cfg_;
+    const int ns = c.num_speakers, h = c.hidden, sub = c.sub;
+    const int nb = (int)items.size();
+    // ---- step plans; the cache counts advance exactly as in plan_streaming
+    std::vector<MelSeg> segs(nb);
+    std::vector<StepPlan> sps(nb);
+    std::vector<long long> aoff(nb);
+    long long total_samples = 0, total_groups = 0, total_frames = 0;
+    for (int i = 0; i < nb; i++) {
+        const SessionChunk& it = items[i];
+        Session& s = *it.s;
+        const long long nm = frame_count(c, it.len, it.centered != 0);
+        const long long groups = ceil_div(nm, sub);
+        if (groups < it.la)
+            throw Error(kStatusAudio, "unsupported audio: a streaming chunk holds " + std::to_string(groups) +
+                                          " encoder frames, fewer than the look-ahead of " + std::to_string(it.la));
+        segs[i] = MelSeg{0, it.len, it.centered, (int)nm, (int)groups, total_groups};
+        aoff[i] = total_samples;
+        total_samples += it.len;
+        total_groups += groups;
+        total_frames += nm;
+        StepPlan sp{};
+        sp.n_new = (int)groups;
+        sp.nchunk = (int)(groups - it.la);
+        sp.S = s.ncache + s.nfifo + sp.n_new;
+        sp.valid = sp.S;
+        sp.keep_rows = (int)std::min((long long)sp.nchunk * sub, nm);
+        if (sp.S > s_cap_) throw Error(kStatusGpu, "window of " + std::to_string(sp.S) + " frames exceeds 1024");
+        CacheSim cs{c.s_fifo, c.s_period, c.cache_len};
+        cs.ncache = s.ncache;
+        cs.nfifo = s.nfifo;
+        cs.compressed = s.compressed;
+        cs.step(sp);
+        s.ncache = cs.ncache;
+        s.nfifo = cs.nfifo;
+        s.compressed = cs.compressed;
+        sps[i] = sp;
+    }
+    // ---- the chunks' audio, log-mel, embedder
+    float* d_audio = (float*)ws("s_audio", (size_t)std::max(total_samples, 1LL) * 4);
+    for (int i = 0; i < nb; i++) {
+        const SessionChunk& it = items[i];
+        if (it.len > 0)  // pageable source: returns once the samples are staged, so trimming below is safe
+            N3D_CUDA(cudaMemcpyAsync(d_audio + aoff[i], it.s->audio.data() + (it.off - it.s->base), it.len * 4,
+                                     cudaMemcpyHostToDevice, stream_));
+    }
+    const float* embeds = mel_embed(d_audio, aoff, segs, total_groups, total_frames);
+    // ---- one step per session
+    long long out_total = 0;
+    std::vector<long long> out_base(nb);
+    for (int i = 0; i < nb; i++) {
+        out_base[i] = out_total;
+        out_total += sps[i].keep_rows;
+    }
+    float* outl = (float*)ws("s_out", (size_t)std::max(out_total, 1LL) * ns * 4);
+    std::vector<SeqStep> table;
+    std::vector<int> seq_len, valid;
+    int Smax = 0;
+    for (int i = 0; i < nb; i++) {
+        const StepPlan& sp = sps[i];
+        if (sp.S == 0) continue;  // nothing cached and no new frames: the step changes nothing
+        Session& s = *items[i].s;
+        const int cur = (int)(s.steps & 1), nxt = cur ^ 1;
+        SeqStep q{};
+        q.S = sp.S;
+        q.valid = sp.valid;
+        q.ncache = sp.ncache;
+        q.nfifo = sp.nfifo;
+        q.nchunk = sp.nchunk;
+        q.popped = sp.popped;
+        q.compress = sp.compress;
+        q.was_compressed = sp.was_compressed;
+        q.keep_rows = sp.keep_rows;
+        q.emb_row = segs[i].group_base;
+        q.pre_in = s.pre + (size_t)cur * s_cap_ * h;
+        q.pre_out = s.pre + (size_t)nxt * s_cap_ * h;
+        q.cp_in = s.cprob + (size_t)cur * s_cap_ * ns;
+        q.cp_out = s.cprob + (size_t)nxt * s_cap_ * ns;
+        q.out_logits = outl + out_base[i] * ns;
+        table.push_back(q);
+        seq_len.push_back(sp.S);
+        valid.push_back(sp.valid);
+        Smax = std::max(Smax, sp.S);
+        s.steps++;
+    }
+    if (!table.empty()) {
+        SeqStep* d_table = (SeqStep*)ws("s_steps", table.size() * sizeof(SeqStep));
+        int* d_len = (int*)ws("s_seq_len", table.size() * 4);
+        int* d_valid = (int*)ws("s_valid", table.size() * 4);
+        N3D_CUDA(cudaMemcpyAsync(d_table, table.data(), table.size() * sizeof(SeqStep), cudaMemcpyHostToDevice,
+                                 stream_));
+        N3D_CUDA(cudaMemcpyAsync(d_len, seq_len.data(), seq_len.size() * 4, cudaMemcpyHostToDevice, stream_));
+        N3D_CUDA(cudaMemcpyAsync(d_valid, valid.data(), valid.size() * 4, cudaMemcpyHostToDevice, stream_));
+        run_step(d_table, (int)table.size(), (Smax + 7) / 8 * 8, d_len, d_valid, embeds);
+    }
+    // ---- new rows
+    std::vector<float> out((size_t)out_total * ns);
+    if (out_total)
+        N3D_CUDA(cudaMemcpyAsync(out.data(), outl, out.size() * 4, cudaMemcpyDeviceToHost, stream_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    prof_collect();
+    check_dev_error();
+    for (int i = 0; i < nb; i++) {
+        std::vector<float>& r = rows[items[i].idx];
+        r.insert(r.end(), out.begin() + out_base[i] * ns, out.begin() + (out_base[i] + sps[i].keep_rows) * ns);
+    }
+    // ---- advance the schedules; drop the samples no later chunk reads
+    for (int i = 0; i < nb; i++) {
+        Session& s = *items[i].s;
+        s.next_chunk++;
+        s.num_chunks++;
+        if (items[i].last) {
+            s.done = true;
+            s.audio.clear();
+            s.audio.shrink_to_fit();
+            s.base = s.received;
+            continue;
+        }
+        const long long mel_step = (long long)c.modes[s.mode][0] * sub;
+        const long long keep_from = std::min((long long)s.next_chunk * mel_step * c.hop - c.n_fft / 2, s.received);
+        if (keep_from > s.base) {
+            s.audio.erase(s.audio.begin(), s.audio.begin() + (keep_from - s.base));
+            s.base = keep_from;
+        }
     }
 }
 

@@ -82,6 +82,30 @@ struct ClipPlan {
 ClipPlan plan_offline(const Config& c, long long n);
 ClipPlan plan_streaming(const Config& c, long long n, int mode);
 
+// ----------------------------------------------------------------- sessions
+
+class Model;
+
+// Incremental streaming (one recording arriving in pieces).  The chunk schedule is
+// run_streaming's (src/model.rs:343-365): chunk 0 runs once its (c+r)·8 mel frames of
+// audio have arrived, every later full chunk once its samples are complete, and the
+// final centred chunk at close; the speaker cache stays on the device between calls.
+struct Session {
+    Model* model = nullptr;
+    int mode = 0;
+    long long received = 0;   // samples pushed so far
+    long long base = 0;       // absolute index of audio[0]; earlier samples are no longer needed
+    std::vector<float> audio;
+    int next_chunk = 0;
+    bool done = false;        // the final chunk has run
+    bool closed = false;
+    bool failed = false;      // a call failed part-way; the session can only be freed
+    int ncache = 0, nfifo = 0, compressed = 0, num_chunks = 0;
+    long long steps = 0;      // steps run (ping-pong parity of the state buffers)
+    float* pre = nullptr;     // [2, s_cap, hidden]: cache ++ FIFO embeddings
+    float* cprob = nullptr;   // [2, s_cap, num_speakers]: their stored probabilities
+};
+
 // ----------------------------------------------------------------- model
 
 struct Buf {
@@ -114,6 +138,16 @@ class Model {
                    std::vector<std::vector<float>>* host_out, float* d_logits,
                    const std::vector<long long>* out_offsets, std::vector<ClipPlan>* plans_out);
 
+    // Sessions of this model (freed before the model).  sessions_push appends
+    // samples[i] to ss[i] and runs every chunk that is complete, the steps of all
+    // sessions batched round by round; with `close` it also runs the final chunks.
+    // rows[i] receives session i's new logits rows ([rows, num_speakers]).
+    struct SessionChunk;  // one ready chunk of one session (model.cpp)
+    Session* session_open(int mode);
+    void session_free(Session* s);
+    void sessions_push(const std::vector<Session*>& ss, const std::vector<const float*>& samples,
+                       const std::vector<long long>& lens, bool close, std::vector<std::vector<float>>& rows);
+
     // Stage entry points (single sequence, host buffers).
     int log_mel(const float* samples, long long n, bool centered, std::vector<float>& out);
     void embed_range(const float* mel, long long num_frames, long long lo, long long hi, float* out);
@@ -138,6 +172,12 @@ class Model {
     void upload_weights(const std::string& dir);
     void tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain);
     void head(int B, int S, const int* d_seq_len);
+    const float* mel_embed(const float* d_audio, const std::vector<long long>& base, const std::vector<MelSeg>& segs,
+                           long long total_groups, long long total_frames);
+    // One chunk-loop step of B sequences (rows of stride S): window assembly, tower,
+    // head, cache update.
+    void run_step(const SeqStep* d_steps, int B, int S, const int* d_len, const int* d_valid, const float* embeds);
+    void session_round(std::vector<SessionChunk>& items, std::vector<std::vector<float>>& rows);
     void* ws(const char* name, size_t bytes);
     void check_dev_error();
 

@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 import re
 import subprocess
 from dataclasses import dataclass
@@ -113,6 +114,12 @@ def lib() -> C.CDLL:
         "n3d_batch_out_frames": ([vp, C.c_int, C.POINTER(_sz), _sz, C.POINTER(_sz)], C.c_int),
         "n3d_run_batch_device": ([vp, C.c_int, vp, C.POINTER(_sz), C.POINTER(_sz), _sz, vp, C.POINTER(_sz)],
                                  C.c_int),
+        "n3d_session_open": ([vp, C.c_int, C.POINTER(vp)], C.c_int),
+        "n3d_session_push": ([vp, fpp, _sz, C.POINTER(_RunOutput)], C.c_int),
+        "n3d_session_close": ([vp, C.POINTER(_RunOutput)], C.c_int),
+        "n3d_session_free": ([vp], None),
+        "n3d_sessions_push": ([C.POINTER(vp), C.POINTER(fpp), C.POINTER(_sz), _sz, C.c_int, C.POINTER(_RunOutput)],
+                              C.c_int),
         "n3d_log_mel": ([vp, fpp, _sz, C.c_int, fpp, _sz, C.POINTER(_sz)], C.c_int),
         "n3d_embed_range": ([vp, fpp, _sz, _sz, _sz, fpp], C.c_int),
         "n3d_forward_embeds": ([vp, fpp, _sz, _sz, fpp], C.c_int),
@@ -170,6 +177,7 @@ class Model:
     def __init__(self, handle: int, device: int):
         self._h = C.c_void_p(handle)
         self.device = device
+        self._sessions = weakref.WeakSet()
 
     @classmethod
     def load_gpu(cls, directory: str, device: int = 0) -> "Model":
@@ -179,6 +187,8 @@ class Model:
 
     def close(self) -> None:
         if self._h:
+            for ss in list(self._sessions):  # sessions must go before their model
+                ss.free()
             lib().n3d_model_free(self._h)
             self._h = C.c_void_p()
 
@@ -219,6 +229,25 @@ class Model:
         lens = (_sz * max(n, 1))(*[a.size for a in arrs])
         outs = (_RunOutput * max(n, 1))()
         _check(lib().n3d_run_batch(self._h, MODES[mode], ptrs, lens, n, outs))
+        return [_collect(outs[i]) for i in range(n)]
+
+    def open_session(self, mode: str) -> "Session":
+        """An incremental streaming session (n3d_session_open)."""
+        h = C.c_void_p()
+        _check(lib().n3d_session_open(self._h, MODES[mode], C.byref(h)))
+        ss = Session(h, self)
+        self._sessions.add(ss)
+        return ss
+
+    def sessions_push(self, sessions, pieces, close: bool = False) -> list[RunOutput]:
+        """n3d_sessions_push: pieces[i] appended to sessions[i]; the new rows of each."""
+        arrs = [_f32(p) for p in pieces]
+        n = len(sessions)
+        hs = (C.c_void_p * max(n, 1))(*[ss._h for ss in sessions])
+        ptrs = (_fp * max(n, 1))(*[_ptr(a) for a in arrs])
+        lens = (_sz * max(n, 1))(*[a.size for a in arrs])
+        outs = (_RunOutput * max(n, 1))()
+        _check(lib().n3d_sessions_push(hs, ptrs, lens, n, int(close), outs))
         return [_collect(outs[i]) for i in range(n)]
 
     def batch_out_frames(self, lens, mode: str = "offline") -> list[int]:
@@ -287,6 +316,37 @@ class Model:
         out = np.zeros(frames * 8 * self.num_speakers, np.float32)
         _check(lib().n3d_forward_window(self._h, _ptr(e), frames, valid, _ptr(out)))
         return out.reshape(frames * 8, self.num_speakers)
+
+
+class Session:
+    """A streaming session: push audio as it arrives, get each completed chunk's logits
+    rows; close() runs the final chunk.  Concatenated, the rows equal run_streaming."""
+
+    def __init__(self, handle, model: Model):
+        self._h = handle
+        self._model = model  # the model outlives its sessions
+
+    def push(self, samples) -> RunOutput:
+        s = _f32(samples)
+        o = _RunOutput()
+        _check(lib().n3d_session_push(self._h, _ptr(s), s.size, C.byref(o)))
+        return _collect(o)
+
+    def close(self) -> RunOutput:
+        o = _RunOutput()
+        _check(lib().n3d_session_close(self._h, C.byref(o)))
+        return _collect(o)
+
+    def free(self) -> None:
+        if self._h:
+            lib().n3d_session_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def extract_speaker_dict(logits, num_frames: int, num_speakers: int, duration: float, mask=None,

@@ -36,6 +36,12 @@ def test_null_arguments_are_rejected():
     st = n3d.lib().n3d_run_offline(None, None, 0, C.byref(out))
     assert n3d.STATUS[st] == "InvalidArgument"
     assert b"null" in n3d.lib().n3d_last_error()
+    h = C.c_void_p()
+    st = n3d.lib().n3d_session_open(None, 2, C.byref(h))
+    assert n3d.STATUS[st] == "InvalidArgument" and not h.value
+    st = n3d.lib().n3d_session_push(None, None, 0, C.byref(out))
+    assert n3d.STATUS[st] == "InvalidArgument"
+    n3d.lib().n3d_session_free(None)  # freeing nothing is a no-op
 
 
 @pytest.mark.parametrize("seed", [0, 1, 2])
