@@ -110,6 +110,28 @@ def oracle_rtfx(ckpt: str, clip: np.ndarray, reps: int = 1):
     return clip.size / SR / dt, dt
 
 
+def live_sessions(model, items, mode: str, push_samples: int):
+    """Serve `items` as live streams: every call of n3d_sessions_push hands each session
+    the next `push_samples` of its audio (pageable host memory, as a server receives
+    it) and returns the rows of every chunk that became complete.  Returns the host
+    wall time of each call (ms) and the total wall time (s)."""
+    sessions = [model.open_session(mode) for _ in items]
+    n = max(c.size for c in items)
+    lat = []
+    t_all = time.perf_counter()
+    for t in range(0, n, push_samples):
+        t0 = time.perf_counter()
+        model.sessions_push(sessions, [c[t:t + push_samples] for c in items])
+        lat.append((time.perf_counter() - t0) * 1e3)
+    t0 = time.perf_counter()
+    model.sessions_push(sessions, [np.zeros(0, np.float32)] * len(items), close=True)
+    lat.append((time.perf_counter() - t0) * 1e3)
+    total = time.perf_counter() - t_all
+    for ss in sessions:
+        ss.free()
+    return np.array(lat), total
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -303,6 +325,20 @@ def main():
     launches = sum(v["launches"] for v in prof.values())
     total_prof_ms = sum(v["ms"] for v in classes.values())
 
+    live = None
+    if args.workload == "c3":
+        # live serving through the session API: 240 ms of audio per session per call
+        # (= one ultra_low_latency chunk step); the first 3 calls are warm-up
+        push = 3 * 8 * 160
+        barrier()
+        lat, wall = live_sessions(model, items, mode, push)
+        steady = lat[3:-1] if lat.size > 5 else lat
+        live = {"push_samples": push, "calls": int(lat.size),
+                "p50_ms": float(np.percentile(steady, 50)), "p99_ms": float(np.percentile(steady, 99)),
+                "max_ms": float(steady.max()), "rtfx": world * n_items * item_s / max_over_ranks(wall),
+                "what": f"host wall time of one n3d_sessions_push call handing 240 ms of new audio to each of "
+                        f"{n_items} sessions (H2D, log-mel, embedder, one chunk step, D2H of the new rows)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rt, dt = oracle_rtfx(ckpt, make_clips(0, 1, CLIP_S)[0])
@@ -348,6 +384,7 @@ def main():
             "dominant_kernel": top[0],
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            **({"live_sessions": live} if live else {}),
         }
         print(json.dumps(line), flush=True)
     model.close()
