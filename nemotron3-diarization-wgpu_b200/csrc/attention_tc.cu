@@ -22,7 +22,10 @@
 //   warps 2..9  softmax, two warps per query row (TMEM lane): each takes half of
 //               the block's keys and half of the output columns; online max/sum;
 //               P_j as bf16 pairs written over the S_j columns it read (QK_{j+2}
-//               is issued once PV_j has completed); O folded into registers
+//               is issued once PV_j has completed); O folded into registers.
+//               exp is 2^x on the special-function unit after one FMA folds the
+//               1/sqrt(hd) scale, log2 e and the running max together; sums and the
+//               O fold use packed f32x2 FMA/add.
 // TMEM (256 columns): S/P[2] 0..127, O[2] 128..255.
 // Every wait is bounded; an expired wait records its site in *err.
 
@@ -43,6 +46,33 @@ constexpr int THREADS = 320;
 constexpr int SMEM_BYTES = 2 * Q_TILE + 2 * STAGE_BYTES + 1024 + 256 + 6 * QT * 4;
 constexpr uint32_t COL_S = 0, COL_O = 128, TMEM_COLS = 256;
 constexpr int DEV_TIMEOUT_ATTN = 5;
+
+// f32 pairs in one 64-bit register: Blackwell's packed FMA / add issue two lanes' worth
+// of work per instruction.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// 2^x on the special-function unit (relative error ~2^-22; results below 2^-126 flush to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
 
 __global__ void __launch_bounds__(THREADS, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tQh, const __grid_constant__ CUtensorMap tQl,
@@ -173,18 +203,21 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
         const uint32_t bar_id = 1 + qd;  // named barrier of this quadrant's two warps
-        const float scaling = 0.125f;    // 1 / sqrt(64), a power of two: s * scaling is exact
-        float o[32];
+        // exp(x) = 2^(x log2 e): p = 2^(s * k - m * k) with k = hd^-1/2 * log2 e, one FMA and
+        // one ex2 per score; m is the running row maximum of the raw scores
+        const float k2 = 0.125f * 1.4426950408889634f;
+        uint64_t o[16];  // this warp's 32 output columns as f32 pairs
 #pragma unroll
-        for (int d = 0; d < 32; d++) o[d] = 0.0f;
+        for (int d = 0; d < 16; d++) o[d] = 0;
         float m = -INFINITY, l = 0.0f, c_prev = 0.0f;
         bool ok = true;
         auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
         auto fold = [&](int jj, float c) {  // O <- O * c + PV_jj, this warp's 32 columns
             float v[32];
             tmem_ld32(lb + COL_O + 64u * (jj & 1) + 32 * hf, v);
+            const uint64_t c2 = pack2(c, c);
 #pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = fmaf(o[i], c, v[i]);
+            for (int i = 0; i < 16; i++) o[i] = fma2(o[i], c2, pack2(v[2 * i], v[2 * i + 1]));
         };
         for (int j = 0; j < nblk; j++) {
             const int bf = j & 1;
@@ -206,15 +239,21 @@ __global__ void __launch_bounds__(THREADS, 2)
             red_max[(bf * 2 + hf) * QT + r] = mloc;
             pair_sync();
             // the row maximum is finite: key 0 is valid and the running max carries it
-            const float mx = fmaxf(m, fmaxf(mloc, red_max[(bf * 2 + (hf ^ 1)) * QT + r]) * scaling);
-            const float corr = expf(m - mx);  // 0 on the first block (m = -inf)
-            float sum = 0.0f;
+            const float mx = fmaxf(m, fmaxf(mloc, red_max[(bf * 2 + (hf ^ 1)) * QT + r]));
+            const float corr = ex2_approx((m - mx) * k2);  // 0 on the first block (m = -inf)
+            const uint64_t k22 = pack2(k2, k2), nmk = pack2(-mx * k2, -mx * k2);
+            uint64_t sum2 = 0;
 #pragma unroll
-            for (int c = 0; c < 32; c++) {
-                s[c] = expf(fmaf(s[c], scaling, -mx));
-                sum += s[c];
+            for (int c = 0; c < 32; c += 2) {
+                float t0, t1;
+                unpack2(fma2(pack2(s[c], s[c + 1]), k22, nmk), t0, t1);  // masked keys: -inf -> p = 0
+                s[c] = ex2_approx(t0);
+                s[c + 1] = ex2_approx(t1);
+                sum2 = add2(sum2, pack2(s[c], s[c + 1]));
             }
-            l = l * corr + sum;  // this half's partial row sum, at the common running max
+            float sa, sb;
+            unpack2(sum2, sa, sb);
+            l = l * corr + (sa + sb);  // this half's partial row sum, at the common running max
             m = mx;
             {
                 uint32_t hi[16], lo[16];
@@ -257,8 +296,10 @@ __global__ void __launch_bounds__(THREADS, 2)
 #pragma unroll
             for (int d = 0; d < 32; d += 4) {
                 float x[4], lo[4];
+                unpack2(o[d / 2], x[0], x[1]);
+                unpack2(o[d / 2 + 1], x[2], x[3]);
 #pragma unroll
-                for (int i = 0; i < 4; i++) x[i] = o[d + i] * inv;
+                for (int i = 0; i < 4; i++) x[i] *= inv;
                 if (ctx_lo) {
 #pragma unroll
                     for (int i = 0; i < 4; i++) split_tf32(x[i], x[i], lo[i]);
