@@ -289,14 +289,14 @@ __device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, con
 // `stg` is this warp's 8 KB staging area (hi box, lo box).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
-                                                  int lane, uint8_t* stg) {
+                                                  int lane, uint8_t* stg, int c_begin = 0, int c_end = BN) {
     const int rowbase = m0 + q * 32;
     if (rowbase >= M) return;  // whole warp past the end: nothing to load or store
     const int r = rowbase + lane;
     uint8_t* bhi = stg;
     uint8_t* blo = stg + 4096;
     if (epi.mode == EPI_QKV_ATTN) {
-        for (int c = 0; c < BN; c += 64) {
+        for (int c = c_begin; c < c_end; c += 64) {
             float v[64];
             tmem_ld32(tl + c, v);
             tmem_ld32(tl + c + 32, v + 32);
@@ -350,7 +350,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
         }
     } else {
         const bool pair = epi.mode != EPI_STORE;
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = c_begin; c < c_end; c += 32) {
             float v[32];
             tmem_ld32(tl + c, v);
             const int col0 = n0 + c;
@@ -540,25 +540,30 @@ __global__ void __launch_bounds__(192, 1)
 // own epilogue warps store.  Barriers: full[s] lives in the leader (both CTAs'
 // loads complete on it), empty[s] and acc_full[b] in both (arrived by the
 // leader's multicast commits), acc_empty[b] in the leader (8 epilogue warps).
-template <int BN>
+template <int BN, int EW>
 struct PairCfg {
     static constexpr int A_BYTES = BM * PBK * 4;
     static constexpr int B_BYTES = (BN / 2) * PBK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int STAGING = 4 * 8192;
+    static constexpr int STAGING = EW * 8192;  // per epilogue warp: hi + lo boxes
+    static constexpr int THREADS = 64 + 32 * EW;
     static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 8 ? 8 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
     static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
 };
 
-template <int BN>
-__global__ void __launch_bounds__(192, 1)
+// EW epilogue warps per CTA: with 8, warps w and w + 4 share TMEM lane quadrant w % 4
+// and take half of the tile's columns each (two warps per SM sub-partition hide the
+// latency of heavy epilogues such as GELU + split).
+template <int BN, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tA_hi, const __grid_constant__ CUtensorMap tA_lo,
                      const __grid_constant__ CUtensorMap tB_hi, const __grid_constant__ CUtensorMap tB_lo, int M,
                      int N, int K, int kb_per_tap, const __grid_constant__ Epi epi, int* err) {
-    using Cfg = PairCfg<BN>;
+    using Cfg = PairCfg<BN, EW>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
@@ -582,7 +587,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 8);
+            mbar_init(&acc_empty[b], 2 * EW);
         }
         mbar_fence_init();
         tma_prefetch_desc(&tA_hi);
@@ -658,7 +663,8 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
-        const int q = warp & 3;
+        const int q = warp & 3, part = (warp - 2) >> 2;
+        constexpr int CW = BN / (EW / 4);  // columns per epilogue warp
         const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
         int it = 0;
         for (int t = cid; t < tiles; t += ncl, it++) {
@@ -671,8 +677,9 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
             if (epi.tma)
                 epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
-            else
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, part * CW,
+                                      part * CW + CW);
+            else if (part == 0)  // direct stores: one warp per quadrant takes the whole tile
                 epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
             tc_fence_before();
             __syncwarp();
@@ -784,10 +791,10 @@ void launch_persistent(cudaStream_t s, const SplitOperand& A, const SplitOperand
     N3D_CUDA(cudaGetLastError());
 }
 
-template <int BN>
+template <int BN, int EW>
 void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
                  const Epi& epi, int* err) {
-    using Cfg = PairCfg<BN>;
+    using Cfg = PairCfg<BN, EW>;
     static int max_clusters = 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -797,13 +804,13 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(Cfg::THREADS);
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     if (!max_clusters) {
-        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
         cfg.gridDim = dim3(2 * (sm_count() / 2));
-        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN>, &cfg));
+        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN, EW>, &cfg));
         if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
     }
     const CUtensorMap a_hi = make_map(A.hi, A.rows, A.cols, A.ld, BM, PBK);
@@ -812,7 +819,7 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     const CUtensorMap b_lo = make_map(B.lo, B.rows, B.cols, B.ld, BN / 2, PBK);
     const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
     cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
-    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, a_hi, a_lo, b_hi, b_lo, M, N, K,
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EW>, a_hi, a_lo, b_hi, b_lo, M, N, K,
                                 kb_per_tap > 0 ? kb_per_tap * (BK / PBK) : 0, epi, err));
 }
 
@@ -872,7 +879,15 @@ void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         case 64: launch_persistent<64>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 128: launch_persistent<128>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
         case 192: launch_persistent<192>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
-        default: launch_pair<256>(s, A, B, M, N, K, kb_per_tap, epi, err); break;
+        default:
+            // the erf-GELU + split epilogue is latency bound on one warp per sub-partition:
+            // 8 epilogue warps (measured: FC1 177 -> 217 TFLOP/s; the lighter epilogues lose
+            // more to the smaller pipeline than they gain)
+            if (epi.tma && epi.mode == EPI_GELU_SPLIT)
+                launch_pair<256, 8>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            else
+                launch_pair<256, 4>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            break;
     }
 }
 
