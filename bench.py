@@ -349,7 +349,7 @@ def main():
         line = {
             "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (3xTF32 GEMMs, 3xBF16 attention, on tcgen05)", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f32 (split GEMMs: TF32 hi*hi + 2 BF16 cross terms; 3xBF16 attention; tcgen05)", "data": "synthetic",
             "config": {"workload": desc, "seconds_per_item": item_s, "items_per_step_per_gpu": n_items,
                        "mode": mode, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},

@@ -123,7 +123,7 @@ struct DevScratch {
 extern "C" {
 
 const char* n3d_last_error(void) { return g_last_error.c_str(); }
-const char* n3d_version(void) { return "n3d-b200 0.1 (sm_100a, 3xTF32 tcgen05)"; }
+const char* n3d_version(void) { return "n3d-b200 0.2 (sm_100a, tcgen05: TF32+2xBF16 split GEMMs, 3xBF16 attention)"; }
 
 n3d_status n3d_model_load_gpu(const char* dir, int device, n3d_model** out) {
     return guarded([&] {
@@ -423,20 +423,18 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
         DevScratch sc;
-        float* xh = sc.get(rows * cols);
-        float* xl = sc.get(rows * cols);
-        float* wh = sc.get(out * cols);
-        float* wl = sc.get(out * cols);
-        n3d::launch_split(k.stream, d_x, (long long)(rows * cols), xh, xl);
-        n3d::launch_split(k.stream, d_w, (long long)(out * cols), wh, wl);
+        const n3d::Split3Out x{sc.get(rows * cols), sc.get(rows * cols / 2), sc.get(rows * cols / 2)};
+        const n3d::Split3Out w{sc.get(out * cols), sc.get(out * cols / 2), sc.get(out * cols / 2)};
+        n3d::launch_split(k.stream, d_x, (long long)(rows * cols), x);
+        n3d::launch_split(k.stream, d_w, (long long)(out * cols), w);
         n3d::Epi e;
         e.mode = n3d::EPI_STORE;
         e.bias = d_bias;
         e.out = d_y;
         e.ldo = (long long)out;
-        n3d::gemm_tf32x3(k.stream, n3d::SplitOperand{xh, xl, (long long)rows, (long long)cols, (long long)cols},
-                         n3d::SplitOperand{wh, wl, (long long)out, (long long)cols, (long long)cols}, (int)rows,
-                         (int)out, (int)cols, 0, e, k.err);
+        n3d::gemm_split3(k.stream, n3d::SplitOperand{x.hi, x.hb, x.lb, (long long)rows, (long long)cols, (long long)cols},
+                         n3d::SplitOperand{w.hi, w.hb, w.lb, (long long)out, (long long)cols, (long long)cols},
+                         (int)rows, (int)out, (int)cols, 0, e, k.err);
         kcheck(k);
     });
 }
@@ -454,7 +452,7 @@ n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols
         arg_check(d_x && d_w && d_b && d_y, "n3d_layer_norm: null argument");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
-        n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, d_y, nullptr);
+        n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, n3d::Split3Out{d_y, nullptr, nullptr});
         kcheck(k);
     });
 }
@@ -502,10 +500,11 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
             op.vt_lo = sc.get(W * vt_ld / 2);
             op.vt_ld = (long long)vt_ld;
             n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, cs, sn, op);
-            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, d_out, nullptr, k.err);
+            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::Split3Out{d_out, nullptr, nullptr},
+                                     k.err);
         } else {
             n3d::launch_pack_qkv(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, qkv);
-            n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out, nullptr);
+            n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out);
         }
         kcheck(k);
     });

@@ -78,8 +78,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tQh, const __grid_constant__ CUtensorMap tQl,
                         const __grid_constant__ CUtensorMap tKh, const __grid_constant__ CUtensorMap tKl,
                         const __grid_constant__ CUtensorMap tVh, const __grid_constant__ CUtensorMap tVl, int S,
-                        const int* __restrict__ valid_arr, int heads, float* __restrict__ ctx_hi,
-                        float* __restrict__ ctx_lo, int* err) {
+                        const int* __restrict__ valid_arr, int heads, Split3Out ctx, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQh = smem;
@@ -288,24 +287,27 @@ __global__ void __launch_bounds__(THREADS, 2)
         red_sum[hf * QT + r] = l;
         pair_sync();
         const float ltot = l + red_sum[(hf ^ 1) * QT + r];
-        // ---- context row, this warp's 32 columns (TF32 pair, or plain fp32 when ctx_lo is null)
+        // ---- context row, this warp's 32 columns (3-term split, or plain fp32 when ctx.hb is null)
         if (q0 + r < S) {
             const float inv = ltot > 0.0f ? 1.0f / ltot : 0.0f;
             const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD + 32 * hf;
-            float* dh = ctx_hi + off;
 #pragma unroll
             for (int d = 0; d < 32; d += 4) {
-                float x[4], lo[4];
+                float x[4];
                 unpack2(o[d / 2], x[0], x[1]);
                 unpack2(o[d / 2 + 1], x[2], x[3]);
 #pragma unroll
                 for (int i = 0; i < 4; i++) x[i] *= inv;
-                if (ctx_lo) {
-#pragma unroll
-                    for (int i = 0; i < 4; i++) split_tf32(x[i], x[i], lo[i]);
-                    *reinterpret_cast<float4*>(ctx_lo + off + d) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                if (ctx.hb) {
+                    float hh[4];
+                    uint2 hb, lb;
+                    split3x4(x, hh, hb, lb);
+                    *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(hh[0], hh[1], hh[2], hh[3]);
+                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.hb) + off + d) = hb;
+                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.lb) + off + d) = lb;
+                } else {
+                    *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(x[0], x[1], x[2], x[3]);
                 }
-                *reinterpret_cast<float4*>(dh + d) = make_float4(x[0], x[1], x[2], x[3]);
             }
         }
     }
@@ -317,7 +319,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 }  // namespace
 
 void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
-                         float* ctx_hi, float* ctx_lo, int* err) {
+                         Split3Out ctx, int* err) {
     if (seqs <= 0 || S <= 0) return;
     if ((seqs > 1 && S % 8) || op.vt_ld % 8)
         throw Error(9, "attention: the sequence stride and the V^T row stride must be multiples of 8");
@@ -334,7 +336,7 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
     const CUtensorMap vh = make_bf16_map(op.vt_hi, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
     const CUtensorMap vl = make_bf16_map(op.vt_lo, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx_hi, ctx_lo, err);
+    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx, err);
     N3D_CUDA(cudaGetLastError());
 }
 

@@ -1,0 +1,809 @@
+// C[M, N] = A[M, K] * B[N, K]^T on the sm_100a tensor cores (tcgen05) with fused
+// epilogues.
+//
+// Replaces the reference's WGSL `gemm` pipeline (src/gpu.rs:1005-1611, wrapper
+// src/gpu.rs:726-744) and the separate `add`, `unary` (GELU/ReLU), `rope` and
+// `col3` dispatches that followed it (src/gpu.rs:1768-1838, 1973-1999): those
+// become epilogue modes of this one kernel.  The reference arithmetic it must
+// agree with is `tensor::linear` (src/tensor.rs:22-57) in fp32.
+//
+// Arithmetic (3-term split): every operand x is stored as hi = RN-TF32(x) (fp32
+// array) and bf16 copies of hi and of lo = x - hi; each k-block issues hi·hi on
+// `kind::tf32` and hb·lb + lb·hb on `kind::f16`, all into one fp32 accumulator.
+// Accuracy matches 3xTF32 within 2x on this model (logit maxdiff 8e-8 vs 5e-8 on
+// config 0, no flips), and two of the three products run at the bf16 rate: under
+// the 1 kW power cap that is 23-38 % more GEMM throughput.
+//
+// k-block = 32: per CTA and stage, A rows as [hi: 128 B | hb: 64 B | lb: 64 B] and
+// the same for B, TMA-loaded with the 128-byte (tf32) and 64-byte (bf16) swizzles.
+// Two kernels:
+//   gemm_kernel<BN>        one CTA per 128 x BN tile, persistent (N = 192 head GEMMs,
+//                          small M, the allocation-free entry point)
+//   gemm_pair_kernel<BN,EW> CTA pairs on 256 x 256 tiles with M = 256
+//                          `cta_group::2` MMAs: each CTA loads its 128 A rows and half
+//                          the B tile, the leader issues, both own 128 accumulator rows
+// Both: warp 0 TMA, warp 1 TMEM owner + MMA issue, epilogue warps 2.. (TMEM lane
+// quadrant = warp % 4); two TMEM accumulators so tile i's epilogue overlaps tile
+// i + 1's main loop.  Every wait is bounded; an expired wait records its site.
+
+#include <cuda_bf16.h>
+
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "n3d_device.cuh"
+#include "n3d_internal.h"
+
+namespace n3d {
+
+namespace {
+
+constexpr int BM = 128;                 // rows per CTA
+constexpr int BK = 32;                  // k-block
+constexpr int ROW_T = BK * 4;           // bytes per row of the tf32 part (128: SW128)
+constexpr int ROW_H = BK * 2;           // bytes per row of a bf16 part (64: SW64)
+constexpr int ROW_3 = ROW_T + 2 * ROW_H;  // all three parts of one row
+
+__device__ __forceinline__ float gelu_erf(float x) {
+    // 0.5 * x * (1 + erf(x / sqrt(2))), the exact form of src/tensor.rs:113-120
+    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+// Store 32 consecutive fp32 values of one output row.
+__device__ __forceinline__ void store_row32(float* dst, const float* v, int ncols_left) {
+    if (ncols_left >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (i < ncols_left) dst[i] = v[i];
+    }
+}
+// 32 bf16 of one row (16 packed words).
+__device__ __forceinline__ void store_row32_bf16(uint16_t* dst, const uint32_t* w, int ncols_left) {
+    if (ncols_left >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(w[i], w[i + 1], w[i + 2], w[i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            if (i < ncols_left) dst[i] = (uint16_t)(w[i / 2] >> (16 * (i & 1)));
+    }
+}
+
+// Epilogue value of accumulator column i: bias, activation.
+__device__ __forceinline__ float epi_value(int mode, float acc, float bias) {
+    float x = __fadd_rn(acc, bias);
+    if (mode == EPI_GELU_SPLIT) x = gelu_erf(x);
+    if (mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
+    return x;
+}
+
+// 32 bias values for columns col0.. (zeros past N or without bias).
+__device__ __forceinline__ void load_bias32(const float* bias, int col0, int N, float* b) {
+    if (bias != nullptr && col0 + 32 <= N) {
+#pragma unroll
+        for (int i4 = 0; i4 < 8; i4++) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(bias + col0) + i4);
+            b[4 * i4] = b4.x;
+            b[4 * i4 + 1] = b4.y;
+            b[4 * i4 + 2] = b4.z;
+            b[4 * i4 + 3] = b4.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) b[i] = (bias != nullptr && col0 + i < N) ? bias[col0 + i] : 0.0f;
+    }
+}
+
+// ------------------------------------------------------ direct-store epilogue
+// For the modes with a row remap (head proj into its padded layout), the fused
+// dense + out_proj, and plain stores without a tensor map.  Tile rows
+// r = m0 + 32 q + lane.
+// `w2s` (EPI_DENSE_OUT): w2 [n2, N] and the dense bias [N] staged in shared memory.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
+                                              int lane, const float* w2s = nullptr) {
+    const int r = m0 + q * 32 + lane;
+    const bool row_ok = r < M;
+    const int qq = r / epi.rdiv, t = r - qq * epi.rdiv;
+    const bool keep = row_ok && t < epi.rkeep;
+    const long long orow = (long long)qq * epi.rmul + t + epi.roff;
+    const bool zero_row = epi.seq_len != nullptr && keep && t >= epi.seq_len[qq];
+    if (epi.mode == EPI_DENSE_OUT) {
+        // relu(dense) then the out projection, sequential over the hidden
+        // index with separate multiply and add (src/tensor.rs:33-43)
+        float acc[8];
+#pragma unroll
+        for (int o = 0; o < 8; o++) acc[o] = 0.0f;
+        const float* bs = w2s + 8 * N;  // N = 192 = BN: one column tile
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tl + c, v);
+            if (!keep) continue;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const int col = n0 + c + i;
+                const float rr = fmaxf(__fadd_rn(v[i], bs[col]), 0.0f);
+#pragma unroll
+                for (int o = 0; o < 8; o++) acc[o] = __fadd_rn(acc[o], __fmul_rn(rr, w2s[o * N + col]));
+            }
+        }
+        if (keep)
+            for (int o = 0; o < epi.n2; o++) epi.out[orow * epi.ldo + o] = __fadd_rn(acc[o], epi.b2[o]);
+        return;
+    }
+    for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tl + c, v);
+        const int col0 = n0 + c;
+        if (!keep || col0 >= N) continue;
+        float bias[32];
+        load_bias32(epi.bias, col0, N, bias);
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = zero_row ? 0.0f : epi_value(epi.mode, v[i], bias[i]);
+        const int left = N - col0;
+        float* dst = epi.out + orow * epi.ldo + col0;
+        if (epi.mode == EPI_STORE) {
+            store_row32(dst, v, left);
+        } else {  // 3-term split of the output
+            uint32_t hb[16], lb[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) split3x2(v[2 * i], v[2 * i + 1], v[2 * i], v[2 * i + 1], hb[i], lb[i]);
+            store_row32(dst, v, left);
+            store_row32_bf16(static_cast<uint16_t*>(epi.out2) + orow * epi.ldo + col0, hb, left);
+            store_row32_bf16(static_cast<uint16_t*>(epi.out3) + orow * epi.ldo + col0, lb, left);
+        }
+    }
+}
+
+// ------------------------------------------------------- TMA-store epilogue
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+                 "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One warp's 32 x 32 fp32 block into a 4 KB 128-byte-swizzled staging box: lane = box row.
+__device__ __forceinline__ void stage_rows(uint8_t* box, int lane, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        *reinterpret_cast<float4*>(box + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+// 32 x 32 bf16 (16 packed words per lane) into a 2 KB 64-byte-swizzled box.
+__device__ __forceinline__ void stage_rows_bf16(uint8_t* box, int lane, const uint32_t* w) {
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        *reinterpret_cast<uint4*>(box + lane * 64 + ((i ^ ((lane >> 1) & 3)) << 4)) =
+            make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+}
+// The warp's previous boxes must have been read before they are overwritten.
+__device__ __forceinline__ void stage_begin(int lane) {
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
+}
+// Make the staged boxes visible to the TMA unit and store them (up to three maps).
+__device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, const void* b0, const CUtensorMap* m1,
+                                            const void* b1, const CUtensorMap* m2, const void* b2, int x, int y) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(m0, b0, x, y);
+        if (m1) tma_store_2d(m1, b1, x, y);
+        if (m2) tma_store_2d(m2, b2, x, y);
+        bulk_commit();
+    }
+}
+
+// Epilogue with TMA stores, for modes whose output rows are the tile's rows:
+// EPI_STORE, EPI_SPLIT, EPI_GELU_SPLIT, EPI_RELU_SPLIT, EPI_QKV_ATTN, over accumulator
+// columns [c_begin, c_end).  `stg` is this warp's 8 KB staging area.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
+                                                  int lane, uint8_t* stg, int c_begin = 0, int c_end = BN) {
+    const int rowbase = m0 + q * 32;
+    if (rowbase >= M) return;  // whole warp past the end: nothing to load or store
+    const int r = rowbase + lane;
+    if (epi.mode == EPI_QKV_ATTN) {
+        uint8_t* bhi = stg;
+        uint8_t* blo = stg + 4096;
+        for (int c = c_begin; c < c_end; c += 64) {
+            float v[64];
+            tmem_ld32(tl + c, v);
+            tmem_ld32(tl + c + 32, v + 32);
+            const int col0 = n0 + c;
+            if (col0 >= N) break;
+            const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
+            if (sec < 2) {
+                // rotate-half RoPE (src/encoder.rs:281-296); the tables repeat their first
+                // half (cat(freqs, freqs)), so one float4 of cos and of sin serves four pairs
+                const int pos = r % epi.rope_seq;
+                const float4* cs = reinterpret_cast<const float4*>(epi.cos_t + (long long)pos * epi.head_dim);
+                const float4* sn = reinterpret_cast<const float4*>(epi.sin_t + (long long)pos * epi.head_dim);
+#pragma unroll
+                for (int i4 = 0; i4 < 8; i4++) {
+                    const float4 c4 = __ldg(cs + i4), s4 = __ldg(sn + i4);
+                    const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const int i = 4 * i4 + j;
+                        const float x1 = v[i], x2 = v[32 + i];
+                        v[i] = __fsub_rn(__fmul_rn(x1, cc[j]), __fmul_rn(x2, ss[j]));
+                        v[32 + i] = __fadd_rn(__fmul_rn(x2, cc[j]), __fmul_rn(x1, ss[j]));
+                    }
+                }
+            }
+            // bf16 pairs: Q / K rows (64 values = one 128-byte swizzled box row), V
+            // transposed (box row = d, 32 rows of the tile = 64 bytes, unswizzled)
+            uint32_t hi[32], lo[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) split_bf16x2(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
+            stage_begin(lane);
+            if (sec < 2) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
+                    *reinterpret_cast<uint4*>(bhi + o) = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
+                    *reinterpret_cast<uint4*>(blo + o) = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
+                }
+                stage_issue(lane, sec == 0 ? &epi.map_out : &epi.map_k_hi, bhi,
+                            sec == 0 ? &epi.map_out2 : &epi.map_k_lo, blo, nullptr, nullptr, hcol, rowbase);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    *reinterpret_cast<uint16_t*>(bhi + (2 * i) * 64 + lane * 2) = (uint16_t)(hi[i] & 0xffffu);
+                    *reinterpret_cast<uint16_t*>(bhi + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(hi[i] >> 16);
+                    *reinterpret_cast<uint16_t*>(blo + (2 * i) * 64 + lane * 2) = (uint16_t)(lo[i] & 0xffffu);
+                    *reinterpret_cast<uint16_t*>(blo + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(lo[i] >> 16);
+                }
+                stage_issue(lane, &epi.map_vt_hi, bhi, &epi.map_vt_lo, blo, nullptr, nullptr, rowbase, hcol);
+            }
+        }
+        return;
+    }
+    const bool split = epi.mode != EPI_STORE;
+    uint8_t* bhi = stg;          // 4 KB fp32 box
+    uint8_t* bhb = stg + 4096;   // 2 KB bf16 box
+    uint8_t* blb = stg + 6144;   // 2 KB bf16 box
+    for (int c = c_begin; c < c_end; c += 32) {
+        float v[32];
+        tmem_ld32(tl + c, v);
+        const int col0 = n0 + c;
+        if (col0 >= N) break;
+        float bias[32];
+        load_bias32(epi.bias, col0, N, bias);
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = epi_value(epi.mode, v[i], bias[i]);
+        uint32_t hb[16], lb[16];
+        if (split) {
+#pragma unroll
+            for (int i = 0; i < 16; i++) split3x2(v[2 * i], v[2 * i + 1], v[2 * i], v[2 * i + 1], hb[i], lb[i]);
+        }
+        stage_begin(lane);
+        stage_rows(bhi, lane, v);
+        if (split) {
+            stage_rows_bf16(bhb, lane, hb);
+            stage_rows_bf16(blb, lane, lb);
+        }
+        stage_issue(lane, &epi.map_out, bhi, split ? &epi.map_out2 : nullptr, bhb, split ? &epi.map_out3 : nullptr,
+                    blb, col0, rowbase);
+    }
+}
+
+// ------------------------------------------------------------- main loops
+// Shared-memory stage of one CTA: [A: hi | hb | lb][B: hi | hb | lb] with `ra` and
+// `rb` rows.  MMAs of one k-block into accumulator `d`.
+template <bool PAIR>
+__device__ __forceinline__ void mma_kblock(uint32_t d, uint32_t st, int ra, int rb, uint32_t idt, uint32_t idb,
+                                           bool first) {
+    const uint32_t ah = st, ahb = ah + ra * ROW_T, alb = ahb + ra * ROW_H;
+    const uint32_t bh = alb + ra * ROW_H, bhb = bh + rb * ROW_T, blb = bhb + rb * ROW_H;
+#pragma unroll
+    for (int k = 0; k < BK / 8; k++) {  // hi·hi: 8 tf32 = 32 bytes along the 128-byte rows
+        const uint64_t a = desc_k_sw128(ah + 32 * k), b = desc_k_sw128(bh + 32 * k);
+        if (PAIR)
+            umma_tf32_pair(d, a, b, idt, !(first && k == 0));
+        else
+            umma_tf32(d, a, b, idt, !(first && k == 0));
+    }
+#pragma unroll
+    for (int k = 0; k < BK / 16; k++) {  // hb·lb + lb·hb: 16 bf16 = 32 bytes along the 64-byte rows
+        const uint64_t a1 = desc_k_sw64(ahb + 32 * k), b1 = desc_k_sw64(blb + 32 * k);
+        const uint64_t a2 = desc_k_sw64(alb + 32 * k), b2 = desc_k_sw64(bhb + 32 * k);
+        if (PAIR) {
+            umma_bf16_pair(d, a1, b1, idb, 1);
+            umma_bf16_pair(d, a2, b2, idb, 1);
+        } else {
+            umma_bf16(d, a1, b1, idb, 1);
+            umma_bf16(d, a2, b2, idb, 1);
+        }
+    }
+}
+
+// TMA loads of one stage: rows [ya, ya + ra) of A at column xa and [yb, yb + rb) of B
+// at column xb, completion on `bar` (pair: the leader's barrier, `bar_cluster`).
+template <bool PAIR>
+__device__ __forceinline__ void load_stage(uint8_t* st, int ra, int rb, const CUtensorMap* m, uint64_t* bar,
+                                           uint32_t bar_cluster, int xa, int ya, int xb, int yb) {
+    uint8_t* p[6] = {st, st + ra * ROW_T, st + ra * (ROW_T + ROW_H), st + ra * ROW_3, st + ra * ROW_3 + rb * ROW_T,
+                     st + ra * ROW_3 + rb * (ROW_T + ROW_H)};
+#pragma unroll
+    for (int i = 0; i < 6; i++) {
+        const int x = i < 3 ? xa : xb, y = i < 3 ? ya : yb;
+        if (PAIR)
+            tma_load_2d_pair(p[i], &m[i], bar_cluster, x, y);
+        else
+            tma_load_2d(p[i], &m[i], bar, x, y);
+    }
+}
+
+struct Maps6 {
+    CUtensorMap m[6];  // A hi, hb, lb; B hi, hb, lb
+};
+
+// ------------------------------------------------------------ one-CTA kernel
+template <int BN>
+struct GemmCfg {
+    static constexpr int STAGE_BYTES = (BM + BN) * ROW_3;
+    static constexpr int STAGING = 4 * 8192;
+    static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static constexpr int ACC_COLS = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
+    static_assert(STAGES >= 2, "need two pipeline stages");
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
+                const __grid_constant__ Epi epi, int* err) {
+    using Cfg = GemmCfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_n = (N + BN - 1) / BN;
+    const int tiles = ((M + BM - 1) / BM) * tiles_n;
+    const int nkb = K / BK;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < Cfg::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_fence_init();
+        for (int i = 0; i < 6; i++) tma_prefetch_desc(&maps.m[i]);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (g >= (uint32_t)Cfg::STAGES &&
+                        !mbar_wait(&empty[s], ((g / Cfg::STAGES) - 1) & 1, err, DEV_TIMEOUT_TMA_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
+                    const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * BK : kb * BK;
+                    load_stage<false>(smem + s * Cfg::STAGE_BYTES, BM, BN, maps.m, &full[s], 0, ka, m0 + tap, kb * BK,
+                                      n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idt = idesc_tf32(BN), idb = idesc_bf16(BN);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, it++) {
+                const int buf = it & 1;
+                if (it >= 2 && !mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * Cfg::ACC_COLS;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (!mbar_wait(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    mma_kblock<false>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN, idt, idb, kb == 0);
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        float* w2s = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024);
+        if (epi.mode == EPI_DENSE_OUT) {
+            // the out_proj weights [8, N] (rows past n2 zero) and the dense bias [N], once
+            // per CTA into the staging area, which direct-store epilogues do not use
+            for (int i = threadIdx.x - 64; i < 9 * N; i += 128)
+                w2s[i] = i < 8 * N ? (i / N < epi.n2 ? epi.w2[i] : 0.0f) : epi.bias[i - 8 * N];
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+        }
+        int it = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
+            const int buf = it & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS;
+            if (epi.tma)
+                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+            else
+                epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane, w2s);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+// ------------------------------------------------------------ CTA-pair kernel
+// A cluster of two CTAs walks 256 x BN output tiles.  CTA r of the pair loads A rows
+// m0 + 128 r and B rows n0 + r BN / 2, so each SM streams half the B tile of the
+// one-CTA kernel for the same work; its TMEM receives output rows m0 + 128 r, which
+// its own epilogue warps store.  Barriers: full[s] lives in the leader (both CTAs'
+// loads complete on it), empty[s] and acc_full[b] in both (arrived by the leader's
+// multicast commits), acc_empty[b] in the leader (2 EW epilogue warps).  With EW = 8,
+// warps w and w + 4 share TMEM lane quadrant w % 4 and take half the columns each.
+template <int BN, int EW>
+struct PairCfg {
+    static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_3;
+    static constexpr int STAGING = EW * 8192;
+    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
+    static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
+    static_assert(STAGES >= 2, "need two pipeline stages");
+};
+
+template <int BN, int EW>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
+    gemm_pair_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
+                     const __grid_constant__ Epi epi, int* err) {
+    using Cfg = PairCfg<BN, EW>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* acc_full = empty + Cfg::STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = static_cast<int>(cluster_rank());
+    const bool leader = rank == 0;
+    const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
+    const int tiles_n = (N + BN - 1) / BN;
+    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * tiles_n;
+    const int nkb = K / BK;
+
+    if (warp == 0 && lane == 0) {
+        for (int s = 0; s < Cfg::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * EW);
+        }
+        mbar_fence_init();
+        for (int i = 0; i < 6; i++) tma_prefetch_desc(&maps.m[i]);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = cid; ok && t < tiles; t += ncl) {
+                const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN + rank * (BN / 2);
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (g >= (uint32_t)Cfg::STAGES &&
+                        !mbar_wait_cluster(&empty[s], ((g / Cfg::STAGES) - 1) & 1, err, DEV_TIMEOUT_TMA_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
+                    const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * BK : kb * BK;
+                    load_stage<true>(smem + s * Cfg::STAGE_BYTES, BM, BN / 2, maps.m, nullptr,
+                                     leader_addr(&full[s]), ka, m0 + tap, kb * BK, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idt = idesc_tf32_pair(BN), idb = idesc_bf16_pair(BN);
+            uint32_t g = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = cid; ok && t < tiles; t += ncl, it++) {
+                const int buf = it & 1;
+                if (it >= 2 && !mbar_wait_cluster(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * BN;
+                for (int kb = 0; kb < nkb; kb++, g++) {
+                    const int s = g % Cfg::STAGES;
+                    if (!mbar_wait_cluster(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    mma_kblock<true>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN / 2, idt, idb, kb == 0);
+                    umma_commit_pair(&empty[s]);
+                }
+                if (ok) umma_commit_pair(&acc_full[buf]);
+            }
+        }
+    } else {
+        const int q = warp & 3, part = (warp - 2) >> 2;
+        constexpr int CW = BN / (EW / 4);  // columns per epilogue warp
+        const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
+        int it = 0;
+        for (int t = cid; t < tiles; t += ncl, it++) {
+            const int buf = it & 1;
+            const bool ok =
+                __all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
+            if (!ok) break;
+            tc_fence_after();
+            const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN;
+            const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+            if (epi.tma)
+                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, part * CW,
+                                      part * CW + CW);
+            else if (part == 0)  // direct stores: one warp per quadrant takes the whole tile
+                epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8u * buf);
+        }
+        if (lane == 0) bulk_wait0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the peer's TMEM reads and remote arrives are done
+    if (warp == 1) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+}
+
+// ------------------------------------------------------------ tensor maps
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) throw Error(9 /*N3D_ERR_GPU*/, "cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+// 2-D map over a row-major matrix [rows, cols] of `esize`-byte elements (row stride ld
+// elements), box = box_cols x box_rows, swizzle = box_cols * esize bytes (32, 64, 128)
+// or none, zero fill out of bounds.
+CUtensorMap encode_map(const void* ptr, int esize, long long rows, long long cols, long long ld, int box_cols,
+                       int box_rows, bool swizzle) {
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * esize) % 16)
+        throw Error(9, "GEMM operand or output is not 16-byte aligned");
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estr[2] = {1, 1};
+    const int span = box_cols * esize;
+    const CUtensorMapSwizzle sw = !swizzle      ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                  : span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                  : span == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_32B;
+    CUresult r = encode_fn()(&m, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+    return m;
+}
+
+CUtensorMap cached_map(const void* ptr, int esize, long long rows, long long cols, long long ld, int box_cols,
+                       int box_rows, bool swizzle) {
+    using Key = std::tuple<const void*, int, long long, long long, long long, int, int, bool>;
+    static std::map<Key, CUtensorMap> cache;
+    static std::mutex mu;
+    const Key key{ptr, esize, rows, cols, ld, box_cols, box_rows, swizzle};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    const CUtensorMap m = encode_map(ptr, esize, rows, cols, ld, box_cols, box_rows, swizzle);
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, m);
+    return m;
+}
+
+// The six operand maps: A with box rows ra, B with box rows rb, BK columns each.
+Maps6 operand_maps(const SplitOperand& A, const SplitOperand& B, int ra, int rb, bool cache) {
+    auto mk = cache ? cached_map : encode_map;
+    Maps6 m;
+    const SplitOperand* ops[2] = {&A, &B};
+    for (int i = 0; i < 2; i++) {
+        const SplitOperand& o = *ops[i];
+        const int rows = i == 0 ? ra : rb;
+        m.m[3 * i] = mk(o.hi, 4, o.rows, o.cols, o.ld, BK, rows, true);
+        m.m[3 * i + 1] = mk(o.hb, 2, o.rows, o.cols, o.ld, BK, rows, true);
+        m.m[3 * i + 2] = mk(o.lb, 2, o.rows, o.cols, o.ld, BK, rows, true);
+    }
+    return m;
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        N3D_CUDA(cudaGetDevice(&dev));
+        N3D_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    }
+    return n;
+}
+
+template <int BN>
+void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err) {
+    using Cfg = GemmCfg<BN>;
+    static bool attr = false;
+    if (!attr) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        attr = true;
+    }
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    gemm_kernel<BN><<<grid, 192, Cfg::SMEM, s>>>(maps, M, N, K, kb_per_tap, epi, err);
+    N3D_CUDA(cudaGetLastError());
+}
+
+template <int BN, int EW>
+void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                 const Epi& epi, int* err) {
+    using Cfg = PairCfg<BN, EW>;
+    static int max_clusters = 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = s;
+    if (!max_clusters) {
+        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM));
+        cfg.gridDim = dim3(2 * (sm_count() / 2));
+        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN, EW>, &cfg));
+        if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
+    }
+    const Maps6 maps = operand_maps(A, B, BM, BN / 2, true);
+    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
+    cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EW>, maps, M, N, K, kb_per_tap, epi, err));
+}
+
+void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi& epi, int bn) {
+    if (K % BK) throw Error(13, "GEMM K must be a multiple of 32");
+    if (!A.hi || !A.hb || !A.lb || !B.hi || !B.hb || !B.lb) throw Error(13, "GEMM operand without all three parts");
+    if (epi.mode == EPI_DENSE_OUT && (bn != 192 || epi.n2 > 8 || epi.tma))
+        throw Error(9, "the fused dense+out_proj epilogue needs N == 192, at most 8 outputs and direct stores");
+    if (epi.mode == EPI_QKV_ATTN && (bn % 64 || !epi.tma))
+        throw Error(9, "the attention-operand epilogue needs 64-column chunks and TMA stores");
+}
+
+}  // namespace
+
+CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld) {
+    return cached_map(p, 4, rows, cols, ld, 32, 32, true);
+}
+
+CUtensorMap make_store_map_bf16(const void* p, long long rows, long long cols, long long ld) {
+    return cached_map(p, 2, rows, cols, ld, 32, 32, true);
+}
+
+CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
+                          bool swizzle) {
+    if (swizzle && box_cols != 64) throw Error(9, "bf16 map: the 128-byte swizzle needs 64-column boxes");
+    return cached_map(p, 2, rows, cols, ld, box_cols, box_rows, swizzle);
+}
+
+void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                 const Epi& epi, int* err) {
+    if (M <= 0 || N <= 0) return;
+    int bn;
+    if (epi.mode == EPI_DENSE_OUT || N == 192) {
+        bn = 192;
+    } else if (N % 256 == 0 && M >= 4096) {
+        bn = 512;  // 256 x 256 tiles on CTA pairs
+    } else if (N % 128 == 0 || N > 64) {
+        bn = 128;
+    } else {
+        bn = 64;
+    }
+    check_shape(A, B, K, epi, bn == 512 ? 256 : bn);
+    switch (bn) {
+        case 64: launch_one<64>(s, operand_maps(A, B, BM, 64, true), M, N, K, kb_per_tap, epi, err); break;
+        case 128: launch_one<128>(s, operand_maps(A, B, BM, 128, true), M, N, K, kb_per_tap, epi, err); break;
+        case 192: launch_one<192>(s, operand_maps(A, B, BM, 192, true), M, N, K, kb_per_tap, epi, err); break;
+        default:
+            // the erf-GELU + split epilogue is latency bound on one warp per sub-partition:
+            // 8 epilogue warps; the lighter epilogues lose more to the smaller pipeline
+            if (epi.tma && epi.mode == EPI_GELU_SPLIT)
+                launch_pair<256, 8>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            else
+                launch_pair<256, 4>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            break;
+    }
+}
+
+// Same kernel (128-column tiles) with tensor maps encoded on the stack: no map cache,
+// so nothing is allocated on the host heap either (the allocation-free entry point).
+void gemm_split3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                            const Epi& epi, int* err) {
+    if (M <= 0 || N <= 0) return;
+    check_shape(A, B, K, epi, 128);
+    launch_one<128>(s, operand_maps(A, B, BM, 128, false), M, N, K, 0, epi, err);
+}
+
+}  // namespace n3d

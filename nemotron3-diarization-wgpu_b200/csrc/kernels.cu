@@ -22,13 +22,13 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ---------------------------------------------------------------- LayerNorm
 // torch LayerNorm, eps 1e-5, two-pass population variance (src/tensor.rs:97-110).
 // One warp per row, VPL values per lane held in registers (128-bit loads).
-// Writes either a plain fp32 row (out_lo == nullptr) or a TF32 hi/lo pair.
+// Writes either a plain fp32 row (out.hb == nullptr) or the row's 3-term split.
 // x_out may alias x (in-place residual add): each lane reads its elements of x before
 // writing them, so neither is __restrict__.
 template <int VPL>
 __global__ void layer_norm_kernel(const float* x, long long rows, const float* __restrict__ w,
-                                  const float* __restrict__ b, float* __restrict__ out, float* __restrict__ out_lo,
-                                  const float* __restrict__ delta = nullptr, float* x_out = nullptr) {
+                                  const float* __restrict__ b, Split3Out out, const float* __restrict__ delta = nullptr,
+                                  float* x_out = nullptr) {
     constexpr int COLS = VPL * 32;
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -68,19 +68,26 @@ __global__ void layer_norm_kernel(const float* x, long long rows, const float* _
     }
     const float var = __fdiv_rn(warp_sum(q), (float)COLS);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-    float* dst = out + row * COLS;
-    float* dlo = out_lo ? out_lo + row * COLS : nullptr;
+    float* dst = out.hi + row * COLS;
+    uint16_t* dhb = out.hb ? static_cast<uint16_t*>(out.hb) + row * COLS : nullptr;
+    uint16_t* dlb = out.hb ? static_cast<uint16_t*>(out.lb) + row * COLS : nullptr;
 #pragma unroll
     for (int i = 0; i < VPL; i += 4) {
         const int c = (i / 4) * 128 + lane * 4;
-        float y[4], lo[4];
+        float y[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
+        for (int j = 0; j < 4; j++)
             y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i + j], mean), inv), w[c + j]), b[c + j]);
-            if (dlo) split_tf32(y[j], y[j], lo[j]);
+        if (dhb) {
+            float h[4];
+            uint2 hb, lb;
+            split3x4(y, h, hb, lb);
+            *reinterpret_cast<float4*>(dst + c) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint2*>(dhb + c) = hb;
+            *reinterpret_cast<uint2*>(dlb + c) = lb;
+        } else {
+            *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
         }
-        *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
-        if (dlo) *reinterpret_cast<float4*>(dlo + c) = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -89,11 +96,11 @@ __global__ void layer_norm_kernel(const float* x, long long rows, const float* _
 // (src/encoder.rs:302-329): scores q.k * hd^-1/2, online softmax over key tiles
 // of 32 staged in shared memory, one query row per thread.  qkv is
 // [seqs * seq_stride, 3 * heads * HD] = Q | K | V (Q and K already rotated);
-// ctx is written as a TF32 hi/lo pair [seqs * seq_stride, heads * HD].
+// ctx is written in fp32 [seqs * seq_stride, heads * HD].
 template <int HD>
 __global__ void __launch_bounds__(128) attention_kernel(const float* __restrict__ qkv, int seq_stride,
                                                         const int* __restrict__ valid_arr, int heads,
-                                                        float* __restrict__ ctx_hi, float* __restrict__ ctx_lo) {
+                                                        float* __restrict__ ctx) {
     constexpr int KT = 32;
     __shared__ __align__(16) float ks[KT][HD];
     __shared__ __align__(16) float vs[KT][HD];
@@ -163,23 +170,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const float* __restrict_
     }
     if (!active) return;
     const float inv = valid > 0 ? 1.0f / l : 0.0f;
-    float* dh = ctx_hi + (base + t) * (heads * HD) + h * HD;
-    if (ctx_lo == nullptr) {
+    float* dh = ctx + (base + t) * (heads * HD) + h * HD;
 #pragma unroll
-        for (int d = 0; d < HD; d += 4)
-            *reinterpret_cast<float4*>(dh + d) =
-                make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
-        return;
-    }
-    float* dl = ctx_lo + (base + t) * (heads * HD) + h * HD;
-#pragma unroll
-    for (int d = 0; d < HD; d += 4) {
-        float hi[4], lo[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) split_tf32(o[d + j] * inv, hi[j], lo[j]);
-        *reinterpret_cast<float4*>(dh + d) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<float4*>(dl + d) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-    }
+    for (int d = 0; d < HD; d += 4)
+        *reinterpret_cast<float4*>(dh + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
 }
 
 // ------------------------------------------------------------------- log-mel
@@ -195,8 +189,7 @@ __global__ void __launch_bounds__(256) mel_kernel(const float* __restrict__ audi
                                                   const int* __restrict__ f_meta, const float* __restrict__ window,
                                                   const float* __restrict__ twiddle, const float* __restrict__ filters,
                                                   const int* __restrict__ filt_lo, const int* __restrict__ filt_hi,
-                                                  float preemph, float* __restrict__ mel_hi,
-                                                  float* __restrict__ mel_lo, float* __restrict__ mel_plain,
+                                                  float preemph, Split3Out mel, float* __restrict__ mel_plain,
                                                   const long long* __restrict__ f_out) {
     __shared__ float re[NFFT], im[NFFT], pw[NBINS];
     const long long f = blockIdx.x;
@@ -238,18 +231,30 @@ __global__ void __launch_bounds__(256) mel_kernel(const float* __restrict__ audi
         for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(filters[m * NBINS + k], pw[k]));
         const float v = (float)log((double)__fadd_rn(acc, 5.9604645e-8f));
         const long long o = f_out[f] * 128 + m;
-        float hi, lo;
-        split_tf32(v, hi, lo);
-        mel_hi[o] = hi;
-        mel_lo[o] = lo;
+        if (mel.hi) {
+            float h;
+            uint16_t hb, lb;
+            split3x1(v, h, hb, lb);
+            mel.hi[o] = h;
+            static_cast<uint16_t*>(mel.hb)[o] = hb;
+            static_cast<uint16_t*>(mel.lb)[o] = lb;
+        }
         if (mel_plain) mel_plain[o] = v;
     }
 }
 
-__global__ void split_kernel(const float* __restrict__ x, long long n, float* __restrict__ hi,
-                             float* __restrict__ lo) {
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        split_tf32(x[i], hi[i], lo[i]);
+// Four elements per thread (n % 4 == 0, 16-byte aligned arrays).
+__global__ void split_kernel(const float* __restrict__ x, long long n4, Split3Out out) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 t = reinterpret_cast<const float4*>(x)[i];
+        const float y[4] = {t.x, t.y, t.z, t.w};
+        float h[4];
+        uint2 hb, lb;
+        split3x4(y, h, hb, lb);
+        reinterpret_cast<float4*>(out.hi)[i] = make_float4(h[0], h[1], h[2], h[3]);
+        reinterpret_cast<uint2*>(out.hb)[i] = hb;
+        reinterpret_cast<uint2*>(out.lb)[i] = lb;
+    }
 }
 
 // Packs q | k | v per row; RoPE as src/encoder.rs:281-296 with explicit rounding.
@@ -333,10 +338,12 @@ void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const floa
     N3D_CUDA(cudaGetLastError());
 }
 
-void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo) {
+void launch_split(cudaStream_t s, const float* x, long long n, Split3Out out) {
     if (n <= 0) return;
-    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
-    split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n, hi, lo);
+    if (n % 4) throw Error(13, "split: the element count must be a multiple of 4");
+    const long long n4 = n / 4;
+    const long long blocks = std::min<long long>((n4 + 255) / 256, 148LL * 16);
+    split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n4, out);
     N3D_CUDA(cudaGetLastError());
 }
 
@@ -350,37 +357,37 @@ void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float
 }
 
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
-                       float* out, float* out_lo) {
+                       Split3Out out) {
     if (rows <= 0) return;
     const int warps = 8;
     const unsigned grid = (unsigned)((rows + warps - 1) / warps);
     if (cols == 512)
-        layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo);
+        layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out);
     else if (cols == 1024)
-        layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo);
+        layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
     N3D_CUDA(cudaGetLastError());
 }
 
 void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
-                           const float* b, float* out, float* out_lo) {
+                           const float* b, Split3Out out) {
     if (rows <= 0) return;
     if (cols != 512) throw Error(13, "add_layer_norm supports 512 columns");
     const int warps = 8;
     const unsigned grid = (unsigned)((rows + warps - 1) / warps);
-    layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, out_lo, delta, x);
+    layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, delta, x);
     N3D_CUDA(cudaGetLastError());
 }
 
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
-                      int head_dim, float* ctx_hi, float* ctx_lo) {
+                      int head_dim, float* ctx) {
     if (seqs <= 0 || seq_stride <= 0) return;
     dim3 grid((seq_stride + 127) / 128, heads, seqs);
     if (head_dim == 64)
-        attention_kernel<64><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx_hi, ctx_lo);
+        attention_kernel<64><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx);
     else if (head_dim == 128)
-        attention_kernel<128><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx_hi, ctx_lo);
+        attention_kernel<128><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx);
     else
         throw Error(13, "attention supports head_dim 64 or 128");
     N3D_CUDA(cudaGetLastError());
@@ -388,11 +395,10 @@ void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride
 
 void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
                 const float* window, const float* twiddle, const float* filters, const int* filt_lo,
-                const int* filt_hi, float preemph, float* mel_hi, float* mel_lo, float* mel_plain,
-                const long long* f_out) {
+                const int* filt_hi, float preemph, Split3Out mel, float* mel_plain, const long long* f_out) {
     if (n_frames <= 0) return;
     mel_kernel<<<(unsigned)n_frames, 256, 0, s>>>(audio, f_base, f_meta, window, twiddle, filters, filt_lo, filt_hi,
-                                                  preemph, mel_hi, mel_lo, mel_plain, f_out);
+                                                  preemph, mel, mel_plain, f_out);
     N3D_CUDA(cudaGetLastError());
 }
 

@@ -20,10 +20,6 @@
 
 namespace n3d {
 
-void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
-void gemm_tf32x3_bn(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
-                    int kb_per_tap, const Epi& epi, int* err, int bn);
-
 void cuda_check(cudaError_t e, const char* what) {
     if (e != cudaSuccess) throw Error(10 /*N3D_ERR_CUDA*/, std::string(what) + ": " + cudaGetErrorString(e));
 }
@@ -49,6 +45,15 @@ const json::Value& need(const json::Value& v, const char* key, const std::string
 }
 int need_int(const json::Value& v, const char* key, const std::string& f) { return (int)need(v, key, f).num; }
 double need_num(const json::Value& v, const char* key, const std::string& f) { return need(v, key, f).num; }
+
+// Round to the nearest bfloat16, ties to even: the host twin of cvt.rn.bf16.f32
+// (finite inputs).
+uint16_t bf16_rn_host(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
 
 // Round to the nearest TF32 (11 significant bits), ties away from zero: the
 // host twin of cvt.rna.tf32.f32.
@@ -419,15 +424,26 @@ void Model::upload_weights(const std::string& dir) {
         for (long long x : shape) n *= x;
         return dev(std::vector<float>(d, d + n));
     };
+    auto dev16 = [&](const std::vector<uint16_t>& v) {
+        void* p = nullptr;
+        N3D_CUDA(cudaMalloc(&p, v.size() * 2 + 16));
+        N3D_CUDA(cudaMemcpy(p, v.data(), v.size() * 2, cudaMemcpyHostToDevice));
+        owned_.push_back(p);
+        return p;
+    };
+    // weights in the 3-term split: hi = RN-TF32(w), hb = bf16(hi), lb = bf16(w - hi)
     auto split = [&](const std::vector<float>& w, int out, int in, const float* bias) {
-        std::vector<float> hi(w.size()), lo(w.size());
+        std::vector<float> hi(w.size());
+        std::vector<uint16_t> hb(w.size()), lb(w.size());
         for (size_t i = 0; i < w.size(); i++) {
             hi[i] = tf32_rna_host(w[i]);
-            lo[i] = tf32_rna_host(w[i] - hi[i]);
+            hb[i] = bf16_rn_host(hi[i]);
+            lb[i] = bf16_rn_host(w[i] - hi[i]);
         }
         DevLinear L;
         L.hi = dev(hi);
-        L.lo = dev(lo);
+        L.hb = dev16(hb);
+        L.lb = dev16(lb);
         L.out = out;
         L.in = in;
         if (bias) L.bias = dev(std::vector<float>(bias, bias + out));
@@ -550,6 +566,18 @@ void* Model::ws(const char* name, size_t bytes) {
     return b.p;
 }
 
+Split3Buf Model::ws3(const std::string& base, long long rows, long long cols) {
+    Split3Buf b;
+    b.hi = (float*)ws((base + "_hi").c_str(), (size_t)rows * cols * 4);
+    b.hb = ws((base + "_hb").c_str(), (size_t)rows * cols * 2);
+    b.lb = ws((base + "_lb").c_str(), (size_t)rows * cols * 2);
+    b.cols = cols;
+    b.rows_cap = std::min({(long long)(ws_[base + "_hi"].bytes / (cols * 4)),
+                           (long long)(ws_[base + "_hb"].bytes / (cols * 2)),
+                           (long long)(ws_[base + "_lb"].bytes / (cols * 2))});
+    return b;
+}
+
 void Model::check_dev_error() {
     int e = 0;
     N3D_CUDA(cudaMemcpy(&e, dev_err_, sizeof(int), cudaMemcpyDeviceToHost));
@@ -640,7 +668,7 @@ void Model::prof_collect() {
 }
 
 // The 31-layer tower on B sequences of stride S rows (S a multiple of 8) held in
-// ws "win".  Output: the final LayerNorm as a TF32 pair in "n_hi"/"n_lo" (and
+// ws "win".  Output: the final LayerNorm in the 3-term split in ws "n" (and
 // plain in enc_plain when given).  Residual adds are fused into the LayerNorm
 // that follows them, so every GEMM epilogue is a pure (TMA) store.
 void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain) {
@@ -649,8 +677,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     float* win = (float*)ws("win", M * h * 4);
     float* x = (float*)ws("x", M * h * 4);
     float* tmp = (float*)ws("tmp", M * h * 4);
-    float* n_hi = (float*)ws("n_hi", M * h * 4);
-    float* n_lo = (float*)ws("n_lo", M * h * 4);
+    const Split3Buf n = ws3("n", M, h);  // LayerNorm output, 3-term split
     // attention operands as bfloat16 pairs: Q, K [M, h]; V^T [h, M] (column = global row)
     AttnOperands ao;
     ao.q_hi = ws("q_hi", M * h * 2);
@@ -661,21 +688,14 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     ao.vt_hi = ws("vt_hi", h * M * 2);
     ao.vt_lo = ws("vt_lo", h * M * 2);
     ao.rows_cap = (long long)(ws_["q_hi"].bytes / (h * 2));
-    float* ctx_hi = (float*)ws("ctx_hi", M * h * 4);
-    float* ctx_lo = (float*)ws("ctx_lo", M * h * 4);
-    float* f_hi = (float*)ws("f_hi", M * c.inter * 4);
-    float* f_lo = (float*)ws("f_lo", M * c.inter * 4);
-    const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_ctx = ws_["ctx_hi"].bytes / (h * 4);
-    const long long rows_f = ws_["f_hi"].bytes / (c.inter * 4);
-    const SplitOperand An{n_hi, n_lo, rows_n, h, h};
-    const SplitOperand Actx{ctx_hi, ctx_lo, rows_ctx, h, h};
-    const SplitOperand Af{f_hi, f_lo, rows_f, c.inter, c.inter};
+    const Split3Buf ctx = ws3("ctx", M, h);     // attention context
+    const Split3Buf f = ws3("f", M, c.inter);   // GELU(fc1)
 
     Epi e;  // QKV: Q/K pairs with RoPE, V^T pair
     e.mode = EPI_QKV_ATTN;
     e.tma = 1;
     e.map_out = make_bf16_map(ao.q_hi, M, h, h, 64, 32, true);
-    e.map_out_lo = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
+    e.map_out2 = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
     e.map_k_hi = make_bf16_map(ao.k_hi, M, h, h, 64, 32, true);
     e.map_k_lo = make_bf16_map(ao.k_lo, M, h, h, 64, 32, true);
     e.map_vt_hi = make_bf16_map(ao.vt_hi, h, M, ao.vt_ld, 32, 64, false);
@@ -690,54 +710,55 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     eo.mode = EPI_STORE;
     eo.tma = 1;
     eo.map_out = make_store_map(tmp, M, h, h);
-    Epi e1;  // fc1: GELU(acc + bias) -> TF32 pair
+    Epi e1;  // fc1: GELU(acc + bias) -> 3-term split
     e1.mode = EPI_GELU_SPLIT;
     e1.tma = 1;
-    e1.map_out = make_store_map(f_hi, M, c.inter, c.inter);
-    e1.map_out_lo = make_store_map(f_lo, M, c.inter, c.inter);
+    e1.map_out = make_store_map(f.hi, M, c.inter, c.inter);
+    e1.map_out2 = make_store_map_bf16(f.hb, M, c.inter, c.inter);
+    e1.map_out3 = make_store_map_bf16(f.lb, M, c.inter, c.inter);
 
-    const double ln_bytes = (double)M * h * 4 * 5;  // read x + delta, write x and a TF32 pair
+    const double ln_bytes = (double)M * h * 4 * 5;  // read x + delta, write x, hi, hb, lb
     prof_begin();
-    launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, x, nullptr);
+    launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, Split3Out{x, nullptr, nullptr});
     prof_end(K_LN, 0, (double)M * h * 8);
     for (int l = 0; l < c.layers; l++) {
         const DevLayer& L = layers_[l];
         prof_begin();
         if (l == 0)
-            launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
+            launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out());
         else
-            launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln1_w, L.ln1_b, n_hi, n_lo);
+            launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln1_w, L.ln1_b, n.out());
         prof_end(K_LN, 0, ln_bytes);
         prof_begin();
-        gemm_tf32x3(stream_, An, L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
+        gemm_split3(stream_, n.op(), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);
         prof_begin();
-        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx_hi, ctx_lo, dev_err_);
+        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx.out(), dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
         eo.bias = L.o.bias;
         prof_begin();
-        gemm_tf32x3(stream_, Actx, L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
+        gemm_split3(stream_, ctx.op(), L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
         prof_end(K_GEMM_O, 2.0 * M * h * h, 0);
         prof_begin();
-        launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln2_w, L.ln2_b, n_hi, n_lo);
+        launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln2_w, L.ln2_b, n.out());
         prof_end(K_LN, 0, ln_bytes);
         e1.bias = L.fc1.bias;
         prof_begin();
-        gemm_tf32x3(stream_, An, L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
+        gemm_split3(stream_, n.op(), L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
         prof_end(K_GEMM_FC1, 2.0 * M * c.inter * h, 0);
         eo.bias = L.fc2.bias;
         prof_begin();
-        gemm_tf32x3(stream_, Af, L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
+        gemm_split3(stream_, f.op(), L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
         prof_end(K_GEMM_FC2, 2.0 * M * h * c.inter, 0);
     }
     prof_begin();
-    launch_add_layer_norm(stream_, x, tmp, M, (int)h, fin_ln_w_, fin_ln_b_, n_hi, n_lo);
+    launch_add_layer_norm(stream_, x, tmp, M, (int)h, fin_ln_w_, fin_ln_b_, n.out());
     prof_end(K_LN, 0, ln_bytes);
-    if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, enc_plain, nullptr);
+    if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, Split3Out{enc_plain, nullptr, nullptr});
     (void)d_seq_len;
 }
 
-// Classification head (src/head.rs:147-157) on the encoder output in n_hi/n_lo:
+// Classification head (src/head.rs:147-157) on the encoder output in ws "n":
 // proj into a per-sequence zero-padded layout [B, S+2, hh] -> implicit-GEMM k=3
 // conv over it (its output keeps that padded row layout; the sub-pixel reshape
 // is free on row-major memory) -> dense + ReLU + out_proj fused.  Logits land
@@ -746,21 +767,18 @@ void Model::head(int B, int S, const int* d_seq_len) {
     const Config& c = cfg_;
     const long long M = (long long)B * S, h = c.hidden, hh = c.head_hidden, up = c.sub;
     const long long PR = (long long)B * (S + 2), MC = PR - 2;
-    float* n_hi = (float*)ws("n_hi", M * h * 4);
-    float* n_lo = (float*)ws("n_lo", M * h * 4);
-    float* p_hi = (float*)ws("p_hi", PR * hh * 4);
-    float* p_lo = (float*)ws("p_lo", PR * hh * 4);
-    float* u_hi = (float*)ws("u_hi", PR * up * hh * 4);
-    float* u_lo = (float*)ws("u_lo", PR * up * hh * 4);
+    const Split3Buf n = ws3("n", M, h);
+    const Split3Buf pb = ws3("p", PR, hh);        // proj output, zero-padded per sequence
+    const Split3Buf u = ws3("u", PR * up, hh);    // conv output as [8 rows per frame, hh]
     float* logits = (float*)ws("logits", PR * up * c.num_speakers * 4);
-    const long long rows_n = ws_["n_hi"].bytes / (h * 4), rows_p = ws_["p_hi"].bytes / (hh * 4);
-    const long long rows_u = ws_["u_hi"].bytes / (hh * 4);
-    N3D_CUDA(cudaMemsetAsync(p_hi, 0, PR * hh * 4, stream_));
-    N3D_CUDA(cudaMemsetAsync(p_lo, 0, PR * hh * 4, stream_));
+    N3D_CUDA(cudaMemsetAsync(pb.hi, 0, PR * hh * 4, stream_));
+    N3D_CUDA(cudaMemsetAsync(pb.hb, 0, PR * hh * 2, stream_));
+    N3D_CUDA(cudaMemsetAsync(pb.lb, 0, PR * hh * 2, stream_));
     Epi ep;
     ep.mode = EPI_SPLIT;
-    ep.out = p_hi;
-    ep.out_lo = p_lo;
+    ep.out = pb.hi;
+    ep.out2 = pb.hb;
+    ep.out3 = pb.lb;
     ep.ldo = hh;
     ep.bias = proj_.bias;
     ep.rdiv = S;
@@ -769,18 +787,18 @@ void Model::head(int B, int S, const int* d_seq_len) {
     ep.roff = 1;
     ep.seq_len = d_seq_len;
     prof_begin();
-    gemm_tf32x3(stream_, SplitOperand{n_hi, n_lo, rows_n, h, h}, proj_.op(), (int)M, (int)hh, (int)h, 0, ep,
-                dev_err_);
+    gemm_split3(stream_, n.op(), proj_.op(), (int)M, (int)hh, (int)h, 0, ep, dev_err_);
     prof_end(K_GEMM_PROJ, 2.0 * M * hh * h, 0);
     Epi ec;
     ec.mode = EPI_RELU_SPLIT;
     ec.tma = 1;
     ec.bias = conv_.bias;
-    ec.map_out = make_store_map(u_hi, MC, up * hh, up * hh);
-    ec.map_out_lo = make_store_map(u_lo, MC, up * hh, up * hh);
+    ec.map_out = make_store_map(u.hi, MC, up * hh, up * hh);
+    ec.map_out2 = make_store_map_bf16(u.hb, MC, up * hh, up * hh);
+    ec.map_out3 = make_store_map_bf16(u.lb, MC, up * hh, up * hh);
     prof_begin();
-    gemm_tf32x3(stream_, SplitOperand{p_hi, p_lo, rows_p, hh, hh}, conv_.op(), (int)MC, (int)(up * hh),
-                (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
+    // k=3 conv: k-block kb (of 32) reads tap kb / 6, i.e. rows shifted by 0, 1, 2
+    gemm_split3(stream_, pb.op(), conv_.op(), (int)MC, (int)(up * hh), (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
     prof_end(K_GEMM_CONV, 2.0 * M * up * hh * 3 * hh, 0);
     Epi ed;
     ed.mode = EPI_DENSE_OUT;
@@ -791,8 +809,7 @@ void Model::head(int B, int S, const int* d_seq_len) {
     ed.b2 = out_b_;
     ed.n2 = c.num_speakers;
     prof_begin();
-    gemm_tf32x3(stream_, SplitOperand{u_hi, u_lo, rows_u, hh, hh}, dense_.op(), (int)(MC * up), (int)hh, (int)hh,
-                0, ed, dev_err_);
+    gemm_split3(stream_, u.op(), dense_.op(), (int)(MC * up), (int)hh, (int)hh, 0, ed, dev_err_);
     prof_end(K_GEMM_DENSE, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
 }
 
@@ -960,10 +977,10 @@ const float* Model::mel_embed(const float* d_audio, const std::vector<long long>
         }
     }
     const long long mel_rows = std::max(total_groups * sub, 1LL);
-    float* mel_hi = (float*)ws("mel_hi", mel_rows * c.n_mels * 4);
-    float* mel_lo = (float*)ws("mel_lo", mel_rows * c.n_mels * 4);
-    N3D_CUDA(cudaMemsetAsync(mel_hi, 0, mel_rows * c.n_mels * 4, stream_));
-    N3D_CUDA(cudaMemsetAsync(mel_lo, 0, mel_rows * c.n_mels * 4, stream_));
+    const Split3Buf mel = ws3("mel", mel_rows, c.n_mels);  // rows past a segment's frames stay zero
+    N3D_CUDA(cudaMemsetAsync(mel.hi, 0, mel_rows * c.n_mels * 4, stream_));
+    N3D_CUDA(cudaMemsetAsync(mel.hb, 0, mel_rows * c.n_mels * 2, stream_));
+    N3D_CUDA(cudaMemsetAsync(mel.lb, 0, mel_rows * c.n_mels * 2, stream_));
     if (total_frames > 0) {
         long long* d_fb = (long long*)ws("f_base", total_frames * 8);
         long long* d_fo = (long long*)ws("f_out", total_frames * 8);
@@ -973,7 +990,7 @@ const float* Model::mel_embed(const float* d_audio, const std::vector<long long>
         N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
         prof_begin();
         launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_,
-                   c.preemph, mel_hi, mel_lo, nullptr, d_fo);
+                   c.preemph, mel.out(), nullptr, d_fo);
         prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
     }
     const long long K_emb = (long long)sub * c.n_mels;
@@ -983,10 +1000,10 @@ const float* Model::mel_embed(const float* d_audio, const std::vector<long long>
         e.mode = EPI_STORE;
         e.out = embeds;
         e.ldo = h;
-        const long long rows_cap = ws_["mel_hi"].bytes / (K_emb * 4);
+        // the [rows, 128] mel viewed as [groups, 8 * 128]: 8 stacked frames per row
+        const SplitOperand A{mel.hi, mel.hb, mel.lb, mel.rows_cap / sub, K_emb, K_emb};
         prof_begin();
-        gemm_tf32x3(stream_, SplitOperand{mel_hi, mel_lo, rows_cap, K_emb, K_emb}, embed_.op(), (int)total_groups, h,
-                    (int)K_emb, 0, e, dev_err_);
+        gemm_split3(stream_, A, embed_.op(), (int)total_groups, h, (int)K_emb, 0, e, dev_err_);
         prof_end(K_GEMM_EMBED, 2.0 * total_groups * h * K_emb, 0);
     }
     return embeds;
@@ -1265,14 +1282,12 @@ int Model::log_mel(const float* samples, long long n, bool centered, std::vector
     long long* d_fb = (long long*)ws("f_base", frames * 8);
     long long* d_fo = (long long*)ws("f_out", frames * 8);
     int* d_fm = (int*)ws("f_meta", frames * 8);
-    float* hi = (float*)ws("mel_hi", frames * c.n_mels * 4);
-    float* lo = (float*)ws("mel_lo", frames * c.n_mels * 4);
     float* pl = (float*)ws("mel_plain", frames * c.n_mels * 4);
     N3D_CUDA(cudaMemcpyAsync(d_fb, fb.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
     N3D_CUDA(cudaMemcpyAsync(d_fo, fo.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
     N3D_CUDA(cudaMemcpyAsync(d_fm, fm.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
-    launch_mel(stream_, a, d_fb, d_fm, frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph, hi, lo,
-               pl, d_fo);
+    launch_mel(stream_, a, d_fb, d_fm, frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph,
+               Split3Out{}, pl, d_fo);
     N3D_CUDA(cudaMemcpyAsync(out.data(), pl, frames * c.n_mels * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));
     return (int)frames;
@@ -1287,17 +1302,15 @@ void Model::embed_range(const float* mel, long long num_frames, long long lo, lo
     const long long end = std::min(hi * c.sub, num_frames);
     if (lo * c.sub < end) std::memcpy(buf.data(), mel + lo * c.sub * c.n_mels, (end - lo * c.sub) * c.n_mels * 4);
     float* plain = (float*)ws("stage_in", groups * K * 4);
-    float* shi = (float*)ws("mel_hi", groups * K * 4);
-    float* slo = (float*)ws("mel_lo", groups * K * 4);
+    const Split3Buf sp = ws3("stage_split", groups, K);
     float* o = (float*)ws("embeds", groups * c.hidden * 4);
     N3D_CUDA(cudaMemcpyAsync(plain, buf.data(), groups * K * 4, cudaMemcpyHostToDevice, stream_));
-    launch_split(stream_, plain, groups * K, shi, slo);
+    launch_split(stream_, plain, groups * K, sp.out());
     Epi e;
     e.mode = EPI_STORE;
     e.out = o;
     e.ldo = c.hidden;
-    gemm_tf32x3(stream_, SplitOperand{shi, slo, (long long)(ws_["mel_hi"].bytes / (K * 4)), K, K}, embed_.op(),
-                (int)groups, c.hidden, (int)K, 0, e, dev_err_);
+    gemm_split3(stream_, sp.op(), embed_.op(), (int)groups, c.hidden, (int)K, 0, e, dev_err_);
     N3D_CUDA(cudaMemcpyAsync(out, o, groups * c.hidden * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));
     check_dev_error();
@@ -1338,11 +1351,10 @@ void Model::head_forward(const float* enc, int frames, float* logits) {
     const int S = (frames + 7) / 8 * 8;
     const long long M = frames, h = c.hidden;
     float* plain = (float*)ws("enc_plain", (long long)S * h * 4);
-    float* n_hi = (float*)ws("n_hi", (long long)S * h * 4);
-    float* n_lo = (float*)ws("n_lo", (long long)S * h * 4);
+    const Split3Buf n = ws3("n", S, h);
     N3D_CUDA(cudaMemsetAsync(plain, 0, (long long)S * h * 4, stream_));
     N3D_CUDA(cudaMemcpyAsync(plain, enc, M * h * 4, cudaMemcpyHostToDevice, stream_));
-    launch_split(stream_, plain, (long long)S * h, n_hi, n_lo);
+    launch_split(stream_, plain, (long long)S * h, n.out());
     int* d_len = (int*)ws("seq_len", 4);
     N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
     head(1, S, d_len);

@@ -39,13 +39,25 @@ Config load_config(const std::string& dir);
 
 // ----------------------------------------------------------------- weights
 
-// A linear layer's weight [out, in] as a TF32 hi/lo pair plus optional bias.
+// A linear layer's weight [out, in] in the 3-term split plus optional bias.
 struct DevLinear {
     float* hi = nullptr;
-    float* lo = nullptr;
+    void* hb = nullptr;
+    void* lb = nullptr;
     float* bias = nullptr;
     int out = 0, in = 0;
-    SplitOperand op() const { return SplitOperand{hi, lo, out, in, in}; }
+    SplitOperand op() const { return SplitOperand{hi, hb, lb, out, in, in}; }
+};
+
+// Workspace for an activation in the 3-term split (base_hi / base_hb / base_lb),
+// rows_cap = rows the buffers hold.
+struct Split3Buf {
+    float* hi = nullptr;
+    void* hb = nullptr;
+    void* lb = nullptr;
+    long long rows_cap = 0, cols = 0;
+    SplitOperand op() const { return SplitOperand{hi, hb, lb, rows_cap, cols, cols}; }
+    Split3Out out() const { return Split3Out{hi, hb, lb}; }
 };
 
 struct DevLayer {
@@ -179,6 +191,7 @@ class Model {
     void run_step(const SeqStep* d_steps, int B, int S, const int* d_len, const int* d_valid, const float* embeds);
     void session_round(std::vector<SessionChunk>& items, std::vector<std::vector<float>>& rows);
     void* ws(const char* name, size_t bytes);
+    Split3Buf ws3(const std::string& base, long long rows, long long cols);
     void check_dev_error();
 
     Config cfg_;

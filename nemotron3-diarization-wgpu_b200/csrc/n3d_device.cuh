@@ -253,6 +253,19 @@ __device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, 
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// kind::f16 pair MMA: D f32, A/B bf16, K-major, M = 256.
+__host__ __device__ constexpr uint32_t idesc_bf16_pair(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((256u >> 4) << 24);
+}
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // Arrive on `bar` (same offset) in both CTAs once the pair MMAs issued so far completed.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
     asm volatile(
@@ -314,6 +327,37 @@ __device__ __forceinline__ float tf32_rna(float x) {
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = tf32_rna(x);
     lo = tf32_rna(__fsub_rn(x, hi));
+}
+
+// ------------------------------------------------ 3-term operand split (GEMMs)
+// Every GEMM operand x is stored as hi = RN-TF32(x) (an fp32 array read by kind::tf32
+// MMAs) plus bf16 copies hb = RN-bf16(hi) and lb = RN-bf16(x - hi) (read by kind::f16
+// MMAs).  A dot product is then hi_x·hi_y (TF32) + hb_x·lb_y + lb_x·hb_y (BF16): the
+// cross terms are 2^-11 of the main one, so their bf16 rounding costs ~2^-20 relative,
+// while two of the three products run at the bf16 rate.
+__device__ __forceinline__ uint32_t bf16x2_rn(float a, float b) {  // a in the low half
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+// Two consecutive elements: hi values, and the bf16 pairs of hb and lb (a in the low half).
+__device__ __forceinline__ void split3x2(float a, float b, float& ha, float& hb, uint32_t& hbf, uint32_t& lbf) {
+    ha = tf32_rna(a);
+    hb = tf32_rna(b);
+    hbf = bf16x2_rn(ha, hb);
+    lbf = bf16x2_rn(__fsub_rn(a, ha), __fsub_rn(b, hb));
+}
+// One element: hi, and its hb / lb bf16 bits (one conversion for both).
+__device__ __forceinline__ void split3x1(float x, float& h, uint16_t& hb, uint16_t& lb) {
+    h = tf32_rna(x);
+    const uint32_t p = bf16x2_rn(h, __fsub_rn(x, h));
+    hb = (uint16_t)(p & 0xffffu);
+    lb = (uint16_t)(p >> 16);
+}
+// Four consecutive elements: hi in h[4], hb / lb as 4 bf16 each (8 bytes).
+__device__ __forceinline__ void split3x4(const float* x, float* h, uint2& hbf, uint2& lbf) {
+    split3x2(x[0], x[1], h[0], h[1], hbf.x, lbf.x);
+    split3x2(x[2], x[3], h[2], h[3], hbf.y, lbf.y);
 }
 
 // ------------------------------------------------------ 3xBF16 (kind::f16)

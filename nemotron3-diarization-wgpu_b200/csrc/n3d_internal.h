@@ -22,24 +22,24 @@ void cuda_check(cudaError_t e, const char* what);
 
 // ------------------------------------------------------------------ GEMM
 
-// Epilogue applied to each 128 x BN accumulator tile of C = A * B^T.
+// Epilogue applied to each accumulator tile of C = A * B^T.
 enum EpiMode : int {
     EPI_STORE = 0,       // out[r, c] = acc + bias                     (fp32)
-    EPI_SPLIT = 1,       // (out, out_lo) = split(acc + bias)          (TF32 hi/lo pair)
-    EPI_GELU_SPLIT = 2,  // split(gelu(acc + bias))
-    EPI_RESID = 3,       // out[r, c] += acc + bias                    (residual stream, in place)
-    EPI_RELU_SPLIT = 4,  // split(relu(acc + bias))
-    EPI_QKV_ROPE = 5,    // Q,K columns rotated by RoPE, V as is; fp32 out
+    EPI_SPLIT = 1,       // split3(acc + bias) -> out (hi), out2 (hb), out3 (lb)
+    EPI_GELU_SPLIT = 2,  // split3(gelu(acc + bias))
+    EPI_RELU_SPLIT = 4,  // split3(relu(acc + bias))
     EPI_DENSE_OUT = 6,   // r = relu(acc + bias); out[r, 0:ns] = r . w2^T + b2
-    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_out*, map_k_*);
-                         // V -> transposed bf16 pair V^T[head*64 + d][row] (map_vt_*); TMA only
+    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_out / map_out2,
+                         // map_k_*); V -> transposed bf16 pair V^T[head*64 + d][row] (map_vt_*); TMA only
 };
 
 struct Epi {
     int mode = EPI_STORE;
     const float* bias = nullptr;
+    // Direct stores: out (fp32 / hi), out2 and out3 (bf16 hb / lb of the split modes).
     float* out = nullptr;
-    float* out_lo = nullptr;
+    void* out2 = nullptr;
+    void* out3 = nullptr;
     long long ldo = 0;
     // Row remap: q = r / rdiv, t = r % rdiv; rows with t >= rkeep are skipped;
     // the output row is q * rmul + t + roff.
@@ -53,56 +53,70 @@ struct Epi {
     int rope_seq = 1;
     int head_dim = 64;
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
-    // Stores through TMA (tma != 0): tensor maps over the destinations, box 32 columns
-    // x 32 rows, 128-byte swizzle (make_store_map).  map_out/map_out_lo: the output
-    // (pair).  EPI_QKV_ATTN: bf16 maps (make_bf16_map) -- map_out*/map_k_* with box
-    // 64 x 32 and 128-byte swizzle, map_vt_* over V^T [heads*64, rows] with box
-    // 32 x 64 and no swizzle.
+    // Stores through TMA (tma != 0), box 32 columns x 32 rows: map_out fp32 (128-byte
+    // swizzle, make_store_map), map_out2 / map_out3 bf16 (64-byte swizzle,
+    // make_store_map_bf16).  EPI_QKV_ATTN: bf16 maps from make_bf16_map -- map_out /
+    // map_out2 and map_k_* with box 64 x 32 and the 128-byte swizzle, map_vt_* over
+    // V^T [heads*64, rows] with box 32 x 64 and no swizzle.
     int tma = 0;
-    CUtensorMap map_out, map_out_lo, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
+    CUtensorMap map_out, map_out2, map_out3, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
     const float* b2 = nullptr;
     int n2 = 0;
 };
 
-// A K-major fp32 operand stored as a TF32 hi/lo pair, [rows, cols] with row stride ld.
+// A K-major operand in the 3-term split, [rows, cols] with row stride ld (elements,
+// shared by the three arrays): hi = RN-TF32(x) (fp32), hb = bf16(hi), lb = bf16(x - hi).
 struct SplitOperand {
     const float* hi = nullptr;
-    const float* lo = nullptr;
+    const void* hb = nullptr;
+    const void* lb = nullptr;
     long long rows = 0, cols = 0, ld = 0;
 };
 
-// TMA-store map (box 32 x 32, 128-byte swizzle) over a row-major fp32 matrix.
+// TMA-store maps (box 32 x 32) over a row-major fp32 matrix (128-byte swizzle) or
+// bf16 matrix (64-byte swizzle).
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
+CUtensorMap make_store_map_bf16(const void* p, long long rows, long long cols, long long ld);
 // 2-D map over a row-major bfloat16 matrix [rows, cols] with row stride ld elements;
 // box box_cols x box_rows, 128-byte swizzle when `swizzle` (box_cols must then be 64).
 CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
                           bool swizzle);
 
-// C[M, N] = A[M, K] * B[N, K]^T in 3xTF32 on tcgen05. `kb_per_tap` > 0 turns on
-// the shifted-row (implicit k=3 conv) mode: k-block kb reads A at column
-// (kb % kb_per_tap) * 32 and row m0 + kb / kb_per_tap.
-void gemm_tf32x3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
-                 int kb_per_tap, const Epi& epi, int* dev_err);
+// C[M, N] = A[M, K] * B[N, K]^T with the 3-term split on tcgen05 (gemm.cu).  K % 32 == 0.
+// `kb_per_tap` > 0 turns on the shifted-row (implicit k=3 conv) mode: k-block kb (of
+// 32) reads A at column (kb % kb_per_tap) * 32 and row m0 + kb / kb_per_tap.
+void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                 const Epi& epi, int* dev_err);
+// Same with tensor maps encoded on the stack (no host allocation), 128 x 128 tiles.
+void gemm_split3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                            const Epi& epi, int* dev_err);
 
 // --------------------------------------------------------------- other kernels
+// Destination of a producer of GEMM operands: the three arrays of the 3-term split
+// (row stride = the producer's row length), or plain fp32 into `hi` when hb == nullptr.
+struct Split3Out {
+    float* hi = nullptr;
+    void* hb = nullptr;
+    void* lb = nullptr;
+};
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
-                       float* out, float* out_lo);
-// Residual add fused into the next LayerNorm: x += delta (in place), out = LN(x) as a TF32 pair.
+                       Split3Out out);
+// Residual add fused into the next LayerNorm: x += delta (in place), out = LN(x).
 void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
-                           const float* b, float* out, float* out_lo);
+                           const float* b, Split3Out out);
+// SIMT attention (head_dim 128 kernel probes): plain fp32 context.
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
-                      int head_dim, float* ctx_hi, float* ctx_lo);
+                      int head_dim, float* ctx);
 // Log-mel frames: frame f reads audio[f_base[f] + p] for p in [p0, p0 + n_fft) with
 // p0 = f_meta[2f] and the clip length f_meta[2f+1] (zeros outside [0, len)), and
-// writes row f_out[f] of the [rows, 128] mel outputs (TF32 pair, plain optional).
+// writes row f_out[f] of the [rows, 128] mel outputs (3-term split, plain optional).
 void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
                 const float* window, const float* twiddle, const float* filters, const int* filt_lo,
-                const int* filt_hi, float preemph, float* mel_hi, float* mel_lo, float* mel_plain,
-                const long long* f_out);
-// x -> (hi, lo) TF32 pair, elementwise.
-void launch_split(cudaStream_t s, const float* x, long long n, float* hi, float* lo);
+                const int* filt_hi, float preemph, Split3Out mel, float* mel_plain, const long long* f_out);
+// x -> its 3-term split, elementwise (n % 4 == 0).
+void launch_split(cudaStream_t s, const float* x, long long n, Split3Out out);
 // Operands of the tcgen05 attention (head_dim 64), all bfloat16 hi/lo pairs:
 // Q, K [rows_cap, heads*64] with sequence b at rows b*S..; V^T [heads*64, vt_ld]
 // whose column is the global row.
@@ -113,9 +127,9 @@ struct AttnOperands {
     long long vt_ld = 0;
 };
 // tcgen05 attention (attention_tc.cu); S (when seqs > 1) and vt_ld must be multiples
-// of 8.  Context [seqs*S, heads*64] as a TF32 pair, or plain fp32 when ctx_lo == nullptr.
+// of 8.  Context [seqs*S, heads*64] in the 3-term split (or plain fp32).
 void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
-                         float* ctx_hi, float* ctx_lo, int* err);
+                         Split3Out ctx, int* err);
 // q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
                       const float* cos_t, const float* sin_t, const AttnOperands& op);

@@ -31,9 +31,6 @@
 
 namespace n3d {
 
-void gemm_tf32x3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
-                            const Epi& epi, int* err);
-
 namespace {
 
 constexpr size_t kScratchFloats = size_t(4) << 20;  // 16 MiB
@@ -72,6 +69,24 @@ DeviceSymbols symbols_for(int device) {
 
 size_t round64(size_t n) { return (n + 63) & ~size_t(63); }
 
+// One operand's 3-term split carved out of the scratch: hi (n floats), then hb and lb
+// (n bf16 each); every part starts on a 256-byte boundary.
+struct Carve {
+    float* hi;
+    void* hb;
+    void* lb;
+    float* next;
+};
+Carve carve(float* p, size_t n) {
+    const size_t nf = round64(n);  // floats, a multiple of 64 (256 bytes)
+    Carve c;
+    c.hi = p;
+    c.hb = p + nf;
+    c.lb = p + nf + nf / 2;
+    c.next = p + 2 * nf;
+    return c;
+}
+
 }  // namespace
 
 size_t linear_noalloc_capacity() { return kScratchFloats; }
@@ -81,29 +96,27 @@ void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, cons
     if (!d_x || !d_w || !d_y) throw Error(13, "n3d_linear_noalloc: null argument");
     if (cols == 0 || cols % 32) throw Error(13, "n3d_linear_noalloc: cols must be a positive multiple of 32");
     if (rows == 0 || out == 0) return;
-    const size_t need = 2 * round64(rows * cols) + 2 * round64(out * cols);
+    const size_t need = 2 * round64(rows * cols) + 2 * round64(out * cols);  // hi + hb + lb per operand
     if (need > kScratchFloats)
         throw Error(13, "n3d_linear_noalloc: request needs " + std::to_string(need) +
                             " scratch floats; the fixed scratch holds " + std::to_string(kScratchFloats) +
                             " (rows*cols + out*cols must stay within about 2097152)");
     N3D_CUDA(cudaSetDevice(device));
     const DeviceSymbols sym = symbols_for(device);
-    float* xh = sym.scratch;
-    float* xl = xh + round64(rows * cols);
-    float* wh = xl + round64(rows * cols);
-    float* wl = wh + round64(out * cols);
+    const Carve x = carve(sym.scratch, rows * cols);
+    const Carve w = carve(x.next, out * cols);
     // the status word starts at zero for every call; the split arrays are fully overwritten
     N3D_CUDA(cudaMemsetAsync(sym.status, 0, sizeof(int), stream));
-    launch_split(stream, d_x, (long long)(rows * cols), xh, xl);
-    launch_split(stream, d_w, (long long)(out * cols), wh, wl);
+    launch_split(stream, d_x, (long long)(rows * cols), Split3Out{x.hi, x.hb, x.lb});
+    launch_split(stream, d_w, (long long)(out * cols), Split3Out{w.hi, w.hb, w.lb});
     Epi e;
     e.mode = EPI_STORE;
     e.bias = d_bias;
     e.out = d_y;
     e.ldo = (long long)out;
-    gemm_tf32x3_stack_maps(stream, SplitOperand{xh, xl, (long long)rows, (long long)cols, (long long)cols},
-                           SplitOperand{wh, wl, (long long)out, (long long)cols, (long long)cols}, (int)rows,
-                           (int)out, (int)cols, e, sym.status);
+    gemm_split3_stack_maps(stream, SplitOperand{x.hi, x.hb, x.lb, (long long)rows, (long long)cols, (long long)cols},
+                           SplitOperand{w.hi, w.hb, w.lb, (long long)out, (long long)cols, (long long)cols},
+                           (int)rows, (int)out, (int)cols, e, sym.status);
     N3D_CUDA(cudaStreamSynchronize(stream));
     int status = 0;
     N3D_CUDA(cudaMemcpy(&status, sym.status, sizeof(int), cudaMemcpyDeviceToHost));
