@@ -13,20 +13,25 @@
 // checkpoint), at half the tensor time and half the operand bytes, which lets
 // two CTAs share an SM.
 //
-// CTA = 128 queries of one (sequence, head); 10 warps, two CTAs per SM:
-//   warp 0      TMA: the Q pair once, then per block of 64 keys the K pair and
-//               the V^T pair into a 2-stage ring
-//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T into TMEM buffer
-//               j % 2 (block j+1's QK^T overlaps block j's softmax) and
-//               O_j = P_j V_j with P_j read from TMEM, into O buffer j % 2
-//   warps 2..9  softmax, two warps per query row (TMEM lane): each takes half of
-//               the block's keys and half of the output columns; online max/sum;
-//               P_j as bf16 pairs written over the S_j columns it read (QK_{j+2}
-//               is issued once PV_j has completed); O folded into registers.
-//               exp is 2^x on the special-function unit after one FMA folds the
-//               1/sqrt(hd) scale, log2 e and the running max together; sums and the
-//               O fold use packed f32x2 FMA/add.
-// TMEM (256 columns): S/P[2] 0..127, O[2] 128..255.
+// CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM:
+//   warp 0      TMA: per block of 64 keys the K pair and the V^T pair into a
+//               3-stage ring (two blocks of prefetch hide the load latency)
+//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T as soon as the softmax
+//               has read S_{j-1}, and O += P_j V_j; both MMAs take their A operand
+//               (Q, P) from TMEM, so only K / V^T are read from shared memory
+//   warps 2..5  softmax, one thread per query row (TMEM lane): first the row's Q
+//               pair into TMEM; per block the row's 64 scores, exp as 2^x on the
+//               special-function unit after one FMA folds the 1/sqrt(hd) scale,
+//               log2 e and the reference max together; then, once PV_{j-1} has
+//               read the P buffer, P_j as bf16 pairs.
+// Lazy rescaling: exponents use a per-row reference max m that is raised only when
+// a block's max exceeds it by more than 2^8 in the exponent; only then is O
+// (in TMEM) multiplied by the correction, after PV_{j-1} has completed and before
+// P_j is released.  P values stay below 2^8; O / l is unchanged mathematically.
+// TMEM (256 columns): S 0..63, P 64..127 (hi 64.., lo 96..), O 128..191,
+// Q 192..255 (hi 192.., lo 224..); bf16 operands two per 32-bit column.
+// Barriers with a phase per key block
+// are double-buffered by block parity, so every waiter is at most one phase behind.
 // Every wait is bounded; an expired wait records its site in *err.
 
 #include "n3d_device.cuh"
@@ -39,13 +44,14 @@ namespace {
 constexpr int HD = 64;                    // head dim
 constexpr int QT = 128;                   // queries per CTA
 constexpr int KB = 64;                    // keys per block
-constexpr int Q_TILE = QT * 128;          // [128 rows x 64 bf16]: 16 KB (hi or lo)
 constexpr int KV_TILE = KB * 128;         // [64 rows x 64 bf16]: 8 KB
 constexpr int STAGE_BYTES = 4 * KV_TILE;  // K_hi, K_lo, V^T_hi, V^T_lo
-constexpr int THREADS = 320;
-constexpr int SMEM_BYTES = 2 * Q_TILE + 2 * STAGE_BYTES + 1024 + 256 + 6 * QT * 4;
-constexpr uint32_t COL_S = 0, COL_O = 128, TMEM_COLS = 256;
+constexpr int THREADS = 192;
+constexpr int NSTAGE = 3;
+constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128, COL_Q = 192, TMEM_COLS = 256;
 constexpr int DEV_TIMEOUT_ATTN = 5;
+constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
 
 // f32 pairs in one 64-bit register: Blackwell's packed FMA / add issue two lanes' worth
 // of work per instruction.
@@ -74,27 +80,58 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return r;
 }
 
+// 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[32 * h + 0]), "=r"(r[32 * h + 1]), "=r"(r[32 * h + 2]), "=r"(r[32 * h + 3]),
+              "=r"(r[32 * h + 4]), "=r"(r[32 * h + 5]), "=r"(r[32 * h + 6]), "=r"(r[32 * h + 7]),
+              "=r"(r[32 * h + 8]), "=r"(r[32 * h + 9]), "=r"(r[32 * h + 10]), "=r"(r[32 * h + 11]),
+              "=r"(r[32 * h + 12]), "=r"(r[32 * h + 13]), "=r"(r[32 * h + 14]), "=r"(r[32 * h + 15]),
+              "=r"(r[32 * h + 16]), "=r"(r[32 * h + 17]), "=r"(r[32 * h + 18]), "=r"(r[32 * h + 19]),
+              "=r"(r[32 * h + 20]), "=r"(r[32 * h + 21]), "=r"(r[32 * h + 22]), "=r"(r[32 * h + 23]),
+              "=r"(r[32 * h + 24]), "=r"(r[32 * h + 25]), "=r"(r[32 * h + 26]), "=r"(r[32 * h + 27]),
+              "=r"(r[32 * h + 28]), "=r"(r[32 * h + 29]), "=r"(r[32 * h + 30]), "=r"(r[32 * h + 31])
+            : "r"(taddr + 32 * h));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+// 32 consecutive TMEM columns from 32-bit words; completes with tmem_wait_st().
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
 __global__ void __launch_bounds__(THREADS, 2)
-    attention_tc_kernel(const __grid_constant__ CUtensorMap tQh, const __grid_constant__ CUtensorMap tQl,
+    attention_tc_kernel(const uint4* __restrict__ q_hi, const uint4* __restrict__ q_lo, long long rows_cap,
                         const __grid_constant__ CUtensorMap tKh, const __grid_constant__ CUtensorMap tKl,
                         const __grid_constant__ CUtensorMap tVh, const __grid_constant__ CUtensorMap tVl, int S,
                         const int* __restrict__ valid_arr, int heads, Split3Out ctx, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQh = smem;
-    uint8_t* sQl = smem + Q_TILE;
-    uint8_t* stages = smem + 2 * Q_TILE;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + 2 * STAGE_BYTES);
-    uint64_t* q_full = bars;        // 1
-    uint64_t* kv_full = bars + 1;   // 2
-    uint64_t* kv_empty = bars + 3;  // 2
-    uint64_t* s_full = bars + 5;    // 2: QK_j committed
-    uint64_t* p_full = bars + 7;    // 2: P_j in TMEM (8 warps)
-    uint64_t* o_full = bars + 9;    // 2: PV_j committed
-    uint64_t* o_free = bars + 11;   // 2: O_j folded (8 warps)
+    uint8_t* stages = smem;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + NSTAGE * STAGE_BYTES);
+    uint64_t* q_ready = bars;       // 1: Q pair in TMEM (4 warps)
+    uint64_t* kv_full = bars + 1;   // NSTAGE
+    uint64_t* kv_empty = bars + 4;  // NSTAGE
+    uint64_t* s_full = bars + 7;    // 1: phase j = QK_j committed
+    uint64_t* s_free = bars + 8;    // 1: phase j = S_j read by the softmax (4 warps)
+    uint64_t* p_full = bars + 9;    // 2: P_j in TMEM, any rescale of O done (4 warps)
+    uint64_t* o_full = bars + 11;   // 2: PV_j committed (j % 2); a waiter for PV_j has always seen PV_{j-2}
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-    float* red_max = reinterpret_cast<float*>(bars + 32);  // [2 blocks][2 halves][QT]
-    float* red_sum = red_max + 4 * QT;                      // [2 halves][QT]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
@@ -103,14 +140,16 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int row0 = b * S;  // first row of this sequence in Q / K, first column in V^T
 
     if (warp == 0 && lane == 0) {
-        mbar_init(q_full, 1);
-        for (int i = 0; i < 2; i++) {
+        mbar_init(q_ready, 4);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        for (int i = 0; i < NSTAGE; i++) {
             mbar_init(&kv_full[i], 1);
             mbar_init(&kv_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 8);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&p_full[i], 4);
             mbar_init(&o_full[i], 1);
-            mbar_init(&o_free[i], 8);
         }
         mbar_fence_init();
     }
@@ -121,13 +160,10 @@ __global__ void __launch_bounds__(THREADS, 2)
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
-            mbar_arrive_expect_tx(q_full, 2 * Q_TILE);
-            tma_load_2d(sQh, &tQh, q_full, h * HD, row0 + q0);
-            tma_load_2d(sQl, &tQl, q_full, h * HD, row0 + q0);
             int issued = 0;
             for (int j = 0; j < nblk; j++) {
-                const int st = j & 1;
-                if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
+                const int st = j % NSTAGE;
+                if (j >= NSTAGE && !mbar_wait(&kv_empty[st], ((j / NSTAGE) - 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
                 uint8_t* sb = stages + st * STAGE_BYTES;
                 mbar_arrive_expect_tx(&kv_full[st], STAGE_BYTES);
                 tma_load_2d(sb, &tKh, &kv_full[st], h * HD, row0 + j * KB);
@@ -138,173 +174,176 @@ __global__ void __launch_bounds__(THREADS, 2)
             }
             // the last loads of each stage have landed before the CTA may exit
             // (already true unless a wait above or in the MMA warp expired)
-            mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);
-            for (int j = max(0, issued - 2); j < issued; j++) mbar_wait(&kv_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+            for (int j = max(0, issued - NSTAGE); j < issued; j++)
+                mbar_wait(&kv_full[j % NSTAGE], (j / NSTAGE) & 1, err, DEV_TIMEOUT_ATTN);
         }
     } else if (warp == 1) {
         if (lane == 0 && nblk > 0) {
             constexpr uint32_t idesc = idesc_bf16(64);
-            bool ok = mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);
-            const uint32_t qh = smem_u32(sQh), ql = smem_u32(sQl);
+            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
             auto issue_qk = [&](int j) {
-                const uint32_t kb = smem_u32(stages + (j & 1) * STAGE_BYTES);
-                const uint32_t d = tmem + COL_S + 64u * (j & 1);
+                const uint32_t kb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES);
+                const uint32_t d = tmem + COL_S;
 #pragma unroll
-                for (int k = 0; k < HD / 16; k++) {  // 16 bf16 = 32 bytes along the swizzled row
-                    const uint32_t off = k * 32;
-                    umma_bf16(d, desc_k_sw128(ql + off), desc_k_sw128(kb + off), idesc, k != 0);
-                    umma_bf16(d, desc_k_sw128(qh + off), desc_k_sw128(kb + KV_TILE + off), idesc, 1);
-                    umma_bf16(d, desc_k_sw128(qh + off), desc_k_sw128(kb + off), idesc, 1);
+                for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at 32 + 8k
+                    const uint32_t off = k * 32;  // 16 bf16 = 32 bytes along the swizzled K rows
+                    const uint32_t qh = tmem + COL_Q + 8 * k, ql = qh + 32;
+                    umma_bf16_ts(d, ql, desc_k_sw128(kb + off), idesc, k != 0);
+                    umma_bf16_ts(d, qh, desc_k_sw128(kb + KV_TILE + off), idesc, 1);
+                    umma_bf16_ts(d, qh, desc_k_sw128(kb + off), idesc, 1);
                 }
-                umma_commit(&s_full[j & 1]);
+                umma_commit(s_full);
             };
-            if (ok) ok = mbar_wait(&kv_full[0], 0, err, DEV_TIMEOUT_ATTN);
+            if (ok) {
+                tc_fence_after();
+                ok = mbar_wait(&kv_full[0], 0, err, DEV_TIMEOUT_ATTN);
+            }
             if (ok) {
                 tc_fence_after();
                 issue_qk(0);
             }
             for (int j = 0; ok && j < nblk; j++) {
                 if (j + 1 < nblk) {
-                    // S buffer (j+1)%2 holds P_{j-1}: MMAs into different accumulators are not
-                    // ordered, so PV_{j-1} must have completed before QK_{j+1} overwrites it
-                    ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-                    if (ok && j >= 1) ok = mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                    // the S buffer is free once the softmax has loaded S_j from it
+                    ok = mbar_wait(&kv_full[(j + 1) % NSTAGE], ((j + 1) / NSTAGE) & 1, err, DEV_TIMEOUT_ATTN);
+                    if (ok) ok = mbar_wait(s_free, j & 1, err, DEV_TIMEOUT_ATTN);
                     if (!ok) break;
                     tc_fence_after();
                     issue_qk(j + 1);
                 }
-                ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-                if (ok && j >= 2) ok = mbar_wait(&o_free[j & 1], ((j >> 1) - 1) & 1, err, DEV_TIMEOUT_ATTN);
-                if (!ok) break;
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
                 tc_fence_after();
-                const uint32_t vb = smem_u32(stages + (j & 1) * STAGE_BYTES + 2 * KV_TILE);
-                const uint32_t d = tmem + COL_O + 64u * (j & 1);
-                const uint32_t pb = tmem + COL_S + 64u * (j & 1);
+                const uint32_t vb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES + 2 * KV_TILE);
+                const uint32_t pb = tmem + COL_P;
 #pragma unroll
-                for (int k = 0; k < KB / 16; k++) {
-                    // keys 16k..16k+15 were written by softmax half k/2: P_hi at its
-                    // columns 0..15, P_lo at 16..31 (8 columns per 16 keys)
-                    const uint32_t ph = pb + 32 * (k >> 1) + 8 * (k & 1), pl = ph + 16;
+                for (int k = 0; k < KB / 16; k++) {  // keys 16k..16k+15: P_hi at column 8k, P_lo at 32 + 8k
                     const uint32_t off = k * 32;
-                    umma_bf16_ts(d, pl, desc_k_sw128(vb + off), idesc, k != 0);
-                    umma_bf16_ts(d, ph, desc_k_sw128(vb + KV_TILE + off), idesc, 1);
-                    umma_bf16_ts(d, ph, desc_k_sw128(vb + off), idesc, 1);
+                    umma_bf16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc, j > 0 || k != 0);
+                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + KV_TILE + off), idesc, 1);
+                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc, 1);
                 }
                 umma_commit(&o_full[j & 1]);
-                umma_commit(&kv_empty[j & 1]);
+                umma_commit(&kv_empty[j % NSTAGE]);
             }
         }
     } else {
-        // ---- softmax warps 2..9: warp w owns TMEM lane quadrant w % 4 (query rows) and
-        // half hf of each 64-key block and of the 64 output columns; the two warps of
-        // a quadrant exchange row maxima and sums through shared memory.
-        const int qd = warp & 3, hf = (warp - 2) >> 2;
+        // ---- softmax warps 2..5: warp w owns TMEM lane quadrant w % 4; thread = query row
+        const int qd = warp & 3;
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-        const uint32_t bar_id = 1 + qd;  // named barrier of this quadrant's two warps
-        // exp(x) = 2^(x log2 e): p = 2^(s * k - m * k) with k = hd^-1/2 * log2 e, one FMA and
-        // one ex2 per score; m is the running row maximum of the raw scores
-        const float k2 = 0.125f * 1.4426950408889634f;
-        uint64_t o[16];  // this warp's 32 output columns as f32 pairs
-#pragma unroll
-        for (int d = 0; d < 16; d++) o[d] = 0;
-        float m = -INFINITY, l = 0.0f, c_prev = 0.0f;
+        const float k2 = 0.125f * 1.4426950408889634f;  // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
+        float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
-        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
-        auto fold = [&](int jj, float c) {  // O <- O * c + PV_jj, this warp's 32 columns
-            float v[32];
-            tmem_ld32(lb + COL_O + 64u * (jj & 1) + 32 * hf, v);
-            const uint64_t c2 = pack2(c, c);
+        if (nblk > 0) {
+            // this row's Q pair (64 bf16 each, RoPE applied) into TMEM columns COL_Q..
+            uint32_t qw[64];
+            const long long grow = row0 + q0 + r;
+            const long long base = (grow * (heads * HD) + h * HD) / 8;  // in 16-byte units
 #pragma unroll
-            for (int i = 0; i < 16; i++) o[i] = fma2(o[i], c2, pack2(v[2 * i], v[2 * i + 1]));
-        };
+            for (int i = 0; i < 8; i++) {
+                const uint4 a = grow < rows_cap ? q_hi[base + i] : make_uint4(0, 0, 0, 0);
+                const uint4 c = grow < rows_cap ? q_lo[base + i] : make_uint4(0, 0, 0, 0);
+                qw[4 * i] = a.x, qw[4 * i + 1] = a.y, qw[4 * i + 2] = a.z, qw[4 * i + 3] = a.w;
+                qw[32 + 4 * i] = c.x, qw[32 + 4 * i + 1] = c.y, qw[32 + 4 * i + 2] = c.z, qw[32 + 4 * i + 3] = c.w;
+            }
+            tmem_st32u(lb + COL_Q, qw);
+            tmem_st32u(lb + COL_Q + 32, qw + 32);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_ready);
+        }
         for (int j = 0; j < nblk; j++) {
             const int bf = j & 1;
-            const uint32_t sp = lb + COL_S + 64u * bf + 32 * hf;  // this warp's S_j / P_j columns
+            const uint32_t sp = lb + COL_S;  // this row's S_j columns
             // after an expired wait the loop keeps running (work skipped, results unused)
-            // so both warps of the pair reach every pair_sync
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[bf], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN));
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full, j & 1, err, DEV_TIMEOUT_ATTN));
             tc_fence_after();
-            float s[32];
-            tmem_ld32(sp, s);
-            if (j * KB + 32 * hf + 32 > valid) {  // the block holding the last valid key
+            float s[64];
+            tmem_ld64(sp, s);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);  // QK_{j+1} may now overwrite S_j
+            if (j * KB + KB > valid) {  // the block holding the last valid key
 #pragma unroll
-                for (int c = 0; c < 32; c++)
-                    if (j * KB + 32 * hf + c >= valid) s[c] = -INFINITY;
+                for (int c = 0; c < 64; c++)
+                    if (j * KB + c >= valid) s[c] = -INFINITY;
             }
-            float mloc = s[0];
+            float mx[16];  // tree reduction: 16 independent chains, then 4 levels
 #pragma unroll
-            for (int c = 1; c < 32; c++) mloc = fmaxf(mloc, s[c]);
-            red_max[(bf * 2 + hf) * QT + r] = mloc;
-            pair_sync();
-            // the row maximum is finite: key 0 is valid and the running max carries it
-            const float mx = fmaxf(m, fmaxf(mloc, red_max[(bf * 2 + (hf ^ 1)) * QT + r]));
-            const float corr = ex2_approx((m - mx) * k2);  // 0 on the first block (m = -inf)
-            const uint64_t k22 = pack2(k2, k2), nmk = pack2(-mx * k2, -mx * k2);
-            uint64_t sum2 = 0;
+            for (int c = 0; c < 16; c++) mx[c] = fmaxf(fmaxf(s[c], s[c + 16]), fmaxf(s[c + 32], s[c + 48]));
 #pragma unroll
-            for (int c = 0; c < 32; c += 2) {
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                for (int c = 0; c < w; c++) mx[c] = fmaxf(mx[c], mx[c + w]);
+            const float mb = mx[0];  // finite: the block has a valid key
+            const bool raise = (mb - m) * k2 > RESCALE_LOG2;      // always on the first block (m = -inf)
+            const float corr = raise ? ex2_approx((m - mb) * k2) : 1.0f;  // 0 on the first block
+            if (raise) m = mb;
+            const uint64_t k22 = pack2(k2, k2), nmk = pack2(-m * k2, -m * k2);
+            uint64_t sum2[4] = {0, 0, 0, 0};  // four independent packed partial sums
+#pragma unroll
+            for (int c = 0; c < 64; c += 2) {
                 float t0, t1;
                 unpack2(fma2(pack2(s[c], s[c + 1]), k22, nmk), t0, t1);  // masked keys: -inf -> p = 0
                 s[c] = ex2_approx(t0);
                 s[c + 1] = ex2_approx(t1);
-                sum2 = add2(sum2, pack2(s[c], s[c + 1]));
+                sum2[(c >> 1) & 3] = add2(sum2[(c >> 1) & 3], pack2(s[c], s[c + 1]));
             }
             float sa, sb;
-            unpack2(sum2, sa, sb);
-            l = l * corr + (sa + sb);  // this half's partial row sum, at the common running max
-            m = mx;
-            {
-                uint32_t hi[16], lo[16];
+            unpack2(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
+            l = l * corr + (sa + sb);
+            uint32_t hi[32], lo[32];
 #pragma unroll
-                for (int i = 0; i < 16; i++) split_bf16x2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
-                tmem_st16(sp, hi);
-                tmem_st16(sp + 16, lo);
+            for (int i = 0; i < 32; i++) split_bf16x2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
+            if (j > 0) {
+                // PV_{j-1} has read the P buffer and finished O up to block j-1
+                ok = __all_sync(0xffffffffu,
+                                ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, raise)) {  // bring O to the new reference max
+                    float o[64];
+                    tmem_ld64(lb + COL_O, o);
+                    const uint64_t c2 = pack2(corr, corr);
+#pragma unroll
+                    for (int d = 0; d < 64; d += 2) {
+                        uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
+                        unpack2(t, o[d], o[d + 1]);
+                    }
+                    tmem_st32(lb + COL_O, o);
+                    tmem_st32(lb + COL_O + 32, o + 32);
+                }
             }
+            tmem_st32u(lb + COL_P, hi);
+            tmem_st32u(lb + COL_P + 32, lo);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[bf]);
-            if (j >= 1) {
-                ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err,
-                                                             DEV_TIMEOUT_ATTN));
-                tc_fence_after();
-                fold(j - 1, c_prev);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&o_free[(j - 1) & 1]);
-            }
-            c_prev = corr;
         }
-        if (ok && nblk > 0) {
-            ok = __all_sync(0xffffffffu,
-                            mbar_wait(&o_full[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
-            if (ok) {
-                tc_fence_after();
-                fold(nblk - 1, c_prev);
-            }
+        float o[64];
+        if (nblk > 0) {
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err,
+                                                         DEV_TIMEOUT_ATTN));
+            tc_fence_after();
+            tmem_ld64(lb + COL_O, o);
         }
-        red_sum[hf * QT + r] = l;
-        pair_sync();
-        const float ltot = l + red_sum[(hf ^ 1) * QT + r];
-        // ---- context row, this warp's 32 columns (3-term split, or plain fp32 when ctx.hb is null)
+        // ---- context row (3-term split, or plain fp32 when ctx.hb is null)
         if (q0 + r < S) {
-            const float inv = ltot > 0.0f ? 1.0f / ltot : 0.0f;
-            const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD + 32 * hf;
+            const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+            const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD;
 #pragma unroll
-            for (int d = 0; d < 32; d += 4) {
+            for (int d = 0; d < 64; d += 4) {
                 float x[4];
-                unpack2(o[d / 2], x[0], x[1]);
-                unpack2(o[d / 2 + 1], x[2], x[3]);
 #pragma unroll
-                for (int i = 0; i < 4; i++) x[i] *= inv;
+                for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
                 if (ctx.hb) {
                     float hh[4];
-                    uint2 hb, lb;
-                    split3x4(x, hh, hb, lb);
+                    uint2 hb, lb2;
+                    split3x4(x, hh, hb, lb2);
                     *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(hh[0], hh[1], hh[2], hh[3]);
                     *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.hb) + off + d) = hb;
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.lb) + off + d) = lb;
+                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.lb) + off + d) = lb2;
                 } else {
                     *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(x[0], x[1], x[2], x[3]);
                 }
@@ -329,14 +368,16 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
         attr = true;
     }
     const long long W = (long long)heads * HD;
-    const CUtensorMap qh = make_bf16_map(op.q_hi, op.rows_cap, W, W, 64, QT, true);
-    const CUtensorMap ql = make_bf16_map(op.q_lo, op.rows_cap, W, W, 64, QT, true);
     const CUtensorMap kh = make_bf16_map(op.k_hi, op.rows_cap, W, W, 64, KB, true);
     const CUtensorMap kl = make_bf16_map(op.k_lo, op.rows_cap, W, W, 64, KB, true);
     const CUtensorMap vh = make_bf16_map(op.vt_hi, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
     const CUtensorMap vl = make_bf16_map(op.vt_lo, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(qh, ql, kh, kl, vh, vl, S, valid, heads, ctx, err);
+    if ((reinterpret_cast<uintptr_t>(op.q_hi) | reinterpret_cast<uintptr_t>(op.q_lo)) & 15)
+        throw Error(9, "attention: Q must be 16-byte aligned");
+    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(static_cast<const uint4*>(op.q_hi),
+                                                          static_cast<const uint4*>(op.q_lo), op.rows_cap, kh, kl,
+                                                          vh, vl, S, valid, heads, ctx, err);
     N3D_CUDA(cudaGetLastError());
 }
 
