@@ -227,7 +227,7 @@ def main():
     torch.cuda.set_device(local)
     ckpt = checkpoint(rank, world)
     if args.workload == "c4":
-        mode, item_s, n_items = "offline", CLIP_S, args.clips or 64
+        mode, item_s, n_items = "offline", CLIP_S, args.clips or 128
         items = make_clips(rank, n_items, item_s)
         metric, desc = METRIC, (f"C4 offline: {n_items} x 60 s 16 kHz clips per GPU per step, random-init weights "
                                 "(seed 0), clips seeded 1000+")
