@@ -389,7 +389,7 @@ n3d_status n3d_profile_enable(n3d_model* model, int on) {
 }
 
 size_t n3d_profile_read(const n3d_model* model, n3d_kernel_stats* out, size_t cap) {
-    static const char* names[n3d::K_NCLASS] = {"gemm_tf32x3",  "attention",  "layer_norm", "mel",
+    static const char* names[n3d::K_NCLASS] = {"gemm_other",   "attention",  "layer_norm", "mel",
                                                "cache_update", "assemble",   "other",      "gemm_qkv",
                                                "gemm_o",       "gemm_fc1",   "gemm_fc2",   "gemm_head_proj",
                                                "gemm_head_conv", "gemm_head_dense", "gemm_embed"};

@@ -956,7 +956,7 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
 }
 
 // Log-mel of every segment (segment i's samples start at d_audio[base[i]]) into one
-// [groups·sub, n_mels] TF32 pair, then one embedder GEMM over all groups ->
+// split [groups·sub, n_mels] array, then one embedder GEMM over all groups ->
 // [total_groups, hidden] (src/mel.rs:160-225, src/encoder.rs:126-146).
 const float* Model::mel_embed(const float* d_audio, const std::vector<long long>& base,
                               const std::vector<MelSeg>& segs, long long total_groups, long long total_frames) {

@@ -311,22 +311,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     return true;
 }
 
-// -------------------------------------------------------- 3xTF32 operand split
-// x = hi + lo with hi = round-to-nearest TF32(x) and lo = TF32(x - hi); the
-// tensor core then forms hi*hi + hi*lo + lo*hi, which carries ~22 significant
-// bits per product (fp32-grade for this model's GEMMs).
-// Rounding is done with integer ops on the bit pattern (add half an ulp of the
-// 10-bit mantissa, clear the 13 dropped bits: nearest, ties away from zero, the
+// ------------------------------------------------------------ RN-TF32 rounding
+// Round-to-nearest TF32 with integer ops on the bit pattern: add half an ulp of the
+// 10-bit mantissa and clear the 13 dropped bits (nearest, ties away from zero, the
 // same bits as cvt.rna.tf32.f32 for finite inputs).  The conversion instruction
-// issues at a fraction of the integer rate, and the GEMM epilogues that split
-// every output element are bound by it.  Non-finite inputs stay non-finite (a
-// NaN may come out as Inf).
+// issues at a fraction of the integer rate, and the GEMM epilogues that split every
+// output element are bound by it.  Non-finite inputs stay non-finite (a NaN may come
+// out as Inf).
 __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
-}
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-    hi = tf32_rna(x);
-    lo = tf32_rna(__fsub_rn(x, hi));
 }
 
 // ------------------------------------------------ 3-term operand split (GEMMs)

@@ -379,7 +379,7 @@ def frame_duration(hop_length: int = 160, sampling_rate: int = 16000) -> float:
 
 
 def linear(device: int, d_x: int, rows: int, cols: int, d_w: int, out: int, d_bias: int | None, d_y: int) -> None:
-    """tensor::linear on device pointers (3xTF32 tcgen05 GEMM)."""
+    """tensor::linear on device pointers (split TF32 + BF16 tcgen05 GEMM)."""
     _check(lib().n3d_linear(device, d_x, rows, cols, d_w, out, d_bias, d_y))
 
 
