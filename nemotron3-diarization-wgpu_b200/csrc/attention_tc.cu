@@ -53,33 +53,6 @@ constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128, COL_Q = 192, TMEM_COLS = 
 constexpr int DEV_TIMEOUT_ATTN = 5;
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
 
-// f32 pairs in one 64-bit register: Blackwell's packed FMA / add issue two lanes' worth
-// of work per instruction.
-__device__ __forceinline__ uint64_t pack2(float a, float b) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void unpack2(uint64_t r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-// 2^x on the special-function unit (relative error ~2^-22; results below 2^-126 flush to 0).
-__device__ __forceinline__ float ex2_approx(float x) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
     uint32_t r[64];
@@ -99,6 +72,8 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
               "=r"(r[32 * h + 28]), "=r"(r[32 * h + 29]), "=r"(r[32 * h + 30]), "=r"(r[32 * h + 31])
             : "r"(taddr + 32 * h));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    reg_fence32(r);
+    reg_fence32(r + 32);
 #pragma unroll
     for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }

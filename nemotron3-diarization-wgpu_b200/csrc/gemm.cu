@@ -19,7 +19,7 @@
 // Two kernels:
 //   gemm_kernel<BN>        one CTA per 128 x BN tile, persistent (N = 192 head GEMMs,
 //                          small M, the allocation-free entry point)
-//   gemm_pair_kernel<BN,EW> CTA pairs on 256 x 256 tiles with M = 256
+//   gemm_pair_kernel<BN>   CTA pairs on 256 x 256 tiles with M = 256
 //                          `cta_group::2` MMAs: each CTA loads its 128 A rows and half
 //                          the B tile, the leader issues, both own 128 accumulator rows
 // Both: warp 0 TMA, warp 1 TMEM owner + MMA issue, epilogue warps 2.. (TMEM lane
@@ -46,9 +46,54 @@ constexpr int ROW_T = BK * 4;           // bytes per row of the tf32 part (128: 
 constexpr int ROW_H = BK * 2;           // bytes per row of a bf16 part (64: SW64)
 constexpr int ROW_3 = ROW_T + 2 * ROW_H;  // all three parts of one row
 
-__device__ __forceinline__ float gelu_erf(float x) {
-    // 0.5 * x * (1 + erf(x / sqrt(2))), the exact form of src/tensor.rs:113-120
-    return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+// ------------------------------------------------------------------- GELU
+// GELU(x) = 0.5 x (1 + erf(x/√2)) (src/tensor.rs:113-120), branch-free.
+// h = Φ(-|x|) = erfc(|x|/√2)/2 is evaluated as t · 2^(Q(t) - x² log2(e)/2) with
+// t = 1/(1 + C1 |x|): the Chebyshev-fitted erfc form of Numerical Recipes (§6.2) with
+// coefficients fitted for this kernel by fit_gelu.py (relative error of erfc 2.3e-8 on
+// [0, 6.5], ~1 ulp of the result in fp32 on average).  Φ(x) = 1/2 + copysign(1/2 - h, x)
+// rounds like the reference's 1 + erf (cancellation included).  A library erff has two
+// code paths per element, which diverge within a warp.
+constexpr float GELU_C1 = 0.265165031f;   // 0.375 / √2
+constexpr float GELU_KX = -0.721347511f;  // -log2(e) / 2
+__host__ __device__ constexpr float gelu_q(int i) {  // Q(t) = sum gelu_q(i) t^i
+    return i == 0 ? -3.24179554f : i == 1 ? 1.46152258f : i == 2 ? 0.468700767f : i == 3 ? 0.961769581f
+         : i == 4 ? -1.82942355f : i == 5 ? 3.28494f : i == 6 ? -3.62900352f : i == 7 ? 1.90515316f
+         : -0.381863475f;
+}
+
+__device__ __forceinline__ float copysign_bits(float mag, float sgn) {
+    return __uint_as_float((__float_as_uint(mag) & 0x7fffffffu) | (__float_as_uint(sgn) & 0x80000000u));
+}
+
+// Two GELUs with packed arithmetic.
+__device__ __forceinline__ void gelu2(float& a, float& b) {
+    const float ta = rcp_approx(__fmaf_rn(GELU_C1, fabsf(a), 1.0f));
+    const float tb = rcp_approx(__fmaf_rn(GELU_C1, fabsf(b), 1.0f));
+    const uint64_t t = pack2(ta, tb), x = pack2(a, b);
+    uint64_t q = fma2(t, pack2(gelu_q(8), gelu_q(8)), pack2(gelu_q(7), gelu_q(7)));
+#pragma unroll
+    for (int i = 6; i >= 0; i--) q = fma2(q, t, pack2(gelu_q(i), gelu_q(i)));
+    const uint64_t y = fma2(mul2(x, pack2(GELU_KX, GELU_KX)), x, q);
+    float ya, yb;
+    unpack2(y, ya, yb);
+    const uint64_t h = mul2(t, pack2(ex2_approx(ya), ex2_approx(yb)));
+    float da, db;  // 1/2 - h
+    unpack2(fma2(h, pack2(-1.0f, -1.0f), pack2(0.5f, 0.5f)), da, db);
+    const uint64_t phi = add2(pack2(0.5f, 0.5f), pack2(copysign_bits(da, a), copysign_bits(db, b)));
+    unpack2(mul2(x, phi), a, b);
+}
+
+// The same arithmetic for one value (identical results to a half of gelu2).
+__device__ __forceinline__ float gelu1(float x) {
+    const float t = rcp_approx(__fmaf_rn(GELU_C1, fabsf(x), 1.0f));
+    float q = __fmaf_rn(t, gelu_q(8), gelu_q(7));
+#pragma unroll
+    for (int i = 6; i >= 0; i--) q = __fmaf_rn(q, t, gelu_q(i));
+    const float y = __fmaf_rn(__fmul_rn(x, GELU_KX), x, q);
+    const float h = __fmul_rn(t, ex2_approx(y));
+    const float d = __fmaf_rn(h, -1.0f, 0.5f);
+    return __fmul_rn(x, __fadd_rn(0.5f, copysign_bits(d, x)));
 }
 
 // Store 32 consecutive fp32 values of one output row.
@@ -79,7 +124,7 @@ __device__ __forceinline__ void store_row32_bf16(uint16_t* dst, const uint32_t* 
 // Epilogue value of accumulator column i: bias, activation.
 __device__ __forceinline__ float epi_value(int mode, float acc, float bias) {
     float x = __fadd_rn(acc, bias);
-    if (mode == EPI_GELU_SPLIT) x = gelu_erf(x);
+    if (mode == EPI_GELU_SPLIT) x = gelu1(x);
     if (mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
     return x;
 }
@@ -168,6 +213,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  "r"(y), "r"(smem_u32(src))
                  : "memory");
 }
+// Element-wise add of the box into global memory (the L2 performs the read-modify-write).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -191,13 +242,18 @@ __device__ __forceinline__ void stage_begin(int lane) {
     if (lane == 0) bulk_wait_read0();
     __syncwarp();
 }
-// Make the staged boxes visible to the TMA unit and store them (up to three maps).
+// Make the staged boxes visible to the TMA unit and store them (up to three maps);
+// `add0`: the first box is added into its destination instead of stored.
 __device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, const void* b0, const CUtensorMap* m1,
-                                            const void* b1, const CUtensorMap* m2, const void* b2, int x, int y) {
+                                            const void* b1, const CUtensorMap* m2, const void* b2, int x, int y,
+                                            bool add0 = false) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(m0, b0, x, y);
+        if (add0)
+            tma_reduce_add_2d(m0, b0, x, y);
+        else
+            tma_store_2d(m0, b0, x, y);
         if (m1) tma_store_2d(m1, b1, x, y);
         if (m2) tma_store_2d(m2, b2, x, y);
         bulk_commit();
@@ -210,10 +266,11 @@ __device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, con
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
                                                   int lane, uint8_t* stg, int c_begin = 0, int c_end = BN) {
+    const int mode = epi.mode;
     const int rowbase = m0 + q * 32;
     if (rowbase >= M) return;  // whole warp past the end: nothing to load or store
     const int r = rowbase + lane;
-    if (epi.mode == EPI_QKV_ATTN) {
+    if (mode == EPI_QKV_ATTN) {
         uint8_t* bhi = stg;
         uint8_t* blo = stg + 4096;
         for (int c = c_begin; c < c_end; c += 64) {
@@ -270,7 +327,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
         }
         return;
     }
-    const bool split = epi.mode != EPI_STORE;
+    const bool split = mode != EPI_STORE;
     uint8_t* bhi = stg;          // 4 KB fp32 box
     uint8_t* bhb = stg + 4096;   // 2 KB bf16 box
     uint8_t* blb = stg + 6144;   // 2 KB bf16 box
@@ -281,8 +338,16 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
         if (col0 >= N) break;
         float bias[32];
         load_bias32(epi.bias, col0, N, bias);
+        if (mode == EPI_GELU_SPLIT) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = epi_value(epi.mode, v[i], bias[i]);
+            for (int i = 0; i < 32; i += 2) {
+                unpack2(add2(pack2(v[i], v[i + 1]), pack2(bias[i], bias[i + 1])), v[i], v[i + 1]);
+                gelu2(v[i], v[i + 1]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = epi_value(mode, v[i], bias[i]);
+        }
         uint32_t hb[16], lb[16];
         if (split) {
 #pragma unroll
@@ -295,7 +360,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             stage_rows_bf16(blb, lane, lb);
         }
         stage_issue(lane, &epi.map_out, bhi, split ? &epi.map_out2 : nullptr, bhb, split ? &epi.map_out3 : nullptr,
-                    blb, col0, rowbase);
+                    blb, col0, rowbase, epi.reduce != 0);
     }
 }
 
@@ -484,27 +549,25 @@ __global__ void __launch_bounds__(192, 1)
 // one-CTA kernel for the same work; its TMEM receives output rows m0 + 128 r, which
 // its own epilogue warps store.  Barriers: full[s] lives in the leader (both CTAs'
 // loads complete on it), empty[s] and acc_full[b] in both (arrived by the leader's
-// multicast commits), acc_empty[b] in the leader (2 EW epilogue warps).  With EW = 8,
-// warps w and w + 4 share TMEM lane quadrant w % 4 and take half the columns each.
-template <int BN, int EW>
+// multicast commits), acc_empty[b] in the leader (the 8 epilogue warps of the pair).
+template <int BN>
 struct PairCfg {
     static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_3;
-    static constexpr int STAGING = EW * 8192;
-    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int STAGING = 4 * 8192;
+    static constexpr int THREADS = 192;
     static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 1024 + STAGING;
     static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
-    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
     static_assert(STAGES >= 2, "need two pipeline stages");
 };
 
-template <int BN, int EW>
-__global__ void __launch_bounds__(64 + 32 * EW, 1)
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
                      const __grid_constant__ Epi epi, int* err) {
-    using Cfg = PairCfg<BN, EW>;
+    using Cfg = PairCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
@@ -528,7 +591,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 2 * EW);
+            mbar_init(&acc_empty[b], 8);
         }
         mbar_fence_init();
         for (int i = 0; i < 6; i++) tma_prefetch_desc(&maps.m[i]);
@@ -585,8 +648,7 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             }
         }
     } else {
-        const int q = warp & 3, part = (warp - 2) >> 2;
-        constexpr int CW = BN / (EW / 4);  // columns per epilogue warp
+        const int q = warp & 3;
         const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
         int it = 0;
         for (int t = cid; t < tiles; t += ncl, it++) {
@@ -599,9 +661,8 @@ __global__ void __launch_bounds__(64 + 32 * EW, 1)
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
             if (epi.tma)
                 epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, part * CW,
-                                      part * CW + CW);
-            else if (part == 0)  // direct stores: one warp per quadrant takes the whole tile
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+            else  // direct stores
                 epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
             tc_fence_before();
             __syncwarp();
@@ -714,10 +775,10 @@ void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_p
     N3D_CUDA(cudaGetLastError());
 }
 
-template <int BN, int EW>
+template <int BN>
 void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
                  const Epi& epi, int* err) {
-    using Cfg = PairCfg<BN, EW>;
+    using Cfg = PairCfg<BN>;
     static int max_clusters = 0;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -731,16 +792,16 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     if (!max_clusters) {
-        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cfg::SMEM));
         cfg.gridDim = dim3(2 * (sm_count() / 2));
-        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN, EW>, &cfg));
+        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN>, &cfg));
         if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
     }
     const Maps6 maps = operand_maps(A, B, BM, BN / 2, true);
     const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
     cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
-    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EW>, maps, M, N, K, kb_per_tap, epi, err));
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err));
 }
 
 void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi& epi, int bn) {
@@ -748,6 +809,8 @@ void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi&
     if (!A.hi || !A.hb || !A.lb || !B.hi || !B.hb || !B.lb) throw Error(13, "GEMM operand without all three parts");
     if (epi.mode == EPI_DENSE_OUT && (bn != 192 || epi.n2 > 8 || epi.tma))
         throw Error(9, "the fused dense+out_proj epilogue needs N == 192, at most 8 outputs and direct stores");
+    if (epi.reduce && (epi.mode != EPI_STORE || !epi.tma))
+        throw Error(9, "the reduce-add epilogue stores plain fp32 through TMA");
     if (epi.mode == EPI_QKV_ATTN && (bn % 64 || !epi.tma))
         throw Error(9, "the attention-operand epilogue needs 64-column chunks and TMA stores");
 }
@@ -787,12 +850,7 @@ void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         case 128: launch_one<128>(s, operand_maps(A, B, BM, 128, true), M, N, K, kb_per_tap, epi, err); break;
         case 192: launch_one<192>(s, operand_maps(A, B, BM, 192, true), M, N, K, kb_per_tap, epi, err); break;
         default:
-            // the erf-GELU + split epilogue is latency bound on one warp per sub-partition:
-            // 8 epilogue warps; the lighter epilogues lose more to the smaller pipeline
-            if (epi.tma && epi.mode == EPI_GELU_SPLIT)
-                launch_pair<256, 8>(s, A, B, M, N, K, kb_per_tap, epi, err);
-            else
-                launch_pair<256, 4>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            launch_pair<256>(s, A, B, M, N, K, kb_per_tap, epi, err);
             break;
     }
 }

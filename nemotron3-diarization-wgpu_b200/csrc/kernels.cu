@@ -26,9 +26,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 // x_out may alias x (in-place residual add): each lane reads its elements of x before
 // writing them, so neither is __restrict__.
 template <int VPL>
-__global__ void layer_norm_kernel(const float* x, long long rows, const float* __restrict__ w,
-                                  const float* __restrict__ b, Split3Out out, const float* __restrict__ delta = nullptr,
-                                  float* x_out = nullptr) {
+__global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
+                                  const float* __restrict__ b, Split3Out out) {
     constexpr int COLS = VPL * 32;
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -42,19 +41,6 @@ __global__ void layer_norm_kernel(const float* x, long long rows, const float* _
         v[i + 1] = t.y;
         v[i + 2] = t.z;
         v[i + 3] = t.w;
-    }
-    if (delta) {  // residual stream: x += delta, exactly the reference's x1[i] += out[i]
-        const float* dsrc = delta + row * COLS;
-#pragma unroll
-        for (int i = 0; i < VPL; i += 4) {
-            const int c = (i / 4) * 128 + lane * 4;
-            const float4 t = *reinterpret_cast<const float4*>(dsrc + c);
-            v[i] = __fadd_rn(v[i], t.x);
-            v[i + 1] = __fadd_rn(v[i + 1], t.y);
-            v[i + 2] = __fadd_rn(v[i + 2], t.z);
-            v[i + 3] = __fadd_rn(v[i + 3], t.w);
-            *reinterpret_cast<float4*>(x_out + row * COLS + c) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-        }
     }
     float s = 0.0f;
 #pragma unroll
@@ -367,16 +353,6 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
         layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
-    N3D_CUDA(cudaGetLastError());
-}
-
-void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
-                           const float* b, Split3Out out) {
-    if (rows <= 0) return;
-    if (cols != 512) throw Error(13, "add_layer_norm supports 512 columns");
-    const int warps = 8;
-    const unsigned grid = (unsigned)((rows + warps - 1) / warps);
-    layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out, delta, x);
     N3D_CUDA(cudaGetLastError());
 }
 

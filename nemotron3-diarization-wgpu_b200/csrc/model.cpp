@@ -676,7 +676,6 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     const long long M = (long long)B * S, h = c.hidden;
     float* win = (float*)ws("win", M * h * 4);
     float* x = (float*)ws("x", M * h * 4);
-    float* tmp = (float*)ws("tmp", M * h * 4);
     const Split3Buf n = ws3("n", M, h);  // LayerNorm output, 3-term split
     // attention operands as bfloat16 pairs: Q, K [M, h]; V^T [h, M] (column = global row)
     AttnOperands ao;
@@ -706,10 +705,11 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     e.head_dim = (int)(h / c.heads);
     e.q_cols = (int)h;
     e.k_cols = (int)h;
-    Epi eo;  // o_proj / fc2: acc + bias -> tmp (added into x by the next LayerNorm)
+    Epi eo;  // o_proj / fc2: x += acc + bias, the residual adds of src/encoder.rs:262-276
     eo.mode = EPI_STORE;
     eo.tma = 1;
-    eo.map_out = make_store_map(tmp, M, h, h);
+    eo.reduce = 1;
+    eo.map_out = make_store_map(x, M, h, h);
     Epi e1;  // fc1: GELU(acc + bias) -> 3-term split
     e1.mode = EPI_GELU_SPLIT;
     e1.tma = 1;
@@ -717,17 +717,14 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     e1.map_out2 = make_store_map_bf16(f.hb, M, c.inter, c.inter);
     e1.map_out3 = make_store_map_bf16(f.lb, M, c.inter, c.inter);
 
-    const double ln_bytes = (double)M * h * 4 * 5;  // read x + delta, write x, hi, hb, lb
+    const double ln_bytes = (double)M * h * 12;  // read x, write hi, hb, lb
     prof_begin();
     launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, Split3Out{x, nullptr, nullptr});
     prof_end(K_LN, 0, (double)M * h * 8);
     for (int l = 0; l < c.layers; l++) {
         const DevLayer& L = layers_[l];
         prof_begin();
-        if (l == 0)
-            launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out());
-        else
-            launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln1_w, L.ln1_b, n.out());
+        launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out());
         prof_end(K_LN, 0, ln_bytes);
         prof_begin();
         gemm_split3(stream_, n.op(), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
@@ -740,7 +737,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         gemm_split3(stream_, ctx.op(), L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
         prof_end(K_GEMM_O, 2.0 * M * h * h, 0);
         prof_begin();
-        launch_add_layer_norm(stream_, x, tmp, M, (int)h, L.ln2_w, L.ln2_b, n.out());
+        launch_layer_norm(stream_, x, M, (int)h, L.ln2_w, L.ln2_b, n.out());
         prof_end(K_LN, 0, ln_bytes);
         e1.bias = L.fc1.bias;
         prof_begin();
@@ -752,7 +749,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         prof_end(K_GEMM_FC2, 2.0 * M * h * c.inter, 0);
     }
     prof_begin();
-    launch_add_layer_norm(stream_, x, tmp, M, (int)h, fin_ln_w_, fin_ln_b_, n.out());
+    launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, n.out());
     prof_end(K_LN, 0, ln_bytes);
     if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, Split3Out{enc_plain, nullptr, nullptr});
     (void)d_seq_len;
@@ -824,7 +821,7 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
     for (int i = 0; i < nclips; i++)
         plans[i] = mode == 3 ? plan_offline(c, lens[i]) : plan_streaming(c, lens[i], mode);
     if (plans_out) *plans_out = plans;
-    const int ns = c.num_speakers, h = c.hidden, sub = c.sub;
+    const int ns = c.num_speakers, h = c.hidden;
     const int B_CAP = 128;
 
     for (int c0 = 0; c0 < nclips; c0 += B_CAP) {

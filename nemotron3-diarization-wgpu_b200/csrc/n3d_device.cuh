@@ -145,6 +145,21 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
+// The registers of a tcgen05.ld are valid only after tcgen05.wait::ld.  These empty
+// volatile statements (ordered after the wait like every volatile asm) redefine them,
+// so no use of the loaded values can be scheduled above the wait.
+__device__ __forceinline__ void reg_fence32(uint32_t* r) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]));
+}
+__device__ __forceinline__ void reg_fence16(uint32_t* r) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
 // 32 consecutive TMEM columns of this thread's lane (32x32b shape, x32).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
     uint32_t r[32];
@@ -159,8 +174,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
           "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    reg_fence32(r);
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+// 16 consecutive TMEM columns of this thread's lane (32x32b.x16), waited for.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    reg_fence16(r);
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
 // MMA with the A operand in TMEM (K-major, one 32-bit element per column).
@@ -322,6 +351,45 @@ __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 
+// ------------------------------------------------------- packed f32 pairs
+// Two f32 in one 64-bit register: Blackwell's packed FMA / add / multiply issue two
+// lanes' worth of work per instruction, each half rounded as the scalar operation.
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// 2^x on the special-function unit (relative error ~2^-22; results below 2^-126 flush to 0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+// 1/x on the special-function unit (within 1 ulp).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 // ------------------------------------------------ 3-term operand split (GEMMs)
 // Every GEMM operand x is stored as hi = RN-TF32(x) (an fp32 array read by kind::tf32
 // MMAs) plus bf16 copies hb = RN-bf16(hi) and lb = RN-bf16(x - hi) (read by kind::f16
@@ -338,7 +406,9 @@ __device__ __forceinline__ void split3x2(float a, float b, float& ha, float& hb,
     ha = tf32_rna(a);
     hb = tf32_rna(b);
     hbf = bf16x2_rn(ha, hb);
-    lbf = bf16x2_rn(__fsub_rn(a, ha), __fsub_rn(b, hb));
+    float la, lb;  // a - ha, b - hb in one packed FMA (exact: hi holds the leading bits)
+    unpack2(fma2(pack2(ha, hb), pack2(-1.0f, -1.0f), pack2(a, b)), la, lb);
+    lbf = bf16x2_rn(la, lb);
 }
 // One element: hi, and its hb / lb bf16 bits (one conversion for both).
 __device__ __forceinline__ void split3x1(float x, float& h, uint16_t& hb, uint16_t& lb) {

@@ -59,6 +59,9 @@ struct Epi {
     // map_out2 and map_k_* with box 64 x 32 and the 128-byte swizzle, map_vt_* over
     // V^T [heads*64, rows] with box 32 x 64 and no swizzle.
     int tma = 0;
+    // EPI_STORE through TMA only: add the tile into map_out's fp32 destination
+    // (cp.reduce.async.bulk.tensor .add; each element is added exactly once).
+    int reduce = 0;
     CUtensorMap map_out, map_out2, map_out3, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
@@ -103,9 +106,6 @@ struct Split3Out {
 };
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
                        Split3Out out);
-// Residual add fused into the next LayerNorm: x += delta (in place), out = LN(x).
-void launch_add_layer_norm(cudaStream_t s, float* x, const float* delta, long long rows, int cols, const float* w,
-                           const float* b, Split3Out out);
 // SIMT attention (head_dim 128 kernel probes): plain fp32 context.
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
                       int head_dim, float* ctx);
