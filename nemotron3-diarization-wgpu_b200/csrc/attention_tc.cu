@@ -14,13 +14,14 @@
 // two CTAs share an SM.
 //
 // CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM:
-//   warp 0      TMA: per block of 64 keys the K pair and the V^T pair into a
-//               3-stage ring (two blocks of prefetch hide the load latency)
+//   warp 0      TMA: the CTA's Q pair into ring slot 2, then per block of 64 keys
+//               the K pair and the V^T pair into a 3-stage ring (two blocks of
+//               prefetch hide the load latency; slot 2 once Q has moved to TMEM)
 //   warp 1      TMEM owner; one thread issues S_j = Q K_j^T as soon as the softmax
 //               has read S_{j-1}, and O += P_j V_j; both MMAs take their A operand
 //               (Q, P) from TMEM, so only K / V^T are read from shared memory
 //   warps 2..5  softmax, one thread per query row (TMEM lane): first the row's Q
-//               pair into TMEM; per block the row's 64 scores, exp as 2^x on the
+//               pair from shared memory into TMEM; per block the row's 64 scores, exp as 2^x on the
 //               special-function unit after one FMA folds the 1/sqrt(hd) scale,
 //               log2 e and the reference max together; then, once PV_{j-1} has
 //               read the P buffer, P_j as bf16 pairs.
@@ -28,6 +29,8 @@
 // a block's max exceeds it by more than 2^8 in the exponent; only then is O
 // (in TMEM) multiplied by the correction, after PV_{j-1} has completed and before
 // P_j is released.  P values stay below 2^8; O / l is unchanged mathematically.
+// Context rows leave through shared memory (the ring, free once the last PV is done)
+// and TMA stores, a warp's 32 rows at a time.
 // TMEM (256 columns): S 0..63, P 64..127 (hi 64.., lo 96..), O 128..191,
 // Q 192..255 (hi 192.., lo 224..); bf16 operands two per 32-bit column.
 // Barriers with a phase per key block
@@ -90,11 +93,16 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
         : "memory");
 }
 
+struct AttnMaps {
+    CUtensorMap qh, ql;      // Q pair [rows, heads*64] bf16, box 64 x 128, 128-byte swizzle
+    CUtensorMap kh, kl;      // K pair, box 64 x 64
+    CUtensorMap vh, vl;      // V^T pair [heads*64, rows], box 64 x 64
+    CUtensorMap ch, cb, cl;  // context hi (fp32, box 32 x 32) and hb / lb (bf16, box 64 x 32)
+};
+
 __global__ void __launch_bounds__(THREADS, 2)
-    attention_tc_kernel(const uint4* __restrict__ q_hi, const uint4* __restrict__ q_lo, long long rows_cap,
-                        const __grid_constant__ CUtensorMap tKh, const __grid_constant__ CUtensorMap tKl,
-                        const __grid_constant__ CUtensorMap tVh, const __grid_constant__ CUtensorMap tVl, int S,
-                        const int* __restrict__ valid_arr, int heads, Split3Out ctx, int* err) {
+    attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
+                        Split3Out ctx, int ctx_tma, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stages = smem;
@@ -106,7 +114,9 @@ __global__ void __launch_bounds__(THREADS, 2)
     uint64_t* s_free = bars + 8;    // 1: phase j = S_j read by the softmax (4 warps)
     uint64_t* p_full = bars + 9;    // 2: P_j in TMEM, any rescale of O done (4 warps)
     uint64_t* o_full = bars + 11;   // 2: PV_j committed (j % 2); a waiter for PV_j has always seen PV_{j-2}
+    uint64_t* q_full = bars + 13;   // 1: the Q pair has landed in ring slot 2
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+    uint8_t* q_smem = stages + 2 * STAGE_BYTES;  // Q hi [128 rows x 128 B], Q lo 16 KB further
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
@@ -116,6 +126,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 
     if (warp == 0 && lane == 0) {
         mbar_init(q_ready, 4);
+        mbar_init(q_full, 1);
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
         for (int i = 0; i < NSTAGE; i++) {
@@ -135,18 +146,29 @@ __global__ void __launch_bounds__(THREADS, 2)
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
+            // Q rows past S belong to the next sequence (or lie past the buffer: zeros);
+            // their context is never stored
+            mbar_arrive_expect_tx(q_full, 2 * QT * 128);
+            tma_load_2d(q_smem, &maps.qh, q_full, h * HD, row0 + q0);
+            tma_load_2d(q_smem + QT * 128, &maps.ql, q_full, h * HD, row0 + q0);
             int issued = 0;
             for (int j = 0; j < nblk; j++) {
                 const int st = j % NSTAGE;
-                if (j >= NSTAGE && !mbar_wait(&kv_empty[st], ((j / NSTAGE) - 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
+                bool ok = true;
+                if (j >= NSTAGE)
+                    ok = mbar_wait(&kv_empty[st], ((j / NSTAGE) - 1) & 1, err, DEV_TIMEOUT_ATTN);
+                else if (st == 2)  // slot 2 held Q until the softmax warps copied it to TMEM
+                    ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
+                if (!ok) break;
                 uint8_t* sb = stages + st * STAGE_BYTES;
                 mbar_arrive_expect_tx(&kv_full[st], STAGE_BYTES);
-                tma_load_2d(sb, &tKh, &kv_full[st], h * HD, row0 + j * KB);
-                tma_load_2d(sb + KV_TILE, &tKl, &kv_full[st], h * HD, row0 + j * KB);
-                tma_load_2d(sb + 2 * KV_TILE, &tVh, &kv_full[st], row0 + j * KB, h * HD);
-                tma_load_2d(sb + 3 * KV_TILE, &tVl, &kv_full[st], row0 + j * KB, h * HD);
+                tma_load_2d(sb, &maps.kh, &kv_full[st], h * HD, row0 + j * KB);
+                tma_load_2d(sb + KV_TILE, &maps.kl, &kv_full[st], h * HD, row0 + j * KB);
+                tma_load_2d(sb + 2 * KV_TILE, &maps.vh, &kv_full[st], row0 + j * KB, h * HD);
+                tma_load_2d(sb + 3 * KV_TILE, &maps.vl, &kv_full[st], row0 + j * KB, h * HD);
                 issued = j + 1;
             }
+            mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);  // landed before the CTA may exit
             // the last loads of each stage have landed before the CTA may exit
             // (already true unless a wait above or in the MMA warp expired)
             for (int j = max(0, issued - NSTAGE); j < issued; j++)
@@ -210,14 +232,15 @@ __global__ void __launch_bounds__(THREADS, 2)
         float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
         if (nblk > 0) {
-            // this row's Q pair (64 bf16 each, RoPE applied) into TMEM columns COL_Q..
+            // this row's Q pair (64 bf16 each, RoPE applied) from ring slot 2 (128-byte
+            // rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
+            ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN));
             uint32_t qw[64];
-            const long long grow = row0 + q0 + r;
-            const long long base = (grow * (heads * HD) + h * HD) / 8;  // in 16-byte units
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                const uint4 a = grow < rows_cap ? q_hi[base + i] : make_uint4(0, 0, 0, 0);
-                const uint4 c = grow < rows_cap ? q_lo[base + i] : make_uint4(0, 0, 0, 0);
+                const int o = r * 128 + ((i ^ (r & 7)) << 4);
+                const uint4 a = *reinterpret_cast<const uint4*>(q_smem + o);
+                const uint4 c = *reinterpret_cast<const uint4*>(q_smem + QT * 128 + o);
                 qw[4 * i] = a.x, qw[4 * i + 1] = a.y, qw[4 * i + 2] = a.z, qw[4 * i + 3] = a.w;
                 qw[32 + 4 * i] = c.x, qw[32 + 4 * i + 1] = c.y, qw[32 + 4 * i + 2] = c.z, qw[32 + 4 * i + 3] = c.w;
             }
@@ -303,8 +326,44 @@ __global__ void __launch_bounds__(THREADS, 2)
             tc_fence_after();
             tmem_ld64(lb + COL_O, o);
         }
-        // ---- context row (3-term split, or plain fp32 when ctx.hb is null)
-        if (q0 + r < S) {
+        // ---- context rows: the 3-term split through TMA stores when all 32 rows of the
+        // warp belong to this sequence; otherwise (and for a plain fp32 context) per row
+        const int wrow0 = q0 + qd * 32;
+        if (ctx_tma && wrow0 + 32 <= S) {
+            // staging in ring slots 0..1 (every load has been consumed by the last PV):
+            // per warp 16 KB = hi cols 0..31 | hi cols 32..63 | hb | lb, 128-byte rows
+            uint8_t* stg = stages + (warp - 2) * 16384;
+            const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+            uint32_t hbw[32], lbw[32];
+#pragma unroll
+            for (int d = 0; d < 64; d += 2) {
+                const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
+                split3x2(x0, x1, o[d], o[d + 1], hbw[d / 2], lbw[d / 2]);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int sw = ((i ^ (lane & 7)) << 4) + lane * 128;
+                *reinterpret_cast<float4*>(stg + sw) = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                *reinterpret_cast<float4*>(stg + 4096 + sw) =
+                    make_float4(o[32 + 4 * i], o[32 + 4 * i + 1], o[32 + 4 * i + 2], o[32 + 4 * i + 3]);
+                *reinterpret_cast<uint4*>(stg + 8192 + sw) =
+                    make_uint4(hbw[4 * i], hbw[4 * i + 1], hbw[4 * i + 2], hbw[4 * i + 3]);
+                *reinterpret_cast<uint4*>(stg + 12288 + sw) =
+                    make_uint4(lbw[4 * i], lbw[4 * i + 1], lbw[4 * i + 2], lbw[4 * i + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                const int y = row0 + wrow0;
+                tma_store_2d(&maps.ch, stg, h * HD, y);
+                tma_store_2d(&maps.ch, stg + 4096, h * HD + 32, y);
+                tma_store_2d(&maps.cb, stg + 8192, h * HD, y);
+                tma_store_2d(&maps.cl, stg + 12288, h * HD, y);
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read before exit
+            }
+            __syncwarp();
+        } else if (q0 + r < S) {
             const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
             const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD;
 #pragma unroll
@@ -342,17 +401,24 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
         N3D_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr = true;
     }
-    const long long W = (long long)heads * HD;
-    const CUtensorMap kh = make_bf16_map(op.k_hi, op.rows_cap, W, W, 64, KB, true);
-    const CUtensorMap kl = make_bf16_map(op.k_lo, op.rows_cap, W, W, 64, KB, true);
-    const CUtensorMap vh = make_bf16_map(op.vt_hi, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
-    const CUtensorMap vl = make_bf16_map(op.vt_lo, W, (long long)seqs * S, op.vt_ld, 64, HD, true);
+    const long long W = (long long)heads * HD, rows = (long long)seqs * S;
+    AttnMaps m;
+    m.qh = make_bf16_map(op.q_hi, op.rows_cap, W, W, 64, QT, true);
+    m.ql = make_bf16_map(op.q_lo, op.rows_cap, W, W, 64, QT, true);
+    m.kh = make_bf16_map(op.k_hi, op.rows_cap, W, W, 64, KB, true);
+    m.kl = make_bf16_map(op.k_lo, op.rows_cap, W, W, 64, KB, true);
+    m.vh = make_bf16_map(op.vt_hi, W, rows, op.vt_ld, 64, HD, true);
+    m.vl = make_bf16_map(op.vt_lo, W, rows, op.vt_ld, 64, HD, true);
+    const int ctx_tma = ctx.hb != nullptr;
+    if (ctx_tma) {
+        m.ch = make_store_map(ctx.hi, rows, W, W);
+        m.cb = make_bf16_map(ctx.hb, rows, W, W, 64, 32, true);
+        m.cl = make_bf16_map(ctx.lb, rows, W, W, 64, 32, true);
+    } else {
+        m.ch = m.cb = m.cl = m.qh;  // unused
+    }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    if ((reinterpret_cast<uintptr_t>(op.q_hi) | reinterpret_cast<uintptr_t>(op.q_lo)) & 15)
-        throw Error(9, "attention: Q must be 16-byte aligned");
-    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(static_cast<const uint4*>(op.q_hi),
-                                                          static_cast<const uint4*>(op.q_lo), op.rows_cap, kh, kl,
-                                                          vh, vl, S, valid, heads, ctx, err);
+    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(m, S, valid, heads, ctx, ctx_tma, err);
     N3D_CUDA(cudaGetLastError());
 }
 

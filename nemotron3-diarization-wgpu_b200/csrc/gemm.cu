@@ -208,11 +208,6 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m
 }
 
 // ------------------------------------------------------- TMA-store epilogue
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
-                 "r"(y), "r"(smem_u32(src))
-                 : "memory");
-}
 // Element-wise add of the box into global memory (the L2 performs the read-modify-write).
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int x, int y) {
     asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
