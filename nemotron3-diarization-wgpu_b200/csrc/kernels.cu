@@ -163,65 +163,140 @@ __global__ void __launch_bounds__(128) attention_kernel(const float* __restrict_
 }
 
 // ------------------------------------------------------------------- log-mel
-// One CTA of 256 threads per frame: preemphasis on the fly, centred 400-tap
-// Hann in the 512 frame, radix-2 FFT in shared memory, power, sparse slaney
-// filterbank, ln(x + 2^-24) (src/mel.rs:160-225).  The butterflies, twiddles
-// and accumulation order are the CPU restatement's exactly, and every
-// operation is explicitly rounded, so the spectrum is bit-identical to it.
+// One warp per frame, 8 frames per CTA: preemphasis on the fly, centred 400-tap
+// Hann in the 512 frame, radix-2 DIT FFT in registers, power, sparse slaney
+// filterbank, ln(x + 2^-24) (src/mel.rs:160-225).  The butterflies (pairs,
+// twiddles, operation order) and the filterbank accumulation order are the CPU
+// restatement's exactly and every operation is explicitly rounded, so the spectrum
+// is bit-identical to it; only the assignment of butterflies to lanes is this
+// kernel's own.
+//   layout A: lane L holds bit-reversed positions 16L + s (s = 0..15): stages with
+//             half 1, 2, 4, 8 in registers; half 16 pairs lanes L and L ^ 1 (shuffles)
+//   layout B: lane L holds positions L + 32t (t = 0..15), reached through shared
+//             memory (padded: no bank conflicts either way): halves 32..256 in registers
 constexpr int NFFT = 512;
 constexpr int NBINS = NFFT / 2 + 1;
+constexpr int MEL_WARPS = 8;
+constexpr int MEL_PAD = NFFT + NFFT / 32;  // padded index p + p / 32
 
-__global__ void __launch_bounds__(256) mel_kernel(const float* __restrict__ audio, const long long* __restrict__ f_base,
-                                                  const int* __restrict__ f_meta, const float* __restrict__ window,
-                                                  const float* __restrict__ twiddle, const float* __restrict__ filters,
-                                                  const int* __restrict__ filt_lo, const int* __restrict__ filt_hi,
-                                                  float preemph, Split3Out mel, float* __restrict__ mel_plain,
-                                                  const long long* __restrict__ f_out) {
-    __shared__ float re[NFFT], im[NFFT], pw[NBINS];
-    const long long f = blockIdx.x;
+// One radix-2 butterfly with twiddle (wr, wi): (u, x) -> (u + x w, u - x w).
+__device__ __forceinline__ void butterfly(float& ur, float& ui, float& xr, float& xi, float wr, float wi) {
+    const float vr = __fsub_rn(__fmul_rn(xr, wr), __fmul_rn(xi, wi));
+    const float vi = __fadd_rn(__fmul_rn(xr, wi), __fmul_rn(xi, wr));
+    xr = __fsub_rn(ur, vr);
+    xi = __fsub_rn(ui, vi);
+    ur = __fadd_rn(ur, vr);
+    ui = __fadd_rn(ui, vi);
+}
+
+__global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
+    const float* __restrict__ audio, const long long* __restrict__ f_base, const int* __restrict__ f_meta,
+    long long n_frames, const float* __restrict__ window, const float* __restrict__ twiddle,
+    const float* __restrict__ filters, const int* __restrict__ filt_lo, const int* __restrict__ filt_hi, float preemph,
+    Split3Out mel, float* __restrict__ mel_plain, const long long* __restrict__ f_out) {
+    __shared__ float tw_s[NFFT];  // (cos, sin) pairs of the 256 twiddles
+    __shared__ float win_s[NFFT];
+    __shared__ float xs[MEL_WARPS][2][MEL_PAD];
+    for (int i = threadIdx.x; i < NFFT; i += blockDim.x) {
+        tw_s[i] = twiddle[i];
+        win_s[i] = window[i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long f = (long long)blockIdx.x * MEL_WARPS + warp;
+    if (f >= n_frames) return;
     const long long base = f_base[f];
     const int p0 = f_meta[2 * f], n = f_meta[2 * f + 1];
-    const int tid = threadIdx.x;
-    for (int j = tid; j < NFFT; j += 256) {
+    float re[16], im[16];
+    // ---- input at bit-reversed positions (layout A): position 16L + s <- sample
+    // j = brev9(16L + s) = brev4(s) * 32 + brev5(L)
+    const int jl = __brev(lane) >> 27;
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int j = ((__brev(s) >> 28) << 5) | jl;
         const int p = p0 + j;
         float x = 0.0f;
         if (p >= 0 && p < n) {
             const float cur = audio[base + p];
             x = p >= 1 ? __fsub_rn(cur, __fmul_rn(preemph, audio[base + p - 1])) : cur;
         }
-        const int r = __brev(j) >> (32 - 9);
-        re[r] = __fmul_rn(x, window[j]);
-        im[r] = 0.0f;
+        re[s] = __fmul_rn(x, win_s[j]);
+        im[s] = 0.0f;
     }
-    __syncthreads();
-    for (int half = 1; half < NFFT; half <<= 1) {
-        const int len = half * 2, step = NFFT / len;
-        const int b = tid;  // 256 butterflies per stage
-        const int j = b % half, i = (b / half) * len + j;
-        const float wr = twiddle[2 * (j * step)], wi = twiddle[2 * (j * step) + 1];
-        const float xr = re[i + half], xi = im[i + half];
-        const float vr = __fsub_rn(__fmul_rn(xr, wr), __fmul_rn(xi, wi));
-        const float vi = __fadd_rn(__fmul_rn(xr, wi), __fmul_rn(xi, wr));
-        const float ur = re[i], ui = im[i];
-        re[i] = __fadd_rn(ur, vr);
-        im[i] = __fadd_rn(ui, vi);
-        re[i + half] = __fsub_rn(ur, vr);
-        im[i + half] = __fsub_rn(ui, vi);
-        __syncthreads();
+    // ---- halves 1, 2, 4, 8 inside the lane: pair (s, s + h), twiddle (s % h) * 256 / h
+#pragma unroll
+    for (int h = 1; h <= 8; h <<= 1) {
+#pragma unroll
+        for (int s = 0; s < 16; s++) {
+            if (s & h) continue;
+            const int t = (s & (h - 1)) * (NFFT / 2 / h);
+            butterfly(re[s], im[s], re[s + h], im[s + h], tw_s[2 * t], tw_s[2 * t + 1]);
+        }
     }
-    for (int k = tid; k < NBINS; k += 256) pw[k] = __fadd_rn(__fmul_rn(re[k], re[k]), __fmul_rn(im[k], im[k]));
-    __syncthreads();
-    if (tid < 128) {
-        const int m = tid;
+    // ---- half 16: positions 16L + s pair with lane L ^ 1; twiddle s * 16.  Both
+    // lanes form v = x w from the upper value with the same operations.
+    {
+        const bool upper = lane & 1;
+#pragma unroll
+        for (int s = 0; s < 16; s++) {
+            const float pr = __shfl_xor_sync(0xffffffffu, re[s], 1), pi = __shfl_xor_sync(0xffffffffu, im[s], 1);
+            float ur = upper ? pr : re[s], ui = upper ? pi : im[s];
+            float xr = upper ? re[s] : pr, xi = upper ? im[s] : pi;
+            butterfly(ur, ui, xr, xi, tw_s[2 * (s * 16)], tw_s[2 * (s * 16) + 1]);
+            re[s] = upper ? xr : ur;
+            im[s] = upper ? xi : ui;
+        }
+    }
+    // ---- layout A -> B through shared memory
+    float* xr_s = xs[warp][0];
+    float* xi_s = xs[warp][1];
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int p = 16 * lane + s;
+        xr_s[p + (p >> 5)] = re[s];
+        xi_s[p + (p >> 5)] = im[s];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+        const int p = lane + 32 * t;
+        re[t] = xr_s[p + (p >> 5)];
+        im[t] = xi_s[p + (p >> 5)];
+    }
+    __syncwarp();
+    // ---- halves 32..256 inside the lane: position lane + 32t pairs with t + h / 32;
+    // twiddle ((lane + 32t) % h) * 256 / h
+#pragma unroll
+    for (int h = 32; h <= 256; h <<= 1) {
+        const int hs = h / 32;
+#pragma unroll
+        for (int t = 0; t < 16; t++) {
+            if (t & hs) continue;
+            const int tix = (lane + 32 * (t & (hs - 1))) * (NFFT / 2 / h);
+            butterfly(re[t], im[t], re[t + hs], im[t + hs], tw_s[2 * tix], tw_s[2 * tix + 1]);
+        }
+    }
+    // ---- power of bins 0..256 into shared memory (bin lane + 32t)
+    float* pw = xr_s;
+#pragma unroll
+    for (int t = 0; t < 8; t++) pw[lane + 32 * t] = __fadd_rn(__fmul_rn(re[t], re[t]), __fmul_rn(im[t], im[t]));
+    if (lane == 0) pw[256] = __fadd_rn(__fmul_rn(re[8], re[8]), __fmul_rn(im[8], im[8]));
+    __syncwarp();
+    // ---- filterbank (sequential over each filter's support) and log
+    const long long orow = f_out[f] * 128;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int m = lane + 32 * q;
         float acc = 0.0f;
-        for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(filters[m * NBINS + k], pw[k]));
+        const float* fw = filters + m * NBINS;
+        for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(fw[k], pw[k]));
         const float v = (float)log((double)__fadd_rn(acc, 5.9604645e-8f));
-        const long long o = f_out[f] * 128 + m;
+        const long long o = orow + m;
         if (mel.hi) {
-            float h;
+            float hv;
             uint16_t hb, lb;
-            split3x1(v, h, hb, lb);
-            mel.hi[o] = h;
+            split3x1(v, hv, hb, lb);
+            mel.hi[o] = hv;
             static_cast<uint16_t*>(mel.hb)[o] = hb;
             static_cast<uint16_t*>(mel.lb)[o] = lb;
         }
@@ -373,8 +448,9 @@ void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, con
                 const float* window, const float* twiddle, const float* filters, const int* filt_lo,
                 const int* filt_hi, float preemph, Split3Out mel, float* mel_plain, const long long* f_out) {
     if (n_frames <= 0) return;
-    mel_kernel<<<(unsigned)n_frames, 256, 0, s>>>(audio, f_base, f_meta, window, twiddle, filters, filt_lo, filt_hi,
-                                                  preemph, mel, mel_plain, f_out);
+    const long long blocks = (n_frames + MEL_WARPS - 1) / MEL_WARPS;
+    mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, f_base, f_meta, n_frames, window, twiddle, filters,
+                                                            filt_lo, filt_hi, preemph, mel, mel_plain, f_out);
     N3D_CUDA(cudaGetLastError());
 }
 

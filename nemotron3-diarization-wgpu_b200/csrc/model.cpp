@@ -381,6 +381,8 @@ Model::Model(const std::string& dir, int device) : device_(device) {
     cfg_ = load_config(dir);
     N3D_CUDA(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
+    N3D_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    N3D_CUDA(cudaEventCreateWithFlags(&upload_start_, cudaEventDisableTiming));
     N3D_CUDA(cudaMalloc(&dev_err_, sizeof(int)));
     N3D_CUDA(cudaMemset(dev_err_, 0, sizeof(int)));
     upload_weights(dir);
@@ -394,6 +396,10 @@ Model::~Model() {
         cudaEventDestroy(r.b);
     }
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
+    if (copy_stream_) cudaStreamSynchronize(copy_stream_);
+    for (cudaEvent_t e : upload_ev_) cudaEventDestroy(e);
+    if (upload_start_) cudaEventDestroy(upload_start_);
+    if (copy_stream_) cudaStreamDestroy(copy_stream_);
     for (void* p : owned_) cudaFree(p);
     for (auto& kv : ws_) cudaFree(kv.second.p);
     if (dev_err_) cudaFree(dev_err_);
@@ -830,16 +836,28 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
         std::vector<long long> aoff(nb);
         long long total_samples = 0;
         const float* d_audio = d_audio_in;
+        const int nparts = d_audio_in ? 0 : (nb + kUploadClips - 1) / kUploadClips;
         if (!d_audio_in) {
             for (int i = 0; i < nb; i++) {
                 aoff[i] = total_samples;
                 total_samples += lens[c0 + i];
             }
             float* buf = (float*)ws("audio", (size_t)std::max(total_samples, 1LL) * 4);
-            for (int i = 0; i < nb; i++)
-                if (lens[c0 + i])
-                    N3D_CUDA(cudaMemcpyAsync(buf + aoff[i], host_audio[c0 + i], lens[c0 + i] * 4,
-                                             cudaMemcpyHostToDevice, stream_));
+            // the previous batch's mel has read the buffer before the upload overwrites it
+            N3D_CUDA(cudaEventRecord(upload_start_, stream_));
+            N3D_CUDA(cudaStreamWaitEvent(copy_stream_, upload_start_, 0));
+            while ((int)upload_ev_.size() < nparts) {
+                cudaEvent_t e;
+                N3D_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+                upload_ev_.push_back(e);
+            }
+            for (int k = 0; k < nparts; k++) {
+                for (int i = k * kUploadClips; i < std::min(nb, (k + 1) * kUploadClips); i++)
+                    if (lens[c0 + i])
+                        N3D_CUDA(cudaMemcpyAsync(buf + aoff[i], host_audio[c0 + i], lens[c0 + i] * 4,
+                                                 cudaMemcpyHostToDevice, copy_stream_));
+                N3D_CUDA(cudaEventRecord(upload_ev_[k], copy_stream_));
+            }
             d_audio = buf;
         } else {
             for (int i = 0; i < nb; i++) aoff[i] = offsets_in[c0 + i];
@@ -848,7 +866,8 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
         long long total_groups = 0, total_frames = 0;
         std::vector<MelSeg> flat;
         std::vector<long long> flat_base;
-        for (int i = 0; i < nb; i++)
+        std::vector<std::pair<long long, cudaEvent_t>> parts;
+        for (int i = 0; i < nb; i++) {
             for (MelSeg& s : plans[c0 + i].segs) {
                 s.group_base = total_groups;
                 total_groups += s.groups;
@@ -856,7 +875,11 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 flat.push_back(s);
                 flat_base.push_back(aoff[i] + s.audio_off);
             }
-        const float* embeds = mel_embed(d_audio, flat_base, flat, total_groups, total_frames);
+            if (nparts && ((i + 1) % kUploadClips == 0 || i + 1 == nb))
+                parts.emplace_back(total_frames, upload_ev_[i / kUploadClips]);
+        }
+        const float* embeds =
+            mel_embed(d_audio, flat_base, flat, total_groups, total_frames, nparts ? &parts : nullptr);
         // ---- per-clip state and outputs
         int max_steps = 0;
         long long out_total = 0;
@@ -956,7 +979,8 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
 // split [groups·sub, n_mels] array, then one embedder GEMM over all groups ->
 // [total_groups, hidden] (src/mel.rs:160-225, src/encoder.rs:126-146).
 const float* Model::mel_embed(const float* d_audio, const std::vector<long long>& base,
-                              const std::vector<MelSeg>& segs, long long total_groups, long long total_frames) {
+                              const std::vector<MelSeg>& segs, long long total_groups, long long total_frames,
+                              const std::vector<std::pair<long long, cudaEvent_t>>* parts) {
     const Config& c = cfg_;
     const int h = c.hidden, sub = c.sub;
     std::vector<long long> f_base(total_frames), f_out(total_frames);
@@ -986,8 +1010,18 @@ const float* Model::mel_embed(const float* d_audio, const std::vector<long long>
         N3D_CUDA(cudaMemcpyAsync(d_fo, f_out.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
         N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
         prof_begin();
-        launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_,
-                   c.preemph, mel.out(), nullptr, d_fo);
+        if (parts) {
+            long long f0 = 0;
+            for (const auto& pt : *parts) {
+                N3D_CUDA(cudaStreamWaitEvent(stream_, pt.second, 0));
+                launch_mel(stream_, d_audio, d_fb + f0, d_fm + 2 * f0, pt.first - f0, window_, twiddle_, mel_filters_,
+                           filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr, d_fo + f0);
+                f0 = pt.first;
+            }
+        } else {
+            launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_,
+                       c.preemph, mel.out(), nullptr, d_fo);
+        }
         prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
     }
     const long long K_emb = (long long)sub * c.n_mels;

@@ -184,8 +184,11 @@ class Model {
     void upload_weights(const std::string& dir);
     void tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain);
     void head(int B, int S, const int* d_seq_len);
+    // `parts` (optional): frame ranges [previous end, end) whose audio arrives on the
+    // copy stream; the mel of each range waits for its event.
     const float* mel_embed(const float* d_audio, const std::vector<long long>& base, const std::vector<MelSeg>& segs,
-                           long long total_groups, long long total_frames);
+                           long long total_groups, long long total_frames,
+                           const std::vector<std::pair<long long, cudaEvent_t>>* parts = nullptr);
     // One chunk-loop step of B sequences (rows of stride S): window assembly, tower,
     // head, cache update.
     void run_step(const SeqStep* d_steps, int B, int S, const int* d_len, const int* d_valid, const float* embeds);
@@ -198,6 +201,12 @@ class Model {
     int device_ = 0;
     cudaStream_t stream_ = nullptr;
     cudaStream_t own_stream_ = nullptr;
+    // Host audio of a batch is uploaded on copy_stream_ in parts of kUploadClips
+    // clips, so the mel of part k overlaps the upload of part k + 1.
+    static constexpr int kUploadClips = 16;
+    cudaStream_t copy_stream_ = nullptr;
+    cudaEvent_t upload_start_ = nullptr;
+    std::vector<cudaEvent_t> upload_ev_;
     int* dev_err_ = nullptr;
 
     DevLinear embed_, proj_, conv_, dense_;
