@@ -1,7 +1,7 @@
 // Allocation-free variant of tensor::linear (src/tensor.rs:22-57) on the GPU.
 //
-// n3d_linear needs temporary device memory for the TF32 hi/lo split of its
-// operands and gets it from cudaMalloc.  Some callers cannot allocate device
+// n3d_linear needs temporary device memory for the 3-term split (hi, hb, lb) of
+// its operands and gets it from cudaMalloc.  Some callers cannot allocate device
 // memory at the point where they call: a real-time audio thread that must not
 // block in the driver's allocator, a host framework that has reserved all of
 // the GPU's memory for its own pool and hands out only its own buffers, or a
