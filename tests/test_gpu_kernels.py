@@ -79,6 +79,24 @@ def test_linear_kernel_sweep(m, k, n):
     assert np.isfinite(got).all()
 
 
+@pytest.mark.parametrize("m,n", [(10240, 512), (49152, 512), (16384, 1024)])
+def test_linear_pair_tiles_with_a_partial_last_wave_match_oracle(m, n):
+    """CTA-pair shapes (256 x 256 tiles) whose last wave is partial (10240 x 512: 80
+    tiles on 74 pairs); every row of the last 1024 and a sample of the others against
+    the oracle."""
+    k = 512
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    b = rng.standard_normal(n, dtype=np.float32)
+    got = _gemm(x, w, b, m, k, n).reshape(m, n)
+    rows = np.unique(np.concatenate([np.arange(m - 1024, m), rng.integers(0, m - 1024, 64)]))
+    want = oracle.linear(x[rows], len(rows), k, w, n, b).reshape(len(rows), n)
+    err = np.abs(got[rows] - want).max()
+    assert err < TOL
+    assert err <= 1e-5 * max(1.0, np.abs(want).max())
+
+
 @pytest.mark.parametrize("rows,cols", [(17, 512), (684, 512), (16384, 1024)])
 def test_layer_norm_matches_oracle(rows, cols):
     import torch
