@@ -62,6 +62,39 @@ void fill_output(n3d_run_output* out, std::vector<float>& logits, const n3d::Cli
     out->fifo_frames = (size_t)p.fifo_frames;
 }
 
+// Run outputs whose logits run_batch writes in place: the sink allocates each clip's
+// array in its n3d_run_output; the remaining fields come from the plans afterwards.
+// On an exception every array allocated so far is freed.
+void run_batch_to_outputs(n3d::Model& m, int mode, const std::vector<const float*>& audio,
+                          const std::vector<long long>& lens, n3d_run_output* outs) {
+    const size_t n = lens.size(), ns = (size_t)m.cfg().num_speakers;
+    for (size_t i = 0; i < n; i++) std::memset(&outs[i], 0, sizeof(outs[i]));
+    std::vector<n3d::ClipPlan> plans;
+    const n3d::Model::HostSink sink = [&](int clip, size_t count) {
+        float* p = (float*)std::malloc(std::max<size_t>(count, 1) * sizeof(float));
+        if (!p) throw std::bad_alloc();
+        outs[clip].logits = p;
+        outs[clip].num_frames = count / ns;
+        return p;
+    };
+    try {
+        m.run_batch(mode, audio, nullptr, std::vector<long long>(n, 0), lens, &sink, nullptr, nullptr, &plans);
+    } catch (...) {
+        for (size_t i = 0; i < n; i++) {
+            std::free(outs[i].logits);
+            outs[i].logits = nullptr;
+        }
+        throw;
+    }
+    for (size_t i = 0; i < n; i++) {
+        outs[i].num_speakers = ns;
+        outs[i].num_chunks = (size_t)plans[i].num_chunks;
+        outs[i].cache_compressed = plans[i].cache_compressed;
+        outs[i].cache_frames = (size_t)plans[i].cache_frames;
+        outs[i].fifo_frames = (size_t)plans[i].fifo_frames;
+    }
+}
+
 // torch.sigmoid in fp32 (src/segments.rs:41-43)
 float sigmoidf(float x) { return 1.0f / (1.0f + std::exp(-x)); }
 
@@ -155,11 +188,7 @@ size_t n3d_hidden_size(const n3d_model* model) { return model ? (size_t)model->m
 static n3d_status run_one(n3d_model* model, const float* samples, size_t n, int mode, n3d_run_output* out) {
     return guarded([&] {
         arg_check(model && out && (samples || n == 0), "null argument");
-        std::memset(out, 0, sizeof(*out));
-        std::vector<std::vector<float>> res(1);
-        std::vector<n3d::ClipPlan> plans;
-        model->m->run_batch(mode, {samples}, nullptr, {0}, {(long long)n}, &res, nullptr, nullptr, &plans);
-        fill_output(out, res[0], plans[0], (size_t)model->m->cfg().num_speakers);
+        run_batch_to_outputs(*model->m, mode, {samples}, {(long long)n}, out);
     });
 }
 
@@ -256,13 +285,8 @@ n3d_status n3d_run_batch(n3d_model* model, n3d_mode mode, const float* const* sa
         arg_check(model && (n_clips == 0 || (samples && lens && outs)), "n3d_run_batch: null argument");
         arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_run_batch: bad mode");
         std::vector<const float*> a(samples, samples + n_clips);
-        std::vector<long long> l(lens, lens + n_clips), off(n_clips, 0);
-        std::vector<std::vector<float>> res(n_clips);
-        std::vector<n3d::ClipPlan> plans;
-        model->m->run_batch((int)mode, a, nullptr, off, l, &res, nullptr, nullptr, &plans);
-        for (size_t i = 0; i < n_clips; i++) std::memset(&outs[i], 0, sizeof(outs[i]));
-        for (size_t i = 0; i < n_clips; i++)
-            fill_output(&outs[i], res[i], plans[i], (size_t)model->m->cfg().num_speakers);
+        std::vector<long long> l(lens, lens + n_clips);
+        run_batch_to_outputs(*model->m, (int)mode, a, l, outs);
     });
 }
 

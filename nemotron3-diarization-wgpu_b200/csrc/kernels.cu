@@ -190,10 +190,10 @@ __device__ __forceinline__ void butterfly(float& ur, float& ui, float& xr, float
 }
 
 __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
-    const float* __restrict__ audio, const long long* __restrict__ f_base, const int* __restrict__ f_meta,
-    long long n_frames, const float* __restrict__ window, const float* __restrict__ twiddle,
+    const float* __restrict__ audio, const MelSegDev* __restrict__ segs, int nsegs, long long f_first,
+    long long n_frames, int hop, const float* __restrict__ window, const float* __restrict__ twiddle,
     const float* __restrict__ filters, const int* __restrict__ filt_lo, const int* __restrict__ filt_hi, float preemph,
-    Split3Out mel, float* __restrict__ mel_plain, const long long* __restrict__ f_out) {
+    Split3Out mel, float* __restrict__ mel_plain) {
     __shared__ float tw_s[NFFT];  // (cos, sin) pairs of the 256 twiddles
     __shared__ float win_s[NFFT];
     __shared__ float xs[MEL_WARPS][2][MEL_PAD];
@@ -203,10 +203,17 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long long f = (long long)blockIdx.x * MEL_WARPS + warp;
-    if (f >= n_frames) return;
-    const long long base = f_base[f];
-    const int p0 = f_meta[2 * f], n = f_meta[2 * f + 1];
+    const long long f = f_first + (long long)blockIdx.x * MEL_WARPS + warp;
+    if (f >= f_first + n_frames) return;
+    int lo = 0, hi = nsegs - 1;  // the segment holding frame f: last f_begin <= f
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (segs[mid].f_begin <= f) lo = mid;
+        else hi = mid - 1;
+    }
+    const MelSegDev sg = segs[lo];
+    const long long base = sg.base;
+    const int p0 = (sg.frame_lo + (int)(f - sg.f_begin)) * hop - (sg.centered ? NFFT / 2 : 0), n = sg.len;
     float re[16], im[16];
     // ---- input at bit-reversed positions (layout A): position 16L + s <- sample
     // j = brev9(16L + s) = brev4(s) * 32 + brev5(L)
@@ -283,7 +290,7 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
     if (lane == 0) pw[256] = __fadd_rn(__fmul_rn(re[8], re[8]), __fmul_rn(im[8], im[8]));
     __syncwarp();
     // ---- filterbank (sequential over each filter's support) and log
-    const long long orow = f_out[f] * 128;
+    const long long orow = (sg.out_row0 + (f - sg.f_begin)) * 128;
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const int m = lane + 32 * q;
@@ -444,13 +451,13 @@ void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride
     N3D_CUDA(cudaGetLastError());
 }
 
-void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
-                const float* window, const float* twiddle, const float* filters, const int* filt_lo,
-                const int* filt_hi, float preemph, Split3Out mel, float* mel_plain, const long long* f_out) {
-    if (n_frames <= 0) return;
+void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
+                long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
+                const int* filt_lo, const int* filt_hi, float preemph, Split3Out mel, float* mel_plain) {
+    if (n_frames <= 0 || nsegs <= 0) return;
     const long long blocks = (n_frames + MEL_WARPS - 1) / MEL_WARPS;
-    mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, f_base, f_meta, n_frames, window, twiddle, filters,
-                                                            filt_lo, filt_hi, preemph, mel, mel_plain, f_out);
+    mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, segs, nsegs, f_first, n_frames, hop, window, twiddle,
+                                                            filters, filt_lo, filt_hi, preemph, mel, mel_plain);
     N3D_CUDA(cudaGetLastError());
 }
 

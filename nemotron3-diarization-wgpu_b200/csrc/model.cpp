@@ -10,6 +10,9 @@
 
 #include <memory>
 #include <algorithm>
+#include <array>
+#include <climits>
+#include <thread>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -398,6 +401,7 @@ Model::~Model() {
     for (cudaEvent_t e : event_pool_) cudaEventDestroy(e);
     if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     for (cudaEvent_t e : upload_ev_) cudaEventDestroy(e);
+    if (host_stage_) cudaFreeHost(host_stage_);
     if (upload_start_) cudaEventDestroy(upload_start_);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
     for (void* p : owned_) cudaFree(p);
@@ -816,9 +820,20 @@ void Model::head(int B, int S, const int* d_seq_len) {
     prof_end(K_GEMM_DENSE, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
 }
 
+float* Model::host_stage(size_t bytes) {
+    if (bytes > host_stage_bytes_) {
+        if (host_stage_) N3D_CUDA(cudaFreeHost(host_stage_));
+        host_stage_ = nullptr;
+        host_stage_bytes_ = 0;
+        N3D_CUDA(cudaHostAlloc(reinterpret_cast<void**>(&host_stage_), bytes, cudaHostAllocDefault));
+        host_stage_bytes_ = bytes;
+    }
+    return host_stage_;
+}
+
 void Model::run_batch(int mode, const std::vector<const float*>& host_audio, const float* d_audio_in,
                       const std::vector<long long>& offsets_in, const std::vector<long long>& lens,
-                      std::vector<std::vector<float>>* host_out, float* d_logits,
+                      const HostSink* host_out, float* d_logits,
                       const std::vector<long long>* out_offsets, std::vector<ClipPlan>* plans_out) {
     const Config& c = cfg_;
     N3D_CUDA(cudaSetDevice(device_));
@@ -832,54 +847,104 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
 
     for (int c0 = 0; c0 < nclips; c0 += B_CAP) {
         const int c1 = std::min(nclips, c0 + B_CAP), nb = c1 - c0;
-        // ---- audio
+        // ---- audio.  Host audio goes up on the copy stream in two phases: the samples
+        // that chunk step 0 of every clip needs, then the rest, which arrives while step 0
+        // computes.  Each phase is cut into parts of kUploadClips clips, and the mel of a
+        // part waits only for that part's upload.
         std::vector<long long> aoff(nb);
         long long total_samples = 0;
         const float* d_audio = d_audio_in;
+        const int nphase = d_audio_in ? 1 : 2;
         const int nparts = d_audio_in ? 0 : (nb + kUploadClips - 1) / kUploadClips;
         if (!d_audio_in) {
             for (int i = 0; i < nb; i++) {
                 aoff[i] = total_samples;
                 total_samples += lens[c0 + i];
             }
-            float* buf = (float*)ws("audio", (size_t)std::max(total_samples, 1LL) * 4);
-            // the previous batch's mel has read the buffer before the upload overwrites it
-            N3D_CUDA(cudaEventRecord(upload_start_, stream_));
-            N3D_CUDA(cudaStreamWaitEvent(copy_stream_, upload_start_, 0));
-            while ((int)upload_ev_.size() < nparts) {
+        } else {
+            for (int i = 0; i < nb; i++) aoff[i] = offsets_in[c0 + i];
+        }
+        // ---- mel parts per phase: the groups of each segment that the phase's steps read
+        // (device audio: one phase with every group of every segment)
+        struct PartRef {
+            long long base = -1, lo = 0;  // group base in the phase's embeddings, first group
+        };
+        std::vector<std::vector<std::array<PartRef, 2>>> ref(nb);
+        std::vector<std::vector<MelSeg>> pseg(nphase);
+        std::vector<std::vector<long long>> pbase(nphase);
+        std::vector<long long> ptot_groups(nphase, 0), ptot_frames(nphase, 0);
+        std::vector<std::vector<std::pair<long long, cudaEvent_t>>> pparts(nphase);
+        std::vector<long long> end0(nb, 0);  // host audio: samples uploaded in phase 0
+        if (!d_audio_in)
+            while ((int)upload_ev_.size() < nphase * nparts) {
                 cudaEvent_t e;
                 N3D_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
                 upload_ev_.push_back(e);
             }
-            for (int k = 0; k < nparts; k++) {
-                for (int i = k * kUploadClips; i < std::min(nb, (k + 1) * kUploadClips); i++)
-                    if (lens[c0 + i])
-                        N3D_CUDA(cudaMemcpyAsync(buf + aoff[i], host_audio[c0 + i], lens[c0 + i] * 4,
-                                                 cudaMemcpyHostToDevice, copy_stream_));
-                N3D_CUDA(cudaEventRecord(upload_ev_[k], copy_stream_));
-            }
-            d_audio = buf;
-        } else {
-            for (int i = 0; i < nb; i++) aoff[i] = offsets_in[c0 + i];
-        }
-        // ---- mel segments, log-mel and the embedder over every segment of every clip
-        long long total_groups = 0, total_frames = 0;
-        std::vector<MelSeg> flat;
-        std::vector<long long> flat_base;
-        std::vector<std::pair<long long, cudaEvent_t>> parts;
         for (int i = 0; i < nb; i++) {
-            for (MelSeg& s : plans[c0 + i].segs) {
-                s.group_base = total_groups;
-                total_groups += s.groups;
-                total_frames += s.frames;
-                flat.push_back(s);
-                flat_base.push_back(aoff[i] + s.audio_off);
+            const ClipPlan& p = plans[c0 + i];
+            const int nseg = (int)p.segs.size();
+            ref[i].assign(nseg, {});
+            std::vector<std::array<long long, 4>> rng(nseg, {LLONG_MAX, -1, LLONG_MAX, -1});  // lo0, hi0, lo1, hi1
+            if (nphase == 1) {
+                for (int sg = 0; sg < nseg; sg++) rng[sg] = {0, p.segs[sg].groups, LLONG_MAX, -1};
+            } else {
+                for (size_t w = 0; w < p.steps.size(); w++) {
+                    const StepPlan& sp = p.steps[w];
+                    const int ph = w == 0 ? 0 : 1;
+                    long long& lo = rng[sp.seg][2 * ph];
+                    long long& hi = rng[sp.seg][2 * ph + 1];
+                    lo = std::min(lo, (long long)sp.group_lo);
+                    hi = std::max(hi, (long long)(sp.group_lo + sp.n_new));
+                }
             }
-            if (nparts && ((i + 1) % kUploadClips == 0 || i + 1 == nb))
-                parts.emplace_back(total_frames, upload_ev_[i / kUploadClips]);
+            for (int ph = 0; ph < nphase; ph++) {
+                for (int sg = 0; sg < nseg; sg++) {
+                    const long long lo = rng[sg][2 * ph], hi = rng[sg][2 * ph + 1];
+                    if (hi <= lo) continue;
+                    MelSeg m = p.segs[sg];
+                    m.frame_lo = (int)(lo * c.sub);
+                    m.groups = (int)(hi - lo);
+                    m.group_base = ptot_groups[ph];
+                    ref[i][sg][ph] = PartRef{ptot_groups[ph], lo};
+                    ptot_groups[ph] += m.groups;
+                    const int nf = mel_frames(m, c.sub);
+                    ptot_frames[ph] += nf;
+                    pseg[ph].push_back(m);
+                    pbase[ph].push_back(aoff[i] + m.audio_off);
+                    if (ph == 0 && nf > 0) {  // last sample phase 0's frames read, plus one
+                        const long long t = m.frame_lo + nf - 1;
+                        const long long e = m.audio_off + t * c.hop - (m.centered ? c.n_fft / 2 : 0) + c.n_fft;
+                        end0[i] = std::max(end0[i], std::min(e, m.audio_off + m.len));
+                    }
+                }
+                if (nparts && ((i + 1) % kUploadClips == 0 || i + 1 == nb))
+                    pparts[ph].emplace_back(ptot_frames[ph], upload_ev_[ph * nparts + i / kUploadClips]);
+            }
         }
-        const float* embeds =
-            mel_embed(d_audio, flat_base, flat, total_groups, total_frames, nparts ? &parts : nullptr);
+        if (!d_audio_in) {
+            float* buf = (float*)ws("audio", (size_t)std::max(total_samples, 1LL) * 4);
+            // the previous batch's mel has read the buffer before the upload overwrites it
+            N3D_CUDA(cudaEventRecord(upload_start_, stream_));
+            N3D_CUDA(cudaStreamWaitEvent(copy_stream_, upload_start_, 0));
+            for (int ph = 0; ph < 2; ph++)
+                for (int k = 0; k < nparts; k++) {
+                    for (int i = k * kUploadClips; i < std::min(nb, (k + 1) * kUploadClips); i++) {
+                        const long long n = lens[c0 + i], e = std::min(std::max(end0[i], 0LL), n);
+                        const long long s0 = ph == 0 ? 0 : e, s1 = ph == 0 ? e : n;
+                        if (s1 > s0)
+                            N3D_CUDA(cudaMemcpyAsync(buf + aoff[i] + s0, host_audio[c0 + i] + s0, (s1 - s0) * 4,
+                                                     cudaMemcpyHostToDevice, copy_stream_));
+                    }
+                    N3D_CUDA(cudaEventRecord(upload_ev_[ph * nparts + k], copy_stream_));
+                }
+            d_audio = buf;
+        }
+        std::vector<MelJob> jobs;
+        for (int ph = 0; ph < nphase; ph++)
+            jobs.push_back(mel_prepare(pbase[ph], pseg[ph], ptot_groups[ph], ptot_frames[ph], ph ? "1" : ""));
+        const float* emb_phase[2] = {nullptr, nullptr};
+        emb_phase[0] = mel_launch(d_audio, jobs[0], nparts ? &pparts[0] : nullptr);
         // ---- per-clip state and outputs
         int max_steps = 0;
         long long out_total = 0;
@@ -916,7 +981,8 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 q.compress = sp.compress;
                 q.was_compressed = sp.was_compressed;
                 q.keep_rows = sp.keep_rows;
-                q.emb_row = p.segs[sp.seg].group_base + sp.group_lo;
+                const PartRef& pr = ref[i][sp.seg][nphase == 2 && w > 0 ? 1 : 0];
+                q.emb_row = pr.base + (sp.group_lo - pr.lo);
                 const int cur = w & 1, nxt = cur ^ 1;
                 q.pre_in = pre + ((size_t)cur * nb + i) * pre_rows * h;
                 q.pre_out = pre + ((size_t)nxt * nb + i) * pre_rows * h;
@@ -944,22 +1010,39 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
             N3D_CUDA(cudaMemcpyAsync(d_len, seq_len.data(), seq_len.size() * 4, cudaMemcpyHostToDevice, stream_));
             N3D_CUDA(cudaMemcpyAsync(d_valid, valid.data(), valid.size() * 4, cudaMemcpyHostToDevice, stream_));
             for (int w = 0; w < max_steps; w++) {
+                if (w == 1 && nphase == 2)  // the later steps' groups, once their audio is up
+                    emb_phase[1] = mel_launch(d_audio, jobs[1], nparts ? &pparts[1] : nullptr);
                 const int B = step_first[w + 1] - step_first[w];
                 if (B == 0) continue;
                 run_step(d_table + step_first[w], B, step_S[w], d_len + step_first[w], d_valid + step_first[w],
-                         embeds);
+                         emb_phase[nphase == 2 && w > 0 ? 1 : 0]);
             }
         }
+        // the caller may release its audio once this returns: every upload has finished
+        if (nparts) N3D_CUDA(cudaStreamSynchronize(copy_stream_));
         // ---- results
         if (host_out) {
-            std::vector<float> all((size_t)out_total * ns);
+            // one copy into pinned staging, then into the caller's buffers (a few host
+            // threads share the copies of a large batch)
+            float* stage = host_stage((size_t)std::max(out_total, 1LL) * ns * 4);
             if (out_total)
-                N3D_CUDA(cudaMemcpyAsync(all.data(), outl, out_total * ns * 4, cudaMemcpyDeviceToHost, stream_));
+                N3D_CUDA(cudaMemcpyAsync(stage, outl, out_total * ns * 4, cudaMemcpyDeviceToHost, stream_));
             N3D_CUDA(cudaStreamSynchronize(stream_));
-            for (int i = 0; i < nb; i++) {
-                const ClipPlan& p = plans[c0 + i];
-                (*host_out)[c0 + i].assign(all.begin() + out_base[i] * ns,
-                                           all.begin() + (out_base[i] + p.out_rows) * ns);
+            std::vector<float*> dst(nb);
+            for (int i = 0; i < nb; i++) dst[i] = (*host_out)(c0 + i, (size_t)plans[c0 + i].out_rows * ns);
+            auto copy_range = [&](int i0, int i1) {
+                for (int i = i0; i < i1; i++)
+                    if (plans[c0 + i].out_rows)
+                        std::memcpy(dst[i], stage + out_base[i] * ns, (size_t)plans[c0 + i].out_rows * ns * 4);
+            };
+            const int nthreads = (size_t)out_total * ns * 4 >= (4u << 20) ? std::min(8, nb) : 1;
+            if (nthreads <= 1) {
+                copy_range(0, nb);
+            } else {
+                std::vector<std::thread> pool;
+                for (int t = 0; t < nthreads; t++)
+                    pool.emplace_back(copy_range, nb * t / nthreads, nb * (t + 1) / nthreads);
+                for (std::thread& th : pool) th.join();
             }
         } else {
             for (int i = 0; i < nb; i++) {
@@ -978,55 +1061,62 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
 // Log-mel of every segment (segment i's samples start at d_audio[base[i]]) into one
 // split [groups·sub, n_mels] array, then one embedder GEMM over all groups ->
 // [total_groups, hidden] (src/mel.rs:160-225, src/encoder.rs:126-146).
-const float* Model::mel_embed(const float* d_audio, const std::vector<long long>& base,
-                              const std::vector<MelSeg>& segs, long long total_groups, long long total_frames,
-                              const std::vector<std::pair<long long, cudaEvent_t>>* parts) {
+Model::MelJob Model::mel_prepare(const std::vector<long long>& base, const std::vector<MelSeg>& segs,
+                                 long long total_groups, long long total_frames, const char* tag) {
+    const Config& c = cfg_;
+    const int sub = c.sub;
+    MelJob job;
+    job.groups = total_groups;
+    job.frames = total_frames;
+    job.tag = tag;
+    if (total_frames <= 0) return job;
+    std::vector<MelSegDev> table;
+    table.reserve(segs.size());
+    long long f = 0;
+    for (size_t i = 0; i < segs.size(); i++) {
+        const MelSeg& s = segs[i];
+        const int nf = mel_frames(s, sub);
+        if (nf == 0) continue;
+        if (s.len > INT_MAX) throw Error(kStatusArg, "mel segment longer than 2^31 samples");
+        table.push_back(MelSegDev{base[i], s.group_base * sub, f, (int)s.len, s.frame_lo, s.centered, 0});
+        f += nf;
+    }
+    if (f != total_frames) throw Error(kStatusGpu, "mel_prepare: frame count mismatch");
+    MelSegDev* d_segs = (MelSegDev*)ws(("melseg" + job.tag).c_str(), table.size() * sizeof(MelSegDev));
+    N3D_CUDA(cudaMemcpyAsync(d_segs, table.data(), table.size() * sizeof(MelSegDev), cudaMemcpyHostToDevice, stream_));
+    job.segs = d_segs;
+    job.nsegs = (int)table.size();
+    return job;
+}
+
+const float* Model::mel_launch(const float* d_audio, const MelJob& job,
+                               const std::vector<std::pair<long long, cudaEvent_t>>* parts) {
     const Config& c = cfg_;
     const int h = c.hidden, sub = c.sub;
-    std::vector<long long> f_base(total_frames), f_out(total_frames);
-    std::vector<int> f_meta(2 * total_frames);
-    {
-        long long f = 0;
-        for (size_t i = 0; i < segs.size(); i++) {
-            const MelSeg& s = segs[i];
-            for (int t = 0; t < s.frames; t++, f++) {
-                f_base[f] = base[i];
-                f_meta[2 * f] = t * c.hop - (s.centered ? c.n_fft / 2 : 0);
-                f_meta[2 * f + 1] = (int)s.len;
-                f_out[f] = s.group_base * sub + t;
-            }
-        }
-    }
-    const long long mel_rows = std::max(total_groups * sub, 1LL);
-    const Split3Buf mel = ws3("mel", mel_rows, c.n_mels);  // rows past a segment's frames stay zero
+    const long long mel_rows = std::max(job.groups * sub, 1LL);
+    const Split3Buf mel = ws3("mel" + job.tag, mel_rows, c.n_mels);  // rows past a segment's frames stay zero
     N3D_CUDA(cudaMemsetAsync(mel.hi, 0, mel_rows * c.n_mels * 4, stream_));
     N3D_CUDA(cudaMemsetAsync(mel.hb, 0, mel_rows * c.n_mels * 2, stream_));
     N3D_CUDA(cudaMemsetAsync(mel.lb, 0, mel_rows * c.n_mels * 2, stream_));
-    if (total_frames > 0) {
-        long long* d_fb = (long long*)ws("f_base", total_frames * 8);
-        long long* d_fo = (long long*)ws("f_out", total_frames * 8);
-        int* d_fm = (int*)ws("f_meta", total_frames * 8);
-        N3D_CUDA(cudaMemcpyAsync(d_fb, f_base.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
-        N3D_CUDA(cudaMemcpyAsync(d_fo, f_out.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
-        N3D_CUDA(cudaMemcpyAsync(d_fm, f_meta.data(), total_frames * 8, cudaMemcpyHostToDevice, stream_));
+    if (job.frames > 0) {
         prof_begin();
         if (parts) {
             long long f0 = 0;
             for (const auto& pt : *parts) {
                 N3D_CUDA(cudaStreamWaitEvent(stream_, pt.second, 0));
-                launch_mel(stream_, d_audio, d_fb + f0, d_fm + 2 * f0, pt.first - f0, window_, twiddle_, mel_filters_,
-                           filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr, d_fo + f0);
+                launch_mel(stream_, d_audio, job.segs, job.nsegs, f0, pt.first - f0, c.hop, window_, twiddle_,
+                           mel_filters_, filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr);
                 f0 = pt.first;
             }
         } else {
-            launch_mel(stream_, d_audio, d_fb, d_fm, total_frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_,
-                       c.preemph, mel.out(), nullptr, d_fo);
+            launch_mel(stream_, d_audio, job.segs, job.nsegs, 0, job.frames, c.hop, window_, twiddle_, mel_filters_,
+                       filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr);
         }
-        prof_end(K_MEL, 0, (double)total_frames * (c.hop * 4 + c.n_mels * 8));
+        prof_end(K_MEL, 0, (double)job.frames * (c.hop * 4 + c.n_mels * 8));
     }
     const long long K_emb = (long long)sub * c.n_mels;
-    float* embeds = (float*)ws("embeds", std::max(total_groups, 1LL) * h * 4);
-    if (total_groups > 0) {
+    float* embeds = (float*)ws(("embeds" + job.tag).c_str(), std::max(job.groups, 1LL) * h * 4);
+    if (job.groups > 0) {
         Epi e;
         e.mode = EPI_STORE;
         e.out = embeds;
@@ -1034,8 +1124,8 @@ const float* Model::mel_embed(const float* d_audio, const std::vector<long long>
         // the [rows, 128] mel viewed as [groups, 8 * 128]: 8 stacked frames per row
         const SplitOperand A{mel.hi, mel.hb, mel.lb, mel.rows_cap / sub, K_emb, K_emb};
         prof_begin();
-        gemm_split3(stream_, A, embed_.op(), (int)total_groups, h, (int)K_emb, 0, e, dev_err_);
-        prof_end(K_GEMM_EMBED, 2.0 * total_groups * h * K_emb, 0);
+        gemm_split3(stream_, A, embed_.op(), (int)job.groups, h, (int)K_emb, 0, e, dev_err_);
+        prof_end(K_GEMM_EMBED, 2.0 * job.groups * h * K_emb, 0);
     }
     return embeds;
 }
@@ -1303,22 +1393,13 @@ int Model::log_mel(const float* samples, long long n, bool centered, std::vector
     if (frames == 0) return 0;
     float* a = (float*)ws("audio", n * 4);
     N3D_CUDA(cudaMemcpyAsync(a, samples, n * 4, cudaMemcpyHostToDevice, stream_));
-    std::vector<long long> fb(frames, 0), fo(frames);
-    std::vector<int> fm(2 * frames);
-    for (long long t = 0; t < frames; t++) {
-        fm[2 * t] = (int)(t * c.hop - (centered ? c.n_fft / 2 : 0));
-        fm[2 * t + 1] = (int)n;
-        fo[t] = t;
-    }
-    long long* d_fb = (long long*)ws("f_base", frames * 8);
-    long long* d_fo = (long long*)ws("f_out", frames * 8);
-    int* d_fm = (int*)ws("f_meta", frames * 8);
+    if (n > INT_MAX) throw Error(kStatusArg, "log_mel: more than 2^31 samples");
+    const MelSegDev seg{0, 0, 0, (int)n, 0, centered ? 1 : 0, 0};
+    MelSegDev* d_seg = (MelSegDev*)ws("melseg", sizeof(MelSegDev));
     float* pl = (float*)ws("mel_plain", frames * c.n_mels * 4);
-    N3D_CUDA(cudaMemcpyAsync(d_fb, fb.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
-    N3D_CUDA(cudaMemcpyAsync(d_fo, fo.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
-    N3D_CUDA(cudaMemcpyAsync(d_fm, fm.data(), frames * 8, cudaMemcpyHostToDevice, stream_));
-    launch_mel(stream_, a, d_fb, d_fm, frames, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph,
-               Split3Out{}, pl, d_fo);
+    N3D_CUDA(cudaMemcpyAsync(d_seg, &seg, sizeof(MelSegDev), cudaMemcpyHostToDevice, stream_));
+    launch_mel(stream_, a, d_seg, 1, 0, frames, c.hop, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph,
+               Split3Out{}, pl);
     N3D_CUDA(cudaMemcpyAsync(out.data(), pl, frames * c.n_mels * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));
     return (int)frames;

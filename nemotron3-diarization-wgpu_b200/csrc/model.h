@@ -6,6 +6,7 @@
 
 #include <cstdint>
 #include <map>
+#include <functional>
 #include <string>
 #include <vector>
 
@@ -74,7 +75,14 @@ struct MelSeg {           // one log_mel call of the reference
     int frames;           // frame_count(len)
     int groups;           // ceil(mel rows / sub); mel rows are padded with zeros to groups * sub
     long long group_base; // global row in the [groups, sub * n_mels] view (set at batch assembly)
+    int frame_lo = 0;     // first frame computed (group g of this launch starts at frame_lo + g * sub)
 };
+
+// Frames of `m` computed in one mel launch: [frame_lo, frame_lo + mel_frames).
+inline int mel_frames(const MelSeg& m, int sub) {
+    const int end = m.frames < m.frame_lo + m.groups * sub ? m.frames : m.frame_lo + m.groups * sub;
+    return end > m.frame_lo ? end - m.frame_lo : 0;
+}
 
 struct StepPlan {
     int S, valid, ncache, nfifo, nchunk, popped, compress, was_compressed, keep_rows;
@@ -145,10 +153,13 @@ class Model {
 
     // Batched chunk loop over independent clips (offline mode = 3).  Host or
     // device audio; results either copied to host vectors or left in d_logits.
+    // Host destination of one clip's logits: given the clip index and the float count,
+    // returns where to write them (called once per clip, from the calling thread).
+    using HostSink = std::function<float*(int clip, size_t n)>;
     void run_batch(int mode, const std::vector<const float*>& host_audio, const float* d_audio,
                    const std::vector<long long>& offsets, const std::vector<long long>& lens,
-                   std::vector<std::vector<float>>* host_out, float* d_logits,
-                   const std::vector<long long>* out_offsets, std::vector<ClipPlan>* plans_out);
+                   const HostSink* host_out, float* d_logits, const std::vector<long long>* out_offsets,
+                   std::vector<ClipPlan>* plans_out);
 
     // Sessions of this model (freed before the model).  sessions_push appends
     // samples[i] to ss[i] and runs every chunk that is complete, the steps of all
@@ -184,11 +195,26 @@ class Model {
     void upload_weights(const std::string& dir);
     void tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain);
     void head(int B, int S, const int* d_seq_len);
-    // `parts` (optional): frame ranges [previous end, end) whose audio arrives on the
-    // copy stream; the mel of each range waits for its event.
+    // Log-mel + embedder of `segs` (segment i's samples start at d_audio[base[i]]).
+    // mel_prepare uploads the segment table (from host memory, so call it before the
+    // stream is busy); mel_launch runs the mel and the embedder GEMM.  `parts`
+    // (optional): frame ranges [previous end, end) whose audio arrives on the copy
+    // stream; the mel of each range waits for its event.  `tag` names the workspace
+    // buffers, so that two prepared launches can be in flight.
+    struct MelJob {
+        long long groups = 0, frames = 0;
+        const MelSegDev* segs = nullptr;
+        int nsegs = 0;
+        std::string tag;
+    };
+    MelJob mel_prepare(const std::vector<long long>& base, const std::vector<MelSeg>& segs, long long total_groups,
+                       long long total_frames, const char* tag = "");
+    const float* mel_launch(const float* d_audio, const MelJob& job,
+                            const std::vector<std::pair<long long, cudaEvent_t>>* parts = nullptr);
     const float* mel_embed(const float* d_audio, const std::vector<long long>& base, const std::vector<MelSeg>& segs,
-                           long long total_groups, long long total_frames,
-                           const std::vector<std::pair<long long, cudaEvent_t>>* parts = nullptr);
+                           long long total_groups, long long total_frames) {
+        return mel_launch(d_audio, mel_prepare(base, segs, total_groups, total_frames));
+    }
     // One chunk-loop step of B sequences (rows of stride S): window assembly, tower,
     // head, cache update.
     void run_step(const SeqStep* d_steps, int B, int S, const int* d_len, const int* d_valid, const float* embeds);
@@ -205,6 +231,10 @@ class Model {
     // clips, so the mel of part k overlaps the upload of part k + 1.
     static constexpr int kUploadClips = 16;
     cudaStream_t copy_stream_ = nullptr;
+    // Pinned staging of a batch's logits on their way to the host (grown on demand).
+    float* host_stage_ = nullptr;
+    size_t host_stage_bytes_ = 0;
+    float* host_stage(size_t bytes);
     cudaEvent_t upload_start_ = nullptr;
     std::vector<cudaEvent_t> upload_ev_;
     int* dev_err_ = nullptr;

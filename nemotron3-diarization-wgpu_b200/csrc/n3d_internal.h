@@ -109,12 +109,19 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
 // SIMT attention (head_dim 128 kernel probes): plain fp32 context.
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
                       int head_dim, float* ctx);
-// Log-mel frames: frame f reads audio[f_base[f] + p] for p in [p0, p0 + n_fft) with
-// p0 = f_meta[2f] and the clip length f_meta[2f+1] (zeros outside [0, len)), and
-// writes row f_out[f] of the [rows, 128] mel outputs (3-term split, plain optional).
-void launch_mel(cudaStream_t s, const float* audio, const long long* f_base, const int* f_meta, long long n_frames,
-                const float* window, const float* twiddle, const float* filters, const int* filt_lo,
-                const int* filt_hi, float preemph, Split3Out mel, float* mel_plain, const long long* f_out);
+// One mel segment of a launch: global frames [f_begin, next segment's f_begin) are
+// frames frame_lo.. of a segment whose `len` samples start at audio[base]; frame t
+// reads samples t * hop - (centered ? 256 : 0) + [0, 512) (zeros outside [0, len))
+// and writes mel row out_row0 + (f - f_begin).  Segments are sorted by f_begin.
+struct MelSegDev {
+    long long base, out_row0, f_begin;
+    int len, frame_lo, centered, pad;
+};
+// Log-mel of global frames [f_first, f_first + n_frames) of the segment table into
+// [rows, 128] outputs (3-term split, plain optional).
+void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
+                long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
+                const int* filt_lo, const int* filt_hi, float preemph, Split3Out mel, float* mel_plain);
 // x -> its 3-term split, elementwise (n % 4 == 0).
 void launch_split(cudaStream_t s, const float* x, long long n, Split3Out out);
 // Operands of the tcgen05 attention (head_dim 64), all bfloat16 hi/lo pairs:

@@ -162,13 +162,24 @@ def _ptr(a: np.ndarray):
     return a.ctypes.data_as(_fp)
 
 
-def _collect(o: _RunOutput) -> RunOutput:
-    n = o.num_frames * o.num_speakers
-    logits = np.ctypeslib.as_array(o.logits, shape=(n,)).copy() if n else np.zeros(0, np.float32)
-    res = RunOutput(logits.reshape(o.num_frames, o.num_speakers), int(o.num_frames), int(o.num_chunks),
-                    bool(o.cache_compressed), int(o.cache_frames), int(o.fifo_frames))
+def _free_output(o: _RunOutput) -> None:
     lib().n3d_run_output_free(C.byref(o))
-    return res
+
+
+def _collect(o: _RunOutput) -> RunOutput:
+    """The output's logits as a numpy array without a copy: the array views the
+    library-allocated buffer, which is released (n3d_run_output_free) once the array
+    and every view of it are gone."""
+    n = o.num_frames * o.num_speakers
+    if n:
+        buf = (C.c_float * n).from_address(C.cast(o.logits, C.c_void_p).value)
+        weakref.finalize(buf, _free_output, _RunOutput.from_buffer_copy(o))
+        logits = np.ctypeslib.as_array(buf)
+    else:
+        logits = np.zeros(0, np.float32)
+        lib().n3d_run_output_free(C.byref(o))
+    return RunOutput(logits.reshape(o.num_frames, o.num_speakers), int(o.num_frames), int(o.num_chunks),
+                     bool(o.cache_compressed), int(o.cache_frames), int(o.fifo_frames))
 
 
 class Model:
