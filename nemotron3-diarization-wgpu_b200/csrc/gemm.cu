@@ -153,7 +153,7 @@ __device__ __forceinline__ void load_bias32(const float* bias, int col0, int N, 
 // `w2s` (EPI_DENSE_OUT): w2 [n2, N] and the dense bias [N] staged in shared memory.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
-                                              int lane, const float* w2s = nullptr) {
+                                              int lane, const float* w2s = nullptr, int ncols = BN) {
     const int r = m0 + q * 32 + lane;
     const bool row_ok = r < M;
     const int qq = r / epi.rdiv, t = r - qq * epi.rdiv;
@@ -183,7 +183,7 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m
             for (int o = 0; o < epi.n2; o++) epi.out[orow * epi.ldo + o] = __fadd_rn(acc[o], epi.b2[o]);
         return;
     }
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = 0; c < ncols; c += 32) {
         float v[32];
         tmem_ld32(tl + c, v);
         const int col0 = n0 + c;
@@ -545,6 +545,20 @@ __global__ void __launch_bounds__(192, 1)
 // its own epilogue warps store.  Barriers: full[s] lives in the leader (both CTAs'
 // loads complete on it), empty[s] and acc_full[b] in both (arrived by the leader's
 // multicast commits), acc_empty[b] in the leader (the 8 epilogue warps of the pair).
+// Tile t of a launch.  The first `full` tiles are 256 x BN in m-major order; the
+// tiles of the last, partial wave are each split along N into `split` sub-tiles of
+// BN / split columns, so that wave ends sooner (same dot products in the same k
+// order, so the results do not depend on the split).
+struct PairTile {
+    int mt, n0, nw;  // 256-row tile index, first column, width
+};
+template <int BN>
+__device__ __forceinline__ PairTile pair_tile(int t, int tiles_n, int full, int split) {
+    if (t < full) return PairTile{t / tiles_n, (t % tiles_n) * BN, BN};
+    const int u = t - full, base = full + u / split, nw = BN / split;
+    return PairTile{base / tiles_n, (base % tiles_n) * BN + (u % split) * nw, nw};
+}
+
 template <int BN>
 struct PairCfg {
     static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_3;
@@ -561,12 +575,12 @@ struct PairCfg {
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_pair_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
-                     const __grid_constant__ Epi epi, int* err) {
+                     const __grid_constant__ Epi epi, int* err, int full, int split) {
     using Cfg = PairCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
-    uint64_t* empty = full + Cfg::STAGES;
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full_bar + Cfg::STAGES;
     uint64_t* acc_full = empty + Cfg::STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
@@ -576,12 +590,12 @@ __global__ void __launch_bounds__(192, 1)
     const bool leader = rank == 0;
     const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
     const int tiles_n = (N + BN - 1) / BN;
-    const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * tiles_n;
+    const int tiles = full + (((M + 2 * BM - 1) / (2 * BM)) * tiles_n - full) * split;
     const int nkb = K / BK;
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < Cfg::STAGES; s++) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full_bar[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -602,7 +616,10 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t g = 0;
             bool ok = true;
             for (int t = cid; ok && t < tiles; t += ncl) {
-                const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN + rank * (BN / 2);
+                const PairTile tile = pair_tile<BN>(t, tiles_n, full, split);
+                // B rows of this CTA: its half of the tile's width (a full BN / 2-row box
+                // is loaded; rows past the sub-tile are not read by the MMA)
+                const int m0 = tile.mt * 2 * BM + rank * BM, n0 = tile.n0 + rank * (tile.nw / 2);
                 for (int kb = 0; kb < nkb; kb++, g++) {
                     const int s = g % Cfg::STAGES;
                     if (g >= (uint32_t)Cfg::STAGES &&
@@ -610,28 +627,29 @@ __global__ void __launch_bounds__(192, 1)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * Cfg::STAGE_BYTES);
                     const int tap = kb_per_tap > 0 ? kb / kb_per_tap : 0;
                     const int ka = kb_per_tap > 0 ? (kb % kb_per_tap) * BK : kb * BK;
                     load_stage<true>(smem + s * Cfg::STAGE_BYTES, BM, BN / 2, maps.m, nullptr,
-                                     leader_addr(&full[s]), ka, m0 + tap, kb * BK, n0);
+                                     leader_addr(&full_bar[s]), ka, m0 + tap, kb * BK, n0);
                 }
             }
         }
     } else if (warp == 1) {
         if (leader && lane == 0) {
-            constexpr uint32_t idt = idesc_tf32_pair(BN), idb = idesc_bf16_pair(BN);
             uint32_t g = 0;
             int it = 0;
             bool ok = true;
             for (int t = cid; ok && t < tiles; t += ncl, it++) {
+                const int nw = pair_tile<BN>(t, tiles_n, full, split).nw;
+                const uint32_t idt = idesc_tf32_pair(nw), idb = idesc_bf16_pair(nw);
                 const int buf = it & 1;
                 if (it >= 2 && !mbar_wait_cluster(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * BN;
                 for (int kb = 0; kb < nkb; kb++, g++) {
                     const int s = g % Cfg::STAGES;
-                    if (!mbar_wait_cluster(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
+                    if (!mbar_wait_cluster(&full_bar[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
                         ok = false;
                         break;
                     }
@@ -652,13 +670,14 @@ __global__ void __launch_bounds__(192, 1)
                 __all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
             if (!ok) break;
             tc_fence_after();
-            const int m0 = (t / tiles_n) * 2 * BM + rank * BM, n0 = (t % tiles_n) * BN;
+            const PairTile tile = pair_tile<BN>(t, tiles_n, full, split);
+            const int m0 = tile.mt * 2 * BM + rank * BM;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
             if (epi.tma)
-                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+                epilogue_tile_tma<BN>(epi, tl, m0, tile.n0, M, N, q, lane,
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, 0, tile.nw);
             else  // direct stores
-                epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane);
+                epilogue_tile<BN>(epi, tl, m0, tile.n0, M, N, q, lane, nullptr, tile.nw);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8u * buf);
@@ -795,8 +814,15 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     }
     const Maps6 maps = operand_maps(A, B, BM, BN / 2, true);
     const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
-    cfg.gridDim = dim3(2 * (tiles < max_clusters ? tiles : max_clusters));
-    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err));
+    const int clusters = tiles < max_clusters ? tiles : max_clusters;
+    // tail split: the R tiles of a partial last wave become R * split narrower tiles
+    // (split 2 or 4, with R * split <= clusters; widths stay multiples of 64 columns)
+    const int waves = tiles / clusters, rem = tiles - waves * clusters;
+    int split = 1;
+    if (waves >= 1 && rem > 0) split = clusters / rem >= 4 && BN / 4 >= 64 ? 4 : clusters / rem >= 2 ? 2 : 1;
+    const int full = tiles - rem;
+    cfg.gridDim = dim3(2 * clusters);
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err, full, split));
 }
 
 void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi& epi, int bn) {
