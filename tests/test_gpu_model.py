@@ -130,18 +130,23 @@ def test_batch_equals_single_runs(tiny_gpu_model, tiny_oracle):
         assert _gates_ok(r), r
 
 
-def test_device_batch_matches_host_batch(tiny_gpu_model):
+@pytest.mark.parametrize("mode,nclips", [("offline", 3), ("offline", 20), ("ultra_low_latency", 20)])
+def test_device_batch_matches_host_batch(tiny_gpu_model, mode, nclips):
+    """Host audio is uploaded in two phases (chunk step 0's samples, then the rest) and
+    in parts of 16 clips, each phase embedding only the groups its steps read; audio
+    already on the device takes one pass over every group.  Both give the same bits."""
     import torch
 
-    clips = [synth.clip(30 + i, 3.0 + i, 2) for i in range(3)]
+    clips = [synth.clip(30 + i, 3.0 + (i % 5) * 0.7, 2) for i in range(nclips)]
     lens = [c.size for c in clips]
     offs = list(np.cumsum([0] + lens[:-1]))
-    frames = tiny_gpu_model.batch_out_frames(lens, "offline")
+    frames = tiny_gpu_model.batch_out_frames(lens, mode)
     ooffs = list(np.cumsum([0] + frames[:-1]))
     d_audio = torch.from_numpy(np.concatenate(clips)).cuda()
     d_out = torch.zeros(sum(frames) * 8, dtype=torch.float32, device="cuda")
-    tiny_gpu_model.run_batch_device("offline", d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
-    host = tiny_gpu_model.run_batch(clips, "offline")
+    tiny_gpu_model.run_batch_device(mode, d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
+    host = tiny_gpu_model.run_batch(clips, mode)
     dev = d_out.cpu().numpy()
     for i, h in enumerate(host):
+        assert h.num_frames == frames[i]
         assert np.array_equal(dev[ooffs[i] * 8:(ooffs[i] + frames[i]) * 8].reshape(-1, 8), h.logits)
