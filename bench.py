@@ -205,8 +205,9 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="c4", choices=["c4", "c3"],
-                   help="c4: offline 60 s clips (headline); c3: ultra_low_latency streaming sessions")
+    p.add_argument("--workload", default="c4", choices=["c4", "c3", "c2"],
+                   help="c4: offline 60 s clips (headline); c3: ultra_low_latency streaming sessions; "
+                        "c2: one 60 min offline clip per GPU (sequential windows of one sequence)")
     p.add_argument("--clips", type=int, default=None, help="clips (c4) or sessions (c3) per GPU per step")
     p.add_argument("--session-seconds", type=float, default=600.0, help="c3 session length")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -231,6 +232,14 @@ def main():
         items = make_clips(rank, n_items, item_s)
         metric, desc = METRIC, (f"C4 offline: {n_items} x 60 s 16 kHz clips per GPU per step, random-init weights "
                                 "(seed 0), clips seeded 1000+")
+    elif args.workload == "c2":
+        import synth
+
+        mode, item_s, n_items = "offline", 3600.0, 1
+        items = [synth.config2_audio(3600.0)]
+        metric = "C2 offline RTFx (audio-s/wall-s) of one 60 min clip; per-window latency"
+        desc = ("C2 offline: one 60 min 16 kHz clip per GPU (replicas; ~133 sequential windows of one "
+                "sequence), random-init weights (seed 0)")
     else:
         import synth
 

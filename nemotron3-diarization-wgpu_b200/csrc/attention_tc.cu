@@ -120,8 +120,6 @@ __global__ void __launch_bounds__(THREADS, 2)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
-    const int valid = min(valid_arr[b], S);
-    const int nblk = (valid + KB - 1) / KB;
     const int row0 = b * S;  // first row of this sequence in Q / K, first column in V^T
 
     if (warp == 0 && lane == 0) {
@@ -143,6 +141,10 @@ __global__ void __launch_bounds__(THREADS, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // Q / K / V^T written by the previous kernel
+    griddep_launch_dependents();
+    const int valid = min(valid_arr[b], S);
+    const int nblk = (valid + KB - 1) / KB;
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
@@ -418,8 +420,7 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
         m.ch = m.cb = m.cl = m.qh;  // unused
     }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    attention_tc_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(m, S, valid, heads, ctx, ctx_tma, err);
-    N3D_CUDA(cudaGetLastError());
+    launch_pdl(attention_tc_kernel, grid, dim3(THREADS), SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma, err);
 }
 
 }  // namespace n3d

@@ -32,6 +32,8 @@ __device__ __forceinline__ float exp_f(float x) { return (float)exp((double)x); 
 // step's new embeddings, then zeros up to the batch stride.
 __global__ void assemble_kernel(const SeqStep* __restrict__ steps, const float* __restrict__ embeds,
                                 float* __restrict__ win, int stride, int hidden) {
+    griddep_wait();
+    griddep_launch_dependents();
     const int i = blockIdx.y, t = blockIdx.x;
     const SeqStep st = steps[i];
     const int prefix = st.ncache + st.nfifo;
@@ -66,6 +68,8 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
                                                            const float* __restrict__ logits, int stride,
                                                            long long logit_rows, CacheParams cp,
                                                            const float* __restrict__ silence, int P_max) {
+    griddep_wait();
+    griddep_launch_dependents();
     extern __shared__ float sm[];
     const int i = blockIdx.x;
     const SeqStep st = steps[i];
@@ -275,8 +279,7 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
 void launch_assemble(cudaStream_t s, const SeqStep* steps, int nseq, const float* embeds, float* win, int stride,
                      int hidden) {
     if (nseq <= 0 || stride <= 0) return;
-    assemble_kernel<<<dim3(stride, nseq), 128, 0, s>>>(steps, embeds, win, stride, hidden);
-    N3D_CUDA(cudaGetLastError());
+    launch_pdl(assemble_kernel, dim3(stride, nseq), dim3(128), 0, s, steps, embeds, win, stride, hidden);
 }
 
 size_t cache_update_smem(int stride, int ns, int P_max) {
@@ -296,9 +299,8 @@ void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const f
     }
     CacheParams cp{c.hidden, c.ns, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
                    c.latest_boost};
-    cache_update_kernel<<<nseq, 512, smem, s>>>(steps, win, logits, stride, (long long)(stride + 2) * c.sub, cp,
-                                                silence, P);
-    N3D_CUDA(cudaGetLastError());
+    launch_pdl(cache_update_kernel, dim3(nseq), dim3(512), smem, s, steps, win, logits, stride,
+               (long long)(stride + 2) * c.sub, cp, silence, P);
 }
 
 }  // namespace n3d

@@ -457,6 +457,8 @@ __global__ void __launch_bounds__(192, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // operands written by the previous kernel
+    griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -610,6 +612,8 @@ __global__ void __launch_bounds__(192, 1)
     cluster_sync_all();  // both CTAs' barriers exist before any cross-CTA arrive
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    griddep_wait();  // operands written by the previous kernel
+    griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -785,8 +789,7 @@ void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_p
     }
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    gemm_kernel<BN><<<grid, 192, Cfg::SMEM, s>>>(maps, M, N, K, kb_per_tap, epi, err);
-    N3D_CUDA(cudaGetLastError());
+    launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::SMEM, s, maps, M, N, K, kb_per_tap, epi, err);
 }
 
 template <int BN>
@@ -795,11 +798,13 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     using Cfg = PairCfg<BN>;
     static int max_clusters = 0;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cfg.blockDim = dim3(Cfg::THREADS);
@@ -822,6 +827,7 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     if (waves >= 1 && rem > 0) split = clusters / rem >= 4 && BN / 4 >= 64 ? 4 : clusters / rem >= 2 ? 2 : 1;
     const int full = tiles - rem;
     cfg.gridDim = dim3(2 * clusters);
+    cfg.numAttrs = 2;
     N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err, full, split));
 }
 
@@ -862,6 +868,10 @@ void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         bn = 512;  // 256 x 256 tiles on CTA pairs
     } else if (N % 128 == 0 || N > 64) {
         bn = 128;
+        // small launches (a single long clip's windows): 128 x 64 tiles when 128 x 128
+        // ones would leave more than half the SMs idle
+        const long long tiles = (long long)((M + BM - 1) / BM) * ((N + 127) / 128);
+        if (N % 64 == 0 && tiles < sm_count() / 2) bn = 64;
     } else {
         bn = 64;
     }

@@ -28,6 +28,8 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int VPL>
 __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
                                   const float* __restrict__ b, Split3Out out) {
+    griddep_wait();
+    griddep_launch_dependents();
     constexpr int COLS = VPL * 32;
     const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -430,9 +432,9 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
     const int warps = 8;
     const unsigned grid = (unsigned)((rows + warps - 1) / warps);
     if (cols == 512)
-        layer_norm_kernel<16><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out);
+        launch_pdl(layer_norm_kernel<16>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
     else if (cols == 1024)
-        layer_norm_kernel<32><<<grid, warps * 32, 0, s>>>(x, rows, w, b, out);
+        launch_pdl(layer_norm_kernel<32>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
     N3D_CUDA(cudaGetLastError());

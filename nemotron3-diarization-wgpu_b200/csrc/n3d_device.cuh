@@ -1,6 +1,6 @@
 // Device-side helpers shared by every sm_100a kernel of the diarization path:
 // mbarriers with bounded waits, TMA tile loads (never multicast), tcgen05
-// (TMEM allocation, UMMA issue/commit, TMEM loads) and the TF32 hi/lo split.
+// (TMEM allocation, UMMA issue/commit, TMEM loads), packed f32 pairs and the 3-term operand split.
 #pragma once
 
 #include <cstdint>
@@ -65,6 +65,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
         }
     }
     return true;
+}
+
+// ------------------------------------------------ programmatic dependent launch
+// Wait until the previous kernel of the stream has completed and its memory is
+// visible (returns at once when the kernel was not launched with launch_pdl).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel of the stream be scheduled (its own griddep_wait still waits
+// for this grid to complete).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ----------------------------------------------------------------------- TMA

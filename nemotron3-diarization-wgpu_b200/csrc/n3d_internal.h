@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace n3d {
 
@@ -19,6 +20,26 @@ struct Error : std::runtime_error {
 
 void cuda_check(cudaError_t e, const char* what);
 #define N3D_CUDA(x) ::n3d::cuda_check((x), #x)
+
+// Launch with programmatic stream serialization: the kernel may become resident and
+// run its set-up while the previous kernel of the stream drains.  Every kernel launched
+// this way calls griddep_wait() (n3d_device.cuh) before it touches global memory that
+// another kernel writes or reads, and griddep_launch_dependents() right after, so at
+// most two such kernels are in flight.
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // ------------------------------------------------------------------ GEMM
 
