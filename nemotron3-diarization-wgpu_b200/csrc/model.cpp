@@ -385,6 +385,7 @@ Model::Model(const std::string& dir, int device) : device_(device) {
     N3D_CUDA(cudaStreamCreateWithFlags(&own_stream_, cudaStreamNonBlocking));
     stream_ = own_stream_;
     N3D_CUDA(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
+    N3D_CUDA(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking));
     N3D_CUDA(cudaEventCreateWithFlags(&upload_start_, cudaEventDisableTiming));
     N3D_CUDA(cudaMalloc(&dev_err_, sizeof(int)));
     N3D_CUDA(cudaMemset(dev_err_, 0, sizeof(int)));
@@ -402,6 +403,9 @@ Model::~Model() {
     if (copy_stream_) cudaStreamSynchronize(copy_stream_);
     for (cudaEvent_t e : upload_ev_) cudaEventDestroy(e);
     if (host_stage_) cudaFreeHost(host_stage_);
+    for (auto& kv : tower_graphs_)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (capture_stream_) cudaStreamDestroy(capture_stream_);
     if (upload_start_) cudaEventDestroy(upload_start_);
     if (copy_stream_) cudaStreamDestroy(copy_stream_);
     for (void* p : owned_) cudaFree(p);
@@ -572,6 +576,7 @@ void* Model::ws(const char* name, size_t bytes) {
         b.p = nullptr;
         N3D_CUDA(cudaMalloc(&b.p, bytes));
         b.bytes = bytes;
+        ws_gen_++;  // captured tower graphs may hold the old address
     }
     return b.p;
 }
@@ -1130,6 +1135,52 @@ const float* Model::mel_launch(const float* d_audio, const MelJob& job,
     return embeds;
 }
 
+void Model::tower_step(int B, int S, const int* d_len, const int* d_valid) {
+    if (B > kGraphMaxSeqs || prof_) {
+        tower(B, S, d_len, d_valid, nullptr);
+        return;
+    }
+    int* len_slot = (int*)ws("graph_len", (size_t)B * 4);
+    int* valid_slot = (int*)ws("graph_valid", (size_t)B * 4);
+    N3D_CUDA(cudaMemcpyAsync(len_slot, d_len, (size_t)B * 4, cudaMemcpyDeviceToDevice, stream_));
+    N3D_CUDA(cudaMemcpyAsync(valid_slot, d_valid, (size_t)B * 4, cudaMemcpyDeviceToDevice, stream_));
+    const std::pair<int, int> key{B, S};
+    auto it = tower_graphs_.find(key);
+    if (it == tower_graphs_.end()) {  // first step of this shape: eager
+        tower(B, S, len_slot, valid_slot, nullptr);
+        tower_graphs_.emplace(key, TowerGraph{});
+        return;
+    }
+    TowerGraph& g = it->second;
+    if (!g.exec || g.gen != ws_gen_) {
+        if (g.exec) N3D_CUDA(cudaGraphExecDestroy(g.exec));
+        g.exec = nullptr;
+        // capture on a private stream (the caller's stream may be the legacy default
+        // stream); every workspace buffer already has its size, so nothing allocates
+        const uint64_t gen = ws_gen_;
+        cudaStream_t caller = stream_;
+        cudaGraph_t graph = nullptr;
+        N3D_CUDA(cudaStreamBeginCapture(capture_stream_, cudaStreamCaptureModeThreadLocal));
+        stream_ = capture_stream_;
+        try {
+            tower(B, S, len_slot, valid_slot, nullptr);
+        } catch (...) {
+            stream_ = caller;
+            cudaStreamEndCapture(capture_stream_, &graph);
+            if (graph) cudaGraphDestroy(graph);
+            throw;
+        }
+        stream_ = caller;
+        N3D_CUDA(cudaStreamEndCapture(capture_stream_, &graph));
+        const cudaError_t e = cudaGraphInstantiate(&g.exec, graph, 0);
+        cudaGraphDestroy(graph);
+        N3D_CUDA(e);
+        if (ws_gen_ != gen) throw Error(kStatusGpu, "tower graph: the workspace changed during capture");
+        g.gen = gen;
+    }
+    N3D_CUDA(cudaGraphLaunch(g.exec, stream_));
+}
+
 void Model::run_step(const SeqStep* d_st, int B, int S, const int* d_len, const int* d_valid, const float* embeds) {
     const Config& c = cfg_;
     const int h = c.hidden;
@@ -1142,7 +1193,7 @@ void Model::run_step(const SeqStep* d_st, int B, int S, const int* d_len, const 
     prof_begin();
     launch_assemble(stream_, d_st, B, embeds, win, S, h);
     prof_end(K_ASSEMBLE, 0, 2.0 * B * S * h * 4);
-    tower(B, S, d_len, d_valid, nullptr);
+    tower_step(B, S, d_len, d_valid);
     head(B, S, d_len);
     const CacheConst cc{h, c.num_speakers, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
                         c.latest_boost};

@@ -194,6 +194,13 @@ class Model {
     void prof_collect();
     void upload_weights(const std::string& dir);
     void tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain);
+    // The tower of one chunk-loop step.  Small batches (at most kGraphMaxSeqs
+    // sequences: the windows of a single long clip, a few sessions) are latency-bound
+    // chains of ~220 short kernels, so the tower runs as a CUDA graph, one per (B, S),
+    // captured on the second step of that shape (the first sizes the workspace) and
+    // captured again after any workspace buffer is reallocated.  The step's key counts
+    // go through fixed slot buffers so that one graph serves every step.
+    void tower_step(int B, int S, const int* d_len, const int* d_valid);
     void head(int B, int S, const int* d_seq_len);
     // Log-mel + embedder of `segs` (segment i's samples start at d_audio[base[i]]).
     // mel_prepare uploads the segment table (from host memory, so call it before the
@@ -231,6 +238,14 @@ class Model {
     // clips, so the mel of part k overlaps the upload of part k + 1.
     static constexpr int kUploadClips = 16;
     cudaStream_t copy_stream_ = nullptr;
+    static constexpr int kGraphMaxSeqs = 16;
+    struct TowerGraph {
+        cudaGraphExec_t exec = nullptr;
+        uint64_t gen = 0;  // ws_gen_ at capture
+    };
+    std::map<std::pair<int, int>, TowerGraph> tower_graphs_;
+    uint64_t ws_gen_ = 0;  // bumped whenever a workspace buffer is (re)allocated
+    cudaStream_t capture_stream_ = nullptr;
     // Pinned staging of a batch's logits on their way to the host (grown on demand).
     float* host_stage_ = nullptr;
     size_t host_stage_bytes_ = 0;

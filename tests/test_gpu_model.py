@@ -97,6 +97,22 @@ def test_offline_on_tiny_model_many_windows(tiny_gpu_model, tiny_oracle):
     assert _gates_ok(r), r
 
 
+def test_tower_graph_replay_matches_eager_launches(tiny_gpu_model):
+    """Single-clip windows run the encoder tower as a replayed CUDA graph; with the
+    per-kernel profiler on, every kernel is launched one by one instead.  Same bits."""
+    a = synth.clip(12, 9.0, 3)
+    tiny_gpu_model.profile_enable(True)
+    try:
+        eager = tiny_gpu_model.run_offline(a)
+    finally:
+        tiny_gpu_model.profile_enable(False)
+    g1 = tiny_gpu_model.run_offline(a)
+    g2 = tiny_gpu_model.run_offline(a)
+    assert eager.num_chunks > 3
+    assert np.array_equal(eager.logits, g1.logits)
+    assert np.array_equal(g1.logits, g2.logits)
+
+
 @pytest.mark.parametrize("n", [0, 1, 159, 160, 161, 2720, 54_400, 54_401])
 def test_offline_edge_lengths(tiny_gpu_model, tiny_oracle, n):
     a = synth.clip(13, max(n, 1) / 16000.0, 2)[:n]
