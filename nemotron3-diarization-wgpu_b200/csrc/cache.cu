@@ -46,10 +46,11 @@ __global__ void assemble_kernel(const SeqStep* __restrict__ steps, const float* 
     for (int c = threadIdx.x; c < hidden / 4; c += blockDim.x) dst[c] = src ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-// Stable descending order on (value, index): a goes first iff it has the larger
-// value, or an equal value and the smaller index (Rust's stable `sort_by`).
-__device__ __forceinline__ bool before(float va, int ia, float vb, int ib) {
-    return va > vb || (va == vb && ia < ib);
+// Order-preserving unsigned image of a float: a > b iff key(a) > key(b) (-inf lowest,
+// +inf highest; the scores here are never NaN).
+__device__ __forceinline__ uint32_t order_key(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 struct CacheParams {
@@ -61,8 +62,12 @@ struct CacheParams {
 //   probs [S*ns]      pooled step probabilities (_pool_probs)
 //   cand  [ne*ns]     probabilities of the compression candidates
 //   sc    [ne*ns]     frame scores
-//   key   [P] / idx [P] (int) bitonic-sorted flat scores (P = pow2 >= ns*(ne+n_sil))
-//   aux   [P] (int)   ranks / selection flags
+//   key   [P] (uint)  order keys of the flat speaker-major scores (P >= ns*(ne+n_sil))
+//   idx   [P] (int)   the picked flat indices, ascending
+//   aux   [P] (int)   selection flags
+// "The first k in (score descending, index ascending) order" -- Rust's stable sort
+// followed by a truncation -- is computed as a selection: an MSB-first radix select
+// of the k-th key, then the elements above it plus the lowest-index ties.
 __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __restrict__ steps,
                                                            const float* __restrict__ win,
                                                            const float* __restrict__ logits, int stride,
@@ -166,87 +171,117 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
         if (e / ns >= cp.cache_len) sc[e] = __fadd_rn(sc[e], cp.latest_boost);
     __syncthreads();
     // ---- _boost_scores twice (src/streaming.rs:333-346): per speaker, the k best frames
+    // (one warp per speaker selects them)
+    const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
     for (int pass = 0; pass < 2; pass++) {
-        const int k = pass == 0 ? cp.k_strong : cp.k_weak;
+        const int kk = min(pass == 0 ? cp.k_strong : cp.k_weak, ne);
         const float boost = pass == 0 ? 2.0f * kLn2 : kLn2;
-        for (int e = tid; e < ne * ns; e += nt) {
-            const int f = e / ns, s = e % ns;
-            const float v = sc[e];
-            int rank = 0;
-            for (int g = 0; g < ne && rank < k; g++) {
-                const float u = sc[g * ns + s];
-                rank += (u > v) || (u == v && g < f);
+        for (int s = warp; s < ns; s += nwarps) {
+            uint32_t prefix = 0, mask = 0;
+            int need = kk;
+            for (int bit = 31; kk > 0 && bit >= 0; bit--) {
+                const uint32_t b = 1u << bit;
+                int c = 0;
+                for (int f0 = 0; f0 < ne; f0 += 32) {
+                    const int f = f0 + lane;
+                    const uint32_t kf = f < ne ? order_key(sc[f * ns + s]) : 0u;
+                    c += __popc(__ballot_sync(0xffffffffu, f < ne && (kf & mask) == prefix && (kf & b)));
+                }
+                if (c >= need) prefix |= b;
+                else need -= c;
+                mask |= b;
             }
-            aux[e] = rank < k;
+            // above the k-th key, or equal to it and among the first `need` such frames
+            int ties = 0;
+            for (int f0 = 0; f0 < ne; f0 += 32) {
+                const int f = f0 + lane;
+                const uint32_t kf = f < ne ? order_key(sc[f * ns + s]) : 0u;
+                const bool eq = kk > 0 && f < ne && kf == prefix;
+                const unsigned m = __ballot_sync(0xffffffffu, eq);
+                const int rank_eq = ties + __popc(m & ((1u << lane) - 1u));
+                if (f < ne) aux[f * ns + s] = kk > 0 && (kf > prefix || (eq && rank_eq < need));
+                ties += __popc(m);
+            }
         }
         __syncthreads();
         for (int e = tid; e < ne * ns; e += nt)
             if (aux[e]) sc[e] = __fadd_rn(sc[e], boost);
         __syncthreads();
     }
-    // ---- flat speaker-major scores with +inf silence slots, bitonic sort (value desc, index asc)
+    // ---- flat speaker-major scores with +inf silence slots; keep the first cache_len in
+    // (score desc, flat index asc) order, except -inf ones (src/streaming.rs:436-463)
     const int nsc = ne + cp.n_sil;
     const int total = ns * nsc;
-    int P = 1;
-    while (P < total) P <<= 1;
-    for (int e = tid; e < P; e += nt) {
-        float v = -INFINITY;
-        if (e < total) {
-            const int s = e / nsc, f = e % nsc;
-            v = f < ne ? sc[f * ns + s] : INFINITY;
-        }
-        key[e] = v;
-        idx[e] = e;  // padding entries carry indices >= total, so they sort after every real one
+    const int L = min(cp.cache_len, total);
+    uint32_t* fkey = reinterpret_cast<uint32_t*>(key);
+    for (int e = tid; e < total; e += nt) {
+        const int sp = e / nsc, f = e % nsc;
+        fkey[e] = order_key(f < ne ? sc[f * ns + sp] : INFINITY);
     }
     __syncthreads();
-    for (int k = 2; k <= P; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int e = tid; e < P; e += nt) {
-                const int p = e ^ j;
-                if (p > e) {
-                    const bool asc = (e & k) == 0;  // this block ends in "before" order
-                    const float ve = key[e], vp = key[p];
-                    const int ie = idx[e], ip = idx[p];
-                    const bool swap = asc ? before(vp, ip, ve, ie) : before(ve, ie, vp, ip);
-                    if (swap) {
-                        key[e] = vp;
-                        key[p] = ve;
-                        idx[e] = ip;
-                        idx[p] = ie;
-                    }
-                }
-            }
-            __syncthreads();
-        }
-    }
-    // ---- topk = first cache_len; -inf picks become the sentinel; indices sorted ascending
-    const int L = cp.cache_len;
-    for (int e = tid; e < P; e += nt) aux[e] = 0;
-    __syncthreads();
-    for (int r = tid; r < L && r < total; r += nt)
-        if (key[r] != -INFINITY) aux[idx[r]] = 1;
-    __syncthreads();
-    // exclusive scan of aux over [0, total) -> position of each kept index (block scan in chunks)
+    __shared__ int part[16];
     __shared__ int carry, warp_tot[16];
+    uint32_t prefix = 0, mask = 0;
+    int need = L;
+    for (int bit = 31; L > 0 && bit >= 0; bit--) {
+        const uint32_t b = 1u << bit;
+        int c = 0;
+        for (int e = tid; e < total; e += nt) c += (fkey[e] & mask) == prefix && (fkey[e] & b);
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0) part[warp] = c;
+        __syncthreads();
+        int sum = 0;
+        for (int q = 0; q < nwarps; q++) sum += part[q];
+        __syncthreads();
+        if (sum >= need) prefix |= b;
+        else need -= sum;
+        mask |= b;
+    }
+    // flags: above the L-th key, or equal to it among the first `need` in flat order
+    // (block scan of the ties); -inf picks become the sentinel, i.e. are dropped
+    const uint32_t ninf = order_key(-INFINITY);
+    if (tid == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < total; base += nt) {
+        const int e = base + tid;
+        const bool in = e < total && L > 0;
+        const uint32_t ke = e < total ? fkey[e] : 0u;
+        const int eq = in && ke == prefix;
+        int x = eq;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[warp] = x;
+        __syncthreads();
+        int woff = 0;
+        for (int q = 0; q < warp; q++) woff += warp_tot[q];
+        const int rank_eq = carry + woff + x - eq;
+        if (e < total) aux[e] = in && ke != ninf && (ke > prefix || (eq && rank_eq < need));
+        __syncthreads();
+        if (tid == nt - 1) carry = rank_eq + eq;
+        __syncthreads();
+    }
+    // exclusive scan of aux over [0, total) -> position of each kept index (block scan in chunks)
     if (tid == 0) carry = 0;
     __syncthreads();
     for (int base = 0; base < total; base += nt) {
         const int e = base + tid;
         const int flag = e < total ? aux[e] : 0;
         int x = flag;
-        const int lane = tid & 31, w = tid >> 5;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, x, o);
             if (lane >= o) x += y;
         }
-        if (lane == 31) warp_tot[w] = x;
+        if (lane == 31) warp_tot[warp] = x;
         __syncthreads();
         int woff = 0;
-        for (int q = 0; q < w; q++) woff += warp_tot[q];
+        for (int q = 0; q < warp; q++) woff += warp_tot[q];
         const int pos = carry + woff + x - flag;
         __syncthreads();
-        if (e < total && flag) idx[pos] = e;  // idx reused as the picked list (sorted ascending)
+        if (e < total && flag) idx[pos] = e;  // the picked list (sorted ascending)
         if (tid == nt - 1) carry = pos + flag;
         __syncthreads();
     }
