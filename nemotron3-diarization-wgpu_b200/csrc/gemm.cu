@@ -28,6 +28,7 @@
 
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <map>
 #include <mutex>
@@ -426,7 +427,7 @@ struct GemmCfg {
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
-                const __grid_constant__ Epi epi, int* err) {
+                const __grid_constant__ Epi epi, int* err, int ksplit, int Mp) {
     using Cfg = GemmCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -438,7 +439,9 @@ __global__ void __launch_bounds__(192, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tiles_n = (N + BN - 1) / BN;
-    const int tiles = ((M + BM - 1) / BM) * tiles_n;
+    // tile t = (output tile, k split): split ks covers k-blocks [ks nkb / ksplit,
+    // (ks + 1) nkb / ksplit) and stores its partial tile at row offset ks * Mp
+    const int tiles = ((M + BM - 1) / BM) * tiles_n * ksplit;
     const int nkb = K / BK;
 
     if (warp == 0 && lane == 0) {
@@ -465,8 +468,9 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t g = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
-                const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
-                for (int kb = 0; kb < nkb; kb++, g++) {
+                const int tmn = t / ksplit, ks = t - tmn * ksplit;
+                const int m0 = (tmn / tiles_n) * BM, n0 = (tmn % tiles_n) * BN;
+                for (int kb = ks * nkb / ksplit; kb < (ks + 1) * nkb / ksplit; kb++, g++) {
                     const int s = g % Cfg::STAGES;
                     if (g >= (uint32_t)Cfg::STAGES &&
                         !mbar_wait(&empty[s], ((g / Cfg::STAGES) - 1) & 1, err, DEV_TIMEOUT_TMA_EMPTY)) {
@@ -492,14 +496,15 @@ __global__ void __launch_bounds__(192, 1)
                 if (it >= 2 && !mbar_wait(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * Cfg::ACC_COLS;
-                for (int kb = 0; kb < nkb; kb++, g++) {
+                const int ks = t % ksplit, kb0 = ks * nkb / ksplit;
+                for (int kb = kb0; kb < (ks + 1) * nkb / ksplit; kb++, g++) {
                     const int s = g % Cfg::STAGES;
                     if (!mbar_wait(&full[s], (g / Cfg::STAGES) & 1, err, DEV_TIMEOUT_TMA_FULL)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    mma_kblock<false>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN, idt, idb, kb == 0);
+                    mma_kblock<false>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN, idt, idb, kb == kb0);
                     umma_commit(&empty[s]);
                 }
                 if (ok) umma_commit(&acc_full[buf]);
@@ -521,10 +526,11 @@ __global__ void __launch_bounds__(192, 1)
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
             if (!ok) break;
             tc_fence_after();
-            const int m0 = (t / tiles_n) * BM, n0 = (t % tiles_n) * BN;
+            const int tmn = t / ksplit, ks = t - tmn * ksplit;
+            const int m0 = (tmn / tiles_n) * BM, n0 = (tmn % tiles_n) * BN;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS;
-            if (epi.tma)
-                epilogue_tile_tma<BN>(epi, tl, m0, n0, M, N, q, lane,
+            if (epi.tma)  // a k split's partial rows start at ks * Mp (rows past M land in padding)
+                epilogue_tile_tma<BN>(epi, tl, m0 + ks * Mp, n0, ksplit > 1 ? ksplit * Mp : M, N, q, lane,
                                       smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
             else
                 epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane, w2s);
@@ -695,6 +701,30 @@ __global__ void __launch_bounds__(192, 1)
     if (warp == 1) tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
 }
 
+// ------------------------------------------------------ split-K reduction
+// dst[r, c] += ((p_0 + p_1 + ...) + bias[c]) over the ks partial tiles (rows r of
+// split s at parts[(s * Mp + r) * N + c]), in split order: the same bits every run.
+__global__ void split_reduce_kernel(const float* __restrict__ parts, int ks, long long Mp, int M, int N,
+                                    const float* __restrict__ bias, float* __restrict__ dst, long long ldd) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const long long n4 = (long long)M * (N / 4);
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / (N / 4);
+        const int c = (int)(i - r * (N / 4)) * 4;
+        float4 a = *reinterpret_cast<const float4*>(parts + r * N + c);
+        for (int sp = 1; sp < ks; sp++) {
+            const float4 b = *reinterpret_cast<const float4*>(parts + ((long long)sp * Mp + r) * N + c);
+            a = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+        }
+        if (bias) a = make_float4(__fadd_rn(a.x, bias[c]), __fadd_rn(a.y, bias[c + 1]), __fadd_rn(a.z, bias[c + 2]),
+                                  __fadd_rn(a.w, bias[c + 3]));
+        float4* d = reinterpret_cast<float4*>(dst + r * ldd + c);
+        const float4 x = *d;
+        *d = make_float4(__fadd_rn(x.x, a.x), __fadd_rn(x.y, a.y), __fadd_rn(x.z, a.z), __fadd_rn(x.w, a.w));
+    }
+}
+
 // ------------------------------------------------------------ tensor maps
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -780,16 +810,18 @@ int sm_count() {
 }
 
 template <int BN>
-void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err) {
+void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err,
+                int ksplit = 1, int Mp = 0) {
     using Cfg = GemmCfg<BN>;
     static bool attr = false;
     if (!attr) {
         N3D_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
         attr = true;
     }
-    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+    const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * ksplit;
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::SMEM, s, maps, M, N, K, kb_per_tap, epi, err);
+    launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::SMEM, s, maps, M, N, K, kb_per_tap, epi, err, ksplit,
+               Mp);
 }
 
 template <int BN>
@@ -876,6 +908,29 @@ void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         bn = 64;
     }
     check_shape(A, B, K, epi, bn == 512 ? 256 : bn);
+    if ((bn == 64 || bn == 128) && epi.mode == EPI_STORE && epi.tma && epi.reduce && epi.split_ws && kb_per_tap == 0 &&
+        N % 4 == 0 && epi.out && epi.ldo > 0) {
+        // split K (2..4 ways, >= 4 k-blocks each) while the tiles still fit one wave
+        const int mt = (M + BM - 1) / BM, tiles = mt * ((N + bn - 1) / bn), nkb = K / BK, sms = sm_count();
+        int ks = 1;
+        while (ks < 4 && tiles * (ks + 1) <= sms && nkb / (ks + 1) >= 4) ks++;
+        const long long Mp = (long long)mt * BM;
+        if (ks > 1 && (long long)ks * Mp * N <= epi.split_ws_floats) {
+            Epi ep = epi;  // partial tiles: plain TMA stores, no bias
+            ep.reduce = 0;
+            ep.bias = nullptr;
+            ep.map_out = make_store_map(epi.split_ws, ks * Mp, N, N);
+            if (bn == 64)
+                launch_one<64>(s, operand_maps(A, B, BM, 64, true), M, N, K, 0, ep, err, ks, (int)Mp);
+            else
+                launch_one<128>(s, operand_maps(A, B, BM, 128, true), M, N, K, 0, ep, err, ks, (int)Mp);
+            const long long n4 = (long long)M * (N / 4);
+            const int blocks = (int)std::min<long long>((n4 + 255) / 256, 4LL * sms);
+            launch_pdl(split_reduce_kernel, dim3(blocks), dim3(256), 0, s, (const float*)epi.split_ws, ks, Mp, M, N,
+                       epi.bias, epi.out, epi.ldo);
+            return;
+        }
+    }
     switch (bn) {
         case 64: launch_one<64>(s, operand_maps(A, B, BM, 64, true), M, N, K, kb_per_tap, epi, err); break;
         case 128: launch_one<128>(s, operand_maps(A, B, BM, 128, true), M, N, K, kb_per_tap, epi, err); break;

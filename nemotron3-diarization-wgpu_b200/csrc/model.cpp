@@ -725,6 +725,13 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     eo.tma = 1;
     eo.reduce = 1;
     eo.map_out = make_store_map(x, M, h, h);
+    eo.out = x;
+    eo.ldo = h;
+    if (M <= 2048) {  // small launches may split K (gemm_split3): 4 partial [M rounded to 128, h] tiles
+        const long long mp = (M + 127) / 128 * 128;
+        eo.split_ws = (float*)ws("split_ws", (size_t)4 * mp * h * 4);
+        eo.split_ws_floats = 4 * mp * h;
+    }
     Epi e1;  // fc1: GELU(acc + bias) -> 3-term split
     e1.mode = EPI_GELU_SPLIT;
     e1.tma = 1;

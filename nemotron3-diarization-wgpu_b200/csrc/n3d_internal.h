@@ -83,6 +83,12 @@ struct Epi {
     // EPI_STORE through TMA only: add the tile into map_out's fp32 destination
     // (cp.reduce.async.bulk.tensor .add; each element is added exactly once).
     int reduce = 0;
+    // Optional split-K scratch for such reduce-add GEMMs (destination `out`, row
+    // stride `ldo`): when a launch would leave most SMs idle, K is split over up to 4
+    // CTAs per tile, each writing its partial tile here, and a second kernel adds
+    // ((p0 + p1 + ...) + bias) into the destination in split order (deterministic).
+    float* split_ws = nullptr;
+    long long split_ws_floats = 0;
     CUtensorMap map_out, map_out2, map_out3, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
