@@ -191,7 +191,7 @@ float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate);
 
 /* tensor::linear (src/tensor.rs:22-57) on device buffers: d_y[rows, out] =
  * d_x[rows, cols] * d_w[out, cols]^T + d_bias (nullable).  cols % 32 == 0.
- * Uses temporary device memory for the TF32 hi/lo operand split. */
+ * Uses temporary device memory for the 3-term operand split (hi, hb, lb). */
 n3d_status n3d_linear(int device, const float *d_x, size_t rows, size_t cols, const float *d_w, size_t out,
                       const float *d_bias, float *d_y);
 
