@@ -1162,6 +1162,18 @@ void Model::tower_step(int B, int S, const int* d_len, const int* d_valid) {
     if (!g.exec || g.gen != ws_gen_) {
         if (g.exec) N3D_CUDA(cudaGraphExecDestroy(g.exec));
         g.exec = nullptr;
+        // bound the host memory of cached graphs (~220 kernel nodes each): past
+        // kGraphCacheMax captured shapes, drop them all and start over
+        int captured = 0;
+        for (const auto& kv : tower_graphs_) captured += kv.second.exec != nullptr;
+        if (captured >= kGraphCacheMax) {
+            N3D_CUDA(cudaStreamSynchronize(stream_));
+            for (auto& kv : tower_graphs_)
+                if (kv.second.exec) {
+                    N3D_CUDA(cudaGraphExecDestroy(kv.second.exec));
+                    kv.second.exec = nullptr;
+                }
+        }
         // capture on a private stream (the caller's stream may be the legacy default
         // stream); every workspace buffer already has its size, so nothing allocates
         const uint64_t gen = ws_gen_;

@@ -239,6 +239,7 @@ class Model {
     static constexpr int kUploadClips = 16;
     cudaStream_t copy_stream_ = nullptr;
     static constexpr int kGraphMaxSeqs = 16;
+    static constexpr int kGraphCacheMax = 64;
     struct TowerGraph {
         cudaGraphExec_t exec = nullptr;
         uint64_t gen = 0;  // ws_gen_ at capture
