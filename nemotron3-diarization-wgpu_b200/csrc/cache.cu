@@ -47,9 +47,10 @@ __global__ void assemble_kernel(const SeqStep* __restrict__ steps, const float* 
 }
 
 // Order-preserving unsigned image of a float: a > b iff key(a) > key(b) (-inf lowest,
-// +inf highest; the scores here are never NaN).
+// +inf highest; the scores here are never NaN).  -0 and +0 compare equal in the
+// reference's sort, so -0 is first mapped to +0 (adding +0 in round-to-nearest).
 __device__ __forceinline__ uint32_t order_key(float v) {
-    const uint32_t u = __float_as_uint(v);
+    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.0f));
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
