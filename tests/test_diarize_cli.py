@@ -1,0 +1,104 @@
+"""The `diarize` command-line tool (nemotron3-diarization-wgpu_b200/diarize, built from
+csrc/diarize.cpp): the reference's src/bin/diarize.rs over the C ABI.
+
+CPU: usage, argument errors, and a clear failure when no B200 is present.  GPU: the
+JSON report (reference field set, serde_json's sorted key order) from .npy and 16-bit
+WAV input, checked against the Python API on the same samples."""
+
+import json
+import math
+import os
+import subprocess
+import wave
+
+import numpy as np
+import pytest
+
+import synth
+from conftest import gpu_available
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CLI = os.path.join(ROOT, "nemotron3-diarization-wgpu_b200", "diarize")
+FIELDS = ["audio", "cache_compressed", "cache_frames", "duration_s", "fifo_frames", "forward_s", "load_s", "mode",
+          "num_chunks", "num_frames", "num_segments", "num_speakers", "rtfx", "segments", "speakers"]
+
+
+def run(*args):
+    if not os.path.exists(CLI):
+        pytest.skip("diarize is not built (make -C nemotron3-diarization-wgpu_b200)")
+    return subprocess.run([CLI, *args], capture_output=True, text=True, timeout=600)
+
+
+def test_usage():
+    r = run("--help")
+    assert r.returncode == 0 and "usage: diarize" in r.stdout and "ultra_low_latency" in r.stdout
+
+
+@pytest.mark.parametrize("args,msg", [(["--bogus"], "unknown flag --bogus"), ([], "no audio file given"),
+                                      (["x.npy", "--mode", "fast"], "unknown mode fast"),
+                                      (["x.npy", "--out"], "--out needs a value")])
+def test_argument_errors(args, msg):
+    r = run(*args)
+    assert r.returncode == 1 and msg in r.stderr
+
+
+def test_unreadable_audio_is_an_error(tmp_path):
+    p = tmp_path / "bad.npy"
+    p.write_bytes(b"not numpy")
+    r = run(str(p))
+    assert r.returncode == 1 and "not a .npy file" in r.stderr
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks the failure without a GPU")
+def test_without_a_gpu_model_load_fails_cleanly(tmp_path, tiny_checkpoint_dir):
+    p = tmp_path / "a.npy"
+    np.save(p, synth.clip(3, 1.0, 2))
+    r = run(str(p), "--model", tiny_checkpoint_dir)
+    assert r.returncode == 1 and "model load" in r.stderr
+
+
+def hundredths(v):
+    """(v as f64 * 100).round() / 100 (src/segments.rs:31-33): halves round away from zero."""
+    return math.floor(float(v) * 100.0 + 0.5) / 100.0
+
+
+def _write_wav16(path, x):
+    pcm = np.clip(np.round(x * 32768.0), -32768, 32767).astype("<i2")
+    with wave.open(str(path), "wb") as w:
+        w.setnchannels(1)
+        w.setsampwidth(2)
+        w.setframerate(16000)
+        w.writeframes(pcm.tobytes())
+    return pcm.astype(np.float32) / np.float32(32768.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fmt,mode", [("npy", "offline"), ("wav", "ultra_low_latency")])
+def test_report_matches_the_python_api(tmp_path, tiny_checkpoint_dir, tiny_gpu_model, fmt, mode):
+    import n3d
+
+    x = synth.clip(21, 6.0, 3)
+    path = tmp_path / f"clip.{fmt}"
+    if fmt == "npy":
+        np.save(path, x)
+        samples = x
+    else:
+        samples = _write_wav16(path, x)
+    out = tmp_path / "report.json"
+    r = run(str(path), "--model", tiny_checkpoint_dir, "--mode", mode, "--out", str(out))
+    assert r.returncode == 0, r.stderr
+    text = out.read_text()
+    rep = json.loads(text)
+    assert list(rep) == FIELDS  # serde_json prints object keys sorted
+    ref = tiny_gpu_model.run_offline(samples) if mode == "offline" else tiny_gpu_model.run_streaming(samples, mode)
+    assert rep["mode"] == mode.replace("_", "")
+    assert (rep["num_frames"], rep["num_chunks"], rep["cache_frames"], rep["fifo_frames"], rep["cache_compressed"]) == \
+        (ref.num_frames, ref.num_chunks, ref.cache_frames, ref.fifo_frames, ref.cache_compressed)
+    assert rep["duration_s"] == math.floor(len(samples) / 16000.0 * 1000.0 + 0.5) / 1000.0
+    segs = n3d.extract_speaker_dict(ref.logits, ref.num_frames, 8, n3d.frame_duration(160, 16000))
+    assert rep["num_segments"] == len(segs) == len(rep["segments"])
+    for got, s in zip(rep["segments"], segs):
+        assert list(got) == ["End", "Speaker", "Start"]
+        assert got["Speaker"] == s.speaker
+        assert got["Start"] == hundredths(s.start) and got["End"] == hundredths(s.end)
+    assert rep["speakers"] == sorted({s.speaker for s in segs}) and rep["num_speakers"] == len(rep["speakers"])
