@@ -91,10 +91,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
+def item_seeds(workload: str, rank: int, n_items: int) -> list:
+    """Seeds of one rank's clips (c4) or sessions (c3): disjoint across ranks, so every
+    rank runs its own audio (weak scaling).  c2 runs the same 60 min clip on every rank."""
+    if workload == "c4":
+        return [rank * 100000 + i for i in range(n_items)]
+    if workload == "c3":
+        return [rank * n_items + i for i in range(n_items)]
+    return [0] * n_items
+
+
 def make_clips(rank: int, n: int, seconds: float):
     import synth
 
-    return [synth.config4_clip(rank * 100000 + i, seconds) for i in range(n)]
+    return [synth.config4_clip(s, seconds) for s in item_seeds("c4", rank, n)]
 
 
 def oracle_rtfx(ckpt: str, clip: np.ndarray, reps: int = 1):
@@ -132,7 +142,11 @@ def live_sessions(model, items, mode: str, push_samples: int):
     return np.array(lat), total
 
 
-def dist_setup():
+def dist_setup(backend: str | None = None, timeout_s: float = 600.0):
+    """Join the process group that torchrun describes (RANK, LOCAL_RANK, WORLD_SIZE,
+    MASTER_ADDR, MASTER_PORT).  NCCL when a GPU is present; gloo runs the same host
+    logic on CPU.  A short `timeout_s` ends a collective with an error when a rank is
+    gone instead of leaving the others waiting."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -142,24 +156,57 @@ def dist_setup():
         import torch
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        kw = {}
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            kw["device_id"] = torch.device("cuda", local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
     return world, rank, local
 
 
-def checkpoint(rank: int, world: int) -> str:
-    import synth
-
-    d = os.path.join(tempfile.gettempdir(), "n3d_bench_ckpt_seed0")
-    if rank == 0 and not os.path.exists(os.path.join(d, "model.safetensors")):
-        tmp = d + f".tmp{os.getpid()}"
-        synth.write_checkpoint(tmp, seed=0)
-        os.replace(tmp, d) if not os.path.exists(d) else None
+def barrier(world: int) -> None:
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    """The largest per-rank value (a device time): the job ends with its slowest rank."""
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_rate(world: int, n_items: int, item_s: float, steps: int, ms: float) -> float:
+    """Whole-job audio seconds per second: the audio of every rank over the slowest
+    rank's time for the same steps."""
+    return world * n_items * item_s * steps / (ms / 1e3)
+
+
+def checkpoint(rank: int, world: int, directory: str | None = None, cfg: dict | None = None) -> str:
+    """The random-init checkpoint (seed 0).  Rank 0 writes it once, file by file with
+    the weights last, so a directory holding model.safetensors is complete; the other
+    ranks wait at a barrier until it is there."""
+    import synth
+
+    d = directory or os.path.join(tempfile.gettempdir(), "n3d_bench_ckpt_seed0")
+    if rank == 0 and not os.path.exists(os.path.join(d, "model.safetensors")):
+        tmp = d + f".tmp{os.getpid()}"
+        synth.write_checkpoint(tmp, seed=0, **({"cfg": cfg} if cfg is not None else {}))
+        os.makedirs(d, exist_ok=True)
+        for name in ("config.json", "processor_config.json", "model.safetensors"):
+            os.replace(os.path.join(tmp, name), os.path.join(d, name))
+        os.rmdir(tmp)
+    barrier(world)
     return d
 
 
@@ -244,7 +291,7 @@ def main():
         import synth
 
         mode, item_s, n_items = "ultra_low_latency", args.session_seconds, args.clips or 32
-        items = [synth.config3_session(rank * n_items + i, item_s) for i in range(n_items)]
+        items = [synth.config3_session(i, item_s) for i in item_seeds("c3", rank, n_items)]
         metric = "ultra_low_latency streaming RTFx (audio-s/wall-s); p50/p99 chunk-step latency"
         desc = (f"C3 ultra_low_latency: {n_items} concurrent {item_s:.0f} s sessions per GPU (seeds 100+), "
                 "3 scored encoder frames per step, random-init weights (seed 0)")
@@ -261,26 +308,11 @@ def main():
     def step():
         model.run_batch_device(mode, d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
 
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        import torch.distributed as dist
-
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     # ---- device-resident timed region: two CUDA events per chunk-loop step only
     for _ in range(args.warmup):
         step()
     model.step_timing_enable(True)
-    barrier()
+    barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -289,8 +321,8 @@ def main():
             step()
         e1.record(stream)
         torch.cuda.synchronize()
-    barrier()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
     step_ms = np.array(model.step_times())
     model.step_timing_enable(False)
     # ---- the same K steps again with CUDA events around every launch: per-kernel
@@ -301,14 +333,13 @@ def main():
     torch.cuda.synchronize()
     prof = model.profile_read()
     model.profile_enable(False)
-    audio_s = world * n_items * item_s * args.steps
-    value = audio_s / (ms / 1e3)
+    value = job_rate(world, n_items, item_s, args.steps, ms)
 
     # ---- end-to-end through the public C-ABI batch call, pinned host buffers
     pinned = [torch.from_numpy(c).pin_memory() for c in items]
     host = [t.numpy() for t in pinned]
     model.run_batch(host, mode)  # warm the host path
-    barrier()
+    barrier(world)
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
@@ -316,8 +347,8 @@ def main():
         outs = model.run_batch(host, mode)
     f1.record(stream)
     torch.cuda.synchronize()
-    barrier()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1))
+    barrier(world)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
     assert all(o.num_frames == f for o, f in zip(outs, frames))
     h2d = sum(lens) * 4
     d2h = sum(frames) * 8 * 4
@@ -339,12 +370,13 @@ def main():
         # live serving through the session API: 240 ms of audio per session per call
         # (= one ultra_low_latency chunk step); the first 3 calls are warm-up
         push = 3 * 8 * 160
-        barrier()
+        barrier(world)
         lat, wall = live_sessions(model, items, mode, push)
         steady = lat[3:-1] if lat.size > 5 else lat
         live = {"push_samples": push, "calls": int(lat.size),
                 "p50_ms": float(np.percentile(steady, 50)), "p99_ms": float(np.percentile(steady, 99)),
-                "max_ms": float(steady.max()), "rtfx": world * n_items * item_s / max_over_ranks(wall),
+                "max_ms": float(steady.max()),
+                "rtfx": job_rate(world, n_items, item_s, 1, max_over_ranks(wall, world) * 1e3),
                 "what": f"host wall time of one n3d_sessions_push call handing 240 ms of new audio to each of "
                         f"{n_items} sessions (H2D, log-mel, embedder, one chunk step, D2H of the new rows)"}
 
@@ -362,7 +394,7 @@ def main():
             "config": {"workload": desc, "seconds_per_item": item_s, "items_per_step_per_gpu": n_items,
                        "mode": mode, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},
-            "e2e": {"value": world * n_items * item_s * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+            "e2e": {"value": job_rate(world, n_items, item_s, args.steps, e2e_ms), "unit": UNIT,
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
             "chunk_step_latency_ms": {
                 "p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
