@@ -180,7 +180,8 @@ n3d_status n3d_extract_speaker_dict(const float *logits, size_t num_frames, size
                                     const uint8_t *mask, float threshold, n3d_segment **out, size_t *count);
 void n3d_segments_free(n3d_segment *segments);
 
-/* activity_stats (src/segments.rs:113-141): returns the speech percentage. */
+/* activity_stats (src/segments.rs:113-141): returns the speech percentage and, when
+ * per_speaker is not NULL, each speaker's active-frame count (num_speakers entries). */
 float n3d_activity_stats(const float *logits, size_t num_frames, size_t num_speakers, const uint8_t *mask,
                          float threshold, size_t *per_speaker);
 
@@ -188,6 +189,9 @@ float n3d_activity_stats(const float *logits, size_t num_frames, size_t num_spea
 float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate);
 
 /* -------------------------------------------------- single kernels (device) */
+/* n3d_linear, n3d_layer_norm and n3d_attention run on a stream of the library's own
+ * per device and return after it has finished; concurrent calls on one device take
+ * turns. */
 
 /* tensor::linear (src/tensor.rs:22-57) on device buffers: d_y[rows, out] =
  * d_x[rows, cols] * d_w[out, cols]^T + d_bias (nullable).  cols % 32 == 0.

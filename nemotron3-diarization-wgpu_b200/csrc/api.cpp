@@ -109,14 +109,17 @@ float round2(float v) {
     return (float)(r / 100.0);
 }
 
-// Per-device scratch for the single-kernel entry points.
+// Per-device stream and error word of the single-kernel entry points.  A call holds
+// `call` from its first launch to its last check, so calls on one device from several
+// threads take turns instead of mixing their launches and error reports.
 struct KernelCtx {
+    std::mutex call;
     cudaStream_t stream = nullptr;
     int* err = nullptr;
 };
 KernelCtx& kctx(int device) {
     static std::mutex mu;
-    static std::vector<KernelCtx> ctxs(64);
+    static KernelCtx ctxs[64];
     std::lock_guard<std::mutex> lock(mu);
     if (device < 0 || device >= 64) throw n3d::Error(N3D_ERR_NO_DEVICE, "bad device index");
     KernelCtx& k = ctxs[device];
@@ -294,6 +297,7 @@ n3d_status n3d_batch_out_frames(const n3d_model* model, n3d_mode mode, const siz
                                 size_t* frames_out) {
     return guarded([&] {
         arg_check(model && (n_clips == 0 || (lens && frames_out)), "n3d_batch_out_frames: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_batch_out_frames: bad mode");
         for (size_t i = 0; i < n_clips; i++) {
             n3d::ClipPlan p = mode == N3D_MODE_OFFLINE ? n3d::plan_offline(model->m->cfg(), (long long)lens[i])
                                                        : n3d::plan_streaming(model->m->cfg(), (long long)lens[i], (int)mode);
@@ -307,6 +311,7 @@ n3d_status n3d_run_batch_device(n3d_model* model, n3d_mode mode, const float* d_
     return guarded([&] {
         arg_check(model && (n_clips == 0 || (d_audio && offsets && lens && d_logits && out_offsets)),
                   "n3d_run_batch_device: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_run_batch_device: bad mode");
         std::vector<long long> off(offsets, offsets + n_clips), l(lens, lens + n_clips),
             oo(out_offsets, out_offsets + n_clips);
         model->m->run_batch((int)mode, {}, d_audio, off, l, nullptr, d_logits, &oo, nullptr);
@@ -386,14 +391,15 @@ void n3d_segments_free(n3d_segment* segments) { std::free(segments); }
 float n3d_activity_stats(const float* logits, size_t num_frames, size_t ns, const uint8_t* mask, float threshold,
                          size_t* per_speaker) {
     size_t any = 0, total = 0;
-    for (size_t s = 0; s < ns; s++) per_speaker[s] = 0;
+    if (per_speaker)
+        for (size_t s = 0; s < ns; s++) per_speaker[s] = 0;
     for (size_t t = 0; t < num_frames; t++) {
         if (mask && !mask[t]) continue;
         total++;
         bool hot = false;
         for (size_t s = 0; s < ns; s++)
             if (sigmoidf(logits[t * ns + s]) > threshold) {
-                per_speaker[s]++;
+                if (per_speaker) per_speaker[s]++;
                 hot = true;
             }
         any += hot;
@@ -446,6 +452,7 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
         arg_check(cols % 32 == 0 && cols > 0, "n3d_linear: cols must be a positive multiple of 32");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
         DevScratch sc;
         const n3d::Split3Out x{sc.get(rows * cols), sc.get(rows * cols / 2), sc.get(rows * cols / 2)};
         const n3d::Split3Out w{sc.get(out * cols), sc.get(out * cols / 2), sc.get(out * cols / 2)};
@@ -476,6 +483,7 @@ n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols
         arg_check(d_x && d_w && d_b && d_y, "n3d_layer_norm: null argument");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
         n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, n3d::Split3Out{d_y, nullptr, nullptr});
         kcheck(k);
     });
@@ -488,6 +496,7 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
         arg_check(head_dim == 64 || head_dim == 128, "n3d_attention: head_dim must be 64 or 128");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
         DevScratch sc;
         float* qkv = sc.get(seq * 3 * heads * head_dim);
         float *cs = nullptr, *sn = nullptr;

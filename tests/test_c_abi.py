@@ -74,3 +74,15 @@ def test_activity_stats_matches_oracle():
     logits = (rng.standard_normal(800) * 0.01).astype(np.float32)
     assert n3d.activity_stats(logits, 100, 8) == oracle.activity_stats(logits, 100, 8)
     assert n3d.frame_duration(160, 16000) == np.float32(0.01)
+
+
+def test_activity_stats_counts_are_optional():
+    rng = np.random.default_rng(6)
+    logits = rng.standard_normal(800).astype(np.float32)
+    lg = logits.ctypes.data_as(C.POINTER(C.c_float))
+    counts = (C.c_size_t * 8)()
+    with_counts = n3d.lib().n3d_activity_stats(lg, 100, 8, None, 0.5, counts)
+    without = n3d.lib().n3d_activity_stats(lg, 100, 8, None, 0.5, None)
+    assert with_counts == without > 0
+    sig = 1.0 / (1.0 + np.exp(-logits.reshape(100, 8).astype(np.float64)))
+    assert list(counts) == list((sig > 0.5).sum(axis=0))

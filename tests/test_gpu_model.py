@@ -131,6 +131,21 @@ def test_streaming_too_short_is_unsupported_audio(tiny_gpu_model):
     assert e.value.kind == "UnsupportedAudio"
 
 
+def test_bad_mode_is_rejected_before_any_device_work(tiny_gpu_model):
+    import ctypes as C
+
+    import n3d
+
+    lens = (C.c_size_t * 1)(16000)
+    offs = (C.c_size_t * 1)(0)
+    frames = (C.c_size_t * 1)()
+    st = n3d.lib().n3d_batch_out_frames(tiny_gpu_model._h, 7, lens, 1, frames)
+    assert n3d.STATUS[st] == "InvalidArgument" and b"bad mode" in n3d.lib().n3d_last_error()
+    # the pointers are never touched: the mode is checked first
+    st = n3d.lib().n3d_run_batch_device(tiny_gpu_model._h, -1, C.c_void_p(256), offs, lens, 1, C.c_void_p(256), offs)
+    assert n3d.STATUS[st] == "InvalidArgument" and b"bad mode" in n3d.lib().n3d_last_error()
+
+
 def test_batch_equals_single_runs(tiny_gpu_model, tiny_oracle):
     clips = [synth.clip(20 + i, d, 3) for i, d in enumerate([4.0, 7.5, 2.2, 7.5])]
     batch = tiny_gpu_model.run_batch(clips, "offline")
