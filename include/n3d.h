@@ -188,6 +188,68 @@ float n3d_activity_stats(const float *logits, size_t num_frames, size_t num_spea
 /* frame_duration (src/segments.rs:36-38). */
 float n3d_frame_duration(size_t hop_length, uint32_t sampling_rate);
 
+/* ------------------------------------------------------- chunk schedule (host) */
+/* These need no GPU: they read the checkpoint's two JSON files and do the integer
+ * chunk arithmetic the runs above follow. */
+
+typedef struct n3d_config n3d_config;
+
+/* load_configs (src/config.rs:221-225): config.json and processor_config.json of a
+ * checkpoint directory.  Free with n3d_config_free. */
+n3d_status n3d_config_load(const char *dir, n3d_config **out);
+void n3d_config_free(n3d_config *cfg);
+
+/* ModeParams (src/config.rs:127-147) as ModeParams::resolve / Model::params build it
+ * (src/config.rs:152-195, src/model.rs:219-221).  Offline has zero chunk geometry and
+ * the latency of the offline window. */
+typedef struct n3d_mode_params {
+    size_t hop_length;
+    size_t n_fft;
+    size_t subsampling;
+    size_t mel_frames_per_chunk;
+    size_t mel_frames_per_step;
+    size_t lookahead_encoder_frames;
+    size_t first_chunk_samples;
+    size_t samples_per_chunk;
+    size_t latency_ms;
+} n3d_mode_params;
+n3d_status n3d_mode_params_resolve(const n3d_config *cfg, n3d_mode mode, n3d_mode_params *out);
+
+/* One chunk of Model::streaming_chunks (src/model.rs:343-365) without its mel
+ * features: samples [start, start + len), centred or not, the mel frames log_mel
+ * keeps (Chunk::num_mel_frames) and the look-ahead in encoder frames. */
+typedef struct n3d_chunk {
+    size_t start;
+    size_t len;
+    int centered;
+    size_t num_mel_frames;
+    size_t lookahead;
+} n3d_chunk;
+/* Writes min(count, cap) chunks; *count is the full number (call with cap 0 to size
+ * the array).  Streaming modes only. */
+n3d_status n3d_streaming_chunks(const n3d_config *cfg, size_t n_samples, n3d_mode mode, n3d_chunk *out,
+                                size_t cap, size_t *count);
+
+/* One chunk-loop step, the counts of ChunkTrace (src/model.rs:57-75): frames carried
+ * in from the cache and FIFO, the window the tower sees, the frames the mask lets
+ * through, the frames scored, and the cache and FIFO after the step's update. */
+typedef struct n3d_step_plan {
+    size_t cached_frames;
+    size_t window_frames;
+    size_t valid_frames;
+    size_t scored_frames;
+    size_t cache_frames;
+    size_t fifo_frames;
+    int cache_compressed;
+} n3d_step_plan;
+/* The steps a run of n_samples in `mode` takes (run_offline_capturing / run_streaming
+ * with chunk_loop, src/model.rs:242-336, 478-538).  Writes min(count, cap) steps and
+ * sets *count; `totals` (nullable) receives the RunOutput fields the run will return,
+ * with logits NULL.  Streaming audio too short for the look-ahead fails with
+ * N3D_ERR_UNSUPPORTED_AUDIO, as the runs do. */
+n3d_status n3d_schedule(const n3d_config *cfg, n3d_mode mode, size_t n_samples, n3d_step_plan *steps,
+                        size_t cap, size_t *count, n3d_run_output *totals);
+
 /* -------------------------------------------------- single kernels (device) */
 /* n3d_linear, n3d_layer_norm and n3d_attention run on a stream of the library's own
  * per device and return after it has finished; concurrent calls on one device take

@@ -24,6 +24,10 @@ struct n3d_session {
     n3d::Session* s;
 };
 
+struct n3d_config {
+    n3d::Config c;
+};
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -443,6 +447,88 @@ size_t n3d_step_times(const n3d_model* model, double* ms, size_t cap) {
     const std::vector<float>& t = model->m->step_times();
     for (size_t i = 0; i < t.size() && i < cap; i++) ms[i] = t[i];
     return t.size();
+}
+
+n3d_status n3d_config_load(const char* dir, n3d_config** out) {
+    return guarded([&] {
+        arg_check(dir && out, "n3d_config_load: null argument");
+        *out = nullptr;
+        auto h = std::make_unique<n3d_config>();
+        h->c = n3d::load_config(dir);
+        *out = h.release();
+    });
+}
+
+void n3d_config_free(n3d_config* cfg) { delete cfg; }
+
+n3d_status n3d_mode_params_resolve(const n3d_config* cfg, n3d_mode mode, n3d_mode_params* out) {
+    return guarded([&] {
+        arg_check(cfg && out, "n3d_mode_params_resolve: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_mode_params_resolve: bad mode");
+        const n3d::Config& c = cfg->c;
+        n3d_mode_params p{};
+        p.hop_length = (size_t)c.hop;
+        p.n_fft = (size_t)c.n_fft;
+        p.subsampling = (size_t)c.proc_sub;
+        if (mode == N3D_MODE_OFFLINE) {
+            p.latency_ms = (size_t)(c.chunk_length + c.chunk_rc) * 80;
+        } else {
+            const size_t cl = (size_t)c.modes[mode][0], rc = (size_t)c.modes[mode][1];
+            p.mel_frames_per_chunk = (cl + rc) * p.subsampling;
+            p.mel_frames_per_step = cl * p.subsampling;
+            p.lookahead_encoder_frames = rc;
+            p.first_chunk_samples = (p.mel_frames_per_chunk - 1) * p.hop_length + (size_t)c.win / 2;
+            p.samples_per_chunk = p.mel_frames_per_chunk * p.hop_length + (size_t)c.win;
+            p.latency_ms = (cl + rc) * 80;
+        }
+        *out = p;
+    });
+}
+
+n3d_status n3d_streaming_chunks(const n3d_config* cfg, size_t n_samples, n3d_mode mode, n3d_chunk* out, size_t cap,
+                                size_t* count) {
+    return guarded([&] {
+        arg_check(cfg && count && (out || cap == 0), "n3d_streaming_chunks: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 2, "n3d_streaming_chunks: mode must be a streaming mode");
+        const std::vector<n3d::StreamChunk> ch = n3d::streaming_chunks(cfg->c, (long long)n_samples, (int)mode);
+        for (size_t i = 0; i < ch.size() && i < cap; i++)
+            out[i] = n3d_chunk{(size_t)ch[i].start, (size_t)ch[i].len, ch[i].centered, (size_t)ch[i].mel_frames,
+                               (size_t)ch[i].lookahead};
+        *count = ch.size();
+    });
+}
+
+n3d_status n3d_schedule(const n3d_config* cfg, n3d_mode mode, size_t n_samples, n3d_step_plan* steps, size_t cap,
+                        size_t* count, n3d_run_output* totals) {
+    return guarded([&] {
+        arg_check(cfg && count && (steps || cap == 0), "n3d_schedule: null argument");
+        arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_schedule: bad mode");
+        const n3d::ClipPlan p = mode == N3D_MODE_OFFLINE ? n3d::plan_offline(cfg->c, (long long)n_samples)
+                                                         : n3d::plan_streaming(cfg->c, (long long)n_samples, (int)mode);
+        const size_t n = p.steps.size();
+        for (size_t i = 0; i < n && i < cap; i++) {
+            const n3d::StepPlan& sp = p.steps[i];
+            // the cache after step i is what step i + 1 starts from
+            const bool last = i + 1 == n;
+            steps[i] = n3d_step_plan{(size_t)(sp.ncache + sp.nfifo),
+                                     (size_t)sp.S,
+                                     (size_t)sp.valid,
+                                     (size_t)sp.nchunk,
+                                     (size_t)(last ? p.cache_frames : p.steps[i + 1].ncache),
+                                     (size_t)(last ? p.fifo_frames : p.steps[i + 1].nfifo),
+                                     last ? p.cache_compressed : p.steps[i + 1].was_compressed};
+        }
+        *count = n;
+        if (totals) {
+            *totals = n3d_run_output{};
+            totals->num_frames = (size_t)p.out_rows;
+            totals->num_speakers = (size_t)cfg->c.num_speakers;
+            totals->num_chunks = (size_t)p.num_chunks;
+            totals->cache_compressed = p.cache_compressed;
+            totals->cache_frames = (size_t)p.cache_frames;
+            totals->fifo_frames = (size_t)p.fifo_frames;
+        }
+    });
 }
 
 n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,

@@ -315,45 +315,49 @@ ClipPlan plan_offline(const Config& c, long long n) {
     return p;
 }
 
-// Model::streaming_chunks + run_streaming + chunk_loop's Streaming arm
-// (src/model.rs:313-365, 504-510; geometry from ModeParams::resolve, src/config.rs:152-202).
-ClipPlan plan_streaming(const Config& c, long long n, int mode) {
+// Model::streaming_chunks (src/model.rs:343-365), geometry from ModeParams::resolve
+// (src/config.rs:152-202): the first chunk centred, later full chunks uncentred one
+// step of mel frames apart, and what is left as a final centred chunk.
+std::vector<StreamChunk> streaming_chunks(const Config& c, long long n, int mode) {
     if (mode < 0 || mode > 2) throw Error(kStatusArg, "streaming mode must be low, very low or ultra low latency");
     const int cl = c.modes[mode][0], rc = c.modes[mode][1];
     const long long mel_chunk = (long long)(cl + rc) * c.sub, mel_step = (long long)cl * c.sub;
     const long long first = (mel_chunk - 1) * c.hop + c.win / 2;
     const long long per_chunk = mel_chunk * c.hop + c.win;
-    ClipPlan p;
-    struct Ch {
-        long long off, len;
-        int centered, la;
-    };
-    std::vector<Ch> chunks;
-    chunks.push_back({0, std::min(first, n), 1, rc});
+    std::vector<StreamChunk> chunks;
+    const long long f0 = std::min(first, n);
+    chunks.push_back({0, f0, frame_count(c, f0, true), 1, rc});
     long long mel_idx = mel_step;
     long long start = mel_idx * c.hop - c.n_fft / 2;
     while (start + per_chunk <= n) {
-        chunks.push_back({start, per_chunk, 0, rc});
+        chunks.push_back({start, per_chunk, frame_count(c, per_chunk, false), 0, rc});
         mel_idx += mel_step;
         start = mel_idx * c.hop - c.n_fft / 2;
     }
     const long long ls = std::min(start, n);
-    chunks.push_back({ls, n - ls, 1, 0});
+    chunks.push_back({ls, n - ls, frame_count(c, n - ls, true), 1, 0});
+    return chunks;
+}
 
+// run_streaming + chunk_loop's Streaming arm (src/model.rs:313-336, 504-510).
+ClipPlan plan_streaming(const Config& c, long long n, int mode) {
+    const std::vector<StreamChunk> chunks = streaming_chunks(c, n, mode);
+    ClipPlan p;
     CacheSim cs{c.s_fifo, c.s_period, c.cache_len};
     for (size_t i = 0; i < chunks.size(); i++) {
-        const Ch& ch = chunks[i];
-        const long long nm = frame_count(c, ch.len, ch.centered != 0);
+        const StreamChunk& ch = chunks[i];
+        const long long nm = ch.mel_frames;
         const long long groups = ceil_div(nm, c.sub);
-        if (groups < ch.la)
+        if (groups < ch.lookahead)
             throw Error(kStatusAudio, "unsupported audio: a streaming chunk holds " + std::to_string(groups) +
-                                          " encoder frames, fewer than the look-ahead of " + std::to_string(ch.la));
-        p.segs.push_back(MelSeg{ch.off, ch.len, ch.centered, (int)nm, (int)groups, 0});
+                                          " encoder frames, fewer than the look-ahead of " +
+                                          std::to_string(ch.lookahead));
+        p.segs.push_back(MelSeg{ch.start, ch.len, ch.centered, (int)nm, (int)groups, 0});
         StepPlan sp{};
         sp.seg = (int)i;
         sp.group_lo = 0;
         sp.n_new = (int)groups;
-        sp.nchunk = (int)(groups - ch.la);
+        sp.nchunk = (int)(groups - ch.lookahead);
         const int prefix = cs.ncache + cs.nfifo;
         sp.S = prefix + sp.n_new;
         sp.valid = sp.S;

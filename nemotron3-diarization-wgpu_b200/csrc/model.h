@@ -102,6 +102,15 @@ struct ClipPlan {
 ClipPlan plan_offline(const Config& c, long long n);
 ClipPlan plan_streaming(const Config& c, long long n, int mode);
 
+// One chunk of Model::streaming_chunks (src/model.rs:343-365): samples [start,
+// start + len) of the recording, centred or not, the mel frames its log_mel keeps, and
+// the encoder frames held back as look-ahead.
+struct StreamChunk {
+    long long start, len, mel_frames;
+    int centered, lookahead;
+};
+std::vector<StreamChunk> streaming_chunks(const Config& c, long long n, int mode);
+
 // ----------------------------------------------------------------- sessions
 
 class Model;

@@ -54,6 +54,21 @@ class _Segment(C.Structure):
     _fields_ = [("start", C.c_float), ("end", C.c_float), ("speaker", _sz)]
 
 
+class _ModeParams(C.Structure):
+    _fields_ = [(n, _sz) for n in ("hop_length", "n_fft", "subsampling", "mel_frames_per_chunk",
+                                   "mel_frames_per_step", "lookahead_encoder_frames", "first_chunk_samples",
+                                   "samples_per_chunk", "latency_ms")]
+
+
+class _Chunk(C.Structure):
+    _fields_ = [("start", _sz), ("len", _sz), ("centered", C.c_int), ("num_mel_frames", _sz), ("lookahead", _sz)]
+
+
+class _StepPlan(C.Structure):
+    _fields_ = [("cached_frames", _sz), ("window_frames", _sz), ("valid_frames", _sz), ("scored_frames", _sz),
+                ("cache_frames", _sz), ("fifo_frames", _sz), ("cache_compressed", C.c_int)]
+
+
 class _KernelStats(C.Structure):
     _fields_ = [("name", C.c_char_p), ("launches", _sz), ("ms", C.c_double), ("flops", C.c_double),
                 ("bytes", C.c_double)]
@@ -130,6 +145,12 @@ def lib() -> C.CDLL:
         "n3d_segments_free": ([C.POINTER(_Segment)], None),
         "n3d_activity_stats": ([fpp, _sz, _sz, vp, C.c_float, C.POINTER(_sz)], C.c_float),
         "n3d_frame_duration": ([_sz, C.c_uint32], C.c_float),
+        "n3d_config_load": ([C.c_char_p, C.POINTER(vp)], C.c_int),
+        "n3d_config_free": ([vp], None),
+        "n3d_mode_params_resolve": ([vp, C.c_int, C.POINTER(_ModeParams)], C.c_int),
+        "n3d_streaming_chunks": ([vp, _sz, C.c_int, C.POINTER(_Chunk), _sz, C.POINTER(_sz)], C.c_int),
+        "n3d_schedule": ([vp, C.c_int, _sz, C.POINTER(_StepPlan), _sz, C.POINTER(_sz), C.POINTER(_RunOutput)],
+                         C.c_int),
         "n3d_linear": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp], C.c_int),
         "n3d_linear_noalloc": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp, vp], C.c_int),
         "n3d_layer_norm": ([C.c_int, vp, _sz, _sz, vp, vp, vp], C.c_int),
@@ -180,6 +201,65 @@ def _collect(o: _RunOutput) -> RunOutput:
         lib().n3d_run_output_free(C.byref(o))
     return RunOutput(logits.reshape(o.num_frames, o.num_speakers), int(o.num_frames), int(o.num_chunks),
                      bool(o.cache_compressed), int(o.cache_frames), int(o.fifo_frames))
+
+
+def _struct_dict(st) -> dict:
+    return {name: getattr(st, name) for name, _ in st._fields_}
+
+
+class Config:
+    """config.json + processor_config.json of a checkpoint (load_configs,
+    src/config.rs:221-225) and the chunk arithmetic the runs follow.  Host only: no
+    GPU is needed."""
+
+    def __init__(self, handle: int):
+        self._h = C.c_void_p(handle)
+
+    @classmethod
+    def load(cls, directory: str) -> "Config":
+        h = C.c_void_p()
+        _check(lib().n3d_config_load(directory.encode(), C.byref(h)))
+        return cls(h.value)
+
+    def close(self) -> None:
+        if self._h:
+            lib().n3d_config_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def mode_params(self, mode: str) -> dict:
+        """ModeParams::resolve (src/config.rs:152-195) as a dict of its fields."""
+        p = _ModeParams()
+        _check(lib().n3d_mode_params_resolve(self._h, MODES[mode], C.byref(p)))
+        return _struct_dict(p)
+
+    def streaming_chunks(self, n_samples: int, mode: str) -> list[dict]:
+        """Model::streaming_chunks (src/model.rs:343-365) without the mel features."""
+        n = _sz()
+        _check(lib().n3d_streaming_chunks(self._h, n_samples, MODES[mode], None, 0, C.byref(n)))
+        arr = (_Chunk * max(n.value, 1))()
+        _check(lib().n3d_streaming_chunks(self._h, n_samples, MODES[mode], arr, n.value, C.byref(n)))
+        return [_struct_dict(arr[i]) for i in range(n.value)]
+
+    def schedule(self, n_samples: int, mode: str) -> tuple[list[dict], dict]:
+        """The chunk-loop steps of a run (ChunkTrace counts, src/model.rs:57-75) and the
+        RunOutput counts it will return (without logits)."""
+        n = _sz()
+        tot = _RunOutput()
+        _check(lib().n3d_schedule(self._h, MODES[mode], n_samples, None, 0, C.byref(n), C.byref(tot)))
+        arr = (_StepPlan * max(n.value, 1))()
+        _check(lib().n3d_schedule(self._h, MODES[mode], n_samples, arr, n.value, C.byref(n), None))
+        steps = [_struct_dict(arr[i]) for i in range(n.value)]
+        for st in steps:
+            st["cache_compressed"] = bool(st["cache_compressed"])
+        totals = {k: v for k, v in _struct_dict(tot).items() if k != "logits"}
+        totals["cache_compressed"] = bool(totals["cache_compressed"])
+        return steps, totals
 
 
 class Model:
