@@ -95,6 +95,12 @@ n3d_status n3d_model_set_stream(n3d_model *model, void *stream);
 size_t n3d_num_speakers(const n3d_model *model);
 size_t n3d_hidden_size(const n3d_model *model);
 
+/* Model::gpu_describe (src/model.rs:207-209; GpuEngine::describe, src/gpu_engine.rs:534):
+ * the device the model runs on and this library's build, e.g. "NVIDIA B200 (device 0,
+ * sm_100, 148 SMs, 179 GiB) | n3d-b200 ...".  The string belongs to the model and stays
+ * valid until the next call on it or n3d_model_free; NULL for a NULL model. */
+const char *n3d_model_describe(n3d_model *model);
+
 /* Model::run_offline (src/model.rs:232-234). */
 n3d_status n3d_run_offline(n3d_model *model, const float *samples, size_t n, n3d_run_output *out);
 

@@ -17,6 +17,7 @@
 
 struct n3d_model {
     std::unique_ptr<n3d::Model> m;
+    std::string describe;  // n3d_model_describe's last answer
 };
 
 struct n3d_session {
@@ -191,6 +192,23 @@ n3d_status n3d_model_set_stream(n3d_model* model, void* stream) {
 
 size_t n3d_num_speakers(const n3d_model* model) { return model ? (size_t)model->m->cfg().num_speakers : 0; }
 size_t n3d_hidden_size(const n3d_model* model) { return model ? (size_t)model->m->cfg().hidden : 0; }
+
+const char* n3d_model_describe(n3d_model* model) {
+    if (!model) return nullptr;
+    const int dev = model->m->device();
+    cudaDeviceProp prop{};
+    std::string d;
+    if (cudaGetDeviceProperties(&prop, dev) == cudaSuccess) {
+        d = std::string(prop.name) + " (device " + std::to_string(dev) + ", sm_" + std::to_string(prop.major) +
+            std::to_string(prop.minor) + ", " + std::to_string(prop.multiProcessorCount) + " SMs, " +
+            std::to_string(prop.totalGlobalMem >> 30) + " GiB)";
+    } else {
+        cudaGetLastError();  // the failed query's error is not sticky: clear it for later calls
+        d = "CUDA device " + std::to_string(dev);
+    }
+    model->describe = d + " | " + n3d_version();
+    return model->describe.c_str();
+}
 
 static n3d_status run_one(n3d_model* model, const float* samples, size_t n, int mode, n3d_run_output* out) {
     return guarded([&] {

@@ -122,6 +122,7 @@ def lib() -> C.CDLL:
         "n3d_model_set_stream": ([vp, vp], C.c_int),
         "n3d_num_speakers": ([vp], _sz),
         "n3d_hidden_size": ([vp], _sz),
+        "n3d_model_describe": ([vp], C.c_char_p),
         "n3d_run_offline": ([vp, fpp, _sz, C.POINTER(_RunOutput)], C.c_int),
         "n3d_run_streaming": ([vp, fpp, _sz, C.c_int, C.POINTER(_RunOutput)], C.c_int),
         "n3d_run_output_free": ([C.POINTER(_RunOutput)], None),
@@ -300,6 +301,10 @@ class Model:
     @property
     def hidden_size(self) -> int:
         return lib().n3d_hidden_size(self._h)
+
+    def describe(self) -> str:
+        """Model::gpu_describe (src/model.rs:207-209): the device and this build."""
+        return lib().n3d_model_describe(self._h).decode()
 
     def run_offline(self, samples) -> RunOutput:
         s = _f32(samples)

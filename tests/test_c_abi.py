@@ -86,3 +86,7 @@ def test_activity_stats_counts_are_optional():
     assert with_counts == without > 0
     sig = 1.0 / (1.0 + np.exp(-logits.reshape(100, 8).astype(np.float64)))
     assert list(counts) == list((sig > 0.5).sum(axis=0))
+
+
+def test_describe_of_no_model_is_null():
+    assert n3d.lib().n3d_model_describe(None) is None

@@ -131,6 +131,12 @@ def test_streaming_too_short_is_unsupported_audio(tiny_gpu_model):
     assert e.value.kind == "UnsupportedAudio"
 
 
+def test_describe_names_the_device_and_build(tiny_gpu_model):
+    d = tiny_gpu_model.describe()
+    assert "sm_100" in d and "148 SMs" in d and "n3d-b200" in d, d
+    assert tiny_gpu_model.describe() == d  # the same answer on a second call
+
+
 def test_bad_mode_is_rejected_before_any_device_work(tiny_gpu_model):
     import ctypes as C
 
