@@ -90,3 +90,37 @@ def test_activity_stats_counts_are_optional():
 
 def test_describe_of_no_model_is_null():
     assert n3d.lib().n3d_model_describe(None) is None
+
+
+def _segment_case(draw):
+    from hypothesis import strategies as st
+
+    T = draw(st.integers(0, 300))
+    ns = draw(st.integers(1, 8))
+    thr = draw(st.sampled_from([0.1, 0.25, 0.5, 0.5000001, 0.9]))
+    edge = float(np.log(thr / (1.0 - thr)))  # the logit whose sigmoid sits on the threshold
+    vals = st.sampled_from([0.0, -0.0, 1e-7, -1e-7, 3.0, -3.0, 40.0, -40.0, edge, np.nextafter(edge, 9.0),
+                            np.nextafter(edge, -9.0)]) | st.floats(-8, 8, width=32)
+    logits = np.array(draw(st.lists(vals, min_size=T * ns, max_size=T * ns)), np.float32)
+    mask = draw(st.none() | st.lists(st.booleans(), min_size=T, max_size=T))
+    mask = None if mask is None else np.array(mask, np.uint8)
+    dur = draw(st.sampled_from([0.01, 0.08, 0.02, 0.0133]))
+    return logits, T, ns, dur, mask, thr
+
+
+def test_segments_and_activity_match_the_oracle_on_random_cases():
+    """extract_speaker_dict and activity_stats (src/segments.rs:70-141) on drawn logits,
+    masks, thresholds and frame durations: the C ABI equals the oracle exactly."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=150, deadline=None, derandomize=True, database=None)
+    @given(st.data())
+    def check(data):
+        logits, T, ns, dur, mask, thr = _segment_case(data.draw)
+        got = n3d.extract_speaker_dict(logits, T, ns, dur, mask, thr)
+        want = oracle.extract_speaker_dict(logits, T, ns, dur, mask, thr)
+        assert [(s.start, s.end, s.speaker) for s in got] == [(np.float32(a), np.float32(b), s) for a, b, s in want]
+        assert n3d.activity_stats(logits, T, ns, mask, thr) == oracle.activity_stats(logits, T, ns, mask, thr)
+
+    check()
