@@ -398,11 +398,10 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
     if (seqs <= 0 || S <= 0) return;
     if ((seqs > 1 && S % 8) || op.vt_ld % 8)
         throw Error(9, "attention: the sequence stride and the V^T row stride must be multiples of 8");
-    static bool attr = false;
-    if (!attr) {
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [] {
         N3D_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        attr = true;
-    }
+    });
     const long long W = (long long)heads * HD, rows = (long long)seqs * S;
     AttnMaps m;
     m.qh = make_bf16_map(op.q_hi, op.rows_cap, W, W, 64, QT, true);

@@ -328,10 +328,16 @@ void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const f
     int P = 1;
     while (P < c.ns * (stride + c.n_sil)) P <<= 1;
     const size_t smem = cache_update_smem(stride, c.ns, P);
-    static size_t attr = 0;
-    if (smem > attr) {
-        N3D_CUDA(cudaFuncSetAttribute(cache_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr = smem;
+    {
+        // the limit set so far on each device; raised when a longer window needs more
+        static size_t attr[kMaxDevices];
+        static std::mutex mu;
+        const int dev = current_device();
+        std::lock_guard<std::mutex> lock(mu);
+        if (smem > attr[dev]) {
+            N3D_CUDA(cudaFuncSetAttribute(cache_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            attr[dev] = smem;
+        }
     }
     CacheParams cp{c.hidden, c.ns, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
                    c.latest_boost};

@@ -800,11 +800,12 @@ Maps6 operand_maps(const SplitOperand& A, const SplitOperand& B, int ra, int rb,
 }
 
 int sm_count() {
-    static int n = 0;
+    static std::atomic<int> count[kMaxDevices];  // per device, 0 until queried
+    const int dev = current_device();
+    int n = count[dev].load(std::memory_order_relaxed);
     if (!n) {
-        int dev = 0;
-        N3D_CUDA(cudaGetDevice(&dev));
         N3D_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        count[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }
@@ -813,11 +814,10 @@ template <int BN>
 void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err,
                 int ksplit = 1, int Mp = 0) {
     using Cfg = GemmCfg<BN>;
-    static bool attr = false;
-    if (!attr) {
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [] {
         N3D_CUDA(cudaFuncSetAttribute(gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-        attr = true;
-    }
+    });
     const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * ksplit;
     const int grid = tiles < sm_count() ? tiles : sm_count();
     launch_pdl(gemm_kernel<BN>, dim3(grid), dim3(192), Cfg::SMEM, s, maps, M, N, K, kb_per_tap, epi, err, ksplit,
@@ -828,7 +828,9 @@ template <int BN>
 void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
                  const Epi& epi, int* err) {
     using Cfg = PairCfg<BN>;
-    static int max_clusters = 0;
+    static std::atomic<int> clusters_per_device[kMaxDevices];  // 0 until measured on that device
+    const int dev = current_device();
+    int max_clusters = clusters_per_device[dev].load(std::memory_order_acquire);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -848,6 +850,7 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         cfg.gridDim = dim3(2 * (sm_count() / 2));
         N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN>, &cfg));
         if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
+        clusters_per_device[dev].store(max_clusters, std::memory_order_release);
     }
     const Maps6 maps = operand_maps(A, B, BM, BN / 2, true);
     const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);

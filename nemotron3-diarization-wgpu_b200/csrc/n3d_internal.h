@@ -4,8 +4,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -20,6 +22,32 @@ struct Error : std::runtime_error {
 
 void cuda_check(cudaError_t e, const char* what);
 #define N3D_CUDA(x) ::n3d::cuda_check((x), #x)
+
+// Per-device tables below hold this many devices.
+constexpr int kMaxDevices = 64;
+
+// The current CUDA device, checked against kMaxDevices.
+inline int current_device() {
+    int dev = 0;
+    N3D_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) throw Error(12 /*N3D_ERR_NO_DEVICE*/, "CUDA device index beyond 63");
+    return dev;
+}
+
+// Runs `set_up` once on each device for the call site that owns `done`.  A kernel's
+// attributes (its dynamic shared-memory limit, for one) belong to the current device,
+// so a process that drives several GPUs must set them on every one; concurrent first
+// calls wait for each other.
+template <class F>
+void once_per_device(std::atomic<unsigned long long>& done, F&& set_up) {
+    const unsigned long long bit = 1ull << current_device();
+    if (done.load(std::memory_order_acquire) & bit) return;
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.load(std::memory_order_relaxed) & bit) return;
+    set_up();
+    done.fetch_or(bit, std::memory_order_release);
+}
 
 // Launch with programmatic stream serialization: the kernel may become resident and
 // run its set-up while the previous kernel of the stream drains.  Every kernel launched
