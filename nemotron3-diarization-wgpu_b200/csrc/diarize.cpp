@@ -75,6 +75,7 @@ std::vector<float> read_npy(const std::string& path) {
     const std::string b = read_bytes(path);
     if (b.size() < 10 || b.compare(0, 6, "\x93NUMPY") != 0) throw std::runtime_error(path + ": not a .npy file");
     const int major = (uint8_t)b[6];
+    if (major != 1 && b.size() < 12) throw std::runtime_error(path + ": truncated .npy header");
     const size_t hlen = major == 1 ? le16(b, 8) : le32(b, 8), off = major == 1 ? 10 : 12;
     if (off + hlen > b.size()) throw std::runtime_error(path + ": truncated .npy header");
     const std::string hdr = b.substr(off, hlen);
@@ -112,6 +113,7 @@ std::vector<float> read_npy(const std::string& path) {
     }
     if (fortran && shape.size() == 2) {  // to row-major, as the reference's reader
         const size_t rows = shape[0], cols = shape[1];
+        if (rows * cols != out.size()) throw std::runtime_error(path + ": .npy data does not match its shape");
         std::vector<float> t(out.size());
         for (size_t r = 0; r < rows; r++)
             for (size_t c = 0; c < cols; c++) t[r * cols + c] = out[c * rows + r];
@@ -126,21 +128,30 @@ std::vector<float> read_wav(const std::string& path) {
     if (b.size() < 12 || b.compare(0, 4, "RIFF") != 0 || b.compare(8, 4, "WAVE") != 0)
         throw std::runtime_error(path + ": not a RIFF/WAVE file");
     int fmt = 0, ch = 0, bits = 0;
+    bool have_fmt = false, have_data = false;
     size_t data = 0, data_len = 0;
     for (size_t o = 12; o + 8 <= b.size();) {
         const std::string id = b.substr(o, 4);
         const size_t len = le32(b, o + 4);
-        if (id == "fmt " && o + 8 + 16 <= b.size()) {
+        if (id == "fmt ") {
+            if (len < 16 || o + 8 + 16 > b.size()) throw std::runtime_error(path + ": truncated fmt chunk");
             fmt = le16(b, o + 8);
             ch = le16(b, o + 10);
             bits = le16(b, o + 22);
-            if (fmt == 0xFFFE && len >= 40) fmt = le16(b, o + 8 + 24);  // WAVE_FORMAT_EXTENSIBLE sub-format
+            if (fmt == 0xFFFE) {  // WAVE_FORMAT_EXTENSIBLE: the sub-format's first two bytes
+                if (len < 40 || o + 8 + 26 > b.size()) throw std::runtime_error(path + ": truncated fmt chunk");
+                fmt = le16(b, o + 8 + 24);
+            }
+            have_fmt = true;
         } else if (id == "data") {
             data = o + 8;
             data_len = std::min(len, b.size() - data);
+            have_data = true;
         }
         o += 8 + len + (len & 1);
     }
+    if (!have_fmt) throw std::runtime_error(path + ": no fmt chunk");
+    if (!have_data) throw std::runtime_error(path + ": no data chunk");
     if (ch < 1) throw std::runtime_error(path + " has no channels");
     const bool flt = fmt == 3 && bits == 32, pcm16 = fmt == 1 && bits == 16;
     if (!flt && !pcm16) throw std::runtime_error(path + " must be 16-bit PCM or float32");

@@ -49,6 +49,79 @@ def test_unreadable_audio_is_an_error(tmp_path):
     assert r.returncode == 1 and "not a .npy file" in r.stderr
 
 
+def _npy_bytes(descr, shape, payload, fortran=False, major=1):
+    hdr = "{'descr': '%s', 'fortran_order': %s, 'shape': %s, }" % (descr, fortran, shape)
+    pad = (-(len(hdr) + 1 + (10 if major == 1 else 12))) % 64
+    hdr = (hdr + " " * pad + "\n").encode()
+    size = len(hdr).to_bytes(2 if major == 1 else 4, "little")
+    return b"\x93NUMPY" + bytes([major, 0]) + size + hdr + payload
+
+
+def _riff(*chunks, size_fix=0):
+    body = b"WAVE" + b"".join(cid + len(data).to_bytes(4, "little") + data + (b"\0" if len(data) % 2 else b"")
+                             for cid, data in chunks)
+    return b"RIFF" + (len(body) + size_fix).to_bytes(4, "little") + body
+
+
+def _fmt(tag, ch, bits, extensible_tag=None):
+    rate, align = 16000, ch * bits // 8
+    f = tag.to_bytes(2, "little") + ch.to_bytes(2, "little") + rate.to_bytes(4, "little") + \
+        (rate * align).to_bytes(4, "little") + align.to_bytes(2, "little") + bits.to_bytes(2, "little")
+    if extensible_tag is not None:
+        f += (22).to_bytes(2, "little") + bits.to_bytes(2, "little") + (0).to_bytes(4, "little") + \
+             extensible_tag.to_bytes(2, "little") + bytes(14)
+    return f
+
+
+MALFORMED = {
+    "short.npy": (b"\x93NUMPY\x02\x00\x10\x00", "truncated .npy header"),
+    "header.npy": (b"\x93NUMPY\x01\x00\xff\x00{'descr'", "truncated .npy header"),
+    "dtype.npy": (_npy_bytes("<f8", "(4,)", bytes(32)), "expected <f4 or <i8, got <f8"),
+    "fortran.npy": (_npy_bytes("<f4", "(3, 5)", bytes(4 * 14), fortran=True), "does not match its shape"),
+    "riff.wav": (b"RIFX\0\0\0\0WAVE", "not a RIFF/WAVE file"),
+    "nofmt.wav": (_riff((b"data", bytes(8))), "no fmt chunk"),
+    "nodata.wav": (_riff((b"fmt ", _fmt(1, 1, 16))), "no data chunk"),
+    "shortfmt.wav": (_riff((b"fmt ", _fmt(1, 1, 16)[:12]), (b"data", bytes(8))), "truncated fmt chunk"),
+    "shortext.wav": (_riff((b"fmt ", _fmt(0xFFFE, 1, 32)[:16] + (22).to_bytes(2, "little"))), "truncated fmt chunk"),
+    "cutext.wav": (b"RIFF\0\0\0\0WAVEfmt \x28\0\0\0" + _fmt(0xFFFE, 1, 32)[:16], "truncated fmt chunk"),
+    "bits24.wav": (_riff((b"fmt ", _fmt(1, 1, 24)), (b"data", bytes(12))), "must be 16-bit PCM or float32"),
+    "nochan.wav": (_riff((b"fmt ", _fmt(1, 0, 16)), (b"data", bytes(8))), "has no channels"),
+    "ragged.wav": (_riff((b"fmt ", _fmt(1, 2, 16)), (b"data", bytes(6))), "not a whole number of frames"),
+}
+
+
+@pytest.mark.parametrize("name", sorted(MALFORMED))
+def test_malformed_audio_is_a_clean_error(tmp_path, name):
+    """Malformed .npy / .wav input ends with exit code 1 and a message that names the
+    problem: never a crash, and never a read past the end of the file."""
+    data, msg = MALFORMED[name]
+    p = tmp_path / name
+    p.write_bytes(data)
+    r = run(str(p), "--model", str(tmp_path))
+    assert r.returncode == 1 and msg in r.stderr, (r.returncode, r.stderr)
+
+
+WELL_FORMED = {
+    "v1_f4.npy": _npy_bytes("<f4", "(6,)", np.arange(6, dtype="<f4").tobytes()),
+    "v2_f4.npy": _npy_bytes("<f4", "(6,)", np.arange(6, dtype="<f4").tobytes(), major=2),
+    "i8.npy": _npy_bytes("<i8", "(2, 3)", np.arange(6, dtype="<i8").tobytes()),
+    "fortran.npy": _npy_bytes("<f4", "(2, 3)", np.arange(6, dtype="<f4").tobytes(), fortran=True),
+    "pcm16_stereo.wav": _riff((b"fmt ", _fmt(1, 2, 16)), (b"LIST", b"odd"), (b"data", bytes(8))),
+    "float.wav": _riff((b"fmt ", _fmt(3, 1, 32)), (b"data", np.ones(4, "<f4").tobytes())),
+    "extensible.wav": _riff((b"fmt ", _fmt(0xFFFE, 1, 32, extensible_tag=3)), (b"data", np.ones(4, "<f4").tobytes())),
+}
+
+
+@pytest.mark.skipif(gpu_available(), reason="uses the model-load failure without a GPU as the stop point")
+@pytest.mark.parametrize("name", sorted(WELL_FORMED))
+def test_well_formed_audio_is_read(tmp_path, tiny_checkpoint_dir, name):
+    """Every supported layout is read; without a B200 the run then stops at model load."""
+    p = tmp_path / name
+    p.write_bytes(WELL_FORMED[name])
+    r = run(str(p), "--model", tiny_checkpoint_dir)
+    assert r.returncode == 1 and "model load" in r.stderr, r.stderr
+
+
 @pytest.mark.skipif(gpu_available(), reason="checks the failure without a GPU")
 def test_without_a_gpu_model_load_fails_cleanly(tmp_path, tiny_checkpoint_dir):
     p = tmp_path / "a.npy"
