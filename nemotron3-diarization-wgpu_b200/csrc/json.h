@@ -2,8 +2,10 @@
 // safetensors header (objects, arrays, numbers, strings, true/false/null).
 #pragma once
 
+#include <charconv>
 #include <cstdlib>
 #include <stdexcept>
+#include <system_error>
 #include <string>
 #include <utility>
 #include <vector>
@@ -37,6 +39,17 @@ class Parser {
     }
 
   private:
+    // Deeper nesting is an error: the files read here are three levels deep, and the
+    // recursion below must not be driven into a stack overflow by a damaged file.
+    static constexpr int kMaxDepth = 128;
+    struct Nest {
+        Parser& p;
+        explicit Nest(Parser& q) : p(q) {
+            if (++p.depth_ > kMaxDepth) p.fail("nesting too deep");
+        }
+        ~Nest() { p.depth_--; }
+    };
+
     [[noreturn]] void fail(const char* what) {
         throw std::runtime_error(std::string(what) + " at byte " + std::to_string(i_));
     }
@@ -58,6 +71,7 @@ class Parser {
         const char c = s_[i_];
         Value v;
         if (c == '{') {
+            const Nest nest(*this);
             v.kind = Value::Obj;
             i_++;
             ws();
@@ -86,6 +100,7 @@ class Parser {
             }
         }
         if (c == '[') {
+            const Nest nest(*this);
             v.kind = Value::Arr;
             i_++;
             ws();
@@ -122,12 +137,14 @@ class Parser {
             return v;
         }
         if (lit("null")) return v;
-        const char* start = s_.c_str() + i_;
-        char* end = nullptr;
-        v.num = std::strtod(start, &end);
-        if (end == start) fail("bad value");
+        // from_chars reads the C number format whatever locale the host process has set
+        // (strtod would stop at the '.' under a locale with a decimal comma)
+        const char* start = s_.data() + i_;
+        const std::from_chars_result r = std::from_chars(start, s_.data() + s_.size(), v.num);
+        if (r.ec == std::errc::result_out_of_range) fail("number out of range");
+        if (r.ec != std::errc() || r.ptr == start) fail("bad value");
         v.kind = Value::Num;
-        i_ += (size_t)(end - start);
+        i_ += (size_t)(r.ptr - start);
         return v;
     }
     std::string string() {
@@ -172,6 +189,7 @@ class Parser {
     }
     const std::string& s_;
     size_t i_ = 0;
+    int depth_ = 0;
 };
 
 inline Value parse(const std::string& s) { return Parser(s).parse_document(); }
