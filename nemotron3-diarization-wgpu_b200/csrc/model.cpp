@@ -84,7 +84,7 @@ struct SafeTensors {
         if (raw.size() < 8) throw Error(kStatusSafetensors, "safetensors error: file too short");
         uint64_t hlen = 0;
         std::memcpy(&hlen, raw.data(), 8);
-        if (8 + hlen > raw.size()) throw Error(kStatusSafetensors, "safetensors error: header out of range");
+        if (hlen > raw.size() - 8) throw Error(kStatusSafetensors, "safetensors error: header out of range");
         json::Value h;
         try {
             h = json::parse(raw.substr(8, hlen));

@@ -56,3 +56,43 @@ def test_python_written_config_and_nesting_at_the_limit(tmp_path, checkpoint_dir
     with pytest.raises(n3d.DiarizationError) as e:
         _load_with(tmp_path, checkpoint_dir, nested)
     assert "nesting" not in str(e.value)
+
+
+def _canonical(v):
+    if isinstance(v, bool) or v is None:
+        return json.dumps(v)
+    if isinstance(v, (int, float)):
+        return "%.17g" % float(v)
+    if isinstance(v, str):
+        return '"' + v + '"'
+    if isinstance(v, list):
+        return "[" + ",".join(_canonical(x) for x in v) + "]"
+    return "{" + ",".join('"%s":%s' % (k, _canonical(x)) for k, x in v.items()) + "}"
+
+
+@pytest.fixture(scope="module")
+def json_dump(tmp_path_factory):
+    exe = tmp_path_factory.mktemp("jd") / "json_dump"
+    r = subprocess.run(["g++", "-std=c++17", "-O1", "-o", str(exe), os.path.join(ROOT, "tests", "json_dump.cpp")],
+                       capture_output=True, text=True)
+    if r.returncode:
+        pytest.skip("no host C++ compiler: " + r.stderr[-300:])
+    return str(exe)
+
+
+def test_reader_matches_python_on_the_checkpoint_files(json_dump, checkpoint_dir):
+    """The same reader parses the checkpoint's two configs and its safetensors header
+    (417 entries of dtype, shape and byte offsets) exactly as Python's json does."""
+    for name in ("config.json", "processor_config.json"):
+        path = os.path.join(checkpoint_dir, name)
+        with open(path) as f:
+            want = _canonical(json.load(f))
+        got = subprocess.run([json_dump, path], capture_output=True, text=True).stdout.strip()
+        assert got == want, name
+    path = os.path.join(checkpoint_dir, "model.safetensors")
+    with open(path, "rb") as f:
+        n = int.from_bytes(f.read(8), "little")
+        header = json.loads(f.read(n))
+    got = subprocess.run([json_dump, "--safetensors", path], capture_output=True, text=True).stdout.strip()
+    assert got == _canonical(header)
+    assert len(header) >= 417
