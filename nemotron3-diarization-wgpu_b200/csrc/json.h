@@ -3,6 +3,7 @@
 #pragma once
 
 #include <charconv>
+#include <cmath>
 #include <cstdlib>
 #include <stdexcept>
 #include <system_error>
@@ -142,7 +143,7 @@ class Parser {
         const char* start = s_.data() + i_;
         const std::from_chars_result r = std::from_chars(start, s_.data() + s_.size(), v.num);
         if (r.ec == std::errc::result_out_of_range) fail("number out of range");
-        if (r.ec != std::errc() || r.ptr == start) fail("bad value");
+        if (r.ec != std::errc() || r.ptr == start || !std::isfinite(v.num)) fail("bad value");  // no nan / inf
         v.kind = Value::Num;
         i_ += (size_t)(r.ptr - start);
         return v;

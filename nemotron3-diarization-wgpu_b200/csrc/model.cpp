@@ -46,8 +46,23 @@ const json::Value& need(const json::Value& v, const char* key, const std::string
     if (!p) throw Error(kStatusJson, "failed to parse " + file + ": missing field `" + key + "`");
     return *p;
 }
-int need_int(const json::Value& v, const char* key, const std::string& f) { return (int)need(v, key, f).num; }
-double need_num(const json::Value& v, const char* key, const std::string& f) { return need(v, key, f).num; }
+// A count: an integer of at least `lo` (the reference reads these fields as usize, so
+// negative, fractional and non-numeric values are errors there too).  Fields that the
+// schedule divides by or steps with pass lo = 1.
+int count_value(const json::Value& x, const char* key, const std::string& f, int lo) {
+    if (x.kind != json::Value::Num || x.num != std::floor(x.num) || x.num < lo || x.num > (double)(1 << 24))
+        throw Error(kStatusJson, "failed to parse " + f + ": `" + key + "` must be an integer of at least " +
+                                     std::to_string(lo));
+    return (int)x.num;
+}
+int need_int(const json::Value& v, const char* key, const std::string& f, int lo = 1) {
+    return count_value(need(v, key, f), key, f, lo);
+}
+double need_num(const json::Value& v, const char* key, const std::string& f) {
+    const json::Value& x = need(v, key, f);
+    if (x.kind != json::Value::Num) throw Error(kStatusJson, "failed to parse " + f + ": `" + key + "` must be a number");
+    return x.num;
+}
 
 // Round to the nearest bfloat16, ties to even: the host twin of cvt.rn.bf16.f32
 // (finite inputs).
@@ -204,10 +219,10 @@ Config load_config(const std::string& dir) {
     c.head_hidden = need_int(h, "hidden_size", fc);
     c.num_speakers = need_int(h, "num_speakers", fc);
     const json::Value& s = need(m, "streaming_config", fc);
-    c.s_fifo = need_int(s, "fifo_length", fc);
+    c.s_fifo = need_int(s, "fifo_length", fc, 0);
     c.cache_len = need_int(s, "speaker_cache_length", fc);
-    c.n_sil = need_int(s, "speaker_cache_silence_frames_per_speaker", fc);
-    c.s_period = need_int(s, "speaker_cache_update_period", fc);
+    c.n_sil = need_int(s, "speaker_cache_silence_frames_per_speaker", fc, 0);
+    c.s_period = need_int(s, "speaker_cache_update_period", fc, 0);
     c.thr = (float)need_num(s, "prediction_score_threshold", fc);
     c.min_pos_rate = (float)need_num(s, "min_positive_scores_rate", fc);
     c.strong_rate = (float)need_num(s, "strong_boost_rate", fc);
@@ -216,9 +231,9 @@ Config load_config(const std::string& dir) {
     c.s_sub = need_int(s, "subsampling_factor", fc);
     c.s_ns = need_int(s, "num_speakers", fc);
     c.chunk_length = need_int(m, "chunk_length", fc);
-    c.chunk_rc = need_int(m, "chunk_right_context", fc);
-    c.o_fifo = need_int(m, "fifo_length", fc);
-    c.o_period = need_int(m, "speaker_cache_update_period", fc);
+    c.chunk_rc = need_int(m, "chunk_right_context", fc, 0);
+    c.o_fifo = need_int(m, "fifo_length", fc, 0);
+    c.o_period = need_int(m, "speaker_cache_update_period", fc, 0);
     const json::Value& fe = need(p, "feature_extractor", fp);
     c.feature_size = need_int(fe, "feature_size", fp);
     c.n_fft = need_int(fe, "n_fft", fp);
@@ -232,11 +247,16 @@ Config load_config(const std::string& dir) {
     for (int i = 0; i < 3; i++) {
         const json::Value& v = need(sm, names[i], fp);
         if (v.arr.size() != 2) throw Error(kStatusJson, "failed to parse " + fp + ": bad streaming mode");
-        c.modes[i][0] = (int)v.arr[0].num;
-        c.modes[i][1] = (int)v.arr[1].num;
+        c.modes[i][0] = count_value(v.arr[0], names[i], fp, 1);  // chunk length, encoder frames
+        c.modes[i][1] = count_value(v.arr[1], names[i], fp, 0);  // right context
     }
-    // CacheConfig::from_model (src/streaming.rs:54-72)
+    // CacheConfig::from_model (src/streaming.rs:54-72); its usize arithmetic needs a
+    // non-negative per-speaker budget
     const int budget = c.cache_len / c.s_ns - c.n_sil;
+    if (budget < 0)
+        throw Error(kStatusJson, "failed to parse " + fc + ": unsupported speaker cache geometry (" +
+                                     std::to_string(c.cache_len) + " frames for " + std::to_string(c.s_ns) +
+                                     " speakers with " + std::to_string(c.n_sil) + " silence frames each)");
     c.min_pos = (int)std::floor((float)budget * c.min_pos_rate);
     c.k_strong = (int)std::floor((float)budget * c.strong_rate);
     c.k_weak = (int)std::floor((float)budget * c.weak_rate);

@@ -96,3 +96,58 @@ def test_reader_matches_python_on_the_checkpoint_files(json_dump, checkpoint_dir
     got = subprocess.run([json_dump, "--safetensors", path], capture_output=True, text=True).stdout.strip()
     assert got == _canonical(header)
     assert len(header) >= 417
+
+
+def test_random_count_values_never_crash_or_hang(tmp_path, checkpoint_dir):
+    """Well-formed configs with random count values (zero, negative, fractional,
+    strings, null, huge): each load succeeds or is a Json error, and planning every
+    loaded one in all four modes ends (a division by zero or an endless schedule loop
+    would crash or time out the child)."""
+    r = subprocess.run([sys.executable, WORKER, checkpoint_dir, str(tmp_path), "9", "1500", "values"],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, (r.returncode, r.stderr[-2000:])
+    ends = json.loads(r.stdout.strip().splitlines()[-1])
+    assert set(ends) <= {"ok", "Json", "plan:UnsupportedAudio"}, ends
+    assert ends["ok"] > 100 and ends["Json"] > 100
+
+
+def _edited(checkpoint_dir, tmp_path, where, key, value):
+    with open(os.path.join(checkpoint_dir, "config.json")) as f:
+        cfg = json.load(f)
+    with open(os.path.join(checkpoint_dir, "processor_config.json")) as f:
+        proc = json.load(f)
+    doc = proc if where.startswith("proc") else cfg
+    sec = where.split(":")[1] if ":" in where else None
+    (doc[sec] if sec else doc)[key] = value
+    d = tmp_path / "e"
+    d.mkdir(exist_ok=True)
+    (d / "config.json").write_text(json.dumps(cfg))
+    (d / "processor_config.json").write_text(json.dumps(proc))
+    return str(d)
+
+
+@pytest.mark.parametrize("where,key,value,ok", [
+    ("cfg", "chunk_length", 0, False),                      # the offline loop steps by it
+    ("proc:feature_extractor", "hop_length", 0, False),     # frame_count divides by it
+    ("cfg:streaming_config", "num_speakers", 0, False),     # the cache budget divides by it
+    ("cfg:streaming_config", "speaker_cache_length", 7, False),  # budget 7 / 8 - 1 < 0
+    ("cfg:streaming_config", "speaker_cache_length", 8, True),   # budget 8 / 8 - 1 = 0
+    ("cfg", "chunk_right_context", 0, True),                # zero look-ahead is allowed
+    ("cfg:streaming_config", "fifo_length", 0, True),
+    ("cfg", "fifo_length", -1, False),
+    ("cfg", "chunk_length", 2.5, False),
+    ("cfg", "chunk_length", "340", False),
+    ("cfg", "chunk_length", None, False),
+    ("cfg", "chunk_length", 340.0, True),                   # an integral float is still a count
+    ("proc:streaming_modes", "ultra_low_latency", [0, 1], False),
+    ("proc:streaming_modes", "ultra_low_latency", [3, 0], True),
+    ("cfg:streaming_config", "prediction_score_threshold", "0.25", False),
+])
+def test_count_fields_are_validated(tmp_path, checkpoint_dir, where, key, value, ok):
+    d = _edited(checkpoint_dir, tmp_path, where, key, value)
+    if ok:
+        n3d.Config.load(d).close()
+        return
+    with pytest.raises(n3d.DiarizationError) as e:
+        n3d.Config.load(d)
+    assert e.value.kind == "Json"
