@@ -20,6 +20,7 @@
 #include <sstream>
 
 #include "json.h"
+#include "safetensors.h"
 
 namespace n3d {
 
@@ -29,9 +30,9 @@ void cuda_check(cudaError_t e, const char* what) {
 
 namespace {
 
-constexpr int kStatusIo = 1, kStatusJson = 2, kStatusSafetensors = 3, kStatusDtype = 4, kStatusMissing = 5,
-              kStatusShape = 6, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11, kStatusNoDevice = 12,
-              kStatusArg = 13, kStatusCuda = 10;
+// n3d_status codes (include/n3d.h); the checkpoint reader's own are in safetensors.h
+constexpr int kStatusIo = 1, kStatusJson = 2, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11,
+              kStatusNoDevice = 12, kStatusArg = 13, kStatusCuda = 10;
 
 std::string read_file(const std::string& path) {
     std::ifstream f(path, std::ios::binary);
@@ -83,71 +84,6 @@ float tf32_rna_host(float x) {
     std::memcpy(&r, &u, 4);
     return r;
 }
-
-// ------------------------------------------------------------- safetensors
-struct Tensor {
-    std::vector<long long> shape;
-    const float* data;
-};
-
-struct SafeTensors {
-    std::string raw;
-    std::map<std::string, Tensor> tensors;
-
-    explicit SafeTensors(const std::string& path) {
-        raw = read_file(path);
-        if (raw.size() < 8) throw Error(kStatusSafetensors, "safetensors error: file too short");
-        uint64_t hlen = 0;
-        std::memcpy(&hlen, raw.data(), 8);
-        if (hlen > raw.size() - 8) throw Error(kStatusSafetensors, "safetensors error: header out of range");
-        json::Value h;
-        try {
-            h = json::parse(raw.substr(8, hlen));
-        } catch (const std::exception& e) {
-            throw Error(kStatusSafetensors, std::string("safetensors error: ") + e.what());
-        }
-        const size_t base = 8 + hlen;
-        for (const auto& kv : h.obj) {
-            if (kv.first == "__metadata__") continue;
-            const json::Value& t = kv.second;
-            const json::Value* dt = t.get("dtype");
-            const json::Value* sh = t.get("shape");
-            const json::Value* off = t.get("data_offsets");
-            if (!dt || !sh || !off || off->arr.size() != 2)
-                throw Error(kStatusSafetensors, "safetensors error: bad entry " + kv.first);
-            if (dt->str != "F32")
-                throw Error(kStatusDtype, "tensor `" + kv.first + "` has dtype " + dt->str + ", this port only reads F32");
-            Tensor tt;
-            long long numel = 1;
-            for (const auto& d : sh->arr) {
-                tt.shape.push_back((long long)d.num);
-                numel *= (long long)d.num;
-            }
-            const size_t s = (size_t)off->arr[0].num, e = (size_t)off->arr[1].num;
-            if (e < s || base + e > raw.size() || (e - s) != (size_t)numel * 4)
-                throw Error(kStatusSafetensors, "safetensors error: bad data offsets for " + kv.first);
-            if ((base + s) % 4) throw Error(kStatusSafetensors, "safetensors error: misaligned tensor " + kv.first);
-            tt.data = reinterpret_cast<const float*>(raw.data() + base + s);
-            tensors[kv.first] = tt;
-        }
-    }
-
-    // Weights::tensor (src/weights.rs:78-93): fetch with a shape check.
-    const float* get(const std::string& name, std::vector<long long> shape) const {
-        auto it = tensors.find(name);
-        if (it == tensors.end()) throw Error(kStatusMissing, "tensor `" + name + "` is missing from the checkpoint");
-        if (it->second.shape != shape) {
-            auto fmt = [](const std::vector<long long>& v) {
-                std::string s = "[";
-                for (size_t i = 0; i < v.size(); i++) s += (i ? ", " : "") + std::to_string(v[i]);
-                return s + "]";
-            };
-            throw Error(kStatusShape,
-                        "tensor `" + name + "` has shape " + fmt(it->second.shape) + ", expected " + fmt(shape));
-        }
-        return it->second.data;
-    }
-};
 
 // ------------------------------------------------------------- mel constants
 // librosa slaney filterbank (src/mel.rs:81-123), f64 math stored as f32.
