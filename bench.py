@@ -47,6 +47,24 @@ def _peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def smi_id(local: int) -> str:
+    """nvidia-smi's name for torch device `local`: its UUID, because CUDA and nvidia-smi
+    may number the GPUs differently (CUDA_VISIBLE_DEVICES, fastest-first ordering).
+    Falls back to the index when the UUID is unavailable or nvidia-smi does not know it."""
+    try:
+        import torch
+
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        gid = u if u.startswith("GPU-") else "GPU-" + u
+        r = subprocess.run(["nvidia-smi", f"--id={gid}", "--query-gpu=index", "--format=csv,noheader"],
+                           capture_output=True, text=True, timeout=10)
+        if r.returncode == 0 and r.stdout.strip():
+            return gid
+    except Exception:
+        pass
+    return str(local)
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons, sampled every 200 ms while running."""
 
@@ -54,8 +72,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, gpu: str):
+        self.gpu = gpu  # an nvidia-smi id (smi_id)
         self.rows = []
         self._stop = threading.Event()
         self._t = threading.Thread(target=self._run, daemon=True)
@@ -63,7 +81,7 @@ class ClockSampler:
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                                       "--format=csv,noheader,nounits"], capture_output=True, text=True,
                                      timeout=5).stdout.strip()
                 if out:
@@ -88,7 +106,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 5 + i and r[5 + i] == "Active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows), "nvidia_smi_index": self.rows[0][0]}
 
 
 def item_seeds(workload: str, rank: int, n_items: int) -> list:
@@ -319,7 +337,7 @@ def main():
     barrier(world)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(smi_id(local)) as clk:
         e0.record(stream)
         for _ in range(args.steps):
             step()
