@@ -1,8 +1,11 @@
 """The C-ABI library on the CPU: it loads, exports every symbol include/n3d.h
 declares, fails loudly without a B200, and its host-only functions
-(extract_speaker_dict, activity_stats) match the oracle exactly."""
+(extract_speaker_dict, activity_stats) match the oracle exactly.  A plain C99 program
+(tests/c_consumer.c) compiles against the header, links the library and gets the same
+answers as the Python binding."""
 
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -10,6 +13,8 @@ import pytest
 import n3d
 import oracle
 from conftest import gpu_available
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_library_exports_every_header_symbol():
@@ -124,3 +129,42 @@ def test_segments_and_activity_match_the_oracle_on_random_cases():
         assert n3d.activity_stats(logits, T, ns, mask, thr) == oracle.activity_stats(logits, T, ns, mask, thr)
 
     check()
+
+
+def test_plain_c_caller(tmp_path, checkpoint_dir):
+    """include/n3d.h compiles as C99 (pedantic) and links against libn3d.so; a C program
+    gets the same answers through it as the Python binding does."""
+    import subprocess
+
+    src = os.path.join(ROOT, "tests", "c_consumer.c")
+    exe = tmp_path / "c_consumer"
+    lib_dir = os.path.dirname(n3d.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", os.path.join(ROOT, "include"),
+                        src, "-o", str(exe), "-L", lib_dir, "-ln3d", "-Wl,-rpath," + lib_dir],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    args = [str(exe), checkpoint_dir] + ([] if gpu_available() else ["load"])
+    r = subprocess.run(args, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = r.stdout.splitlines()
+    assert out[0] == "version " + n3d.lib().n3d_version().decode()
+    assert out[1] == "frame_duration 0.00999999978"
+    cfg = n3d.Config.load(checkpoint_dir)
+    p = cfg.mode_params("ultra_low_latency")
+    assert out[2] == (f"ultra first_chunk_samples {p['first_chunk_samples']} samples_per_chunk "
+                      f"{p['samples_per_chunk']} latency_ms {p['latency_ms']}")
+    steps, tot = cfg.schedule(480000, "offline")
+    assert out[3] == (f"offline steps {len(steps)} frames {tot['num_frames']} chunks {tot['num_chunks']}" +
+                      "".join(f" [{s['window_frames']} {s['valid_frames']} {s['scored_frames']}]" for s in steps))
+    assert out[4].startswith("short streaming audio: unsupported audio")
+    segs = n3d.extract_speaker_dict(_segment_logits(), 6, 2, 0.01)
+    assert out[5:5 + len(segs)] == [f"segment {s.start:.2f} {s.end:.2f} {s.speaker}" for s in segs]
+    if not gpu_available():
+        assert out[-1] == "load status 12"  # N3D_ERR_NO_DEVICE
+
+
+def _segment_logits():
+    """The C helper's logits: [6 frames, 2 speakers], speaker 0 in frames 1-2, speaker 1 in frame 3."""
+    lg = np.full(12, -4.0, np.float32)
+    lg[[2, 4, 7]] = 4.0
+    return lg
