@@ -259,6 +259,39 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def window_flops(cfg: dict, S: int, G: int) -> int:
+    """Algorithmic FLOP of one chunk-loop window of S frames with G newly embedded ones:
+    per layer 8h^2 + 4hI per frame (q, k, v, o, fc1, fc2) and 4hS per frame of
+    attention; the head's projection, k=3 conv, dense and out_proj per frame; the
+    embedder's 8-frame projection per new frame.  For the reference architecture this is
+    197 615 616 S + 63 488 S^2 + 1 048 576 G."""
+    a, hc = cfg["audio_config"], cfg["head_config"]
+    h, inter, layers, sub, mels = (a["hidden_size"], a["intermediate_size"], a["num_hidden_layers"],
+                                   a["subsampling_factor"], a["num_mel_bins"])
+    hh, ns = hc["hidden_size"], hc["num_speakers"]
+    per_frame = layers * (8 * h * h + 4 * h * inter) + 2 * h * hh + 2 * 3 * hh * hh * sub + sub * (2 * hh * hh + 2 * hh * ns)
+    return per_frame * S + layers * 4 * h * S * S + 2 * sub * mels * h * G
+
+
+def run_flops(ckpt: str, lens, mode: str) -> int:
+    """Algorithmic FLOP of running `lens` samples per item in `mode`: window_flops
+    summed over the schedule the library plans (n3d_schedule)."""
+    import n3d
+
+    with open(os.path.join(ckpt, "config.json")) as f:
+        cfg = json.load(f)
+    c = n3d.Config.load(ckpt)
+    total, memo = 0, {}
+    for n in lens:
+        if n not in memo:
+            steps, _ = c.schedule(int(n), mode)
+            memo[n] = sum(window_flops(cfg, st["window_frames"], st["window_frames"] - st["cached_frames"])
+                          for st in steps)
+        total += memo[n]
+    c.close()
+    return total
+
+
 # Mean DRAM read + write bytes of one encoder GEMM launch (QKV, O, FC1, FC2 of one layer)
 # at 32 clips per step, from the ncu capture summarised in profiles/ (grows with rows).
 GEMM_DRAM_BYTES_32CLIPS = 155.7e6
@@ -402,6 +435,15 @@ def main():
                 "what": f"host wall time of one n3d_sessions_push call handing 240 ms of new audio to each of "
                         f"{n_items} sessions (H2D, log-mel, embedder, one chunk step, D2H of the new rows)"}
 
+    try:  # the whole step's algorithmic rate (host arithmetic over the planned schedule)
+        step_flop = run_flops(ckpt, lens, mode)
+        step_rate = {"flop_per_step_per_gpu": step_flop,
+                     "tflops_per_gpu": step_flop / (ms / args.steps / 1e3) / 1e12,
+                     "what": "sum over the step's windows of F(S, G) = 197 615 616 S + 63 488 S^2 + 1 048 576 G "
+                             "(tower, head, embedder; S window frames, G new frames) over the device time"}
+    except Exception as e:  # never lose the bench line to this report
+        step_rate = {"error": f"{type(e).__name__}: {e}"[:200]}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rt, dt = oracle_rtfx(ckpt, make_clips(0, 1, CLIP_S)[0])
@@ -438,6 +480,7 @@ def main():
                          "avg_launch_ms": g["ms"] / max(g["launches"], 1),
                          "measured": "CUDA events around each launch on the model's stream, over a second "
                                      "run of the same K steps (events would perturb the headline region)"},
+            "step_algorithmic": step_rate,
             "kernel_share": {k: round(v["ms"] / total_prof_ms, 4) for k, v in classes.items()},
             "gemm_sites": {k: {"share": round(v["ms"] / total_prof_ms, 4),
                                "tflops": round(v["flops"] / (v["ms"] / 1e3) / 1e12, 1) if v["ms"] else None}

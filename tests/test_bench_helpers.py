@@ -33,3 +33,21 @@ def test_smi_id_falls_back_to_the_index():
 def test_job_rate():
     # 8 ranks x 128 clips x 60 s x 10 steps over the slowest rank's 1.875 s
     assert bench.job_rate(8, 128, 60.0, 10, 1875.0) == pytest.approx(8 * 128 * 60.0 * 10 / 1.875)
+
+
+def test_window_flops_is_the_published_formula():
+    import synth
+
+    cfg = synth.MODEL_CONFIG
+    for S, G in [(1, 0), (684, 380), (370, 3), (0, 1)]:
+        assert bench.window_flops(cfg, S, G) == 197_615_616 * S + 63_488 * S * S + 1_048_576 * G
+
+
+def test_run_flops_over_the_planned_schedule(checkpoint_dir):
+    """A 60 s clip: 3 offline windows, 333.0 GFLOP; 250 ultra-low-latency windows,
+    14 600.6 GFLOP (G counts every newly embedded row, look-ahead included, since each
+    streaming chunk is embedded whole); identical lengths are planned once."""
+    off = bench.run_flops(checkpoint_dir, [960_000] * 3, "offline")
+    assert round(off / 3 / 1e9, 1) == 333.0
+    ultra = bench.run_flops(checkpoint_dir, [960_000], "ultra_low_latency")
+    assert round(ultra / 1e9, 1) == 14600.6
