@@ -87,6 +87,7 @@ class RunOutput:
 
 @dataclass(frozen=True)
 class Segment:
+    """Segment (src/segments.rs:9-14): one speaker's active span, in seconds."""
     start: float
     end: float
     speaker: int
@@ -109,6 +110,8 @@ _lib = None
 
 
 def lib() -> C.CDLL:
+    """The loaded libn3d.so with every entry point's argument and result types set.
+    Raises OSError when the library is not built: there is no CPU fallback."""
     global _lib
     if _lib is not None:
         return _lib
@@ -218,11 +221,13 @@ class Config:
 
     @classmethod
     def load(cls, directory: str) -> "Config":
+        """load_configs (src/config.rs:221-225) through n3d_config_load."""
         h = C.c_void_p()
         _check(lib().n3d_config_load(directory.encode(), C.byref(h)))
         return cls(h.value)
 
     def close(self) -> None:
+        """Release the configuration (n3d_config_free)."""
         if self._h:
             lib().n3d_config_free(self._h)
             self._h = C.c_void_p()
@@ -273,11 +278,14 @@ class Model:
 
     @classmethod
     def load_gpu(cls, directory: str, device: int = 0) -> "Model":
+        """Model::load_gpu (src/model.rs:160-166): config.json, processor_config.json and
+        model.safetensors from `directory`, with the weights resident on `device`."""
         h = C.c_void_p()
         _check(lib().n3d_model_load_gpu(directory.encode(), device, C.byref(h)))
         return cls(h.value, device)
 
     def close(self) -> None:
+        """Free the model (n3d_model_free), after any sessions still open on it."""
         if self._h:
             for ss in list(self._sessions):  # sessions must go before their model
                 ss.free()
@@ -296,10 +304,12 @@ class Model:
 
     @property
     def num_speakers(self) -> int:
+        """Model::num_speakers (src/model.rs:211-213)."""
         return lib().n3d_num_speakers(self._h)
 
     @property
     def hidden_size(self) -> int:
+        """Model::hidden_size (src/model.rs:215-217)."""
         return lib().n3d_hidden_size(self._h)
 
     def describe(self) -> str:
@@ -307,18 +317,22 @@ class Model:
         return lib().n3d_model_describe(self._h).decode()
 
     def run_offline(self, samples) -> RunOutput:
+        """Model::run_offline (src/model.rs:232-234) on 16 kHz mono samples."""
         s = _f32(samples)
         o = _RunOutput()
         _check(lib().n3d_run_offline(self._h, _ptr(s), s.size, C.byref(o)))
         return _collect(o)
 
     def run_streaming(self, samples, mode: str) -> RunOutput:
+        """Model::run_streaming (src/model.rs:313-336) in "low_latency",
+        "very_low_latency" or "ultra_low_latency"."""
         s = _f32(samples)
         o = _RunOutput()
         _check(lib().n3d_run_streaming(self._h, _ptr(s), s.size, MODES[mode], C.byref(o)))
         return _collect(o)
 
     def run_batch(self, clips, mode: str = "offline") -> list[RunOutput]:
+        """n3d_run_batch: many clips in one call; each result equals the clip's own run."""
         arrs = [_f32(c) for c in clips]
         n = len(arrs)
         ptrs = (_fp * max(n, 1))(*[_ptr(a) for a in arrs])
@@ -347,6 +361,7 @@ class Model:
         return [_collect(outs[i]) for i in range(n)]
 
     def batch_out_frames(self, lens, mode: str = "offline") -> list[int]:
+        """Logit rows each clip of the given lengths returns in `mode` (n3d_batch_out_frames)."""
         n = len(lens)
         arr = (_sz * max(n, 1))(*lens)
         out = (_sz * max(n, 1))()
@@ -354,6 +369,8 @@ class Model:
         return [int(out[i]) for i in range(n)]
 
     def run_batch_device(self, mode: str, d_audio: int, offsets, lens, d_logits: int, out_offsets) -> None:
+        """n3d_run_batch_device: clips already in device memory (d_audio at `offsets`),
+        logits written to device memory at `out_offsets` rows of d_logits."""
         n = len(lens)
         _check(lib().n3d_run_batch_device(self._h, MODES[mode], C.c_void_p(d_audio), (_sz * max(n, 1))(*offsets),
                                           (_sz * max(n, 1))(*lens), n, C.c_void_p(d_logits),
@@ -361,18 +378,22 @@ class Model:
 
     # ---- profiling (device time per kernel class, CUDA events on the model's stream)
     def profile_enable(self, on: bool = True) -> None:
+        """Time every launch of later runs with CUDA events (n3d_profile_enable; resets)."""
         _check(lib().n3d_profile_enable(self._h, int(on)))
 
     def profile_read(self) -> dict:
+        """Per kernel class: launches, device ms, algorithmic FLOP and bytes (n3d_profile_read)."""
         buf = (_KernelStats * 16)()
         n = lib().n3d_profile_read(self._h, buf, 16)
         return {buf[i].name.decode(): dict(launches=int(buf[i].launches), ms=buf[i].ms, flops=buf[i].flops,
                                            bytes=buf[i].bytes) for i in range(n)}
 
     def step_timing_enable(self, on: bool = True) -> None:
+        """Record the device time of each chunk-loop step of later runs (n3d_step_timing_enable)."""
         _check(lib().n3d_step_timing_enable(self._h, int(on)))
 
     def step_times(self) -> list[float]:
+        """The recorded chunk-loop step times, ms (n3d_step_times)."""
         n = lib().n3d_step_times(self._h, None, 0)
         buf = (C.c_double * max(n, 1))()
         lib().n3d_step_times(self._h, buf, n)
@@ -380,6 +401,7 @@ class Model:
 
     # ---- stages (GpuEngine, src/gpu_engine.rs)
     def log_mel(self, samples, centered: bool = True) -> np.ndarray:
+        """log_mel (src/mel.rs:160-225) on the device: [frames, 128]."""
         s = _f32(samples)
         cap = (s.size // 160 + 2) * 128
         out = np.zeros(max(cap, 1), np.float32)
@@ -388,12 +410,15 @@ class Model:
         return out[: frames.value * 128].reshape(frames.value, 128)
 
     def embed_range(self, mel, num_frames: int, lo: int, hi: int) -> np.ndarray:
+        """GpuEngine::embed_mel_range (src/gpu_engine.rs:1335-1379): groups lo..hi."""
         m = _f32(mel) if num_frames else np.zeros(1, np.float32)
         out = np.zeros((hi - lo) * self.hidden_size, np.float32)
         _check(lib().n3d_embed_range(self._h, _ptr(m), num_frames, lo, hi, _ptr(out)))
         return out.reshape(hi - lo, self.hidden_size)
 
     def forward_embeds(self, embeds, valid: int) -> np.ndarray:
+        """GpuEngine::forward_embeds (src/gpu_engine.rs:1506): the tower over a window
+        whose first `valid` frames are unmasked."""
         e = _f32(embeds)
         frames = e.size // self.hidden_size
         out = np.zeros(e.size, np.float32)
@@ -401,12 +426,14 @@ class Model:
         return out.reshape(frames, self.hidden_size)
 
     def head_forward(self, encoder_out, frames: int) -> np.ndarray:
+        """GpuEngine::head_forward (src/gpu_engine.rs:1695): [frames * 8, speakers] logits."""
         e = _f32(encoder_out)
         out = np.zeros(frames * 8 * self.num_speakers, np.float32)
         _check(lib().n3d_head_forward(self._h, _ptr(e), frames, _ptr(out)))
         return out.reshape(frames * 8, self.num_speakers)
 
     def forward_window(self, embeds, valid: int) -> np.ndarray:
+        """GpuEngine::forward_window (src/gpu_engine.rs:1516-1520): tower and head."""
         e = _f32(embeds)
         frames = e.size // self.hidden_size
         out = np.zeros(frames * 8 * self.num_speakers, np.float32)
@@ -423,17 +450,20 @@ class Session:
         self._model = model  # the model outlives its sessions
 
     def push(self, samples) -> RunOutput:
+        """Append samples; the logit rows of every chunk they complete."""
         s = _f32(samples)
         o = _RunOutput()
         _check(lib().n3d_session_push(self._h, _ptr(s), s.size, C.byref(o)))
         return _collect(o)
 
     def close(self) -> RunOutput:
+        """Run the final centred chunk; its rows, and the run's totals."""
         o = _RunOutput()
         _check(lib().n3d_session_close(self._h, C.byref(o)))
         return _collect(o)
 
     def free(self) -> None:
+        """Release the session's device state (n3d_session_free)."""
         if self._h:
             lib().n3d_session_free(self._h)
             self._h = None
@@ -471,6 +501,7 @@ def activity_stats(logits, num_frames: int, num_speakers: int, mask=None, thresh
 
 
 def frame_duration(hop_length: int = 160, sampling_rate: int = 16000) -> float:
+    """frame_duration (src/segments.rs:36-38): seconds per logit row."""
     return lib().n3d_frame_duration(hop_length, sampling_rate)
 
 
@@ -488,9 +519,11 @@ def linear_noalloc(device: int, d_x: int, rows: int, cols: int, d_w: int, out: i
 
 
 def layer_norm(device: int, d_x: int, rows: int, cols: int, d_w: int, d_b: int, d_y: int) -> None:
+    """tensor::layer_norm (src/tensor.rs:97-110) on device pointers; cols 512 or 1024."""
     _check(lib().n3d_layer_norm(device, d_x, rows, cols, d_w, d_b, d_y))
 
 
 def attention(device: int, d_q: int, d_k: int, d_v: int, seq: int, heads: int, head_dim: int, valid: int,
               d_out: int, rope: bool = True, theta: float = 10000.0) -> None:
+    """RoPE then masked attention (src/encoder.rs:163-185, 281-329) on device pointers."""
     _check(lib().n3d_attention(device, d_q, d_k, d_v, seq, heads, head_dim, valid, int(rope), theta, d_out))
