@@ -321,7 +321,12 @@ size_t n3d_step_times(const n3d_model *model, double *ms, size_t cap);
 
 /* ------------------------------------------------------------------ misc */
 
+/* The message of this thread's last failed call (empty after a success): the text the
+ * reference's DiarizationError carries (src/error.rs:7-45).  Valid until this thread's
+ * next call into the library. */
 const char *n3d_last_error(void);
+/* This build: library version, target architecture and precision scheme.  No reference
+ * counterpart (a static string). */
 const char *n3d_version(void);
 
 #ifdef __cplusplus
