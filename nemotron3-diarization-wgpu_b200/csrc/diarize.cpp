@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <cctype>
+#include <charconv>
 #include <chrono>
 #include <cmath>
 #include <cstdint>
@@ -252,9 +253,15 @@ int main(int argc, char** argv) {
             } else if (a == "--out") {
                 out = value("--out");
             } else if (a == "--threshold") {
-                threshold = std::stof(value("--threshold"));
+                const std::string v = value("--threshold");
+                const auto r = std::from_chars(v.data(), v.data() + v.size(), threshold);
+                if (r.ec != std::errc() || r.ptr != v.data() + v.size() || !std::isfinite(threshold))
+                    throw std::runtime_error("--threshold needs a finite number, got " + v);
             } else if (a == "--device") {
-                device = std::stoi(value("--device"));
+                const std::string v = value("--device");
+                const auto r = std::from_chars(v.data(), v.data() + v.size(), device);
+                if (r.ec != std::errc() || r.ptr != v.data() + v.size() || device < 0)
+                    throw std::runtime_error("--device needs a non-negative integer, got " + v);
             } else if (a == "--gpu") {
             } else if (a == "-h" || a == "--help") {
                 return usage(0);

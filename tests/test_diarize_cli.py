@@ -36,7 +36,12 @@ def test_usage():
 
 @pytest.mark.parametrize("args,msg", [(["--bogus"], "unknown flag --bogus"), ([], "no audio file given"),
                                       (["x.npy", "--mode", "fast"], "unknown mode fast"),
-                                      (["x.npy", "--out"], "--out needs a value")])
+                                      (["x.npy", "--out"], "--out needs a value"),
+                                      (["x.npy", "--threshold", "abc"], "--threshold needs a finite number, got abc"),
+                                      (["x.npy", "--threshold", "1e99"], "--threshold needs a finite number"),
+                                      (["x.npy", "--threshold", "0.5x"], "--threshold needs a finite number"),
+                                      (["x.npy", "--device", "-1"], "--device needs a non-negative integer"),
+                                      (["x.npy", "--device", "one"], "--device needs a non-negative integer")])
 def test_argument_errors(args, msg):
     r = run(*args)
     assert r.returncode == 1 and msg in r.stderr
