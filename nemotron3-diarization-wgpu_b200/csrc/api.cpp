@@ -3,6 +3,7 @@
 // reference API (extract_speaker_dict, activity_stats).
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -321,6 +322,7 @@ n3d_status n3d_batch_out_frames(const n3d_model* model, n3d_mode mode, const siz
         arg_check(model && (n_clips == 0 || (lens && frames_out)), "n3d_batch_out_frames: null argument");
         arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_batch_out_frames: bad mode");
         for (size_t i = 0; i < n_clips; i++) {
+            arg_check(lens[i] <= (size_t)INT_MAX, "n3d_batch_out_frames: a clip of more than 2^31 samples");
             n3d::ClipPlan p = mode == N3D_MODE_OFFLINE ? n3d::plan_offline(model->m->cfg(), (long long)lens[i])
                                                        : n3d::plan_streaming(model->m->cfg(), (long long)lens[i], (int)mode);
             frames_out[i] = (size_t)p.out_rows;
@@ -508,6 +510,7 @@ n3d_status n3d_streaming_chunks(const n3d_config* cfg, size_t n_samples, n3d_mod
     return guarded([&] {
         arg_check(cfg && count && (out || cap == 0), "n3d_streaming_chunks: null argument");
         arg_check((int)mode >= 0 && (int)mode <= 2, "n3d_streaming_chunks: mode must be a streaming mode");
+        arg_check(n_samples <= (size_t)INT_MAX, "n3d_streaming_chunks: more than 2^31 samples");
         const std::vector<n3d::StreamChunk> ch = n3d::streaming_chunks(cfg->c, (long long)n_samples, (int)mode);
         for (size_t i = 0; i < ch.size() && i < cap; i++)
             out[i] = n3d_chunk{(size_t)ch[i].start, (size_t)ch[i].len, ch[i].centered, (size_t)ch[i].mel_frames,
@@ -521,6 +524,7 @@ n3d_status n3d_schedule(const n3d_config* cfg, n3d_mode mode, size_t n_samples, 
     return guarded([&] {
         arg_check(cfg && count && (steps || cap == 0), "n3d_schedule: null argument");
         arg_check((int)mode >= 0 && (int)mode <= 3, "n3d_schedule: bad mode");
+        arg_check(n_samples <= (size_t)INT_MAX, "n3d_schedule: more than 2^31 samples");
         const n3d::ClipPlan p = mode == N3D_MODE_OFFLINE ? n3d::plan_offline(cfg->c, (long long)n_samples)
                                                          : n3d::plan_streaming(cfg->c, (long long)n_samples, (int)mode);
         const size_t n = p.steps.size();

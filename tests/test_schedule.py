@@ -153,3 +153,18 @@ def test_config_errors(tmp_path, checkpoint_dir):
     with pytest.raises(n3d.DiarizationError) as e:
         good.streaming_chunks(16000, "offline")
     assert e.value.kind == "InvalidArgument"
+
+
+def test_lengths_beyond_2_31_samples_are_rejected(cfg):
+    """The runs reject recordings of more than 2^31 samples (about 37 hours); the
+    planners do too, instead of overflowing their frame counts."""
+    n = 2**31 - 1
+    steps, tot = cfg.schedule(n, "offline")
+    assert tot["num_frames"] == n // 160 + 1
+    for mode in ("offline", "ultra_low_latency"):
+        with pytest.raises(n3d.DiarizationError) as e:
+            cfg.schedule(2**31, mode)
+        assert e.value.kind == "InvalidArgument"
+    with pytest.raises(n3d.DiarizationError) as e:
+        cfg.streaming_chunks(2**40, "low_latency")
+    assert e.value.kind == "InvalidArgument"
