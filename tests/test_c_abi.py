@@ -105,7 +105,7 @@ def _segment_case(draw):
     thr = draw(st.sampled_from([0.1, 0.25, 0.5, 0.5000001, 0.9]))
     edge = float(np.log(thr / (1.0 - thr)))  # the logit whose sigmoid sits on the threshold
     vals = st.sampled_from([0.0, -0.0, 1e-7, -1e-7, 3.0, -3.0, 40.0, -40.0, edge, np.nextafter(edge, 9.0),
-                            np.nextafter(edge, -9.0)]) | st.floats(-8, 8, width=32)
+                            np.nextafter(edge, -9.0), np.inf, -np.inf, np.nan]) | st.floats(-8, 8, width=32)
     logits = np.array(draw(st.lists(vals, min_size=T * ns, max_size=T * ns)), np.float32)
     mask = draw(st.none() | st.lists(st.booleans(), min_size=T, max_size=T))
     mask = None if mask is None else np.array(mask, np.uint8)
@@ -114,8 +114,9 @@ def _segment_case(draw):
 
 
 def test_segments_and_activity_match_the_oracle_on_random_cases():
-    """extract_speaker_dict and activity_stats (src/segments.rs:70-141) on drawn logits,
-    masks, thresholds and frame durations: the C ABI equals the oracle exactly."""
+    """extract_speaker_dict and activity_stats (src/segments.rs:70-141) on drawn logits
+    (non-finite ones included), masks, thresholds and frame durations: the C ABI equals
+    the oracle exactly."""
     from hypothesis import given, settings
     from hypothesis import strategies as st
 
