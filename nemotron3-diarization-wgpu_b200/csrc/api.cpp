@@ -357,6 +357,10 @@ n3d_status n3d_log_mel(n3d_model* model, const float* samples, size_t n, int cen
 n3d_status n3d_embed_range(n3d_model* model, const float* mel, size_t num_frames, size_t lo, size_t hi, float* out) {
     return guarded([&] {
         arg_check(model && out && (mel || num_frames == 0) && hi >= lo, "n3d_embed_range: bad argument");
+        // one call embeds at most MAX_SEQ groups (src/gpu_engine.rs:1328-1334), and the
+        // frame arithmetic stays inside 64-bit range
+        arg_check(hi - lo <= 1024 && hi <= (size_t)INT_MAX && num_frames <= (size_t)INT_MAX,
+                  "n3d_embed_range: at most 1024 groups per call, indices below 2^31");
         model->m->embed_range(mel, (long long)num_frames, (long long)lo, (long long)hi, out);
     });
 }
@@ -364,13 +368,15 @@ n3d_status n3d_embed_range(n3d_model* model, const float* mel, size_t num_frames
 n3d_status n3d_forward_embeds(n3d_model* model, const float* embeds, size_t frames, size_t valid, float* out) {
     return guarded([&] {
         arg_check(model && embeds && out, "n3d_forward_embeds: null argument");
-        model->m->forward_window(embeds, (int)frames, (int)valid, out, nullptr);
+        arg_check(frames <= (size_t)INT_MAX, "n3d_forward_embeds: frames beyond 2^31");
+        model->m->forward_window(embeds, (int)frames, (int)std::min(valid, frames), out, nullptr);
     });
 }
 
 n3d_status n3d_head_forward(n3d_model* model, const float* encoder_out, size_t frames, float* logits) {
     return guarded([&] {
         arg_check(model && encoder_out && logits, "n3d_head_forward: null argument");
+        arg_check(frames <= (size_t)INT_MAX, "n3d_head_forward: frames beyond 2^31");
         model->m->head_forward(encoder_out, (int)frames, logits);
     });
 }
@@ -378,7 +384,8 @@ n3d_status n3d_head_forward(n3d_model* model, const float* encoder_out, size_t f
 n3d_status n3d_forward_window(n3d_model* model, const float* embeds, size_t frames, size_t valid, float* logits) {
     return guarded([&] {
         arg_check(model && embeds && logits, "n3d_forward_window: null argument");
-        model->m->forward_window(embeds, (int)frames, (int)valid, nullptr, logits);
+        arg_check(frames <= (size_t)INT_MAX, "n3d_forward_window: frames beyond 2^31");
+        model->m->forward_window(embeds, (int)frames, (int)std::min(valid, frames), nullptr, logits);
     });
 }
 

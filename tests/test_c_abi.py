@@ -169,3 +169,21 @@ def _segment_logits():
     lg = np.full(12, -4.0, np.float32)
     lg[[2, 4, 7]] = 4.0
     return lg
+
+
+def test_stage_arguments_are_range_checked_before_any_model_use():
+    """Out-of-range sizes are rejected before the model is touched (the handle below is
+    a placeholder that is never dereferenced): at most 1024 groups per embed_range call,
+    as the reference's MAX_SEQ, and no size that would wrap the library's int counts."""
+    fake = C.c_void_p(64)
+    buf = np.zeros(16, np.float32)
+    p = buf.ctypes.data_as(C.POINTER(C.c_float))
+    cases = [lambda: n3d.lib().n3d_embed_range(fake, p, 100, 0, 1025, p),
+             lambda: n3d.lib().n3d_embed_range(fake, p, 2**31, 0, 4, p),
+             lambda: n3d.lib().n3d_embed_range(fake, p, 100, 2**40, 2**40 + 1, p),
+             lambda: n3d.lib().n3d_forward_embeds(fake, p, 2**32 + 5, 3, p),
+             lambda: n3d.lib().n3d_head_forward(fake, p, 2**32, p),
+             lambda: n3d.lib().n3d_forward_window(fake, p, 2**33, 1, p)]
+    for call in cases:
+        assert n3d.STATUS[call()] == "InvalidArgument"
+        assert b"2^31" in n3d.lib().n3d_last_error() or b"1024 groups" in n3d.lib().n3d_last_error()
