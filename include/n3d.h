@@ -165,12 +165,15 @@ n3d_status n3d_log_mel(n3d_model *model, const float *samples, size_t n, int cen
                        size_t out_cap, size_t *frames);
 
 /* GpuEngine::embed_mel_range (src/gpu_engine.rs:1335-1379) / Tower::embed_range
- * (src/encoder.rs:126-146): groups lo..hi of 8 stacked mel frames -> [hi-lo, hidden]. */
+ * (src/encoder.rs:126-146): groups lo..hi of 8 stacked mel frames -> [hi-lo, hidden],
+ * frames past num_frames read as zeros.  At most 1024 groups per call, as the
+ * reference's MAX_SEQ. */
 n3d_status n3d_embed_range(n3d_model *model, const float *mel, size_t num_frames, size_t lo, size_t hi,
                            float *out);
 
 /* GpuEngine::forward_embeds (src/gpu_engine.rs:1506-1514): the 31-layer tower on one
- * window [frames, hidden] with `valid` unmasked keys -> final LayerNorm output. */
+ * window [frames, hidden] (1..1024 frames) with `valid` unmasked keys (clamped to
+ * frames) -> final LayerNorm output. */
 n3d_status n3d_forward_embeds(n3d_model *model, const float *embeds, size_t frames, size_t valid, float *out);
 
 /* GpuEngine::head_forward (src/gpu_engine.rs:1695-1699): [frames, hidden] -> [frames*8, ns] logits. */
