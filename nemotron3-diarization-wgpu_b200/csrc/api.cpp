@@ -565,6 +565,8 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
     return guarded([&] {
         arg_check(d_x && d_w && d_y, "n3d_linear: null argument");
         arg_check(cols % 32 == 0 && cols > 0, "n3d_linear: cols must be a positive multiple of 32");
+        arg_check(rows <= (size_t)INT_MAX && cols <= (size_t)INT_MAX && out <= (size_t)INT_MAX,
+                  "n3d_linear: sizes beyond 2^31");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);
@@ -596,6 +598,8 @@ n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols
                           float* d_y) {
     return guarded([&] {
         arg_check(d_x && d_w && d_b && d_y, "n3d_layer_norm: null argument");
+        arg_check(cols == 512 || cols == 1024, "n3d_layer_norm: cols must be 512 or 1024");
+        arg_check(rows <= (size_t)INT_MAX, "n3d_layer_norm: rows beyond 2^31");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);
@@ -609,6 +613,8 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
     return guarded([&] {
         arg_check(d_q && d_k && d_v && d_out, "n3d_attention: null argument");
         arg_check(head_dim == 64 || head_dim == 128, "n3d_attention: head_dim must be 64 or 128");
+        arg_check(seq <= (size_t)INT_MAX && heads >= 1 && heads <= 65535, "n3d_attention: seq beyond 2^31 or heads "
+                                                                           "outside 1..65535");
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);

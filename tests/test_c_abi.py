@@ -187,3 +187,20 @@ def test_stage_arguments_are_range_checked_before_any_model_use():
     for call in cases:
         assert n3d.STATUS[call()] == "InvalidArgument"
         assert b"2^31" in n3d.lib().n3d_last_error() or b"1024 groups" in n3d.lib().n3d_last_error()
+
+
+def test_single_kernel_sizes_are_checked_before_any_cuda_call():
+    """n3d_linear, n3d_layer_norm and n3d_attention reject sizes that would wrap the
+    kernels' int counts or grid limits before they touch a device (the device pointers
+    below are placeholders that are never used)."""
+    d = C.c_void_p(256)
+    lib = n3d.lib()
+    cases = [lambda: lib.n3d_linear(0, d, 2**31, 32, d, 8, None, d),
+             lambda: lib.n3d_linear(0, d, 8, 32, d, 2**32, None, d),
+             lambda: lib.n3d_layer_norm(0, d, 8, 768, d, d, d),
+             lambda: lib.n3d_layer_norm(0, d, 2**31, 512, d, d, d),
+             lambda: lib.n3d_attention(0, d, d, d, 2**31, 8, 64, 8, 1, 10000.0, d),
+             lambda: lib.n3d_attention(0, d, d, d, 64, 0, 64, 8, 1, 10000.0, d),
+             lambda: lib.n3d_attention(0, d, d, d, 64, 70000, 64, 8, 1, 10000.0, d)]
+    for call in cases:
+        assert n3d.STATUS[call()] == "InvalidArgument", lib.n3d_last_error()
