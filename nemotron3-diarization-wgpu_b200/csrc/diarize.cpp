@@ -28,6 +28,7 @@
 
 #include "../../include/n3d.h"
 #include "json.h"
+#include "report_json.h"
 
 namespace {
 
@@ -178,36 +179,8 @@ std::vector<float> read_wav(const std::string& path) {
     return mono;
 }
 
-// serde_json's float output: shortest round-trip digits, ".0" on integral values,
-// null for non-finite values.
-std::string num(double v) {
-    if (!std::isfinite(v)) return "null";
-    char buf[40];
-    for (int p = 1; p <= 17; p++) {
-        std::snprintf(buf, sizeof buf, "%.*g", p, v);
-        if (std::strtod(buf, nullptr) == v) break;
-    }
-    std::string s = buf;
-    if (s.find_first_of(".eEn") == std::string::npos) s += ".0";
-    return s;
-}
-
-std::string quote(const std::string& s) {
-    std::string o = "\"";
-    for (unsigned char c : s) {
-        if (c == '"' || c == '\\') {
-            o += '\\';
-            o += (char)c;
-        } else if (c < 0x20) {
-            char u[8];
-            std::snprintf(u, sizeof u, "\\u%04x", c);
-            o += u;
-        } else {
-            o += (char)c;
-        }
-    }
-    return o + "\"";
-}
+using n3d::report::number;
+using n3d::report::quote;
 
 double round_to(double v, double scale) { return std::round(v * scale) / scale; }
 
@@ -318,25 +291,25 @@ int main(int argc, char** argv) {
         j << "  \"audio\": " << quote(audio) << ",\n";
         j << "  \"cache_compressed\": " << (r.cache_compressed ? "true" : "false") << ",\n";
         j << "  \"cache_frames\": " << r.cache_frames << ",\n";
-        j << "  \"duration_s\": " << num(round_to(duration_s, 1000.0)) << ",\n";
+        j << "  \"duration_s\": " << number(round_to(duration_s, 1000.0)) << ",\n";
         j << "  \"fifo_frames\": " << r.fifo_frames << ",\n";
-        j << "  \"forward_s\": " << num(round_to(infer, 1000.0)) << ",\n";
-        j << "  \"load_s\": " << num(round_to(loaded, 1000.0)) << ",\n";
+        j << "  \"forward_s\": " << number(round_to(infer, 1000.0)) << ",\n";
+        j << "  \"load_s\": " << number(round_to(loaded, 1000.0)) << ",\n";
         j << "  \"mode\": " << quote(mode->report) << ",\n";
         j << "  \"num_chunks\": " << r.num_chunks << ",\n";
         j << "  \"num_frames\": " << r.num_frames << ",\n";
         j << "  \"num_segments\": " << nseg << ",\n";
         j << "  \"num_speakers\": " << speakers.size() << ",\n";
-        j << "  \"rtfx\": " << num(round_to(rtfx, 100.0)) << ",\n";
+        j << "  \"rtfx\": " << number(round_to(rtfx, 100.0)) << ",\n";
         if (nseg == 0) {
             j << "  \"segments\": [],\n";
         } else {
             j << "  \"segments\": [\n";
             for (size_t g = 0; g < nseg; g++) {
                 j << "    {\n";
-                j << "      \"End\": " << num(round_to((double)segs[g].end, 100.0)) << ",\n";
+                j << "      \"End\": " << number(round_to((double)segs[g].end, 100.0)) << ",\n";
                 j << "      \"Speaker\": " << segs[g].speaker << ",\n";
-                j << "      \"Start\": " << num(round_to((double)segs[g].start, 100.0)) << "\n";
+                j << "      \"Start\": " << number(round_to((double)segs[g].start, 100.0)) << "\n";
                 j << "    }" << (g + 1 < nseg ? "," : "") << "\n";
             }
             j << "  ],\n";
