@@ -109,20 +109,30 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows), "nvidia_smi_index": self.rows[0][0]}
 
 
-def item_seeds(workload: str, rank: int, n_items: int) -> list:
-    """Seeds of one rank's clips (c4) or sessions (c3): disjoint across ranks, so every
-    rank runs its own audio (weak scaling).  c2 runs the same 60 min clip on every rank."""
-    if workload == "c4":
-        return [rank * 100000 + i for i in range(n_items)]
-    if workload == "c3":
-        return [rank * n_items + i for i in range(n_items)]
-    return [0] * n_items
+# 8192 clips (seeds 1000-9191) split evenly over the GPUs; config 3:
+# 256 sessions (seeds 100-355) split the same way.
+C4_CLIPS, C3_SESSIONS = 8192, 256
 
 
-def make_clips(rank: int, n: int, seconds: float):
+def item_seeds(workload: str, rank: int, n_items: int, world: int = 1) -> list:
+    """Indices of one rank's clips (c4: synth.config4_clip, seed 1000 + index) or
+    sessions (c3: synth.config3_session, seed 100 + index).  Rank r of N owns the r-th
+    of N even contiguous ranges of the configuration's items and takes the first
+    n_items of it, so the ranks' audio is disjoint (weak scaling).  c2 runs the same
+    60 min clip on every rank."""
+    total = {"c4": C4_CLIPS, "c3": C3_SESSIONS}.get(workload)
+    if total is None:
+        return [0] * n_items
+    share = total // world
+    if n_items > share:
+        raise ValueError(f"{n_items} {workload} items per GPU exceed the configuration's {share} per GPU at {world}")
+    return [rank * share + i for i in range(n_items)]
+
+
+def make_clips(rank: int, n: int, seconds: float, world: int = 1):
     import synth
 
-    return [synth.config4_clip(s, seconds) for s in item_seeds("c4", rank, n)]
+    return [synth.config4_clip(s, seconds) for s in item_seeds("c4", rank, n, world)]
 
 
 def oracle_rtfx(ckpt: str, clip: np.ndarray, reps: int = 1):
@@ -158,6 +168,62 @@ def live_sessions(model, items, mode: str, push_samples: int):
     for ss in sessions:
         ss.free()
     return np.array(lat), total
+
+
+def streaming_leg(model, world: int, rank: int, n_sessions: int, seconds: float) -> dict:
+    """The metric's streaming half on this GPU: BASELINE config 3's ultra-low-latency
+    sessions (this rank's share of the 256), `n_sessions` of `seconds` each, run
+    (1) from HBM through n3d_run_batch_device, with two CUDA events per chunk step, and
+    (2) live through n3d_sessions_push, 240 ms of new audio per session per call.
+    Latencies are the max over ranks of each rank's percentile."""
+    import torch
+
+    import synth
+
+    mode = "ultra_low_latency"
+    items = [synth.config3_session(i, seconds) for i in item_seeds("c3", rank, n_sessions, world)]
+    lens = [c.size for c in items]
+    frames = model.batch_out_frames(lens, mode)
+    offs = [int(x) for x in np.cumsum([0] + lens[:-1])]
+    ooffs = [int(x) for x in np.cumsum([0] + frames[:-1])]
+    d_audio = torch.from_numpy(np.concatenate(items)).cuda()
+    d_out = torch.empty(sum(frames) * 8, dtype=torch.float32, device="cuda")
+    run = lambda: model.run_batch_device(mode, d_audio.data_ptr(), offs, lens, d_out.data_ptr(), ooffs)
+    run()  # warm-up
+    model.step_timing_enable(True)
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    step_ms = np.array(model.step_times())
+    model.step_timing_enable(False)
+    push = 3 * 8 * 160
+    barrier(world)
+    lat, wall = live_sessions(model, items, mode, push)
+    steady = lat[3:-1] if lat.size > 5 else lat
+    del d_audio, d_out
+    return {
+        "workload": f"C3 ultra_low_latency: {n_sessions} concurrent {seconds:.0f} s sessions per GPU (config 3 "
+                    f"sessions {item_seeds('c3', rank, n_sessions, world)[0]}.. of 256 on rank {rank})",
+        "device_step_ms": {"p50": max_over_ranks(float(np.percentile(step_ms, 50)), world),
+                           "p99": max_over_ranks(float(np.percentile(step_ms, 99)), world),
+                           "steps": int(step_ms.size),
+                           "what": "device time of one chunk step of every session of a GPU (CUDA events), "
+                                   "inputs in HBM"},
+        "device_rtfx": job_rate(world, n_sessions, seconds, 1, ms),
+        "live_push_ms": {"p50": max_over_ranks(float(np.percentile(steady, 50)), world),
+                         "p99": max_over_ranks(float(np.percentile(steady, 99)), world),
+                         "calls": int(lat.size),
+                         "what": "host wall time of one n3d_sessions_push call handing 240 ms of new audio to each "
+                                 "session (H2D, log-mel, embedder, one chunk step, D2H of the new rows)"},
+        "live_rtfx": job_rate(world, n_sessions, seconds, 1, max_over_ranks(wall, world) * 1e3),
+        "unit": UNIT,
+    }
 
 
 def dist_setup(backend: str | None = None, timeout_s: float = 600.0):
@@ -259,6 +325,55 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_kernel_sweep(args, world, rank, local):
+    """every GEMM shape (M in {1024, 4096, 16384} x K, N in
+    {512..4096}), attention (8 heads, head_dim 64/128, S in {512, 1024, 4096}) and
+    LayerNorm [16384 x 1024], each timed alone through the library's probe benchmarks
+    (CUDA events, resident synthetic operands), as TFLOP/s or GB/s and as a fraction of
+    the measured peaks.  Every rank times its own GPU; rank 0 prints its line."""
+    import n3d
+
+    peaks, src = _peaks()
+    burst = float(peaks.get("bf16_tflops"))
+    hbm = float(peaks.get("hbm_gbs"))
+    iters = max(args.steps, 5)
+    gemm, tot_f, tot_ms = [], 0.0, 0.0
+    with ClockSampler(smi_id(local)) as clk:
+        for m in (1024, 4096, 16384):
+            for k in (512, 1024, 2048, 4096):
+                for n in (512, 1024, 2048, 4096):
+                    ms = n3d.bench_linear(local, m, k, n, iters)
+                    f = 2.0 * m * n * k
+                    tot_f += f
+                    tot_ms += ms
+                    gemm.append({"m": m, "k": k, "n": n, "ms": round(ms, 4), "tflops": round(f / ms / 1e9, 1),
+                                 "frac": round(f / ms / 1e9 / burst, 3)})
+        attn = []
+        for hd in (64, 128):
+            for S in (512, 1024, 4096):
+                ms = n3d.bench_attention(local, S, 8, hd, iters)
+                f = 4.0 * S * S * hd * 8
+                attn.append({"head_dim": hd, "seq": S, "ms": round(ms, 4), "tflops": round(f / ms / 1e9, 1),
+                             "frac": round(f / ms / 1e9 / burst, 3)})
+        ms_ln = n3d.bench_layer_norm(local, 16384, 1024, iters)
+    ln_gbs = 2 * 16384 * 1024 * 4 / ms_ln / 1e6
+    value = tot_f / tot_ms / 1e9
+    if rank == 0:
+        line = {"metric": "C1 kernel sweep: GEMM TFLOP/s over the 48 shapes", "value": value, "unit": "TFLOP/s",
+                "n_gpus": world, "steps": iters, "warmup": 3, "ms_per_step": tot_ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 (split GEMMs: TF32 hi*hi + 2 BF16 cross terms; 3xBF16 attention at head_dim 64)",
+                "data": "synthetic", "config": {"workload": "C1 kernel sweep (BASELINE config 1), each kernel alone",
+                                                "l2": "operands resident: shapes under 126 MB run L2-warm"},
+                "gemm_frac_of_burst_peak": value / burst,
+                "peak_source": f"{src} bf16 dense burst {burst} TFLOP/s, HBM {hbm} GB/s (MEASURED_PEAKS.json)",
+                "gemm": gemm, "attention": attn,
+                "layer_norm": {"rows": 16384, "cols": 1024, "ms": round(ms_ln, 4), "gbs": round(ln_gbs, 1),
+                               "frac": round(ln_gbs / hbm, 3), "bytes": "8 B per element (fp32 in, fp32 out)"},
+                "clocks": clk.summary()}
+        print(json.dumps(line), flush=True)
+
+
 def window_flops(cfg: dict, S: int, G: int) -> int:
     """Algorithmic FLOP of one chunk-loop window of S frames with G newly embedded ones:
     per layer 8h^2 + 4hI per frame (q, k, v, o, fc1, fc2) and 4hS per frame of
@@ -303,15 +418,19 @@ def main():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--workload", default="c4", choices=["c4", "c3", "c2"],
+    p.add_argument("--workload", default="c4", choices=["c4", "c3", "c2", "c1"],
                    help="c4: offline 60 s clips (headline); c3: ultra_low_latency streaming sessions; "
-                        "c2: one 60 min offline clip per GPU (sequential windows of one sequence)")
+                        "c2: one 60 min offline clip per GPU (sequential windows of one sequence); "
+                        "c1: the kernel sweep (GEMM, attention, LayerNorm shapes) as fractions of peak")
     p.add_argument("--mode", default="offline",
                    choices=["offline", "low_latency", "very_low_latency", "ultra_low_latency"],
                    help="c4 only: the mode every clip runs in (config 4 is run in each of the four)")
     p.add_argument("--clips", type=int, default=None, help="clips (c4) or sessions (c3) per GPU per step")
     p.add_argument("--session-seconds", type=float, default=600.0, help="c3 session length")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--streaming-sessions", type=int, default=32,
+                   help="c4 offline line: sessions per GPU of the streaming sub-record (0 skips it)")
+    p.add_argument("--streaming-seconds", type=float, default=120.0)
     args = p.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":
@@ -327,13 +446,20 @@ def main():
     import n3d
 
     torch.cuda.set_device(local)
+    if args.workload == "c1":
+        run_kernel_sweep(args, world, rank, local)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     ckpt = checkpoint(rank, world)
     if args.workload == "c4":
         mode, item_s, n_items = args.mode, CLIP_S, args.clips or 128
-        items = make_clips(rank, n_items, item_s)
+        items = make_clips(rank, n_items, item_s, world)
         metric = METRIC if mode == "offline" else f"C4 {mode} batch RTFx (audio-s/wall-s)"
         desc = (f"C4 {mode}: {n_items} x 60 s 16 kHz clips per GPU per step, random-init weights "
-                "(seed 0), clips seeded 1000+")
+                f"(seed 0), config 4 clips {item_seeds('c4', rank, n_items, world)[0]}.. of 8192 (seed 1000 + index)")
     elif args.workload == "c2":
         import synth
 
@@ -346,7 +472,7 @@ def main():
         import synth
 
         mode, item_s, n_items = "ultra_low_latency", args.session_seconds, args.clips or 32
-        items = [synth.config3_session(i, item_s) for i in item_seeds("c3", rank, n_items)]
+        items = [synth.config3_session(i, item_s) for i in item_seeds("c3", rank, n_items, world)]
         metric = "ultra_low_latency streaming RTFx (audio-s/wall-s); p50/p99 chunk-step latency"
         desc = (f"C3 ultra_low_latency: {n_items} concurrent {item_s:.0f} s sessions per GPU (seeds 100+), "
                 "3 scored encoder frames per step, random-init weights (seed 0)")
@@ -435,6 +561,13 @@ def main():
                 "what": f"host wall time of one n3d_sessions_push call handing 240 ms of new audio to each of "
                         f"{n_items} sessions (H2D, log-mel, embedder, one chunk step, D2H of the new rows)"}
 
+    streaming = None
+    if args.workload == "c4" and mode == "offline" and args.streaming_sessions > 0:
+        try:
+            streaming = streaming_leg(model, world, rank, args.streaming_sessions, args.streaming_seconds)
+        except Exception as e:  # never lose the headline line to the sub-record
+            streaming = {"error": f"{type(e).__name__}: {e}"[:300]}
+
     try:  # the whole step's algorithmic rate (host arithmetic over the planned schedule)
         step_flop = run_flops(ckpt, lens, mode)
         step_rate = {"flop_per_step_per_gpu": step_flop,
@@ -492,6 +625,7 @@ def main():
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             **({"live_sessions": live} if live else {}),
+            **({"streaming": streaming} if streaming else {}),
         }
         print(json.dumps(line), flush=True)
     model.close()

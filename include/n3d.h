@@ -3,7 +3,7 @@
  * forward pass.
  *
  * This is the `extern "C"` layer a Rust `Model` would bind with `extern "C"`
- * declarations (see INTEGRATION.md).  It replaces the reference crate's public
+ * declarations.  It replaces the reference crate's public
  * API (src/lib.rs:45-64) and its accelerator plug point
  * `Model.accel: Option<RefCell<GpuEngine>>` (src/model.rs:137-139):
  *
@@ -182,6 +182,38 @@ n3d_status n3d_head_forward(n3d_model *model, const float *encoder_out, size_t f
 /* GpuEngine::forward_window (src/gpu_engine.rs:1516-1520): tower + head on one window. */
 n3d_status n3d_forward_window(n3d_model *model, const float *embeds, size_t frames, size_t valid, float *logits);
 
+/* CacheConfig (src/streaming.rs:39-52): the speaker-cache policy, as
+ * CacheConfig::from_model resolves it (src/streaming.rs:54-76). */
+typedef struct n3d_cache_config {
+    size_t fifo_length;
+    size_t speaker_cache_length;
+    size_t update_period;
+    size_t num_silence_frames;
+    float score_threshold;
+    float latest_frames_score_boost;
+    size_t num_speakers;
+    size_t subsampling_factor;
+    size_t min_positive_scores;
+    size_t num_strong_boosted_frames;
+    size_t num_weak_boosted_frames;
+} n3d_cache_config;
+
+/* SpeakerCache::trace_compress / compress (src/streaming.rs:353-482) on device
+ * `device`, through the same selection and gather code the chunk loop's cache kernel
+ * runs.  `probs` [frames, num_speakers] are the candidate frames' probabilities.
+ * picked (room for speaker_cache_length entries) receives trace_compress's `picked`:
+ * the first L = min(speaker_cache_length, num_speakers * (frames + num_silence_frames))
+ * flat speaker-major indices in (score desc, index asc) order, -inf picks replaced by
+ * *sentinel = num_speakers * (frames + num_silence_frames), sorted ascending; *count = L.
+ * When `embeds` [frames, hidden] is not NULL, out_embeds [L, hidden] and out_probs
+ * [L, num_speakers] receive compress()'s result: each pick's row and probabilities,
+ * `silence` [hidden] and a zero row for silence slots and sentinels.  Host pointers.
+ * 1 <= frames, num_speakers <= 16, hidden % 4 == 0, and the working set must fit one
+ * CTA's shared memory (8 speakers: about 1500 frames). */
+n3d_status n3d_cache_compress(int device, const n3d_cache_config *cfg, const float *probs, size_t frames,
+                              const float *embeds, size_t hidden, const float *silence, size_t *picked,
+                              size_t *sentinel, size_t *count, float *out_embeds, float *out_probs);
+
 /* ------------------------------------------------------------ segments */
 
 /* extract_speaker_dict (src/segments.rs:70-109).  `mask` may be NULL. */
@@ -295,6 +327,20 @@ n3d_status n3d_layer_norm(int device, const float *d_x, size_t rows, size_t cols
  * q, k, v, out of shape [seq, heads * head_dim]; head_dim 64 or 128. */
 n3d_status n3d_attention(int device, const float *d_q, const float *d_k, const float *d_v, size_t seq,
                          size_t heads, size_t head_dim, size_t valid, int rope, double rope_theta, float *d_out);
+
+/* Probe benchmarks: GpuEngine::bench_gemm (src/gpu_engine.rs:562-596) and the
+ * GEMM_BENCH / ATTN_BENCH / STAGE_BENCH probes (src/bin/gpu_check.rs:132-289), for
+ * the kernels above.  Each sets up synthetic operands in the kernel's own device
+ * layout (n3d_linear's split operands, the attention's packed operands), launches the
+ * kernel 3 times untimed, then `iters` times between two CUDA events on the library's
+ * stream of `device`, and returns the mean device time of one launch in *ms.  The
+ * operands stay resident, so shapes smaller than the 126 MB L2 run L2-warm.
+ * n3d_bench_linear times n3d_linear's GEMM (output [rows, out] fp32 with a bias);
+ * n3d_bench_attention the attention over all `seq` keys (no RoPE); n3d_bench_layer_norm
+ * n3d_layer_norm. */
+n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, int iters, double *ms);
+n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head_dim, int iters, double *ms);
+n3d_status n3d_bench_layer_norm(int device, size_t rows, size_t cols, int iters, double *ms);
 
 /* ------------------------------------------------------------- profiling */
 

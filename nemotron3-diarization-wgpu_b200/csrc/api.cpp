@@ -664,4 +664,195 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
     });
 }
 
+n3d_status n3d_cache_compress(int device, const n3d_cache_config* cfg, const float* probs, size_t frames,
+                              const float* embeds, size_t hidden, const float* silence, size_t* picked,
+                              size_t* sentinel, size_t* count, float* out_embeds, float* out_probs) {
+    return guarded([&] {
+        arg_check(cfg && probs && picked && sentinel && count, "n3d_cache_compress: null argument");
+        arg_check(!embeds || (silence && out_embeds && out_probs), "n3d_cache_compress: null gather argument");
+        arg_check(frames >= 1 && frames <= 65536, "n3d_cache_compress: frames outside 1..65536");
+        arg_check(cfg->num_speakers >= 1 && cfg->num_speakers <= 16, "n3d_cache_compress: num_speakers outside 1..16");
+        arg_check(cfg->num_silence_frames <= 65536 && cfg->speaker_cache_length <= (size_t)INT_MAX &&
+                      cfg->min_positive_scores <= (size_t)INT_MAX && cfg->num_strong_boosted_frames <= (size_t)INT_MAX &&
+                      cfg->num_weak_boosted_frames <= (size_t)INT_MAX,
+                  "n3d_cache_compress: cache sizes beyond 2^31");
+        arg_check(!embeds || (hidden >= 4 && hidden % 4 == 0 && hidden <= 65536),
+                  "n3d_cache_compress: hidden must be a positive multiple of 4");
+        const int ne = (int)frames, ns = (int)cfg->num_speakers, n_sil = (int)cfg->num_silence_frames;
+        if (n3d::cache_compress_smem(ne, ns, n_sil) > 227 * 1024)
+            throw n3d::Error(N3D_ERR_INVALID_ARGUMENT, "n3d_cache_compress: frames * speakers too large for one CTA");
+        const n3d::CacheConst cc{embeds ? (int)hidden : 0, ns, (int)cfg->subsampling_factor,
+                                 (int)cfg->speaker_cache_length, n_sil, (int)cfg->min_positive_scores,
+                                 (int)cfg->num_strong_boosted_frames, (int)cfg->num_weak_boosted_frames,
+                                 cfg->score_threshold, cfg->latest_frames_score_boost};
+        const size_t total = (size_t)ns * (frames + (size_t)n_sil);
+        const size_t L = std::min(cfg->speaker_cache_length, total);
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
+        DevScratch sc;
+        float* d_probs = sc.get(frames * ns);
+        int* d_picked = (int*)sc.get(L);
+        int* d_counts = (int*)sc.get(2);
+        float *d_rows = nullptr, *d_sil = nullptr, *d_oe = nullptr, *d_op = nullptr;
+        N3D_CUDA(cudaMemcpyAsync(d_probs, probs, frames * ns * 4, cudaMemcpyHostToDevice, k.stream));
+        if (embeds) {
+            d_rows = sc.get(frames * hidden);
+            d_sil = sc.get(hidden);
+            d_oe = sc.get(L * hidden);
+            d_op = sc.get(L * ns);
+            N3D_CUDA(cudaMemcpyAsync(d_rows, embeds, frames * hidden * 4, cudaMemcpyHostToDevice, k.stream));
+            N3D_CUDA(cudaMemcpyAsync(d_sil, silence, hidden * 4, cudaMemcpyHostToDevice, k.stream));
+        }
+        n3d::launch_cache_compress(k.stream, d_probs, ne, d_rows, d_sil, cc, d_picked, d_counts, d_oe, d_op);
+        kcheck(k);
+        int counts[2] = {0, 0};
+        N3D_CUDA(cudaMemcpy(counts, d_counts, sizeof(counts), cudaMemcpyDeviceToHost));
+        const size_t n_real = (size_t)counts[0];
+        if ((size_t)counts[1] != L || n_real > L) throw n3d::Error(N3D_ERR_GPU, "n3d_cache_compress: bad pick count");
+        std::vector<int> got(n_real);
+        if (n_real) N3D_CUDA(cudaMemcpy(got.data(), d_picked, n_real * 4, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < n_real; i++) picked[i] = (size_t)got[i];
+        for (size_t i = n_real; i < L; i++) picked[i] = total;  // the -inf picks, remapped and sorted last
+        *sentinel = total;
+        *count = L;
+        if (embeds) {
+            N3D_CUDA(cudaMemcpy(out_embeds, d_oe, L * hidden * 4, cudaMemcpyDeviceToHost));
+            N3D_CUDA(cudaMemcpy(out_probs, d_op, L * ns * 4, cudaMemcpyDeviceToHost));
+        }
+    });
+}
+
+}  // extern "C"
+
+namespace {
+
+// Times `launch` (3 untimed calls, then `iters` between two events on k's stream).
+template <class F>
+double time_launches(KernelCtx& k, int iters, F&& launch) {
+    for (int i = 0; i < 3; i++) launch();
+    cudaEvent_t e0, e1;
+    N3D_CUDA(cudaEventCreate(&e0));
+    N3D_CUDA(cudaEventCreate(&e1));
+    N3D_CUDA(cudaEventRecord(e0, k.stream));
+    for (int i = 0; i < iters; i++) launch();
+    N3D_CUDA(cudaEventRecord(e1, k.stream));
+    kcheck(k);
+    float ms = 0.0f;
+    N3D_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return (double)ms / iters;
+}
+
+}  // namespace
+
+extern "C" {
+
+n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, int iters, double* ms) {
+    return guarded([&] {
+        arg_check(ms != nullptr && iters >= 1, "n3d_bench_linear: null ms or iters < 1");
+        arg_check(cols % 32 == 0 && cols > 0 && rows > 0 && out > 0, "n3d_bench_linear: cols must be a positive "
+                                                                     "multiple of 32, rows and out positive");
+        arg_check(rows <= (size_t)INT_MAX && cols <= (size_t)INT_MAX && out <= (size_t)INT_MAX &&
+                      rows * cols <= ((size_t)1 << 33) && out * cols <= ((size_t)1 << 33) &&
+                      rows * out <= ((size_t)1 << 33),
+                  "n3d_bench_linear: sizes beyond 2^31 or operands beyond 2^33 elements");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
+        DevScratch sc;
+        float* x = sc.get(rows * cols);
+        float* w = sc.get(out * cols);
+        float* bias = sc.get(out);
+        float* y = sc.get(rows * out);
+        n3d::launch_fill_random(k.stream, x, (long long)(rows * cols), 1, 1.0f);
+        n3d::launch_fill_random(k.stream, w, (long long)(out * cols), 2, 1.0f / std::sqrt((float)cols));
+        n3d::launch_fill_random(k.stream, bias, (long long)out, 3, 1.0f);
+        const n3d::Split3Out xs{sc.get(rows * cols), sc.get(rows * cols / 2), sc.get(rows * cols / 2)};
+        const n3d::Split3Out ws{sc.get(out * cols), sc.get(out * cols / 2), sc.get(out * cols / 2)};
+        n3d::launch_split(k.stream, x, (long long)(rows * cols), xs);
+        n3d::launch_split(k.stream, w, (long long)(out * cols), ws);
+        n3d::Epi e;
+        e.mode = n3d::EPI_STORE;
+        e.bias = bias;
+        e.out = y;
+        e.ldo = (long long)out;
+        *ms = time_launches(k, iters, [&] {
+            n3d::gemm_split3(k.stream, n3d::SplitOperand{xs.hi, xs.hb, xs.lb, (long long)rows, (long long)cols, (long long)cols},
+                             n3d::SplitOperand{ws.hi, ws.hb, ws.lb, (long long)out, (long long)cols, (long long)cols},
+                             (int)rows, (int)out, (int)cols, 0, e, k.err);
+        });
+    });
+}
+
+n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head_dim, int iters, double* ms) {
+    return guarded([&] {
+        arg_check(ms != nullptr && iters >= 1, "n3d_bench_attention: null ms or iters < 1");
+        arg_check(head_dim == 64 || head_dim == 128, "n3d_bench_attention: head_dim must be 64 or 128");
+        arg_check(seq >= 1 && seq <= 65536 && heads >= 1 && heads <= 64,
+                  "n3d_bench_attention: seq outside 1..65536 or heads outside 1..64");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
+        DevScratch sc;
+        const size_t W = heads * head_dim;
+        float* q = sc.get(seq * W);
+        float* kk = sc.get(seq * W);
+        float* v = sc.get(seq * W);
+        float* ctx = sc.get(seq * W);
+        n3d::launch_fill_random(k.stream, q, (long long)(seq * W), 4, 1.0f);
+        n3d::launch_fill_random(k.stream, kk, (long long)(seq * W), 5, 1.0f);
+        n3d::launch_fill_random(k.stream, v, (long long)(seq * W), 6, 1.0f);
+        int vv = (int)seq;
+        int* dv = (int*)sc.get(1);
+        N3D_CUDA(cudaMemcpyAsync(dv, &vv, 4, cudaMemcpyHostToDevice, k.stream));
+        if (head_dim == 64) {
+            const size_t vt_ld = (seq + 7) / 8 * 8;
+            n3d::AttnOperands op;
+            op.q_hi = sc.get(seq * W / 2);
+            op.q_lo = sc.get(seq * W / 2);
+            op.k_hi = sc.get(seq * W / 2);
+            op.k_lo = sc.get(seq * W / 2);
+            op.rows_cap = (long long)seq;
+            op.vt_hi = sc.get(W * vt_ld / 2);
+            op.vt_lo = sc.get(W * vt_ld / 2);
+            op.vt_ld = (long long)vt_ld;
+            n3d::launch_pack_attn(k.stream, q, kk, v, (long long)seq, (int)heads, nullptr, nullptr, op);
+            *ms = time_launches(k, iters, [&] {
+                n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::Split3Out{ctx, nullptr, nullptr},
+                                         k.err);
+            });
+        } else {
+            float* qkv = sc.get(seq * 3 * W);
+            n3d::launch_pack_qkv(k.stream, q, kk, v, (long long)seq, (int)heads, (int)head_dim, nullptr, nullptr, qkv);
+            *ms = time_launches(k, iters, [&] {
+                n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, ctx);
+            });
+        }
+    });
+}
+
+n3d_status n3d_bench_layer_norm(int device, size_t rows, size_t cols, int iters, double* ms) {
+    return guarded([&] {
+        arg_check(ms != nullptr && iters >= 1, "n3d_bench_layer_norm: null ms or iters < 1");
+        arg_check(cols == 512 || cols == 1024, "n3d_bench_layer_norm: cols must be 512 or 1024");
+        arg_check(rows >= 1 && rows <= ((size_t)1 << 24), "n3d_bench_layer_norm: rows outside 1..2^24");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
+        DevScratch sc;
+        float* x = sc.get(rows * cols);
+        float* y = sc.get(rows * cols);
+        float* w = sc.get(cols);
+        float* b = sc.get(cols);
+        n3d::launch_fill_random(k.stream, x, (long long)(rows * cols), 7, 3.0f);
+        n3d::launch_fill_random(k.stream, w, (long long)cols, 8, 1.0f);
+        n3d::launch_fill_random(k.stream, b, (long long)cols, 9, 0.1f);
+        *ms = time_launches(k, iters, [&] {
+            n3d::launch_layer_norm(k.stream, x, (long long)rows, (int)cols, w, b, n3d::Split3Out{y, nullptr, nullptr});
+        });
+    });
+}
+
 }  // extern "C"

@@ -54,94 +54,21 @@ __device__ __forceinline__ uint32_t order_key(float v) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-struct CacheParams {
-    int hidden, ns, sub, cache_len, n_sil, min_pos, k_strong, k_weak;
-    float thr, latest_boost;
-};
-
-// One CTA per sequence.  Shared layout (floats unless noted):
-//   probs [S*ns]      pooled step probabilities (_pool_probs)
-//   cand  [ne*ns]     probabilities of the compression candidates
-//   sc    [ne*ns]     frame scores
-//   key   [P] (uint)  order keys of the flat speaker-major scores (P >= ns*(ne+n_sil))
-//   idx   [P] (int)   the picked flat indices, ascending
-//   aux   [P] (int)   selection flags
+// _compress's ranking (src/streaming.rs:410-463) of `ne` candidate frames whose
+// probabilities are cand[ne * ns]: frame scores (into sc), the latest-frames boost,
+// the strong and weak per-speaker top-k boosts, then the flat speaker-major pick of
+// the first L = min(cache_len, ns * (ne + n_sil)) in (score desc, flat index asc)
+// order.  Leaves the picked flat indices ascending in idx[0, n_real) -- the -inf
+// picks are dropped, they become the sentinel -- and returns n_real in every thread,
+// with L in *L_out.  Every thread of the block calls it (it synchronises).
 // "The first k in (score descending, index ascending) order" -- Rust's stable sort
 // followed by a truncation -- is computed as a selection: an MSB-first radix select
 // of the k-th key, then the elements above it plus the lowest-index ties.
-__global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __restrict__ steps,
-                                                           const float* __restrict__ win,
-                                                           const float* __restrict__ logits, int stride,
-                                                           long long logit_rows, CacheParams cp,
-                                                           const float* __restrict__ silence, int P_max) {
-    griddep_wait();
-    griddep_launch_dependents();
-    extern __shared__ float sm[];
-    const int i = blockIdx.x;
-    const SeqStep st = steps[i];
-    const int ns = cp.ns, sub = cp.sub, hidden = cp.hidden;
-    const int S = st.S;
+__device__ int compress_select(const float* __restrict__ cand, float* __restrict__ sc, uint32_t* __restrict__ fkey,
+                               int* __restrict__ idx, int* __restrict__ aux, int ne, const CacheConst& cp,
+                               int* L_out) {
+    const int ns = cp.ns;
     const int tid = threadIdx.x, nt = blockDim.x;
-    const float* wrow = win + (long long)i * stride * hidden;
-    const float* lrow = logits + (long long)i * logit_rows * ns;  // head output keeps 2 pad rows per sequence
-
-    float* probs = sm;
-    float* cand = probs + stride * ns;
-    float* sc = cand + stride * ns;
-    float* key = sc + stride * ns;
-    int* idx = reinterpret_cast<int*>(key + P_max);
-    int* aux = idx + P_max;
-
-    // ---- _pool_probs (src/streaming.rs:202-217): sigmoid averaged over sub-frames, mask after
-    for (int e = tid; e < S * ns; e += nt) {
-        const int g = e / ns, c = e % ns;
-        float acc = 0.0f;
-        for (int k = 0; k < sub; k++) {
-            const float l = lrow[((long long)g * sub + k) * ns + c];
-            acc = __fadd_rn(acc, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f(-l))));
-        }
-        probs[e] = g < st.valid ? __fdiv_rn(acc, (float)sub) : 0.0f;
-    }
-    // ---- scored logit rows [cached*sub, (cached+nchunk)*sub), capped (src/model.rs:455-461)
-    {
-        const long long s0 = (long long)(st.ncache + st.nfifo) * sub * ns;
-        const long long n = (long long)st.keep_rows * ns;
-        for (long long e = tid; e < n; e += nt) st.out_logits[e] = lrow[s0 + e];
-    }
-    __syncthreads();
-
-    const int ne = st.ncache + st.popped;
-    // ---- candidates' probabilities: stored (compressed cache) or this step's, then popped FIFO frames
-    for (int e = tid; e < ne * ns; e += nt) {
-        const int f = e / ns;
-        cand[e] = (f < st.ncache && st.was_compressed) ? st.cp_in[e] : probs[e];
-    }
-    __syncthreads();
-
-    // ---- new FIFO: window rows [ncache + popped, ncache + nfifo + nchunk)
-    const int cf_new = st.popped > 0 ? (st.compress ? cp.cache_len : ne) : st.ncache;
-    const int ff_new = st.nfifo + st.nchunk - st.popped;
-    for (long long e = tid; e < (long long)ff_new * (hidden / 4); e += nt) {
-        const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
-        reinterpret_cast<float4*>(st.pre_out + (long long)(cf_new + r) * hidden)[c] =
-            reinterpret_cast<const float4*>(wrow + (long long)(st.ncache + st.popped + r) * hidden)[c];
-    }
-
-    if (!st.compress) {
-        // cache rows = window rows [0, cf_new); stored probs follow them
-        for (long long e = tid; e < (long long)cf_new * (hidden / 4); e += nt) {
-            const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
-            reinterpret_cast<float4*>(st.pre_out + (long long)r * hidden)[c] =
-                reinterpret_cast<const float4*>(wrow + (long long)r * hidden)[c];
-        }
-        if (st.popped > 0)
-            for (int e = tid; e < ne * ns; e += nt) st.cp_out[e] = cand[e];
-        else if (st.was_compressed)
-            for (int e = tid; e < st.ncache * ns; e += nt) st.cp_out[e] = st.cp_in[e];
-        return;
-    }
-
-    // ================= _compress (src/streaming.rs:410-482) =================
     // ---- _get_frame_scores (src/streaming.rs:294-330)
     for (int f = tid; f < ne; f += nt) {
         const float* row = cand + f * ns;
@@ -214,7 +141,6 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
     const int nsc = ne + cp.n_sil;
     const int total = ns * nsc;
     const int L = min(cp.cache_len, total);
-    uint32_t* fkey = reinterpret_cast<uint32_t*>(key);
     for (int e = tid; e < total; e += nt) {
         const int sp = e / nsc, f = e % nsc;
         fkey[e] = order_key(f < ne ? sc[f * ns + sp] : INFINITY);
@@ -286,8 +212,18 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
         if (tid == nt - 1) carry = pos + flag;
         __syncthreads();
     }
-    const int n_real = carry;
-    // ---- gather (src/streaming.rs:464-481): silence rows are silence_embeds with zero probs
+    *L_out = L;
+    return carry;
+}
+
+// The gather of src/streaming.rs:464-481: output row p is candidate frame
+// idx[p] % nsc for p < n_real and that slot is a frame; silence slots and the
+// sentinels get `silence` and a zero probability row.
+__device__ void compress_gather(const int* __restrict__ idx, int n_real, int L, int ne, int nsc,
+                                const float* __restrict__ rows, const float* __restrict__ cand,
+                                const float* __restrict__ silence, int hidden, int ns, float* __restrict__ out_rows,
+                                float* __restrict__ out_probs) {
+    const int tid = threadIdx.x, nt = blockDim.x;
     for (long long e = tid; e < (long long)L * (hidden / 4); e += nt) {
         const int p = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
         int frame = ne;
@@ -295,9 +231,9 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
             const int f = idx[p] % nsc;
             frame = f < ne ? f : ne;
         }
-        const float4* src = frame < ne ? reinterpret_cast<const float4*>(wrow + (long long)frame * hidden)
+        const float4* src = frame < ne ? reinterpret_cast<const float4*>(rows + (long long)frame * hidden)
                                        : reinterpret_cast<const float4*>(silence);
-        reinterpret_cast<float4*>(st.pre_out + (long long)p * hidden)[c] = src[c];
+        reinterpret_cast<float4*>(out_rows + (long long)p * hidden)[c] = src[c];
     }
     for (int e = tid; e < L * ns; e += nt) {
         const int p = e / ns, s = e % ns;
@@ -306,8 +242,122 @@ __global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __rest
             const int f = idx[p] % nsc;
             frame = f < ne ? f : ne;
         }
-        st.cp_out[e] = frame < ne ? cand[frame * ns + s] : 0.0f;
+        out_probs[e] = frame < ne ? cand[frame * ns + s] : 0.0f;
     }
+}
+
+// One CTA per sequence.  Shared layout (floats unless noted):
+//   probs [S*ns]      pooled step probabilities (_pool_probs)
+//   cand  [ne*ns]     probabilities of the compression candidates
+//   sc    [ne*ns]     frame scores
+//   key   [P] (uint)  order keys of the flat speaker-major scores (P >= ns*(ne+n_sil))
+//   idx   [P] (int)   the picked flat indices, ascending
+//   aux   [P] (int)   selection flags
+__global__ void __launch_bounds__(512) cache_update_kernel(const SeqStep* __restrict__ steps,
+                                                           const float* __restrict__ win,
+                                                           const float* __restrict__ logits, int stride,
+                                                           long long logit_rows, CacheConst cp,
+                                                           const float* __restrict__ silence, int P_max) {
+    griddep_wait();
+    griddep_launch_dependents();
+    extern __shared__ float sm[];
+    const int i = blockIdx.x;
+    const SeqStep st = steps[i];
+    const int ns = cp.ns, sub = cp.sub, hidden = cp.hidden;
+    const int S = st.S;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    const float* wrow = win + (long long)i * stride * hidden;
+    const float* lrow = logits + (long long)i * logit_rows * ns;  // head output keeps 2 pad rows per sequence
+
+    float* probs = sm;
+    float* cand = probs + stride * ns;
+    float* sc = cand + stride * ns;
+    float* key = sc + stride * ns;
+    int* idx = reinterpret_cast<int*>(key + P_max);
+    int* aux = idx + P_max;
+
+    // ---- _pool_probs (src/streaming.rs:202-217): sigmoid averaged over sub-frames, mask after
+    for (int e = tid; e < S * ns; e += nt) {
+        const int g = e / ns, c = e % ns;
+        float acc = 0.0f;
+        for (int k = 0; k < sub; k++) {
+            const float l = lrow[((long long)g * sub + k) * ns + c];
+            acc = __fadd_rn(acc, __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f(-l))));
+        }
+        probs[e] = g < st.valid ? __fdiv_rn(acc, (float)sub) : 0.0f;
+    }
+    // ---- scored logit rows [cached*sub, (cached+nchunk)*sub), capped (src/model.rs:455-461)
+    {
+        const long long s0 = (long long)(st.ncache + st.nfifo) * sub * ns;
+        const long long n = (long long)st.keep_rows * ns;
+        for (long long e = tid; e < n; e += nt) st.out_logits[e] = lrow[s0 + e];
+    }
+    __syncthreads();
+
+    const int ne = st.ncache + st.popped;
+    // ---- candidates' probabilities: stored (compressed cache) or this step's, then popped FIFO frames
+    for (int e = tid; e < ne * ns; e += nt) {
+        const int f = e / ns;
+        cand[e] = (f < st.ncache && st.was_compressed) ? st.cp_in[e] : probs[e];
+    }
+    __syncthreads();
+
+    // ---- new FIFO: window rows [ncache + popped, ncache + nfifo + nchunk)
+    const int cf_new = st.popped > 0 ? (st.compress ? cp.cache_len : ne) : st.ncache;
+    const int ff_new = st.nfifo + st.nchunk - st.popped;
+    for (long long e = tid; e < (long long)ff_new * (hidden / 4); e += nt) {
+        const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
+        reinterpret_cast<float4*>(st.pre_out + (long long)(cf_new + r) * hidden)[c] =
+            reinterpret_cast<const float4*>(wrow + (long long)(st.ncache + st.popped + r) * hidden)[c];
+    }
+
+    if (!st.compress) {
+        // cache rows = window rows [0, cf_new); stored probs follow them
+        for (long long e = tid; e < (long long)cf_new * (hidden / 4); e += nt) {
+            const int r = (int)(e / (hidden / 4)), c = (int)(e % (hidden / 4));
+            reinterpret_cast<float4*>(st.pre_out + (long long)r * hidden)[c] =
+                reinterpret_cast<const float4*>(wrow + (long long)r * hidden)[c];
+        }
+        if (st.popped > 0)
+            for (int e = tid; e < ne * ns; e += nt) st.cp_out[e] = cand[e];
+        else if (st.was_compressed)
+            for (int e = tid; e < st.ncache * ns; e += nt) st.cp_out[e] = st.cp_in[e];
+        return;
+    }
+
+    // ================= _compress (src/streaming.rs:410-482) =================
+    int L = 0;
+    const int n_real = compress_select(cand, sc, reinterpret_cast<uint32_t*>(key), idx, aux, ne, cp, &L);
+    compress_gather(idx, n_real, L, ne, ne + cp.n_sil, wrow, cand, silence, hidden, ns, st.pre_out, st.cp_out);
+}
+
+// SpeakerCache::compress / trace_compress (src/streaming.rs:353-482) alone, for the
+// stage entry point: one CTA runs compress_select and compress_gather -- the code the
+// chunk loop's cache_update_kernel runs -- on `ne` given candidate frames.  Shared
+// layout as cache_update_kernel's: cand [ne*ns], sc [ne*ns], key/idx/aux [P_max].
+__global__ void __launch_bounds__(512) cache_compress_kernel(const float* __restrict__ probs, int ne,
+                                                             const float* __restrict__ rows,
+                                                             const float* __restrict__ silence, CacheConst cp,
+                                                             int P_max, int* __restrict__ picked,
+                                                             int* __restrict__ counts, float* __restrict__ out_rows,
+                                                             float* __restrict__ out_probs) {
+    extern __shared__ float sm[];
+    const int ns = cp.ns;
+    float* cand = sm;
+    float* sc = cand + ne * ns;
+    float* key = sc + ne * ns;
+    int* idx = reinterpret_cast<int*>(key + P_max);
+    int* aux = idx + P_max;
+    for (int e = threadIdx.x; e < ne * ns; e += blockDim.x) cand[e] = probs[e];
+    __syncthreads();
+    int L = 0;
+    const int n_real = compress_select(cand, sc, reinterpret_cast<uint32_t*>(key), idx, aux, ne, cp, &L);
+    for (int p = threadIdx.x; p < n_real; p += blockDim.x) picked[p] = idx[p];
+    if (threadIdx.x == 0) {
+        counts[0] = n_real;
+        counts[1] = L;
+    }
+    if (rows) compress_gather(idx, n_real, L, ne, ne + cp.n_sil, rows, cand, silence, cp.hidden, ns, out_rows, out_probs);
 }
 
 }  // namespace
@@ -339,10 +389,22 @@ void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const f
             attr[dev] = smem;
         }
     }
-    CacheParams cp{c.hidden, c.ns, c.sub, c.cache_len, c.n_sil, c.min_pos, c.k_strong, c.k_weak, c.thr,
-                   c.latest_boost};
     launch_pdl(cache_update_kernel, dim3(nseq), dim3(512), smem, s, steps, win, logits, stride,
-               (long long)(stride + 2) * c.sub, cp, silence, P);
+               (long long)(stride + 2) * c.sub, c, silence, P);
+}
+
+size_t cache_compress_smem(int ne, int ns, int n_sil) {
+    const long long P = ((long long)ns * (ne + n_sil) + 3) / 4 * 4;
+    return (size_t)2 * ne * ns * 4 + (size_t)P * 4 * 3;
+}
+
+void launch_cache_compress(cudaStream_t s, const float* probs, int ne, const float* rows, const float* silence,
+                           const CacheConst& c, int* picked, int* counts, float* out_rows, float* out_probs) {
+    const int P = (c.ns * (ne + c.n_sil) + 3) / 4 * 4;
+    const size_t smem = cache_compress_smem(ne, c.ns, c.n_sil);
+    N3D_CUDA(cudaFuncSetAttribute(cache_compress_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cache_compress_kernel<<<1, 512, smem, s>>>(probs, ne, rows, silence, c, P, picked, counts, out_rows, out_probs);
+    N3D_CUDA(cudaGetLastError());
 }
 
 }  // namespace n3d

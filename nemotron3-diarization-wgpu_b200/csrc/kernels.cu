@@ -394,6 +394,24 @@ __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __res
     }
 }
 
+// Synthetic operands for the probe benchmarks: x[i] = scale * (sum of 4 uniforms in
+// [-1, 1) from a hash of (seed, i)), roughly N(0, scale^2 * 4/3).
+__global__ void fill_random_kernel(float* __restrict__ p, long long n, uint32_t seed, float scale) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        uint32_t h = (uint32_t)i * 2654435761u ^ (uint32_t)(i >> 32) * 40503u ^ seed * 2246822519u;
+        float acc = 0.0f;
+        for (int k = 0; k < 4; k++) {
+            h ^= h >> 15;
+            h *= 0x2c1b3c6du;
+            h ^= h >> 12;
+            h *= 0x297a2d39u;
+            h ^= h >> 15;
+            acc += (float)(h >> 8) * (1.0f / 8388608.0f) - 1.0f;
+        }
+        p[i] = acc * scale;
+    }
+}
+
 }  // namespace
 
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
@@ -460,6 +478,13 @@ void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int n
     const long long blocks = (n_frames + MEL_WARPS - 1) / MEL_WARPS;
     mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, segs, nsegs, f_first, n_frames, hop, window, twiddle,
                                                             filters, filt_lo, filt_hi, preemph, mel, mel_plain);
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_fill_random(cudaStream_t s, float* p, long long n, uint32_t seed, float scale) {
+    if (n <= 0) return;
+    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
+    fill_random_kernel<<<(unsigned)blocks, 256, 0, s>>>(p, n, seed, scale);
     N3D_CUDA(cudaGetLastError());
 }
 

@@ -38,5 +38,14 @@ void launch_assemble(cudaStream_t s, const SeqStep* steps, int nseq, const float
                      int hidden);
 void launch_cache_update(cudaStream_t s, const SeqStep* steps, int nseq, const float* win, const float* logits,
                          int stride, const CacheConst& c, const float* silence);
+// SpeakerCache::compress alone (one CTA, the selection and gather code of
+// cache_update_kernel): probs [ne, ns]; rows [ne, hidden] and silence [hidden], or
+// rows == nullptr for the ranking only.  Writes the n_real picked flat indices
+// (ascending, -inf picks dropped) to picked, counts[0] = n_real, counts[1] = L =
+// min(cache_len, ns * (ne + n_sil)), and the gathered [L, hidden] rows and [L, ns]
+// probabilities.  cache_compress_smem() is its shared memory (at most 227 KB).
+size_t cache_compress_smem(int ne, int ns, int n_sil);
+void launch_cache_compress(cudaStream_t s, const float* probs, int ne, const float* rows, const float* silence,
+                           const CacheConst& c, int* picked, int* counts, float* out_rows, float* out_probs);
 
 }  // namespace n3d

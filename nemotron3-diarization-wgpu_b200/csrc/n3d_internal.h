@@ -195,6 +195,8 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
 // q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
                       const float* cos_t, const float* sin_t, const AttnOperands& op);
+// Synthetic benchmark operands: p[i] ~ scale * (sum of 4 hashed uniforms in [-1, 1)).
+void launch_fill_random(cudaStream_t s, float* p, long long n, uint32_t seed, float scale);
 // tensor::linear without any allocation: scratch is a fixed device array (noalloc.cu).
 void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
                     const float* d_bias, float* d_y, cudaStream_t stream);

@@ -24,6 +24,7 @@
 //    address of the array (which also loads the library's GPU code onto that
 //    device).  Make that first call before any stream capture.
 
+#include <climits>
 #include <mutex>
 
 #include "n3d_device.cuh"
@@ -95,12 +96,17 @@ void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, cons
                     const float* d_bias, float* d_y, cudaStream_t stream) {
     if (!d_x || !d_w || !d_y) throw Error(13, "n3d_linear_noalloc: null argument");
     if (cols == 0 || cols % 32) throw Error(13, "n3d_linear_noalloc: cols must be a positive multiple of 32");
+    // the same limits as n3d_linear: the kernels count rows, columns and outputs in int
+    if (rows > (size_t)INT_MAX || cols > (size_t)INT_MAX || out > (size_t)INT_MAX)
+        throw Error(13, "n3d_linear_noalloc: sizes beyond 2^31");
     if (rows == 0 || out == 0) return;
-    const size_t need = 2 * round64(rows * cols) + 2 * round64(out * cols);  // hi + hb + lb per operand
-    if (need > kScratchFloats)
-        throw Error(13, "n3d_linear_noalloc: request needs " + std::to_string(need) +
-                            " scratch floats; the fixed scratch holds " + std::to_string(kScratchFloats) +
-                            " (rows*cols + out*cols must stay within about 2097152)");
+    // each operand on its own first (rows * cols < 2^62 cannot wrap), so the sum below cannot wrap either
+    const bool fits = rows * cols <= kScratchFloats && out * cols <= kScratchFloats;
+    const size_t need = fits ? 2 * round64(rows * cols) + 2 * round64(out * cols) : 0;  // hi + hb + lb per operand
+    if (!fits || need > kScratchFloats)
+        throw Error(13, "n3d_linear_noalloc: the request needs more scratch than the fixed " +
+                            std::to_string(kScratchFloats) +
+                            " floats (rows*cols + out*cols must stay within about 2097152)");
     N3D_CUDA(cudaSetDevice(device));
     const DeviceSymbols sym = symbols_for(device);
     const Carve x = carve(sym.scratch, rows * cols);
@@ -117,9 +123,11 @@ void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, cons
     gemm_split3_stack_maps(stream, SplitOperand{x.hi, x.hb, x.lb, (long long)rows, (long long)cols, (long long)cols},
                            SplitOperand{w.hi, w.hb, w.lb, (long long)out, (long long)cols, (long long)cols},
                            (int)rows, (int)out, (int)cols, e, sym.status);
-    N3D_CUDA(cudaStreamSynchronize(stream));
+    // read the status word back on the caller's stream only (one plain copy), so the call
+    // waits for its own work and not for other streams of the device
     int status = 0;
-    N3D_CUDA(cudaMemcpy(&status, sym.status, sizeof(int), cudaMemcpyDeviceToHost));
+    N3D_CUDA(cudaMemcpyAsync(&status, sym.status, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    N3D_CUDA(cudaStreamSynchronize(stream));
     if (status) throw Error(11, "n3d_linear_noalloc: a device-side wait timed out (site " + std::to_string(status) + ")");
 }
 

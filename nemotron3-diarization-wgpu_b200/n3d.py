@@ -69,6 +69,14 @@ class _StepPlan(C.Structure):
                 ("cache_frames", _sz), ("fifo_frames", _sz), ("cache_compressed", C.c_int)]
 
 
+class CacheConfig(C.Structure):
+    """CacheConfig (src/streaming.rs:39-52), as n3d_cache_config."""
+    _fields_ = [("fifo_length", _sz), ("speaker_cache_length", _sz), ("update_period", _sz),
+                ("num_silence_frames", _sz), ("score_threshold", C.c_float), ("latest_frames_score_boost", C.c_float),
+                ("num_speakers", _sz), ("subsampling_factor", _sz), ("min_positive_scores", _sz),
+                ("num_strong_boosted_frames", _sz), ("num_weak_boosted_frames", _sz)]
+
+
 class _KernelStats(C.Structure):
     _fields_ = [("name", C.c_char_p), ("launches", _sz), ("ms", C.c_double), ("flops", C.c_double),
                 ("bytes", C.c_double)]
@@ -159,6 +167,11 @@ def lib() -> C.CDLL:
         "n3d_linear_noalloc": ([C.c_int, vp, _sz, _sz, vp, _sz, vp, vp, vp], C.c_int),
         "n3d_layer_norm": ([C.c_int, vp, _sz, _sz, vp, vp, vp], C.c_int),
         "n3d_attention": ([C.c_int, vp, vp, vp, _sz, _sz, _sz, _sz, C.c_int, C.c_double, vp], C.c_int),
+        "n3d_cache_compress": ([C.c_int, C.POINTER(CacheConfig), fpp, _sz, vp, _sz, vp, C.POINTER(_sz),
+                                C.POINTER(_sz), C.POINTER(_sz), vp, vp], C.c_int),
+        "n3d_bench_linear": ([C.c_int, _sz, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
+        "n3d_bench_attention": ([C.c_int, _sz, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
+        "n3d_bench_layer_norm": ([C.c_int, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
         "n3d_profile_enable": ([vp, C.c_int], C.c_int),
         "n3d_profile_read": ([vp, C.POINTER(_KernelStats), _sz], _sz),
         "n3d_step_timing_enable": ([vp, C.c_int], C.c_int),
@@ -527,3 +540,49 @@ def attention(device: int, d_q: int, d_k: int, d_v: int, seq: int, heads: int, h
               d_out: int, rope: bool = True, theta: float = 10000.0) -> None:
     """RoPE then masked attention (src/encoder.rs:163-185, 281-329) on device pointers."""
     _check(lib().n3d_attention(device, d_q, d_k, d_v, seq, heads, head_dim, valid, int(rope), theta, d_out))
+
+
+def cache_compress(device: int, cfg: CacheConfig, probs, frames: int, embeds=None, hidden: int = 0, silence=None):
+    """SpeakerCache::trace_compress / compress (src/streaming.rs:353-482) on the device,
+    through the chunk loop's own selection and gather code.  Returns (picked, sentinel)
+    and, when `embeds` is given, also the gathered (embeds [L, hidden], probs [L, ns])."""
+    p = _f32(probs)
+    L = cfg.speaker_cache_length
+    picked = (_sz * max(L, 1))()
+    sentinel, count = _sz(), _sz()
+    ns = cfg.num_speakers
+    if embeds is not None:
+        e, sil = _f32(embeds), _f32(silence)
+        oe = np.empty(L * hidden, np.float32)
+        op = np.empty(L * ns, np.float32)
+        _check(lib().n3d_cache_compress(device, C.byref(cfg), _ptr(p), frames, e.ctypes.data, hidden, sil.ctypes.data,
+                                        picked, C.byref(sentinel), C.byref(count), oe.ctypes.data, op.ctypes.data))
+    else:
+        _check(lib().n3d_cache_compress(device, C.byref(cfg), _ptr(p), frames, None, 0, None, picked,
+                                        C.byref(sentinel), C.byref(count), None, None))
+    n = count.value
+    out = np.array(picked[:n], np.int64), sentinel.value
+    if embeds is not None:
+        return out + (oe[:n * hidden].reshape(n, hidden), op[:n * ns].reshape(n, ns))
+    return out
+
+
+def bench_linear(device: int, rows: int, cols: int, out: int, iters: int = 20) -> float:
+    """Mean device ms of one launch of n3d_linear's GEMM on resident synthetic operands."""
+    ms = C.c_double()
+    _check(lib().n3d_bench_linear(device, rows, cols, out, iters, C.byref(ms)))
+    return ms.value
+
+
+def bench_attention(device: int, seq: int, heads: int, head_dim: int, iters: int = 20) -> float:
+    """Mean device ms of one attention launch over all `seq` keys on resident operands."""
+    ms = C.c_double()
+    _check(lib().n3d_bench_attention(device, seq, heads, head_dim, iters, C.byref(ms)))
+    return ms.value
+
+
+def bench_layer_norm(device: int, rows: int, cols: int, iters: int = 20) -> float:
+    """Mean device ms of one LayerNorm launch (fp32 in and out)."""
+    ms = C.c_double()
+    _check(lib().n3d_bench_layer_norm(device, rows, cols, iters, C.byref(ms)))
+    return ms.value

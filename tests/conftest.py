@@ -103,8 +103,12 @@ def frame_check(got, want, ns=8, duration=0.01):
         return res
     d = np.abs(got.astype(np.float64) - want.astype(np.float64))
     res["maxdiff"] = float(d.max()) if d.size else 0.0
-    sg = 1.0 / (1.0 + np.exp(-got))
-    sw = 1.0 / (1.0 + np.exp(-want))
+    # the sigmoid in f32, as the gate computes it (src/bin/frame_check.rs:188-189): a
+    # logit within about 3e-8 of zero gives exactly 0.5, which is not a decision
+    one = np.float32(1.0)
+    sg = one / (one + np.exp(-got, dtype=np.float32))
+    sw = one / (one + np.exp(-want, dtype=np.float32))
+    assert sg.dtype == sw.dtype == np.float32
     res["flips"] = int(((sg > 0.5) != (sw > 0.5)).sum())
     a = oracle.extract_speaker_dict(got.ravel(), got.shape[0], ns, duration)
     b = oracle.extract_speaker_dict(want.ravel(), want.shape[0], ns, duration)

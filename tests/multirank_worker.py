@@ -38,8 +38,8 @@ def ok(out_dir, ckpt_dir):
     # device times differ per rank; every rank must report the slowest
     rec["max"] = bench.max_over_ranks(1.5 + rank, world)
     gathered = [None] * world
-    dist.all_gather_object(gathered, {"c4": bench.item_seeds("c4", rank, 3),
-                                      "c3": bench.item_seeds("c3", rank, 3)})
+    dist.all_gather_object(gathered, {"c4": bench.item_seeds("c4", rank, 3, world),
+                                      "c3": bench.item_seeds("c3", rank, 3, world)})
     rec["seeds"] = gathered
     # rank 0 writes the checkpoint; rank 1 must find it complete when checkpoint() returns
     cfg = copy.deepcopy(synth.MODEL_CONFIG)

@@ -201,6 +201,31 @@ def test_single_kernel_sizes_are_checked_before_any_cuda_call():
              lambda: lib.n3d_layer_norm(0, d, 2**31, 512, d, d, d),
              lambda: lib.n3d_attention(0, d, d, d, 2**31, 8, 64, 8, 1, 10000.0, d),
              lambda: lib.n3d_attention(0, d, d, d, 64, 0, 64, 8, 1, 10000.0, d),
-             lambda: lib.n3d_attention(0, d, d, d, 64, 70000, 64, 8, 1, 10000.0, d)]
+             lambda: lib.n3d_attention(0, d, d, d, 64, 70000, 64, 8, 1, 10000.0, d),
+             # sizes whose products wrap a 64-bit count must not slip past the scratch check
+             lambda: lib.n3d_linear_noalloc(0, d, 32, 2**59, d, 32, None, d, None),
+             lambda: lib.n3d_linear_noalloc(0, d, 2**32, 2**32, d, 2**32, None, d, None),
+             lambda: lib.n3d_linear_noalloc(0, d, 2**31, 32, d, 8, None, d, None),
+             lambda: lib.n3d_linear_noalloc(0, d, 8, 32, d, 2**32, None, d, None),
+             lambda: lib.n3d_linear_noalloc(0, d, 4096, 1024, d, 1024, None, d, None)]
     for call in cases:
         assert n3d.STATUS[call()] == "InvalidArgument", lib.n3d_last_error()
+
+
+def test_cache_compress_arguments_are_checked_before_any_cuda_call():
+    probs = np.full(64 * 8, 0.75, np.float32)
+    picked = (C.c_size_t * 64)()
+    sentinel, count = C.c_size_t(), C.c_size_t()
+
+    def call(frames=64, **kw):
+        cfg = n3d.CacheConfig(speaker_cache_length=32, num_silence_frames=1, score_threshold=0.25,
+                              num_speakers=8, subsampling_factor=8, num_strong_boosted_frames=2,
+                              num_weak_boosted_frames=4)
+        for k, v in kw.items():
+            setattr(cfg, k, v)
+        return n3d.lib().n3d_cache_compress(0, C.byref(cfg), probs.ctypes.data_as(C.POINTER(C.c_float)), frames,
+                                            None, 0, None, picked, C.byref(sentinel), C.byref(count), None, None)
+
+    for st in [call(frames=0), call(num_speakers=0), call(num_speakers=17), call(frames=2**40),
+               call(speaker_cache_length=2**40), call(frames=60000)]:
+        assert n3d.STATUS[st] == "InvalidArgument", n3d.lib().n3d_last_error()

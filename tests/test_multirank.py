@@ -53,6 +53,8 @@ def test_two_ranks_torchrun(tmp_path):
         s0, s1 = r0["seeds"][0][key], r0["seeds"][1][key]
         assert len(s0) == len(s1) == 3 and not set(s0) & set(s1)
         assert r0["seeds"] == r1["seeds"]
+    # config 4's 8192 clips and config 3's 256 sessions split evenly: rank 1 owns the second half
+    assert r0["seeds"][1]["c4"] == [4096, 4097, 4098] and r0["seeds"][1]["c3"] == [128, 129, 130]
     # one checkpoint, complete on every rank when checkpoint() returns
     assert r0["ckpt"] == r1["ckpt"] == str(ckpt)
     for r in (r0, r1):
