@@ -5,8 +5,8 @@ real-time audio thread that must not block in the driver's allocator, a host
 framework that owns all GPU memory through its own pool): its operand split
 lives in a fixed 16 MiB array inside the library instead of cudaMalloc'd
 scratch.  These tests call it through the C ABI twice in a row and check each
-result against the CPU oracle's tensor::linear within the kernel tests' gates
-(1e-3 absolute and 1e-5 relative to the largest output), and against the
+result against the CPU oracle's tensor::linear within the kernel sweep's gate
+(1e-3 absolute, and 3e-5 relative to the largest output), and against the
 allocating entry point n3d_linear, which runs the same dot products in the same
 order.  The array keeps the previous call's contents, so the second call also
 shows that stale scratch does not leak into a result.  This file is named to run
@@ -53,12 +53,12 @@ def _need(rows, cols, out):
 
 def _check(x, w, b, rows, cols, out, **kw):
     got = _run(n3d.linear_noalloc, x, w, b, rows, cols, out, **kw)
-    want = oracle.linear(x, rows, cols, w, out, b)
-    err = np.abs(got - want).max()
     assert np.isfinite(got).all()
-    assert err < TOL and err <= 1e-5 * max(1.0, np.abs(want).max()), err
     ref = _run(n3d.linear, x, w, b, rows, cols, out)
     assert np.array_equal(got, ref)
+    want = oracle.linear(x, rows, cols, w, out, b)
+    err = np.abs(got - want).max()
+    assert err < TOL and err <= 3e-5 * max(1.0, np.abs(want).max()), err
 
 
 CASES = [  # rows, cols, out, bias
