@@ -298,7 +298,8 @@ n3d_status n3d_schedule(const n3d_config *cfg, n3d_mode mode, size_t n_samples, 
 
 /* tensor::linear (src/tensor.rs:22-57) on device buffers: d_y[rows, out] =
  * d_x[rows, cols] * d_w[out, cols]^T + d_bias (nullable).  cols % 32 == 0.
- * Uses temporary device memory for the 3-term operand split (hi, hb, lb). */
+ * Uses temporary device memory for the fp16 operand split (h, l, each operand
+ * scaled by a power of two from its max |x|). */
 n3d_status n3d_linear(int device, const float *d_x, size_t rows, size_t cols, const float *d_w, size_t out,
                       const float *d_bias, float *d_y);
 
@@ -308,7 +309,7 @@ n3d_status n3d_linear(int device, const float *d_x, size_t rows, size_t cols, co
  * an allocation budget fixed at start-up).  No counterpart in the reference.
  * The operand split uses a fixed 16 MiB array inside the library's GPU image
  * instead of temporary memory, so the call allocates nothing.  Limits:
- * rows*cols + out*cols at most about 2 Mi floats (larger requests fail with
+ * rows*cols + out*cols at most 4194240 (larger requests fail with
  * N3D_ERR_INVALID_ARGUMENT); every GPU that loads the library keeps the 16 MiB
  * until exit; all calls on a device share the array, so calls whose GPU work
  * overlaps race and must be serialised by the caller.  The first call on each

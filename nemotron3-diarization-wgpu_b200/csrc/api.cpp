@@ -160,12 +160,25 @@ struct DevScratch {
     }
 };
 
+// The fp16-split scales of two device operands from their max |x| (one readback).
+void operand_scales(KernelCtx& k, DevScratch& sc, const float* a, size_t na, const float* b, size_t nb, float* out) {
+    float* m = sc.get(2);
+    N3D_CUDA(cudaMemsetAsync(m, 0, 8, k.stream));
+    n3d::launch_absmax(k.stream, a, (long long)na, m);
+    n3d::launch_absmax(k.stream, b, (long long)nb, m + 1);
+    float hm[2] = {0.0f, 0.0f};
+    N3D_CUDA(cudaMemcpyAsync(hm, m, 8, cudaMemcpyDeviceToHost, k.stream));
+    N3D_CUDA(cudaStreamSynchronize(k.stream));
+    out[0] = n3d::split_scale(hm[0]);
+    out[1] = n3d::split_scale(hm[1]);
+}
+
 }  // namespace
 
 extern "C" {
 
 const char* n3d_last_error(void) { return g_last_error.c_str(); }
-const char* n3d_version(void) { return "n3d-b200 0.2 (sm_100a, tcgen05: TF32+2xBF16 split GEMMs, 3xBF16 attention)"; }
+const char* n3d_version(void) { return "n3d-b200 0.3 (sm_100a, tcgen05: fp16-split GEMMs (h*h + h*l + l*h), 3xBF16 attention)"; }
 
 n3d_status n3d_model_load_gpu(const char* dir, int device, n3d_model** out) {
     return guarded([&] {
@@ -571,8 +584,10 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);
         DevScratch sc;
-        const n3d::Split3Out x{sc.get(rows * cols), sc.get(rows * cols / 2), sc.get(rows * cols / 2)};
-        const n3d::Split3Out w{sc.get(out * cols), sc.get(out * cols / 2), sc.get(out * cols / 2)};
+        float scale[2];
+        operand_scales(k, sc, d_x, rows * cols, d_w, out * cols, scale);
+        const n3d::SplitOut x{sc.get(rows * cols / 2), sc.get(rows * cols / 2), scale[0], nullptr};
+        const n3d::SplitOut w{sc.get(out * cols / 2), sc.get(out * cols / 2), scale[1], nullptr};
         n3d::launch_split(k.stream, d_x, (long long)(rows * cols), x);
         n3d::launch_split(k.stream, d_w, (long long)(out * cols), w);
         n3d::Epi e;
@@ -580,9 +595,9 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
         e.bias = d_bias;
         e.out = d_y;
         e.ldo = (long long)out;
-        n3d::gemm_split3(k.stream, n3d::SplitOperand{x.hi, x.hb, x.lb, (long long)rows, (long long)cols, (long long)cols},
-                         n3d::SplitOperand{w.hi, w.hb, w.lb, (long long)out, (long long)cols, (long long)cols},
-                         (int)rows, (int)out, (int)cols, 0, e, k.err);
+        n3d::gemm_split(k.stream, n3d::SplitOperand{x.h, x.l, (long long)rows, (long long)cols, (long long)cols, x.scale},
+                        n3d::SplitOperand{w.h, w.l, (long long)out, (long long)cols, (long long)cols, w.scale},
+                        (int)rows, (int)out, (int)cols, 0, e, k.err);
         kcheck(k);
     });
 }
@@ -603,7 +618,7 @@ n3d_status n3d_layer_norm(int device, const float* d_x, size_t rows, size_t cols
         N3D_CUDA(cudaSetDevice(device));
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);
-        n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, n3d::Split3Out{d_y, nullptr, nullptr});
+        n3d::launch_layer_norm(k.stream, d_x, (long long)rows, (int)cols, d_w, d_b, n3d::plain_out(d_y));
         kcheck(k);
     });
 }
@@ -654,8 +669,7 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
             op.vt_lo = sc.get(W * vt_ld / 2);
             op.vt_ld = (long long)vt_ld;
             n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, cs, sn, op);
-            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::Split3Out{d_out, nullptr, nullptr},
-                                     k.err);
+            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::plain_out(d_out), k.err);
         } else {
             n3d::launch_pack_qkv(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, qkv);
             n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out);
@@ -769,8 +783,10 @@ n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, in
         n3d::launch_fill_random(k.stream, x, (long long)(rows * cols), 1, 1.0f);
         n3d::launch_fill_random(k.stream, w, (long long)(out * cols), 2, 1.0f / std::sqrt((float)cols));
         n3d::launch_fill_random(k.stream, bias, (long long)out, 3, 1.0f);
-        const n3d::Split3Out xs{sc.get(rows * cols), sc.get(rows * cols / 2), sc.get(rows * cols / 2)};
-        const n3d::Split3Out ws{sc.get(out * cols), sc.get(out * cols / 2), sc.get(out * cols / 2)};
+        float scale[2];
+        operand_scales(k, sc, x, rows * cols, w, out * cols, scale);
+        const n3d::SplitOut xs{sc.get(rows * cols / 2), sc.get(rows * cols / 2), scale[0], nullptr};
+        const n3d::SplitOut ws{sc.get(out * cols / 2), sc.get(out * cols / 2), scale[1], nullptr};
         n3d::launch_split(k.stream, x, (long long)(rows * cols), xs);
         n3d::launch_split(k.stream, w, (long long)(out * cols), ws);
         n3d::Epi e;
@@ -779,9 +795,9 @@ n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, in
         e.out = y;
         e.ldo = (long long)out;
         *ms = time_launches(k, iters, [&] {
-            n3d::gemm_split3(k.stream, n3d::SplitOperand{xs.hi, xs.hb, xs.lb, (long long)rows, (long long)cols, (long long)cols},
-                             n3d::SplitOperand{ws.hi, ws.hb, ws.lb, (long long)out, (long long)cols, (long long)cols},
-                             (int)rows, (int)out, (int)cols, 0, e, k.err);
+            n3d::gemm_split(k.stream, n3d::SplitOperand{xs.h, xs.l, (long long)rows, (long long)cols, (long long)cols, xs.scale},
+                            n3d::SplitOperand{ws.h, ws.l, (long long)out, (long long)cols, (long long)cols, ws.scale},
+                            (int)rows, (int)out, (int)cols, 0, e, k.err);
         });
     });
 }
@@ -820,8 +836,7 @@ n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head
             op.vt_ld = (long long)vt_ld;
             n3d::launch_pack_attn(k.stream, q, kk, v, (long long)seq, (int)heads, nullptr, nullptr, op);
             *ms = time_launches(k, iters, [&] {
-                n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::Split3Out{ctx, nullptr, nullptr},
-                                         k.err);
+                n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::plain_out(ctx), k.err);
             });
         } else {
             float* qkv = sc.get(seq * 3 * W);
@@ -850,7 +865,7 @@ n3d_status n3d_bench_layer_norm(int device, size_t rows, size_t cols, int iters,
         n3d::launch_fill_random(k.stream, w, (long long)cols, 8, 1.0f);
         n3d::launch_fill_random(k.stream, b, (long long)cols, 9, 0.1f);
         *ms = time_launches(k, iters, [&] {
-            n3d::launch_layer_norm(k.stream, x, (long long)rows, (int)cols, w, b, n3d::Split3Out{y, nullptr, nullptr});
+            n3d::launch_layer_norm(k.stream, x, (long long)rows, (int)cols, w, b, n3d::plain_out(y));
         });
     });
 }

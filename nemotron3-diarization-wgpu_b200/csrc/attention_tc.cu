@@ -97,12 +97,12 @@ struct AttnMaps {
     CUtensorMap qh, ql;      // Q pair [rows, heads*64] bf16, box 64 x 128, 128-byte swizzle
     CUtensorMap kh, kl;      // K pair, box 64 x 64
     CUtensorMap vh, vl;      // V^T pair [heads*64, rows], box 64 x 64
-    CUtensorMap ch, cb, cl;  // context hi (fp32, box 32 x 32) and hb / lb (bf16, box 64 x 32)
+    CUtensorMap ch, cl;      // context fp16 split h / l [rows, heads*64], box 64 x 32, 128-byte swizzle
 };
 
 __global__ void __launch_bounds__(THREADS, 2)
     attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
-                        Split3Out ctx, int ctx_tma, int* err) {
+                        SplitOut ctx, int ctx_tma, int* err) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stages = smem;
@@ -328,39 +328,33 @@ __global__ void __launch_bounds__(THREADS, 2)
             tc_fence_after();
             tmem_ld64(lb + COL_O, o);
         }
-        // ---- context rows: the 3-term split through TMA stores when all 32 rows of the
+        // ---- context rows: the fp16 split through TMA stores when all 32 rows of the
         // warp belong to this sequence; otherwise (and for a plain fp32 context) per row
         const int wrow0 = q0 + qd * 32;
         if (ctx_tma && wrow0 + 32 <= S) {
-            // staging in ring slots 0..1 (every load has been consumed by the last PV):
-            // per warp 16 KB = hi cols 0..31 | hi cols 32..63 | hb | lb, 128-byte rows
-            uint8_t* stg = stages + (warp - 2) * 16384;
+            // staging in ring slot 0 (every load has been consumed by the last PV):
+            // per warp 8 KB = h | l, 128-byte rows of 64 fp16
+            uint8_t* stg = stages + (warp - 2) * 8192;
             const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
-            uint32_t hbw[32], lbw[32];
+            uint32_t hw[32], lw[32];
 #pragma unroll
             for (int d = 0; d < 64; d += 2) {
                 const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
-                split3x2(x0, x1, o[d], o[d + 1], hbw[d / 2], lbw[d / 2]);
+                split2x2(x0, x1, ctx.scale, hw[d / 2], lw[d / 2]);
             }
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int sw = ((i ^ (lane & 7)) << 4) + lane * 128;
-                *reinterpret_cast<float4*>(stg + sw) = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-                *reinterpret_cast<float4*>(stg + 4096 + sw) =
-                    make_float4(o[32 + 4 * i], o[32 + 4 * i + 1], o[32 + 4 * i + 2], o[32 + 4 * i + 3]);
-                *reinterpret_cast<uint4*>(stg + 8192 + sw) =
-                    make_uint4(hbw[4 * i], hbw[4 * i + 1], hbw[4 * i + 2], hbw[4 * i + 3]);
-                *reinterpret_cast<uint4*>(stg + 12288 + sw) =
-                    make_uint4(lbw[4 * i], lbw[4 * i + 1], lbw[4 * i + 2], lbw[4 * i + 3]);
+                *reinterpret_cast<uint4*>(stg + sw) = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+                *reinterpret_cast<uint4*>(stg + 4096 + sw) =
+                    make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 const int y = row0 + wrow0;
                 tma_store_2d(&maps.ch, stg, h * HD, y);
-                tma_store_2d(&maps.ch, stg + 4096, h * HD + 32, y);
-                tma_store_2d(&maps.cb, stg + 8192, h * HD, y);
-                tma_store_2d(&maps.cl, stg + 12288, h * HD, y);
+                tma_store_2d(&maps.cl, stg + 4096, h * HD, y);
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read before exit
             }
@@ -373,15 +367,13 @@ __global__ void __launch_bounds__(THREADS, 2)
                 float x[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
-                if (ctx.hb) {
-                    float hh[4];
-                    uint2 hb, lb2;
-                    split3x4(x, hh, hb, lb2);
-                    *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(hh[0], hh[1], hh[2], hh[3]);
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.hb) + off + d) = hb;
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.lb) + off + d) = lb2;
+                if (ctx.h) {
+                    uint2 hw, lw;
+                    split2x4(x, ctx.scale, hw, lw);
+                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.h) + off + d) = hw;
+                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.l) + off + d) = lw;
                 } else {
-                    *reinterpret_cast<float4*>(ctx.hi + off + d) = make_float4(x[0], x[1], x[2], x[3]);
+                    *reinterpret_cast<float4*>(ctx.plain + off + d) = make_float4(x[0], x[1], x[2], x[3]);
                 }
             }
         }
@@ -394,7 +386,7 @@ __global__ void __launch_bounds__(THREADS, 2)
 }  // namespace
 
 void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
-                         Split3Out ctx, int* err) {
+                         SplitOut ctx, int* err) {
     if (seqs <= 0 || S <= 0) return;
     if ((seqs > 1 && S % 8) || op.vt_ld % 8)
         throw Error(9, "attention: the sequence stride and the V^T row stride must be multiples of 8");
@@ -410,13 +402,12 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
     m.kl = make_bf16_map(op.k_lo, op.rows_cap, W, W, 64, KB, true);
     m.vh = make_bf16_map(op.vt_hi, W, rows, op.vt_ld, 64, HD, true);
     m.vl = make_bf16_map(op.vt_lo, W, rows, op.vt_ld, 64, HD, true);
-    const int ctx_tma = ctx.hb != nullptr;
+    const int ctx_tma = ctx.h != nullptr;
     if (ctx_tma) {
-        m.ch = make_store_map(ctx.hi, rows, W, W);
-        m.cb = make_bf16_map(ctx.hb, rows, W, W, 64, 32, true);
-        m.cl = make_bf16_map(ctx.lb, rows, W, W, 64, 32, true);
+        m.ch = make_f16_map(ctx.h, rows, W, W, 64, 32);
+        m.cl = make_f16_map(ctx.l, rows, W, W, 64, 32);
     } else {
-        m.ch = m.cb = m.cl = m.qh;  // unused
+        m.ch = m.cl = m.qh;  // unused
     }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
     launch_pdl(attention_tc_kernel, grid, dim3(THREADS), SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma, err);

@@ -7,15 +7,16 @@
 // become epilogue modes of this one kernel.  The reference arithmetic it must
 // agree with is `tensor::linear` (src/tensor.rs:22-57) in fp32.
 //
-// Arithmetic (3-term split): every operand x is stored as hi = RN-TF32(x) (fp32
-// array) and bf16 copies of hi and of lo = x - hi; each k-block issues hi·hi on
-// `kind::tf32` and hb·lb + lb·hb on `kind::f16`, all into one fp32 accumulator.
-// Accuracy matches 3xTF32 within 2x on this model (logit maxdiff 8e-8 vs 5e-8 on
-// config 0, no flips), and two of the three products run at the bf16 rate: under
-// the 1 kW power cap that is 23-38 % more GEMM throughput.
+// Arithmetic (fp16 split): every operand x is stored as two fp16 arrays of x s (s a
+// power of two per tensor): h = RN-fp16(x s), l = RN-fp16(x s - h).  Each k-step issues
+// h·h, h·l and l·h on `kind::f16`, all into one fp32 TMEM accumulator, and the epilogue
+// multiplies by 1 / (s_A s_B).  fp16's 11 significant bits make h + l good to ~2^-22,
+// as accurate as 3xTF32, while all three products run at the 16-bit tensor rate and an
+// operand costs 4 bytes per element.
 //
-// k-block = 32: per CTA and stage, A rows as [hi: 128 B | hb: 64 B | lb: 64 B] and
-// the same for B, TMA-loaded with the 128-byte (tf32) and 64-byte (bf16) swizzles.
+// k-block = 64: per CTA and stage, A rows as [h: 128 B | l: 128 B] and the same for B,
+// TMA-loaded with the 128-byte swizzle.  A K that is an odd multiple of 32 ends with a
+// half block whose upper columns the TMA fills with zeros.
 // Two kernels:
 //   gemm_kernel<BN>        one CTA per 128 x BN tile, persistent (N = 192 head GEMMs,
 //                          small M, the allocation-free entry point)
@@ -29,6 +30,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <map>
 #include <mutex>
@@ -42,10 +44,9 @@ namespace n3d {
 namespace {
 
 constexpr int BM = 128;                 // rows per CTA
-constexpr int BK = 32;                  // k-block
-constexpr int ROW_T = BK * 4;           // bytes per row of the tf32 part (128: SW128)
-constexpr int ROW_H = BK * 2;           // bytes per row of a bf16 part (64: SW64)
-constexpr int ROW_3 = ROW_T + 2 * ROW_H;  // all three parts of one row
+constexpr int BK = 64;                  // k-block (fp16 elements)
+constexpr int ROW = BK * 2;             // bytes per row of one fp16 array (128: SW128)
+constexpr int ROW_2 = 2 * ROW;          // both arrays of one row
 
 // ------------------------------------------------------------------- GELU
 // GELU(x) = 0.5 x (1 + erf(x/√2)) (src/tensor.rs:113-120), branch-free.
@@ -109,8 +110,8 @@ __device__ __forceinline__ void store_row32(float* dst, const float* v, int ncol
             if (i < ncols_left) dst[i] = v[i];
     }
 }
-// 32 bf16 of one row (16 packed words).
-__device__ __forceinline__ void store_row32_bf16(uint16_t* dst, const uint32_t* w, int ncols_left) {
+// 32 16-bit values of one row (16 packed words).
+__device__ __forceinline__ void store_row32_16(uint16_t* dst, const uint32_t* w, int ncols_left) {
     if (ncols_left >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
 #pragma unroll
         for (int i = 0; i < 16; i += 4)
@@ -122,9 +123,9 @@ __device__ __forceinline__ void store_row32_bf16(uint16_t* dst, const uint32_t* 
     }
 }
 
-// Epilogue value of accumulator column i: bias, activation.
-__device__ __forceinline__ float epi_value(int mode, float acc, float bias) {
-    float x = __fadd_rn(acc, bias);
+// Epilogue value of accumulator column i: operand scales undone, bias, activation.
+__device__ __forceinline__ float epi_value(int mode, float acc, float scale, float bias) {
+    float x = __fadd_rn(__fmul_rn(acc, scale), bias);
     if (mode == EPI_GELU_SPLIT) x = gelu1(x);
     if (mode == EPI_RELU_SPLIT) x = fmaxf(x, 0.0f);
     return x;
@@ -175,7 +176,7 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m
 #pragma unroll
             for (int i = 0; i < 32; i++) {
                 const int col = n0 + c + i;
-                const float rr = fmaxf(__fadd_rn(v[i], bs[col]), 0.0f);
+                const float rr = fmaxf(__fadd_rn(__fmul_rn(v[i], epi.acc_scale), bs[col]), 0.0f);
 #pragma unroll
                 for (int o = 0; o < 8; o++) acc[o] = __fadd_rn(acc[o], __fmul_rn(rr, w2s[o * N + col]));
             }
@@ -192,18 +193,16 @@ __device__ __forceinline__ void epilogue_tile(const Epi& epi, uint32_t tl, int m
         float bias[32];
         load_bias32(epi.bias, col0, N, bias);
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = zero_row ? 0.0f : epi_value(epi.mode, v[i], bias[i]);
+        for (int i = 0; i < 32; i++) v[i] = zero_row ? 0.0f : epi_value(epi.mode, v[i], epi.acc_scale, bias[i]);
         const int left = N - col0;
-        float* dst = epi.out + orow * epi.ldo + col0;
         if (epi.mode == EPI_STORE) {
-            store_row32(dst, v, left);
-        } else {  // 3-term split of the output
-            uint32_t hb[16], lb[16];
+            store_row32(epi.out + orow * epi.ldo + col0, v, left);
+        } else {  // fp16 split of the output
+            uint32_t hw[16], lw[16];
 #pragma unroll
-            for (int i = 0; i < 16; i++) split3x2(v[2 * i], v[2 * i + 1], v[2 * i], v[2 * i + 1], hb[i], lb[i]);
-            store_row32(dst, v, left);
-            store_row32_bf16(static_cast<uint16_t*>(epi.out2) + orow * epi.ldo + col0, hb, left);
-            store_row32_bf16(static_cast<uint16_t*>(epi.out3) + orow * epi.ldo + col0, lb, left);
+            for (int i = 0; i < 16; i++) split2x2(v[2 * i], v[2 * i + 1], epi.out_scale, hw[i], lw[i]);
+            store_row32_16(static_cast<uint16_t*>(epi.out_h) + orow * epi.ldo + col0, hw, left);
+            store_row32_16(static_cast<uint16_t*>(epi.out_l) + orow * epi.ldo + col0, lw, left);
         }
     }
 }
@@ -226,8 +225,8 @@ __device__ __forceinline__ void stage_rows(uint8_t* box, int lane, const float* 
         *reinterpret_cast<float4*>(box + lane * 128 + ((i ^ (lane & 7)) << 4)) =
             make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
-// 32 x 32 bf16 (16 packed words per lane) into a 2 KB 64-byte-swizzled box.
-__device__ __forceinline__ void stage_rows_bf16(uint8_t* box, int lane, const uint32_t* w) {
+// 32 x 32 16-bit values (16 packed words per lane) into a 2 KB 64-byte-swizzled box.
+__device__ __forceinline__ void stage_rows_16(uint8_t* box, int lane, const uint32_t* w) {
 #pragma unroll
     for (int i = 0; i < 4; i++)
         *reinterpret_cast<uint4*>(box + lane * 64 + ((i ^ ((lane >> 1) & 3)) << 4)) =
@@ -275,6 +274,8 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             tmem_ld32(tl + c + 32, v + 32);
             const int col0 = n0 + c;
             if (col0 >= N) break;
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) unpack2(mul2(pack2(v[i], v[i + 1]), pack2(epi.acc_scale, epi.acc_scale)), v[i], v[i + 1]);
             const int sec = col0 / epi.q_cols, hcol = col0 - sec * epi.q_cols;
             if (sec < 2) {
                 // rotate-half RoPE (src/encoder.rs:281-296); the tables repeat their first
@@ -308,8 +309,8 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                     *reinterpret_cast<uint4*>(bhi + o) = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
                     *reinterpret_cast<uint4*>(blo + o) = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
                 }
-                stage_issue(lane, sec == 0 ? &epi.map_out : &epi.map_k_hi, bhi,
-                            sec == 0 ? &epi.map_out2 : &epi.map_k_lo, blo, nullptr, nullptr, hcol, rowbase);
+                stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_hi, bhi,
+                            sec == 0 ? &epi.map_l : &epi.map_k_lo, blo, nullptr, nullptr, hcol, rowbase);
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
@@ -324,9 +325,10 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
         return;
     }
     const bool split = mode != EPI_STORE;
-    uint8_t* bhi = stg;          // 4 KB fp32 box
-    uint8_t* bhb = stg + 4096;   // 2 KB bf16 box
-    uint8_t* blb = stg + 6144;   // 2 KB bf16 box
+    uint8_t* bst = stg;          // 4 KB fp32 box (EPI_STORE)
+    uint8_t* bh = stg;           // 2 KB fp16 box (split modes)
+    uint8_t* bl = stg + 2048;    // 2 KB fp16 box
+    const uint64_t sc2 = pack2(epi.acc_scale, epi.acc_scale);
     for (int c = c_begin; c < c_end; c += 32) {
         float v[32];
         tmem_ld32(tl + c, v);
@@ -337,55 +339,46 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
         if (mode == EPI_GELU_SPLIT) {
 #pragma unroll
             for (int i = 0; i < 32; i += 2) {
-                unpack2(add2(pack2(v[i], v[i + 1]), pack2(bias[i], bias[i + 1])), v[i], v[i + 1]);
+                unpack2(fma2(pack2(v[i], v[i + 1]), sc2, pack2(bias[i], bias[i + 1])), v[i], v[i + 1]);
                 gelu2(v[i], v[i + 1]);
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < 32; i++) v[i] = epi_value(mode, v[i], bias[i]);
-        }
-        uint32_t hb[16], lb[16];
-        if (split) {
-#pragma unroll
-            for (int i = 0; i < 16; i++) split3x2(v[2 * i], v[2 * i + 1], v[2 * i], v[2 * i + 1], hb[i], lb[i]);
+            for (int i = 0; i < 32; i++) v[i] = epi_value(mode, v[i], epi.acc_scale, bias[i]);
         }
         stage_begin(lane);
-        stage_rows(bhi, lane, v);
         if (split) {
-            stage_rows_bf16(bhb, lane, hb);
-            stage_rows_bf16(blb, lane, lb);
+            uint32_t hw[16], lw[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) split2x2(v[2 * i], v[2 * i + 1], epi.out_scale, hw[i], lw[i]);
+            stage_rows_16(bh, lane, hw);
+            stage_rows_16(bl, lane, lw);
+            stage_issue(lane, &epi.map_h, bh, &epi.map_l, bl, nullptr, nullptr, col0, rowbase);
+        } else {
+            stage_rows(bst, lane, v);
+            stage_issue(lane, &epi.map_out, bst, nullptr, nullptr, nullptr, nullptr, col0, rowbase, epi.reduce != 0);
         }
-        stage_issue(lane, &epi.map_out, bhi, split ? &epi.map_out2 : nullptr, bhb, split ? &epi.map_out3 : nullptr,
-                    blb, col0, rowbase, epi.reduce != 0);
     }
 }
 
 // ------------------------------------------------------------- main loops
-// Shared-memory stage of one CTA: [A: hi | hb | lb][B: hi | hb | lb] with `ra` and
-// `rb` rows.  MMAs of one k-block into accumulator `d`.
+// Shared-memory stage of one CTA: [A: h | l][B: h | l] with `ra` and `rb` rows of
+// 128 bytes.  MMAs of one k-block (4 steps of 16) into accumulator `d`.
 template <bool PAIR>
-__device__ __forceinline__ void mma_kblock(uint32_t d, uint32_t st, int ra, int rb, uint32_t idt, uint32_t idb,
-                                           bool first) {
-    const uint32_t ah = st, ahb = ah + ra * ROW_T, alb = ahb + ra * ROW_H;
-    const uint32_t bh = alb + ra * ROW_H, bhb = bh + rb * ROW_T, blb = bhb + rb * ROW_H;
+__device__ __forceinline__ void mma_kblock(uint32_t d, uint32_t st, int ra, int rb, uint32_t idesc, bool first) {
+    const uint32_t ah = st, al = ah + ra * ROW, bh = al + ra * ROW, bl = bh + rb * ROW;
 #pragma unroll
-    for (int k = 0; k < BK / 8; k++) {  // hi·hi: 8 tf32 = 32 bytes along the 128-byte rows
-        const uint64_t a = desc_k_sw128(ah + 32 * k), b = desc_k_sw128(bh + 32 * k);
-        if (PAIR)
-            umma_tf32_pair(d, a, b, idt, !(first && k == 0));
-        else
-            umma_tf32(d, a, b, idt, !(first && k == 0));
-    }
-#pragma unroll
-    for (int k = 0; k < BK / 16; k++) {  // hb·lb + lb·hb: 16 bf16 = 32 bytes along the 64-byte rows
-        const uint64_t a1 = desc_k_sw64(ahb + 32 * k), b1 = desc_k_sw64(blb + 32 * k);
-        const uint64_t a2 = desc_k_sw64(alb + 32 * k), b2 = desc_k_sw64(bhb + 32 * k);
+    for (int k = 0; k < BK / 16; k++) {  // 16 fp16 = 32 bytes along the 128-byte rows
+        const uint64_t a_h = desc_k_sw128(ah + 32 * k), a_l = desc_k_sw128(al + 32 * k);
+        const uint64_t b_h = desc_k_sw128(bh + 32 * k), b_l = desc_k_sw128(bl + 32 * k);
         if (PAIR) {
-            umma_bf16_pair(d, a1, b1, idb, 1);
-            umma_bf16_pair(d, a2, b2, idb, 1);
+            umma_f16_pair(d, a_h, b_h, idesc, !(first && k == 0));
+            umma_f16_pair(d, a_h, b_l, idesc, 1);
+            umma_f16_pair(d, a_l, b_h, idesc, 1);
         } else {
-            umma_bf16(d, a1, b1, idb, 1);
-            umma_bf16(d, a2, b2, idb, 1);
+            umma_f16(d, a_h, b_h, idesc, !(first && k == 0));
+            umma_f16(d, a_h, b_l, idesc, 1);
+            umma_f16(d, a_l, b_h, idesc, 1);
         }
     }
 }
@@ -395,11 +388,10 @@ __device__ __forceinline__ void mma_kblock(uint32_t d, uint32_t st, int ra, int 
 template <bool PAIR>
 __device__ __forceinline__ void load_stage(uint8_t* st, int ra, int rb, const CUtensorMap* m, uint64_t* bar,
                                            uint32_t bar_cluster, int xa, int ya, int xb, int yb) {
-    uint8_t* p[6] = {st, st + ra * ROW_T, st + ra * (ROW_T + ROW_H), st + ra * ROW_3, st + ra * ROW_3 + rb * ROW_T,
-                     st + ra * ROW_3 + rb * (ROW_T + ROW_H)};
+    uint8_t* p[4] = {st, st + ra * ROW, st + ra * ROW_2, st + ra * ROW_2 + rb * ROW};
 #pragma unroll
-    for (int i = 0; i < 6; i++) {
-        const int x = i < 3 ? xa : xb, y = i < 3 ? ya : yb;
+    for (int i = 0; i < 4; i++) {
+        const int x = i < 2 ? xa : xb, y = i < 2 ? ya : yb;
         if (PAIR)
             tma_load_2d_pair(p[i], &m[i], bar_cluster, x, y);
         else
@@ -407,14 +399,14 @@ __device__ __forceinline__ void load_stage(uint8_t* st, int ra, int rb, const CU
     }
 }
 
-struct Maps6 {
-    CUtensorMap m[6];  // A hi, hb, lb; B hi, hb, lb
+struct Maps4 {
+    CUtensorMap m[4];  // A h, l; B h, l
 };
 
 // ------------------------------------------------------------ one-CTA kernel
 template <int BN>
 struct GemmCfg {
-    static constexpr int STAGE_BYTES = (BM + BN) * ROW_3;
+    static constexpr int STAGE_BYTES = (BM + BN) * ROW_2;
     static constexpr int STAGING = 4 * 8192;
     static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
@@ -426,7 +418,7 @@ struct GemmCfg {
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
-    gemm_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
+    gemm_kernel(const __grid_constant__ Maps4 maps, int M, int N, int K, int kb_per_tap,
                 const __grid_constant__ Epi epi, int* err, int ksplit, int Mp) {
     using Cfg = GemmCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -442,7 +434,7 @@ __global__ void __launch_bounds__(192, 1)
     // tile t = (output tile, k split): split ks covers k-blocks [ks nkb / ksplit,
     // (ks + 1) nkb / ksplit) and stores its partial tile at row offset ks * Mp
     const int tiles = ((M + BM - 1) / BM) * tiles_n * ksplit;
-    const int nkb = K / BK;
+    const int nkb = (K + BK - 1) / BK;
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < Cfg::STAGES; s++) {
@@ -454,7 +446,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&acc_empty[b], 4);
         }
         mbar_fence_init();
-        for (int i = 0; i < 6; i++) tma_prefetch_desc(&maps.m[i]);
+        for (int i = 0; i < 4; i++) tma_prefetch_desc(&maps.m[i]);
     }
     if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
     __syncthreads();
@@ -487,7 +479,7 @@ __global__ void __launch_bounds__(192, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idt = idesc_tf32(BN), idb = idesc_bf16(BN);
+            constexpr uint32_t idesc = idesc_f16(BN);
             uint32_t g = 0;
             int it = 0;
             bool ok = true;
@@ -504,7 +496,7 @@ __global__ void __launch_bounds__(192, 1)
                         break;
                     }
                     tc_fence_after();
-                    mma_kblock<false>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN, idt, idb, kb == kb0);
+                    mma_kblock<false>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN, idesc, kb == kb0);
                     umma_commit(&empty[s]);
                 }
                 if (ok) umma_commit(&acc_full[buf]);
@@ -569,7 +561,7 @@ __device__ __forceinline__ PairTile pair_tile(int t, int tiles_n, int full, int 
 
 template <int BN>
 struct PairCfg {
-    static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_3;
+    static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_2;
     static constexpr int STAGING = 4 * 8192;
     static constexpr int THREADS = 192;
     static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
@@ -582,7 +574,7 @@ struct PairCfg {
 
 template <int BN>
 __global__ void __launch_bounds__(192, 1)
-    gemm_pair_kernel(const __grid_constant__ Maps6 maps, int M, int N, int K, int kb_per_tap,
+    gemm_pair_kernel(const __grid_constant__ Maps4 maps, int M, int N, int K, int kb_per_tap,
                      const __grid_constant__ Epi epi, int* err, int full, int split) {
     using Cfg = PairCfg<BN>;
     extern __shared__ uint8_t smem_raw[];
@@ -599,7 +591,7 @@ __global__ void __launch_bounds__(192, 1)
     const int cid = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
     const int tiles_n = (N + BN - 1) / BN;
     const int tiles = full + (((M + 2 * BM - 1) / (2 * BM)) * tiles_n - full) * split;
-    const int nkb = K / BK;
+    const int nkb = (K + BK - 1) / BK;
 
     if (warp == 0 && lane == 0) {
         for (int s = 0; s < Cfg::STAGES; s++) {
@@ -611,7 +603,7 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(&acc_empty[b], 8);
         }
         mbar_fence_init();
-        for (int i = 0; i < 6; i++) tma_prefetch_desc(&maps.m[i]);
+        for (int i = 0; i < 4; i++) tma_prefetch_desc(&maps.m[i]);
     }
     if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
     __syncthreads();
@@ -652,7 +644,7 @@ __global__ void __launch_bounds__(192, 1)
             bool ok = true;
             for (int t = cid; ok && t < tiles; t += ncl, it++) {
                 const int nw = pair_tile<BN>(t, tiles_n, full, split).nw;
-                const uint32_t idt = idesc_tf32_pair(nw), idb = idesc_bf16_pair(nw);
+                const uint32_t idesc = idesc_f16_pair(nw);
                 const int buf = it & 1;
                 if (it >= 2 && !mbar_wait_cluster(&acc_empty[buf], ((it >> 1) - 1) & 1, err, DEV_TIMEOUT_ACC)) break;
                 tc_fence_after();
@@ -664,7 +656,7 @@ __global__ void __launch_bounds__(192, 1)
                         break;
                     }
                     tc_fence_after();
-                    mma_kblock<true>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN / 2, idt, idb, kb == 0);
+                    mma_kblock<true>(d, smem_u32(smem + s * Cfg::STAGE_BYTES), BM, BN / 2, idesc, kb == 0);
                     umma_commit_pair(&empty[s]);
                 }
                 if (ok) umma_commit_pair(&acc_full[buf]);
@@ -745,11 +737,15 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// 2-D map over a row-major matrix [rows, cols] of `esize`-byte elements (row stride ld
-// elements), box = box_cols x box_rows, swizzle = box_cols * esize bytes (32, 64, 128)
-// or none, zero fill out of bounds.
-CUtensorMap encode_map(const void* ptr, int esize, long long rows, long long cols, long long ld, int box_cols,
+// Element types of the maps: fp32, fp16 (GEMM operands) and bf16 (attention operands).
+enum MapType : int { MAP_F32 = 4, MAP_F16 = 2, MAP_BF16 = 3 };
+
+// 2-D map over a row-major matrix [rows, cols] of `type` elements (row stride ld
+// elements), box = box_cols x box_rows, swizzle = box_cols * element size bytes (32,
+// 64, 128) or none, zero fill out of bounds.
+CUtensorMap encode_map(const void* ptr, int type, long long rows, long long cols, long long ld, int box_cols,
                        int box_rows, bool swizzle) {
+    const int esize = type == MAP_F32 ? 4 : 2;
     if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * esize) % 16)
         throw Error(9, "GEMM operand or output is not 16-byte aligned");
     CUtensorMap m;
@@ -762,39 +758,41 @@ CUtensorMap encode_map(const void* ptr, int esize, long long rows, long long col
                                   : span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                   : span == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
                                                 : CU_TENSOR_MAP_SWIZZLE_32B;
-    CUresult r = encode_fn()(&m, esize == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+    const CUtensorMapDataType dt = type == MAP_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : type == MAP_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = encode_fn()(&m, dt, 2,
                              const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw Error(9, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
     return m;
 }
 
-CUtensorMap cached_map(const void* ptr, int esize, long long rows, long long cols, long long ld, int box_cols,
+CUtensorMap cached_map(const void* ptr, int type, long long rows, long long cols, long long ld, int box_cols,
                        int box_rows, bool swizzle) {
     using Key = std::tuple<const void*, int, long long, long long, long long, int, int, bool>;
     static std::map<Key, CUtensorMap> cache;
     static std::mutex mu;
-    const Key key{ptr, esize, rows, cols, ld, box_cols, box_rows, swizzle};
+    const Key key{ptr, type, rows, cols, ld, box_cols, box_rows, swizzle};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
-    const CUtensorMap m = encode_map(ptr, esize, rows, cols, ld, box_cols, box_rows, swizzle);
+    const CUtensorMap m = encode_map(ptr, type, rows, cols, ld, box_cols, box_rows, swizzle);
     if (cache.size() > 4096) cache.clear();
     cache.emplace(key, m);
     return m;
 }
 
-// The six operand maps: A with box rows ra, B with box rows rb, BK columns each.
-Maps6 operand_maps(const SplitOperand& A, const SplitOperand& B, int ra, int rb, bool cache) {
+// The four operand maps: A with box rows ra, B with box rows rb, BK columns each.
+Maps4 operand_maps(const SplitOperand& A, const SplitOperand& B, int ra, int rb, bool cache) {
     auto mk = cache ? cached_map : encode_map;
-    Maps6 m;
+    Maps4 m;
     const SplitOperand* ops[2] = {&A, &B};
     for (int i = 0; i < 2; i++) {
         const SplitOperand& o = *ops[i];
         const int rows = i == 0 ? ra : rb;
-        m.m[3 * i] = mk(o.hi, 4, o.rows, o.cols, o.ld, BK, rows, true);
-        m.m[3 * i + 1] = mk(o.hb, 2, o.rows, o.cols, o.ld, BK, rows, true);
-        m.m[3 * i + 2] = mk(o.lb, 2, o.rows, o.cols, o.ld, BK, rows, true);
+        m.m[2 * i] = mk(o.h, MAP_F16, o.rows, o.cols, o.ld, BK, rows, true);
+        m.m[2 * i + 1] = mk(o.l, MAP_F16, o.rows, o.cols, o.ld, BK, rows, true);
     }
     return m;
 }
@@ -811,7 +809,7 @@ int sm_count() {
 }
 
 template <int BN>
-void launch_one(cudaStream_t s, const Maps6& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err,
+void launch_one(cudaStream_t s, const Maps4& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err,
                 int ksplit = 1, int Mp = 0) {
     using Cfg = GemmCfg<BN>;
     static std::atomic<unsigned long long> attr{0};
@@ -852,7 +850,7 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
         if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
         clusters_per_device[dev].store(max_clusters, std::memory_order_release);
     }
-    const Maps6 maps = operand_maps(A, B, BM, BN / 2, true);
+    const Maps4 maps = operand_maps(A, B, BM, BN / 2, true);
     const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + BN - 1) / BN);
     const int clusters = tiles < max_clusters ? tiles : max_clusters;
     // tail split: the R tiles of a partial last wave become R * split narrower tiles
@@ -866,9 +864,10 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err, full, split));
 }
 
-void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi& epi, int bn) {
-    if (K % BK) throw Error(13, "GEMM K must be a multiple of 32");
-    if (!A.hi || !A.hb || !A.lb || !B.hi || !B.hb || !B.lb) throw Error(13, "GEMM operand without all three parts");
+void check_shape(const SplitOperand& A, const SplitOperand& B, int K, int kb_per_tap, const Epi& epi, int bn) {
+    if (K % 32) throw Error(13, "GEMM K must be a multiple of 32");
+    if (kb_per_tap > 0 && K % BK) throw Error(13, "the implicit-conv GEMM needs K and its taps in blocks of 64");
+    if (!A.h || !A.l || !B.h || !B.l) throw Error(13, "GEMM operand without both fp16 parts");
     if (epi.mode == EPI_DENSE_OUT && (bn != 192 || epi.n2 > 8 || epi.tma))
         throw Error(9, "the fused dense+out_proj epilogue needs N == 192, at most 8 outputs and direct stores");
     if (epi.reduce && (epi.mode != EPI_STORE || !epi.tma))
@@ -879,23 +878,38 @@ void check_shape(const SplitOperand& A, const SplitOperand& B, int K, const Epi&
 
 }  // namespace
 
-CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld) {
-    return cached_map(p, 4, rows, cols, ld, 32, 32, true);
+float split_scale(double bound) {
+    if (!(bound > 0.0) || !std::isfinite(bound)) return 1.0f;
+    int e = (int)std::floor(std::log2(32768.0 / bound));
+    while (e > -60 && std::ldexp(bound, e) > 32768.0) e--;  // guard the log2 rounding
+    e = std::max(-60, std::min(60, e));
+    return (float)std::ldexp(1.0, e);
 }
 
-CUtensorMap make_store_map_bf16(const void* p, long long rows, long long cols, long long ld) {
-    return cached_map(p, 2, rows, cols, ld, 32, 32, true);
+CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld) {
+    return cached_map(p, MAP_F32, rows, cols, ld, 32, 32, true);
+}
+
+CUtensorMap make_store_map_f16(const void* p, long long rows, long long cols, long long ld) {
+    return cached_map(p, MAP_F16, rows, cols, ld, 32, 32, true);
 }
 
 CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
                           bool swizzle) {
     if (swizzle && box_cols != 64) throw Error(9, "bf16 map: the 128-byte swizzle needs 64-column boxes");
-    return cached_map(p, 2, rows, cols, ld, box_cols, box_rows, swizzle);
+    return cached_map(p, MAP_BF16, rows, cols, ld, box_cols, box_rows, swizzle);
 }
 
-void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
-                 const Epi& epi, int* err) {
+CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows) {
+    if (box_cols != 64) throw Error(9, "fp16 map: the 128-byte swizzle needs 64-column boxes");
+    return cached_map(p, MAP_F16, rows, cols, ld, box_cols, box_rows, true);
+}
+
+void gemm_split(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                const Epi& epi_in, int* err) {
     if (M <= 0 || N <= 0) return;
+    Epi epi = epi_in;
+    epi.acc_scale = (float)(1.0 / ((double)A.scale * (double)B.scale));
     int bn;
     if (epi.mode == EPI_DENSE_OUT || N == 192) {
         bn = 192;
@@ -910,11 +924,11 @@ void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     } else {
         bn = 64;
     }
-    check_shape(A, B, K, epi, bn == 512 ? 256 : bn);
+    check_shape(A, B, K, kb_per_tap, epi, bn == 512 ? 256 : bn);
     if ((bn == 64 || bn == 128) && epi.mode == EPI_STORE && epi.tma && epi.reduce && epi.split_ws && kb_per_tap == 0 &&
         N % 4 == 0 && epi.out && epi.ldo > 0) {
         // split K (2..4 ways, >= 4 k-blocks each) while the tiles still fit one wave
-        const int mt = (M + BM - 1) / BM, tiles = mt * ((N + bn - 1) / bn), nkb = K / BK, sms = sm_count();
+        const int mt = (M + BM - 1) / BM, tiles = mt * ((N + bn - 1) / bn), nkb = (K + BK - 1) / BK, sms = sm_count();
         int ks = 1;
         while (ks < 4 && tiles * (ks + 1) <= sms && nkb / (ks + 1) >= 4) ks++;
         const long long Mp = (long long)mt * BM;
@@ -946,10 +960,12 @@ void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
 
 // Same kernel (128-column tiles) with tensor maps encoded on the stack: no map cache,
 // so nothing is allocated on the host heap either (the allocation-free entry point).
-void gemm_split3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
-                            const Epi& epi, int* err) {
+void gemm_split_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                           const Epi& epi_in, int* err) {
     if (M <= 0 || N <= 0) return;
-    check_shape(A, B, K, epi, 128);
+    Epi epi = epi_in;
+    epi.acc_scale = (float)(1.0 / ((double)A.scale * (double)B.scale));
+    check_shape(A, B, K, 0, epi, 128);
     launch_one<128>(s, operand_maps(A, B, BM, 128, false), M, N, K, 0, epi, err);
 }
 

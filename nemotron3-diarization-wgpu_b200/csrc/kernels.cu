@@ -22,12 +22,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ---------------------------------------------------------------- LayerNorm
 // torch LayerNorm, eps 1e-5, two-pass population variance (src/tensor.rs:97-110).
 // One warp per row, VPL values per lane held in registers (128-bit loads).
-// Writes either a plain fp32 row (out.hb == nullptr) or the row's 3-term split.
+// Writes either a plain fp32 row (out.h == nullptr) or the fp16 split of row * out.scale.
 // x_out may alias x (in-place residual add): each lane reads its elements of x before
 // writing them, so neither is __restrict__.
 template <int VPL>
 __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
-                                  const float* __restrict__ b, Split3Out out) {
+                                  const float* __restrict__ b, SplitOut out) {
     griddep_wait();
     griddep_launch_dependents();
     constexpr int COLS = VPL * 32;
@@ -56,9 +56,9 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, c
     }
     const float var = __fdiv_rn(warp_sum(q), (float)COLS);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-    float* dst = out.hi + row * COLS;
-    uint16_t* dhb = out.hb ? static_cast<uint16_t*>(out.hb) + row * COLS : nullptr;
-    uint16_t* dlb = out.hb ? static_cast<uint16_t*>(out.lb) + row * COLS : nullptr;
+    float* dst = out.h ? nullptr : out.plain + row * COLS;
+    uint16_t* dh = out.h ? static_cast<uint16_t*>(out.h) + row * COLS : nullptr;
+    uint16_t* dl = out.h ? static_cast<uint16_t*>(out.l) + row * COLS : nullptr;
 #pragma unroll
     for (int i = 0; i < VPL; i += 4) {
         const int c = (i / 4) * 128 + lane * 4;
@@ -66,13 +66,11 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, c
 #pragma unroll
         for (int j = 0; j < 4; j++)
             y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i + j], mean), inv), w[c + j]), b[c + j]);
-        if (dhb) {
-            float h[4];
-            uint2 hb, lb;
-            split3x4(y, h, hb, lb);
-            *reinterpret_cast<float4*>(dst + c) = make_float4(h[0], h[1], h[2], h[3]);
-            *reinterpret_cast<uint2*>(dhb + c) = hb;
-            *reinterpret_cast<uint2*>(dlb + c) = lb;
+        if (dh) {
+            uint2 hw, lw;
+            split2x4(y, out.scale, hw, lw);
+            *reinterpret_cast<uint2*>(dh + c) = hw;
+            *reinterpret_cast<uint2*>(dl + c) = lw;
         } else {
             *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
         }
@@ -195,7 +193,7 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
     const float* __restrict__ audio, const MelSegDev* __restrict__ segs, int nsegs, long long f_first,
     long long n_frames, int hop, const float* __restrict__ window, const float* __restrict__ twiddle,
     const float* __restrict__ filters, const int* __restrict__ filt_lo, const int* __restrict__ filt_hi, float preemph,
-    Split3Out mel, float* __restrict__ mel_plain) {
+    SplitOut mel, float* __restrict__ mel_plain) {
     __shared__ float tw_s[NFFT];  // (cos, sin) pairs of the 256 twiddles
     __shared__ float win_s[NFFT];
     __shared__ float xs[MEL_WARPS][2][MEL_PAD];
@@ -301,30 +299,40 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
         for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(fw[k], pw[k]));
         const float v = (float)log((double)__fadd_rn(acc, 5.9604645e-8f));
         const long long o = orow + m;
-        if (mel.hi) {
-            float hv;
-            uint16_t hb, lb;
-            split3x1(v, hv, hb, lb);
-            mel.hi[o] = hv;
-            static_cast<uint16_t*>(mel.hb)[o] = hb;
-            static_cast<uint16_t*>(mel.lb)[o] = lb;
+        if (mel.h) {
+            uint32_t hw, lw;
+            split2x2(v, 0.0f, mel.scale, hw, lw);
+            static_cast<uint16_t*>(mel.h)[o] = (uint16_t)(hw & 0xffffu);
+            static_cast<uint16_t*>(mel.l)[o] = (uint16_t)(lw & 0xffffu);
         }
         if (mel_plain) mel_plain[o] = v;
     }
 }
 
 // Four elements per thread (n % 4 == 0, 16-byte aligned arrays).
-__global__ void split_kernel(const float* __restrict__ x, long long n4, Split3Out out) {
+__global__ void split_kernel(const float* __restrict__ x, long long n4, SplitOut out) {
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
         const float4 t = reinterpret_cast<const float4*>(x)[i];
         const float y[4] = {t.x, t.y, t.z, t.w};
-        float h[4];
-        uint2 hb, lb;
-        split3x4(y, h, hb, lb);
-        reinterpret_cast<float4*>(out.hi)[i] = make_float4(h[0], h[1], h[2], h[3]);
-        reinterpret_cast<uint2*>(out.hb)[i] = hb;
-        reinterpret_cast<uint2*>(out.lb)[i] = lb;
+        uint2 hw, lw;
+        split2x4(y, out.scale, hw, lw);
+        reinterpret_cast<uint2*>(out.h)[i] = hw;
+        reinterpret_cast<uint2*>(out.l)[i] = lw;
     }
+}
+
+// max |x| (as its bit pattern: non-negative floats order like their bits; NaN above
+// +inf) over n4 float4s into *d_max.
+__global__ void absmax_kernel(const float* __restrict__ x, long long n4, unsigned* __restrict__ d_max) {
+    unsigned m = 0;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 t = reinterpret_cast<const float4*>(x)[i];
+        m = max(m, max(max(__float_as_uint(t.x) & 0x7fffffffu, __float_as_uint(t.y) & 0x7fffffffu),
+                       max(__float_as_uint(t.z) & 0x7fffffffu, __float_as_uint(t.w) & 0x7fffffffu)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(d_max, m);
 }
 
 // Packs q | k | v per row; RoPE as src/encoder.rs:281-296 with explicit rounding.
@@ -426,12 +434,21 @@ void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const floa
     N3D_CUDA(cudaGetLastError());
 }
 
-void launch_split(cudaStream_t s, const float* x, long long n, Split3Out out) {
+void launch_split(cudaStream_t s, const float* x, long long n, SplitOut out) {
     if (n <= 0) return;
     if (n % 4) throw Error(13, "split: the element count must be a multiple of 4");
     const long long n4 = n / 4;
     const long long blocks = std::min<long long>((n4 + 255) / 256, 148LL * 16);
     split_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n4, out);
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max) {
+    if (n <= 0) return;
+    if (n % 4) throw Error(13, "absmax: the element count must be a multiple of 4");
+    const long long n4 = n / 4;
+    const long long blocks = std::min<long long>((n4 + 255) / 256, 148LL * 8);
+    absmax_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, n4, reinterpret_cast<unsigned*>(d_max));
     N3D_CUDA(cudaGetLastError());
 }
 
@@ -445,7 +462,7 @@ void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float
 }
 
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
-                       Split3Out out) {
+                       SplitOut out) {
     if (rows <= 0) return;
     const int warps = 8;
     const unsigned grid = (unsigned)((rows + warps - 1) / warps);
@@ -473,7 +490,7 @@ void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride
 
 void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
                 long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
-                const int* filt_lo, const int* filt_hi, float preemph, Split3Out mel, float* mel_plain) {
+                const int* filt_lo, const int* filt_hi, float preemph, SplitOut mel, float* mel_plain) {
     if (n_frames <= 0 || nsegs <= 0) return;
     const long long blocks = (n_frames + MEL_WARPS - 1) / MEL_WARPS;
     mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, segs, nsegs, f_first, n_frames, hop, window, twiddle,

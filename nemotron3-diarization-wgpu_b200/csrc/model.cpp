@@ -31,7 +31,7 @@ void cuda_check(cudaError_t e, const char* what) {
 namespace {
 
 // n3d_status codes (include/n3d.h); the checkpoint reader's own are in safetensors.h
-constexpr int kStatusIo = 1, kStatusJson = 2, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11,
+constexpr int kStatusIo = 1, kStatusJson = 2, kStatusShape = 6, kStatusAudio = 7, kStatusGpu = 9, kStatusTimeout = 11,
               kStatusNoDevice = 12, kStatusArg = 13, kStatusCuda = 10;
 
 std::string read_file(const std::string& path) {
@@ -65,24 +65,36 @@ double need_num(const json::Value& v, const char* key, const std::string& f) {
     return x.num;
 }
 
-// Round to the nearest bfloat16, ties to even: the host twin of cvt.rn.bf16.f32
-// (finite inputs).
-uint16_t bf16_rn_host(float x) {
-    uint32_t u;
-    std::memcpy(&u, &x, 4);
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
+// Magnitude bounds for the fp16-split scales (see DevLayer).
+double absmax_host(const float* p, size_t n) {
+    double m = 0.0;
+    for (size_t i = 0; i < n; i++) m = std::max(m, (double)std::fabs(p[i]));
+    return m;
 }
-
-// Round to the nearest TF32 (11 significant bits), ties away from zero: the
-// host twin of cvt.rna.tf32.f32.
-float tf32_rna_host(float x) {
-    uint32_t u;
-    std::memcpy(&u, &x, 4);
-    if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
-    float r;
-    std::memcpy(&r, &u, 4);
-    return r;
+// Largest row L1 norm of w [out, in].
+double row_l1_max(const float* w, long long out, long long in) {
+    double m = 0.0;
+    for (long long o = 0; o < out; o++) {
+        double a = 0.0;
+        for (long long i = 0; i < in; i++) a += std::fabs(w[o * in + i]);
+        m = std::max(m, a);
+    }
+    return m;
+}
+// |LayerNorm(x)| <= sqrt(cols - 1) max|w| + max|b|: a normalised element is at most
+// sqrt(cols - 1) standard deviations from the mean (population variance).
+double ln_bound(const float* w, const float* b, long long cols) {
+    return std::sqrt((double)(cols - 1)) * absmax_host(w, cols) + absmax_host(b, cols);
+}
+// |y| <= max over rows of (L1(w_row) * bound + |b|) for y = x w^T + b, |x| <= bound.
+double linear_bound(const float* w, const float* b, long long out, long long in, double bound) {
+    double m = 0.0;
+    for (long long o = 0; o < out; o++) {
+        double a = 0.0;
+        for (long long i = 0; i < in; i++) a += std::fabs(w[o * in + i]);
+        m = std::max(m, a * bound + (b ? std::fabs(b[o]) : 0.0));
+    }
+    return m;
 }
 
 // ------------------------------------------------------------- mel constants
@@ -398,26 +410,21 @@ void Model::upload_weights(const std::string& dir) {
         for (long long x : shape) n *= x;
         return dev(std::vector<float>(d, d + n));
     };
-    auto dev16 = [&](const std::vector<uint16_t>& v) {
-        void* p = nullptr;
-        N3D_CUDA(cudaMalloc(&p, v.size() * 2 + 16));
-        N3D_CUDA(cudaMemcpy(p, v.data(), v.size() * 2, cudaMemcpyHostToDevice));
-        owned_.push_back(p);
-        return p;
-    };
-    // weights in the 3-term split: hi = RN-TF32(w), hb = bf16(hi), lb = bf16(w - hi)
+    // weights in the fp16 split with a per-matrix scale: h + l = w s, s from max |w|;
+    // split on the device by the same kernel that splits activations
     auto split = [&](const std::vector<float>& w, int out, int in, const float* bias) {
-        std::vector<float> hi(w.size());
-        std::vector<uint16_t> hb(w.size()), lb(w.size());
-        for (size_t i = 0; i < w.size(); i++) {
-            hi[i] = tf32_rna_host(w[i]);
-            hb[i] = bf16_rn_host(hi[i]);
-            lb[i] = bf16_rn_host(w[i] - hi[i]);
-        }
         DevLinear L;
-        L.hi = dev(hi);
-        L.hb = dev16(hb);
-        L.lb = dev16(lb);
+        L.scale = split_scale(absmax_host(w.data(), w.size()));
+        float* tmp = nullptr;
+        N3D_CUDA(cudaMalloc(&tmp, w.size() * 4 + 16));
+        N3D_CUDA(cudaMemcpy(tmp, w.data(), w.size() * 4, cudaMemcpyHostToDevice));
+        for (void** p : {&L.h, &L.l}) {
+            N3D_CUDA(cudaMalloc(p, w.size() * 2 + 16));
+            owned_.push_back(*p);
+        }
+        launch_split(nullptr, tmp, (long long)w.size(), SplitOut{L.h, L.l, L.scale, nullptr});
+        N3D_CUDA(cudaDeviceSynchronize());
+        N3D_CUDA(cudaFree(tmp));
         L.out = out;
         L.in = in;
         if (bias) L.bias = dev(std::vector<float>(bias, bias + out));
@@ -429,7 +436,11 @@ void Model::upload_weights(const std::string& dir) {
         return split(std::vector<float>(w, w + (size_t)out * in), out, in, b);
     };
     const std::string P = "model.audio_tower";
+    if (h % 4 || hh % 64 || (c.sub * c.n_mels) % 32 || c.inter % 32)
+        throw Error(kStatusShape, "the GEMMs need hidden % 4, head hidden % 64, sub * n_mels % 32 and "
+                                  "intermediate % 32 to be 0");
     embed_ = linear(P + ".embedder.projection.weight", (int)h, c.sub * c.n_mels, nullptr);
+    s_mel_ = split_scale(89.0);  // ln of any finite float >= 2^-24 lies in [-16.7, 88.8]
     in_ln_w_ = plain(P + ".input_layer_norm.weight", {h});
     in_ln_b_ = plain(P + ".input_layer_norm.bias", {h});
     fin_ln_w_ = plain(P + ".layer_norm.weight", {h});
@@ -452,6 +463,13 @@ void Model::upload_weights(const std::string& dir) {
         L.o = linear(b + ".self_attn.o_proj.weight", (int)h, (int)h, (b + ".self_attn.o_proj.bias").c_str());
         L.fc1 = linear(b + ".mlp.fc1.weight", c.inter, (int)h, (b + ".mlp.fc1.bias").c_str());
         L.fc2 = linear(b + ".mlp.fc2.weight", (int)h, c.inter, (b + ".mlp.fc2.bias").c_str());
+        const double b1 = ln_bound(st.get(b + ".layer_norm1.weight", {h}), st.get(b + ".layer_norm1.bias", {h}), h);
+        const double b2 = ln_bound(st.get(b + ".layer_norm2.weight", {h}), st.get(b + ".layer_norm2.bias", {h}), h);
+        L.s_ln1 = split_scale(b1);
+        L.s_ln2 = split_scale(b2);
+        L.s_ctx = split_scale(row_l1_max(st.get(b + ".self_attn.v_proj.weight", {h, h}), h, h) * b1);
+        L.s_ffn = split_scale(linear_bound(st.get(b + ".mlp.fc1.weight", {c.inter, h}),
+                                           st.get(b + ".mlp.fc1.bias", {c.inter}), c.inter, h, b2));
         layers_.push_back(L);
     }
     proj_ = linear("model.proj.weight", (int)hh, (int)h, "model.proj.bias");
@@ -468,6 +486,16 @@ void Model::upload_weights(const std::string& dir) {
         conv_ = split(r, oc, (int)(3 * hh), b);
     }
     dense_ = linear("classifier.dense.weight", (int)hh, (int)hh, "classifier.dense.bias");
+    {
+        const double bf = ln_bound(st.get(P + ".layer_norm.weight", {h}), st.get(P + ".layer_norm.bias", {h}), h);
+        const double bp = linear_bound(st.get("model.proj.weight", {hh, h}), st.get("model.proj.bias", {hh}), hh, h, bf);
+        const long long oc = hh * c.sub;
+        const double bc = linear_bound(st.get("model.upsampler.conv.weight", {oc, hh, 3}),
+                                       st.get("model.upsampler.conv.bias", {oc}), oc, 3 * hh, bp);
+        s_fin_ = split_scale(bf);
+        s_proj_ = split_scale(bp);
+        s_conv_ = split_scale(bc);  // |relu(y)| <= |y|
+    }
     out_w_ = plain("classifier.out_proj.weight", {c.num_speakers, hh});
     out_b_ = plain("classifier.out_proj.bias", {c.num_speakers});
     silence_ = plain("silence_embeds", {h});
@@ -541,16 +569,24 @@ void* Model::ws(const char* name, size_t bytes) {
     return b.p;
 }
 
-Split3Buf Model::ws3(const std::string& base, long long rows, long long cols) {
-    Split3Buf b;
-    b.hi = (float*)ws((base + "_hi").c_str(), (size_t)rows * cols * 4);
-    b.hb = ws((base + "_hb").c_str(), (size_t)rows * cols * 2);
-    b.lb = ws((base + "_lb").c_str(), (size_t)rows * cols * 2);
+SplitBuf Model::ws2(const std::string& base, long long rows, long long cols) {
+    SplitBuf b;
+    b.h = ws((base + "_h").c_str(), (size_t)rows * cols * 2);
+    b.l = ws((base + "_l").c_str(), (size_t)rows * cols * 2);
     b.cols = cols;
-    b.rows_cap = std::min({(long long)(ws_[base + "_hi"].bytes / (cols * 4)),
-                           (long long)(ws_[base + "_hb"].bytes / (cols * 2)),
-                           (long long)(ws_[base + "_lb"].bytes / (cols * 2))});
+    b.rows_cap = std::min((long long)(ws_[base + "_h"].bytes / (cols * 2)),
+                          (long long)(ws_[base + "_l"].bytes / (cols * 2)));
     return b;
+}
+
+float Model::dyn_scale(const float* d, long long n) {
+    float* m = (float*)ws("absmax", 4);
+    N3D_CUDA(cudaMemsetAsync(m, 0, 4, stream_));
+    launch_absmax(stream_, d, n, m);
+    float hm = 0.0f;
+    N3D_CUDA(cudaMemcpyAsync(&hm, m, 4, cudaMemcpyDeviceToHost, stream_));
+    N3D_CUDA(cudaStreamSynchronize(stream_));
+    return split_scale(hm);
 }
 
 void Model::check_dev_error() {
@@ -643,7 +679,7 @@ void Model::prof_collect() {
 }
 
 // The 31-layer tower on B sequences of stride S rows (S a multiple of 8) held in
-// ws "win".  Output: the final LayerNorm in the 3-term split in ws "n" (and
+// ws "win".  Output: the final LayerNorm in the fp16 split in ws "n" (and
 // plain in enc_plain when given).  Residual adds are fused into the LayerNorm
 // that follows them, so every GEMM epilogue is a pure (TMA) store.
 void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float* enc_plain) {
@@ -651,7 +687,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     const long long M = (long long)B * S, h = c.hidden;
     float* win = (float*)ws("win", M * h * 4);
     float* x = (float*)ws("x", M * h * 4);
-    const Split3Buf n = ws3("n", M, h);  // LayerNorm output, 3-term split
+    const SplitBuf n = ws2("n", M, h);  // LayerNorm output, fp16 split
     // attention operands as bfloat16 pairs: Q, K [M, h]; V^T [h, M] (column = global row)
     AttnOperands ao;
     ao.q_hi = ws("q_hi", M * h * 2);
@@ -662,14 +698,14 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     ao.vt_hi = ws("vt_hi", h * M * 2);
     ao.vt_lo = ws("vt_lo", h * M * 2);
     ao.rows_cap = (long long)(ws_["q_hi"].bytes / (h * 2));
-    const Split3Buf ctx = ws3("ctx", M, h);     // attention context
-    const Split3Buf f = ws3("f", M, c.inter);   // GELU(fc1)
+    const SplitBuf ctx = ws2("ctx", M, h);     // attention context
+    const SplitBuf f = ws2("f", M, c.inter);   // GELU(fc1)
 
     Epi e;  // QKV: Q/K pairs with RoPE, V^T pair
     e.mode = EPI_QKV_ATTN;
     e.tma = 1;
-    e.map_out = make_bf16_map(ao.q_hi, M, h, h, 64, 32, true);
-    e.map_out2 = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
+    e.map_h = make_bf16_map(ao.q_hi, M, h, h, 64, 32, true);
+    e.map_l = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
     e.map_k_hi = make_bf16_map(ao.k_hi, M, h, h, 64, 32, true);
     e.map_k_lo = make_bf16_map(ao.k_lo, M, h, h, 64, 32, true);
     e.map_vt_hi = make_bf16_map(ao.vt_hi, h, M, ao.vt_ld, 32, 64, false);
@@ -687,53 +723,53 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     eo.map_out = make_store_map(x, M, h, h);
     eo.out = x;
     eo.ldo = h;
-    if (M <= 2048) {  // small launches may split K (gemm_split3): 4 partial [M rounded to 128, h] tiles
+    if (M <= 2048) {  // small launches may split K (gemm_split): 4 partial [M rounded to 128, h] tiles
         const long long mp = (M + 127) / 128 * 128;
         eo.split_ws = (float*)ws("split_ws", (size_t)4 * mp * h * 4);
         eo.split_ws_floats = 4 * mp * h;
     }
-    Epi e1;  // fc1: GELU(acc + bias) -> 3-term split
+    Epi e1;  // fc1: GELU(acc + bias) -> fp16 split
     e1.mode = EPI_GELU_SPLIT;
     e1.tma = 1;
-    e1.map_out = make_store_map(f.hi, M, c.inter, c.inter);
-    e1.map_out2 = make_store_map_bf16(f.hb, M, c.inter, c.inter);
-    e1.map_out3 = make_store_map_bf16(f.lb, M, c.inter, c.inter);
+    e1.map_h = make_store_map_f16(f.h, M, c.inter, c.inter);
+    e1.map_l = make_store_map_f16(f.l, M, c.inter, c.inter);
 
-    const double ln_bytes = (double)M * h * 12;  // read x, write hi, hb, lb
+    const double ln_bytes = (double)M * h * 8;  // read x, write h, l
     prof_begin();
-    launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, Split3Out{x, nullptr, nullptr});
+    launch_layer_norm(stream_, win, M, (int)h, in_ln_w_, in_ln_b_, plain_out(x));
     prof_end(K_LN, 0, (double)M * h * 8);
     for (int l = 0; l < c.layers; l++) {
         const DevLayer& L = layers_[l];
         prof_begin();
-        launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out());
+        launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out(L.s_ln1));
         prof_end(K_LN, 0, ln_bytes);
         prof_begin();
-        gemm_split3(stream_, n.op(), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
+        gemm_split(stream_, n.op(L.s_ln1), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);
         prof_begin();
-        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx.out(), dev_err_);
+        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx.out(L.s_ctx), dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
         eo.bias = L.o.bias;
         prof_begin();
-        gemm_split3(stream_, ctx.op(), L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
+        gemm_split(stream_, ctx.op(L.s_ctx), L.o.op(), (int)M, (int)h, (int)h, 0, eo, dev_err_);
         prof_end(K_GEMM_O, 2.0 * M * h * h, 0);
         prof_begin();
-        launch_layer_norm(stream_, x, M, (int)h, L.ln2_w, L.ln2_b, n.out());
+        launch_layer_norm(stream_, x, M, (int)h, L.ln2_w, L.ln2_b, n.out(L.s_ln2));
         prof_end(K_LN, 0, ln_bytes);
         e1.bias = L.fc1.bias;
+        e1.out_scale = L.s_ffn;
         prof_begin();
-        gemm_split3(stream_, n.op(), L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
+        gemm_split(stream_, n.op(L.s_ln2), L.fc1.op(), (int)M, c.inter, (int)h, 0, e1, dev_err_);
         prof_end(K_GEMM_FC1, 2.0 * M * c.inter * h, 0);
         eo.bias = L.fc2.bias;
         prof_begin();
-        gemm_split3(stream_, f.op(), L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
+        gemm_split(stream_, f.op(L.s_ffn), L.fc2.op(), (int)M, (int)h, c.inter, 0, eo, dev_err_);
         prof_end(K_GEMM_FC2, 2.0 * M * h * c.inter, 0);
     }
     prof_begin();
-    launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, n.out());
+    launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, n.out(s_fin_));
     prof_end(K_LN, 0, ln_bytes);
-    if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, Split3Out{enc_plain, nullptr, nullptr});
+    if (enc_plain) launch_layer_norm(stream_, x, M, (int)h, fin_ln_w_, fin_ln_b_, plain_out(enc_plain));
     (void)d_seq_len;
 }
 
@@ -742,22 +778,23 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
 // conv over it (its output keeps that padded row layout; the sub-pixel reshape
 // is free on row-major memory) -> dense + ReLU + out_proj fused.  Logits land
 // in ws "logits" with sequence i at rows i * (S + 2) * sub.
-void Model::head(int B, int S, const int* d_seq_len) {
+void Model::head(int B, int S, const int* d_seq_len, float widen) {
     const Config& c = cfg_;
     const long long M = (long long)B * S, h = c.hidden, hh = c.head_hidden, up = c.sub;
     const long long PR = (long long)B * (S + 2), MC = PR - 2;
-    const Split3Buf n = ws3("n", M, h);
-    const Split3Buf pb = ws3("p", PR, hh);        // proj output, zero-padded per sequence
-    const Split3Buf u = ws3("u", PR * up, hh);    // conv output as [8 rows per frame, hh]
+    const SplitBuf n = ws2("n", M, h);
+    const SplitBuf pb = ws2("p", PR, hh);        // proj output, zero-padded per sequence
+    const SplitBuf u = ws2("u", PR * up, hh);    // conv output as [8 rows per frame, hh]
     float* logits = (float*)ws("logits", PR * up * c.num_speakers * 4);
-    N3D_CUDA(cudaMemsetAsync(pb.hi, 0, PR * hh * 4, stream_));
-    N3D_CUDA(cudaMemsetAsync(pb.hb, 0, PR * hh * 2, stream_));
-    N3D_CUDA(cudaMemsetAsync(pb.lb, 0, PR * hh * 2, stream_));
+    N3D_CUDA(cudaMemsetAsync(pb.h, 0, PR * hh * 2, stream_));
+    N3D_CUDA(cudaMemsetAsync(pb.l, 0, PR * hh * 2, stream_));
     Epi ep;
     ep.mode = EPI_SPLIT;
-    ep.out = pb.hi;
-    ep.out2 = pb.hb;
-    ep.out3 = pb.lb;
+    ep.out_h = pb.h;
+    ep.out_l = pb.l;
+    // the input's scale is s_fin_ / widen; proj's and the conv's output bounds grow with it
+    const float s_in = s_fin_ / widen, s_p = s_proj_ / widen, s_u = s_conv_ / widen;
+    ep.out_scale = s_p;
     ep.ldo = hh;
     ep.bias = proj_.bias;
     ep.rdiv = S;
@@ -766,18 +803,19 @@ void Model::head(int B, int S, const int* d_seq_len) {
     ep.roff = 1;
     ep.seq_len = d_seq_len;
     prof_begin();
-    gemm_split3(stream_, n.op(), proj_.op(), (int)M, (int)hh, (int)h, 0, ep, dev_err_);
+    gemm_split(stream_, n.op(s_in), proj_.op(), (int)M, (int)hh, (int)h, 0, ep, dev_err_);
     prof_end(K_GEMM_PROJ, 2.0 * M * hh * h, 0);
     Epi ec;
     ec.mode = EPI_RELU_SPLIT;
     ec.tma = 1;
     ec.bias = conv_.bias;
-    ec.map_out = make_store_map(u.hi, MC, up * hh, up * hh);
-    ec.map_out2 = make_store_map_bf16(u.hb, MC, up * hh, up * hh);
-    ec.map_out3 = make_store_map_bf16(u.lb, MC, up * hh, up * hh);
+    ec.out_scale = s_u;
+    ec.map_h = make_store_map_f16(u.h, MC, up * hh, up * hh);
+    ec.map_l = make_store_map_f16(u.l, MC, up * hh, up * hh);
     prof_begin();
-    // k=3 conv: k-block kb (of 32) reads tap kb / 6, i.e. rows shifted by 0, 1, 2
-    gemm_split3(stream_, pb.op(), conv_.op(), (int)MC, (int)(up * hh), (int)(3 * hh), (int)(hh / 32), ec, dev_err_);
+    // k=3 conv: k-block kb (of 64) reads tap kb / (hh / 64), i.e. rows shifted by 0, 1, 2
+    gemm_split(stream_, pb.op(s_p), conv_.op(), (int)MC, (int)(up * hh), (int)(3 * hh), (int)(hh / 64), ec,
+               dev_err_);
     prof_end(K_GEMM_CONV, 2.0 * M * up * hh * 3 * hh, 0);
     Epi ed;
     ed.mode = EPI_DENSE_OUT;
@@ -788,7 +826,7 @@ void Model::head(int B, int S, const int* d_seq_len) {
     ed.b2 = out_b_;
     ed.n2 = c.num_speakers;
     prof_begin();
-    gemm_split3(stream_, u.op(), dense_.op(), (int)(MC * up), (int)hh, (int)hh, 0, ed, dev_err_);
+    gemm_split(stream_, u.op(s_u), dense_.op(), (int)(MC * up), (int)hh, (int)hh, 0, ed, dev_err_);
     prof_end(K_GEMM_DENSE, 2.0 * M * up * hh * hh + 2.0 * M * up * hh * c.num_speakers, 0);
 }
 
@@ -1066,10 +1104,9 @@ const float* Model::mel_launch(const float* d_audio, const MelJob& job,
     const Config& c = cfg_;
     const int h = c.hidden, sub = c.sub;
     const long long mel_rows = std::max(job.groups * sub, 1LL);
-    const Split3Buf mel = ws3("mel" + job.tag, mel_rows, c.n_mels);  // rows past a segment's frames stay zero
-    N3D_CUDA(cudaMemsetAsync(mel.hi, 0, mel_rows * c.n_mels * 4, stream_));
-    N3D_CUDA(cudaMemsetAsync(mel.hb, 0, mel_rows * c.n_mels * 2, stream_));
-    N3D_CUDA(cudaMemsetAsync(mel.lb, 0, mel_rows * c.n_mels * 2, stream_));
+    const SplitBuf mel = ws2("mel" + job.tag, mel_rows, c.n_mels);  // rows past a segment's frames stay zero
+    N3D_CUDA(cudaMemsetAsync(mel.h, 0, mel_rows * c.n_mels * 2, stream_));
+    N3D_CUDA(cudaMemsetAsync(mel.l, 0, mel_rows * c.n_mels * 2, stream_));
     if (job.frames > 0) {
         prof_begin();
         if (parts) {
@@ -1077,14 +1114,14 @@ const float* Model::mel_launch(const float* d_audio, const MelJob& job,
             for (const auto& pt : *parts) {
                 N3D_CUDA(cudaStreamWaitEvent(stream_, pt.second, 0));
                 launch_mel(stream_, d_audio, job.segs, job.nsegs, f0, pt.first - f0, c.hop, window_, twiddle_,
-                           mel_filters_, filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr);
+                           mel_filters_, filt_lo_, filt_hi_, c.preemph, mel.out(s_mel_), nullptr);
                 f0 = pt.first;
             }
         } else {
             launch_mel(stream_, d_audio, job.segs, job.nsegs, 0, job.frames, c.hop, window_, twiddle_, mel_filters_,
-                       filt_lo_, filt_hi_, c.preemph, mel.out(), nullptr);
+                       filt_lo_, filt_hi_, c.preemph, mel.out(s_mel_), nullptr);
         }
-        prof_end(K_MEL, 0, (double)job.frames * (c.hop * 4 + c.n_mels * 8));
+        prof_end(K_MEL, 0, (double)job.frames * (c.hop * 4 + c.n_mels * 4));
     }
     const long long K_emb = (long long)sub * c.n_mels;
     float* embeds = (float*)ws(("embeds" + job.tag).c_str(), std::max(job.groups, 1LL) * h * 4);
@@ -1094,9 +1131,9 @@ const float* Model::mel_launch(const float* d_audio, const MelJob& job,
         e.out = embeds;
         e.ldo = h;
         // the [rows, 128] mel viewed as [groups, 8 * 128]: 8 stacked frames per row
-        const SplitOperand A{mel.hi, mel.hb, mel.lb, mel.rows_cap / sub, K_emb, K_emb};
+        const SplitOperand A{mel.h, mel.l, mel.rows_cap / sub, K_emb, K_emb, s_mel_};
         prof_begin();
-        gemm_split3(stream_, A, embed_.op(), (int)job.groups, h, (int)K_emb, 0, e, dev_err_);
+        gemm_split(stream_, A, embed_.op(), (int)job.groups, h, (int)K_emb, 0, e, dev_err_);
         prof_end(K_GEMM_EMBED, 2.0 * job.groups * h * K_emb, 0);
     }
     return embeds;
@@ -1429,7 +1466,7 @@ int Model::log_mel(const float* samples, long long n, bool centered, std::vector
     float* pl = (float*)ws("mel_plain", frames * c.n_mels * 4);
     N3D_CUDA(cudaMemcpyAsync(d_seg, &seg, sizeof(MelSegDev), cudaMemcpyHostToDevice, stream_));
     launch_mel(stream_, a, d_seg, 1, 0, frames, c.hop, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph,
-               Split3Out{}, pl);
+               SplitOut{}, pl);
     N3D_CUDA(cudaMemcpyAsync(out.data(), pl, frames * c.n_mels * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));
     return (int)frames;
@@ -1444,15 +1481,16 @@ void Model::embed_range(const float* mel, long long num_frames, long long lo, lo
     const long long end = std::min(hi * c.sub, num_frames);
     if (lo * c.sub < end) std::memcpy(buf.data(), mel + lo * c.sub * c.n_mels, (end - lo * c.sub) * c.n_mels * 4);
     float* plain = (float*)ws("stage_in", groups * K * 4);
-    const Split3Buf sp = ws3("stage_split", groups, K);
+    const SplitBuf sp = ws2("stage_split", groups, K);
     float* o = (float*)ws("embeds", groups * c.hidden * 4);
     N3D_CUDA(cudaMemcpyAsync(plain, buf.data(), groups * K * 4, cudaMemcpyHostToDevice, stream_));
-    launch_split(stream_, plain, groups * K, sp.out());
+    const float sc = dyn_scale(plain, groups * K);  // caller data: scaled by its own max
+    launch_split(stream_, plain, groups * K, sp.out(sc));
     Epi e;
     e.mode = EPI_STORE;
     e.out = o;
     e.ldo = c.hidden;
-    gemm_split3(stream_, sp.op(), embed_.op(), (int)groups, c.hidden, (int)K, 0, e, dev_err_);
+    gemm_split(stream_, sp.op(sc), embed_.op(), (int)groups, c.hidden, (int)K, 0, e, dev_err_);
     N3D_CUDA(cudaMemcpyAsync(out, o, groups * c.hidden * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));
     check_dev_error();
@@ -1493,13 +1531,17 @@ void Model::head_forward(const float* enc, int frames, float* logits) {
     const int S = (frames + 7) / 8 * 8;
     const long long M = frames, h = c.hidden;
     float* plain = (float*)ws("enc_plain", (long long)S * h * 4);
-    const Split3Buf n = ws3("n", S, h);
+    const SplitBuf n = ws2("n", S, h);
     N3D_CUDA(cudaMemsetAsync(plain, 0, (long long)S * h * 4, stream_));
     N3D_CUDA(cudaMemcpyAsync(plain, enc, M * h * 4, cudaMemcpyHostToDevice, stream_));
-    launch_split(stream_, plain, (long long)S * h, n.out());
+    // caller data: scaled like the final LayerNorm's output when it respects that
+    // bound, else by a power of two more (and proj's and the conv's outputs with it)
+    const float sc = dyn_scale(plain, (long long)S * h);
+    const float widen = sc < s_fin_ ? s_fin_ / sc : 1.0f;
+    launch_split(stream_, plain, (long long)S * h, n.out(s_fin_ / widen));
     int* d_len = (int*)ws("seq_len", 4);
     N3D_CUDA(cudaMemcpyAsync(d_len, &frames, 4, cudaMemcpyHostToDevice, stream_));
-    head(1, S, d_len);
+    head(1, S, d_len, widen);
     N3D_CUDA(cudaMemcpyAsync(logits, ws("logits", 0), M * c.sub * c.num_speakers * 4, cudaMemcpyDeviceToHost,
                              stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));

@@ -40,30 +40,36 @@ Config load_config(const std::string& dir);
 
 // ----------------------------------------------------------------- weights
 
-// A linear layer's weight [out, in] in the 3-term split plus optional bias.
+// A linear layer's weight [out, in] in the fp16 split (scale s: h + l = w s) plus an
+// optional bias.
 struct DevLinear {
-    float* hi = nullptr;
-    void* hb = nullptr;
-    void* lb = nullptr;
+    void* h = nullptr;
+    void* l = nullptr;
     float* bias = nullptr;
     int out = 0, in = 0;
-    SplitOperand op() const { return SplitOperand{hi, hb, lb, out, in, in}; }
+    float scale = 1.0f;
+    SplitOperand op() const { return SplitOperand{h, l, out, in, in, scale}; }
 };
 
-// Workspace for an activation in the 3-term split (base_hi / base_hb / base_lb),
-// rows_cap = rows the buffers hold.
-struct Split3Buf {
-    float* hi = nullptr;
-    void* hb = nullptr;
-    void* lb = nullptr;
+// Workspace for an activation in the fp16 split (base_h / base_l), rows_cap = rows the
+// buffers hold.  The scale belongs to the producer and consumer of each use.
+struct SplitBuf {
+    void* h = nullptr;
+    void* l = nullptr;
     long long rows_cap = 0, cols = 0;
-    SplitOperand op() const { return SplitOperand{hi, hb, lb, rows_cap, cols, cols}; }
-    Split3Out out() const { return Split3Out{hi, hb, lb}; }
+    SplitOperand op(float scale) const { return SplitOperand{h, l, rows_cap, cols, cols, scale}; }
+    SplitOut out(float scale) const { return SplitOut{h, l, scale, nullptr}; }
 };
 
+// Per layer: LayerNorm parameters, weights, and the fp16-split scales of the layer's
+// GEMM inputs, each from a bound on the tensor's magnitude known at load: the two
+// LayerNorm outputs (sqrt(cols - 1) max|w| + max|b|), the attention context (a convex
+// combination of V rows: max row L1 norm of W_v times the LayerNorm bound) and
+// GELU(fc1) (|gelu(x)| <= |x|: max over rows of L1(W_fc1) times the bound plus |b|).
 struct DevLayer {
     float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
     DevLinear qkv, o, fc1, fc2;
+    float s_ln1 = 1.0f, s_ln2 = 1.0f, s_ctx = 1.0f, s_ffn = 1.0f;
 };
 
 // ----------------------------------------------------------------- schedule
@@ -210,7 +216,9 @@ class Model {
     // captured again after any workspace buffer is reallocated.  The step's key counts
     // go through fixed slot buffers so that one graph serves every step.
     void tower_step(int B, int S, const int* d_len, const int* d_valid);
-    void head(int B, int S, const int* d_seq_len);
+    // `widen` (a power of two >= 1) lowers the scales of the head's GEMM inputs below
+    // the final LayerNorm's for inputs that exceed its bound (head_forward's caller data).
+    void head(int B, int S, const int* d_seq_len, float widen = 1.0f);
     // Log-mel + embedder of `segs` (segment i's samples start at d_audio[base[i]]).
     // mel_prepare uploads the segment table (from host memory, so call it before the
     // stream is busy); mel_launch runs the mel and the embedder GEMM.  `parts`
@@ -236,7 +244,9 @@ class Model {
     void run_step(const SeqStep* d_steps, int B, int S, const int* d_len, const int* d_valid, const float* embeds);
     void session_round(std::vector<SessionChunk>& items, std::vector<std::vector<float>>& rows);
     void* ws(const char* name, size_t bytes);
-    Split3Buf ws3(const std::string& base, long long rows, long long cols);
+    SplitBuf ws2(const std::string& base, long long rows, long long cols);
+    // The fp16-split scale of n floats on the device from their max |x| (one readback).
+    float dyn_scale(const float* d, long long n);
     void check_dev_error();
 
     Config cfg_;
@@ -265,6 +275,10 @@ class Model {
     int* dev_err_ = nullptr;
 
     DevLinear embed_, proj_, conv_, dense_;
+    // fp16-split scales of the other GEMM inputs: the log-mel (|ln x| <= 89 for any
+    // finite positive x >= 2^-24), the final LayerNorm output, proj's output and the
+    // conv's ReLU output (row L1 bounds as for the layers).
+    float s_mel_ = 1.0f, s_fin_ = 1.0f, s_proj_ = 1.0f, s_conv_ = 1.0f;
     std::vector<DevLayer> layers_;
     float *in_ln_w_, *in_ln_b_, *fin_ln_w_, *fin_ln_b_;
     float *out_w_, *out_b_, *silence_;

@@ -1,6 +1,6 @@
 // Device-side helpers shared by every sm_100a kernel of the diarization path:
 // mbarriers with bounded waits, TMA tile loads (never multicast), tcgen05
-// (TMEM allocation, UMMA issue/commit, TMEM loads), packed f32 pairs and the 3-term operand split.
+// (TMEM allocation, UMMA issue/commit, TMEM loads), packed f32 pairs and the fp16 operand split.
 #pragma once
 
 #include <cstdint>
@@ -140,17 +140,19 @@ __device__ __forceinline__ uint64_t desc_k_sw64(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor for kind::tf32: D f32, A/B tf32, both K-major, M=128.
-__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
+// Instruction descriptor for kind::f16 with fp16 A and B: D f32, both K-major, M=128
+// (A/B format 0 = f16; 1 would be bf16).
+__host__ __device__ constexpr uint32_t idesc_f16(int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
 }
-
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+// kind::f16 MMA, A and B from shared memory (the same issue for fp16 and bf16 operands;
+// the instruction descriptor names the type).
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
@@ -206,17 +208,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
     reg_fence16(r);
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// MMA with the A operand in TMEM (K-major, one 32-bit element per column).
-__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
 }
 
 // Store 32 consecutive TMEM columns of this thread's lane (32x32b shape, x32);
@@ -285,25 +276,12 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
         "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
         : "memory");
 }
-// Instruction descriptor for a pair MMA: D f32, A/B tf32, K-major, M = 256.
-__host__ __device__ constexpr uint32_t idesc_tf32_pair(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((256u >> 4) << 24);
+// kind::f16 pair MMA with fp16 A and B: D f32, K-major, M = 256.
+__host__ __device__ constexpr uint32_t idesc_f16_pair(int n) {
+    return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((256u >> 4) << 24);
 }
-__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                               uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// kind::f16 pair MMA: D f32, A/B bf16, K-major, M = 256.
-__host__ __device__ constexpr uint32_t idesc_bf16_pair(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((256u >> 4) << 24);
-}
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                               uint32_t accumulate) {
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
@@ -356,17 +334,6 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
     return true;
 }
 
-// ------------------------------------------------------------ RN-TF32 rounding
-// Round-to-nearest TF32 with integer ops on the bit pattern: add half an ulp of the
-// 10-bit mantissa and clear the 13 dropped bits (nearest, ties away from zero, the
-// same bits as cvt.rna.tf32.f32 for finite inputs).  The conversion instruction
-// issues at a fraction of the integer rate, and the GEMM epilogues that split every
-// output element are bound by it.  Non-finite inputs stay non-finite (a NaN may come
-// out as Inf).
-__device__ __forceinline__ float tf32_rna(float x) {
-    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
-}
-
 // ------------------------------------------------------- packed f32 pairs
 // Two f32 in one 64-bit register: Blackwell's packed FMA / add / multiply issue two
 // lanes' worth of work per instruction, each half rounded as the scalar operation.
@@ -406,40 +373,44 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return r;
 }
 
-// ------------------------------------------------ 3-term operand split (GEMMs)
-// Every GEMM operand x is stored as hi = RN-TF32(x) (an fp32 array read by kind::tf32
-// MMAs) plus bf16 copies hb = RN-bf16(hi) and lb = RN-bf16(x - hi) (read by kind::f16
-// MMAs).  A dot product is then hi_x·hi_y (TF32) + hb_x·lb_y + lb_x·hb_y (BF16): the
-// cross terms are 2^-11 of the main one, so their bf16 rounding costs ~2^-20 relative,
-// while two of the three products run at the bf16 rate.
-__device__ __forceinline__ uint32_t bf16x2_rn(float a, float b) {  // a in the low half
+// ------------------------------------------------- fp16 operand split (GEMMs)
+// Every GEMM operand x is stored as two fp16 arrays of x * s, where s is a power of two
+// chosen per tensor (the scale keeps |x s| <= 2^15): h = RN-fp16(x s) and
+// l = RN-fp16(x s - h).  fp16 carries 11 significant bits, so h holds x to 2^-11 and
+// h + l to about 2^-22; a dot product h_x h_y + h_x l_y + l_x h_y (three kind::f16
+// MMAs into one fp32 accumulator, the dropped l_x l_y ~2^-22) is then as accurate as
+// 3xTF32 while every product runs at the 16-bit rate.  The epilogue multiplies the
+// accumulator by 1 / (s_x s_y), which is exact.
+__device__ __forceinline__ uint32_t f16x2_rn(float a, float b) {  // a in the low half
     uint32_t r;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
     return r;
 }
-// Two consecutive elements: hi values, and the bf16 pairs of hb and lb (a in the low half).
-__device__ __forceinline__ void split3x2(float a, float b, float& ha, float& hb, uint32_t& hbf, uint32_t& lbf) {
-    ha = tf32_rna(a);
-    hb = tf32_rna(b);
-    hbf = bf16x2_rn(ha, hb);
-    float la, lb;  // a - ha, b - hb in one packed FMA (exact: hi holds the leading bits)
-    unpack2(fma2(pack2(ha, hb), pack2(-1.0f, -1.0f), pack2(a, b)), la, lb);
-    lbf = bf16x2_rn(la, lb);
+__device__ __forceinline__ void f16x2_to_f32(uint32_t v, float& a, float& b) {
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(a), "=f"(b)
+        : "r"(v));
 }
-// One element: hi, and its hb / lb bf16 bits (one conversion for both).
-__device__ __forceinline__ void split3x1(float x, float& h, uint16_t& hb, uint16_t& lb) {
-    h = tf32_rna(x);
-    const uint32_t p = bf16x2_rn(h, __fsub_rn(x, h));
-    hb = (uint16_t)(p & 0xffffu);
-    lb = (uint16_t)(p >> 16);
+// Two consecutive elements (a in the low half of each word): h and l of (a s, b s).
+// x s - h is exact in fp32 (h agrees with x s in all but its last 13 bits).
+__device__ __forceinline__ void split2x2(float a, float b, float s, uint32_t& h, uint32_t& l) {
+    float as, bs;
+    unpack2(mul2(pack2(a, b), pack2(s, s)), as, bs);
+    h = f16x2_rn(as, bs);
+    float ha, hb;
+    f16x2_to_f32(h, ha, hb);
+    float la, lb;
+    unpack2(fma2(pack2(ha, hb), pack2(-1.0f, -1.0f), pack2(as, bs)), la, lb);
+    l = f16x2_rn(la, lb);
 }
-// Four consecutive elements: hi in h[4], hb / lb as 4 bf16 each (8 bytes).
-__device__ __forceinline__ void split3x4(const float* x, float* h, uint2& hbf, uint2& lbf) {
-    split3x2(x[0], x[1], h[0], h[1], hbf.x, lbf.x);
-    split3x2(x[2], x[3], h[2], h[3], hbf.y, lbf.y);
+// Four consecutive elements: h and l as 4 fp16 each (8 bytes).
+__device__ __forceinline__ void split2x4(const float* x, float s, uint2& h, uint2& l) {
+    split2x2(x[0], x[1], s, h.x, l.x);
+    split2x2(x[2], x[3], s, h.y, l.y);
 }
 
 // ------------------------------------------------------ 3xBF16 (kind::f16)
+// Attention operands are bfloat16 pairs (hi + lo, ~16 significant bits).
 // Instruction descriptor for kind::f16: D f32, A/B bf16, both K-major, M=128.
 __host__ __device__ constexpr uint32_t idesc_bf16(int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);

@@ -72,23 +72,28 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
 // ------------------------------------------------------------------ GEMM
 
 // Epilogue applied to each accumulator tile of C = A * B^T.
+// Every mode first forms v = acc * acc_scale + bias, where acc_scale = 1 / (s_A s_B)
+// undoes the operands' power-of-two scales (exact).
 enum EpiMode : int {
-    EPI_STORE = 0,       // out[r, c] = acc + bias                     (fp32)
-    EPI_SPLIT = 1,       // split3(acc + bias) -> out (hi), out2 (hb), out3 (lb)
-    EPI_GELU_SPLIT = 2,  // split3(gelu(acc + bias))
-    EPI_RELU_SPLIT = 4,  // split3(relu(acc + bias))
-    EPI_DENSE_OUT = 6,   // r = relu(acc + bias); out[r, 0:ns] = r . w2^T + b2
-    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_out / map_out2,
+    EPI_STORE = 0,       // out[r, c] = v                               (fp32)
+    EPI_SPLIT = 1,       // fp16 split of v * out_scale -> out_h, out_l
+    EPI_GELU_SPLIT = 2,  // fp16 split of gelu(v) * out_scale
+    EPI_RELU_SPLIT = 4,  // fp16 split of relu(v) * out_scale
+    EPI_DENSE_OUT = 6,   // r = relu(v); out[r, 0:ns] = r . w2^T + b2
+    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_h / map_l,
                          // map_k_*); V -> transposed bf16 pair V^T[head*64 + d][row] (map_vt_*); TMA only
 };
 
 struct Epi {
     int mode = EPI_STORE;
     const float* bias = nullptr;
-    // Direct stores: out (fp32 / hi), out2 and out3 (bf16 hb / lb of the split modes).
+    float acc_scale = 1.0f;  // set by gemm_split from the operands' scales
+    float out_scale = 1.0f;  // the split modes' output scale (the consumer operand's s)
+    // Direct stores: out (fp32, EPI_STORE and EPI_DENSE_OUT), out_h and out_l (the
+    // fp16 arrays of the split modes).
     float* out = nullptr;
-    void* out2 = nullptr;
-    void* out3 = nullptr;
+    void* out_h = nullptr;
+    void* out_l = nullptr;
     long long ldo = 0;
     // Row remap: q = r / rdiv, t = r % rdiv; rows with t >= rkeep are skipped;
     // the output row is q * rmul + t + roff.
@@ -103,9 +108,9 @@ struct Epi {
     int head_dim = 64;
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
     // Stores through TMA (tma != 0), box 32 columns x 32 rows: map_out fp32 (128-byte
-    // swizzle, make_store_map), map_out2 / map_out3 bf16 (64-byte swizzle,
-    // make_store_map_bf16).  EPI_QKV_ATTN: bf16 maps from make_bf16_map -- map_out /
-    // map_out2 and map_k_* with box 64 x 32 and the 128-byte swizzle, map_vt_* over
+    // swizzle, make_store_map), map_h / map_l fp16 (64-byte swizzle,
+    // make_store_map_f16).  EPI_QKV_ATTN: bf16 maps from make_bf16_map -- map_h /
+    // map_l (Q) and map_k_* with box 64 x 32 and the 128-byte swizzle, map_vt_* over
     // V^T [heads*64, rows] with box 32 x 64 and no swizzle.
     int tma = 0;
     // EPI_STORE through TMA only: add the tile into map_out's fp32 destination
@@ -117,50 +122,66 @@ struct Epi {
     // ((p0 + p1 + ...) + bias) into the destination in split order (deterministic).
     float* split_ws = nullptr;
     long long split_ws_floats = 0;
-    CUtensorMap map_out, map_out2, map_out3, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
+    CUtensorMap map_out, map_h, map_l, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
     const float* b2 = nullptr;
     int n2 = 0;
 };
 
-// A K-major operand in the 3-term split, [rows, cols] with row stride ld (elements,
-// shared by the three arrays): hi = RN-TF32(x) (fp32), hb = bf16(hi), lb = bf16(x - hi).
+// A K-major GEMM operand [rows, cols] in the fp16 split, row stride ld (elements,
+// shared by both arrays): for the logical fp32 values x and the operand's power-of-two
+// scale s, h = RN-fp16(x s) and l = RN-fp16(x s - h).
 struct SplitOperand {
-    const float* hi = nullptr;
-    const void* hb = nullptr;
-    const void* lb = nullptr;
+    const void* h = nullptr;
+    const void* l = nullptr;
     long long rows = 0, cols = 0, ld = 0;
+    float scale = 1.0f;
 };
 
+// The power-of-two scale for a tensor whose magnitudes are at most `bound`:
+// bound * s <= 2^15 (half the fp16 range), s as large as that allows, within
+// [2^-60, 2^60]; 1 for a zero or non-finite bound.
+float split_scale(double bound);
+
 // TMA-store maps (box 32 x 32) over a row-major fp32 matrix (128-byte swizzle) or
-// bf16 matrix (64-byte swizzle).
+// fp16 matrix (64-byte swizzle).
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
-CUtensorMap make_store_map_bf16(const void* p, long long rows, long long cols, long long ld);
+CUtensorMap make_store_map_f16(const void* p, long long rows, long long cols, long long ld);
 // 2-D map over a row-major bfloat16 matrix [rows, cols] with row stride ld elements;
 // box box_cols x box_rows, 128-byte swizzle when `swizzle` (box_cols must then be 64).
 CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
                           bool swizzle);
+// The same over an fp16 matrix, 128-byte swizzle (box_cols 64).
+CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows);
 
-// C[M, N] = A[M, K] * B[N, K]^T with the 3-term split on tcgen05 (gemm.cu).  K % 32 == 0.
-// `kb_per_tap` > 0 turns on the shifted-row (implicit k=3 conv) mode: k-block kb (of
-// 32) reads A at column (kb % kb_per_tap) * 32 and row m0 + kb / kb_per_tap.
-void gemm_split3(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
-                 const Epi& epi, int* dev_err);
+// C[M, N] = A[M, K] * B[N, K]^T with the fp16 split on tcgen05 (gemm.cu).  K % 32 == 0
+// (k-blocks of 64; a last half block reads zeros past K).  `kb_per_tap` > 0 turns on
+// the shifted-row (implicit k=3 conv) mode: k-block kb (of 64) reads A at column
+// (kb % kb_per_tap) * 64 and row m0 + kb / kb_per_tap.
+void gemm_split(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
+                const Epi& epi, int* dev_err);
 // Same with tensor maps encoded on the stack (no host allocation), 128 x 128 tiles.
-void gemm_split3_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
-                            const Epi& epi, int* dev_err);
+void gemm_split_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K,
+                           const Epi& epi, int* dev_err);
 
 // --------------------------------------------------------------- other kernels
-// Destination of a producer of GEMM operands: the three arrays of the 3-term split
-// (row stride = the producer's row length), or plain fp32 into `hi` when hb == nullptr.
-struct Split3Out {
-    float* hi = nullptr;
-    void* hb = nullptr;
-    void* lb = nullptr;
+// Destination of a producer of GEMM operands: the two fp16 arrays of the split of
+// x * scale (row stride = the producer's row length), or plain fp32 into `plain` when
+// h == nullptr.
+struct SplitOut {
+    void* h = nullptr;
+    void* l = nullptr;
+    float scale = 1.0f;
+    float* plain = nullptr;
 };
+inline SplitOut plain_out(float* p) {
+    SplitOut o;
+    o.plain = p;
+    return o;
+}
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
-                       Split3Out out);
+                       SplitOut out);
 // SIMT attention (head_dim 128 kernel probes): plain fp32 context.
 void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
                       int head_dim, float* ctx);
@@ -173,12 +194,14 @@ struct MelSegDev {
     int len, frame_lo, centered, pad;
 };
 // Log-mel of global frames [f_first, f_first + n_frames) of the segment table into
-// [rows, 128] outputs (3-term split, plain optional).
+// [rows, 128] outputs (fp16 split, plain optional).
 void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
                 long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
-                const int* filt_lo, const int* filt_hi, float preemph, Split3Out mel, float* mel_plain);
-// x -> its 3-term split, elementwise (n % 4 == 0).
-void launch_split(cudaStream_t s, const float* x, long long n, Split3Out out);
+                const int* filt_lo, const int* filt_hi, float preemph, SplitOut mel, float* mel_plain);
+// x -> the fp16 split of x * out.scale, elementwise (n % 4 == 0).
+void launch_split(cudaStream_t s, const float* x, long long n, SplitOut out);
+// max |x| over n floats (n % 4 == 0) into *d_max (a float the caller zeroes first).
+void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max);
 // Operands of the tcgen05 attention (head_dim 64), all bfloat16 hi/lo pairs:
 // Q, K [rows_cap, heads*64] with sequence b at rows b*S..; V^T [heads*64, vt_ld]
 // whose column is the global row.
@@ -189,9 +212,9 @@ struct AttnOperands {
     long long vt_ld = 0;
 };
 // tcgen05 attention (attention_tc.cu); S (when seqs > 1) and vt_ld must be multiples
-// of 8.  Context [seqs*S, heads*64] in the 3-term split (or plain fp32).
+// of 8.  Context [seqs*S, heads*64] in the fp16 split (or plain fp32).
 void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
-                         Split3Out ctx, int* err);
+                         SplitOut ctx, int* err);
 // q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
                       const float* cos_t, const float* sin_t, const AttnOperands& op);

@@ -1,6 +1,6 @@
 // Allocation-free variant of tensor::linear (src/tensor.rs:22-57) on the GPU.
 //
-// n3d_linear needs temporary device memory for the 3-term split (hi, hb, lb) of
+// n3d_linear needs temporary device memory for the fp16 split (h, l) of
 // its operands and gets it from cudaMalloc.  Some callers cannot allocate device
 // memory at the point where they call: a real-time audio thread that must not
 // block in the driver's allocator, a host framework that has reserved all of
@@ -11,10 +11,11 @@
 // allocating library routine, no host-heap map cache.
 //
 // Limits and sharing rules:
-//  * the scratch holds kScratchFloats fp32 values (16 MiB).  The split needs
-//    2 * (rows * cols + out * cols) of them (each part rounded up to 64
-//    floats), so rows * cols + out * cols may be at most ~2 Mi floats; larger
-//    requests are rejected with N3D_ERR_INVALID_ARGUMENT.
+//  * the scratch holds kScratchFloats 4-byte words (16 MiB).  The first 64 hold the
+//    two operands' max |x| (which set their fp16-split scales); the split of each
+//    operand takes n fp16 values twice, i.e. n words rounded up to 64, so
+//    rows * cols + out * cols may be at most 4 Mi - 64; larger requests are
+//    rejected with N3D_ERR_INVALID_ARGUMENT.
 //  * every GPU that loads the library holds these 16 MiB until the process
 //    exits.
 //  * all calls on a device share the one array and it keeps the last call's
@@ -70,21 +71,19 @@ DeviceSymbols symbols_for(int device) {
 
 size_t round64(size_t n) { return (n + 63) & ~size_t(63); }
 
-// One operand's 3-term split carved out of the scratch: hi (n floats), then hb and lb
-// (n bf16 each); every part starts on a 256-byte boundary.
+// One operand's fp16 split carved out of the scratch: h and l (n fp16 each), each
+// part starting on a 256-byte boundary; n words in all, rounded up to 64.
 struct Carve {
-    float* hi;
-    void* hb;
-    void* lb;
+    void* h;
+    void* l;
     float* next;
 };
 Carve carve(float* p, size_t n) {
-    const size_t nf = round64(n);  // floats, a multiple of 64 (256 bytes)
+    const size_t nf = round64(n);  // words, a multiple of 64 (256 bytes)
     Carve c;
-    c.hi = p;
-    c.hb = p + nf;
-    c.lb = p + nf + nf / 2;
-    c.next = p + 2 * nf;
+    c.h = p;
+    c.l = p + nf / 2;
+    c.next = p + nf;
     return c;
 }
 
@@ -102,27 +101,36 @@ void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, cons
     if (rows == 0 || out == 0) return;
     // each operand on its own first (rows * cols < 2^62 cannot wrap), so the sum below cannot wrap either
     const bool fits = rows * cols <= kScratchFloats && out * cols <= kScratchFloats;
-    const size_t need = fits ? 2 * round64(rows * cols) + 2 * round64(out * cols) : 0;  // hi + hb + lb per operand
+    const size_t need = fits ? 64 + round64(rows * cols) + round64(out * cols) : 0;  // maxima, then h + l per operand
     if (!fits || need > kScratchFloats)
         throw Error(13, "n3d_linear_noalloc: the request needs more scratch than the fixed " +
                             std::to_string(kScratchFloats) +
-                            " floats (rows*cols + out*cols must stay within about 2097152)");
+                            " words (rows*cols + out*cols must stay within 4194240)");
     N3D_CUDA(cudaSetDevice(device));
     const DeviceSymbols sym = symbols_for(device);
-    const Carve x = carve(sym.scratch, rows * cols);
+    float* maxima = sym.scratch;  // [0]: max |x|, [1]: max |w|
+    const Carve x = carve(sym.scratch + 64, rows * cols);
     const Carve w = carve(x.next, out * cols);
-    // the status word starts at zero for every call; the split arrays are fully overwritten
+    // the status word and the maxima start at zero for every call; the split arrays are
+    // fully overwritten
     N3D_CUDA(cudaMemsetAsync(sym.status, 0, sizeof(int), stream));
-    launch_split(stream, d_x, (long long)(rows * cols), Split3Out{x.hi, x.hb, x.lb});
-    launch_split(stream, d_w, (long long)(out * cols), Split3Out{w.hi, w.hb, w.lb});
+    N3D_CUDA(cudaMemsetAsync(maxima, 0, 2 * sizeof(float), stream));
+    launch_absmax(stream, d_x, (long long)(rows * cols), maxima);
+    launch_absmax(stream, d_w, (long long)(out * cols), maxima + 1);
+    float hm[2] = {0.0f, 0.0f};
+    N3D_CUDA(cudaMemcpyAsync(hm, maxima, sizeof(hm), cudaMemcpyDeviceToHost, stream));
+    N3D_CUDA(cudaStreamSynchronize(stream));
+    const float sx = split_scale(hm[0]), sw = split_scale(hm[1]);
+    launch_split(stream, d_x, (long long)(rows * cols), SplitOut{x.h, x.l, sx, nullptr});
+    launch_split(stream, d_w, (long long)(out * cols), SplitOut{w.h, w.l, sw, nullptr});
     Epi e;
     e.mode = EPI_STORE;
     e.bias = d_bias;
     e.out = d_y;
     e.ldo = (long long)out;
-    gemm_split3_stack_maps(stream, SplitOperand{x.hi, x.hb, x.lb, (long long)rows, (long long)cols, (long long)cols},
-                           SplitOperand{w.hi, w.hb, w.lb, (long long)out, (long long)cols, (long long)cols},
-                           (int)rows, (int)out, (int)cols, e, sym.status);
+    gemm_split_stack_maps(stream, SplitOperand{x.h, x.l, (long long)rows, (long long)cols, (long long)cols, sx},
+                          SplitOperand{w.h, w.l, (long long)out, (long long)cols, (long long)cols, sw},
+                          (int)rows, (int)out, (int)cols, e, sym.status);
     // read the status word back on the caller's stream only (one plain copy), so the call
     // waits for its own work and not for other streams of the device
     int status = 0;

@@ -519,7 +519,7 @@ def frame_duration(hop_length: int = 160, sampling_rate: int = 16000) -> float:
 
 
 def linear(device: int, d_x: int, rows: int, cols: int, d_w: int, out: int, d_bias: int | None, d_y: int) -> None:
-    """tensor::linear on device pointers (split TF32 + BF16 tcgen05 GEMM)."""
+    """tensor::linear on device pointers (fp16-split tcgen05 GEMM)."""
     _check(lib().n3d_linear(device, d_x, rows, cols, d_w, out, d_bias, d_y))
 
 
@@ -527,7 +527,7 @@ def linear_noalloc(device: int, d_x: int, rows: int, cols: int, d_w: int, out: i
                    stream: int | None = None) -> None:
     """tensor::linear for callers that cannot allocate device memory: the operand
     split uses the library's fixed 16 MiB device scratch (limit: rows*cols +
-    out*cols of about 2 Mi floats; calls overlapping on the GPU race)."""
+    out*cols at most 4194240; calls overlapping on the GPU race)."""
     _check(lib().n3d_linear_noalloc(device, d_x, rows, cols, d_w, out, d_bias, d_y, stream))
 
 

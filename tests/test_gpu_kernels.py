@@ -1,5 +1,5 @@
-"""Kernel-level parity on a B200 through the C ABI: the tcgen05 GEMM (3-term split:
-TF32 hi*hi + two BF16 cross terms),
+"""Kernel-level parity on a B200 through the C ABI: the tcgen05 GEMM (fp16 split:
+h*h + h*l + l*h with per-operand power-of-two scales),
 LayerNorm and RoPE+attention against the CPU oracle's restatement of
 src/tensor.rs and src/encoder.rs.
 
@@ -8,8 +8,8 @@ the kernel-sweep configuration (GEMM M in {1024, 4096, 16384} x K, N in
 {512..4096}, A ~ N(0,1), B ~ N(0,1/K) + bias; attention 8 heads, head_dim
 64/128, seq 512/1024/4096 with RoPE and a key mask; LayerNorm [16384 x 1024]).
 Tolerance: the sweep's 1e-3 max-abs gate (and the probes' 1e-3).  The GEMM
-lands orders of magnitude inside it (~2^-20 relative), which the tighter relative
-bound also checks; attention at head_dim 64 runs in 3xBF16 (~16 significant bits per
+lands orders of magnitude inside it (~2^-22 relative per product), which the tighter
+relative bound also checks; attention at head_dim 64 runs in 3xBF16 (~16 significant bits per
 operand), about 1e-4 from the fp32 oracle on these N(0,1) inputs.
 """
 
