@@ -343,6 +343,16 @@ n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, in
 n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head_dim, int iters, double *ms);
 n3d_status n3d_bench_layer_norm(int device, size_t rows, size_t cols, int iters, double *ms);
 
+/* Self-test of failure detection on the device, for a health check or a test: the
+ * reference has no device-side wait to bound (its error path only reports wgpu
+ * failures, src/gpu_engine.rs:1345-1349), while every wait of this library's kernels
+ * gives up after a limit, records where, and lets the kernel return.  This runs one
+ * such wait on `device` with a limit of `limit_ms` (0.001..2000) on a flag that
+ * nothing sets, exactly as an expired wait in a real kernel would: the call returns
+ * N3D_ERR_TIMEOUT, n3d_last_error() names the site, *waited_ms (nullable) receives the
+ * device time the wait took, and the device stays usable for the next call. */
+n3d_status n3d_selftest_wait_timeout(int device, double limit_ms, double *waited_ms);
+
 /* ------------------------------------------------------------- profiling */
 
 /* Device time per kernel class of the launches n3d_run_* make while profiling

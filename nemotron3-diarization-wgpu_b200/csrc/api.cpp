@@ -634,7 +634,6 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
         KernelCtx& k = kctx(device);
         std::lock_guard<std::mutex> turn(k.call);
         DevScratch sc;
-        float* qkv = sc.get(seq * 3 * heads * head_dim);
         float *cs = nullptr, *sn = nullptr;
         if (rope) {
             // rope_tables (src/encoder.rs:163-185), positions 0..seq-1
@@ -656,25 +655,39 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
         int v = (int)std::min(valid, seq);
         int* dv = (int*)sc.get(1);
         N3D_CUDA(cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, k.stream));
-        if (head_dim == 64) {
-            // tcgen05 path (the model's): operands as bfloat16 pairs, V transposed
-            const size_t W = heads * 64, vt_ld = (seq + 7) / 8 * 8;
-            n3d::AttnOperands op;
-            op.q_hi = sc.get(seq * W / 2);
-            op.q_lo = sc.get(seq * W / 2);
-            op.k_hi = sc.get(seq * W / 2);
-            op.k_lo = sc.get(seq * W / 2);
-            op.rows_cap = (long long)seq;
-            op.vt_hi = sc.get(W * vt_ld / 2);
-            op.vt_lo = sc.get(W * vt_ld / 2);
-            op.vt_ld = (long long)vt_ld;
-            n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, cs, sn, op);
-            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::plain_out(d_out), k.err);
-        } else {
-            n3d::launch_pack_qkv(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, qkv);
-            n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, d_out);
-        }
+        // tcgen05 path: operands as bfloat16 pairs, V transposed
+        const size_t W = heads * head_dim, vt_ld = (seq + 7) / 8 * 8;
+        n3d::AttnOperands op;
+        op.q_hi = sc.get(seq * W / 2);
+        op.q_lo = sc.get(seq * W / 2);
+        op.k_hi = sc.get(seq * W / 2);
+        op.k_lo = sc.get(seq * W / 2);
+        op.rows_cap = (long long)seq;
+        op.vt_hi = sc.get(W * vt_ld / 2);
+        op.vt_lo = sc.get(W * vt_ld / 2);
+        op.vt_ld = (long long)vt_ld;
+        n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, op);
+        n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, (int)head_dim, n3d::plain_out(d_out),
+                                 k.err);
         kcheck(k);
+    });
+}
+
+n3d_status n3d_selftest_wait_timeout(int device, double limit_ms, double* waited_ms) {
+    return guarded([&] {
+        arg_check(limit_ms >= 0.001 && limit_ms <= 2000.0, "n3d_selftest_wait_timeout: limit_ms outside 0.001..2000");
+        N3D_CUDA(cudaSetDevice(device));
+        KernelCtx& k = kctx(device);
+        std::lock_guard<std::mutex> turn(k.call);
+        DevScratch sc;
+        unsigned long long* d_waited = (unsigned long long*)sc.get(2);
+        N3D_CUDA(cudaMemsetAsync(d_waited, 0, 8, k.stream));
+        n3d::launch_wait_probe(k.stream, k.err, (unsigned long long)(limit_ms * 1e6), d_waited);
+        N3D_CUDA(cudaStreamSynchronize(k.stream));
+        unsigned long long ns = 0;
+        N3D_CUDA(cudaMemcpy(&ns, d_waited, 8, cudaMemcpyDeviceToHost));
+        if (waited_ms) *waited_ms = (double)ns / 1e6;
+        kcheck(k);  // the expired wait's status: N3D_ERR_TIMEOUT, and the word is cleared
     });
 }
 
@@ -823,28 +836,21 @@ n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head
         int vv = (int)seq;
         int* dv = (int*)sc.get(1);
         N3D_CUDA(cudaMemcpyAsync(dv, &vv, 4, cudaMemcpyHostToDevice, k.stream));
-        if (head_dim == 64) {
-            const size_t vt_ld = (seq + 7) / 8 * 8;
-            n3d::AttnOperands op;
-            op.q_hi = sc.get(seq * W / 2);
-            op.q_lo = sc.get(seq * W / 2);
-            op.k_hi = sc.get(seq * W / 2);
-            op.k_lo = sc.get(seq * W / 2);
-            op.rows_cap = (long long)seq;
-            op.vt_hi = sc.get(W * vt_ld / 2);
-            op.vt_lo = sc.get(W * vt_ld / 2);
-            op.vt_ld = (long long)vt_ld;
-            n3d::launch_pack_attn(k.stream, q, kk, v, (long long)seq, (int)heads, nullptr, nullptr, op);
-            *ms = time_launches(k, iters, [&] {
-                n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, n3d::plain_out(ctx), k.err);
-            });
-        } else {
-            float* qkv = sc.get(seq * 3 * W);
-            n3d::launch_pack_qkv(k.stream, q, kk, v, (long long)seq, (int)heads, (int)head_dim, nullptr, nullptr, qkv);
-            *ms = time_launches(k, iters, [&] {
-                n3d::launch_attention(k.stream, qkv, 1, (int)seq, dv, (int)heads, (int)head_dim, ctx);
-            });
-        }
+        const size_t vt_ld = (seq + 7) / 8 * 8;
+        n3d::AttnOperands op;
+        op.q_hi = sc.get(seq * W / 2);
+        op.q_lo = sc.get(seq * W / 2);
+        op.k_hi = sc.get(seq * W / 2);
+        op.k_lo = sc.get(seq * W / 2);
+        op.rows_cap = (long long)seq;
+        op.vt_hi = sc.get(W * vt_ld / 2);
+        op.vt_lo = sc.get(W * vt_ld / 2);
+        op.vt_ld = (long long)vt_ld;
+        n3d::launch_pack_attn(k.stream, q, kk, v, (long long)seq, (int)heads, (int)head_dim, nullptr, nullptr, op);
+        *ms = time_launches(k, iters, [&] {
+            n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, (int)head_dim, n3d::plain_out(ctx),
+                                     k.err);
+        });
     });
 }
 

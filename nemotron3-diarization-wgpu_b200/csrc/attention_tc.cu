@@ -1,4 +1,5 @@
-// Softmax attention on the sm_100a tensor cores (tcgen05, kind::f16), head_dim 64.
+// Softmax attention on the sm_100a tensor cores (tcgen05, kind::f16), head_dim 64
+// (the model's) or 128 (BASELINE config 1's kernel sweep).
 //
 // Replaces the reference's three attention dispatches -- `gemm_strided` QK^T,
 // `attn_sm` softmax with the key-padding mask, `gemm_n64` PV (src/gpu.rs:390-396,
@@ -11,9 +12,10 @@
 // this keeps the model's logits as close to the fp32 CPU path as 3xTF32 does
 // (max |diff| 5e-8 either way, measured by emulation on the synthetic
 // checkpoint), at half the tensor time and half the operand bytes, which lets
-// two CTAs share an SM.
+// two CTAs share an SM at head_dim 64.
 //
-// CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM:
+// CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM at head_dim
+// 64, one at 128 (its ring and TMEM are twice as large):
 //   warp 0      TMA: the CTA's Q pair into ring slot 2, then per block of 64 keys
 //               the K pair and the V^T pair into a 3-stage ring (two blocks of
 //               prefetch hide the load latency; slot 2 once Q has moved to TMEM)
@@ -31,8 +33,10 @@
 // P_j is released.  P values stay below 2^8; O / l is unchanged mathematically.
 // Context rows leave through shared memory (the ring, free once the last PV is done)
 // and TMA stores, a warp's 32 rows at a time.
-// TMEM (256 columns): S 0..63, P 64..127 (hi 64.., lo 96..), O 128..191,
-// Q 192..255 (hi 192.., lo 224..); bf16 operands two per 32-bit column.
+// TMEM: S 0..63, P 64..127 (hi 64.., lo 96..), O 128..128+HD-1, Q 128+HD..128+2HD-1
+// (hi first, then lo); bf16 operands two per 32-bit column.  256 columns at head_dim
+// 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of 64 columns (the
+// 128-byte swizzle's limit), as is the Q tile.
 // Barriers with a phase per key block
 // are double-buffered by block parity, so every waiter is at most one phase behind.
 // Every wait is bounded; an expired wait records its site in *err.
@@ -44,16 +48,28 @@ namespace n3d {
 
 namespace {
 
-constexpr int HD = 64;                    // head dim
 constexpr int QT = 128;                   // queries per CTA
 constexpr int KB = 64;                    // keys per block
-constexpr int KV_TILE = KB * 128;         // [64 rows x 64 bf16]: 8 KB
-constexpr int STAGE_BYTES = 4 * KV_TILE;  // K_hi, K_lo, V^T_hi, V^T_lo
+constexpr int BOX = KB * 128;             // one 64-column TMA box of 64 rows: 8 KB
 constexpr int THREADS = 192;
 constexpr int NSTAGE = 3;
-constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + 1024 + 256;
-constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128, COL_Q = 192, TMEM_COLS = 256;
+constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128;
 constexpr int DEV_TIMEOUT_ATTN = 5;
+
+template <int HD>
+struct AttnCfg {
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+    static constexpr int KTILE = KB * HD * 2;                  // K block [64 keys x HD] bf16
+    static constexpr int VTILE = HD * KB * 2;                  // V^T block [HD x 64 keys] bf16
+    static constexpr int STAGE_BYTES = 2 * KTILE + 2 * VTILE;  // K_hi, K_lo, V^T_hi, V^T_lo
+    static constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + 1024 + 256;
+    static constexpr uint32_t COL_Q = COL_O + HD, TMEM_COLS = HD == 64 ? 256 : 512;
+    static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
+    // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
+    static constexpr float K2 = (HD == 64 ? 0.125f : 0.0883883476483184f) * 1.4426950408889634f;
+    static_assert(2 * QT * HD * 2 == STAGE_BYTES, "the Q pair fills ring slot 2");
+    static_assert(4 * 32 * HD * 4 == STAGE_BYTES, "the context staging of the 4 softmax warps fills slot 0");
+};
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
 
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
@@ -100,9 +116,13 @@ struct AttnMaps {
     CUtensorMap ch, cl;      // context fp16 split h / l [rows, heads*64], box 64 x 32, 128-byte swizzle
 };
 
-__global__ void __launch_bounds__(THREADS, 2)
+template <int HD>
+__global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
     attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
                         SplitOut ctx, int ctx_tma, int* err) {
+    using Cfg = AttnCfg<HD>;
+    constexpr int STAGE_BYTES = Cfg::STAGE_BYTES, KTILE = Cfg::KTILE, VTILE = Cfg::VTILE;
+    constexpr uint32_t COL_Q = Cfg::COL_Q, TMEM_COLS = Cfg::TMEM_COLS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* stages = smem;
@@ -116,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     uint64_t* o_full = bars + 11;   // 2: PV_j committed (j % 2); a waiter for PV_j has always seen PV_{j-2}
     uint64_t* q_full = bars + 13;   // 1: the Q pair has landed in ring slot 2
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-    uint8_t* q_smem = stages + 2 * STAGE_BYTES;  // Q hi [128 rows x 128 B], Q lo 16 KB further
+    uint8_t* q_smem = stages + 2 * STAGE_BYTES;  // Q hi [HD/64 boxes of 128 rows x 128 B], then Q lo
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
@@ -150,9 +170,12 @@ __global__ void __launch_bounds__(THREADS, 2)
         if (lane == 0 && nblk > 0) {
             // Q rows past S belong to the next sequence (or lie past the buffer: zeros);
             // their context is never stored
-            mbar_arrive_expect_tx(q_full, 2 * QT * 128);
-            tma_load_2d(q_smem, &maps.qh, q_full, h * HD, row0 + q0);
-            tma_load_2d(q_smem + QT * 128, &maps.ql, q_full, h * HD, row0 + q0);
+            mbar_arrive_expect_tx(q_full, 2 * QT * HD * 2);
+#pragma unroll
+            for (int i = 0; i < HD / 64; i++) {
+                tma_load_2d(q_smem + i * QT * 128, &maps.qh, q_full, h * HD + 64 * i, row0 + q0);
+                tma_load_2d(q_smem + QT * HD * 2 + i * QT * 128, &maps.ql, q_full, h * HD + 64 * i, row0 + q0);
+            }
             int issued = 0;
             for (int j = 0; j < nblk; j++) {
                 const int st = j % NSTAGE;
@@ -164,10 +187,13 @@ __global__ void __launch_bounds__(THREADS, 2)
                 if (!ok) break;
                 uint8_t* sb = stages + st * STAGE_BYTES;
                 mbar_arrive_expect_tx(&kv_full[st], STAGE_BYTES);
-                tma_load_2d(sb, &maps.kh, &kv_full[st], h * HD, row0 + j * KB);
-                tma_load_2d(sb + KV_TILE, &maps.kl, &kv_full[st], h * HD, row0 + j * KB);
-                tma_load_2d(sb + 2 * KV_TILE, &maps.vh, &kv_full[st], row0 + j * KB, h * HD);
-                tma_load_2d(sb + 3 * KV_TILE, &maps.vl, &kv_full[st], row0 + j * KB, h * HD);
+#pragma unroll
+                for (int i = 0; i < HD / 64; i++) {
+                    tma_load_2d(sb + i * BOX, &maps.kh, &kv_full[st], h * HD + 64 * i, row0 + j * KB);
+                    tma_load_2d(sb + KTILE + i * BOX, &maps.kl, &kv_full[st], h * HD + 64 * i, row0 + j * KB);
+                }
+                tma_load_2d(sb + 2 * KTILE, &maps.vh, &kv_full[st], row0 + j * KB, h * HD);
+                tma_load_2d(sb + 2 * KTILE + VTILE, &maps.vl, &kv_full[st], row0 + j * KB, h * HD);
                 issued = j + 1;
             }
             mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);  // landed before the CTA may exit
@@ -178,18 +204,19 @@ __global__ void __launch_bounds__(THREADS, 2)
         }
     } else if (warp == 1) {
         if (lane == 0 && nblk > 0) {
-            constexpr uint32_t idesc = idesc_bf16(64);
+            constexpr uint32_t idesc_qk = idesc_bf16(KB), idesc_pv = idesc_bf16(HD);
             bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
             auto issue_qk = [&](int j) {
                 const uint32_t kb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES);
                 const uint32_t d = tmem + COL_S;
 #pragma unroll
-                for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at 32 + 8k
-                    const uint32_t off = k * 32;  // 16 bf16 = 32 bytes along the swizzled K rows
-                    const uint32_t qh = tmem + COL_Q + 8 * k, ql = qh + 32;
-                    umma_bf16_ts(d, ql, desc_k_sw128(kb + off), idesc, k != 0);
-                    umma_bf16_ts(d, qh, desc_k_sw128(kb + KV_TILE + off), idesc, 1);
-                    umma_bf16_ts(d, qh, desc_k_sw128(kb + off), idesc, 1);
+                for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at HD/2 + 8k
+                    // 16 bf16 = 32 bytes along the swizzled K rows, in box k / 4
+                    const uint32_t off = (k / 4) * BOX + (k % 4) * 32;
+                    const uint32_t qh = tmem + COL_Q + 8 * k, ql = qh + HD / 2;
+                    umma_bf16_ts(d, ql, desc_k_sw128(kb + off), idesc_qk, k != 0);
+                    umma_bf16_ts(d, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
+                    umma_bf16_ts(d, qh, desc_k_sw128(kb + off), idesc_qk, 1);
                 }
                 umma_commit(s_full);
             };
@@ -212,14 +239,14 @@ __global__ void __launch_bounds__(THREADS, 2)
                 }
                 if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
                 tc_fence_after();
-                const uint32_t vb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES + 2 * KV_TILE);
+                const uint32_t vb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES + 2 * KTILE);
                 const uint32_t pb = tmem + COL_P;
 #pragma unroll
                 for (int k = 0; k < KB / 16; k++) {  // keys 16k..16k+15: P_hi at column 8k, P_lo at 32 + 8k
                     const uint32_t off = k * 32;
-                    umma_bf16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc, j > 0 || k != 0);
-                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + KV_TILE + off), idesc, 1);
-                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc, 1);
+                    umma_bf16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc_pv, j > 0 || k != 0);
+                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + VTILE + off), idesc_pv, 1);
+                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc_pv, 1);
                 }
                 umma_commit(&o_full[j & 1]);
                 umma_commit(&kv_empty[j % NSTAGE]);
@@ -230,24 +257,27 @@ __global__ void __launch_bounds__(THREADS, 2)
         const int qd = warp & 3;
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-        const float k2 = 0.125f * 1.4426950408889634f;  // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
+        const float k2 = Cfg::K2;                        // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
         float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
         if (nblk > 0) {
-            // this row's Q pair (64 bf16 each, RoPE applied) from ring slot 2 (128-byte
-            // rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
+            // this row's Q pair (HD bf16 each, RoPE applied) from ring slot 2 (boxes of
+            // 128-byte rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
             ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN));
-            uint32_t qw[64];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int o = r * 128 + ((i ^ (r & 7)) << 4);
-                const uint4 a = *reinterpret_cast<const uint4*>(q_smem + o);
-                const uint4 c = *reinterpret_cast<const uint4*>(q_smem + QT * 128 + o);
-                qw[4 * i] = a.x, qw[4 * i + 1] = a.y, qw[4 * i + 2] = a.z, qw[4 * i + 3] = a.w;
-                qw[32 + 4 * i] = c.x, qw[32 + 4 * i + 1] = c.y, qw[32 + 4 * i + 2] = c.z, qw[32 + 4 * i + 3] = c.w;
+            for (int part = 0; part < 2; part++) {  // hi, then lo
+#pragma unroll
+                for (int box = 0; box < HD / 64; box++) {
+                    uint32_t qw[32];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int o = part * QT * HD * 2 + box * QT * 128 + r * 128 + ((i ^ (r & 7)) << 4);
+                        const uint4 a = *reinterpret_cast<const uint4*>(q_smem + o);
+                        qw[4 * i] = a.x, qw[4 * i + 1] = a.y, qw[4 * i + 2] = a.z, qw[4 * i + 3] = a.w;
+                    }
+                    tmem_st32u(lb + COL_Q + part * (HD / 2) + 32 * box, qw);
+                }
             }
-            tmem_st32u(lb + COL_Q, qw);
-            tmem_st32u(lb + COL_Q + 32, qw + 32);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -302,16 +332,19 @@ __global__ void __launch_bounds__(THREADS, 2)
                                 ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, raise)) {  // bring O to the new reference max
-                    float o[64];
-                    tmem_ld64(lb + COL_O, o);
                     const uint64_t c2 = pack2(corr, corr);
 #pragma unroll
-                    for (int d = 0; d < 64; d += 2) {
-                        uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
-                        unpack2(t, o[d], o[d + 1]);
+                    for (int cb = 0; cb < HD; cb += 64) {
+                        float o[64];
+                        tmem_ld64(lb + COL_O + cb, o);
+#pragma unroll
+                        for (int d = 0; d < 64; d += 2) {
+                            uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
+                            unpack2(t, o[d], o[d + 1]);
+                        }
+                        tmem_st32(lb + COL_O + cb, o);
+                        tmem_st32(lb + COL_O + cb + 32, o + 32);
                     }
-                    tmem_st32(lb + COL_O, o);
-                    tmem_st32(lb + COL_O + 32, o + 32);
                 }
             }
             tmem_st32u(lb + COL_P, hi);
@@ -321,61 +354,71 @@ __global__ void __launch_bounds__(THREADS, 2)
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[bf]);
         }
-        float o[64];
         if (nblk > 0) {
             ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err,
                                                          DEV_TIMEOUT_ATTN));
             tc_fence_after();
-            tmem_ld64(lb + COL_O, o);
         }
-        // ---- context rows: the fp16 split through TMA stores when all 32 rows of the
-        // warp belong to this sequence; otherwise (and for a plain fp32 context) per row
+        // ---- context rows, 64 columns at a time: the fp16 split through TMA stores when
+        // all 32 rows of the warp belong to this sequence; otherwise (and for a plain
+        // fp32 context) per row
         const int wrow0 = q0 + qd * 32;
-        if (ctx_tma && wrow0 + 32 <= S) {
-            // staging in ring slot 0 (every load has been consumed by the last PV):
-            // per warp 8 KB = h | l, 128-byte rows of 64 fp16
-            uint8_t* stg = stages + (warp - 2) * 8192;
-            const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
-            uint32_t hw[32], lw[32];
+        const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+        const bool via_tma = ctx_tma && wrow0 + 32 <= S;
+        // staging in ring slot 0 (every load has been consumed by the last PV): per warp
+        // HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
+        uint8_t* stg = stages + (warp - 2) * (HD * 128);
 #pragma unroll
-            for (int d = 0; d < 64; d += 2) {
-                const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
-                split2x2(x0, x1, ctx.scale, hw[d / 2], lw[d / 2]);
-            }
+        for (int cb = 0; cb < HD; cb += 64) {
+            float o[64];
+            if (nblk > 0) tmem_ld64(lb + COL_O + cb, o);
+            if (via_tma) {
+                uint32_t hw[32], lw[32];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int sw = ((i ^ (lane & 7)) << 4) + lane * 128;
-                *reinterpret_cast<uint4*>(stg + sw) = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
-                *reinterpret_cast<uint4*>(stg + 4096 + sw) =
-                    make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+                for (int d = 0; d < 64; d += 2) {
+                    const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
+                    split2x2(x0, x1, ctx.scale, hw[d / 2], lw[d / 2]);
+                }
+                uint8_t* bx = stg + (cb / 64) * 8192;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int sw = ((i ^ (lane & 7)) << 4) + lane * 128;
+                    *reinterpret_cast<uint4*>(bx + sw) = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+                    *reinterpret_cast<uint4*>(bx + 4096 + sw) =
+                        make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+                }
+            } else if (q0 + r < S) {
+                const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD + cb;
+#pragma unroll
+                for (int d = 0; d < 64; d += 4) {
+                    float x[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
+                    if (ctx.h) {
+                        uint2 hw, lw;
+                        split2x4(x, ctx.scale, hw, lw);
+                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.h) + off + d) = hw;
+                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.l) + off + d) = lw;
+                    } else {
+                        *reinterpret_cast<float4*>(ctx.plain + off + d) = make_float4(x[0], x[1], x[2], x[3]);
+                    }
+                }
             }
+        }
+        if (via_tma) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 const int y = row0 + wrow0;
-                tma_store_2d(&maps.ch, stg, h * HD, y);
-                tma_store_2d(&maps.cl, stg + 4096, h * HD, y);
+#pragma unroll
+                for (int cb = 0; cb < HD; cb += 64) {
+                    tma_store_2d(&maps.ch, stg + (cb / 64) * 8192, h * HD + cb, y);
+                    tma_store_2d(&maps.cl, stg + (cb / 64) * 8192 + 4096, h * HD + cb, y);
+                }
                 asm volatile("cp.async.bulk.commit_group;" ::: "memory");
                 asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read before exit
             }
             __syncwarp();
-        } else if (q0 + r < S) {
-            const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
-            const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD;
-#pragma unroll
-            for (int d = 0; d < 64; d += 4) {
-                float x[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
-                if (ctx.h) {
-                    uint2 hw, lw;
-                    split2x4(x, ctx.scale, hw, lw);
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.h) + off + d) = hw;
-                    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.l) + off + d) = lw;
-                } else {
-                    *reinterpret_cast<float4*>(ctx.plain + off + d) = make_float4(x[0], x[1], x[2], x[3]);
-                }
-            }
         }
     }
     tc_fence_before();
@@ -383,16 +426,14 @@ __global__ void __launch_bounds__(THREADS, 2)
     if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-}  // namespace
-
-void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
+template <int HD>
+void launch_attention_hd(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
                          SplitOut ctx, int* err) {
-    if (seqs <= 0 || S <= 0) return;
-    if ((seqs > 1 && S % 8) || op.vt_ld % 8)
-        throw Error(9, "attention: the sequence stride and the V^T row stride must be multiples of 8");
+    using Cfg = AttnCfg<HD>;
     static std::atomic<unsigned long long> attr{0};
     once_per_device(attr, [] {
-        N3D_CUDA(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        N3D_CUDA(cudaFuncSetAttribute(attention_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM_BYTES));
     });
     const long long W = (long long)heads * HD, rows = (long long)seqs * S;
     AttnMaps m;
@@ -410,7 +451,23 @@ void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S
         m.ch = m.cl = m.qh;  // unused
     }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
-    launch_pdl(attention_tc_kernel, grid, dim3(THREADS), SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma, err);
+    launch_pdl(attention_tc_kernel<HD>, grid, dim3(THREADS), Cfg::SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma,
+               err);
+}
+
+}  // namespace
+
+void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads, int hd,
+                         SplitOut ctx, int* err) {
+    if (seqs <= 0 || S <= 0) return;
+    if ((seqs > 1 && S % 8) || op.vt_ld % 8)
+        throw Error(9, "attention: the sequence stride and the V^T row stride must be multiples of 8");
+    if (hd == 64)
+        launch_attention_hd<64>(s, op, seqs, S, valid, heads, ctx, err);
+    else if (hd == 128)
+        launch_attention_hd<128>(s, op, seqs, S, valid, heads, ctx, err);
+    else
+        throw Error(13, "attention: head_dim must be 64 or 128");
 }
 
 }  // namespace n3d

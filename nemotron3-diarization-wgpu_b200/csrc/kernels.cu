@@ -1,5 +1,5 @@
-// Memory-bound and small kernels of the diarization path: LayerNorm, softmax
-// attention, and the fused log-mel front-end.
+// Memory-bound and small kernels of the diarization path: LayerNorm, the fused
+// log-mel front-end, the operand split and the attention operand packing.
 
 #include <cuda_bf16.h>
 #include <algorithm>
@@ -75,91 +75,6 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, c
             *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
         }
     }
-}
-
-// ---------------------------------------------------------------- attention
-// Softmax attention over the first valid[b] keys of each sequence
-// (src/encoder.rs:302-329): scores q.k * hd^-1/2, online softmax over key tiles
-// of 32 staged in shared memory, one query row per thread.  qkv is
-// [seqs * seq_stride, 3 * heads * HD] = Q | K | V (Q and K already rotated);
-// ctx is written in fp32 [seqs * seq_stride, heads * HD].
-template <int HD>
-__global__ void __launch_bounds__(128) attention_kernel(const float* __restrict__ qkv, int seq_stride,
-                                                        const int* __restrict__ valid_arr, int heads,
-                                                        float* __restrict__ ctx) {
-    constexpr int KT = 32;
-    __shared__ __align__(16) float ks[KT][HD];
-    __shared__ __align__(16) float vs[KT][HD];
-    const int b = blockIdx.z, h = blockIdx.y;
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    const int width = 3 * heads * HD;
-    const int valid = valid_arr[b];
-    const long long base = (long long)b * seq_stride;
-    const bool active = t < seq_stride;
-    const float scaling = 1.0f / sqrtf((float)HD);
-
-    float q[HD], o[HD];
-    if (active) {
-        const float* qr = qkv + (base + t) * width + h * HD;
-#pragma unroll
-        for (int d = 0; d < HD; d += 4) {
-            const float4 v4 = *reinterpret_cast<const float4*>(qr + d);
-            q[d] = v4.x;
-            q[d + 1] = v4.y;
-            q[d + 2] = v4.z;
-            q[d + 3] = v4.w;
-        }
-    }
-#pragma unroll
-    for (int d = 0; d < HD; d++) o[d] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
-
-    for (int k0 = 0; k0 < valid; k0 += KT) {
-        const int nk = min(KT, valid - k0);
-        for (int i = threadIdx.x; i < KT * HD / 4; i += blockDim.x) {
-            const int j = i / (HD / 4), d = (i % (HD / 4)) * 4;
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (j < nk) {
-                const float* row = qkv + (base + k0 + j) * width;
-                kv = *reinterpret_cast<const float4*>(row + heads * HD + h * HD + d);
-                vv = *reinterpret_cast<const float4*>(row + 2 * heads * HD + h * HD + d);
-            }
-            *reinterpret_cast<float4*>(&ks[j][d]) = kv;
-            *reinterpret_cast<float4*>(&vs[j][d]) = vv;
-        }
-        __syncthreads();
-        if (active) {
-            float s[KT];
-            float mt = m;
-#pragma unroll
-            for (int j = 0; j < KT; j++) {
-                float acc = 0.0f;
-#pragma unroll
-                for (int d = 0; d < HD; d++) acc = fmaf(q[d], ks[j][d], acc);
-                s[j] = j < nk ? acc * scaling : -INFINITY;
-                mt = fmaxf(mt, s[j]);
-            }
-            const float corr = expf(m - mt);
-            l *= corr;
-#pragma unroll
-            for (int d = 0; d < HD; d++) o[d] *= corr;
-#pragma unroll
-            for (int j = 0; j < KT; j++) {
-                const float p = j < nk ? expf(s[j] - mt) : 0.0f;
-                l += p;
-#pragma unroll
-                for (int d = 0; d < HD; d++) o[d] = fmaf(p, vs[j][d], o[d]);
-            }
-            m = mt;
-        }
-        __syncthreads();
-    }
-    if (!active) return;
-    const float inv = valid > 0 ? 1.0f / l : 0.0f;
-    float* dh = ctx + (base + t) * (heads * HD) + h * HD;
-#pragma unroll
-    for (int d = 0; d < HD; d += 4)
-        *reinterpret_cast<float4*>(dh + d) = make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
 }
 
 // ------------------------------------------------------------------- log-mel
@@ -335,49 +250,19 @@ __global__ void absmax_kernel(const float* __restrict__ x, long long n4, unsigne
     if ((threadIdx.x & 31) == 0) atomicMax(d_max, m);
 }
 
-// Packs q | k | v per row; RoPE as src/encoder.rs:281-296 with explicit rounding.
-__global__ void pack_qkv_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                const float* __restrict__ v, long long seq, int heads, int hd,
-                                const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                float* __restrict__ qkv) {
-    const long long W = (long long)heads * hd;
-    for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < seq * W;
-         e += (long long)gridDim.x * blockDim.x) {
-        const long long r = e / W;
-        const int c = (int)(e % W), d = c % hd, half = hd / 2;
-        float qo = q[e], ko = k[e];
-        if (cos_t) {
-            const float* cs = cos_t + r * hd;
-            const float* sn = sin_t + r * hd;
-            const long long pe = d < half ? e + half : e - half;
-            if (d < half) {
-                qo = __fsub_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
-                ko = __fsub_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
-            } else {
-                qo = __fadd_rn(__fmul_rn(q[e], cs[d]), __fmul_rn(q[pe], sn[d]));
-                ko = __fadd_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
-            }
-        }
-        float* row = qkv + r * 3 * W;
-        row[c] = qo;
-        row[W + c] = ko;
-        row[2 * W + c] = v[e];
-    }
-}
-
 // Kernel-level attention operands: RoPE'd Q and K as bfloat16 pairs, V transposed as a pair.
 __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
     hi = __float2bfloat16_rn(x);
     lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
 }
 __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __restrict__ k,
-                                 const float* __restrict__ v, long long seq, int heads,
+                                 const float* __restrict__ v, long long seq, int heads, int hd,
                                  const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                  __nv_bfloat16* __restrict__ q_hi, __nv_bfloat16* __restrict__ q_lo,
                                  __nv_bfloat16* __restrict__ k_hi, __nv_bfloat16* __restrict__ k_lo,
                                  __nv_bfloat16* __restrict__ vt_hi, __nv_bfloat16* __restrict__ vt_lo,
                                  long long vt_ld) {
-    const int hd = 64, half = 32;
+    const int half = hd / 2;
     const long long W = (long long)heads * hd;
     for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < seq * W;
          e += (long long)gridDim.x * blockDim.x) {
@@ -420,15 +305,43 @@ __global__ void fill_random_kernel(float* __restrict__ p, long long n, uint32_t 
     }
 }
 
+// Self-test of the bounded waits (failure detection without a fault): one warp
+// allocates TMEM as the tensor-core kernels do, arms an mbarrier for a 1 KB transfer
+// that is never issued -- a flag nothing sets -- and waits on it with the production
+// wait, limited to limit_ns.  The wait gives up, records DEV_TIMEOUT_PROBE in *err
+// like any expired wait, the warp frees its TMEM and the kernel returns, leaving the
+// context usable.  waited[0] receives the wait's duration in ns (globaltimer).
+__global__ void __launch_bounds__(32) wait_probe_kernel(int* __restrict__ err, unsigned long long limit_ns,
+                                                        unsigned long long* __restrict__ waited) {
+    __shared__ uint64_t bar;
+    __shared__ uint32_t tmem_slot;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    tmem_alloc(&tmem_slot, 32);
+    tc_fence_after();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, 1024);  // the phase completes only when 1 KB arrives: never
+        const uint64_t t0 = globaltimer_ns();
+        const bool ok = mbar_wait(&bar, 0, err, DEV_TIMEOUT_PROBE, limit_ns);
+        *waited = ok ? 0ull : globaltimer_ns() - t0;
+    }
+    tc_fence_before();
+    __syncwarp();
+    tmem_dealloc(tmem_slot, 32);
+}
+
 }  // namespace
 
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                      const float* cos_t, const float* sin_t, const AttnOperands& op) {
+                      int hd, const float* cos_t, const float* sin_t, const AttnOperands& op) {
     using bf = __nv_bfloat16;
-    const long long n = seq * heads * 64;
+    const long long n = seq * heads * hd;
     if (n <= 0) return;
     const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
-    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, cos_t, sin_t, (bf*)op.q_hi, (bf*)op.q_lo,
+    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, hd, cos_t, sin_t, (bf*)op.q_hi, (bf*)op.q_lo,
                                                       (bf*)op.k_hi, (bf*)op.k_lo, (bf*)op.vt_hi, (bf*)op.vt_lo,
                                                       op.vt_ld);
     N3D_CUDA(cudaGetLastError());
@@ -452,15 +365,6 @@ void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max) {
     N3D_CUDA(cudaGetLastError());
 }
 
-void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                     int hd, const float* cos_t, const float* sin_t, float* qkv) {
-    const long long n = seq * heads * hd;
-    if (n <= 0) return;
-    const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
-    pack_qkv_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, hd, cos_t, sin_t, qkv);
-    N3D_CUDA(cudaGetLastError());
-}
-
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
                        SplitOut out) {
     if (rows <= 0) return;
@@ -472,19 +376,6 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
         launch_pdl(layer_norm_kernel<32>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
-    N3D_CUDA(cudaGetLastError());
-}
-
-void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
-                      int head_dim, float* ctx) {
-    if (seqs <= 0 || seq_stride <= 0) return;
-    dim3 grid((seq_stride + 127) / 128, heads, seqs);
-    if (head_dim == 64)
-        attention_kernel<64><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx);
-    else if (head_dim == 128)
-        attention_kernel<128><<<grid, 128, 0, s>>>(qkv, seq_stride, valid, heads, ctx);
-    else
-        throw Error(13, "attention supports head_dim 64 or 128");
     N3D_CUDA(cudaGetLastError());
 }
 
@@ -502,6 +393,11 @@ void launch_fill_random(cudaStream_t s, float* p, long long n, uint32_t seed, fl
     if (n <= 0) return;
     const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
     fill_random_kernel<<<(unsigned)blocks, 256, 0, s>>>(p, n, seed, scale);
+    N3D_CUDA(cudaGetLastError());
+}
+
+void launch_wait_probe(cudaStream_t s, int* err, unsigned long long limit_ns, unsigned long long* waited) {
+    wait_probe_kernel<<<1, 32, 0, s>>>(err, limit_ns, waited);
     N3D_CUDA(cudaGetLastError());
 }
 

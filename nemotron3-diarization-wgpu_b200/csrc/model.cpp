@@ -747,7 +747,7 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         gemm_split(stream_, n.op(L.s_ln1), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);
         prof_begin();
-        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, ctx.out(L.s_ctx), dev_err_);
+        launch_attention_tc(stream_, ao, B, S, d_valid, c.heads, (int)(h / c.heads), ctx.out(L.s_ctx), dev_err_);
         prof_end(K_ATTN, 4.0 * B * (double)S * S * h, 0);
         eo.bias = L.o.bias;
         prof_begin();

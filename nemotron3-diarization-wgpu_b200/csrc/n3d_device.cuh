@@ -17,6 +17,8 @@ enum DevError : int {
     DEV_TIMEOUT_TMA_FULL = 2,
     DEV_TIMEOUT_ACC = 3,
     DEV_BAD_SHAPE = 4,
+    // 5: the attention kernel's waits (attention_tc.cu)
+    DEV_TIMEOUT_PROBE = 6,  // the wait self-test (n3d_selftest_wait_timeout)
 };
 
 // ~2 s of wall time, far above any legitimate wait in these kernels.
@@ -54,12 +56,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and records `code`) after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Bounded wait: returns false (and records `code`) after limit_ns (kWaitLimitNs unless
+// the wait self-test asks for less).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             if (err) atomicExch(err, code);
             return false;
         }

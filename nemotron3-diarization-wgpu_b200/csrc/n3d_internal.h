@@ -182,9 +182,6 @@ inline SplitOut plain_out(float* p) {
 }
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
                        SplitOut out);
-// SIMT attention (head_dim 128 kernel probes): plain fp32 context.
-void launch_attention(cudaStream_t s, const float* qkv, int seqs, int seq_stride, const int* valid, int heads,
-                      int head_dim, float* ctx);
 // One mel segment of a launch: global frames [f_begin, next segment's f_begin) are
 // frames frame_lo.. of a segment whose `len` samples start at audio[base]; frame t
 // reads samples t * hop - (centered ? 256 : 0) + [0, 512) (zeros outside [0, len))
@@ -202,8 +199,8 @@ void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int n
 void launch_split(cudaStream_t s, const float* x, long long n, SplitOut out);
 // max |x| over n floats (n % 4 == 0) into *d_max (a float the caller zeroes first).
 void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max);
-// Operands of the tcgen05 attention (head_dim 64), all bfloat16 hi/lo pairs:
-// Q, K [rows_cap, heads*64] with sequence b at rows b*S..; V^T [heads*64, vt_ld]
+// Operands of the tcgen05 attention (head_dim hd = 64 or 128), all bfloat16 hi/lo
+// pairs: Q, K [rows_cap, heads*hd] with sequence b at rows b*S..; V^T [heads*hd, vt_ld]
 // whose column is the global row.
 struct AttnOperands {
     const void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr;
@@ -211,21 +208,22 @@ struct AttnOperands {
     const void *vt_hi = nullptr, *vt_lo = nullptr;
     long long vt_ld = 0;
 };
-// tcgen05 attention (attention_tc.cu); S (when seqs > 1) and vt_ld must be multiples
-// of 8.  Context [seqs*S, heads*64] in the fp16 split (or plain fp32).
+// tcgen05 attention (attention_tc.cu), head_dim 64 or 128; S (when seqs > 1) and
+// vt_ld must be multiples of 8.  Context [seqs*S, heads*hd] in the fp16 split (or
+// plain fp32).
 void launch_attention_tc(cudaStream_t s, const AttnOperands& op, int seqs, int S, const int* valid, int heads,
-                         SplitOut ctx, int* err);
-// q, k, v [seq, heads*64] -> the attention operands (RoPE on q, k when cos_t != nullptr).
+                         int hd, SplitOut ctx, int* err);
+// q, k, v [seq, heads*hd] -> the attention operands (RoPE on q, k when cos_t != nullptr).
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                      const float* cos_t, const float* sin_t, const AttnOperands& op);
+                      int hd, const float* cos_t, const float* sin_t, const AttnOperands& op);
+// The bounded-wait self-test kernel: a wait on a flag that nothing sets, limited to
+// limit_ns; it records its timeout in *err and writes the time waited (ns) to *waited.
+void launch_wait_probe(cudaStream_t s, int* err, unsigned long long limit_ns, unsigned long long* waited);
 // Synthetic benchmark operands: p[i] ~ scale * (sum of 4 hashed uniforms in [-1, 1)).
 void launch_fill_random(cudaStream_t s, float* p, long long n, uint32_t seed, float scale);
 // tensor::linear without any allocation: scratch is a fixed device array (noalloc.cu).
 void linear_noalloc(int device, const float* d_x, size_t rows, size_t cols, const float* d_w, size_t out,
                     const float* d_bias, float* d_y, cudaStream_t stream);
 size_t linear_noalloc_capacity();
-// q, k, v [seq, heads*hd] -> qkv [seq, 3*heads*hd] with RoPE applied to q and k when cos_t != nullptr.
-void launch_pack_qkv(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
-                     int hd, const float* cos_t, const float* sin_t, float* qkv);
 
 }  // namespace n3d

@@ -169,6 +169,7 @@ def lib() -> C.CDLL:
         "n3d_attention": ([C.c_int, vp, vp, vp, _sz, _sz, _sz, _sz, C.c_int, C.c_double, vp], C.c_int),
         "n3d_cache_compress": ([C.c_int, C.POINTER(CacheConfig), fpp, _sz, vp, _sz, vp, C.POINTER(_sz),
                                 C.POINTER(_sz), C.POINTER(_sz), vp, vp], C.c_int),
+        "n3d_selftest_wait_timeout": ([C.c_int, C.c_double, C.POINTER(C.c_double)], C.c_int),
         "n3d_bench_linear": ([C.c_int, _sz, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
         "n3d_bench_attention": ([C.c_int, _sz, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
         "n3d_bench_layer_norm": ([C.c_int, _sz, _sz, C.c_int, C.POINTER(C.c_double)], C.c_int),
@@ -586,3 +587,11 @@ def bench_layer_norm(device: int, rows: int, cols: int, iters: int = 20) -> floa
     ms = C.c_double()
     _check(lib().n3d_bench_layer_norm(device, rows, cols, iters, C.byref(ms)))
     return ms.value
+
+
+def selftest_wait_timeout(device: int, limit_ms: float) -> tuple[int, str, float]:
+    """Run one bounded device wait on a flag nothing sets (n3d_selftest_wait_timeout).
+    Returns (status, message, waited_ms); the status is Timeout when the wait gave up."""
+    w = C.c_double()
+    st = lib().n3d_selftest_wait_timeout(device, limit_ms, C.byref(w))
+    return st, lib().n3d_last_error().decode(), w.value

@@ -212,6 +212,12 @@ def test_single_kernel_sizes_are_checked_before_any_cuda_call():
         assert n3d.STATUS[call()] == "InvalidArgument", lib.n3d_last_error()
 
 
+def test_wait_selftest_limit_is_checked_before_any_cuda_call():
+    w = C.c_double()
+    for limit in (0.0, -1.0, 2001.0, float("nan")):
+        assert n3d.STATUS[n3d.lib().n3d_selftest_wait_timeout(0, limit, C.byref(w))] == "InvalidArgument"
+
+
 def test_cache_compress_arguments_are_checked_before_any_cuda_call():
     probs = np.full(64 * 8, 0.75, np.float32)
     picked = (C.c_size_t * 64)()

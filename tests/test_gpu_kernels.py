@@ -116,7 +116,8 @@ def test_layer_norm_matches_oracle(rows, cols):
 # ATTN_GEMM_CHECK seqs (src/bin/gpu_check.rs:84) and the sweep's (512, 1024, 4096)
 @pytest.mark.parametrize("seq,hd,valid", [(8, 64, 5), (17, 64, 17), (130, 64, 101), (380, 64, 380), (684, 64, 683),
                                           (512, 64, 512), (512, 128, 400), (1024, 64, 1000), (1024, 128, 1024),
-                                          (4096, 64, 4000), (4096, 128, 4096)])
+                                          (4096, 64, 4000), (4096, 128, 4096), (8, 128, 5), (17, 128, 17),
+                                          (130, 128, 101), (684, 128, 683)])
 def test_rope_attention_matches_oracle(seq, hd, valid):
     import torch
 
@@ -134,10 +135,11 @@ def test_rope_attention_matches_oracle(seq, hd, valid):
     assert np.abs(got - want).max() < TOL
 
 
-def test_attention_with_no_valid_keys_is_zero():
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_with_no_valid_keys_is_zero(hd):
     import torch
 
-    seq, heads, hd = 8, 8, 64
+    seq, heads = 8, 8
     q = np.ones(seq * heads * hd, np.float32)
     dq = _cuda(q)
     do = torch.full((seq * heads * hd,), 7.0, dtype=torch.float32, device="cuda")
