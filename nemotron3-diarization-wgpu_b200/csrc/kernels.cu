@@ -21,58 +21,84 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // ---------------------------------------------------------------- LayerNorm
 // torch LayerNorm, eps 1e-5, two-pass population variance (src/tensor.rs:97-110).
-// One warp per row, VPL values per lane held in registers (128-bit loads).
-// Writes either a plain fp32 row (out.h == nullptr) or the fp16 split of row * out.scale.
-// x_out may alias x (in-place residual add): each lane reads its elements of x before
-// writing them, so neither is __restrict__.
-template <int VPL>
+// One warp per RPW rows, VPL values per lane and row held in registers (128-bit
+// loads, all of a warp's rows issued before any reduction, so each warp keeps RPW
+// rows of loads in flight; VPL a multiple of 8).  Writes either a plain fp32 row (out.h == nullptr) or the
+// fp16 split of row * out.scale.
+template <int VPL, int RPW>
 __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, const float* __restrict__ w,
                                   const float* __restrict__ b, SplitOut out) {
     griddep_wait();
     griddep_launch_dependents();
     constexpr int COLS = VPL * 32;
-    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const long long row0 = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float* src = x + row * COLS;
-    float v[VPL];
+    if (row0 >= rows) return;
+    // lane L holds columns 256 c + 8 L .. + 7 of chunk c: two 16-byte loads, and the
+    // split's 8 fp16 per array leave as one 16-byte store
+    float v[RPW][VPL];
 #pragma unroll
-    for (int i = 0; i < VPL; i += 4) {
-        const float4 t = *reinterpret_cast<const float4*>(src + (i / 4) * 128 + lane * 4);
-        v[i] = t.x;
-        v[i + 1] = t.y;
-        v[i + 2] = t.z;
-        v[i + 3] = t.w;
+    for (int k = 0; k < RPW; k++) {
+        if (row0 + k >= rows) break;
+        const float* src = x + (row0 + k) * COLS;
+#pragma unroll
+        for (int i = 0; i < VPL; i += 8) {
+            const float4 t0 = *reinterpret_cast<const float4*>(src + (i / 8) * 256 + lane * 8);
+            const float4 t1 = *reinterpret_cast<const float4*>(src + (i / 8) * 256 + lane * 8 + 4);
+            v[k][i] = t0.x, v[k][i + 1] = t0.y, v[k][i + 2] = t0.z, v[k][i + 3] = t0.w;
+            v[k][i + 4] = t1.x, v[k][i + 5] = t1.y, v[k][i + 6] = t1.z, v[k][i + 7] = t1.w;
+        }
     }
-    float s = 0.0f;
+    float mean[RPW], inv[RPW];
 #pragma unroll
-    for (int i = 0; i < VPL; i++) s += v[i];
-    const float mean = __fdiv_rn(warp_sum(s), (float)COLS);
-    float q = 0.0f;
+    for (int k = 0; k < RPW; k++) {
+        float s = 0.0f;
 #pragma unroll
-    for (int i = 0; i < VPL; i++) {
-        const float d = __fsub_rn(v[i], mean);
-        q = __fadd_rn(q, __fmul_rn(d, d));
+        for (int i = 0; i < VPL; i++) s += v[k][i];
+        mean[k] = __fdiv_rn(warp_sum(s), (float)COLS);
     }
-    const float var = __fdiv_rn(warp_sum(q), (float)COLS);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-    float* dst = out.h ? nullptr : out.plain + row * COLS;
-    uint16_t* dh = out.h ? static_cast<uint16_t*>(out.h) + row * COLS : nullptr;
-    uint16_t* dl = out.h ? static_cast<uint16_t*>(out.l) + row * COLS : nullptr;
 #pragma unroll
-    for (int i = 0; i < VPL; i += 4) {
-        const int c = (i / 4) * 128 + lane * 4;
-        float y[4];
+    for (int k = 0; k < RPW; k++) {
+        float q = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            y[j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[i + j], mean), inv), w[c + j]), b[c + j]);
-        if (dh) {
-            uint2 hw, lw;
-            split2x4(y, out.scale, hw, lw);
-            *reinterpret_cast<uint2*>(dh + c) = hw;
-            *reinterpret_cast<uint2*>(dl + c) = lw;
-        } else {
-            *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
+        for (int i = 0; i < VPL; i++) {
+            const float d = __fsub_rn(v[k][i], mean[k]);
+            q = __fadd_rn(q, __fmul_rn(d, d));
+        }
+        const float var = __fdiv_rn(warp_sum(q), (float)COLS);
+        inv[k] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+    }
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const long long row = row0 + k;
+        if (row >= rows) break;
+        float* dst = out.h ? nullptr : out.plain + row * COLS;
+        uint16_t* dh = out.h ? static_cast<uint16_t*>(out.h) + row * COLS : nullptr;
+        uint16_t* dl = out.h ? static_cast<uint16_t*>(out.l) + row * COLS : nullptr;
+#pragma unroll
+        for (int i = 0; i < VPL; i += 8) {
+            const int c = (i / 8) * 256 + lane * 8;
+            float y[8];
+#pragma unroll
+            for (int j4 = 0; j4 < 8; j4 += 4) {
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + c + j4));
+                const float4 b4 = __ldg(reinterpret_cast<const float4*>(b + c + j4));
+                const float ww[4] = {w4.x, w4.y, w4.z, w4.w}, bb[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    y[j4 + j] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v[k][i + j4 + j], mean[k]), inv[k]), ww[j]),
+                                          bb[j]);
+            }
+            if (dh) {
+                uint2 h0, l0, h1, l1;
+                split2x4(y, out.scale, h0, l0);
+                split2x4(y + 4, out.scale, h1, l1);
+                *reinterpret_cast<uint4*>(dh + c) = make_uint4(h0.x, h0.y, h1.x, h1.y);
+                *reinterpret_cast<uint4*>(dl + c) = make_uint4(l0.x, l0.y, l1.x, l1.y);
+            } else {
+                *reinterpret_cast<float4*>(dst + c) = make_float4(y[0], y[1], y[2], y[3]);
+                *reinterpret_cast<float4*>(dst + c + 4) = make_float4(y[4], y[5], y[6], y[7]);
+            }
         }
     }
 }
@@ -368,12 +394,14 @@ void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max) {
 void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols, const float* w, const float* b,
                        SplitOut out) {
     if (rows <= 0) return;
-    const int warps = 8;
-    const unsigned grid = (unsigned)((rows + warps - 1) / warps);
+    // two rows per warp at 512 columns (72 registers), one at 1024 (where two rows would
+    // need 120 registers and halve the resident warps)
+    const int warps = 8, rpw = cols == 512 ? 2 : 1;
+    const unsigned grid = (unsigned)((rows + warps * rpw - 1) / (warps * rpw));
     if (cols == 512)
-        launch_pdl(layer_norm_kernel<16>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
+        launch_pdl(layer_norm_kernel<16, 2>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
     else if (cols == 1024)
-        launch_pdl(layer_norm_kernel<32>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
+        launch_pdl(layer_norm_kernel<32, 1>, dim3(grid), dim3(warps * 32), 0, s, x, rows, w, b, out);
     else
         throw Error(13, "layer_norm supports 512 or 1024 columns");
     N3D_CUDA(cudaGetLastError());

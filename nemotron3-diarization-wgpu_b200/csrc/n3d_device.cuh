@@ -390,19 +390,22 @@ __device__ __forceinline__ uint32_t f16x2_rn(float a, float b) {  // a in the lo
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
     return r;
 }
-__device__ __forceinline__ void f16x2_to_f32(uint32_t v, float& a, float& b) {
-    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
-        : "=f"(a), "=f"(b)
-        : "r"(v));
+// x rounded to 11 significant bits (nearest, ties away from zero) with integer
+// operations on its bit pattern: the value fp16 stores for x in fp16's normal range.
+// Conversions run on the narrow conversion pipe; these two ALU operations do not.
+__device__ __forceinline__ float round11(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xffffe000u);
 }
 // Two consecutive elements (a in the low half of each word): h and l of (a s, b s).
-// x s - h is exact in fp32 (h agrees with x s in all but its last 13 bits).
+// h = round11(x s), which the fp16 conversion stores exactly; x s - h is exact in
+// fp32 (the two agree in all but the last 13 bits), and l is its RN-fp16.  Where x s
+// lies below fp16's normal range (|x s| < 2^-14) h is rounded once more, by at most
+// 2^-25, far below the magnitudes the scales give the tensors.
 __device__ __forceinline__ void split2x2(float a, float b, float s, uint32_t& h, uint32_t& l) {
     float as, bs;
     unpack2(mul2(pack2(a, b), pack2(s, s)), as, bs);
-    h = f16x2_rn(as, bs);
-    float ha, hb;
-    f16x2_to_f32(h, ha, hb);
+    const float ha = round11(as), hb = round11(bs);
+    h = f16x2_rn(ha, hb);
     float la, lb;
     unpack2(fma2(pack2(ha, hb), pack2(-1.0f, -1.0f), pack2(as, bs)), la, lb);
     l = f16x2_rn(la, lb);
@@ -447,15 +450,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
         "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
-// (a, b) -> bfloat16 pairs x = hi + lo, hi = RN-bf16(x), lo = RN-bf16(x - hi), packed
-// two per word with a in the low half.  hi + lo carries ~16 significant bits; the
-// three products lo*hi + hi*lo + hi*hi keep that precision.
+// (a, b) -> bfloat16 pairs x = hi + lo, packed two per word with a in the low half:
+// hi = x rounded to 8 significant bits (nearest, ties away from zero) by integer
+// operations on the bit pattern, lo = RN-bf16(x - hi) (x - hi is exact in fp32).
+// hi + lo carries ~16 significant bits; the three products lo*hi + hi*lo + hi*hi keep
+// that precision.  Only lo uses the conversion pipe.
 __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-    uint32_t h, l;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
-    const float ha = __uint_as_float(h << 16), hb = __uint_as_float(h & 0xffff0000u);
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l) : "f"(__fsub_rn(b, hb)), "f"(__fsub_rn(a, ha)));
-    hi = h;
+    const uint32_t ra = (__float_as_uint(a) + 0x8000u) & 0xffff0000u;
+    const uint32_t rb = (__float_as_uint(b) + 0x8000u) & 0xffff0000u;
+    hi = __byte_perm(ra, rb, 0x7632);  // the high halves: a's low, b's high
+    uint32_t l;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l)
+        : "f"(__fsub_rn(b, __uint_as_float(rb))), "f"(__fsub_rn(a, __uint_as_float(ra))));
     lo = l;
 }
 

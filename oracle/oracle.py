@@ -16,7 +16,9 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "liboracle.so")
+# N3D_ORACLE_LIB selects another build of the same restatement (the FMA-contracted
+# variant that tests/golden/noise_floor.py compares against); unset, the plain oracle.
+LIB_PATH = os.environ.get("N3D_ORACLE_LIB") or os.path.join(HERE, "liboracle.so")
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")

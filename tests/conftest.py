@@ -109,7 +109,10 @@ def frame_check(got, want, ns=8, duration=0.01):
     sg = one / (one + np.exp(-got, dtype=np.float32))
     sw = one / (one + np.exp(-want, dtype=np.float32))
     assert sg.dtype == sw.dtype == np.float32
-    res["flips"] = int(((sg > 0.5) != (sw > 0.5)).sum())
+    flips = np.argwhere((sg > 0.5) != (sw > 0.5))
+    res["flips"] = int(len(flips))
+    # each flip as (row, speaker, reference logit, our logit), for the failure message
+    res["flip_values"] = [(int(r), int(c), float(want[r, c]), float(got[r, c])) for r, c in flips[:8]]
     a = oracle.extract_speaker_dict(got.ravel(), got.shape[0], ns, duration)
     b = oracle.extract_speaker_dict(want.ravel(), want.shape[0], ns, duration)
     res["segments_identical"] = a == b
