@@ -362,7 +362,7 @@ def run_kernel_sweep(args, world, rank, local):
         line = {"metric": "C1 kernel sweep: GEMM TFLOP/s over the 48 shapes", "value": value, "unit": "TFLOP/s",
                 "n_gpus": world, "steps": iters, "warmup": 3, "ms_per_step": tot_ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None,
-                "dtype": "f32 (fp16-split GEMMs: h*h + h*l + l*h; 3xBF16 attention at head_dim 64)",
+                "dtype": "f32 (fp16 split on tcgen05: h*h + h*l + l*h, GEMMs and attention)",
                 "data": "synthetic", "config": {"workload": "C1 kernel sweep (BASELINE config 1), each kernel alone",
                                                 "l2": "operands resident: shapes under 126 MB run L2-warm"},
                 "gemm_frac_of_burst_peak": value / burst,
@@ -582,7 +582,7 @@ def main():
         line = {
             "metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32 (fp16-split GEMMs: h*h + h*l + l*h; 3xBF16 attention; tcgen05)", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f32 (fp16 split on tcgen05: h*h + h*l + l*h, GEMMs and attention)", "data": "synthetic",
             "config": {"workload": desc, "seconds_per_item": item_s, "items_per_step_per_gpu": n_items,
                        "mode": mode, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},

@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <memory>
 #include <mutex>
 #include <new>
@@ -160,17 +161,18 @@ struct DevScratch {
     }
 };
 
-// The fp16-split scales of two device operands from their max |x| (one readback).
-void operand_scales(KernelCtx& k, DevScratch& sc, const float* a, size_t na, const float* b, size_t nb, float* out) {
-    float* m = sc.get(2);
-    N3D_CUDA(cudaMemsetAsync(m, 0, 8, k.stream));
-    n3d::launch_absmax(k.stream, a, (long long)na, m);
-    n3d::launch_absmax(k.stream, b, (long long)nb, m + 1);
-    float hm[2] = {0.0f, 0.0f};
-    N3D_CUDA(cudaMemcpyAsync(hm, m, 8, cudaMemcpyDeviceToHost, k.stream));
+// The fp16-split scales of up to four device operands from their max |x| (one
+// readback); grow[i] widens operand i's bound (RoPE may double a Q or K element).
+void operand_scales(KernelCtx& k, DevScratch& sc, std::initializer_list<std::pair<const float*, size_t>> ops,
+                    float* out, const double* grow = nullptr) {
+    float* m = sc.get(4);
+    N3D_CUDA(cudaMemsetAsync(m, 0, 16, k.stream));
+    int i = 0;
+    for (const auto& o : ops) n3d::launch_absmax(k.stream, o.first, (long long)o.second, m + i++);
+    float hm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    N3D_CUDA(cudaMemcpyAsync(hm, m, 16, cudaMemcpyDeviceToHost, k.stream));
     N3D_CUDA(cudaStreamSynchronize(k.stream));
-    out[0] = n3d::split_scale(hm[0]);
-    out[1] = n3d::split_scale(hm[1]);
+    for (int j = 0; j < i; j++) out[j] = n3d::split_scale((double)hm[j] * (grow ? grow[j] : 1.0));
 }
 
 }  // namespace
@@ -178,7 +180,7 @@ void operand_scales(KernelCtx& k, DevScratch& sc, const float* a, size_t na, con
 extern "C" {
 
 const char* n3d_last_error(void) { return g_last_error.c_str(); }
-const char* n3d_version(void) { return "n3d-b200 0.3 (sm_100a, tcgen05: fp16-split GEMMs (h*h + h*l + l*h), 3xBF16 attention)"; }
+const char* n3d_version(void) { return "n3d-b200 0.4 (sm_100a, tcgen05: fp16-split GEMMs and attention (h*h + h*l + l*h))"; }
 
 n3d_status n3d_model_load_gpu(const char* dir, int device, n3d_model** out) {
     return guarded([&] {
@@ -585,7 +587,7 @@ n3d_status n3d_linear(int device, const float* d_x, size_t rows, size_t cols, co
         std::lock_guard<std::mutex> turn(k.call);
         DevScratch sc;
         float scale[2];
-        operand_scales(k, sc, d_x, rows * cols, d_w, out * cols, scale);
+        operand_scales(k, sc, {{d_x, rows * cols}, {d_w, out * cols}}, scale);
         const n3d::SplitOut x{sc.get(rows * cols / 2), sc.get(rows * cols / 2), scale[0], nullptr};
         const n3d::SplitOut w{sc.get(out * cols / 2), sc.get(out * cols / 2), scale[1], nullptr};
         n3d::launch_split(k.stream, d_x, (long long)(rows * cols), x);
@@ -655,17 +657,26 @@ n3d_status n3d_attention(int device, const float* d_q, const float* d_k, const f
         int v = (int)std::min(valid, seq);
         int* dv = (int*)sc.get(1);
         N3D_CUDA(cudaMemcpyAsync(dv, &v, 4, cudaMemcpyHostToDevice, k.stream));
-        // tcgen05 path: operands as bfloat16 pairs, V transposed
+        // tcgen05 path: operands in the fp16 split with scales from their maxima, V transposed
         const size_t W = heads * head_dim, vt_ld = (seq + 7) / 8 * 8;
         n3d::AttnOperands op;
-        op.q_hi = sc.get(seq * W / 2);
-        op.q_lo = sc.get(seq * W / 2);
-        op.k_hi = sc.get(seq * W / 2);
-        op.k_lo = sc.get(seq * W / 2);
+        op.q_h = sc.get(seq * W / 2);
+        op.q_l = sc.get(seq * W / 2);
+        op.k_h = sc.get(seq * W / 2);
+        op.k_l = sc.get(seq * W / 2);
         op.rows_cap = (long long)seq;
-        op.vt_hi = sc.get(W * vt_ld / 2);
-        op.vt_lo = sc.get(W * vt_ld / 2);
+        op.vt_h = sc.get(W * vt_ld / 2);
+        op.vt_l = sc.get(W * vt_ld / 2);
         op.vt_ld = (long long)vt_ld;
+        {
+            const size_t n = seq * W;
+            const double grow[3] = {rope ? 2.0 : 1.0, rope ? 2.0 : 1.0, 1.0};
+            float sc3[3];
+            operand_scales(k, sc, {{d_q, n}, {d_k, n}, {d_v, n}}, sc3, grow);
+            op.q_scale = sc3[0];
+            op.k_scale = sc3[1];
+            op.v_scale = sc3[2];
+        }
         n3d::launch_pack_attn(k.stream, d_q, d_k, d_v, (long long)seq, (int)heads, (int)head_dim, cs, sn, op);
         n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, (int)head_dim, n3d::plain_out(d_out),
                                  k.err);
@@ -797,7 +808,7 @@ n3d_status n3d_bench_linear(int device, size_t rows, size_t cols, size_t out, in
         n3d::launch_fill_random(k.stream, w, (long long)(out * cols), 2, 1.0f / std::sqrt((float)cols));
         n3d::launch_fill_random(k.stream, bias, (long long)out, 3, 1.0f);
         float scale[2];
-        operand_scales(k, sc, x, rows * cols, w, out * cols, scale);
+        operand_scales(k, sc, {{x, rows * cols}, {w, out * cols}}, scale);
         const n3d::SplitOut xs{sc.get(rows * cols / 2), sc.get(rows * cols / 2), scale[0], nullptr};
         const n3d::SplitOut ws{sc.get(out * cols / 2), sc.get(out * cols / 2), scale[1], nullptr};
         n3d::launch_split(k.stream, x, (long long)(rows * cols), xs);
@@ -838,14 +849,21 @@ n3d_status n3d_bench_attention(int device, size_t seq, size_t heads, size_t head
         N3D_CUDA(cudaMemcpyAsync(dv, &vv, 4, cudaMemcpyHostToDevice, k.stream));
         const size_t vt_ld = (seq + 7) / 8 * 8;
         n3d::AttnOperands op;
-        op.q_hi = sc.get(seq * W / 2);
-        op.q_lo = sc.get(seq * W / 2);
-        op.k_hi = sc.get(seq * W / 2);
-        op.k_lo = sc.get(seq * W / 2);
+        op.q_h = sc.get(seq * W / 2);
+        op.q_l = sc.get(seq * W / 2);
+        op.k_h = sc.get(seq * W / 2);
+        op.k_l = sc.get(seq * W / 2);
         op.rows_cap = (long long)seq;
-        op.vt_hi = sc.get(W * vt_ld / 2);
-        op.vt_lo = sc.get(W * vt_ld / 2);
+        op.vt_h = sc.get(W * vt_ld / 2);
+        op.vt_l = sc.get(W * vt_ld / 2);
         op.vt_ld = (long long)vt_ld;
+        {
+            float sc3[3];
+            operand_scales(k, sc, {{q, seq * W}, {kk, seq * W}, {v, seq * W}}, sc3);
+            op.q_scale = sc3[0];
+            op.k_scale = sc3[1];
+            op.v_scale = sc3[2];
+        }
         n3d::launch_pack_attn(k.stream, q, kk, v, (long long)seq, (int)heads, (int)head_dim, nullptr, nullptr, op);
         *ms = time_launches(k, iters, [&] {
             n3d::launch_attention_tc(k.stream, op, 1, (int)seq, dv, (int)heads, (int)head_dim, n3d::plain_out(ctx),

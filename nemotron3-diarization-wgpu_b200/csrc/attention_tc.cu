@@ -7,12 +7,12 @@
 // `attention` (src/encoder.rs:302-329): scores q.k * hd^-1/2 over the first
 // `valid` keys, softmax, context = sum p v.  No S x S scores buffer exists.
 //
-// Arithmetic ("3xBF16"): Q, K, V^T and P are bfloat16 pairs x = hi + lo; each
-// k-step issues lo*hi + hi*lo + hi*hi into an fp32 accumulator.  On the encoder
-// this keeps the model's logits as close to the fp32 CPU path as 3xTF32 does
-// (max |diff| 5e-8 either way, measured by emulation on the synthetic
-// checkpoint), at half the tensor time and half the operand bytes, which lets
-// two CTAs share an SM at head_dim 64.
+// Arithmetic (the fp16 split, as the GEMMs): Q, K, V^T and P are each two fp16 arrays
+// h + l of the values times a power-of-two scale; each k-step issues l*h + h*l + h*h
+// into an fp32 accumulator, ~2^-22 per product, at the 16-bit tensor rate.  Q, K and
+// V carry the scales the QKV epilogue gave them (from load-time bounds); P <= 2^8
+// (the lazy rescale below) is scaled by 2^7.  The score scale 1/sqrt(hd) log2 e is
+// divided by s_Q s_K, and the context by 2^7 s_V, exactly (powers of two).
 //
 // CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM at head_dim
 // 64, one at 128 (its ring and TMEM are twice as large):
@@ -26,7 +26,7 @@
 //               pair from shared memory into TMEM; per block the row's 64 scores, exp as 2^x on the
 //               special-function unit after one FMA folds the 1/sqrt(hd) scale,
 //               log2 e and the reference max together; then, once PV_{j-1} has
-//               read the P buffer, P_j as bf16 pairs.
+//               read the P buffer, P_j as fp16 splits.
 // Lazy rescaling: exponents use a per-row reference max m that is raised only when
 // a block's max exceeds it by more than 2^8 in the exponent; only then is O
 // (in TMEM) multiplied by the correction, after PV_{j-1} has completed and before
@@ -34,12 +34,14 @@
 // Context rows leave through shared memory (the ring, free once the last PV is done)
 // and TMA stores, a warp's 32 rows at a time.
 // TMEM: S 0..63, P 64..127 (hi 64.., lo 96..), O 128..128+HD-1, Q 128+HD..128+2HD-1
-// (hi first, then lo); bf16 operands two per 32-bit column.  256 columns at head_dim
+// (h first, then l); 16-bit operands two per 32-bit column.  256 columns at head_dim
 // 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of 64 columns (the
 // 128-byte swizzle's limit), as is the Q tile.
 // Barriers with a phase per key block
 // are double-buffered by block parity, so every waiter is at most one phase behind.
 // Every wait is bounded; an expired wait records its site in *err.
+
+#include <cmath>
 
 #include "n3d_device.cuh"
 #include "n3d_internal.h"
@@ -59,18 +61,17 @@ constexpr int DEV_TIMEOUT_ATTN = 5;
 template <int HD>
 struct AttnCfg {
     static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
-    static constexpr int KTILE = KB * HD * 2;                  // K block [64 keys x HD] bf16
-    static constexpr int VTILE = HD * KB * 2;                  // V^T block [HD x 64 keys] bf16
+    static constexpr int KTILE = KB * HD * 2;                  // K block [64 keys x HD] fp16
+    static constexpr int VTILE = HD * KB * 2;                  // V^T block [HD x 64 keys] fp16
     static constexpr int STAGE_BYTES = 2 * KTILE + 2 * VTILE;  // K_hi, K_lo, V^T_hi, V^T_lo
     static constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + 1024 + 256;
     static constexpr uint32_t COL_Q = COL_O + HD, TMEM_COLS = HD == 64 ? 256 : 512;
     static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
-    // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
-    static constexpr float K2 = (HD == 64 ? 0.125f : 0.0883883476483184f) * 1.4426950408889634f;
     static_assert(2 * QT * HD * 2 == STAGE_BYTES, "the Q pair fills ring slot 2");
     static_assert(4 * 32 * HD * 4 == STAGE_BYTES, "the context staging of the 4 softmax warps fills slot 0");
 };
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
+constexpr float P_SCALE = 128.0f;         // P <= 2^8, so P * 2^7 <= 2^15 stays in fp16's range
 
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
@@ -110,16 +111,16 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t* v) {
 }
 
 struct AttnMaps {
-    CUtensorMap qh, ql;      // Q pair [rows, heads*64] bf16, box 64 x 128, 128-byte swizzle
-    CUtensorMap kh, kl;      // K pair, box 64 x 64
-    CUtensorMap vh, vl;      // V^T pair [heads*64, rows], box 64 x 64
+    CUtensorMap qh, ql;      // Q split [rows, heads*hd] fp16, box 64 x 128, 128-byte swizzle
+    CUtensorMap kh, kl;      // K split, box 64 x 64
+    CUtensorMap vh, vl;      // V^T split [heads*hd, rows], box 64 x hd
     CUtensorMap ch, cl;      // context fp16 split h / l [rows, heads*64], box 64 x 32, 128-byte swizzle
 };
 
 template <int HD>
 __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
     attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
-                        SplitOut ctx, int ctx_tma, int* err) {
+                        SplitOut ctx, int ctx_tma, float k2, float out_unscale, int* err) {
     using Cfg = AttnCfg<HD>;
     constexpr int STAGE_BYTES = Cfg::STAGE_BYTES, KTILE = Cfg::KTILE, VTILE = Cfg::VTILE;
     constexpr uint32_t COL_Q = Cfg::COL_Q, TMEM_COLS = Cfg::TMEM_COLS;
@@ -204,19 +205,19 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         }
     } else if (warp == 1) {
         if (lane == 0 && nblk > 0) {
-            constexpr uint32_t idesc_qk = idesc_bf16(KB), idesc_pv = idesc_bf16(HD);
+            constexpr uint32_t idesc_qk = idesc_f16(KB), idesc_pv = idesc_f16(HD);
             bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
             auto issue_qk = [&](int j) {
                 const uint32_t kb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES);
                 const uint32_t d = tmem + COL_S;
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at HD/2 + 8k
-                    // 16 bf16 = 32 bytes along the swizzled K rows, in box k / 4
+                    // 16 fp16 = 32 bytes along the swizzled K rows, in box k / 4
                     const uint32_t off = (k / 4) * BOX + (k % 4) * 32;
                     const uint32_t qh = tmem + COL_Q + 8 * k, ql = qh + HD / 2;
-                    umma_bf16_ts(d, ql, desc_k_sw128(kb + off), idesc_qk, k != 0);
-                    umma_bf16_ts(d, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
-                    umma_bf16_ts(d, qh, desc_k_sw128(kb + off), idesc_qk, 1);
+                    umma_f16_ts(d, ql, desc_k_sw128(kb + off), idesc_qk, k != 0);
+                    umma_f16_ts(d, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
+                    umma_f16_ts(d, qh, desc_k_sw128(kb + off), idesc_qk, 1);
                 }
                 umma_commit(s_full);
             };
@@ -244,9 +245,9 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
 #pragma unroll
                 for (int k = 0; k < KB / 16; k++) {  // keys 16k..16k+15: P_hi at column 8k, P_lo at 32 + 8k
                     const uint32_t off = k * 32;
-                    umma_bf16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc_pv, j > 0 || k != 0);
-                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + VTILE + off), idesc_pv, 1);
-                    umma_bf16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc_pv, 1);
+                    umma_f16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc_pv, j > 0 || k != 0);
+                    umma_f16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + VTILE + off), idesc_pv, 1);
+                    umma_f16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc_pv, 1);
                 }
                 umma_commit(&o_full[j & 1]);
                 umma_commit(&kv_empty[j % NSTAGE]);
@@ -257,11 +258,11 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         const int qd = warp & 3;
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-        const float k2 = Cfg::K2;                        // hd^-1/2 * log2 e: p = 2^(s k2 - m k2)
+        // k2 = hd^-1/2 log2 e / (s_Q s_K): p = 2^(s k2 - m k2) for raw accumulator scores s
         float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
         if (nblk > 0) {
-            // this row's Q pair (HD bf16 each, RoPE applied) from ring slot 2 (boxes of
+            // this row's Q split (HD fp16 each, RoPE applied) from ring slot 2 (boxes of
             // 128-byte rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
             ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN));
 #pragma unroll
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             l = l * corr + (sa + sb);
             uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) split_bf16x2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
+            for (int i = 0; i < 32; i++) split2x2(s[2 * i], s[2 * i + 1], P_SCALE, hi[i], lo[i]);
             if (j > 0) {
                 // PV_{j-1} has read the P buffer and finished O up to block j-1
                 ok = __all_sync(0xffffffffu,
@@ -363,7 +364,8 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         // all 32 rows of the warp belong to this sequence; otherwise (and for a plain
         // fp32 context) per row
         const int wrow0 = q0 + qd * 32;
-        const float inv = (nblk > 0 && l > 0.0f) ? 1.0f / l : 0.0f;
+        // 1 / l, and O's scales undone (a power of two: exact)
+        const float inv = (nblk > 0 && l > 0.0f) ? (1.0f / l) * out_unscale : 0.0f;
         const bool via_tma = ctx_tma && wrow0 + 32 <= S;
         // staging in ring slot 0 (every load has been consumed by the last PV): per warp
         // HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
@@ -437,22 +439,24 @@ void launch_attention_hd(cudaStream_t s, const AttnOperands& op, int seqs, int S
     });
     const long long W = (long long)heads * HD, rows = (long long)seqs * S;
     AttnMaps m;
-    m.qh = make_bf16_map(op.q_hi, op.rows_cap, W, W, 64, QT, true);
-    m.ql = make_bf16_map(op.q_lo, op.rows_cap, W, W, 64, QT, true);
-    m.kh = make_bf16_map(op.k_hi, op.rows_cap, W, W, 64, KB, true);
-    m.kl = make_bf16_map(op.k_lo, op.rows_cap, W, W, 64, KB, true);
-    m.vh = make_bf16_map(op.vt_hi, W, rows, op.vt_ld, 64, HD, true);
-    m.vl = make_bf16_map(op.vt_lo, W, rows, op.vt_ld, 64, HD, true);
+    m.qh = make_f16_map(op.q_h, op.rows_cap, W, W, 64, QT, true);
+    m.ql = make_f16_map(op.q_l, op.rows_cap, W, W, 64, QT, true);
+    m.kh = make_f16_map(op.k_h, op.rows_cap, W, W, 64, KB, true);
+    m.kl = make_f16_map(op.k_l, op.rows_cap, W, W, 64, KB, true);
+    m.vh = make_f16_map(op.vt_h, W, rows, op.vt_ld, 64, HD, true);
+    m.vl = make_f16_map(op.vt_l, W, rows, op.vt_ld, 64, HD, true);
     const int ctx_tma = ctx.h != nullptr;
     if (ctx_tma) {
-        m.ch = make_f16_map(ctx.h, rows, W, W, 64, 32);
-        m.cl = make_f16_map(ctx.l, rows, W, W, 64, 32);
+        m.ch = make_f16_map(ctx.h, rows, W, W, 64, 32, true);
+        m.cl = make_f16_map(ctx.l, rows, W, W, 64, 32, true);
     } else {
         m.ch = m.cl = m.qh;  // unused
     }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
+    const float k2 = (float)((1.0 / std::sqrt((double)HD)) * 1.4426950408889634 / ((double)op.q_scale * op.k_scale));
+    const float out_unscale = (float)(1.0 / ((double)P_SCALE * op.v_scale));
     launch_pdl(attention_tc_kernel<HD>, grid, dim3(THREADS), Cfg::SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma,
-               err);
+               k2, out_unscale, err);
 }
 
 }  // namespace

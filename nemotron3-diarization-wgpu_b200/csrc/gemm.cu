@@ -296,11 +296,13 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                     }
                 }
             }
-            // bf16 pairs: Q / K rows (64 values = one 128-byte swizzled box row), V
-            // transposed (box row = d, 32 rows of the tile = 64 bytes, unswizzled)
+            // fp16 splits with the section's scale: Q / K rows (64 values = one 128-byte
+            // swizzled box row), V transposed (box row = d, 32 rows of the tile = 64
+            // bytes, unswizzled)
+            const float sc = epi.sec_scale[sec < 3 ? sec : 2];
             uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) split_bf16x2(v[2 * i], v[2 * i + 1], hi[i], lo[i]);
+            for (int i = 0; i < 32; i++) split2x2(v[2 * i], v[2 * i + 1], sc, hi[i], lo[i]);
             stage_begin(lane);
             if (sec < 2) {
 #pragma unroll
@@ -309,17 +311,24 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                     *reinterpret_cast<uint4*>(bhi + o) = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
                     *reinterpret_cast<uint4*>(blo + o) = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
                 }
-                stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_hi, bhi,
-                            sec == 0 ? &epi.map_l : &epi.map_k_lo, blo, nullptr, nullptr, hcol, rowbase);
+                stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_h, bhi,
+                            sec == 0 ? &epi.map_l : &epi.map_k_l, blo, nullptr, nullptr, hcol, rowbase);
             } else {
+                // transpose by lane pairs: word i of lane L holds d = 2i, 2i + 1 of token L;
+                // an even lane stores row 2i for tokens L, L + 1 and an odd lane row 2i + 1
+                // for tokens L - 1, L, one 32-bit store each (rows 2i and 2i + 1 fall in
+                // disjoint banks)
+                const bool odd = lane & 1;
+                const int tok = (lane & ~1) * 2;
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
-                    *reinterpret_cast<uint16_t*>(bhi + (2 * i) * 64 + lane * 2) = (uint16_t)(hi[i] & 0xffffu);
-                    *reinterpret_cast<uint16_t*>(bhi + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(hi[i] >> 16);
-                    *reinterpret_cast<uint16_t*>(blo + (2 * i) * 64 + lane * 2) = (uint16_t)(lo[i] & 0xffffu);
-                    *reinterpret_cast<uint16_t*>(blo + (2 * i + 1) * 64 + lane * 2) = (uint16_t)(lo[i] >> 16);
+                    const uint32_t ph = __shfl_xor_sync(0xffffffffu, hi[i], 1);
+                    const uint32_t pl = __shfl_xor_sync(0xffffffffu, lo[i], 1);
+                    const int row = (2 * i + (odd ? 1 : 0)) * 64 + tok;
+                    *reinterpret_cast<uint32_t*>(bhi + row) = odd ? __byte_perm(ph, hi[i], 0x7632) : __byte_perm(hi[i], ph, 0x5410);
+                    *reinterpret_cast<uint32_t*>(blo + row) = odd ? __byte_perm(pl, lo[i], 0x7632) : __byte_perm(lo[i], pl, 0x5410);
                 }
-                stage_issue(lane, &epi.map_vt_hi, bhi, &epi.map_vt_lo, blo, nullptr, nullptr, rowbase, hcol);
+                stage_issue(lane, &epi.map_vt_h, bhi, &epi.map_vt_l, blo, nullptr, nullptr, rowbase, hcol);
             }
         }
         return;
@@ -737,8 +746,8 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// Element types of the maps: fp32, fp16 (GEMM operands) and bf16 (attention operands).
-enum MapType : int { MAP_F32 = 4, MAP_F16 = 2, MAP_BF16 = 3 };
+// Element types of the maps: fp32 and fp16 (the split operands).
+enum MapType : int { MAP_F32 = 4, MAP_F16 = 2 };
 
 // 2-D map over a row-major matrix [rows, cols] of `type` elements (row stride ld
 // elements), box = box_cols x box_rows, swizzle = box_cols * element size bytes (32,
@@ -758,9 +767,7 @@ CUtensorMap encode_map(const void* ptr, int type, long long rows, long long cols
                                   : span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                   : span == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
                                                 : CU_TENSOR_MAP_SWIZZLE_32B;
-    const CUtensorMapDataType dt = type == MAP_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                   : type == MAP_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const CUtensorMapDataType dt = type == MAP_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = encode_fn()(&m, dt, 2,
                              const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -894,15 +901,10 @@ CUtensorMap make_store_map_f16(const void* p, long long rows, long long cols, lo
     return cached_map(p, MAP_F16, rows, cols, ld, 32, 32, true);
 }
 
-CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
-                          bool swizzle) {
-    if (swizzle && box_cols != 64) throw Error(9, "bf16 map: the 128-byte swizzle needs 64-column boxes");
-    return cached_map(p, MAP_BF16, rows, cols, ld, box_cols, box_rows, swizzle);
-}
-
-CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows) {
-    if (box_cols != 64) throw Error(9, "fp16 map: the 128-byte swizzle needs 64-column boxes");
-    return cached_map(p, MAP_F16, rows, cols, ld, box_cols, box_rows, true);
+CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
+                         bool swizzle) {
+    if (swizzle && box_cols != 64) throw Error(9, "fp16 map: the 128-byte swizzle needs 64-column boxes");
+    return cached_map(p, MAP_F16, rows, cols, ld, box_cols, box_rows, swizzle);
 }
 
 void gemm_split(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,

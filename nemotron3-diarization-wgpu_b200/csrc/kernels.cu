@@ -1,7 +1,6 @@
 // Memory-bound and small kernels of the diarization path: LayerNorm, the fused
 // log-mel front-end, the operand split and the attention operand packing.
 
-#include <cuda_bf16.h>
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -276,18 +275,20 @@ __global__ void absmax_kernel(const float* __restrict__ x, long long n4, unsigne
     if ((threadIdx.x & 31) == 0) atomicMax(d_max, m);
 }
 
-// Kernel-level attention operands: RoPE'd Q and K as bfloat16 pairs, V transposed as a pair.
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
-    hi = __float2bfloat16_rn(x);
-    lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+// Kernel-level attention operands: RoPE'd Q and K, and V transposed, each as the fp16
+// split (h, l) of the values times the operand's scale.
+__device__ __forceinline__ void split16(float x, float s, uint16_t& h, uint16_t& l) {
+    uint32_t hw, lw;
+    split2x2(x, 0.0f, s, hw, lw);
+    h = (uint16_t)(hw & 0xffffu);
+    l = (uint16_t)(lw & 0xffffu);
 }
 __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                  const float* __restrict__ v, long long seq, int heads, int hd,
                                  const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                                 __nv_bfloat16* __restrict__ q_hi, __nv_bfloat16* __restrict__ q_lo,
-                                 __nv_bfloat16* __restrict__ k_hi, __nv_bfloat16* __restrict__ k_lo,
-                                 __nv_bfloat16* __restrict__ vt_hi, __nv_bfloat16* __restrict__ vt_lo,
-                                 long long vt_ld) {
+                                 uint16_t* __restrict__ q_h, uint16_t* __restrict__ q_l, uint16_t* __restrict__ k_h,
+                                 uint16_t* __restrict__ k_l, uint16_t* __restrict__ vt_h, uint16_t* __restrict__ vt_l,
+                                 long long vt_ld, float sq, float sk, float sv) {
     const int half = hd / 2;
     const long long W = (long long)heads * hd;
     for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < seq * W;
@@ -307,9 +308,9 @@ __global__ void pack_attn_kernel(const float* __restrict__ q, const float* __res
                 ko = __fadd_rn(__fmul_rn(k[e], cs[d]), __fmul_rn(k[pe], sn[d]));
             }
         }
-        split_bf16(qo, q_hi[e], q_lo[e]);
-        split_bf16(ko, k_hi[e], k_lo[e]);
-        split_bf16(v[e], vt_hi[(long long)c * vt_ld + r], vt_lo[(long long)c * vt_ld + r]);
+        split16(qo, sq, q_h[e], q_l[e]);
+        split16(ko, sk, k_h[e], k_l[e]);
+        split16(v[e], sv, vt_h[(long long)c * vt_ld + r], vt_l[(long long)c * vt_ld + r]);
     }
 }
 
@@ -363,13 +364,13 @@ __global__ void __launch_bounds__(32) wait_probe_kernel(int* __restrict__ err, u
 
 void launch_pack_attn(cudaStream_t s, const float* q, const float* k, const float* v, long long seq, int heads,
                       int hd, const float* cos_t, const float* sin_t, const AttnOperands& op) {
-    using bf = __nv_bfloat16;
+    using u16 = uint16_t;
     const long long n = seq * heads * hd;
     if (n <= 0) return;
     const long long blocks = std::min<long long>((n + 255) / 256, 148LL * 16);
-    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, hd, cos_t, sin_t, (bf*)op.q_hi, (bf*)op.q_lo,
-                                                      (bf*)op.k_hi, (bf*)op.k_lo, (bf*)op.vt_hi, (bf*)op.vt_lo,
-                                                      op.vt_ld);
+    pack_attn_kernel<<<(unsigned)blocks, 256, 0, s>>>(q, k, v, seq, heads, hd, cos_t, sin_t, (u16*)op.q_h, (u16*)op.q_l,
+                                                      (u16*)op.k_h, (u16*)op.k_l, (u16*)op.vt_h, (u16*)op.vt_l,
+                                                      op.vt_ld, op.q_scale, op.k_scale, op.v_scale);
     N3D_CUDA(cudaGetLastError());
 }
 

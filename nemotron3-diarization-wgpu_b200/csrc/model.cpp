@@ -468,6 +468,8 @@ void Model::upload_weights(const std::string& dir) {
         L.s_ln1 = split_scale(b1);
         L.s_ln2 = split_scale(b2);
         L.s_ctx = split_scale(row_l1_max(st.get(b + ".self_attn.v_proj.weight", {h, h}), h, h) * b1);
+        L.s_q = split_scale(2.0 * row_l1_max(st.get(b + ".self_attn.q_proj.weight", {h, h}), h, h) * b1);
+        L.s_k = split_scale(2.0 * row_l1_max(st.get(b + ".self_attn.k_proj.weight", {h, h}), h, h) * b1);
         L.s_ffn = split_scale(linear_bound(st.get(b + ".mlp.fc1.weight", {c.inter, h}),
                                            st.get(b + ".mlp.fc1.bias", {c.inter}), c.inter, h, b2));
         layers_.push_back(L);
@@ -688,28 +690,28 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
     float* win = (float*)ws("win", M * h * 4);
     float* x = (float*)ws("x", M * h * 4);
     const SplitBuf n = ws2("n", M, h);  // LayerNorm output, fp16 split
-    // attention operands as bfloat16 pairs: Q, K [M, h]; V^T [h, M] (column = global row)
+    // attention operands in the fp16 split: Q, K [M, h]; V^T [h, M] (column = global row)
     AttnOperands ao;
-    ao.q_hi = ws("q_hi", M * h * 2);
-    ao.q_lo = ws("q_lo", M * h * 2);
-    ao.k_hi = ws("k_hi", M * h * 2);
-    ao.k_lo = ws("k_lo", M * h * 2);
+    ao.q_h = ws("q_h", M * h * 2);
+    ao.q_l = ws("q_l", M * h * 2);
+    ao.k_h = ws("k_h", M * h * 2);
+    ao.k_l = ws("k_l", M * h * 2);
     ao.vt_ld = M;
-    ao.vt_hi = ws("vt_hi", h * M * 2);
-    ao.vt_lo = ws("vt_lo", h * M * 2);
-    ao.rows_cap = (long long)(ws_["q_hi"].bytes / (h * 2));
+    ao.vt_h = ws("vt_h", h * M * 2);
+    ao.vt_l = ws("vt_l", h * M * 2);
+    ao.rows_cap = (long long)(ws_["q_h"].bytes / (h * 2));
     const SplitBuf ctx = ws2("ctx", M, h);     // attention context
     const SplitBuf f = ws2("f", M, c.inter);   // GELU(fc1)
 
     Epi e;  // QKV: Q/K pairs with RoPE, V^T pair
     e.mode = EPI_QKV_ATTN;
     e.tma = 1;
-    e.map_h = make_bf16_map(ao.q_hi, M, h, h, 64, 32, true);
-    e.map_l = make_bf16_map(ao.q_lo, M, h, h, 64, 32, true);
-    e.map_k_hi = make_bf16_map(ao.k_hi, M, h, h, 64, 32, true);
-    e.map_k_lo = make_bf16_map(ao.k_lo, M, h, h, 64, 32, true);
-    e.map_vt_hi = make_bf16_map(ao.vt_hi, h, M, ao.vt_ld, 32, 64, false);
-    e.map_vt_lo = make_bf16_map(ao.vt_lo, h, M, ao.vt_ld, 32, 64, false);
+    e.map_h = make_f16_map(ao.q_h, M, h, h, 64, 32, true);
+    e.map_l = make_f16_map(ao.q_l, M, h, h, 64, 32, true);
+    e.map_k_h = make_f16_map(ao.k_h, M, h, h, 64, 32, true);
+    e.map_k_l = make_f16_map(ao.k_l, M, h, h, 64, 32, true);
+    e.map_vt_h = make_f16_map(ao.vt_h, h, M, ao.vt_ld, 32, 64, false);
+    e.map_vt_l = make_f16_map(ao.vt_l, h, M, ao.vt_ld, 32, 64, false);
     e.cos_t = rope_cos_;
     e.sin_t = rope_sin_;
     e.rope_seq = S;
@@ -743,6 +745,9 @@ void Model::tower(int B, int S, const int* d_seq_len, const int* d_valid, float*
         prof_begin();
         launch_layer_norm(stream_, x, M, (int)h, L.ln1_w, L.ln1_b, n.out(L.s_ln1));
         prof_end(K_LN, 0, ln_bytes);
+        e.sec_scale[0] = ao.q_scale = L.s_q;
+        e.sec_scale[1] = ao.k_scale = L.s_k;
+        e.sec_scale[2] = ao.v_scale = L.s_ctx;
         prof_begin();
         gemm_split(stream_, n.op(L.s_ln1), L.qkv.op(), (int)M, (int)(3 * h), (int)h, 0, e, dev_err_);
         prof_end(K_GEMM_QKV, 2.0 * M * 3 * h * h, 0);

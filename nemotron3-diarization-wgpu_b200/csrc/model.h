@@ -64,12 +64,14 @@ struct SplitBuf {
 // Per layer: LayerNorm parameters, weights, and the fp16-split scales of the layer's
 // GEMM inputs, each from a bound on the tensor's magnitude known at load: the two
 // LayerNorm outputs (sqrt(cols - 1) max|w| + max|b|), the attention context (a convex
-// combination of V rows: max row L1 norm of W_v times the LayerNorm bound) and
-// GELU(fc1) (|gelu(x)| <= |x|: max over rows of L1(W_fc1) times the bound plus |b|).
+// combination of V rows: max row L1 norm of W_v times the LayerNorm bound; also V's
+// own scale), GELU(fc1) (|gelu(x)| <= |x|: max over rows of L1(W_fc1) times the bound
+// plus |b|), and the attention operands Q and K (rotate-half RoPE at most doubles the
+// bound of W_q n or W_k n).
 struct DevLayer {
     float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
     DevLinear qkv, o, fc1, fc2;
-    float s_ln1 = 1.0f, s_ln2 = 1.0f, s_ctx = 1.0f, s_ffn = 1.0f;
+    float s_ln1 = 1.0f, s_ln2 = 1.0f, s_ctx = 1.0f, s_ffn = 1.0f, s_q = 1.0f, s_k = 1.0f;
 };
 
 // ----------------------------------------------------------------- schedule

@@ -132,17 +132,6 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t saddr) {
     return d;
 }
 
-// Same for a K-major tile written with the 64-byte swizzle: rows of 64 B
-// (16 fp32), 8-row atoms 512 B apart, layout SWIZZLE_64B (4).
-__device__ __forceinline__ uint64_t desc_k_sw64(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
-    d |= static_cast<uint64_t>(1) << 16;
-    d |= static_cast<uint64_t>(512 >> 4) << 32;
-    d |= static_cast<uint64_t>(1) << 46;
-    d |= static_cast<uint64_t>(4) << 61;
-    return d;
-}
 
 // Instruction descriptor for kind::f16 with fp16 A and B: D f32, both K-major, M=128
 // (A/B format 0 = f16; 1 would be bf16).
@@ -416,23 +405,9 @@ __device__ __forceinline__ void split2x4(const float* x, float s, uint2& h, uint
     split2x2(x[2], x[3], s, h.y, l.y);
 }
 
-// ------------------------------------------------------ 3xBF16 (kind::f16)
-// Attention operands are bfloat16 pairs (hi + lo, ~16 significant bits).
-// Instruction descriptor for kind::f16: D f32, A/B bf16, both K-major, M=128.
-__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | ((128u >> 4) << 24);
-}
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// A operand in TMEM: two bf16 per 32-bit column (the lower k in the low half).
-__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+// ------------------------------------------------------ TMEM A operands (kind::f16)
+// A operand in TMEM: two 16-bit values per 32-bit column (the lower k in the low half).
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                              uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -440,29 +415,6 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, u
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
-}
-// Store 16 consecutive TMEM columns of this thread's lane (32x32b shape, x16).
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-        : "memory");
-}
-// (a, b) -> bfloat16 pairs x = hi + lo, packed two per word with a in the low half:
-// hi = x rounded to 8 significant bits (nearest, ties away from zero) by integer
-// operations on the bit pattern, lo = RN-bf16(x - hi) (x - hi is exact in fp32).
-// hi + lo carries ~16 significant bits; the three products lo*hi + hi*lo + hi*hi keep
-// that precision.  Only lo uses the conversion pipe.
-__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-    const uint32_t ra = (__float_as_uint(a) + 0x8000u) & 0xffff0000u;
-    const uint32_t rb = (__float_as_uint(b) + 0x8000u) & 0xffff0000u;
-    hi = __byte_perm(ra, rb, 0x7632);  // the high halves: a's low, b's high
-    uint32_t l;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(l)
-        : "f"(__fsub_rn(b, __uint_as_float(rb))), "f"(__fsub_rn(a, __uint_as_float(ra))));
-    lo = l;
 }
 
 }  // namespace n3d

@@ -80,8 +80,9 @@ enum EpiMode : int {
     EPI_GELU_SPLIT = 2,  // fp16 split of gelu(v) * out_scale
     EPI_RELU_SPLIT = 4,  // fp16 split of relu(v) * out_scale
     EPI_DENSE_OUT = 6,   // r = relu(v); out[r, 0:ns] = r . w2^T + b2
-    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> bf16 pairs [rows, heads*64] (map_h / map_l,
-                         // map_k_*); V -> transposed bf16 pair V^T[head*64 + d][row] (map_vt_*); TMA only
+    EPI_QKV_ATTN = 7,    // Q, K rotated by RoPE -> fp16 splits [rows, heads*64] (map_h / map_l,
+                         // map_k_*); V -> transposed fp16 split V^T[head*64 + d][row] (map_vt_*), with
+                         // the scales sec_scale[0..2]; TMA only
 };
 
 struct Epi {
@@ -89,6 +90,7 @@ struct Epi {
     const float* bias = nullptr;
     float acc_scale = 1.0f;  // set by gemm_split from the operands' scales
     float out_scale = 1.0f;  // the split modes' output scale (the consumer operand's s)
+    float sec_scale[3] = {1.0f, 1.0f, 1.0f};  // EPI_QKV_ATTN: the Q, K and V scales
     // Direct stores: out (fp32, EPI_STORE and EPI_DENSE_OUT), out_h and out_l (the
     // fp16 arrays of the split modes).
     float* out = nullptr;
@@ -109,7 +111,7 @@ struct Epi {
     int q_cols = 0, k_cols = 0;  // [0,q_cols) is Q, [q_cols,q_cols+k_cols) is K
     // Stores through TMA (tma != 0), box 32 columns x 32 rows: map_out fp32 (128-byte
     // swizzle, make_store_map), map_h / map_l fp16 (64-byte swizzle,
-    // make_store_map_f16).  EPI_QKV_ATTN: bf16 maps from make_bf16_map -- map_h /
+    // make_store_map_f16).  EPI_QKV_ATTN: fp16 maps from make_f16_map -- map_h /
     // map_l (Q) and map_k_* with box 64 x 32 and the 128-byte swizzle, map_vt_* over
     // V^T [heads*64, rows] with box 32 x 64 and no swizzle.
     int tma = 0;
@@ -122,7 +124,7 @@ struct Epi {
     // ((p0 + p1 + ...) + bias) into the destination in split order (deterministic).
     float* split_ws = nullptr;
     long long split_ws_floats = 0;
-    CUtensorMap map_out, map_h, map_l, map_k_hi, map_k_lo, map_vt_hi, map_vt_lo;
+    CUtensorMap map_out, map_h, map_l, map_k_h, map_k_l, map_vt_h, map_vt_l;
     // EPI_DENSE_OUT second projection
     const float* w2 = nullptr;
     const float* b2 = nullptr;
@@ -148,12 +150,10 @@ float split_scale(double bound);
 // fp16 matrix (64-byte swizzle).
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
 CUtensorMap make_store_map_f16(const void* p, long long rows, long long cols, long long ld);
-// 2-D map over a row-major bfloat16 matrix [rows, cols] with row stride ld elements;
+// 2-D map over a row-major fp16 matrix [rows, cols] with row stride ld elements;
 // box box_cols x box_rows, 128-byte swizzle when `swizzle` (box_cols must then be 64).
-CUtensorMap make_bf16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
-                          bool swizzle);
-// The same over an fp16 matrix, 128-byte swizzle (box_cols 64).
-CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows);
+CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long long ld, int box_cols, int box_rows,
+                         bool swizzle);
 
 // C[M, N] = A[M, K] * B[N, K]^T with the fp16 split on tcgen05 (gemm.cu).  K % 32 == 0
 // (k-blocks of 64; a last half block reads zeros past K).  `kb_per_tap` > 0 turns on
@@ -199,14 +199,15 @@ void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int n
 void launch_split(cudaStream_t s, const float* x, long long n, SplitOut out);
 // max |x| over n floats (n % 4 == 0) into *d_max (a float the caller zeroes first).
 void launch_absmax(cudaStream_t s, const float* x, long long n, float* d_max);
-// Operands of the tcgen05 attention (head_dim hd = 64 or 128), all bfloat16 hi/lo
-// pairs: Q, K [rows_cap, heads*hd] with sequence b at rows b*S..; V^T [heads*hd, vt_ld]
-// whose column is the global row.
+// Operands of the tcgen05 attention (head_dim hd = 64 or 128), all in the fp16 split
+// (h, l) of the values times their power-of-two scale: Q, K [rows_cap, heads*hd] with
+// sequence b at rows b*S..; V^T [heads*hd, vt_ld] whose column is the global row.
 struct AttnOperands {
-    const void *q_hi = nullptr, *q_lo = nullptr, *k_hi = nullptr, *k_lo = nullptr;
+    const void *q_h = nullptr, *q_l = nullptr, *k_h = nullptr, *k_l = nullptr;
     long long rows_cap = 0;
-    const void *vt_hi = nullptr, *vt_lo = nullptr;
+    const void *vt_h = nullptr, *vt_l = nullptr;
     long long vt_ld = 0;
+    float q_scale = 1.0f, k_scale = 1.0f, v_scale = 1.0f;
 };
 // tcgen05 attention (attention_tc.cu), head_dim 64 or 128; S (when seqs > 1) and
 // vt_ld must be multiples of 8.  Context [seqs*S, heads*hd] in the fp16 split (or

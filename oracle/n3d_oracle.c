@@ -877,6 +877,13 @@ float orc_round2(float v) {
 
 static float sigmoidf(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+/* frame_check's decision per logit (src/bin/frame_check.rs:188-190): the f32 sigmoid
+ * above 0.5, with the same f32 exp the segments use, so that a counted flip and a
+ * changed segment come from the same arithmetic. */
+void orc_sigmoid_above_half(const float *logits, size_t n, uint8_t *out) {
+    for (size_t i = 0; i < n; i++) out[i] = sigmoidf(logits[i]) > 0.5f;
+}
+
 static int seg_cmp(const void *a, const void *b) {
     const orc_segment *x = a, *y = b;
     if (x->start < y->start) return -1;

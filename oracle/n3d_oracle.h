@@ -131,6 +131,7 @@ void orc_run_output_free(orc_run_output *o);
 
 /* ---- src/segments.rs ---- */
 float orc_round2(float v);
+void orc_sigmoid_above_half(const float *logits, size_t n, uint8_t *out);
 size_t orc_extract_speaker_dict(const float *logits, size_t num_frames, size_t ns, float duration,
                                 const uint8_t *mask, float threshold, orc_segment *out, size_t cap);
 float orc_activity_stats(const float *logits, size_t num_frames, size_t ns, const uint8_t *mask, float threshold,

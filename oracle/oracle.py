@@ -116,6 +116,7 @@ def lib():
         L.orc_num_popped.restype = _sz
         L.orc_frame_scores.argtypes = [C.POINTER(CacheCfg), _f32p, _sz, _f32p]
         L.orc_boost_top.argtypes = [C.POINTER(CacheCfg), _f32p, _sz, _sz, C.c_float]
+        L.orc_sigmoid_above_half.argtypes = [_f32p, _sz, _u8p]
         L.orc_compress_picked.argtypes = [C.POINTER(CacheCfg), _f32p, _sz, np.ctypeslib.ndpointer(np.uintp)]
         L.orc_compress_picked.restype = _sz
         L.orc_compress.argtypes = [C.POINTER(CacheCfg), _sz, _f32p, _f32p, _sz, _f32p, _f32p, _f32p]
@@ -308,6 +309,14 @@ def compress(cc: CacheCfg, hidden, embeds, probs, num_frames, silence):
 
 def round2(v: float) -> float:
     return lib().orc_round2(v)
+
+
+def sigmoid_above_half(logits) -> np.ndarray:
+    """frame_check's per-logit decision, the f32 sigmoid above 0.5 (src/bin/frame_check.rs:188-190)."""
+    lg = f32(logits).ravel()
+    out = np.zeros(lg.size, np.uint8)
+    lib().orc_sigmoid_above_half(lg, lg.size, out)
+    return out.astype(bool)
 
 
 def extract_speaker_dict(logits, num_frames, ns, duration, mask=None, threshold=0.5):

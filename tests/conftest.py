@@ -103,14 +103,14 @@ def frame_check(got, want, ns=8, duration=0.01):
         return res
     d = np.abs(got.astype(np.float64) - want.astype(np.float64))
     res["maxdiff"] = float(d.max()) if d.size else 0.0
-    # the sigmoid in f32, as the gate computes it (src/bin/frame_check.rs:188-189): a
-    # logit within about 3e-8 of zero gives exactly 0.5, which is not a decision
-    one = np.float32(1.0)
-    sg = one / (one + np.exp(-got, dtype=np.float32))
-    sw = one / (one + np.exp(-want, dtype=np.float32))
-    assert sg.dtype == sw.dtype == np.float32
-    flips = np.argwhere((sg > 0.5) != (sw > 0.5))
+    # the decision sigmoid(x) > 0.5 in f32, as the gate computes it
+    # (src/bin/frame_check.rs:188-190), with the oracle's libm expf -- the arithmetic its
+    # segments use.  In f32 a logit below about 1.2e-7 gives exactly 0.5, not a decision.
+    dg = oracle.sigmoid_above_half(got).reshape(got.shape)
+    dw = oracle.sigmoid_above_half(want).reshape(want.shape)
+    flips = np.argwhere(dg != dw)
     res["flips"] = int(len(flips))
+    res["flip_ref_abs_max"] = float(np.abs(want[flips[:, 0], flips[:, 1]]).max()) if len(flips) else 0.0
     # each flip as (row, speaker, reference logit, our logit), for the failure message
     res["flip_values"] = [(int(r), int(c), float(want[r, c]), float(got[r, c])) for r, c in flips[:8]]
     a = oracle.extract_speaker_dict(got.ravel(), got.shape[0], ns, duration)
