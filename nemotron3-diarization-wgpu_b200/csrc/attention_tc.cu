@@ -11,8 +11,9 @@
 // h + l of the values times a power-of-two scale; each k-step issues l*h + h*l + h*h
 // into an fp32 accumulator, ~2^-22 per product, at the 16-bit tensor rate.  Q, K and
 // V carry the scales the QKV epilogue gave them (from load-time bounds); P <= 2^8
-// (the lazy rescale below) is scaled by 2^7.  The score scale 1/sqrt(hd) log2 e is
-// divided by s_Q s_K, and the context by 2^7 s_V, exactly (powers of two).
+// (the lazy rescale below) is kept as P * 2^7, the 7 added to its exponent.  The score
+// scale 1/sqrt(hd) log2 e is divided by s_Q s_K, and the context by s_V (the row sum l
+// carries P's 2^7), exactly (powers of two).
 //
 // CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM at head_dim
 // 64, one at 128 (its ring and TMEM are twice as large):
@@ -71,7 +72,19 @@ struct AttnCfg {
     static_assert(4 * 32 * HD * 4 == STAGE_BYTES, "the context staging of the 4 softmax warps fills slot 0");
 };
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
-constexpr float P_SCALE = 128.0f;         // P <= 2^8, so P * 2^7 <= 2^15 stays in fp16's range
+constexpr float P_LOG2_SCALE = 7.0f;      // P <= 2^8 is kept as P * 2^7 <= 2^15, inside fp16's range
+
+// Two scaled probabilities x = P * 2^7 in [0, 2^15] -> their fp16 split words (a in the
+// low half).  h = x rounded to 11 significant bits, its fp16 bits formed with integer
+// operations ((bits(x) + 2^12 - (112 << 23)) >> 13: rebias the exponent, drop 13
+// mantissa bits); x below fp16's normal range takes h = 2^-14 and a negative l.  Only
+// l goes through the conversion pipe.
+__device__ __forceinline__ void split_p2(float a, float b, uint32_t& h, uint32_t& l) {
+    const uint32_t ua = __float_as_uint(fmaxf(a, 6.103515625e-05f)) + 0x1000u;
+    const uint32_t ub = __float_as_uint(fmaxf(b, 6.103515625e-05f)) + 0x1000u;
+    h = __byte_perm((ua - 0x38000000u) >> 13, (ub - 0x38000000u) >> 13, 0x5410);
+    l = f16x2_rn(__fsub_rn(a, __uint_as_float(ua & 0xffffe000u)), __fsub_rn(b, __uint_as_float(ub & 0xffffe000u)));
+}
 
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
@@ -311,7 +324,9 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             const bool raise = (mb - m) * k2 > RESCALE_LOG2;      // always on the first block (m = -inf)
             const float corr = raise ? ex2_approx((m - mb) * k2) : 1.0f;  // 0 on the first block
             if (raise) m = mb;
-            const uint64_t k22 = pack2(k2, k2), nmk = pack2(-m * k2, -m * k2);
+            // exponents carry the 2^7 scale of P: s = 2^(t + 7) = P * 2^7, and l sums those
+            const float off = P_LOG2_SCALE - m * k2;
+            const uint64_t k22 = pack2(k2, k2), nmk = pack2(off, off);
             uint64_t sum2[4] = {0, 0, 0, 0};  // four independent packed partial sums
 #pragma unroll
             for (int c = 0; c < 64; c += 2) {
@@ -326,7 +341,7 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             l = l * corr + (sa + sb);
             uint32_t hi[32], lo[32];
 #pragma unroll
-            for (int i = 0; i < 32; i++) split2x2(s[2 * i], s[2 * i + 1], P_SCALE, hi[i], lo[i]);
+            for (int i = 0; i < 32; i++) split_p2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
             if (j > 0) {
                 // PV_{j-1} has read the P buffer and finished O up to block j-1
                 ok = __all_sync(0xffffffffu,
@@ -454,7 +469,7 @@ void launch_attention_hd(cudaStream_t s, const AttnOperands& op, int seqs, int S
     }
     dim3 grid((S + QT - 1) / QT, heads, seqs);
     const float k2 = (float)((1.0 / std::sqrt((double)HD)) * 1.4426950408889634 / ((double)op.q_scale * op.k_scale));
-    const float out_unscale = (float)(1.0 / ((double)P_SCALE * op.v_scale));
+    const float out_unscale = (float)(1.0 / (double)op.v_scale);  // l already carries P's 2^7
     launch_pdl(attention_tc_kernel<HD>, grid, dim3(THREADS), Cfg::SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma,
                k2, out_unscale, err);
 }

@@ -215,7 +215,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
                  : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // One warp's 32 x 32 fp32 block into a 4 KB 128-byte-swizzled staging box: lane = box row.
@@ -232,9 +232,11 @@ __device__ __forceinline__ void stage_rows_16(uint8_t* box, int lane, const uint
         *reinterpret_cast<uint4*>(box + lane * 64 + ((i ^ ((lane >> 1) & 3)) << 4)) =
             make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 }
-// The warp's previous boxes must have been read before they are overwritten.
+// The staging area is double-buffered: consecutive store groups of a warp alternate
+// between its two halves, so before a half is overwritten only the group before the
+// latest -- the last one that used this half -- must have finished reading it.
 __device__ __forceinline__ void stage_begin(int lane) {
-    if (lane == 0) bulk_wait_read0();
+    if (lane == 0) bulk_wait_read1();
     __syncwarp();
 }
 // Make the staged boxes visible to the TMA unit and store them (up to three maps);
@@ -257,10 +259,13 @@ __device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, con
 
 // Epilogue with TMA stores, for modes whose output rows are the tile's rows:
 // EPI_STORE, EPI_SPLIT, EPI_GELU_SPLIT, EPI_RELU_SPLIT, EPI_QKV_ATTN, over accumulator
-// columns [c_begin, c_end).  `stg` is this warp's 8 KB staging area.
+// columns [c_begin, c_end).  `stg` is this warp's 8 KB staging area, two 4 KB halves
+// that consecutive store groups alternate between (`sbuf` counts the warp's groups
+// across tiles).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
-                                                  int lane, uint8_t* stg, int c_begin = 0, int c_end = BN) {
+                                                  int lane, uint8_t* stg, uint32_t& sbuf, int c_begin = 0,
+                                                  int c_end = BN) {
     const int mode = epi.mode;
     const int rowbase = m0 + q * 32;
     if (rowbase >= M) return;  // whole warp past the end: nothing to load or store
@@ -303,16 +308,24 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int i = 0; i < 32; i++) split2x2(v[2 * i], v[2 * i + 1], sc, hi[i], lo[i]);
-            stage_begin(lane);
+            // h goes out from the first half, then l from the second, each as its own group
             if (sec < 2) {
+                stage_begin(lane);
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
                     *reinterpret_cast<uint4*>(bhi + o) = make_uint4(hi[4 * i], hi[4 * i + 1], hi[4 * i + 2], hi[4 * i + 3]);
+                }
+                stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_h, bhi, nullptr, nullptr, nullptr, nullptr, hcol,
+                            rowbase);
+                stage_begin(lane);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
                     *reinterpret_cast<uint4*>(blo + o) = make_uint4(lo[4 * i], lo[4 * i + 1], lo[4 * i + 2], lo[4 * i + 3]);
                 }
-                stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_h, bhi,
-                            sec == 0 ? &epi.map_l : &epi.map_k_l, blo, nullptr, nullptr, hcol, rowbase);
+                stage_issue(lane, sec == 0 ? &epi.map_l : &epi.map_k_l, blo, nullptr, nullptr, nullptr, nullptr, hcol,
+                            rowbase);
             } else {
                 // transpose by lane pairs: word i of lane L holds d = 2i, 2i + 1 of token L;
                 // an even lane stores row 2i for tokens L, L + 1 and an odd lane row 2i + 1
@@ -320,23 +333,27 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                 // disjoint banks)
                 const bool odd = lane & 1;
                 const int tok = (lane & ~1) * 2;
+                stage_begin(lane);
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const uint32_t ph = __shfl_xor_sync(0xffffffffu, hi[i], 1);
-                    const uint32_t pl = __shfl_xor_sync(0xffffffffu, lo[i], 1);
                     const int row = (2 * i + (odd ? 1 : 0)) * 64 + tok;
                     *reinterpret_cast<uint32_t*>(bhi + row) = odd ? __byte_perm(ph, hi[i], 0x7632) : __byte_perm(hi[i], ph, 0x5410);
+                }
+                stage_issue(lane, &epi.map_vt_h, bhi, nullptr, nullptr, nullptr, nullptr, rowbase, hcol);
+                stage_begin(lane);
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const uint32_t pl = __shfl_xor_sync(0xffffffffu, lo[i], 1);
+                    const int row = (2 * i + (odd ? 1 : 0)) * 64 + tok;
                     *reinterpret_cast<uint32_t*>(blo + row) = odd ? __byte_perm(pl, lo[i], 0x7632) : __byte_perm(lo[i], pl, 0x5410);
                 }
-                stage_issue(lane, &epi.map_vt_h, bhi, &epi.map_vt_l, blo, nullptr, nullptr, rowbase, hcol);
+                stage_issue(lane, &epi.map_vt_l, blo, nullptr, nullptr, nullptr, nullptr, rowbase, hcol);
             }
         }
         return;
     }
     const bool split = mode != EPI_STORE;
-    uint8_t* bst = stg;          // 4 KB fp32 box (EPI_STORE)
-    uint8_t* bh = stg;           // 2 KB fp16 box (split modes)
-    uint8_t* bl = stg + 2048;    // 2 KB fp16 box
     const uint64_t sc2 = pack2(epi.acc_scale, epi.acc_scale);
     for (int c = c_begin; c < c_end; c += 32) {
         float v[32];
@@ -355,6 +372,10 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
 #pragma unroll
             for (int i = 0; i < 32; i++) v[i] = epi_value(mode, v[i], epi.acc_scale, bias[i]);
         }
+        uint8_t* half = stg + (sbuf++ & 1u) * 4096;
+        uint8_t* bst = half;         // 4 KB fp32 box (EPI_STORE)
+        uint8_t* bh = half;          // 2 KB fp16 box (split modes)
+        uint8_t* bl = half + 2048;   // 2 KB fp16 box
         stage_begin(lane);
         if (split) {
             uint32_t hw[16], lw[16];
@@ -522,6 +543,7 @@ __global__ void __launch_bounds__(192, 1)
             asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
         }
         int it = 0;
+        uint32_t sbuf = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, it++) {
             const int buf = it & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (it >> 1) & 1, err, DEV_TIMEOUT_ACC));
@@ -532,7 +554,7 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * Cfg::ACC_COLS;
             if (epi.tma)  // a k split's partial rows start at ks * Mp (rows past M land in padding)
                 epilogue_tile_tma<BN>(epi, tl, m0 + ks * Mp, n0, ksplit > 1 ? ksplit * Mp : M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192);
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, sbuf);
             else
                 epilogue_tile<BN>(epi, tl, m0, n0, M, N, q, lane, w2s);
             tc_fence_before();
@@ -675,6 +697,7 @@ __global__ void __launch_bounds__(192, 1)
         const int q = warp & 3;
         const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
         int it = 0;
+        uint32_t sbuf = 0;
         for (int t = cid; t < tiles; t += ncl, it++) {
             const int buf = it & 1;
             const bool ok =
@@ -686,7 +709,8 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
             if (epi.tma)
                 epilogue_tile_tma<BN>(epi, tl, m0, tile.n0, M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, 0, tile.nw);
+                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, sbuf, 0,
+                                      tile.nw);
             else  // direct stores
                 epilogue_tile<BN>(epi, tl, m0, tile.n0, M, N, q, lane, nullptr, tile.nw);
             tc_fence_before();

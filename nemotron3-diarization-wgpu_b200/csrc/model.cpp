@@ -325,9 +325,26 @@ ClipPlan plan_streaming(const Config& c, long long n, int mode) {
         sp.seg = (int)i;
         sp.group_lo = 0;
         sp.n_new = (int)groups;
+        // An uncentred chunk after the first or another uncentred chunk starts exactly
+        // c * 8 mel frames later on the same frame grid (Model::streaming_chunks,
+        // src/model.rs:343-365), so its first r = look-ahead groups are the previous
+        // chunk's last r: the same samples, and the same pre-emphasised values wherever
+        // the Hann window is non-zero (the chunk's own first sample, which has no
+        // predecessor in its slice, falls under the window's zero taps).  Those
+        // embeddings are taken from the previous step; only the c new groups are
+        // computed.  The final chunk is centred on a shifted grid and computed whole.
+        if (i > 0 && !ch.centered && (i == 1 || !chunks[i - 1].centered)) {
+            const int r = chunks[i - 1].lookahead;
+            const long long prev_groups = ceil_div(chunks[i - 1].mel_frames, c.sub);
+            if (r > 0 && groups > r && prev_groups >= r) {
+                sp.reuse = r;
+                sp.group_lo = r;
+                sp.n_new = (int)(groups - r);
+            }
+        }
         sp.nchunk = (int)(groups - ch.lookahead);
         const int prefix = cs.ncache + cs.nfifo;
-        sp.S = prefix + sp.n_new;
+        sp.S = prefix + sp.reuse + sp.n_new;
         sp.valid = sp.S;
         sp.keep_rows = (int)std::min((long long)sp.nchunk * c.sub, nm);
         cs.step(sp);
@@ -896,6 +913,18 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 N3D_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
                 upload_ev_.push_back(e);
             }
+        // A step reuses the previous step's embedding rows only when both embed in the
+        // same phase (host audio: step 0 embeds in phase 0, the rest in phase 1); step 1
+        // of a two-phase batch embeds its whole chunk instead.
+        if (nphase == 2)
+            for (int i = 0; i < nb; i++) {
+                std::vector<StepPlan>& st = plans[c0 + i].steps;
+                if (st.size() > 1 && st[1].reuse > 0) {
+                    st[1].group_lo -= st[1].reuse;
+                    st[1].n_new += st[1].reuse;
+                    st[1].reuse = 0;
+                }
+            }
         for (int i = 0; i < nb; i++) {
             const ClipPlan& p = plans[c0 + i];
             const int nseg = (int)p.segs.size();
@@ -997,7 +1026,9 @@ void Model::run_batch(int mode, const std::vector<const float*>& host_audio, con
                 q.was_compressed = sp.was_compressed;
                 q.keep_rows = sp.keep_rows;
                 const PartRef& pr = ref[i][sp.seg][nphase == 2 && w > 0 ? 1 : 0];
-                q.emb_row = pr.base + (sp.group_lo - pr.lo);
+                // reused rows: the previous step's last rows, which end where this
+                // step's segment begins in the same phase
+                q.emb_row = pr.base + (sp.group_lo - pr.lo) - sp.reuse;
                 const int cur = w & 1, nxt = cur ^ 1;
                 q.pre_in = pre + ((size_t)cur * nb + i) * pre_rows * h;
                 q.pre_out = pre + ((size_t)nxt * nb + i) * pre_rows * h;

@@ -95,8 +95,12 @@ inline int mel_frames(const MelSeg& m, int sub) {
 struct StepPlan {
     int S, valid, ncache, nfifo, nchunk, popped, compress, was_compressed, keep_rows;
     int seg;              // mel segment holding this step's new frames
-    int group_lo;         // first new group within that segment
-    int n_new;            // new embedding rows
+    int group_lo;         // first group of that segment the step embeds
+    int n_new;            // groups of that segment it embeds
+    // Embedding rows taken from the previous step instead (streaming middle chunks): the
+    // window's new rows are the previous step's last `reuse` rows, then the n_new rows
+    // from group_lo on.  0 = none.
+    int reuse;
 };
 
 struct ClipPlan {

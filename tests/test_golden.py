@@ -93,3 +93,28 @@ def test_gpu_linear_matches_golden():
     n3d.linear(0, dx.data_ptr(), m, k, dw.data_ptr(), n, db.data_ptr(), dy.data_ptr())
     torch.cuda.synchronize()
     assert np.abs(dy.cpu().numpy().reshape(m, n) - _load("linear_17x24x512.npy")).max() < 1e-3
+
+
+def test_gate_decision_is_the_f32_sigmoid_with_libm_expf():
+    """frame_check decides sigmoid(x) > 0.5 in f32 (src/bin/frame_check.rs:188-190).  The
+    oracle's decision helper must be exactly 1 / (1 + expf(-x)) > 0.5 with libm's expf,
+    the arithmetic of its segments: around the boundary (the smallest deciding logit is
+    8.94e-8, where the f32 sigmoid stops rounding to 0.5) numpy's float32 exp rounds
+    differently."""
+    import ctypes
+
+    import oracle
+
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.argtypes = [ctypes.c_float]
+    libm.expf.restype = ctypes.c_float
+    xs = np.concatenate([np.linspace(-3e-7, 3e-7, 601), [0.0, -0.0, 8.94069742685133e-08, 1.0, -1.0, 40.0, -40.0]])
+    xs = xs.astype(np.float32)
+    want = []
+    for x in xs:
+        e = np.float32(libm.expf(ctypes.c_float(-x)))
+        want.append(np.float32(1.0) / (np.float32(1.0) + e) > np.float32(0.5))
+    got = oracle.sigmoid_above_half(xs)
+    assert list(got) == want
+    b = np.float32(8.94069742685133e-08)
+    assert oracle.sigmoid_above_half(np.array([np.nextafter(b, np.float32(0)), b], np.float32)).tolist() == [False, True]
