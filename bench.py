@@ -246,7 +246,18 @@ def dist_setup(backend: str | None = None, timeout_s: float = 600.0):
         if backend == "nccl":
             torch.cuda.set_device(local)
             kw["device_id"] = torch.device("cuda", local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+        # NCCL may print a version banner on stdout while it creates the communicator;
+        # stdout carries only the bench's JSON line, so the banner goes to stderr
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     return world, rank, local
 
 
@@ -427,7 +438,8 @@ def main():
                    help="c4 offline line: sessions per GPU of the streaming sub-record (0 skips it)")
     p.add_argument("--streaming-seconds", type=float, default=120.0)
     args = p.parse_args()
-    world, rank, local = dist_setup()
+    # the reference arm runs on host cores only: its ranks need no NCCL
+    world, rank, local = dist_setup("gloo" if args.impl == "reference" else None)
     if args.impl == "reference":
         run_reference(args, world, rank)
         if world > 1:
