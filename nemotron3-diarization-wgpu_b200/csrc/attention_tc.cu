@@ -16,31 +16,37 @@
 // carries P's 2^7), exactly (powers of two).
 //
 // CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM at head_dim
-// 64, one at 128 (its ring and TMEM are twice as large):
-//   warp 0      TMA: the CTA's Q pair into ring slot 2, then per block of 64 keys
-//               the K pair and the V^T pair into a 3-stage ring (two blocks of
-//               prefetch hide the load latency; slot 2 once Q has moved to TMEM)
-//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T as soon as the softmax
-//               has read S_{j-1}, and O += P_j V_j; both MMAs take their A operand
-//               (Q, P) from TMEM, so only K / V^T are read from shared memory
+// 64, one at 128 (its rings and TMEM are twice as large):
+//   warp 0      TMA: the CTA's Q pair (into the V ring, until the softmax warps have
+//               copied it to TMEM), then per block of 64 keys the K pair into a
+//               2-stage K ring and the V^T pair into a 2-stage V ring.  K_{j+2} loads
+//               once QK_j has completed, V_{j+2} once PV_j has, so the K loads run a
+//               block ahead of the V loads
+//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T and O += P_j V_j.  Both
+//               MMAs take their A operand (Q, P) from TMEM, so only K / V^T are read
+//               from shared memory
 //   warps 2..5  softmax, one thread per query row (TMEM lane): first the row's Q
-//               pair from shared memory into TMEM; per block the row's 64 scores, exp as 2^x on the
-//               special-function unit after one FMA folds the 1/sqrt(hd) scale,
-//               log2 e and the reference max together; then, once PV_{j-1} has
-//               read the P buffer, P_j as fp16 splits.
+//               pair from shared memory into TMEM; per block the row's 64 scores, exp
+//               as 2^x on the special-function unit after one FMA folds the
+//               1/sqrt(hd) scale, log2 e and the reference max together; then P_j as
+//               fp16 splits, written over S_j.
+// S / P double buffer: block j uses TMEM buffer j % 2; the softmax writes P_j over the
+// S_j it has read, PV_j reads it, and QK_{j+2} is issued into it once PV_j has
+// completed.  QK_{j+1} therefore computes while the softmax works on S_j, and the
+// softmax never waits for a PV except to rescale O.
 // Lazy rescaling: exponents use a per-row reference max m that is raised only when
 // a block's max exceeds it by more than 2^8 in the exponent; only then is O
 // (in TMEM) multiplied by the correction, after PV_{j-1} has completed and before
 // P_j is released.  P values stay below 2^8; O / l is unchanged mathematically.
-// Context rows leave through shared memory (the ring, free once the last PV is done)
-// and TMA stores, a warp's 32 rows at a time.
-// TMEM: S 0..63, P 64..127 (hi 64.., lo 96..), O 128..128+HD-1, Q 128+HD..128+2HD-1
-// (h first, then l); 16-bit operands two per 32-bit column.  256 columns at head_dim
-// 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of 64 columns (the
-// 128-byte swizzle's limit), as is the Q tile.
-// Barriers with a phase per key block
-// are double-buffered by block parity, so every waiter is at most one phase behind.
-// Every wait is bounded; an expired wait records its site in *err.
+// Context rows leave through shared memory (the K ring, free once the last QK is
+// done) and TMA stores, a warp's 32 rows at a time.
+// TMEM: S/P buffers 0..63 and 64..127 (P hi at +0, lo at +32), O 128..128+HD-1, Q
+// 128+HD..128+2HD-1 (h first, then l); 16-bit operands two per 32-bit column.  256
+// columns at head_dim 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of
+// 64 columns (the 128-byte swizzle's limit), as is the Q tile.
+// Every barrier is double-buffered by block parity and every waiter is at most one
+// phase behind (argued at each wait).  Every wait is bounded; an expired wait records
+// its site in *err.
 
 #include <cmath>
 
@@ -55,8 +61,7 @@ constexpr int QT = 128;                   // queries per CTA
 constexpr int KB = 64;                    // keys per block
 constexpr int BOX = KB * 128;             // one 64-column TMA box of 64 rows: 8 KB
 constexpr int THREADS = 192;
-constexpr int NSTAGE = 3;
-constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128;
+constexpr uint32_t COL_SP = 0, COL_O = 128;  // S/P buffer b at COL_SP + 64 b
 constexpr int DEV_TIMEOUT_ATTN = 5;
 
 template <int HD>
@@ -64,12 +69,13 @@ struct AttnCfg {
     static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
     static constexpr int KTILE = KB * HD * 2;                  // K block [64 keys x HD] fp16
     static constexpr int VTILE = HD * KB * 2;                  // V^T block [HD x 64 keys] fp16
-    static constexpr int STAGE_BYTES = 2 * KTILE + 2 * VTILE;  // K_hi, K_lo, V^T_hi, V^T_lo
-    static constexpr int SMEM_BYTES = NSTAGE * STAGE_BYTES + 1024 + 256;
+    static constexpr int KSTAGE = 2 * KTILE, VSTAGE = 2 * VTILE;  // hi + lo
+    static constexpr int RING_BYTES = 2 * KSTAGE + 2 * VSTAGE;    // 2-stage K ring, then 2-stage V ring
+    static constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
     static constexpr uint32_t COL_Q = COL_O + HD, TMEM_COLS = HD == 64 ? 256 : 512;
     static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
-    static_assert(2 * QT * HD * 2 == STAGE_BYTES, "the Q pair fills ring slot 2");
-    static_assert(4 * 32 * HD * 4 == STAGE_BYTES, "the context staging of the 4 softmax warps fills slot 0");
+    static_assert(2 * QT * HD * 2 == 2 * VSTAGE, "the Q pair fills the V ring");
+    static_assert(4 * 32 * HD * 4 == 2 * KSTAGE, "the context staging of the 4 softmax warps fills the K ring");
 };
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
 constexpr float P_LOG2_SCALE = 7.0f;      // P <= 2^8 is kept as P * 2^7 <= 2^15, inside fp16's range
@@ -135,37 +141,38 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
     attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
                         SplitOut ctx, int ctx_tma, float k2, float out_unscale, int* err) {
     using Cfg = AttnCfg<HD>;
-    constexpr int STAGE_BYTES = Cfg::STAGE_BYTES, KTILE = Cfg::KTILE, VTILE = Cfg::VTILE;
+    constexpr int KTILE = Cfg::KTILE, VTILE = Cfg::VTILE, KSTAGE = Cfg::KSTAGE, VSTAGE = Cfg::VSTAGE;
     constexpr uint32_t COL_Q = Cfg::COL_Q, TMEM_COLS = Cfg::TMEM_COLS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* stages = smem;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(stages + NSTAGE * STAGE_BYTES);
-    uint64_t* q_ready = bars;       // 1: Q pair in TMEM (4 warps)
-    uint64_t* kv_full = bars + 1;   // NSTAGE
-    uint64_t* kv_empty = bars + 4;  // NSTAGE
-    uint64_t* s_full = bars + 7;    // 1: phase j = QK_j committed
-    uint64_t* s_free = bars + 8;    // 1: phase j = S_j read by the softmax (4 warps)
-    uint64_t* p_full = bars + 9;    // 2: P_j in TMEM, any rescale of O done (4 warps)
-    uint64_t* o_full = bars + 11;   // 2: PV_j committed (j % 2); a waiter for PV_j has always seen PV_{j-2}
-    uint64_t* q_full = bars + 13;   // 1: the Q pair has landed in ring slot 2
+    uint8_t* kring = smem;                  // K pair of block j in stage j % 2
+    uint8_t* vring = smem + 2 * KSTAGE;     // V^T pair of block j in stage j % 2
+    uint8_t* q_smem = vring;                // Q hi [HD/64 boxes of 128 rows x 128 B], then Q lo
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::RING_BYTES);
+    uint64_t* q_full = bars;        // 1: the Q pair has landed in the V ring
+    uint64_t* q_ready = bars + 1;   // 1: Q pair in TMEM, V ring free (4 warps)
+    uint64_t* k_full = bars + 2;    // 2: K_j landed (stage j % 2)
+    uint64_t* k_empty = bars + 4;   // 2: QK_j completed
+    uint64_t* v_full = bars + 6;    // 2: V_j landed
+    uint64_t* v_empty = bars + 8;   // 2: PV_j completed
+    uint64_t* s_full = bars + 10;   // 2: QK_j committed into buffer j % 2
+    uint64_t* p_full = bars + 12;   // 2: P_j in buffer j % 2, any rescale of O done (4 warps)
+    uint64_t* o_full = bars + 14;   // 2: PV_j committed (j % 2)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-    uint8_t* q_smem = stages + 2 * STAGE_BYTES;  // Q hi [HD/64 boxes of 128 rows x 128 B], then Q lo
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
     const int row0 = b * S;  // first row of this sequence in Q / K, first column in V^T
 
     if (warp == 0 && lane == 0) {
-        mbar_init(q_ready, 4);
         mbar_init(q_full, 1);
-        mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
-        for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
-        }
+        mbar_init(q_ready, 4);
         for (int i = 0; i < 2; i++) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], 4);
             mbar_init(&o_full[i], 1);
         }
@@ -182,6 +189,21 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
 
     if (warp == 0) {
         if (lane == 0 && nblk > 0) {
+            auto load_k = [&](int j) {
+                uint8_t* sb = kring + (j & 1) * KSTAGE;
+                mbar_arrive_expect_tx(&k_full[j & 1], KSTAGE);
+#pragma unroll
+                for (int i = 0; i < HD / 64; i++) {
+                    tma_load_2d(sb + i * BOX, &maps.kh, &k_full[j & 1], h * HD + 64 * i, row0 + j * KB);
+                    tma_load_2d(sb + KTILE + i * BOX, &maps.kl, &k_full[j & 1], h * HD + 64 * i, row0 + j * KB);
+                }
+            };
+            auto load_v = [&](int j) {
+                uint8_t* sb = vring + (j & 1) * VSTAGE;
+                mbar_arrive_expect_tx(&v_full[j & 1], VSTAGE);
+                tma_load_2d(sb, &maps.vh, &v_full[j & 1], row0 + j * KB, h * HD);
+                tma_load_2d(sb + VTILE, &maps.vl, &v_full[j & 1], row0 + j * KB, h * HD);
+            };
             // Q rows past S belong to the next sequence (or lie past the buffer: zeros);
             // their context is never stored
             mbar_arrive_expect_tx(q_full, 2 * QT * HD * 2);
@@ -190,39 +212,42 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
                 tma_load_2d(q_smem + i * QT * 128, &maps.qh, q_full, h * HD + 64 * i, row0 + q0);
                 tma_load_2d(q_smem + QT * HD * 2 + i * QT * 128, &maps.ql, q_full, h * HD + 64 * i, row0 + q0);
             }
-            int issued = 0;
-            for (int j = 0; j < nblk; j++) {
-                const int st = j % NSTAGE;
-                bool ok = true;
-                if (j >= NSTAGE)
-                    ok = mbar_wait(&kv_empty[st], ((j / NSTAGE) - 1) & 1, err, DEV_TIMEOUT_ATTN);
-                else if (st == 2)  // slot 2 held Q until the softmax warps copied it to TMEM
-                    ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
+            int k_issued = 0, v_issued = 0;
+            for (; k_issued < min(nblk, 2); k_issued++) load_k(k_issued);
+            // the V ring holds Q until the softmax warps have copied it to TMEM
+            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
+            for (; ok && v_issued < min(nblk, 2); v_issued++) load_v(v_issued);
+            for (int t = 0; ok && t + 2 < nblk; t++) {
+                // stage t % 2 frees when QK_t (K) / PV_t (V) completes: phase t / 2 of the
+                // stage's empty barrier; K_{t+2} / V_{t+2} are not issued before it, so the
+                // barrier cannot be a phase further on
+                ok = mbar_wait(&k_empty[t & 1], (t >> 1) & 1, err, DEV_TIMEOUT_ATTN);
                 if (!ok) break;
-                uint8_t* sb = stages + st * STAGE_BYTES;
-                mbar_arrive_expect_tx(&kv_full[st], STAGE_BYTES);
-#pragma unroll
-                for (int i = 0; i < HD / 64; i++) {
-                    tma_load_2d(sb + i * BOX, &maps.kh, &kv_full[st], h * HD + 64 * i, row0 + j * KB);
-                    tma_load_2d(sb + KTILE + i * BOX, &maps.kl, &kv_full[st], h * HD + 64 * i, row0 + j * KB);
-                }
-                tma_load_2d(sb + 2 * KTILE, &maps.vh, &kv_full[st], row0 + j * KB, h * HD);
-                tma_load_2d(sb + 2 * KTILE + VTILE, &maps.vl, &kv_full[st], row0 + j * KB, h * HD);
-                issued = j + 1;
+                load_k(t + 2);
+                k_issued = t + 3;
+                ok = mbar_wait(&v_empty[t & 1], (t >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                if (!ok) break;
+                load_v(t + 2);
+                v_issued = t + 3;
             }
-            mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);  // landed before the CTA may exit
-            // the last loads of each stage have landed before the CTA may exit
-            // (already true unless a wait above or in the MMA warp expired)
-            for (int j = max(0, issued - NSTAGE); j < issued; j++)
-                mbar_wait(&kv_full[j % NSTAGE], (j / NSTAGE) & 1, err, DEV_TIMEOUT_ATTN);
+            // every load has landed before the CTA may exit (already true unless a wait
+            // here or in the MMA warp expired)
+            mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);
+            for (int j = max(0, k_issued - 2); j < k_issued; j++)
+                mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+            for (int j = max(0, v_issued - 2); j < v_issued; j++)
+                mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
         }
     } else if (warp == 1) {
         if (lane == 0 && nblk > 0) {
             constexpr uint32_t idesc_qk = idesc_f16(KB), idesc_pv = idesc_f16(HD);
-            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
-            auto issue_qk = [&](int j) {
-                const uint32_t kb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES);
-                const uint32_t d = tmem + COL_S;
+            // S_j = Q K_j^T into buffer j % 2, once K_j has landed (k_full phase j / 2:
+            // K_{j+2} waits for this QK, so the barrier cannot be further on)
+            auto issue_qk = [&](int j) -> bool {
+                if (!mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN)) return false;
+                tc_fence_after();
+                const uint32_t kb = smem_u32(kring + (j & 1) * KSTAGE);
+                const uint32_t d = tmem + COL_SP + 64 * (j & 1);
 #pragma unroll
                 for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at HD/2 + 8k
                     // 16 fp16 = 32 bytes along the swizzled K rows, in box k / 4
@@ -232,29 +257,24 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
                     umma_f16_ts(d, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
                     umma_f16_ts(d, qh, desc_k_sw128(kb + off), idesc_qk, 1);
                 }
-                umma_commit(s_full);
+                umma_commit(&s_full[j & 1]);
+                umma_commit(&k_empty[j & 1]);
+                return true;
             };
+            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
             if (ok) {
                 tc_fence_after();
-                ok = mbar_wait(&kv_full[0], 0, err, DEV_TIMEOUT_ATTN);
+                ok = issue_qk(0);
             }
-            if (ok) {
-                tc_fence_after();
-                issue_qk(0);
-            }
+            if (ok && nblk > 1) ok = issue_qk(1);
             for (int j = 0; ok && j < nblk; j++) {
-                if (j + 1 < nblk) {
-                    // the S buffer is free once the softmax has loaded S_j from it
-                    ok = mbar_wait(&kv_full[(j + 1) % NSTAGE], ((j + 1) / NSTAGE) & 1, err, DEV_TIMEOUT_ATTN);
-                    if (ok) ok = mbar_wait(s_free, j & 1, err, DEV_TIMEOUT_ATTN);
-                    if (!ok) break;
-                    tc_fence_after();
-                    issue_qk(j + 1);
-                }
-                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN)) break;
+                // P_j (p_full phase j / 2: P_{j+2} needs S_{j+2}, issued only below) and V_j
+                ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN) &&
+                     mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                if (!ok) break;
                 tc_fence_after();
-                const uint32_t vb = smem_u32(stages + (j % NSTAGE) * STAGE_BYTES + 2 * KTILE);
-                const uint32_t pb = tmem + COL_P;
+                const uint32_t vb = smem_u32(vring + (j & 1) * VSTAGE);
+                const uint32_t pb = tmem + COL_SP + 64 * (j & 1);
 #pragma unroll
                 for (int k = 0; k < KB / 16; k++) {  // keys 16k..16k+15: P_hi at column 8k, P_lo at 32 + 8k
                     const uint32_t off = k * 32;
@@ -263,7 +283,17 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
                     umma_f16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc_pv, 1);
                 }
                 umma_commit(&o_full[j & 1]);
-                umma_commit(&kv_empty[j % NSTAGE]);
+                umma_commit(&v_empty[j & 1]);
+                if (j + 2 < nblk) {
+                    // buffer j % 2 is free once PV_j has read P_j (o_full phase j / 2; this
+                    // thread waited for phase j / 2 - 1 two blocks ago, and PV_{j+2} is not
+                    // issued yet)
+                    ok = mbar_wait(&o_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                    if (ok) {
+                        tc_fence_after();
+                        ok = issue_qk(j + 2);
+                    }
+                }
             }
         }
     } else {
@@ -275,7 +305,7 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
         if (nblk > 0) {
-            // this row's Q split (HD fp16 each, RoPE applied) from ring slot 2 (boxes of
+            // this row's Q split (HD fp16 each, RoPE applied) from the V ring (boxes of
             // 128-byte rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
             ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN));
 #pragma unroll
@@ -299,15 +329,13 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         }
         for (int j = 0; j < nblk; j++) {
             const int bf = j & 1;
-            const uint32_t sp = lb + COL_S;  // this row's S_j columns
-            // after an expired wait the loop keeps running (work skipped, results unused)
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full, j & 1, err, DEV_TIMEOUT_ATTN));
+            const uint32_t sp = lb + COL_SP + 64 * bf;  // this row's S_j, then P_j, columns
+            // s_full phase j / 2: QK_{j+2} waits for PV_j, which waits for this P_j.
+            // After an expired wait the loop keeps running (work skipped, results unused).
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[bf], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN));
             tc_fence_after();
             float s[64];
             tmem_ld64(sp, s);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free);  // QK_{j+1} may now overwrite S_j
             if (j * KB + KB > valid) {  // the block holding the last valid key
 #pragma unroll
                 for (int c = 0; c < 64; c++)
@@ -342,35 +370,37 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             uint32_t hi[32], lo[32];
 #pragma unroll
             for (int i = 0; i < 32; i++) split_p2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
-            if (j > 0) {
-                // PV_{j-1} has read the P buffer and finished O up to block j-1
+            if (j > 0 && __any_sync(0xffffffffu, raise)) {
+                // bring O to the new reference max once PV_{j-1} has completed: o_full
+                // phase (j-1) / 2 of buffer (j-1) % 2; its previous phase (PV_{j-3})
+                // completed before QK_j was issued, and PV_{j+1} needs P_{j+1}
                 ok = __all_sync(0xffffffffu,
                                 ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
                 tc_fence_after();
-                if (__any_sync(0xffffffffu, raise)) {  // bring O to the new reference max
-                    const uint64_t c2 = pack2(corr, corr);
+                const uint64_t c2 = pack2(corr, corr);
 #pragma unroll
-                    for (int cb = 0; cb < HD; cb += 64) {
-                        float o[64];
-                        tmem_ld64(lb + COL_O + cb, o);
+                for (int cb = 0; cb < HD; cb += 64) {
+                    float o[64];
+                    tmem_ld64(lb + COL_O + cb, o);
 #pragma unroll
-                        for (int d = 0; d < 64; d += 2) {
-                            uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
-                            unpack2(t, o[d], o[d + 1]);
-                        }
-                        tmem_st32(lb + COL_O + cb, o);
-                        tmem_st32(lb + COL_O + cb + 32, o + 32);
+                    for (int d = 0; d < 64; d += 2) {
+                        uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
+                        unpack2(t, o[d], o[d + 1]);
                     }
+                    tmem_st32(lb + COL_O + cb, o);
+                    tmem_st32(lb + COL_O + cb + 32, o + 32);
                 }
             }
-            tmem_st32u(lb + COL_P, hi);
-            tmem_st32u(lb + COL_P + 32, lo);
+            tmem_st32u(sp, hi);
+            tmem_st32u(sp + 32, lo);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[bf]);
         }
         if (nblk > 0) {
+            // PV_{nblk-1}: its barrier's previous phase (PV_{nblk-3}) completed before
+            // QK_{nblk-1} was issued; its commit covers every earlier MMA
             ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err,
                                                          DEV_TIMEOUT_ATTN));
             tc_fence_after();
@@ -382,9 +412,9 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
         // 1 / l, and O's scales undone (a power of two: exact)
         const float inv = (nblk > 0 && l > 0.0f) ? (1.0f / l) * out_unscale : 0.0f;
         const bool via_tma = ctx_tma && wrow0 + 32 <= S;
-        // staging in ring slot 0 (every load has been consumed by the last PV): per warp
-        // HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
-        uint8_t* stg = stages + (warp - 2) * (HD * 128);
+        // staging in the K ring (every K load has been consumed by a completed QK): per
+        // warp HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
+        uint8_t* stg = kring + (warp - 2) * (HD * 128);
 #pragma unroll
         for (int cb = 0; cb < HD; cb += 64) {
             float o[64];

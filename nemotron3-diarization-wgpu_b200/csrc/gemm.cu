@@ -931,11 +931,24 @@ CUtensorMap make_f16_map(const void* p, long long rows, long long cols, long lon
     return cached_map(p, MAP_F16, rows, cols, ld, box_cols, box_rows, swizzle);
 }
 
+// A plain fp32 output (EPI_STORE without a reduce) whose rows start on 16-byte
+// boundaries leaves through the TMA epilogue: 32 x 32 boxes staged in shared memory,
+// instead of each thread writing its own row.  The values are the same either way.
+void store_via_tma(Epi& epi, int M, int N, bool cache) {
+    if (epi.mode != EPI_STORE || epi.tma || epi.reduce || !epi.out || epi.ldo < N || epi.ldo % 4 ||
+        (reinterpret_cast<uintptr_t>(epi.out) & 15))
+        return;
+    epi.map_out = cache ? make_store_map(epi.out, M, N, epi.ldo)
+                        : encode_map(epi.out, MAP_F32, M, N, epi.ldo, 32, 32, true);
+    epi.tma = 1;
+}
+
 void gemm_split(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
                 const Epi& epi_in, int* err) {
     if (M <= 0 || N <= 0) return;
     Epi epi = epi_in;
     epi.acc_scale = (float)(1.0 / ((double)A.scale * (double)B.scale));
+    store_via_tma(epi, M, N, true);
     int bn;
     if (epi.mode == EPI_DENSE_OUT || N == 192) {
         bn = 192;
@@ -991,6 +1004,7 @@ void gemm_split_stack_maps(cudaStream_t s, const SplitOperand& A, const SplitOpe
     if (M <= 0 || N <= 0) return;
     Epi epi = epi_in;
     epi.acc_scale = (float)(1.0 / ((double)A.scale * (double)B.scale));
+    store_via_tma(epi, M, N, false);
     check_shape(A, B, K, 0, epi, 128);
     launch_one<128>(s, operand_maps(A, B, BM, 128, false), M, N, K, 0, epi, err);
 }
