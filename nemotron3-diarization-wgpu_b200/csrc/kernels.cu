@@ -114,10 +114,16 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long rows, c
 //             half 1, 2, 4, 8 in registers; half 16 pairs lanes L and L ^ 1 (shuffles)
 //   layout B: lane L holds positions L + 32t (t = 0..15), reached through shared
 //             memory (padded: no bank conflicts either way): halves 32..256 in registers
+// Shared-memory reads are conflict-free: the stages of layout A read one twiddle for
+// the whole warp; those of layout B read per-stage copies of their twiddles, indexed
+// by lane (stage h: twiddle (lane + 32u) * 256 / h at position lane + 32u); the
+// filterbank reads its weights transposed (lane m reads word i * 128 + m).
 constexpr int NFFT = 512;
 constexpr int NBINS = NFFT / 2 + 1;
 constexpr int MEL_WARPS = 8;
 constexpr int MEL_PAD = NFFT + NFFT / 32;  // padded index p + p / 32
+constexpr int TWB = 32 + 64 + 128 + 256;   // layout B's per-stage twiddle copies
+__host__ __device__ constexpr int twb_offset(int h) { return h - 32; }  // 32 -> 0, 64 -> 32, 128 -> 96, 256 -> 224
 
 // One radix-2 butterfly with twiddle (wr, wi): (u, x) -> (u + x w, u - x w).
 __device__ __forceinline__ void butterfly(float& ur, float& ui, float& xr, float& xi, float wr, float wi) {
@@ -131,16 +137,23 @@ __device__ __forceinline__ void butterfly(float& ur, float& ui, float& xr, float
 
 __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
     const float* __restrict__ audio, const MelSegDev* __restrict__ segs, int nsegs, long long f_first,
-    long long n_frames, int hop, const float* __restrict__ window, const float* __restrict__ twiddle,
-    const float* __restrict__ filters, const int* __restrict__ filt_lo, const int* __restrict__ filt_hi, float preemph,
-    SplitOut mel, float* __restrict__ mel_plain) {
+    long long n_frames, int hop, const MelTables tab, float preemph, SplitOut mel, float* __restrict__ mel_plain) {
     __shared__ float tw_s[NFFT];  // (cos, sin) pairs of the 256 twiddles
     __shared__ float win_s[NFFT];
+    __shared__ float twb_re[TWB], twb_im[TWB];
     __shared__ float xs[MEL_WARPS][2][MEL_PAD];
+    extern __shared__ float fb_s[];  // [fb_w][128]
     for (int i = threadIdx.x; i < NFFT; i += blockDim.x) {
-        tw_s[i] = twiddle[i];
-        win_s[i] = window[i];
+        tw_s[i] = tab.twiddle[i];
+        win_s[i] = tab.window[i];
     }
+    for (int i = threadIdx.x; i < TWB; i += blockDim.x) {
+        const int h = i < 32 ? 32 : i < 96 ? 64 : i < 224 ? 128 : 256;
+        const int t = (i - twb_offset(h)) * (NFFT / 2 / h);
+        twb_re[i] = tab.twiddle[2 * t];
+        twb_im[i] = tab.twiddle[2 * t + 1];
+    }
+    for (int i = threadIdx.x; i < tab.fb_w * 128; i += blockDim.x) fb_s[i] = tab.fbank_t[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long f = f_first + (long long)blockIdx.x * MEL_WARPS + warp;
@@ -219,8 +232,8 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
 #pragma unroll
         for (int t = 0; t < 16; t++) {
             if (t & hs) continue;
-            const int tix = (lane + 32 * (t & (hs - 1))) * (NFFT / 2 / h);
-            butterfly(re[t], im[t], re[t + hs], im[t + hs], tw_s[2 * tix], tw_s[2 * tix + 1]);
+            const int ix = twb_offset(h) + lane + 32 * (t & (hs - 1));  // twiddle (lane + 32u) * 256 / h
+            butterfly(re[t], im[t], re[t + hs], im[t + hs], twb_re[ix], twb_im[ix]);
         }
     }
     // ---- power of bins 0..256 into shared memory (bin lane + 32t)
@@ -229,14 +242,17 @@ __global__ void __launch_bounds__(MEL_WARPS * 32) mel_kernel(
     for (int t = 0; t < 8; t++) pw[lane + 32 * t] = __fadd_rn(__fmul_rn(re[t], re[t]), __fmul_rn(im[t], im[t]));
     if (lane == 0) pw[256] = __fadd_rn(__fmul_rn(re[8], re[8]), __fmul_rn(im[8], im[8]));
     __syncwarp();
-    // ---- filterbank (sequential over each filter's support) and log
+    // ---- filterbank (sequential over each filter's support, bins ascending) and log
     const long long orow = (sg.out_row0 + (f - sg.f_begin)) * 128;
 #pragma unroll
     for (int q = 0; q < 4; q++) {
         const int m = lane + 32 * q;
+        const int lo = __ldg(tab.filt_lo + m), w = __ldg(tab.filt_w + m);
         float acc = 0.0f;
-        const float* fw = filters + m * NBINS;
-        for (int k = filt_lo[m]; k <= filt_hi[m]; k++) acc = __fadd_rn(acc, __fmul_rn(fw[k], pw[k]));
+        for (int i = 0; i < tab.group_w[q]; i++) {  // the group's widest filter; lanes past their own skip
+            const float prod = __fmul_rn(fb_s[i * 128 + m], pw[min(lo + i, NBINS - 1)]);
+            if (i < w) acc = __fadd_rn(acc, prod);
+        }
         const float v = (float)log((double)__fadd_rn(acc, 5.9604645e-8f));
         const long long o = orow + m;
         if (mel.h) {
@@ -409,12 +425,17 @@ void launch_layer_norm(cudaStream_t s, const float* x, long long rows, int cols,
 }
 
 void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
-                long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
-                const int* filt_lo, const int* filt_hi, float preemph, SplitOut mel, float* mel_plain) {
+                long long n_frames, int hop, const MelTables& tab, float preemph, SplitOut mel, float* mel_plain) {
     if (n_frames <= 0 || nsegs <= 0) return;
+    if (tab.fb_w < 0 || tab.fb_w > MEL_FB_MAX_W) throw Error(13, "log-mel: a filter wider than the kernel's table");
+    static std::atomic<unsigned long long> attr{0};
+    once_per_device(attr, [] {
+        N3D_CUDA(cudaFuncSetAttribute(mel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      MEL_FB_MAX_W * 128 * (int)sizeof(float)));
+    });
     const long long blocks = (n_frames + MEL_WARPS - 1) / MEL_WARPS;
-    mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, 0, s>>>(audio, segs, nsegs, f_first, n_frames, hop, window, twiddle,
-                                                            filters, filt_lo, filt_hi, preemph, mel, mel_plain);
+    mel_kernel<<<(unsigned)blocks, MEL_WARPS * 32, tab.fb_w * 128 * sizeof(float), s>>>(
+        audio, segs, nsegs, f_first, n_frames, hop, tab, preemph, mel, mel_plain);
     N3D_CUDA(cudaGetLastError());
 }
 

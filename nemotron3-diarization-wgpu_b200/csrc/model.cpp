@@ -522,7 +522,11 @@ void Model::upload_weights(const std::string& dir) {
     // front-end constants
     const int nf = c.n_fft / 2 + 1;
     std::vector<float> filt = slaney(c.n_mels, c.n_fft, c.sr, 0.0, (double)c.sr / 2.0);
-    std::vector<int> flo(c.n_mels), fhi(c.n_mels);
+    // each filter's support [lo, lo + w) (w = 0: an empty filter), and the weights
+    // transposed: row i holds every filter's weight for its bin lo + i
+    if (c.n_mels != 128 || c.n_fft != 512) throw Error(13, "the log-mel kernel is built for 128 mels of a 512 FFT");
+    std::vector<int> flo(c.n_mels), fw(c.n_mels);
+    int fb_w = 0;
     for (int m = 0; m < c.n_mels; m++) {
         int lo = nf, hi = -1;
         for (int k = 0; k < nf; k++)
@@ -531,9 +535,14 @@ void Model::upload_weights(const std::string& dir) {
                 hi = std::max(hi, k);
             }
         flo[m] = lo;
-        fhi[m] = hi;
+        fw[m] = hi >= lo ? hi - lo + 1 : 0;
+        fb_w = std::max(fb_w, fw[m]);
+        mel_tab_.group_w[m / 32] = std::max(mel_tab_.group_w[m / 32], fw[m]);
     }
-    mel_filters_ = dev(filt);
+    if (fb_w > MEL_FB_MAX_W) throw Error(13, "slaney filterbank: a filter wider than the log-mel kernel's table");
+    std::vector<float> fbt((size_t)std::max(fb_w, 1) * c.n_mels, 0.0f);
+    for (int m = 0; m < c.n_mels; m++)
+        for (int i = 0; i < fw[m]; i++) fbt[(size_t)i * c.n_mels + m] = filt[(size_t)m * nf + flo[m] + i];
     auto devi = [&](const std::vector<int>& v) {
         int* p = nullptr;
         N3D_CUDA(cudaMalloc(&p, v.size() * 4));
@@ -541,22 +550,24 @@ void Model::upload_weights(const std::string& dir) {
         owned_.push_back(p);
         return p;
     };
-    filt_lo_ = devi(flo);
-    filt_hi_ = devi(fhi);
+    mel_tab_.fbank_t = dev(fbt);
+    mel_tab_.filt_lo = devi(flo);
+    mel_tab_.filt_w = devi(fw);
+    mel_tab_.fb_w = fb_w;
     // torch.hann_window(win, periodic=False) centred in the n_fft frame (src/mel.rs:43-48, 197-200)
     std::vector<float> window(c.n_fft, 0.0f);
     const int left = (c.n_fft - c.win) / 2;
     const float denom = (float)(c.win - 1);
     for (int i = 0; i < c.win; i++)
         window[left + i] = 0.5f * (1.0f - std::cos(2.0f * 3.14159265358979323846f * (float)i / denom));
-    window_ = dev(window);
+    mel_tab_.window = dev(window);
     std::vector<float> tw(c.n_fft);
     for (int k = 0; k < c.n_fft / 2; k++) {
         const double ang = -2.0 * 3.14159265358979323846 * (double)k / (double)c.n_fft;
         tw[2 * k] = (float)std::cos(ang);
         tw[2 * k + 1] = (float)std::sin(ang);
     }
-    twiddle_ = dev(tw);
+    mel_tab_.twiddle = dev(tw);
     // RoPE tables for positions 0..s_cap-1 (src/encoder.rs:163-185)
     const int hd = c.hidden / c.heads, half = hd / 2;
     std::vector<float> inv(half), cs((size_t)s_cap_ * hd), sn((size_t)s_cap_ * hd);
@@ -1149,13 +1160,13 @@ const float* Model::mel_launch(const float* d_audio, const MelJob& job,
             long long f0 = 0;
             for (const auto& pt : *parts) {
                 N3D_CUDA(cudaStreamWaitEvent(stream_, pt.second, 0));
-                launch_mel(stream_, d_audio, job.segs, job.nsegs, f0, pt.first - f0, c.hop, window_, twiddle_,
-                           mel_filters_, filt_lo_, filt_hi_, c.preemph, mel.out(s_mel_), nullptr);
+                launch_mel(stream_, d_audio, job.segs, job.nsegs, f0, pt.first - f0, c.hop, mel_tab_, c.preemph,
+                           mel.out(s_mel_), nullptr);
                 f0 = pt.first;
             }
         } else {
-            launch_mel(stream_, d_audio, job.segs, job.nsegs, 0, job.frames, c.hop, window_, twiddle_, mel_filters_,
-                       filt_lo_, filt_hi_, c.preemph, mel.out(s_mel_), nullptr);
+            launch_mel(stream_, d_audio, job.segs, job.nsegs, 0, job.frames, c.hop, mel_tab_, c.preemph, mel.out(s_mel_),
+                       nullptr);
         }
         prof_end(K_MEL, 0, (double)job.frames * (c.hop * 4 + c.n_mels * 4));
     }
@@ -1501,7 +1512,7 @@ int Model::log_mel(const float* samples, long long n, bool centered, std::vector
     MelSegDev* d_seg = (MelSegDev*)ws("melseg", sizeof(MelSegDev));
     float* pl = (float*)ws("mel_plain", frames * c.n_mels * 4);
     N3D_CUDA(cudaMemcpyAsync(d_seg, &seg, sizeof(MelSegDev), cudaMemcpyHostToDevice, stream_));
-    launch_mel(stream_, a, d_seg, 1, 0, frames, c.hop, window_, twiddle_, mel_filters_, filt_lo_, filt_hi_, c.preemph,
+    launch_mel(stream_, a, d_seg, 1, 0, frames, c.hop, mel_tab_, c.preemph,
                SplitOut{}, pl);
     N3D_CUDA(cudaMemcpyAsync(out.data(), pl, frames * c.n_mels * 4, cudaMemcpyDeviceToHost, stream_));
     N3D_CUDA(cudaStreamSynchronize(stream_));

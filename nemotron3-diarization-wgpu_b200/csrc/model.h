@@ -288,8 +288,7 @@ class Model {
     std::vector<DevLayer> layers_;
     float *in_ln_w_, *in_ln_b_, *fin_ln_w_, *fin_ln_b_;
     float *out_w_, *out_b_, *silence_;
-    float *mel_filters_, *window_, *twiddle_;
-    int *filt_lo_, *filt_hi_;
+    MelTables mel_tab_;  // log-mel window, twiddles and transposed filterbank
     float *rope_cos_, *rope_sin_;
     int s_cap_ = 1024;  // MAX_SEQ, src/gpu_engine.rs:12
     std::vector<void*> owned_;

@@ -190,11 +190,25 @@ struct MelSegDev {
     long long base, out_row0, f_begin;
     int len, frame_lo, centered, pad;
 };
+// The log-mel's constant tables (device pointers): the centred Hann window [512], the
+// 256 twiddles as (cos, sin) pairs, and the slaney filterbank in its sparse, transposed
+// form: filter m's weights for bins filt_lo[m] + i at fbank_t[i * 128 + m] for
+// i < filt_w[m] (zeros up to fb_w rows), group_w[q] = the widest filter of mels
+// 32q..32q+31.
+struct MelTables {
+    const float* window = nullptr;
+    const float* twiddle = nullptr;
+    const float* fbank_t = nullptr;
+    const int* filt_lo = nullptr;
+    const int* filt_w = nullptr;
+    int fb_w = 0;
+    int group_w[4] = {0, 0, 0, 0};
+};
+constexpr int MEL_FB_MAX_W = 64;  // widest filter the kernel's shared table holds
 // Log-mel of global frames [f_first, f_first + n_frames) of the segment table into
 // [rows, 128] outputs (fp16 split, plain optional).
 void launch_mel(cudaStream_t s, const float* audio, const MelSegDev* segs, int nsegs, long long f_first,
-                long long n_frames, int hop, const float* window, const float* twiddle, const float* filters,
-                const int* filt_lo, const int* filt_hi, float preemph, SplitOut mel, float* mel_plain);
+                long long n_frames, int hop, const MelTables& tab, float preemph, SplitOut mel, float* mel_plain);
 // x -> the fp16 split of x * out.scale, elementwise (n % 4 == 0).
 void launch_split(cudaStream_t s, const float* x, long long n, SplitOut out);
 // max |x| over n floats (n % 4 == 0) into *d_max (a float the caller zeroes first).
