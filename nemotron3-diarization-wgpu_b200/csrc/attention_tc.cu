@@ -15,39 +15,42 @@
 // scale 1/sqrt(hd) log2 e is divided by s_Q s_K, and the context by s_V (the row sum l
 // carries P's 2^7), exactly (powers of two).
 //
-// CTA = 128 queries of one (sequence, head); 6 warps, two CTAs per SM at head_dim
-// 64, one at 128 (its rings and TMEM are twice as large):
-//   warp 0      TMA: the CTA's Q pair (into the V ring, until the softmax warps have
-//               copied it to TMEM), then per block of 64 keys the K pair into a
-//               2-stage K ring and the V^T pair into a 2-stage V ring.  K_{j+2} loads
-//               once QK_j has completed, V_{j+2} once PV_j has, so the K loads run a
-//               block ahead of the V loads
-//   warp 1      TMEM owner; one thread issues S_j = Q K_j^T and O += P_j V_j.  Both
-//               MMAs take their A operand (Q, P) from TMEM, so only K / V^T are read
-//               from shared memory
-//   warps 2..5  softmax, one thread per query row (TMEM lane): first the row's Q
-//               pair from shared memory into TMEM; per block the row's 64 scores, exp
-//               as 2^x on the special-function unit after one FMA folds the
-//               1/sqrt(hd) scale, log2 e and the reference max together; then P_j as
-//               fp16 splits, written over S_j.
-// S / P double buffer: block j uses TMEM buffer j % 2; the softmax writes P_j over the
-// S_j it has read, PV_j reads it, and QK_{j+2} is issued into it once PV_j has
-// completed.  QK_{j+1} therefore computes while the softmax works on S_j, and the
-// softmax never waits for a PV except to rescale O.
+// Persistent CTAs: each resident CTA (two per SM at head_dim 64, one at 128) takes
+// items blockIdx.x, + gridDim.x, ...; an item is 128 queries of one (sequence, head).
+// Key blocks of 64 are numbered g across the CTA's items, and the rings and the S, P
+// and O columns run on g.  6 warps; two threads issue the tensor-core work, so that
+// neither waits for the other's MMAs:
+//   warp 0      the next item's Q pair (TMA into the Q buffer) and the K pairs into a
+//               2-stage K ring; issues S_g = Q K_g^T once the softmax has read S_{g-1}
+//   warp 1      TMEM owner; the V^T pairs into a 2-stage V ring; issues O += P_g V_g
+//               once the softmax has written P_g
+//   warps 2..5  softmax, one thread per query row (TMEM lane): per block the row's 64
+//               scores, exp as 2^x on the special-function unit after one FMA folds the
+//               1/sqrt(hd) scale, log2 e and the reference max together; then, once
+//               PV_{g-1} has read the P buffer, P_g as fp16 splits; after an item's last
+//               block the next item's Q pair from the Q buffer into TMEM, then the
+//               item's context.
+// Both MMAs take their A operand (Q, P) from TMEM, so only K / V^T are read from
+// shared memory.  QK_{g+1} computes while the softmax works on S_g and PV_{g-1}
+// alongside it; the next item's first QK computes during the epilogue.  K_{g+2} loads
+// once QK_g has completed, V_{g+2} once PV_g has.  (Writing P over S in two alternating
+// buffers, so that the softmax need not wait for PV_{g-1}, measured slower: the QK
+// issue then waits for PV completion instead.)
 // Lazy rescaling: exponents use a per-row reference max m that is raised only when
 // a block's max exceeds it by more than 2^8 in the exponent; only then is O
-// (in TMEM) multiplied by the correction, after PV_{j-1} has completed and before
-// P_j is released.  P values stay below 2^8; O / l is unchanged mathematically.
-// Context rows leave through shared memory (the K ring, free once the last QK is
-// done) and TMA stores, a warp's 32 rows at a time.
-// TMEM: S/P buffers 0..63 and 64..127 (P hi at +0, lo at +32), O 128..128+HD-1, Q
-// 128+HD..128+2HD-1 (h first, then l); 16-bit operands two per 32-bit column.  256
-// columns at head_dim 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of
-// 64 columns (the 128-byte swizzle's limit), as is the Q tile.
-// Every barrier is double-buffered by block parity and every waiter is at most one
-// phase behind (argued at each wait).  Every wait is bounded; an expired wait records
-// its site in *err.
+// (in TMEM) multiplied by the correction, after PV_{g-1} has completed and before
+// P_g is released.  P values stay below 2^8; O / l is unchanged mathematically.
+// Context rows leave through shared memory (the Q buffer, once the next Q has moved
+// to TMEM) and TMA stores, a warp's 32 rows at a time.
+// TMEM: S 0..63, P 64..127 (hi 64.., lo 96..), O 128..128+HD-1, Q 128+HD..128+2HD-1
+// (h first, then l); 16-bit operands two per 32-bit column.  256 columns at head_dim
+// 64, 512 at 128.  A K block [64 keys, HD] is HD/64 TMA boxes of 64 columns (the
+// 128-byte swizzle's limit), as is the Q tile.
+// Every waiter is at most one phase behind its barrier (argued at each wait).  Every
+// wait is bounded; an expired wait records its site in *err.
 
+#include <algorithm>
+#include <climits>
 #include <cmath>
 
 #include "n3d_device.cuh"
@@ -61,7 +64,7 @@ constexpr int QT = 128;                   // queries per CTA
 constexpr int KB = 64;                    // keys per block
 constexpr int BOX = KB * 128;             // one 64-column TMA box of 64 rows: 8 KB
 constexpr int THREADS = 192;
-constexpr uint32_t COL_SP = 0, COL_O = 128;  // S/P buffer b at COL_SP + 64 b
+constexpr uint32_t COL_S = 0, COL_P = 64, COL_O = 128;
 constexpr int DEV_TIMEOUT_ATTN = 5;
 
 template <int HD>
@@ -70,26 +73,28 @@ struct AttnCfg {
     static constexpr int KTILE = KB * HD * 2;                  // K block [64 keys x HD] fp16
     static constexpr int VTILE = HD * KB * 2;                  // V^T block [HD x 64 keys] fp16
     static constexpr int KSTAGE = 2 * KTILE, VSTAGE = 2 * VTILE;  // hi + lo
-    static constexpr int RING_BYTES = 2 * KSTAGE + 2 * VSTAGE;    // 2-stage K ring, then 2-stage V ring
+    static constexpr int QBUF = 2 * QT * HD * 2;                  // the next item's Q pair, or the context staging
+    static constexpr int RING_BYTES = 2 * KSTAGE + 2 * VSTAGE + QBUF;
     static constexpr int SMEM_BYTES = RING_BYTES + 1024 + 256;
     static constexpr uint32_t COL_Q = COL_O + HD, TMEM_COLS = HD == 64 ? 256 : 512;
     static constexpr int CTAS_PER_SM = HD == 64 ? 2 : 1;
-    static_assert(2 * QT * HD * 2 == 2 * VSTAGE, "the Q pair fills the V ring");
-    static_assert(4 * 32 * HD * 4 == 2 * KSTAGE, "the context staging of the 4 softmax warps fills the K ring");
+    static_assert(4 * 32 * HD * 4 == QBUF, "the context staging of the 4 softmax warps fills the Q buffer");
 };
 constexpr float RESCALE_LOG2 = 8.0f;      // raise the reference max when exponents would exceed 2^8
 constexpr float P_LOG2_SCALE = 7.0f;      // P <= 2^8 is kept as P * 2^7 <= 2^15, inside fp16's range
 
 // Two scaled probabilities x = P * 2^7 in [0, 2^15] -> their fp16 split words (a in the
-// low half).  h = x rounded to 11 significant bits, its fp16 bits formed with integer
-// operations ((bits(x) + 2^12 - (112 << 23)) >> 13: rebias the exponent, drop 13
-// mantissa bits); x below fp16's normal range takes h = 2^-14 and a negative l.  Only
-// l goes through the conversion pipe.
+// low half).  h = x rounded to 11 significant bits; its fp16 bits are
+// (bits(x) + 2^12 - (112 << 23)) >> 13 (rebias the exponent, drop 13 mantissa bits),
+// formed as the high half of bits(x) * 8 + 0x40008000 (the same sum shifted left by 3,
+// modulo 2^32; it stays below 2^29 before the shift for x in [2^-14, 2^15]), and one
+// byte permute packs the two high halves.  x below fp16's normal range takes
+// h = 2^-14 and a negative l.  Only l goes through the conversion pipe.
 __device__ __forceinline__ void split_p2(float a, float b, uint32_t& h, uint32_t& l) {
-    const uint32_t ua = __float_as_uint(fmaxf(a, 6.103515625e-05f)) + 0x1000u;
-    const uint32_t ub = __float_as_uint(fmaxf(b, 6.103515625e-05f)) + 0x1000u;
-    h = __byte_perm((ua - 0x38000000u) >> 13, (ub - 0x38000000u) >> 13, 0x5410);
-    l = f16x2_rn(__fsub_rn(a, __uint_as_float(ua & 0xffffe000u)), __fsub_rn(b, __uint_as_float(ub & 0xffffe000u)));
+    const uint32_t ba = __float_as_uint(fmaxf(a, 6.103515625e-05f)), bb = __float_as_uint(fmaxf(b, 6.103515625e-05f));
+    h = __byte_perm(ba * 8u + 0x40008000u, bb * 8u + 0x40008000u, 0x7632);
+    const uint32_t ua = (ba + 0x1000u) & 0xffffe000u, ub = (bb + 0x1000u) & 0xffffe000u;
+    l = f16x2_rn(__fsub_rn(a, __uint_as_float(ua)), __fsub_rn(b, __uint_as_float(ub)));
 }
 
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
@@ -139,31 +144,30 @@ struct AttnMaps {
 template <int HD>
 __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
     attention_tc_kernel(const __grid_constant__ AttnMaps maps, int S, const int* __restrict__ valid_arr, int heads,
-                        SplitOut ctx, int ctx_tma, float k2, float out_unscale, int* err) {
+                        int qblocks, int items, SplitOut ctx, int ctx_tma, float k2, float out_unscale, int* err) {
     using Cfg = AttnCfg<HD>;
     constexpr int KTILE = Cfg::KTILE, VTILE = Cfg::VTILE, KSTAGE = Cfg::KSTAGE, VSTAGE = Cfg::VSTAGE;
     constexpr uint32_t COL_Q = Cfg::COL_Q, TMEM_COLS = Cfg::TMEM_COLS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* kring = smem;                  // K pair of block j in stage j % 2
-    uint8_t* vring = smem + 2 * KSTAGE;     // V^T pair of block j in stage j % 2
-    uint8_t* q_smem = vring;                // Q hi [HD/64 boxes of 128 rows x 128 B], then Q lo
+    uint8_t* kring = smem;                             // K pair of block g in stage g % 2
+    uint8_t* vring = smem + 2 * KSTAGE;                // V^T pair of block g in stage g % 2
+    uint8_t* qbuf = smem + 2 * KSTAGE + 2 * VSTAGE;    // Q hi [HD/64 boxes of 128 rows x 128 B], then Q lo
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::RING_BYTES);
-    uint64_t* q_full = bars;        // 1: the Q pair has landed in the V ring
-    uint64_t* q_ready = bars + 1;   // 1: Q pair in TMEM, V ring free (4 warps)
-    uint64_t* k_full = bars + 2;    // 2: K_j landed (stage j % 2)
-    uint64_t* k_empty = bars + 4;   // 2: QK_j completed
-    uint64_t* v_full = bars + 6;    // 2: V_j landed
-    uint64_t* v_empty = bars + 8;   // 2: PV_j completed
-    uint64_t* s_full = bars + 10;   // 2: QK_j committed into buffer j % 2
-    uint64_t* p_full = bars + 12;   // 2: P_j in buffer j % 2, any rescale of O done (4 warps)
-    uint64_t* o_full = bars + 14;   // 2: PV_j committed (j % 2)
+    uint64_t* q_full = bars;        // 1: phase k = item k's Q pair landed in the Q buffer
+    uint64_t* q_ready = bars + 1;   // 1: phase k = item k's Q pair in TMEM, Q buffer free (4 warps)
+    uint64_t* k_full = bars + 2;    // 2: K_g landed (stage g % 2)
+    uint64_t* k_empty = bars + 4;   // 2: QK_g completed
+    uint64_t* v_full = bars + 6;    // 2: V_g landed
+    uint64_t* v_empty = bars + 8;   // 2: PV_g completed
+    uint64_t* s_full = bars + 10;   // 1: phase g = QK_g completed
+    uint64_t* s_free = bars + 11;   // 1: phase g = S_g read by the softmax (4 warps)
+    uint64_t* p_full = bars + 12;   // 1: phase g = P_g in TMEM, any rescale of O done (4 warps)
+    uint64_t* o_full = bars + 13;   // 1: phase g = PV_g completed
+    uint64_t* ctx_done = bars + 14; // 1: phase k = item k's context has left the Q buffer (4 warps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
-    const int row0 = b * S;  // first row of this sequence in Q / K, first column in V^T
-
     if (warp == 0 && lane == 0) {
         mbar_init(q_full, 1);
         mbar_init(q_ready, 4);
@@ -172,142 +176,206 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
-            mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 4);
-            mbar_init(&o_full[i], 1);
         }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init(ctx_done, 4);
         mbar_fence_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    griddep_wait();  // Q / K / V^T written by the previous kernel
+    griddep_wait();  // Q / K / V^T and the key counts written by earlier kernels
     griddep_launch_dependents();
-    const int valid = min(valid_arr[b], S);
-    const int nblk = (valid + KB - 1) / KB;
+
+    // This CTA's items: blockIdx.x + k * gridDim.x, k = 0.. ; item = (b * heads + h) *
+    // qblocks + qb covers queries qb*128.. of head h of sequence b, and its key blocks
+    // are numbered g = 0, 1, ... across the CTA's items (the rings, S, P and O run on g)
+    const int n_items = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    struct Item {
+        int qb, h, b, valid, nblk;
+    };
+    auto item = [&](int k) {
+        const int it = (int)blockIdx.x + k * (int)gridDim.x, t = it / qblocks;
+        Item r;
+        r.qb = it - t * qblocks;
+        r.h = t % heads;
+        r.b = t / heads;
+        r.valid = min(valid_arr[r.b], S);
+        r.nblk = (r.valid + KB - 1) / KB;
+        return r;
+    };
+    // the next key block a ring loads: item ck, block cj of sequence cb, head ch (items
+    // without keys skipped; ck = n_items once every block is loaded)
+    auto settle = [&](int& ck, int& cj, int& cb, int& ch) {
+        for (; ck < n_items; ck++, cj = 0) {
+            const Item it = item(ck);
+            cb = it.b;
+            ch = it.h;
+            if (cj < it.nblk) break;
+        }
+    };
 
     if (warp == 0) {
-        if (lane == 0 && nblk > 0) {
-            auto load_k = [&](int j) {
-                uint8_t* sb = kring + (j & 1) * KSTAGE;
-                mbar_arrive_expect_tx(&k_full[j & 1], KSTAGE);
+        // ---- Q and K loads, S_g = Q K_g^T
+        if (lane == 0 && n_items > 0) {
+            auto load_q = [&](int k) {
+                const Item it = item(k);
+                // Q rows past S belong to the next sequence (or lie past the buffer:
+                // zeros); their context is never stored
+                mbar_arrive_expect_tx(q_full, Cfg::QBUF);
 #pragma unroll
                 for (int i = 0; i < HD / 64; i++) {
-                    tma_load_2d(sb + i * BOX, &maps.kh, &k_full[j & 1], h * HD + 64 * i, row0 + j * KB);
-                    tma_load_2d(sb + KTILE + i * BOX, &maps.kl, &k_full[j & 1], h * HD + 64 * i, row0 + j * KB);
+                    const int x = it.h * HD + 64 * i, y = it.b * S + it.qb * QT;
+                    tma_load_2d(qbuf + i * QT * 128, &maps.qh, q_full, x, y);
+                    tma_load_2d(qbuf + QT * HD * 2 + i * QT * 128, &maps.ql, q_full, x, y);
                 }
             };
-            auto load_v = [&](int j) {
-                uint8_t* sb = vring + (j & 1) * VSTAGE;
-                mbar_arrive_expect_tx(&v_full[j & 1], VSTAGE);
-                tma_load_2d(sb, &maps.vh, &v_full[j & 1], row0 + j * KB, h * HD);
-                tma_load_2d(sb + VTILE, &maps.vl, &v_full[j & 1], row0 + j * KB, h * HD);
-            };
-            // Q rows past S belong to the next sequence (or lie past the buffer: zeros);
-            // their context is never stored
-            mbar_arrive_expect_tx(q_full, 2 * QT * HD * 2);
+            int kk_ = 0, kj = 0, kb_ = 0, kh = 0;
+            settle(kk_, kj, kb_, kh);
+            int gk = 0;  // K blocks issued
+            auto load_k = [&] {
+                uint8_t* sb = kring + (gk & 1) * KSTAGE;
+                uint64_t* bar = &k_full[gk & 1];
+                mbar_arrive_expect_tx(bar, KSTAGE);
 #pragma unroll
-            for (int i = 0; i < HD / 64; i++) {
-                tma_load_2d(q_smem + i * QT * 128, &maps.qh, q_full, h * HD + 64 * i, row0 + q0);
-                tma_load_2d(q_smem + QT * HD * 2 + i * QT * 128, &maps.ql, q_full, h * HD + 64 * i, row0 + q0);
-            }
-            int k_issued = 0, v_issued = 0;
-            for (; k_issued < min(nblk, 2); k_issued++) load_k(k_issued);
-            // the V ring holds Q until the softmax warps have copied it to TMEM
-            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
-            for (; ok && v_issued < min(nblk, 2); v_issued++) load_v(v_issued);
-            for (int t = 0; ok && t + 2 < nblk; t++) {
-                // stage t % 2 frees when QK_t (K) / PV_t (V) completes: phase t / 2 of the
-                // stage's empty barrier; K_{t+2} / V_{t+2} are not issued before it, so the
-                // barrier cannot be a phase further on
-                ok = mbar_wait(&k_empty[t & 1], (t >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                for (int i = 0; i < HD / 64; i++) {
+                    const int x = kh * HD + 64 * i, y = kb_ * S + kj * KB;
+                    tma_load_2d(sb + i * BOX, &maps.kh, bar, x, y);
+                    tma_load_2d(sb + KTILE + i * BOX, &maps.kl, bar, x, y);
+                }
+                gk++;
+                kj++;
+                settle(kk_, kj, kb_, kh);
+            };
+            load_q(0);
+            int q_loaded = 1;
+            for (int t = 0; t < 2 && kk_ < n_items; t++) load_k();
+            constexpr uint32_t idesc_qk = idesc_f16(KB);
+            bool ok = true;
+            int g = 0;  // QK blocks issued
+            for (int k = 0; ok && k < n_items; k++) {
+                // item k's Q in TMEM (q_ready phase k: phase k+1 needs Q_{k+1}, loaded below)
+                ok = mbar_wait(q_ready, k & 1, err, DEV_TIMEOUT_ATTN);
                 if (!ok) break;
-                load_k(t + 2);
-                k_issued = t + 3;
-                ok = mbar_wait(&v_empty[t & 1], (t >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-                if (!ok) break;
-                load_v(t + 2);
-                v_issued = t + 3;
+                tc_fence_after();
+                // the next item's Q goes into the Q buffer once item k-1's context has left
+                // it (ctx_done phase k-1: phase k needs this item's P, hence its QKs, or, for
+                // an item without keys, the Q loaded here).  Done after this item's first
+                // QK, which then computes during item k-1's epilogue.
+                auto load_next_q = [&] {
+                    if (k + 1 < n_items) {
+                        if (k >= 1) ok = mbar_wait(ctx_done, (k - 1) & 1, err, DEV_TIMEOUT_ATTN);
+                        if (ok) {
+                            load_q(k + 1);
+                            q_loaded = k + 2;
+                        }
+                    }
+                };
+                const int nblk = item(k).nblk;
+                if (nblk == 0) load_next_q();
+                for (int j = 0; ok && j < nblk; j++, g++) {
+                    if (g > 0) {
+                        // S_{g-1} read (s_free phase g-1: phase g needs QK_g, issued below)
+                        ok = mbar_wait(s_free, (g - 1) & 1, err, DEV_TIMEOUT_ATTN);
+                        if (!ok) break;
+                    }
+                    if (gk == g + 1 && kk_ < n_items) {
+                        // K_{g+1}: its stage frees when QK_{g-1} completes (k_empty phase
+                        // (g-1)/2; implied by s_free, and K_{g+1} is not issued yet)
+                        ok = mbar_wait(&k_empty[(g - 1) & 1], ((g - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                        if (!ok) break;
+                        load_k();
+                    }
+                    // K_g landed (k_full phase g/2: K_{g+2} waits for this QK)
+                    ok = mbar_wait(&k_full[g & 1], (g >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t kb = smem_u32(kring + (g & 1) * KSTAGE);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; kk++) {  // d 16kk..: Q_hi at column 8kk, Q_lo at HD/2 + 8kk
+                        // 16 fp16 = 32 bytes along the swizzled K rows, in box kk / 4
+                        const uint32_t off = (kk / 4) * BOX + (kk % 4) * 32;
+                        const uint32_t qh = tmem + COL_Q + 8 * kk, ql = qh + HD / 2;
+                        umma_f16_ts(tmem + COL_S, ql, desc_k_sw128(kb + off), idesc_qk, kk != 0);
+                        umma_f16_ts(tmem + COL_S, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
+                        umma_f16_ts(tmem + COL_S, qh, desc_k_sw128(kb + off), idesc_qk, 1);
+                    }
+                    umma_commit(s_full);
+                    umma_commit(&k_empty[g & 1]);
+                    if (j == 0) load_next_q();
+                }
             }
             // every load has landed before the CTA may exit (already true unless a wait
-            // here or in the MMA warp expired)
-            mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN);
-            for (int j = max(0, k_issued - 2); j < k_issued; j++)
-                mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-            for (int j = max(0, v_issued - 2); j < v_issued; j++)
-                mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+            // here or elsewhere expired)
+            mbar_wait(q_full, (q_loaded - 1) & 1, err, DEV_TIMEOUT_ATTN);
+            for (int x = max(0, gk - 2); x < gk; x++) mbar_wait(&k_full[x & 1], (x >> 1) & 1, err, DEV_TIMEOUT_ATTN);
         }
     } else if (warp == 1) {
-        if (lane == 0 && nblk > 0) {
-            constexpr uint32_t idesc_qk = idesc_f16(KB), idesc_pv = idesc_f16(HD);
-            // S_j = Q K_j^T into buffer j % 2, once K_j has landed (k_full phase j / 2:
-            // K_{j+2} waits for this QK, so the barrier cannot be further on)
-            auto issue_qk = [&](int j) -> bool {
-                if (!mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN)) return false;
-                tc_fence_after();
-                const uint32_t kb = smem_u32(kring + (j & 1) * KSTAGE);
-                const uint32_t d = tmem + COL_SP + 64 * (j & 1);
-#pragma unroll
-                for (int k = 0; k < HD / 16; k++) {  // d 16k..16k+15: Q_hi at column 8k, Q_lo at HD/2 + 8k
-                    // 16 fp16 = 32 bytes along the swizzled K rows, in box k / 4
-                    const uint32_t off = (k / 4) * BOX + (k % 4) * 32;
-                    const uint32_t qh = tmem + COL_Q + 8 * k, ql = qh + HD / 2;
-                    umma_f16_ts(d, ql, desc_k_sw128(kb + off), idesc_qk, k != 0);
-                    umma_f16_ts(d, qh, desc_k_sw128(kb + KTILE + off), idesc_qk, 1);
-                    umma_f16_ts(d, qh, desc_k_sw128(kb + off), idesc_qk, 1);
-                }
-                umma_commit(&s_full[j & 1]);
-                umma_commit(&k_empty[j & 1]);
-                return true;
+        // ---- V loads, O += P_g V_g
+        if (lane == 0 && n_items > 0) {
+            int vk = 0, vj = 0, vb_ = 0, vh = 0;
+            settle(vk, vj, vb_, vh);
+            int gv = 0;  // V blocks issued
+            auto load_v = [&] {
+                uint8_t* sb = vring + (gv & 1) * VSTAGE;
+                uint64_t* bar = &v_full[gv & 1];
+                mbar_arrive_expect_tx(bar, VSTAGE);
+                const int x = vb_ * S + vj * KB, y = vh * HD;
+                tma_load_2d(sb, &maps.vh, bar, x, y);
+                tma_load_2d(sb + VTILE, &maps.vl, bar, x, y);
+                gv++;
+                vj++;
+                settle(vk, vj, vb_, vh);
             };
-            bool ok = mbar_wait(q_ready, 0, err, DEV_TIMEOUT_ATTN);
-            if (ok) {
-                tc_fence_after();
-                ok = issue_qk(0);
-            }
-            if (ok && nblk > 1) ok = issue_qk(1);
-            for (int j = 0; ok && j < nblk; j++) {
-                // P_j (p_full phase j / 2: P_{j+2} needs S_{j+2}, issued only below) and V_j
-                ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN) &&
-                     mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-                if (!ok) break;
-                tc_fence_after();
-                const uint32_t vb = smem_u32(vring + (j & 1) * VSTAGE);
-                const uint32_t pb = tmem + COL_SP + 64 * (j & 1);
+            for (int t = 0; t < 2 && vk < n_items; t++) load_v();
+            constexpr uint32_t idesc_pv = idesc_f16(HD);
+            bool ok = true;
+            int g = 0;  // PV blocks issued
+            for (int k = 0; ok && k < n_items; k++) {
+                const int nblk = item(k).nblk;
+                for (int j = 0; ok && j < nblk; j++, g++) {
+                    // P_g (p_full phase g: phase g+1 needs PV_g) and V_g (v_full phase g/2)
+                    ok = mbar_wait(p_full, g & 1, err, DEV_TIMEOUT_ATTN) &&
+                         mbar_wait(&v_full[g & 1], (g >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t vb = smem_u32(vring + (g & 1) * VSTAGE);
+                    const uint32_t pb = tmem + COL_P;
 #pragma unroll
-                for (int k = 0; k < KB / 16; k++) {  // keys 16k..16k+15: P_hi at column 8k, P_lo at 32 + 8k
-                    const uint32_t off = k * 32;
-                    umma_f16_ts(tmem + COL_O, pb + 32 + 8 * k, desc_k_sw128(vb + off), idesc_pv, j > 0 || k != 0);
-                    umma_f16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + VTILE + off), idesc_pv, 1);
-                    umma_f16_ts(tmem + COL_O, pb + 8 * k, desc_k_sw128(vb + off), idesc_pv, 1);
-                }
-                umma_commit(&o_full[j & 1]);
-                umma_commit(&v_empty[j & 1]);
-                if (j + 2 < nblk) {
-                    // buffer j % 2 is free once PV_j has read P_j (o_full phase j / 2; this
-                    // thread waited for phase j / 2 - 1 two blocks ago, and PV_{j+2} is not
-                    // issued yet)
-                    ok = mbar_wait(&o_full[j & 1], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN);
-                    if (ok) {
-                        tc_fence_after();
-                        ok = issue_qk(j + 2);
+                    for (int kk = 0; kk < KB / 16; kk++) {  // keys 16kk..: P_hi at column 8kk, P_lo at 32 + 8kk
+                        const uint32_t off = kk * 32;
+                        // the item's first PV starts O afresh
+                        umma_f16_ts(tmem + COL_O, pb + 32 + 8 * kk, desc_k_sw128(vb + off), idesc_pv, j > 0 || kk != 0);
+                        umma_f16_ts(tmem + COL_O, pb + 8 * kk, desc_k_sw128(vb + VTILE + off), idesc_pv, 1);
+                        umma_f16_ts(tmem + COL_O, pb + 8 * kk, desc_k_sw128(vb + off), idesc_pv, 1);
+                    }
+                    umma_commit(o_full);
+                    umma_commit(&v_empty[g & 1]);
+                    if (gv == g + 1 && vk < n_items) {
+                        // V_{g+1}: its stage frees when PV_{g-1} completes (v_empty phase
+                        // (g-1)/2: issued a block ago; V_{g+1} is not issued yet)
+                        ok = mbar_wait(&v_empty[(g - 1) & 1], ((g - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN);
+                        if (!ok) break;
+                        load_v();
                     }
                 }
             }
+            for (int x = max(0, gv - 2); x < gv; x++) mbar_wait(&v_full[x & 1], (x >> 1) & 1, err, DEV_TIMEOUT_ATTN);
         }
     } else {
         // ---- softmax warps 2..5: warp w owns TMEM lane quadrant w % 4; thread = query row
         const int qd = warp & 3;
         const int r = qd * 32 + lane;
         const uint32_t lb = tmem + (static_cast<uint32_t>(qd * 32) << 16);
-        // k2 = hd^-1/2 log2 e / (s_Q s_K): p = 2^(s k2 - m k2) for raw accumulator scores s
-        float m = -INFINITY, l = 0.0f;                   // reference max (raw score units), row sum
         bool ok = true;
-        if (nblk > 0) {
-            // this row's Q split (HD fp16 each, RoPE applied) from the V ring (boxes of
-            // 128-byte rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
-            ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, DEV_TIMEOUT_ATTN));
+        // item k's Q split (HD fp16 each, RoPE applied) from the Q buffer (boxes of
+        // 128-byte rows, 16-byte chunk c at c ^ (row % 8)) into TMEM columns COL_Q..
+        auto copy_q = [&](int k) {
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(q_full, k & 1, err, DEV_TIMEOUT_ATTN));
 #pragma unroll
             for (int part = 0; part < 2; part++) {  // hi, then lo
 #pragma unroll
@@ -316,7 +384,7 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
                         const int o = part * QT * HD * 2 + box * QT * 128 + r * 128 + ((i ^ (r & 7)) << 4);
-                        const uint4 a = *reinterpret_cast<const uint4*>(q_smem + o);
+                        const uint4 a = *reinterpret_cast<const uint4*>(qbuf + o);
                         qw[4 * i] = a.x, qw[4 * i + 1] = a.y, qw[4 * i + 2] = a.z, qw[4 * i + 3] = a.w;
                     }
                     tmem_st32u(lb + COL_Q + part * (HD / 2) + 32 * box, qw);
@@ -326,146 +394,173 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(q_ready);
-        }
-        for (int j = 0; j < nblk; j++) {
-            const int bf = j & 1;
-            const uint32_t sp = lb + COL_SP + 64 * bf;  // this row's S_j, then P_j, columns
-            // s_full phase j / 2: QK_{j+2} waits for PV_j, which waits for this P_j.
-            // After an expired wait the loop keeps running (work skipped, results unused).
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[bf], (j >> 1) & 1, err, DEV_TIMEOUT_ATTN));
-            tc_fence_after();
-            float s[64];
-            tmem_ld64(sp, s);
-            if (j * KB + KB > valid) {  // the block holding the last valid key
-#pragma unroll
-                for (int c = 0; c < 64; c++)
-                    if (j * KB + c >= valid) s[c] = -INFINITY;
+        };
+        if (n_items > 0) copy_q(0);
+        int g = 0;  // key blocks done
+        for (int k = 0; k < n_items; k++) {
+            int valid, nblk;
+            {
+                const Item it = item(k);
+                valid = it.valid;
+                nblk = it.nblk;
             }
-            float mx[16];  // tree reduction: 16 independent chains, then 4 levels
-#pragma unroll
-            for (int c = 0; c < 16; c++) mx[c] = fmaxf(fmaxf(s[c], s[c + 16]), fmaxf(s[c + 32], s[c + 48]));
-#pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                for (int c = 0; c < w; c++) mx[c] = fmaxf(mx[c], mx[c + w]);
-            const float mb = mx[0];  // finite: the block has a valid key
-            const bool raise = (mb - m) * k2 > RESCALE_LOG2;      // always on the first block (m = -inf)
-            const float corr = raise ? ex2_approx((m - mb) * k2) : 1.0f;  // 0 on the first block
-            if (raise) m = mb;
-            // exponents carry the 2^7 scale of P: s = 2^(t + 7) = P * 2^7, and l sums those
-            const float off = P_LOG2_SCALE - m * k2;
-            const uint64_t k22 = pack2(k2, k2), nmk = pack2(off, off);
-            uint64_t sum2[4] = {0, 0, 0, 0};  // four independent packed partial sums
-#pragma unroll
-            for (int c = 0; c < 64; c += 2) {
-                float t0, t1;
-                unpack2(fma2(pack2(s[c], s[c + 1]), k22, nmk), t0, t1);  // masked keys: -inf -> p = 0
-                s[c] = ex2_approx(t0);
-                s[c + 1] = ex2_approx(t1);
-                sum2[(c >> 1) & 3] = add2(sum2[(c >> 1) & 3], pack2(s[c], s[c + 1]));
-            }
-            float sa, sb;
-            unpack2(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
-            l = l * corr + (sa + sb);
-            uint32_t hi[32], lo[32];
-#pragma unroll
-            for (int i = 0; i < 32; i++) split_p2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
-            if (j > 0 && __any_sync(0xffffffffu, raise)) {
-                // bring O to the new reference max once PV_{j-1} has completed: o_full
-                // phase (j-1) / 2 of buffer (j-1) % 2; its previous phase (PV_{j-3})
-                // completed before QK_j was issued, and PV_{j+1} needs P_{j+1}
-                ok = __all_sync(0xffffffffu,
-                                ok && mbar_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, err, DEV_TIMEOUT_ATTN));
+            // the next item's Q moves into TMEM once this item's last QK has completed
+            // (after its last block; at once for an item without keys: every earlier QK has)
+            if (nblk == 0 && k + 1 < n_items) copy_q(k + 1);
+            // k2 = hd^-1/2 log2 e / (s_Q s_K): p = 2^(s k2 - m k2) for raw accumulator scores s
+            float m = -INFINITY, l = 0.0f;  // reference max (raw score units), row sum
+            for (int j = 0; j < nblk; j++, g++) {
+                // S_g (s_full phase g: QK_{g+1} waits for this block's s_free).  After an
+                // expired wait the loop keeps running (work skipped, results unused).
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(s_full, g & 1, err, DEV_TIMEOUT_ATTN));
                 tc_fence_after();
-                const uint64_t c2 = pack2(corr, corr);
+                float s[64];
+                tmem_ld64(lb + COL_S, s);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free);  // QK_{g+1} may now overwrite S_g
+                if (j * KB + KB > valid) {  // the block holding the last valid key
 #pragma unroll
-                for (int cb = 0; cb < HD; cb += 64) {
-                    float o[64];
-                    tmem_ld64(lb + COL_O + cb, o);
+                    for (int c = 0; c < 64; c++)
+                        if (j * KB + c >= valid) s[c] = -INFINITY;
+                }
+                float mx[16];  // tree reduction: 16 independent chains, then 4 levels
 #pragma unroll
-                    for (int d = 0; d < 64; d += 2) {
-                        uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
-                        unpack2(t, o[d], o[d + 1]);
+                for (int c = 0; c < 16; c++) mx[c] = fmaxf(fmaxf(s[c], s[c + 16]), fmaxf(s[c + 32], s[c + 48]));
+#pragma unroll
+                for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                    for (int c = 0; c < w; c++) mx[c] = fmaxf(mx[c], mx[c + w]);
+                const float mb = mx[0];  // finite: the block has a valid key
+                const bool raise = (mb - m) * k2 > RESCALE_LOG2;              // always on the first block (m = -inf)
+                const float corr = raise ? ex2_approx((m - mb) * k2) : 1.0f;  // 0 on the first block
+                if (raise) m = mb;
+                // exponents carry the 2^7 scale of P: s = 2^(t + 7) = P * 2^7, and l sums those
+                const float off = P_LOG2_SCALE - m * k2;
+                const uint64_t k22 = pack2(k2, k2), nmk = pack2(off, off);
+                uint64_t sum2[4] = {0, 0, 0, 0};  // four independent packed partial sums
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) {
+                    float t0, t1;
+                    unpack2(fma2(pack2(s[c], s[c + 1]), k22, nmk), t0, t1);  // masked keys: -inf -> p = 0
+                    s[c] = ex2_approx(t0);
+                    s[c + 1] = ex2_approx(t1);
+                    sum2[(c >> 1) & 3] = add2(sum2[(c >> 1) & 3], pack2(s[c], s[c + 1]));
+                }
+                float sa, sb;
+                unpack2(add2(add2(sum2[0], sum2[1]), add2(sum2[2], sum2[3])), sa, sb);
+                l = l * corr + (sa + sb);
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) split_p2(s[2 * i], s[2 * i + 1], hi[i], lo[i]);
+                if (j > 0) {
+                    // PV_{g-1} has read the P buffer and finished O up to block j-1 (o_full
+                    // phase g-1: this loop waited for phase g-2 a block ago, and PV_g needs P_g)
+                    ok = __all_sync(0xffffffffu, ok && mbar_wait(o_full, (g - 1) & 1, err, DEV_TIMEOUT_ATTN));
+                    tc_fence_after();
+                }
+                if (j > 0 && __any_sync(0xffffffffu, raise)) {  // bring O to the new reference max
+                    const uint64_t c2 = pack2(corr, corr);
+#pragma unroll 1
+                    for (int cb = 0; cb < HD; cb += 32) {  // 32 columns at a time, not unrolled: hi / lo stay live
+                        float o[32];
+                        tmem_ld32(lb + COL_O + cb, o);
+#pragma unroll
+                        for (int d = 0; d < 32; d += 2) {
+                            uint64_t t = fma2(pack2(o[d], o[d + 1]), c2, 0);
+                            unpack2(t, o[d], o[d + 1]);
+                        }
+                        tmem_st32(lb + COL_O + cb, o);
                     }
-                    tmem_st32(lb + COL_O + cb, o);
-                    tmem_st32(lb + COL_O + cb + 32, o + 32);
+                }
+                tmem_st32u(lb + COL_P, hi);
+                tmem_st32u(lb + COL_P + 32, lo);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full);
+                // the item's last QK has completed (S_g was read): the next item's Q may
+                // take its TMEM columns, and its first QK computes during this epilogue
+                if (j == nblk - 1 && k + 1 < n_items) copy_q(k + 1);
+            }
+            if (nblk > 0) {
+                // the item's last PV (o_full phase g-1; phase g-2 was waited for above, or
+                // at the end of the previous item)
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(o_full, (g - 1) & 1, err, DEV_TIMEOUT_ATTN));
+                tc_fence_after();
+            }
+            // ---- context rows, 64 columns at a time: the fp16 split through TMA stores when
+            // all 32 rows of the warp belong to this sequence; otherwise (and for a plain
+            // fp32 context) per row
+            const Item it = item(k);  // recomputed: fewer registers live across the key loop
+            const int q0 = it.qb * QT, row0 = it.b * S, wrow0 = q0 + qd * 32;
+            // 1 / l, and O's scales undone (a power of two: exact)
+            const float inv = (nblk > 0 && l > 0.0f) ? (1.0f / l) * out_unscale : 0.0f;
+            const bool via_tma = ctx_tma && wrow0 + 32 <= S;
+            // staging in the Q buffer, once every warp has copied the next item's Q out of
+            // it (q_ready phase k+1: phase k+2 needs Q_{k+2}, loaded after ctx_done of this
+            // item): per warp HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
+            if (via_tma && k + 1 < n_items)
+                ok = __all_sync(0xffffffffu, ok && mbar_wait(q_ready, (k + 1) & 1, err, DEV_TIMEOUT_ATTN));
+            uint8_t* stg = qbuf + (warp - 2) * (HD * 128);
+#pragma unroll 1
+            for (int cb = 0; cb < HD; cb += 32) {  // 32 columns: half a 128-byte staging row (not unrolled: registers)
+                float o[32];
+                if (nblk > 0) tmem_ld32(lb + COL_O + cb, o);
+                if (via_tma) {
+                    uint32_t hw[16], lw[16];
+#pragma unroll
+                    for (int d = 0; d < 32; d += 2) {
+                        const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
+                        split2x2(x0, x1, ctx.scale, hw[d / 2], lw[d / 2]);
+                    }
+                    uint8_t* bx = stg + (cb / 64) * 8192;
+                    const int c0 = (cb % 64) / 8;  // first 16-byte chunk of the row
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int sw = (((c0 + i) ^ (lane & 7)) << 4) + lane * 128;
+                        *reinterpret_cast<uint4*>(bx + sw) =
+                            make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
+                        *reinterpret_cast<uint4*>(bx + 4096 + sw) =
+                            make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
+                    }
+                } else if (q0 + r < S) {
+                    const long long off = (long long)(row0 + q0 + r) * (heads * HD) + it.h * HD + cb;
+#pragma unroll
+                    for (int d = 0; d < 32; d += 4) {
+                        float x[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
+                        if (ctx.h) {
+                            uint2 hw, lw;
+                            split2x4(x, ctx.scale, hw, lw);
+                            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.h) + off + d) = hw;
+                            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.l) + off + d) = lw;
+                        } else {
+                            *reinterpret_cast<float4*>(ctx.plain + off + d) = make_float4(x[0], x[1], x[2], x[3]);
+                        }
+                    }
                 }
             }
-            tmem_st32u(sp, hi);
-            tmem_st32u(sp + 32, lo);
-            tmem_wait_st();
+            if (via_tma) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    const int y = row0 + wrow0;
+#pragma unroll
+                    for (int cb = 0; cb < HD; cb += 64) {
+                        tma_store_2d(&maps.ch, stg + (cb / 64) * 8192, it.h * HD + cb, y);
+                        tma_store_2d(&maps.cl, stg + (cb / 64) * 8192 + 4096, it.h * HD + cb, y);
+                    }
+                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read
+                }
+            }
+            // O is read (the next item's first PV may overwrite it once P is released) and
+            // the staging is free for the item after next's Q
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[bf]);
-        }
-        if (nblk > 0) {
-            // PV_{nblk-1}: its barrier's previous phase (PV_{nblk-3}) completed before
-            // QK_{nblk-1} was issued; its commit covers every earlier MMA
-            ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[(nblk - 1) & 1], ((nblk - 1) >> 1) & 1, err,
-                                                         DEV_TIMEOUT_ATTN));
-            tc_fence_after();
-        }
-        // ---- context rows, 64 columns at a time: the fp16 split through TMA stores when
-        // all 32 rows of the warp belong to this sequence; otherwise (and for a plain
-        // fp32 context) per row
-        const int wrow0 = q0 + qd * 32;
-        // 1 / l, and O's scales undone (a power of two: exact)
-        const float inv = (nblk > 0 && l > 0.0f) ? (1.0f / l) * out_unscale : 0.0f;
-        const bool via_tma = ctx_tma && wrow0 + 32 <= S;
-        // staging in the K ring (every K load has been consumed by a completed QK): per
-        // warp HD/64 pairs of 4 KB boxes (h, l), 128-byte rows of 64 fp16
-        uint8_t* stg = kring + (warp - 2) * (HD * 128);
-#pragma unroll
-        for (int cb = 0; cb < HD; cb += 64) {
-            float o[64];
-            if (nblk > 0) tmem_ld64(lb + COL_O + cb, o);
-            if (via_tma) {
-                uint32_t hw[32], lw[32];
-#pragma unroll
-                for (int d = 0; d < 64; d += 2) {
-                    const float x0 = nblk > 0 ? o[d] * inv : 0.0f, x1 = nblk > 0 ? o[d + 1] * inv : 0.0f;
-                    split2x2(x0, x1, ctx.scale, hw[d / 2], lw[d / 2]);
-                }
-                uint8_t* bx = stg + (cb / 64) * 8192;
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int sw = ((i ^ (lane & 7)) << 4) + lane * 128;
-                    *reinterpret_cast<uint4*>(bx + sw) = make_uint4(hw[4 * i], hw[4 * i + 1], hw[4 * i + 2], hw[4 * i + 3]);
-                    *reinterpret_cast<uint4*>(bx + 4096 + sw) =
-                        make_uint4(lw[4 * i], lw[4 * i + 1], lw[4 * i + 2], lw[4 * i + 3]);
-                }
-            } else if (q0 + r < S) {
-                const long long off = (long long)(row0 + q0 + r) * (heads * HD) + h * HD + cb;
-#pragma unroll
-                for (int d = 0; d < 64; d += 4) {
-                    float x[4];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) x[i] = nblk > 0 ? o[d + i] * inv : 0.0f;
-                    if (ctx.h) {
-                        uint2 hw, lw;
-                        split2x4(x, ctx.scale, hw, lw);
-                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.h) + off + d) = hw;
-                        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ctx.l) + off + d) = lw;
-                    } else {
-                        *reinterpret_cast<float4*>(ctx.plain + off + d) = make_float4(x[0], x[1], x[2], x[3]);
-                    }
-                }
-            }
-        }
-        if (via_tma) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                const int y = row0 + wrow0;
-#pragma unroll
-                for (int cb = 0; cb < HD; cb += 64) {
-                    tma_store_2d(&maps.ch, stg + (cb / 64) * 8192, h * HD + cb, y);
-                    tma_store_2d(&maps.cl, stg + (cb / 64) * 8192 + 4096, h * HD + cb, y);
-                }
-                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // staging read before exit
-            }
-            __syncwarp();
+            if (lane == 0) mbar_arrive(ctx_done);
         }
     }
     tc_fence_before();
@@ -497,11 +592,15 @@ void launch_attention_hd(cudaStream_t s, const AttnOperands& op, int seqs, int S
     } else {
         m.ch = m.cl = m.qh;  // unused
     }
-    dim3 grid((S + QT - 1) / QT, heads, seqs);
+    // persistent CTAs: every resident slot takes items blockIdx.x, + gridDim.x, ...
+    const int qblocks = (S + QT - 1) / QT;
+    const long long items = (long long)qblocks * heads * seqs;
+    if (items > INT_MAX) throw Error(9, "attention: more than 2^31 query blocks");
+    const int grid = (int)std::min<long long>(items, (long long)Cfg::CTAS_PER_SM * sm_count());
     const float k2 = (float)((1.0 / std::sqrt((double)HD)) * 1.4426950408889634 / ((double)op.q_scale * op.k_scale));
     const float out_unscale = (float)(1.0 / (double)op.v_scale);  // l already carries P's 2^7
-    launch_pdl(attention_tc_kernel<HD>, grid, dim3(THREADS), Cfg::SMEM_BYTES, s, m, S, valid, heads, ctx, ctx_tma,
-               k2, out_unscale, err);
+    launch_pdl(attention_tc_kernel<HD>, dim3(grid), dim3(THREADS), Cfg::SMEM_BYTES, s, m, S, valid, heads, qblocks,
+               (int)items, ctx, ctx_tma, k2, out_unscale, err);
 }
 
 }  // namespace

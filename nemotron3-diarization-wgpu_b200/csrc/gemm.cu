@@ -828,16 +828,6 @@ Maps4 operand_maps(const SplitOperand& A, const SplitOperand& B, int ra, int rb,
     return m;
 }
 
-int sm_count() {
-    static std::atomic<int> count[kMaxDevices];  // per device, 0 until queried
-    const int dev = current_device();
-    int n = count[dev].load(std::memory_order_relaxed);
-    if (!n) {
-        N3D_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
-        count[dev].store(n, std::memory_order_relaxed);
-    }
-    return n;
-}
 
 template <int BN>
 void launch_one(cudaStream_t s, const Maps4& maps, int M, int N, int K, int kb_per_tap, const Epi& epi, int* err,
@@ -908,6 +898,18 @@ void check_shape(const SplitOperand& A, const SplitOperand& B, int K, int kb_per
 }
 
 }  // namespace
+
+// Streaming multiprocessors of the current device (queried once per device).
+int sm_count() {
+    static std::atomic<int> count[kMaxDevices];  // per device, 0 until queried
+    const int dev = current_device();
+    int n = count[dev].load(std::memory_order_relaxed);
+    if (!n) {
+        N3D_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        count[dev].store(n, std::memory_order_relaxed);
+    }
+    return n;
+}
 
 float split_scale(double bound) {
     if (!(bound > 0.0) || !std::isfinite(bound)) return 1.0f;

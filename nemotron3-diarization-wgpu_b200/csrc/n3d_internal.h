@@ -148,6 +148,8 @@ float split_scale(double bound);
 
 // TMA-store maps (box 32 x 32) over a row-major fp32 matrix (128-byte swizzle) or
 // fp16 matrix (64-byte swizzle).
+// Streaming multiprocessors of the current device.
+int sm_count();
 CUtensorMap make_store_map(const float* p, long long rows, long long cols, long long ld);
 CUtensorMap make_store_map_f16(const void* p, long long rows, long long cols, long long ld);
 // 2-D map over a row-major fp16 matrix [rows, cols] with row stride ld elements;
