@@ -20,9 +20,11 @@
 // Two kernels:
 //   gemm_kernel<BN>        one CTA per 128 x BN tile, persistent (N = 192 head GEMMs,
 //                          small M, the allocation-free entry point)
-//   gemm_pair_kernel<BN>   CTA pairs on 256 x 256 tiles with M = 256
+//   gemm_pair_kernel<BN, EW> CTA pairs on 256 x 256 tiles with M = 256
 //                          `cta_group::2` MMAs: each CTA loads its 128 A rows and half
-//                          the B tile, the leader issues, both own 128 accumulator rows
+//                          the B tile, the leader issues, both own 128 accumulator rows;
+//                          EW = 4 or 8 epilogue warps (8: two per lane quadrant, each
+//                          storing half of the tile's columns)
 // Both: warp 0 TMA, warp 1 TMEM owner + MMA issue, epilogue warps 2.. (TMEM lane
 // quadrant = warp % 4); two TMEM accumulators so tile i's epilogue overlaps tile
 // i + 1's main loop.  Every wait is bounded; an expired wait records its site.
@@ -235,8 +237,14 @@ __device__ __forceinline__ void stage_rows_16(uint8_t* box, int lane, const uint
 // The staging area is double-buffered: consecutive store groups of a warp alternate
 // between its two halves, so before a half is overwritten only the group before the
 // latest -- the last one that used this half -- must have finished reading it.
+template <bool DB = true>
 __device__ __forceinline__ void stage_begin(int lane) {
-    if (lane == 0) bulk_wait_read1();
+    if (lane == 0) {
+        if (DB)
+            bulk_wait_read1();
+        else  // one 4 KB area: every earlier group must have read it
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    }
     __syncwarp();
 }
 // Make the staged boxes visible to the TMA unit and store them (up to three maps);
@@ -262,7 +270,7 @@ __device__ __forceinline__ void stage_issue(int lane, const CUtensorMap* m0, con
 // columns [c_begin, c_end).  `stg` is this warp's 8 KB staging area, two 4 KB halves
 // that consecutive store groups alternate between (`sbuf` counts the warp's groups
 // across tiles).
-template <int BN>
+template <int BN, bool DB = true>
 __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, int m0, int n0, int M, int N, int q,
                                                   int lane, uint8_t* stg, uint32_t& sbuf, int c_begin = 0,
                                                   int c_end = BN) {
@@ -272,7 +280,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
     const int r = rowbase + lane;
     if (mode == EPI_QKV_ATTN) {
         uint8_t* bhi = stg;
-        uint8_t* blo = stg + 4096;
+        uint8_t* blo = DB ? stg + 4096 : stg;
         for (int c = c_begin; c < c_end; c += 64) {
             float v[64];
             tmem_ld32(tl + c, v);
@@ -310,7 +318,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
             for (int i = 0; i < 32; i++) split2x2(v[2 * i], v[2 * i + 1], sc, hi[i], lo[i]);
             // h goes out from the first half, then l from the second, each as its own group
             if (sec < 2) {
-                stage_begin(lane);
+                stage_begin<DB>(lane);
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
@@ -318,7 +326,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                 }
                 stage_issue(lane, sec == 0 ? &epi.map_h : &epi.map_k_h, bhi, nullptr, nullptr, nullptr, nullptr, hcol,
                             rowbase);
-                stage_begin(lane);
+                stage_begin<DB>(lane);
 #pragma unroll
                 for (int i = 0; i < 8; i++) {
                     const int o = lane * 128 + ((i ^ (lane & 7)) << 4);
@@ -333,7 +341,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                 // disjoint banks)
                 const bool odd = lane & 1;
                 const int tok = (lane & ~1) * 2;
-                stage_begin(lane);
+                stage_begin<DB>(lane);
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const uint32_t ph = __shfl_xor_sync(0xffffffffu, hi[i], 1);
@@ -341,7 +349,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
                     *reinterpret_cast<uint32_t*>(bhi + row) = odd ? __byte_perm(ph, hi[i], 0x7632) : __byte_perm(hi[i], ph, 0x5410);
                 }
                 stage_issue(lane, &epi.map_vt_h, bhi, nullptr, nullptr, nullptr, nullptr, rowbase, hcol);
-                stage_begin(lane);
+                stage_begin<DB>(lane);
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const uint32_t pl = __shfl_xor_sync(0xffffffffu, lo[i], 1);
@@ -372,11 +380,11 @@ __device__ __forceinline__ void epilogue_tile_tma(const Epi& epi, uint32_t tl, i
 #pragma unroll
             for (int i = 0; i < 32; i++) v[i] = epi_value(mode, v[i], epi.acc_scale, bias[i]);
         }
-        uint8_t* half = stg + (sbuf++ & 1u) * 4096;
+        uint8_t* half = DB ? stg + (sbuf++ & 1u) * 4096 : stg;
         uint8_t* bst = half;         // 4 KB fp32 box (EPI_STORE)
         uint8_t* bh = half;          // 2 KB fp16 box (split modes)
         uint8_t* bl = half + 2048;   // 2 KB fp16 box
-        stage_begin(lane);
+        stage_begin<DB>(lane);
         if (split) {
             uint32_t hw[16], lw[16];
 #pragma unroll
@@ -590,11 +598,19 @@ __device__ __forceinline__ PairTile pair_tile(int t, int tiles_n, int full, int 
     return PairTile{base / tiles_n, (base % tiles_n) * BN + (u % split) * nw, nw};
 }
 
-template <int BN>
+// EW epilogue warps: 4 (one per TMEM lane quadrant, each with a double-buffered 8 KB
+// staging area) or 8 (two per quadrant, each storing half of the tile's columns
+// through a single 4 KB box, so that three 64 KB stages still fit).  8 suits the
+// epilogues with arithmetic per element (GELU, ReLU, plain stores); 4 those whose
+// stores dominate (the attention operands' hi/lo pairs, the reduce-adds).
+template <int BN, int EW>
 struct PairCfg {
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
     static constexpr int STAGE_BYTES = (BM + BN / 2) * ROW_2;
-    static constexpr int STAGING = 4 * 8192;
-    static constexpr int THREADS = 192;
+    static constexpr int EPI_WARPS = EW;
+    static constexpr int STAGE_BOX = EW == 8 ? 4096 : 8192;
+    static constexpr int STAGING = EPI_WARPS * STAGE_BOX;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr int STAGES_FIT = (232448 - STAGING - 2048) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static constexpr int TMEM_COLS = 2 * BN;
@@ -603,11 +619,11 @@ struct PairCfg {
     static_assert(STAGES >= 2, "need two pipeline stages");
 };
 
-template <int BN>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int EW>
+__global__ void __launch_bounds__(PairCfg<BN, EW>::THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ Maps4 maps, int M, int N, int K, int kb_per_tap,
                      const __grid_constant__ Epi epi, int* err, int full, int split) {
-    using Cfg = PairCfg<BN>;
+    using Cfg = PairCfg<BN, EW>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
@@ -631,7 +647,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 8);
+            mbar_init(&acc_empty[b], 2 * Cfg::EPI_WARPS);
         }
         mbar_fence_init();
         for (int i = 0; i < 4; i++) tma_prefetch_desc(&maps.m[i]);
@@ -694,7 +710,7 @@ __global__ void __launch_bounds__(192, 1)
             }
         }
     } else {
-        const int q = warp & 3;
+        const int q = warp & 3, half = (warp - 2) / 4;  // TMEM lane quadrant, column half
         const uint32_t acc_empty_leader = leader_addr(&acc_empty[0]);
         int it = 0;
         uint32_t sbuf = 0;
@@ -707,12 +723,19 @@ __global__ void __launch_bounds__(192, 1)
             const PairTile tile = pair_tile<BN>(t, tiles_n, full, split);
             const int m0 = tile.mt * 2 * BM + rank * BM;
             const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
-            if (epi.tma)
-                epilogue_tile_tma<BN>(epi, tl, m0, tile.n0, M, N, q, lane,
-                                      smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * 8192, sbuf, 0,
-                                      tile.nw);
-            else  // direct stores
+            if (epi.tma) {
+                // this warp's columns: half of the tile, in the mode's chunks (64 columns for
+                // the attention operands, else 32)
+                const int chunk = epi.mode == EPI_QKV_ATTN ? 64 : 32;
+                const int cw = Cfg::EPI_WARPS == 8 ? ((tile.nw / 2 + chunk - 1) / chunk) * chunk : tile.nw;
+                const int c0 = half * cw, c1 = min(tile.nw, c0 + cw);
+                if (c0 < c1)
+                    epilogue_tile_tma<BN, Cfg::STAGE_BOX == 8192>(
+                        epi, tl, m0, tile.n0, M, N, q, lane,
+                        smem + Cfg::STAGES * Cfg::STAGE_BYTES + 1024 + (warp - 2) * Cfg::STAGE_BOX, sbuf, c0, c1);
+            } else if (half == 0) {  // direct stores, one warp per quadrant
                 epilogue_tile<BN>(epi, tl, m0, tile.n0, M, N, q, lane, nullptr, tile.nw);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8u * buf);
@@ -843,10 +866,10 @@ void launch_one(cudaStream_t s, const Maps4& maps, int M, int N, int K, int kb_p
                Mp);
 }
 
-template <int BN>
+template <int BN, int EW>
 void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, int M, int N, int K, int kb_per_tap,
                  const Epi& epi, int* err) {
-    using Cfg = PairCfg<BN>;
+    using Cfg = PairCfg<BN, EW>;
     static std::atomic<int> clusters_per_device[kMaxDevices];  // 0 until measured on that device
     const int dev = current_device();
     int max_clusters = clusters_per_device[dev].load(std::memory_order_acquire);
@@ -864,10 +887,10 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     cfg.dynamicSmemBytes = Cfg::SMEM;
     cfg.stream = s;
     if (!max_clusters) {
-        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        N3D_CUDA(cudaFuncSetAttribute(gemm_pair_kernel<BN, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cfg::SMEM));
         cfg.gridDim = dim3(2 * (sm_count() / 2));
-        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN>, &cfg));
+        N3D_CUDA(cudaOccupancyMaxActiveClusters(&max_clusters, gemm_pair_kernel<BN, EW>, &cfg));
         if (max_clusters <= 0) throw Error(9, "no CTA pair of the GEMM fits on this device");
         clusters_per_device[dev].store(max_clusters, std::memory_order_release);
     }
@@ -882,7 +905,7 @@ void launch_pair(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, i
     const int full = tiles - rem;
     cfg.gridDim = dim3(2 * clusters);
     cfg.numAttrs = 2;
-    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN>, maps, M, N, K, kb_per_tap, epi, err, full, split));
+    N3D_CUDA(cudaLaunchKernelEx(&cfg, gemm_pair_kernel<BN, EW>, maps, M, N, K, kb_per_tap, epi, err, full, split));
 }
 
 void check_shape(const SplitOperand& A, const SplitOperand& B, int K, int kb_per_tap, const Epi& epi, int bn) {
@@ -994,7 +1017,10 @@ void gemm_split(cudaStream_t s, const SplitOperand& A, const SplitOperand& B, in
         case 128: launch_one<128>(s, operand_maps(A, B, BM, 128, true), M, N, K, kb_per_tap, epi, err); break;
         case 192: launch_one<192>(s, operand_maps(A, B, BM, 192, true), M, N, K, kb_per_tap, epi, err); break;
         default:
-            launch_pair<256>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            if (epi.mode == EPI_QKV_ATTN || epi.reduce)
+                launch_pair<256, 4>(s, A, B, M, N, K, kb_per_tap, epi, err);
+            else
+                launch_pair<256, 8>(s, A, B, M, N, K, kb_per_tap, epi, err);
             break;
     }
 }
