@@ -94,7 +94,18 @@ __device__ __forceinline__ void split_p2(float a, float b, uint32_t& h, uint32_t
     const uint32_t ba = __float_as_uint(fmaxf(a, 6.103515625e-05f)), bb = __float_as_uint(fmaxf(b, 6.103515625e-05f));
     h = __byte_perm(ba * 8u + 0x40008000u, bb * 8u + 0x40008000u, 0x7632);
     const uint32_t ua = (ba + 0x1000u) & 0xffffe000u, ub = (bb + 0x1000u) & 0xffffe000u;
-    l = f16x2_rn(__fsub_rn(a, __uint_as_float(ua)), __fsub_rn(b, __uint_as_float(ub)));
+    uint64_t d;  // (a, b) - (h_a, h_b), both lanes rounded to nearest (exact here)
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pack2(a, b)), "l"(pack2(__uint_as_float(ua), __uint_as_float(ub))));
+    float la, lb;
+    unpack2(d, la, lb);
+    l = f16x2_rn(la, lb);
+}
+
+// max(a, b, c) in one instruction
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
 }
 
 // 64 consecutive TMEM columns of this thread's lane: two loads, one wait.
@@ -424,14 +435,17 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
                     for (int c = 0; c < 64; c++)
                         if (j * KB + c >= valid) s[c] = -INFINITY;
                 }
-                float mx[16];  // tree reduction: 16 independent chains, then 4 levels
+                // block max by three-input maxima: 64 -> 22 -> 8 -> 3 -> 1 (31 instructions)
+                float m22[22];
 #pragma unroll
-                for (int c = 0; c < 16; c++) mx[c] = fmaxf(fmaxf(s[c], s[c + 16]), fmaxf(s[c + 32], s[c + 48]));
+                for (int c = 0; c < 21; c++) m22[c] = max3f(s[c], s[c + 21], s[c + 42]);
+                m22[21] = s[63];
+                float m8[8];
 #pragma unroll
-                for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                    for (int c = 0; c < w; c++) mx[c] = fmaxf(mx[c], mx[c + w]);
-                const float mb = mx[0];  // finite: the block has a valid key
+                for (int c = 0; c < 7; c++) m8[c] = max3f(m22[c], m22[c + 7], m22[c + 14]);
+                m8[7] = m22[21];
+                const float mb = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+                // (finite: the block has a valid key)
                 const bool raise = (mb - m) * k2 > RESCALE_LOG2;              // always on the first block (m = -inf)
                 const float corr = raise ? ex2_approx((m - mb) * k2) : 1.0f;  // 0 on the first block
                 if (raise) m = mb;
