@@ -599,7 +599,12 @@ def main():
                        "mode": mode, "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2 (0.8 GB of split weights + GBs of activations per step)"},
             "e2e": {"value": job_rate(world, n_items, item_s, args.steps, e2e_ms), "unit": UNIT,
-                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "ms_per_step": e2e_ms / args.steps,
+                    "host_ms_per_step": (e2e_ms - ms) / args.steps,
+                    "what": "n3d_run_batch from pinned host buffers (uploads, mel, steps, logits back), max over "
+                            "ranks; host_ms_per_step = its step time minus the device-resident step time, the "
+                            "host-side cost a rank adds (its share of host memory bandwidth and cores)"},
             "chunk_step_latency_ms": {
                 "p50": float(np.percentile(step_ms, 50)), "p99": float(np.percentile(step_ms, 99)),
                 "max": float(step_ms.max()), "count": int(step_ms.size),
