@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(THREADS, AttnCfg<HD>::CTAS_PER_SM)
     // while the tensor pipe idles, then both issuing MMAs.  Starting the second one
     // ~1.6 us late (about a key block) staggers them: +2 % attention throughput measured
     // at C4's shapes on one box, results unchanged.
-    if (blockIdx.x >= gridDim.x / 2) __nanosleep(1600);
+    if (Cfg::CTAS_PER_SM == 2 && blockIdx.x >= gridDim.x / 2) __nanosleep(1600);
 
     // This CTA's items: blockIdx.x + k * gridDim.x, k = 0.. ; item = (b * heads + h) *
     // qblocks + qb covers queries qb*128.. of head h of sequence b, and its key blocks
